@@ -1,0 +1,149 @@
+// Shared device-side types and helpers for the Needle-3 B200 path.
+//
+// Data layout in HBM (one copy of the container per GPU):
+//   * CQ tensors stay exactly as the `.cact` v3 blob stores them: `rows` packed
+//     rows of `row_bytes` (LSB-first index bitstream, crates/needle-core/src/
+//     cq.rs:908-925) followed by `rows * groups` FP16 norms. The whole container
+//     is copied to the device once and kernels read those blobs in place.
+//   * FP16/FP32 vectors (norm scales, taps, HadamardMLP factors, mHC scalars) are
+//     widened to f32 once at load time into a parameter arena.
+//   * Per-session state (KV rings, conv and Engram tails, token history) lives in
+//     one device allocation per session, described by a `SessDesc` kept in device
+//     memory so a captured CUDA graph can replay across decode steps.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace nb {
+
+constexpr int WARP = 32;
+constexpr int MAX_SEG = 4;
+
+// One CQ tensor slice read in place from the container: `rows` packed rows
+// followed by FP16 group norms (cq.rs:181-238).
+struct CqSeg {
+  const uint8_t* packed;
+  const __half* norms;
+  int rows;
+};
+
+// A logical projection = row-concatenation of up to MAX_SEG tensors that share
+// in_feat, group and width (q|k|v|gate, Engram key|value).
+struct CqMat {
+  CqSeg seg[MAX_SEG];
+  int nseg;
+  int rows;       // total rows
+  int in_feat;
+  int in_pad;     // in_feat rounded up to the group
+  int row_bytes;  // in_pad * bits / 8
+  int groups;     // in_pad / group
+  int group;      // 128 on every shipped tensor
+  int bits;       // 2 or 4 (byte-aligned widths)
+  float levels[16];
+};
+
+// Per-layer KV ring of one session. Device layout is head-major so one KV
+// head's keys are contiguous: k [kv_heads][slots][qk] (f32 or i8),
+// v [kv_heads][slots][vh], scales [kv_heads][slots] (int8 only).
+struct LayerKV {
+  void* k;
+  void* v;
+  float* ks;
+  float* vs;
+  int slots;
+  int cap;
+};
+
+// Device-resident session descriptor (crates/needle-core/src/v3/cache.rs:148).
+struct SessDesc {
+  int pos;        // next position to write
+  int int8;       // KvPrecision::Int8
+  LayerKV* layers;
+  float* qkv_tail;   // [layers][taps-1][q_dim+k_dim+v_dim], ring slot = pos % (taps-1)
+  float* eng_tail;   // [sites][reach][d_model], ring slot = pos % reach
+  uint32_t* toks;    // [4] token ring, slot = pos % 4
+};
+
+// One activation row of a batched forward: a (session, position) pair.
+struct RowInfo {
+  SessDesc* s;
+  int pos;
+  int base;  // prefill: row index of this session's position 0 in the launch; -1 for decode
+  int len;   // prefill: prompt length of the session; -1 for decode
+  int pad;
+};
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// Block-wide sum; `red` is shared scratch of >= 32 floats. All threads get the
+// result. Contains __syncthreads: call from every thread of the block.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_sum(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : 0.f;
+  return warp_sum(t);
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = (blockDim.x + 31) >> 5;
+  v = warp_max(v);
+  __syncthreads();
+  if (lane == 0) red[wid] = v;
+  __syncthreads();
+  float t = lane < nw ? red[lane] : -INFINITY;
+  return warp_max(t);
+}
+
+// Normalised Walsh-Hadamard transform of 128 floats held by one warp, 4 per
+// lane (element e = lane*4 + i). Same butterfly pairs and operand order as
+// crates/needle-core/src/hadamard.rs:24-55 (stride 1, 2, 4, ..., 64; a+b to the
+// lower index, a-b to the upper), so the result is bit-identical; the
+// 1/sqrt(128) scale (0x3db504f3 = 1.0f/sqrtf(128.f)) is applied at the end.
+__device__ __forceinline__ void fwht128_warp(float (&x)[4]) {
+  int lane = threadIdx.x & 31;
+  float a0 = x[0] + x[1], a1 = x[0] - x[1], a2 = x[2] + x[3], a3 = x[2] - x[3];
+  x[0] = a0 + a2;
+  x[2] = a0 - a2;
+  x[1] = a1 + a3;
+  x[3] = a1 - a3;
+#pragma unroll
+  for (int b = 0; b < 5; ++b) {
+    int m = 1 << b;
+    bool upper = (lane & m) != 0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float o = __shfl_xor_sync(0xffffffffu, x[i], m);
+      x[i] = upper ? (o - x[i]) : (x[i] + o);
+    }
+  }
+  const float s = __int_as_float(0x3db504f3);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) x[i] *= s;
+}
+
+// FWHT of `n128` consecutive 128-float groups stored in shared (or global)
+// memory, one warp per group, in place.
+__device__ __forceinline__ void fwht_groups_warp(float* buf, int n128) {
+  int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  for (int g = wid; g < n128; g += nw) {
+    float4 v = reinterpret_cast<float4*>(buf + g * 128)[lane];
+    float x[4] = {v.x, v.y, v.z, v.w};
+    fwht128_warp(x);
+    reinterpret_cast<float4*>(buf + g * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+  }
+}
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+}  // namespace nb

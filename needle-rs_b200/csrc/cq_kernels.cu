@@ -1,0 +1,317 @@
+// Codebook-quantized (CQ) projections read straight from the `.cact` v3 blobs.
+//
+// Replaces the reference's batch-1 GEMV (`CqWeight::matvec_lut_impl` /
+// `dot_group`, crates/needle-core/src/cq.rs:721-735, 838-873) and the batched
+// GEMM (`matmul_rows_prepared_impl`, cq.rs:632-679). As in the reference the
+// activation arrives already rotated by the per-group Walsh-Hadamard transform
+// (`prepare_input`, cq.rs:264-274), so the inner loop is a dot product of
+// codebook-decoded levels against the rotated activation with one FP16 norm
+// per (row, group):  y[o] = sum_g norm[o,g] * sum_k level[idx[o,g,k]] * xh[g,k].
+//
+// Index unpacking is bit-exact with cq.rs:908-925 (LSB-first bitstream; a
+// 2-bit byte holds indices 4b..4b+3 at bits 0-1, 2-3, 4-5, 6-7).
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.hpp"
+
+namespace nb {
+
+// ----------------------------------------------------------------------------
+// GEMV: MT activation rows at most (the batch-1 decode path and small batches).
+//
+// Each output row is split over LPR lanes; lane `sub` of a row reads the row's
+// 16-byte chunks sub, sub+LPR, ... with 128-bit loads, so a warp reads
+// 32/LPR rows x LPR*16 contiguous bytes per instruction. The codebook is
+// expanded into a byte-indexed table in shared memory (one table entry decodes
+// all indices of a packed byte, the GPU form of cq.rs:932-964), replicated so
+// the lanes of one shared-memory phase hit distinct banks. The activation rows
+// sit in shared memory with a 4-float pad after every chunk-sized block so that
+// lanes working on different chunks of the same row hit different banks.
+// ----------------------------------------------------------------------------
+template <int BITS>
+struct ChunkTraits;
+template <>
+struct ChunkTraits<2> {
+  static constexpr int E = 64;       // elements per 16-byte chunk
+  static constexpr int P = 4;        // levels per byte
+  static constexpr int COPIES = 8;   // LUT copies (LDS.128: 8 lanes per phase)
+};
+template <>
+struct ChunkTraits<4> {
+  static constexpr int E = 32;
+  static constexpr int P = 2;
+  static constexpr int COPIES = 16;  // LDS.64: 16 lanes per phase
+};
+
+__host__ __device__ inline int padded_len(int in_pad, int E) { return in_pad + (in_pad / E) * 4; }
+
+template <int BITS>
+__device__ __forceinline__ void build_lut_smem(const CqMat& W, float* lut) {
+  using T = ChunkTraits<BITS>;
+  const int total = 256 * T::COPIES;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    int byte = i / T::COPIES;
+#pragma unroll
+    for (int j = 0; j < T::P; ++j) lut[i * T::P + j] = W.levels[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
+  }
+}
+
+__device__ __forceinline__ int find_seg(const CqMat& W, int r, int* local) {
+  int s = 0, base = 0;
+#pragma unroll
+  for (int i = 0; i < MAX_SEG; ++i) {
+    if (i < W.nseg - 1 && r >= base + W.seg[i].rows) {
+      base += W.seg[i].rows;
+      s = i + 1;
+    }
+  }
+  *local = r - base;
+  return s;
+}
+
+template <int BITS, int LPR, int MT>
+__global__ void __launch_bounds__(256) cq_gemv_kernel(CqMat W, const float* __restrict__ xh, int ldx,
+                                                      int M, float* __restrict__ y, int ldy,
+                                                      int row0, int nrows) {
+  using T = ChunkTraits<BITS>;
+  extern __shared__ __align__(16) float smem[];
+  const int plen = padded_len(W.in_pad, T::E);
+  float* xs = smem;                       // [MT][plen]
+  float* lut = smem + MT * plen;          // [256 * COPIES * P]
+  for (int m = 0; m < M; ++m)
+    for (int k = threadIdx.x; k < W.in_pad; k += blockDim.x)
+      xs[m * plen + k + (k / T::E) * 4] = xh[(size_t)m * ldx + k];
+  build_lut_smem<BITS>(W, lut);
+  __syncthreads();
+
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int rows_per_warp = 32 / LPR;
+  const int sub = lane % LPR;
+  const int r = (blockIdx.x * (blockDim.x >> 5) + warp) * rows_per_warp + lane / LPR;
+  const bool active = r < nrows;
+  float acc[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+  if (active) {
+    int local;
+    int s = find_seg(W, row0 + r, &local);
+    const uint8_t* row = W.seg[s].packed + (size_t)local * W.row_bytes;
+    const __half* nrm = W.seg[s].norms + (size_t)local * W.groups;
+    const int nchunks = W.row_bytes / 16;
+    const int copy = lane % T::COPIES;
+    for (int c = sub; c < nchunks; c += LPR) {
+      uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + c);
+      const int k0 = c * T::E;
+      const float nv = __half2float(nrm[k0 / W.group]);
+      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+      float part[MT];
+#pragma unroll
+      for (int m = 0; m < MT; ++m) part[m] = 0.f;
+      const float* xc = xs + c * (T::E + 4);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+#pragma unroll
+        for (int bb = 0; bb < 4; ++bb) {
+          const int byte = (wd[q] >> (8 * bb)) & 0xff;
+          const int e0 = (q * 4 + bb) * T::P;
+          if (BITS == 2) {
+            const float4 lv = *reinterpret_cast<const float4*>(lut + (byte * T::COPIES + copy) * 4);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              if (m < M) {
+                const float4 xv = *reinterpret_cast<const float4*>(xc + m * plen + e0);
+                part[m] += lv.x * xv.x + lv.y * xv.y + lv.z * xv.z + lv.w * xv.w;
+              }
+            }
+          } else {
+            const float2 lv = *reinterpret_cast<const float2*>(lut + (byte * T::COPIES + copy) * 2);
+#pragma unroll
+            for (int m = 0; m < MT; ++m) {
+              if (m < M) {
+                const float2 xv = *reinterpret_cast<const float2*>(xc + m * plen + e0);
+                part[m] += lv.x * xv.x + lv.y * xv.y;
+              }
+            }
+          }
+        }
+      }
+#pragma unroll
+      for (int m = 0; m < MT; ++m) acc[m] += nv * part[m];
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) {
+#pragma unroll
+    for (int o = LPR / 2; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+  }
+  if (active && sub == 0) {
+#pragma unroll
+    for (int m = 0; m < MT; ++m)
+      if (m < M) y[(size_t)m * ldy + r] = acc[m];
+  }
+}
+
+// ----------------------------------------------------------------------------
+// SIMT GEMM for many activation rows (prefill, batched decode).
+// Tile: 64 weight rows x 64 activation rows, K stepped one quantisation group
+// (128) at a time. The group's packed bytes are decoded once into shared memory
+// (levels only; the FP16 norm is applied per group to the fp32 partial, as the
+// reference applies `norm * group_dot` in cq.rs:666-672) and reused by every
+// activation row of the tile.
+// ----------------------------------------------------------------------------
+constexpr int GB_N = 64, GB_M = 64, GB_K = 128, GB_PAD = 4;
+
+template <int BITS>
+__global__ void __launch_bounds__(256) cq_gemm_simt_kernel(CqMat W, const float* __restrict__ xh,
+                                                           int ldx, int M, float* __restrict__ y,
+                                                           int ldy, int row0, int nrows) {
+  __shared__ __align__(16) float Ws[GB_K][GB_N + GB_PAD];
+  __shared__ __align__(16) float Xs[GB_K][GB_M + GB_PAD];
+  __shared__ float Ns[GB_N];
+  const int tid = threadIdx.x;
+  const int n_base = blockIdx.x * GB_N, m_base = blockIdx.y * GB_M;
+  const int tn = (tid % 16) * 4, tm = (tid / 16) * 4;
+  constexpr int P = 8 / BITS;
+  constexpr int BPG = GB_K * BITS / 8;  // packed bytes per group per row
+  // Each thread decodes bytes of one fixed weight row (tid % 64).
+  const int my_nl = tid % GB_N;
+  const uint8_t* my_row = nullptr;
+  const __half* my_norm = nullptr;
+  if (n_base + my_nl < nrows) {
+    int local;
+    int s = find_seg(W, row0 + n_base + my_nl, &local);
+    my_row = W.seg[s].packed + (size_t)local * W.row_bytes;
+    my_norm = W.seg[s].norms + (size_t)local * W.groups;
+  }
+  float total[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) total[i][j] = 0.f;
+  for (int g = 0; g < W.groups; ++g) {
+    __syncthreads();
+    for (int bi = tid / GB_N; bi < BPG; bi += 256 / GB_N) {
+      uint8_t byte = my_row ? my_row[(size_t)g * BPG + bi] : 0;
+#pragma unroll
+      for (int j = 0; j < P; ++j) Ws[bi * P + j][my_nl] = W.levels[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
+    }
+    if (tid < GB_N) Ns[tid] = my_norm ? __half2float(my_norm[g]) : 0.f;
+    for (int i = tid; i < GB_M * (GB_K / 4); i += 256) {
+      int ml = i % GB_M, k4 = (i / GB_M) * 4;
+      int m = m_base + ml;
+      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+      if (m < M) v = *reinterpret_cast<const float4*>(xh + (size_t)m * ldx + (size_t)g * GB_K + k4);
+      Xs[k4 + 0][ml] = v.x;
+      Xs[k4 + 1][ml] = v.y;
+      Xs[k4 + 2][ml] = v.z;
+      Xs[k4 + 3][ml] = v.w;
+    }
+    __syncthreads();
+    float acc[4][4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+#pragma unroll 8
+    for (int k = 0; k < GB_K; ++k) {
+      float4 a = *reinterpret_cast<const float4*>(&Xs[k][tm]);
+      float4 b = *reinterpret_cast<const float4*>(&Ws[k][tn]);
+      float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      float nv = Ns[tn + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) total[i][j] += nv * acc[i][j];
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int m = m_base + tm + i;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int r = n_base + tn + j;
+      if (r < nrows) y[(size_t)m * ldy + r] = total[i][j];
+    }
+  }
+}
+
+// ----------------------------------------------------------------------------
+// Host dispatch
+// ----------------------------------------------------------------------------
+template <int BITS, int LPR, int MT>
+static cudaError_t launch_gemv(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
+                               int row0, int nrows, cudaStream_t st) {
+  using T = ChunkTraits<BITS>;
+  const int threads = 256;
+  const int rows_per_cta = (threads / 32) * (32 / LPR);
+  const int grid = (nrows + rows_per_cta - 1) / rows_per_cta;
+  const size_t smem = (size_t)(MT * padded_len(W.in_pad, T::E) + 256 * T::COPIES * T::P) * sizeof(float);
+  auto kern = cq_gemv_kernel<BITS, LPR, MT>;
+  if (smem > 48 * 1024) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  kern<<<grid, threads, smem, st>>>(W, xh, ldx, M, y, ldy, row0, nrows);
+  return cudaGetLastError();
+}
+
+template <int BITS, int MT>
+static cudaError_t gemv_lpr(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
+                            int row0, int nrows, cudaStream_t st) {
+  // Lanes per row: keep a few chunks per lane so every load is issued up front.
+  const int nchunks = W.row_bytes / 16;
+  if (nchunks <= 8) return launch_gemv<BITS, 2, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (nchunks <= 16) return launch_gemv<BITS, 4, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (nchunks <= 32) return launch_gemv<BITS, 8, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  return launch_gemv<BITS, 16, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+}
+
+template <int BITS>
+static cudaError_t launch_gemm_simt(const CqMat& W, const float* xh, int ldx, int M, float* y,
+                                    int ldy, int row0, int nrows, cudaStream_t st) {
+  dim3 grid((nrows + GB_N - 1) / GB_N, (M + GB_M - 1) / GB_M);
+  cq_gemm_simt_kernel<BITS><<<grid, 256, 0, st>>>(W, xh, ldx, M, y, ldy, row0, nrows);
+  return cudaGetLastError();
+}
+
+template <int BITS>
+static cudaError_t project_bits(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
+                                int row0, int nrows, cudaStream_t st) {
+  if (M <= 1) return gemv_lpr<BITS, 1>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (M <= 2) return gemv_lpr<BITS, 2>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (M <= 4) return gemv_lpr<BITS, 4>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (M <= 8) return gemv_lpr<BITS, 8>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  return launch_gemm_simt<BITS>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+}
+
+// Argument checks shared by every projection path: the kernels assume 16-byte
+// aligned rows and activations and a group of 128.
+static bool cq_args_ok(const CqMat& W, const float* xh, int ldx) {
+  if (W.group != GB_K || (W.bits != 2 && W.bits != 4)) return false;
+  if (W.row_bytes % 16 || W.in_pad % GB_K || ldx % 4 || (reinterpret_cast<uintptr_t>(xh) & 15)) return false;
+  if (W.nseg < 1 || W.nseg > MAX_SEG) return false;
+  for (int i = 0; i < W.nseg; ++i)
+    if (reinterpret_cast<uintptr_t>(W.seg[i].packed) & 15) return false;
+  return true;
+}
+
+cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
+                       int nrows, cudaStream_t st, int force_path) {
+  if (M <= 0 || nrows <= 0) return cudaSuccess;
+  if (!cq_args_ok(W, xh, ldx) || row0 < 0 || row0 + nrows > W.rows) return cudaErrorInvalidValue;
+  if (force_path == 1 && M > 8) return cudaErrorInvalidValue;
+  if (force_path == 2)
+    return W.bits == 2 ? launch_gemm_simt<2>(W, xh, ldx, M, y, ldy, row0, nrows, st)
+                       : launch_gemm_simt<4>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  return W.bits == 2 ? project_bits<2>(W, xh, ldx, M, y, ldy, row0, nrows, st)
+                     : project_bits<4>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+}
+
+}  // namespace nb

@@ -1,0 +1,83 @@
+// Host-side launch interface of the Needle-3 B200 kernels.
+#pragma once
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+
+namespace nb {
+
+// Model geometry as the kernels need it (crates/needle-core/src/v3/config.rs).
+struct Geo {
+  int d, heads, kvh, qk, vh, layers, lanes, hada_n, ba, bb, taps, window, max_seq, vocab, logit_rows;
+  int q_dim, k_dim, v_dim, o_dim, qkv_dim, proj_dim;
+  int e_tables, e_heads, e_slots, e_sub, e_taps, e_dil, e_maxorder, e_reach, n_orders, n_sites;
+  int orders[4];
+  int cond_rank;
+  float embed_scale;
+};
+
+// f32 parameters of one layer, widened from the container's FP16 records.
+struct LayerParams {
+  const float *norm_in, *q_taps, *k_taps, *v_taps, *q_norm, *k_norm, *post_norm, *pre_hada;
+  float attn_gate;
+  const float *d1, *d2, *b2, *d3, *d4, *w1a, *w1b, *w2a, *w2b, *w3a, *w3b, *cond_v, *cond_u;
+  int window;  // attention span, 0 = unbounded (config.rs:216)
+};
+
+struct MhcParams {
+  float a_pre, a_post, a_res;
+  const float *b_pre, *b_post, *b_res;  // this layer's slices
+};
+
+enum RowMode { MODE_DECODE = 0, MODE_PREFILL = 1 };
+
+struct RowBatch {
+  RowInfo* rows;            // [M] device
+  const uint32_t* tokens;   // [M] device: token fed at each row
+  int M;
+  int mode;
+};
+
+cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
+                       int nrows, cudaStream_t st, int force_path = 0);
+
+cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, float* lanes,
+                         cudaStream_t st);
+cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBatch& rb,
+                                 float* fetched, cudaStream_t st);
+cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const RowBatch& rb,
+                               const float* ekv, float* evc, cudaStream_t st);
+cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
+                             const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
+                             const MhcParams& mp, const float* norm_in, int site, const float* ekv,
+                             const float* evc, float* u, float* bx, float* xh, float* gates,
+                             cudaStream_t st);
+cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                            const float* rope_cs, const float* proj, float* qpost, void* pk,
+                            void* pv, float* pks, float* pvs, cudaStream_t st);
+cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                             const float* qpost, const void* pk, const void* pv, const float* pks,
+                             const float* pvs, float* attn, cudaStream_t st);
+cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, const float* attn,
+                               const float* proj, float* oh, cudaStream_t st);
+cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                              const uint32_t* p1, const uint32_t* p2, const float* projo,
+                              const float* u, float* bx, const float* gates, float* lanes,
+                              cudaStream_t st);
+cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
+                         const float* final_norm, float* lm_in, cudaStream_t st);
+cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st);
+cudaError_t launch_step_begin(const RowBatch& rb, SessDesc* const* sess, cudaStream_t st);
+cudaError_t launch_step_end(const RowBatch& rb, cudaStream_t st);
+
+// Standalone int8 quantiser of head vectors (cache.rs:100-106), bit-exact.
+cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float* scales,
+                            cudaStream_t st);
+// Standalone batched decode attention over caller-provided rings
+// (attention.rs:300-377): B independent sessions, each with its own [lo, hi].
+cudaError_t launch_attend_step(const float* q, const void* k, const void* v, const float* ks,
+                               const float* vs, int int8, int slots, const int* lo, const int* hi,
+                               int B, int heads, int kvh, int qk, int vh, float* out,
+                               cudaStream_t st);
+
+}  // namespace nb
