@@ -1,0 +1,189 @@
+/*
+ * needle.h — C ABI of the B200 Needle-3 engine (libneedle_b200.so).
+ *
+ * Part 1 mirrors the Needle-3 surface of bynds/needle-rs
+ * (crates/needle-c/include/needle.h:360-487, crates/needle-c/src/v3.rs:63-382,
+ * crates/needle-c/src/lib.rs:27-40, :118): same symbol names, argument meaning,
+ * ownership and error behaviour, so a caller of the reference's C library can
+ * link this one instead. Every call clears the thread-local last error first;
+ * failures return NULL / false / 0 and set it.
+ *
+ * Part 2 is an extension with no counterpart in the reference: token-level
+ * sessions and batches (what the reference exposes only inside Rust as
+ * V3Model::prefill / decode_step and V3Cache), used for multi-session serving.
+ *
+ * Part 3 exposes single kernels with device pointers for callers that manage
+ * their own memory and streams (tests, benchmarks, other runtimes).
+ *
+ * Device: a handle binds to the CUDA device that is current when it is loaded.
+ * One handle may be used from several threads; calls on one handle are
+ * serialised internally.
+ */
+#ifndef NEEDLE_B200_H
+#define NEEDLE_B200_H
+
+#include <stdbool.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ── Part 1: the reference's Needle 3 surface ─────────────────────────── */
+
+typedef struct NeedleV3Handle NeedleV3Handle;
+
+/* needle.h:370 / v3.rs:63-77. NULL on failure; free with needle_v3_free(). */
+NeedleV3Handle *needle_v3_load(const char *cact_path);
+
+/* needle.h:382 / v3.rs:109-128. This build serves the full depth only:
+ * `layers` must equal the container's layer count, anything else fails. */
+NeedleV3Handle *needle_v3_load_with_depth(const char *cact_path, size_t layers);
+
+/* needle.h:385 / v3.rs:135-138. 0 for NULL. */
+size_t needle_v3_num_layers(NeedleV3Handle *handle);
+
+/* needle.h:388 / v3.rs:85-100. */
+NeedleV3Handle *needle_v3_load_bytes(const unsigned char *data, size_t len);
+
+/* needle.h:396 / v3.rs:153-164; needle.h:405 / v3.rs:176-187;
+ * needle.h:411 / v3.rs:198-211; needle.h:417 / v3.rs:219-250;
+ * needle.h:431 / v3.rs:259-281. Text-level calls: they need the container's
+ * SentencePiece tokenizer record; when it is absent (as in synthetic
+ * containers) they return NULL and set the last error. */
+char *needle_v3_run(NeedleV3Handle *handle, const char *query, const char *tools_json);
+char *needle_v3_run_json(NeedleV3Handle *handle, const char *query, const char *tools_json);
+char *needle_v3_reasoning(NeedleV3Handle *handle, const char *text);
+char *needle_v3_generate(NeedleV3Handle *handle, const char *query, const char *tools_json,
+                         size_t max_new_tokens, float temperature, uint64_t seed,
+                         bool constrain, bool kv_int8);
+char *needle_v3_run_stream(NeedleV3Handle *handle, const char *query, const char *tools_json,
+                           void (*cb)(const char *piece, void *userdata), void *userdata);
+
+/* needle.h:438 / v3.rs:287-291. */
+bool needle_v3_has_confidence(NeedleV3Handle *handle);
+
+/* needle.h:452 / v3.rs:307-334. The probe head is not run by this build:
+ * returns false with the last error set. */
+bool needle_v3_confidence_for(NeedleV3Handle *handle, const char *query, const char *tools_json,
+                              const char *completion, float *out);
+
+/* needle.h:464 / v3.rs:350-362 (config.rs:234-272). */
+size_t needle_v3_kv_bytes(NeedleV3Handle *handle, size_t seq_len, bool kv_int8);
+
+/* needle.h:467 / v3.rs:369-373. */
+size_t needle_v3_max_seq_len(NeedleV3Handle *handle);
+
+/* needle.h:470 / v3.rs:378-382. Safe with NULL. */
+void needle_v3_free(NeedleV3Handle *handle);
+
+/* lib.rs:118. Safe with NULL. */
+void needle_free_str(char *s);
+
+/* needle.h:479-487 / lib.rs:27-40. Borrowed; valid until the next needle_*
+ * call on this thread. */
+const char *needle_last_error(void);
+
+/* ── Part 2: token-level sessions and batches (extension) ─────────────── */
+
+typedef struct NeedleV3Session NeedleV3Session;
+typedef struct NeedleV3Batch NeedleV3Batch;
+
+/* A per-generation KV cache on the device (V3Cache::with_precision,
+ * cache.rs:177-238): `hint` sizes the first allocation, rings grow on demand. */
+NeedleV3Session *needle_v3_session_new(NeedleV3Handle *handle, size_t hint, bool kv_int8);
+void needle_v3_session_free(NeedleV3Session *session);
+size_t needle_v3_session_pos(NeedleV3Session *session);
+/* Device bytes the session's cache holds (V3Cache::bytes, cache.rs:255-268). */
+size_t needle_v3_session_bytes(NeedleV3Session *session);
+size_t needle_v3_session_slots(NeedleV3Session *session, size_t layer);
+
+/* Prefill a fresh session with `n` token ids (V3Model::prefill, model.rs:512).
+ * Writes the last position's logits (logit_rows floats) when `logits` is not
+ * NULL. Host buffers. */
+bool needle_v3_prefill(NeedleV3Handle *handle, NeedleV3Session *session, const uint32_t *ids,
+                       size_t n, float *logits);
+
+/* One decode step (V3Model::decode_step, model.rs:150). Host buffers. */
+bool needle_v3_decode_step(NeedleV3Handle *handle, NeedleV3Session *session, uint32_t token,
+                           float *logits);
+
+/* Batched forms over `n` distinct sessions that share one KV precision.
+ * prefill: ids concatenated, lens[i] tokens for session i; last_logits
+ * [n][logit_rows] and picks [n] (greedy argmax, v3_engine.rs:410-420) may be
+ * NULL. decode: one token per session. Host buffers. */
+bool needle_v3_prefill_batch(NeedleV3Handle *handle, NeedleV3Session *const *sessions,
+                             const uint32_t *ids, const size_t *lens, size_t n,
+                             float *last_logits, uint32_t *picks);
+bool needle_v3_decode_batch(NeedleV3Handle *handle, NeedleV3Session *const *sessions,
+                            const uint32_t *tokens, size_t n, float *logits, uint32_t *picks);
+
+/* Greedy or sampled generation from token ids (V3Engine::generate_with loop,
+ * v3_engine.rs:193-315, without the text layers): prefill, then up to
+ * max_new_tokens steps; temperature <= 0 is greedy, else SplitMix64 sampling
+ * (v3_engine.rs:422-464). Stops at `eos_id` unless it is UINT32_MAX. Writes the
+ * generated ids to out_ids (capacity max_new_tokens) and returns their count;
+ * (size_t)-1 on failure. */
+size_t needle_v3_generate_ids(NeedleV3Handle *handle, const uint32_t *prompt, size_t n,
+                              size_t max_new_tokens, float temperature, uint64_t seed,
+                              bool kv_int8, uint32_t eos_id, uint32_t *out_ids);
+
+/* A fixed set of sessions decoded together with device-resident tokens; one
+ * step is captured once as a CUDA graph and replayed. */
+NeedleV3Batch *needle_v3_batch_new(NeedleV3Handle *handle, NeedleV3Session *const *sessions,
+                                   size_t n);
+void needle_v3_batch_free(NeedleV3Batch *batch);
+/* Device pointers to the batch's token buffers: `tokens` [n] is read by the
+ * next step, `next` [n] receives its greedy picks. */
+uint32_t *needle_v3_batch_tokens(NeedleV3Batch *batch);
+uint32_t *needle_v3_batch_next(NeedleV3Batch *batch);
+/* One step on `stream` (a cudaStream_t, NULL = the handle's stream).
+ * d_logits (device, [n][logit_rows]) may be NULL. Asynchronous. */
+bool needle_v3_batch_step(NeedleV3Batch *batch, float *d_logits, void *stream, bool use_graph);
+/* Copy `next` into `tokens` on `stream` (feed the greedy picks back). */
+bool needle_v3_batch_feed_next(NeedleV3Batch *batch, void *stream);
+
+/* Geometry: vocab, out_vocab, d_model, heads, kv_heads, layers, qk, v_head,
+ * max_seq, hada_n, lanes, window, conv_taps, logit_rows (14 int64). */
+bool needle_v3_geometry(NeedleV3Handle *handle, int64_t *out14);
+/* CUDA device a handle is bound to; -1 for NULL. */
+int needle_v3_device(NeedleV3Handle *handle);
+
+/* ── Part 3: single kernels on device pointers ─────────────────────────── */
+
+/* CQ projection y[m, row0 + r] = W[row0 + r] . xh[m] for m < M, r < nrows,
+ * reading one `.cact` CQ blob in place: `packed` = rows*in_pad*bits/8 bytes,
+ * `norms` = rows*(in_pad/128) FP16 (cq.rs:181-238). `levels` = the 2^bits
+ * codebook entries (host). xh is the rotated input (prepare_input, cq.rs:264),
+ * [M][ldx] f32. path: 0 auto, 1 GEMV (M <= 8), 2 tiled GEMM. Replaces
+ * CqWeight::matvec_rows_prepared / matmul_rows_prepared (cq.rs:301, :446). */
+int nd_cq_project(const void *packed, const void *norms, int rows, int in_feat, int bits,
+                  const float *levels, const float *xh, int ldx, int M, float *y, int ldy,
+                  int row0, int nrows, int path, void *stream);
+
+/* prepare_input (cq.rs:264-274): zero-pad x [M][in_feat] to in_pad and apply
+ * the normalised Walsh-Hadamard transform to every group of 128. */
+int nd_cq_prepare(const float *x, int M, int in_feat, float *xh, int ld_out, void *stream);
+
+/* quant_into (cache.rs:100-106) over `rows` vectors of `dim` <= 64 floats:
+ * int8 codes and one f32 scale per vector, bit-exact with the reference. */
+int nd_kv_quant(const float *x, int rows, int dim, int8_t *q, float *scales, void *stream);
+
+/* attend_step (attention.rs:300-377) for B independent sessions. Rings use the
+ * reference layout k [slots][kv_heads][qk], v [slots][kv_heads][vh], scales
+ * [slots][kv_heads] (int8 only), session b at b*slots*...; lo/hi are device
+ * int arrays [B] of the inclusive logical range; q [B][heads][qk] (already
+ * fake-quantised for int8), out [B][heads][vh]. */
+int nd_attend_step(const float *q, const void *k, const void *v, const float *ks, const float *vs,
+                   int int8, int slots, const int *lo, const int *hi, int B, int heads, int kv_heads,
+                   int qk, int vh, float *out, void *stream);
+
+/* Returns the cudaError_t of the last nd_* failure on this thread as text. */
+const char *nd_last_error(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* NEEDLE_B200_H */

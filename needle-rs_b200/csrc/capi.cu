@@ -1,0 +1,587 @@
+// extern "C" surface of libneedle_b200.so (declared in include/needle.h).
+//
+// Error model as crates/needle-c/src/lib.rs:27-40: a thread-local last error,
+// cleared at the start of every needle_* call and set on failure; pointer
+// results are NULL on failure, boolean results false, sizes 0.
+#include <cuda_runtime.h>
+
+#include <cstdio>
+#include <cstring>
+#include <fstream>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/needle.h"
+#include "engine.hpp"
+
+struct NeedleV3Handle {
+  std::unique_ptr<nb::Engine> eng;
+};
+struct NeedleV3Session {
+  NeedleV3Handle* h;
+  std::unique_ptr<nb::Session> s;
+};
+struct NeedleV3Batch {
+  NeedleV3Handle* h;
+  std::unique_ptr<nb::Batch> b;
+};
+
+namespace {
+thread_local std::string g_err;
+thread_local bool g_has_err = false;
+thread_local std::string g_nd_err;
+
+void clear_err() {
+  g_has_err = false;
+  g_err.clear();
+}
+void set_err(const std::string& m) {
+  g_err = m;
+  g_has_err = true;
+}
+
+NeedleV3Handle* load_engine(const uint8_t* data, size_t len, const std::string& what) {
+  std::string err;
+  nb::Engine* e = nb::Engine::load(data, len, &err);
+  if (!e) {
+    set_err(what + err);
+    return nullptr;
+  }
+  NeedleV3Handle* h = new NeedleV3Handle();
+  h->eng.reset(e);
+  return h;
+}
+
+bool read_file(const char* path, std::vector<uint8_t>* out) {
+  std::ifstream f(path, std::ios::binary);
+  if (!f) return false;
+  f.seekg(0, std::ios::end);
+  std::streamoff n = f.tellg();
+  if (n < 0) return false;
+  f.seekg(0, std::ios::beg);
+  out->resize((size_t)n);
+  return (bool)f.read(reinterpret_cast<char*>(out->data()), n) || n == 0;
+}
+
+char* out_string(const std::string& s) {
+  char* p = (char*)std::malloc(s.size() + 1);
+  if (!p) {
+    set_err("out of host memory");
+    return nullptr;
+  }
+  std::memcpy(p, s.c_str(), s.size() + 1);
+  return p;
+}
+
+const char* kNoText =
+    "text-level generation needs the container's SentencePiece tokenizer and prompt layer, "
+    "which this GPU build does not implement; use the token-level API "
+    "(needle_v3_prefill / needle_v3_decode_step / needle_v3_generate_ids)";
+
+int nd_status(cudaError_t e) {
+  if (e == cudaSuccess) return 0;
+  g_nd_err = std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e);
+  return (int)e;
+}
+
+nb::CqMat make_cq(const void* packed, const void* norms, int rows, int in_feat, int bits,
+                  const float* levels) {
+  nb::CqMat W;
+  std::memset(&W, 0, sizeof(W));
+  const int in_pad = (in_feat + 127) / 128 * 128;
+  W.seg[0].packed = (const uint8_t*)packed;
+  W.seg[0].norms = (const __half*)norms;
+  W.seg[0].rows = rows;
+  W.nseg = 1;
+  W.rows = rows;
+  W.in_feat = in_feat;
+  W.in_pad = in_pad;
+  W.row_bytes = in_pad * bits / 8;
+  W.groups = in_pad / 128;
+  W.group = 128;
+  W.bits = bits;
+  for (int i = 0; i < (1 << bits) && i < 16; ++i) W.levels[i] = levels[i];
+  return W;
+}
+
+// SplitMix64 and temperature sampling as crates/needle-infer/src/v3_engine.rs:422-464.
+struct SplitMix64 {
+  uint64_t s;
+  uint64_t next_u64() {
+    s += 0x9E3779B97F4A7C15ull;
+    uint64_t z = s;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+  }
+  double next_f64() { return (double)(next_u64() >> 11) / (double)(1ull << 53); }
+};
+uint32_t sample(const float* logits, size_t n, float temperature, SplitMix64* rng) {
+  const float inv = 1.0f / temperature;
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; ++i)
+    if (logits[i] > mx) mx = logits[i];
+  double sum = 0.0;
+  for (size_t i = 0; i < n; ++i) sum += (double)expf((logits[i] - mx) * inv);
+  double target = rng->next_f64() * sum;
+  for (size_t i = 0; i < n; ++i) {
+    target -= (double)expf((logits[i] - mx) * inv);
+    if (target <= 0.0) return (uint32_t)i;
+  }
+  return (uint32_t)(n - 1);
+}
+}  // namespace
+
+extern "C" {
+
+// ------------------------------------------------------------------ Part 1
+NeedleV3Handle* needle_v3_load(const char* cact_path) {
+  clear_err();
+  if (!cact_path) {
+    set_err("cact_path was null or not UTF-8");
+    return nullptr;
+  }
+  std::vector<uint8_t> raw;
+  if (!read_file(cact_path, &raw)) {
+    set_err(std::string("failed to load ") + cact_path + ": cannot read file");
+    return nullptr;
+  }
+  return load_engine(raw.data(), raw.size(), std::string("failed to load ") + cact_path + ": ");
+}
+
+NeedleV3Handle* needle_v3_load_bytes(const unsigned char* data, size_t len) {
+  clear_err();
+  if (!data) {
+    set_err("data was null");
+    return nullptr;
+  }
+  return load_engine(data, len, "failed to load container: ");
+}
+
+NeedleV3Handle* needle_v3_load_with_depth(const char* cact_path, size_t layers) {
+  clear_err();
+  NeedleV3Handle* h = needle_v3_load(cact_path);
+  if (!h) return nullptr;
+  if (layers != h->eng->cfg.layers) {
+    set_err(std::string("failed to load ") + cact_path + " at " + std::to_string(layers) +
+            " layers: this GPU engine serves the full depth (" + std::to_string(h->eng->cfg.layers) +
+            " layers) only");
+    delete h;
+    return nullptr;
+  }
+  return h;
+}
+
+size_t needle_v3_num_layers(NeedleV3Handle* h) {
+  clear_err();
+  if (!h) {
+    set_err("handle was null");
+    return 0;
+  }
+  return h->eng->cfg.layers;
+}
+
+char* needle_v3_run(NeedleV3Handle* h, const char* query, const char* tools_json) {
+  clear_err();
+  if (!h) set_err("handle was null");
+  else if (!query || !tools_json) set_err("query or tools_json was null");
+  else set_err(kNoText);
+  return nullptr;
+}
+
+char* needle_v3_run_json(NeedleV3Handle* h, const char* query, const char* tools_json) {
+  return needle_v3_run(h, query, tools_json);
+}
+
+// V3Engine::reasoning (v3_engine.rs:382-401): the text between <think> and
+// </think> (or to the end when unterminated), trimmed; NULL when absent.
+char* needle_v3_reasoning(NeedleV3Handle* h, const char* text) {
+  clear_err();
+  if (!h) {
+    set_err("handle was null");
+    return nullptr;
+  }
+  if (!text) {
+    set_err("text was null or not UTF-8");
+    return nullptr;
+  }
+  std::string s(text);
+  size_t a = s.find("<think>");
+  if (a == std::string::npos) return nullptr;
+  a += 7;
+  size_t b = s.find("</think>", a);
+  std::string mid = s.substr(a, b == std::string::npos ? std::string::npos : b - a);
+  const char* ws = " \t\n\r\f\v";
+  size_t i = mid.find_first_not_of(ws), j = mid.find_last_not_of(ws);
+  return out_string(i == std::string::npos ? std::string() : mid.substr(i, j - i + 1));
+}
+
+char* needle_v3_generate(NeedleV3Handle* h, const char* query, const char* tools_json,
+                         size_t max_new_tokens, float temperature, uint64_t seed, bool constrain,
+                         bool kv_int8) {
+  (void)max_new_tokens;
+  (void)temperature;
+  (void)seed;
+  (void)constrain;
+  (void)kv_int8;
+  return needle_v3_run(h, query, tools_json);
+}
+
+char* needle_v3_run_stream(NeedleV3Handle* h, const char* query, const char* tools_json,
+                           void (*cb)(const char*, void*), void* userdata) {
+  (void)cb;
+  (void)userdata;
+  return needle_v3_run(h, query, tools_json);
+}
+
+bool needle_v3_has_confidence(NeedleV3Handle* h) {
+  clear_err();
+  if (!h) {
+    set_err("handle was null");
+    return false;
+  }
+  return h->eng->cfg.has_heads;
+}
+
+bool needle_v3_confidence_for(NeedleV3Handle* h, const char* query, const char* tools_json,
+                              const char* completion, float* out) {
+  clear_err();
+  if (!h) set_err("handle was null");
+  else if (!query || !tools_json || !completion) set_err("an argument was null or not UTF-8");
+  else if (!out) set_err("out was null");
+  else if (!h->eng->cfg.has_heads) set_err("this container exports no confidence head");
+  else set_err("the confidence probe head is not run by this GPU build");
+  return false;
+}
+
+size_t needle_v3_kv_bytes(NeedleV3Handle* h, size_t seq_len, bool kv_int8) {
+  clear_err();
+  if (!h) {
+    set_err("handle was null");
+    return 0;
+  }
+  return h->eng->cfg.kv_bytes_at(seq_len, kv_int8);
+}
+
+size_t needle_v3_max_seq_len(NeedleV3Handle* h) {
+  clear_err();
+  if (!h) {
+    set_err("handle was null");
+    return 0;
+  }
+  return h->eng->cfg.max_seq;
+}
+
+void needle_v3_free(NeedleV3Handle* h) { delete h; }
+
+void needle_free_str(char* s) { std::free(s); }
+
+const char* needle_last_error(void) { return g_has_err ? g_err.c_str() : nullptr; }
+
+// ------------------------------------------------------------------ Part 2
+NeedleV3Session* needle_v3_session_new(NeedleV3Handle* h, size_t hint, bool kv_int8) {
+  clear_err();
+  if (!h) {
+    set_err("handle was null");
+    return nullptr;
+  }
+  std::string err;
+  nb::Session* s = h->eng->new_session(hint, kv_int8, &err);
+  if (!s) {
+    set_err(err);
+    return nullptr;
+  }
+  NeedleV3Session* r = new NeedleV3Session();
+  r->h = h;
+  r->s.reset(s);
+  return r;
+}
+
+void needle_v3_session_free(NeedleV3Session* s) { delete s; }
+
+size_t needle_v3_session_pos(NeedleV3Session* s) {
+  clear_err();
+  if (!s) {
+    set_err("session was null");
+    return 0;
+  }
+  return s->s->pos;
+}
+
+size_t needle_v3_session_bytes(NeedleV3Session* s) {
+  clear_err();
+  if (!s) {
+    set_err("session was null");
+    return 0;
+  }
+  return s->s->bytes();
+}
+
+size_t needle_v3_session_slots(NeedleV3Session* s, size_t layer) {
+  clear_err();
+  if (!s || layer >= s->s->layers.size()) {
+    set_err("session was null or layer out of range");
+    return 0;
+  }
+  return (size_t)s->s->layers[layer].slots;
+}
+
+static bool check_sessions(NeedleV3Handle* h, NeedleV3Session* const* ss, size_t n,
+                           std::vector<nb::Session*>* out) {
+  if (!h) {
+    set_err("handle was null");
+    return false;
+  }
+  if (n && !ss) {
+    set_err("sessions was null");
+    return false;
+  }
+  out->resize(n);
+  for (size_t i = 0; i < n; ++i) {
+    if (!ss[i] || ss[i]->h != h) {
+      set_err("session was null or belongs to another handle");
+      return false;
+    }
+    (*out)[i] = ss[i]->s.get();
+  }
+  return true;
+}
+
+bool needle_v3_prefill(NeedleV3Handle* h, NeedleV3Session* s, const uint32_t* ids, size_t n,
+                       float* logits) {
+  clear_err();
+  std::vector<nb::Session*> v;
+  if (!check_sessions(h, &s, 1, &v)) return false;
+  if (!ids && n) {
+    set_err("ids was null");
+    return false;
+  }
+  if (n == 0) return true;  // empty prompt: nothing to report (model.rs:516-518)
+  std::string err;
+  const uint32_t* idp[1] = {ids};
+  size_t lens[1] = {n};
+  if (!h->eng->prefill(v.data(), idp, lens, 1, logits, nullptr, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
+bool needle_v3_decode_step(NeedleV3Handle* h, NeedleV3Session* s, uint32_t token, float* logits) {
+  clear_err();
+  std::vector<nb::Session*> v;
+  if (!check_sessions(h, &s, 1, &v)) return false;
+  std::string err;
+  if (!h->eng->decode(v.data(), &token, 1, logits, nullptr, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
+bool needle_v3_prefill_batch(NeedleV3Handle* h, NeedleV3Session* const* ss, const uint32_t* ids,
+                             const size_t* lens, size_t n, float* last_logits, uint32_t* picks) {
+  clear_err();
+  std::vector<nb::Session*> v;
+  if (!check_sessions(h, ss, n, &v)) return false;
+  if (n && (!ids || !lens)) {
+    set_err("ids or lens was null");
+    return false;
+  }
+  std::vector<const uint32_t*> idp(n);
+  size_t off = 0;
+  for (size_t i = 0; i < n; ++i) {
+    idp[i] = ids + off;
+    off += lens[i];
+  }
+  std::string err;
+  if (!h->eng->prefill(v.data(), idp.data(), lens, n, last_logits, picks, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
+bool needle_v3_decode_batch(NeedleV3Handle* h, NeedleV3Session* const* ss, const uint32_t* tokens,
+                            size_t n, float* logits, uint32_t* picks) {
+  clear_err();
+  std::vector<nb::Session*> v;
+  if (!check_sessions(h, ss, n, &v)) return false;
+  if (n && !tokens) {
+    set_err("tokens was null");
+    return false;
+  }
+  std::string err;
+  if (!h->eng->decode(v.data(), tokens, n, logits, picks, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
+size_t needle_v3_generate_ids(NeedleV3Handle* h, const uint32_t* prompt, size_t n,
+                              size_t max_new_tokens, float temperature, uint64_t seed, bool kv_int8,
+                              uint32_t eos_id, uint32_t* out_ids) {
+  clear_err();
+  const size_t FAIL = (size_t)-1;
+  if (!h) {
+    set_err("handle was null");
+    return FAIL;
+  }
+  if ((!prompt && n) || (!out_ids && max_new_tokens)) {
+    set_err("prompt or out_ids was null");
+    return FAIL;
+  }
+  if (n == 0 || max_new_tokens == 0) return 0;
+  nb::Engine* E = h->eng.get();
+  const size_t max = E->cfg.max_seq;
+  if (n > max) n = max;  // prompt truncation, v3_engine.rs:206-214
+  const size_t budget = std::min(max - n, max_new_tokens);
+  std::string err;
+  std::unique_ptr<nb::Session> s(E->new_session(n + budget, kv_int8, &err));
+  if (!s) {
+    set_err(err);
+    return FAIL;
+  }
+  const size_t rows = E->cfg.logit_rows();
+  std::vector<float> logits(rows);
+  nb::Session* sp = s.get();
+  const uint32_t* idp[1] = {prompt};
+  size_t lens[1] = {n};
+  uint32_t pick = 0;
+  if (!E->prefill(&sp, idp, lens, 1, temperature > 0.f ? logits.data() : nullptr, &pick, &err)) {
+    set_err(err);
+    return FAIL;
+  }
+  SplitMix64 rng{seed};
+  size_t count = 0;
+  for (size_t t = 0; t < budget; ++t) {
+    uint32_t next = temperature > 0.f ? sample(logits.data(), rows, temperature, &rng) : pick;
+    if (eos_id != UINT32_MAX && next == eos_id) break;
+    out_ids[count++] = next;
+    if (sp->pos >= max) break;
+    if (!E->decode(&sp, &next, 1, temperature > 0.f ? logits.data() : nullptr, &pick, &err)) {
+      set_err(err);
+      return FAIL;
+    }
+  }
+  return count;
+}
+
+NeedleV3Batch* needle_v3_batch_new(NeedleV3Handle* h, NeedleV3Session* const* ss, size_t n) {
+  clear_err();
+  std::vector<nb::Session*> v;
+  if (!check_sessions(h, ss, n, &v)) return nullptr;
+  std::string err;
+  nb::Batch* b = h->eng->new_batch(v.data(), n, &err);
+  if (!b) {
+    set_err(err);
+    return nullptr;
+  }
+  NeedleV3Batch* r = new NeedleV3Batch();
+  r->h = h;
+  r->b.reset(b);
+  return r;
+}
+
+void needle_v3_batch_free(NeedleV3Batch* b) { delete b; }
+
+uint32_t* needle_v3_batch_tokens(NeedleV3Batch* b) {
+  clear_err();
+  if (!b) {
+    set_err("batch was null");
+    return nullptr;
+  }
+  return b->b->d_tok;
+}
+
+uint32_t* needle_v3_batch_next(NeedleV3Batch* b) {
+  clear_err();
+  if (!b) {
+    set_err("batch was null");
+    return nullptr;
+  }
+  return b->b->d_next;
+}
+
+bool needle_v3_batch_step(NeedleV3Batch* b, float* d_logits, void* stream, bool use_graph) {
+  clear_err();
+  if (!b) {
+    set_err("batch was null");
+    return false;
+  }
+  nb::Engine* E = b->h->eng.get();
+  cudaStream_t st = stream ? (cudaStream_t)stream : E->stream;
+  std::string err;
+  if (!E->decode_batch_device(b->b.get(), d_logits, st, use_graph, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
+bool needle_v3_batch_feed_next(NeedleV3Batch* b, void* stream) {
+  clear_err();
+  if (!b) {
+    set_err("batch was null");
+    return false;
+  }
+  nb::Engine* E = b->h->eng.get();
+  cudaStream_t st = stream ? (cudaStream_t)stream : E->stream;
+  cudaError_t e = cudaMemcpyAsync(b->b->d_tok, b->b->d_next, b->b->sessions.size() * 4,
+                                  cudaMemcpyDeviceToDevice, st);
+  if (e != cudaSuccess) {
+    set_err(std::string("feeding tokens: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+bool needle_v3_geometry(NeedleV3Handle* h, int64_t* out) {
+  clear_err();
+  if (!h || !out) {
+    set_err("handle or out was null");
+    return false;
+  }
+  const nb::HostConfig& c = h->eng->cfg;
+  int64_t v[14] = {(int64_t)c.vocab, (int64_t)c.out_vocab, (int64_t)c.d,       (int64_t)c.heads,
+                   (int64_t)c.kvh,   (int64_t)c.layers,    (int64_t)c.qk,      (int64_t)c.vh,
+                   (int64_t)c.max_seq, (int64_t)c.hada_n,  (int64_t)c.lanes,   (int64_t)c.window,
+                   (int64_t)c.taps,  (int64_t)c.logit_rows()};
+  std::memcpy(out, v, sizeof(v));
+  return true;
+}
+
+int needle_v3_device(NeedleV3Handle* h) { return h ? h->eng->device : -1; }
+
+// ------------------------------------------------------------------ Part 3
+int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, int bits,
+                  const float* levels, const float* xh, int ldx, int M, float* y, int ldy, int row0,
+                  int nrows, int path, void* stream) {
+  if (!packed || !norms || !levels || !xh || !y || rows <= 0 || in_feat <= 0 || (bits != 2 && bits != 4))
+    return nd_status(cudaErrorInvalidValue);
+  nb::CqMat W = make_cq(packed, norms, rows, in_feat, bits, levels);
+  return nd_status(nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, (cudaStream_t)stream, path));
+}
+
+int nd_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out, void* stream) {
+  return nd_status(nb::launch_cq_prepare(x, M, in_feat, xh, ld_out, (cudaStream_t)stream));
+}
+
+int nd_kv_quant(const float* x, int rows, int dim, int8_t* q, float* scales, void* stream) {
+  if (!x || !q || !scales) return nd_status(cudaErrorInvalidValue);
+  return nd_status(nb::launch_kv_quant(x, rows, dim, q, scales, (cudaStream_t)stream));
+}
+
+int nd_attend_step(const float* q, const void* k, const void* v, const float* ks, const float* vs,
+                   int int8, int slots, const int* lo, const int* hi, int B, int heads, int kv_heads,
+                   int qk, int vh, float* out, void* stream) {
+  if (!q || !k || !v || !lo || !hi || !out || (int8 && (!ks || !vs))) return nd_status(cudaErrorInvalidValue);
+  return nd_status(nb::launch_attend_step(q, k, v, ks, vs, int8, slots, lo, hi, B, heads, kv_heads, qk,
+                                          vh, out, (cudaStream_t)stream));
+}
+
+const char* nd_last_error(void) { return g_nd_err.c_str(); }
+
+}  // extern "C"

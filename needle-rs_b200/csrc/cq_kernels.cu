@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "kernels.hpp"
+#include "launch_util.hpp"
 
 namespace nb {
 
@@ -160,20 +161,22 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(CqMat W, const float* __re
 // reference applies `norm * group_dot` in cq.rs:666-672) and reused by every
 // activation row of the tile.
 // ----------------------------------------------------------------------------
-constexpr int GB_N = 64, GB_M = 64, GB_K = 128, GB_PAD = 4;
+constexpr int GB_N = 64, GB_M = 64, GB_K = 128, GB_KS = 64, GB_PAD = 4;
 
 template <int BITS>
 __global__ void __launch_bounds__(256) cq_gemm_simt_kernel(CqMat W, const float* __restrict__ xh,
                                                            int ldx, int M, float* __restrict__ y,
                                                            int ldy, int row0, int nrows) {
-  __shared__ __align__(16) float Ws[GB_K][GB_N + GB_PAD];
-  __shared__ __align__(16) float Xs[GB_K][GB_M + GB_PAD];
+  // Half a group (64 of K) is staged at a time so the tiles fit static shared memory.
+  __shared__ __align__(16) float Ws[GB_KS][GB_N + GB_PAD];
+  __shared__ __align__(16) float Xs[GB_KS][GB_M + GB_PAD];
   __shared__ float Ns[GB_N];
   const int tid = threadIdx.x;
   const int n_base = blockIdx.x * GB_N, m_base = blockIdx.y * GB_M;
   const int tn = (tid % 16) * 4, tm = (tid / 16) * 4;
   constexpr int P = 8 / BITS;
-  constexpr int BPG = GB_K * BITS / 8;  // packed bytes per group per row
+  constexpr int BPG = GB_K * BITS / 8;   // packed bytes per group per row
+  constexpr int BPS = GB_KS * BITS / 8;  // packed bytes per half group
   // Each thread decodes bytes of one fixed weight row (tid % 64).
   const int my_nl = tid % GB_N;
   const uint8_t* my_row = nullptr;
@@ -190,38 +193,40 @@ __global__ void __launch_bounds__(256) cq_gemm_simt_kernel(CqMat W, const float*
 #pragma unroll
     for (int j = 0; j < 4; ++j) total[i][j] = 0.f;
   for (int g = 0; g < W.groups; ++g) {
-    __syncthreads();
-    for (int bi = tid / GB_N; bi < BPG; bi += 256 / GB_N) {
-      uint8_t byte = my_row ? my_row[(size_t)g * BPG + bi] : 0;
-#pragma unroll
-      for (int j = 0; j < P; ++j) Ws[bi * P + j][my_nl] = W.levels[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
-    }
-    if (tid < GB_N) Ns[tid] = my_norm ? __half2float(my_norm[g]) : 0.f;
-    for (int i = tid; i < GB_M * (GB_K / 4); i += 256) {
-      int ml = i % GB_M, k4 = (i / GB_M) * 4;
-      int m = m_base + ml;
-      float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-      if (m < M) v = *reinterpret_cast<const float4*>(xh + (size_t)m * ldx + (size_t)g * GB_K + k4);
-      Xs[k4 + 0][ml] = v.x;
-      Xs[k4 + 1][ml] = v.y;
-      Xs[k4 + 2][ml] = v.z;
-      Xs[k4 + 3][ml] = v.w;
-    }
-    __syncthreads();
     float acc[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i)
 #pragma unroll
       for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
+    for (int hk = 0; hk < GB_K / GB_KS; ++hk) {
+      __syncthreads();
+      for (int bi = tid / GB_N; bi < BPS; bi += 256 / GB_N) {
+        uint8_t byte = my_row ? my_row[(size_t)g * BPG + hk * BPS + bi] : 0;
+#pragma unroll
+        for (int j = 0; j < P; ++j) Ws[bi * P + j][my_nl] = W.levels[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
+      }
+      if (hk == 0 && tid < GB_N) Ns[tid] = my_norm ? __half2float(my_norm[g]) : 0.f;
+      for (int i = tid; i < GB_M * (GB_KS / 4); i += 256) {
+        int ml = i % GB_M, k4 = (i / GB_M) * 4;
+        int m = m_base + ml;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (m < M) v = *reinterpret_cast<const float4*>(xh + (size_t)m * ldx + (size_t)g * GB_K + hk * GB_KS + k4);
+        Xs[k4 + 0][ml] = v.x;
+        Xs[k4 + 1][ml] = v.y;
+        Xs[k4 + 2][ml] = v.z;
+        Xs[k4 + 3][ml] = v.w;
+      }
+      __syncthreads();
 #pragma unroll 8
-    for (int k = 0; k < GB_K; ++k) {
-      float4 a = *reinterpret_cast<const float4*>(&Xs[k][tm]);
-      float4 b = *reinterpret_cast<const float4*>(&Ws[k][tn]);
-      float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
+      for (int k = 0; k < GB_KS; ++k) {
+        float4 a = *reinterpret_cast<const float4*>(&Xs[k][tm]);
+        float4 b = *reinterpret_cast<const float4*>(&Ws[k][tn]);
+        float av[4] = {a.x, a.y, a.z, a.w}, bv[4] = {b.x, b.y, b.z, b.w};
 #pragma unroll
-      for (int i = 0; i < 4; ++i)
+        for (int i = 0; i < 4; ++i)
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
+          for (int j = 0; j < 4; ++j) acc[i][j] += av[i] * bv[j];
+      }
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
@@ -254,10 +259,8 @@ static cudaError_t launch_gemv(const CqMat& W, const float* xh, int ldx, int M, 
   const int grid = (nrows + rows_per_cta - 1) / rows_per_cta;
   const size_t smem = (size_t)(MT * padded_len(W.in_pad, T::E) + 256 * T::COPIES * T::P) * sizeof(float);
   auto kern = cq_gemv_kernel<BITS, LPR, MT>;
-  if (smem > 48 * 1024) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-  }
+  cudaError_t e = allow_smem((const void*)kern, smem);
+  if (e != cudaSuccess) return e;
   kern<<<grid, threads, smem, st>>>(W, xh, ldx, M, y, ldy, row0, nrows);
   return cudaGetLastError();
 }
@@ -300,6 +303,32 @@ static bool cq_args_ok(const CqMat& W, const float* xh, int ldx) {
   for (int i = 0; i < W.nseg; ++i)
     if (reinterpret_cast<uintptr_t>(W.seg[i].packed) & 15) return false;
   return true;
+}
+
+// prepare_input (cq.rs:264-274): zero-pad to a multiple of 128 and rotate
+// every group by the normalised Walsh-Hadamard transform. One warp per group.
+__global__ void cq_prepare_kernel(const float* __restrict__ x, int in_feat, float* __restrict__ xh,
+                                  int ld_out) {
+  const int m = blockIdx.x, g = blockIdx.y, lane = threadIdx.x;
+  float v[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int k = g * 128 + lane * 4 + i;
+    v[i] = k < in_feat ? x[(size_t)m * in_feat + k] : 0.f;
+  }
+  fwht128_warp(v);
+  reinterpret_cast<float4*>(xh + (size_t)m * ld_out + g * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+}
+
+cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out,
+                              cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  const int in_pad = (in_feat + 127) / 128 * 128;
+  if (!x || !xh || in_feat <= 0 || ld_out < in_pad || ld_out % 4 || (reinterpret_cast<uintptr_t>(xh) & 15))
+    return cudaErrorInvalidValue;
+  dim3 grid(M, in_pad / 128);
+  cq_prepare_kernel<<<grid, 32, 0, st>>>(x, in_feat, xh, ld_out);
+  return cudaGetLastError();
 }
 
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,

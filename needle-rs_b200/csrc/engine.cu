@@ -1,0 +1,999 @@
+// Needle-3 engine on one B200: container upload, sessions, batched forward.
+//
+// The container is parsed as crates/needle-infer/src/cact.rs:306-525 and
+// 981-1100 read it, the canon is walked as v3.rs:236-332 walks it and shapes
+// are validated as v3.rs:336-383 validates them. The whole container is then
+// copied to the device once and CQ tensors are read in place.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "engine.hpp"
+
+namespace nb {
+
+#define NB_TRY(expr)                                        \
+  do {                                                      \
+    cudaError_t _e = (expr);                                \
+    if (_e != cudaSuccess) return _e;                       \
+  } while (0)
+
+static std::string cuda_msg(const char* what, cudaError_t e) {
+  return std::string(what) + ": " + cudaGetErrorName(e) + " (" + cudaGetErrorString(e) + ")";
+}
+
+static uint32_t rd32(const uint8_t* p) {
+  return (uint32_t)p[0] | ((uint32_t)p[1] << 8) | ((uint32_t)p[2] << 16) | ((uint32_t)p[3] << 24);
+}
+static uint64_t rd64(const uint8_t* p) { return (uint64_t)rd32(p) | ((uint64_t)rd32(p + 4) << 32); }
+
+static float half_to_float(uint16_t h) {  // exact binary16 -> f32 (math.rs:53-68)
+  uint32_t sign = (uint32_t)(h >> 15) << 31, exp = (h >> 10) & 0x1F, mant = h & 0x3FF, u;
+  if (exp == 0) {
+    float v = (float)mant / (float)(1u << 24);
+    return sign ? -v : v;
+  }
+  u = exp == 31 ? (sign | 0x7F800000u | (mant << 13)) : (sign | ((exp + 112) << 23) | (mant << 13));
+  float f;
+  std::memcpy(&f, &u, 4);
+  return f;
+}
+
+bool HostConfig::is_global(size_t l) const {
+  return std::find(global_layers.begin(), global_layers.end(), (int)l) != global_layers.end();
+}
+size_t HostConfig::span(size_t l) const { return (is_global(l) || window == 0) ? 0 : window; }
+size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
+  size_t per_pos = int8 ? kvh * (qk + vh) + kvh * 8 : kvh * (qk + vh) * 4;
+  size_t total = 0;
+  for (size_t l = 0; l < layers; ++l) {
+    size_t w = span(l);
+    total += (w ? std::min(seq_len, w) : seq_len) * per_pos;
+  }
+  return total;
+}
+
+// ------------------------------------------------------------------ workspace
+void Workspace::release() {
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, attn, oh, projo, gates, fetched, ekv, evc, lm_in,
+                pks, pvs, pk, pv, rows, tokens, next, last_rows};
+  for (void* p : ps)
+    if (p) cudaFree(p);
+  if (logits) cudaFree(logits);
+  if (lm_last) cudaFree(lm_last);
+  *this = Workspace();
+}
+
+bool Engine::ensure_ws(size_t rows, std::string* err) {
+  if (rows <= ws.cap) return true;
+  cudaStreamSynchronize(stream);
+  size_t cap = std::max(rows, ws.cap * 2);
+  ws.release();
+  const size_t d = G.d, dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
+  const size_t S = std::max(1, G.n_sites);
+  struct A {
+    void** p;
+    size_t bytes;
+  } allocs[] = {
+      {(void**)&ws.lanes, cap * G.lanes * d * 4},   {(void**)&ws.u, cap * d * 4},
+      {(void**)&ws.bx, cap * d * 4},                {(void**)&ws.xh, cap * dpad * 4},
+      {(void**)&ws.proj, cap * G.proj_dim * 4},     {(void**)&ws.qpost, cap * G.q_dim * 4},
+      {(void**)&ws.attn, cap * G.o_dim * 4},        {(void**)&ws.oh, cap * opad * 4},
+      {(void**)&ws.projo, cap * d * 4},             {(void**)&ws.gates, cap * 24 * 4},
+      {(void**)&ws.fetched, cap * S * d * 4},       {(void**)&ws.ekv, cap * S * 2 * d * 4},
+      {(void**)&ws.evc, cap * S * d * 4},           {(void**)&ws.lm_in, cap * dpad * 4},
+      {(void**)&ws.pk, cap * G.kvh * G.qk * 4},     {(void**)&ws.pv, cap * G.kvh * G.vh * 4},
+      {(void**)&ws.pks, cap * G.kvh * 4},           {(void**)&ws.pvs, cap * G.kvh * 4},
+      {(void**)&ws.rows, cap * sizeof(RowInfo)},    {(void**)&ws.tokens, cap * 4},
+      {(void**)&ws.next, cap * 4},                  {(void**)&ws.last_rows, cap * 4},
+  };
+  for (auto& a : allocs) {
+    cudaError_t e = cudaMalloc(a.p, std::max<size_t>(a.bytes, 256));
+    if (e != cudaSuccess) {
+      ws.release();
+      *err = cuda_msg("workspace allocation", e);
+      return false;
+    }
+  }
+  ws.cap = cap;
+  epoch++;
+  return true;
+}
+
+// ------------------------------------------------------------------ loading
+namespace {
+struct Loader {
+  const uint8_t* raw;
+  size_t len;
+  std::vector<Record> recs;
+  float codebook[28];
+  std::vector<float> arena;  // f32 parameters, each tensor 16-byte aligned
+  std::string err;
+
+  // FP16/FP32 record -> offset (floats) into the arena (cact.rs:494-524).
+  long floats(size_t i, size_t expect = 0) {
+    const Record& r = recs[i];
+    size_t n;
+    if (r.dtype == 1) {
+      if (r.nbytes % 2) return fail("ragged fp16 blob", i);
+      n = r.nbytes / 2;
+    } else if (r.dtype == 2) {
+      if (r.nbytes % 4) return fail("ragged fp32 blob", i);
+      n = r.nbytes / 4;
+    } else {
+      return fail("expected an fp16/fp32 tensor", i);
+    }
+    if (expect && n != expect) return fail("unexpected element count", i);
+    long off = (long)arena.size();
+    const uint8_t* b = raw + r.offset;
+    for (size_t k = 0; k < n; ++k) {
+      if (r.dtype == 1)
+        arena.push_back(half_to_float((uint16_t)(b[2 * k] | (b[2 * k + 1] << 8))));
+      else {
+        float f;
+        std::memcpy(&f, b + 4 * k, 4);
+        arena.push_back(f);
+      }
+    }
+    while (arena.size() % 4) arena.push_back(0.f);
+    return off;
+  }
+  long fail(const char* m, size_t i) {
+    err = std::string(m) + " (tensor " + std::to_string(i) + ")";
+    return -1;
+  }
+  // CQ record -> CqMat with one segment pointing into the device copy.
+  bool cq(size_t i, const uint8_t* d_blob, CqMat* W) {
+    const Record& r = recs[i];
+    if (r.dtype != 3) return fail("expected a CQ tensor", i) >= 0;
+    if (r.group != 128) return fail("GPU path supports CQ group 128 only", i) >= 0;
+    if (r.bits != 2 && r.bits != 4) return fail("GPU path supports 2- and 4-bit CQ tensors only", i) >= 0;
+    size_t out = r.shape[0], in = r.shape[1];
+    if (!out || !in) return fail("empty CQ shape", i) >= 0;
+    size_t in_pad = (in + 127) / 128 * 128, groups = in_pad / 128, rb = in_pad * r.bits / 8;
+    if (r.nbytes < out * rb + out * groups * 2) return fail("short CQ blob", i) >= 0;
+    if (r.offset % 16) return fail("CQ blob not 16-byte aligned", i) >= 0;
+    std::memset(W, 0, sizeof(*W));
+    W->seg[0].packed = d_blob + r.offset;
+    W->seg[0].norms = reinterpret_cast<const __half*>(d_blob + r.offset + out * rb);
+    W->seg[0].rows = (int)out;
+    W->nseg = 1;
+    W->rows = (int)out;
+    W->in_feat = (int)in;
+    W->in_pad = (int)in_pad;
+    W->row_bytes = (int)rb;
+    W->groups = (int)groups;
+    W->group = 128;
+    W->bits = (int)r.bits;
+    const float* lv = r.bits == 2 ? codebook : codebook + 12;  // cb2 | cb3 | cb4
+    for (int k = 0; k < (1 << r.bits); ++k) W->levels[k] = lv[k];
+    return true;
+  }
+};
+
+bool concat(CqMat* dst, const CqMat& add, std::string* err) {
+  if (dst->nseg == 0) {
+    *dst = add;
+    return true;
+  }
+  if (dst->nseg >= MAX_SEG || dst->in_feat != add.in_feat || dst->bits != add.bits) {
+    *err = "projections to fuse disagree in width or input";
+    return false;
+  }
+  dst->seg[dst->nseg++] = add.seg[0];
+  dst->rows += add.rows;
+  return true;
+}
+}  // namespace
+
+Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
+  if (!raw) {
+    *err = "data was null";
+    return nullptr;
+  }
+  if (len < 196) {
+    *err = "container too short for a v3 header";
+    return nullptr;
+  }
+  uint32_t w[49];
+  for (int i = 0; i < 49; ++i) w[i] = rd32(raw + 4 * i);
+  if (w[0] != 0x05E12A84u) {  // TAG_V3, cact.rs:29-31
+    *err = "not a Needle 3 container (bad tag)";
+    return nullptr;
+  }
+  if (w[2] != 28) {
+    *err = "bad codebook length";
+    return nullptr;
+  }
+  Loader L{raw, len, {}, {}, {}, ""};
+  std::memcpy(L.codebook, raw + 196, 28 * 4);
+  const size_t nt = w[1], dir = 196 + 28 * 4;
+  if (len < dir + nt * 44) {
+    *err = "container too short for its directory";
+    return nullptr;
+  }
+  for (size_t i = 0; i < nt; ++i) {
+    const uint8_t* b = raw + dir + i * 44;
+    Record r;
+    r.dtype = b[0];
+    r.ndim = b[1];
+    if (r.ndim > 4) {
+      *err = "bad ndim in directory";
+      return nullptr;
+    }
+    for (int k = 0; k < 4; ++k) r.shape[k] = rd32(b + 4 + 4 * k);
+    r.offset = rd64(b + 20);
+    r.nbytes = rd64(b + 28);
+    r.group = rd32(b + 36);
+    r.bits = rd32(b + 40);
+    if (r.offset + r.nbytes > len || r.offset + r.nbytes < r.offset) {
+      *err = "blob out of range (tensor " + std::to_string(i) + ")";
+      return nullptr;
+    }
+    L.recs.push_back(r);
+  }
+  std::unique_ptr<Engine> E(new Engine());
+  HostConfig& c = E->cfg;
+  c.num_tensors = nt;
+  c.kv_window = w[3];
+  c.kv_bits = w[4];
+  c.vocab = w[5];
+  c.out_vocab = w[6];
+  c.d = w[7];
+  c.heads = w[8];
+  c.kvh = w[9];
+  c.layers = w[10];
+  c.qk = w[11];
+  c.vh = w[12];
+  c.max_seq = w[13];
+  c.hada_n = w[14];
+  c.lanes = w[15];
+  c.window = w[16];
+  uint64_t gmask = (uint64_t)w[17] | ((uint64_t)w[18] << 32);
+  for (size_t i = 0; i < c.layers && i < 64; ++i)
+    if ((gmask >> i) & 1) c.global_layers.push_back((int)i);
+  c.taps = w[19];
+  c.e_slots = w[20];
+  c.e_sub = w[21];
+  c.e_tables = w[22];
+  c.e_taps = w[23];
+  c.e_dil = w[24];
+  c.e_seed_heads = w[25];
+  for (size_t k = 0; k < std::min<size_t>(w[26], 4); ++k) c.orders.push_back((int)w[27 + k]);
+  for (size_t k = 0; k < std::min<size_t>(w[31], 16); ++k) c.sites.push_back((int)w[32 + k]);
+  std::memcpy(&c.rope_theta, &w[48], 4);
+  // config_from_geometry (v3.rs:25-70)
+  if (c.orders.empty()) {
+    *err = "container declares no engram orders";
+    return nullptr;
+  }
+  if (c.e_tables % c.orders.size()) {
+    *err = "engram tables not divisible by orders";
+    return nullptr;
+  }
+  c.e_heads = c.e_tables / c.orders.size();
+  if (c.e_heads == 0 || c.d / (c.orders.size() * c.e_heads) != c.e_sub) {
+    *err = "engram sub_dim disagrees with d_model / (orders * heads)";
+    return nullptr;
+  }
+  if (c.kvh == 0 || c.heads % c.kvh) {
+    *err = "query heads do not divide into kv heads";
+    return nullptr;
+  }
+  // Limits of this GPU path (checked, not assumed).
+  if (c.d % 128 || c.e_sub != 128 || c.e_tables * 128 != c.d || (c.lanes != 1 && c.lanes != 2 && c.lanes != 4) ||
+      c.heads / c.kvh > 8 || (c.qk != 16 && c.qk != 32 && c.qk != 48 && c.qk != 64) || c.vh > 64 ||
+      c.vh % 2 || (c.heads / c.kvh) * c.vh > 512 || c.hada_n > 1024 || c.hada_n < c.d ||
+      (c.hada_n & (c.hada_n - 1)) || c.sites.size() > 16 || c.max_seq == 0 ||
+      c.heads * c.vh % 128 || c.out_vocab > c.vocab) {
+    *err = "geometry outside what this GPU path supports";
+    return nullptr;
+  }
+
+  // Canon walk (v3.rs:236-332).
+  size_t cur = 0;
+  auto take = [&](size_t* idx) -> bool {
+    if (cur >= nt) return false;
+    *idx = cur++;
+    return true;
+  };
+  auto shape2 = [&](size_t i, size_t a, size_t b) { return L.recs[i].shape[0] == a && L.recs[i].shape[1] == b; };
+  const size_t qd = c.heads * c.qk, kd = c.kvh * c.qk, vd = c.kvh * c.vh, od = c.heads * c.vh, d = c.d;
+  struct LayerIdx {
+    size_t norm_in, q, k, v, qt, kt, vt, qn, kn, gate, out, post, agate, pre, mlp[13];
+  };
+  std::vector<LayerIdx> li(c.layers);
+  size_t emb;
+  bool ok = take(&emb);
+  for (size_t l = 0; ok && l < c.layers; ++l) {
+    LayerIdx& x = li[l];
+    ok = take(&x.norm_in) && take(&x.q) && take(&x.k) && take(&x.v);
+    if (ok && c.taps) ok = take(&x.qt) && take(&x.kt) && take(&x.vt);
+    ok = ok && take(&x.qn) && take(&x.kn) && take(&x.gate) && take(&x.out) && take(&x.post) &&
+         take(&x.agate) && take(&x.pre);
+    for (int j = 0; ok && j < 13; ++j) ok = take(&x.mlp[j]);
+  }
+  size_t sc[6], phi[3], perm[2];
+  for (int j = 0; ok && j < 6; ++j) ok = take(&sc[j]);
+  for (int j = 0; ok && j < 3; ++j) ok = take(&phi[j]);
+  for (int j = 0; ok && j < 2; ++j) ok = take(&perm[j]);
+  std::vector<size_t> et(c.sites.size()), ek(c.sites.size()), ev(c.sites.size()), etap(c.sites.size());
+  for (size_t s = 0; ok && s < c.sites.size(); ++s) ok = take(&et[s]) && take(&ek[s]) && take(&ev[s]) && take(&etap[s]);
+  size_t fn = 0;
+  ok = ok && take(&fn);
+  if (!ok) {
+    *err = "directory has fewer tensors than the canon needs";
+    return nullptr;
+  }
+  c.has_heads = false;
+  for (size_t i = cur; i < nt; ++i)
+    if (L.recs[i].dtype != 4) c.has_heads = true;
+  // Shape validation (v3.rs:336-383).
+  const char* bad = nullptr;
+  if (!shape2(emb, c.vocab, d)) bad = "embedding";
+  for (size_t l = 0; !bad && l < c.layers; ++l) {
+    if (!shape2(li[l].q, qd, d)) bad = "q_proj";
+    else if (!shape2(li[l].k, kd, d)) bad = "k_proj";
+    else if (!shape2(li[l].v, vd, d)) bad = "v_proj";
+    else if (!shape2(li[l].gate, od, d)) bad = "gate_proj";
+    else if (!shape2(li[l].out, d, od)) bad = "out_proj";
+  }
+  for (size_t s = 0; !bad && s < c.sites.size(); ++s) {
+    if (!shape2(et[s], c.e_tables * c.e_slots, c.e_sub)) bad = "engram tables";
+    else if (!shape2(ek[s], d, d)) bad = "engram key_proj";
+    else if (!shape2(ev[s], d, d)) bad = "engram value_proj";
+  }
+  if (!bad && !(shape2(phi[0], c.layers * c.lanes, c.lanes * d) && shape2(phi[1], c.layers * c.lanes, c.lanes * d) &&
+                shape2(phi[2], c.layers * c.lanes * c.lanes, c.lanes * d)))
+    bad = "mhc phi";
+  if (bad) {
+    *err = std::string("tensor shape does not match the geometry: ") + bad;
+    return nullptr;
+  }
+
+  // Device upload of the container.
+  cudaError_t e = cudaGetDevice(&E->device);
+  if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = cudaMalloc(&E->d_blob, len);
+  if (e == cudaSuccess) e = cudaMemcpy(E->d_blob, raw, len, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("uploading the container", e);
+    return nullptr;
+  }
+  // f32 parameter arena.
+  struct LOff {
+    long norm_in, qt, kt, vt, qn, kn, post, pre, mlp[13];
+    float agate;
+  };
+  std::vector<LOff> lo(c.layers);
+  const size_t n = c.hada_n;
+  size_t ba, bb;
+  {
+    size_t v = n - 1, bits = 0;
+    while (v) {
+      ++bits;
+      v >>= 1;
+    }
+    ba = (size_t)1 << (bits / 2);  // hada_blocks, v3/kernels.rs:26-34
+    bb = n / ba;
+  }
+  for (size_t l = 0; l < c.layers && L.err.empty(); ++l) {
+    LOff& o = lo[l];
+    o.norm_in = L.floats(li[l].norm_in, d);
+    if (c.taps) {
+      o.qt = L.floats(li[l].qt, c.taps * qd);
+      o.kt = L.floats(li[l].kt, c.taps * kd);
+      o.vt = L.floats(li[l].vt, c.taps * vd);
+    }
+    o.qn = L.floats(li[l].qn, c.qk);
+    o.kn = L.floats(li[l].kn, c.qk);
+    o.post = L.floats(li[l].post, d);
+    long ag = L.floats(li[l].agate);
+    o.agate = ag >= 0 ? L.arena[ag] : 0.f;
+    o.pre = L.floats(li[l].pre, d);
+    const size_t expect[13] = {n, n, n, n, n, ba * ba, bb * bb, ba * ba, bb * bb, ba * ba, bb * bb, 0, 0};
+    for (int j = 0; j < 13; ++j) o.mlp[j] = L.floats(li[l].mlp[j], expect[j]);
+  }
+  size_t rank = c.layers ? L.recs[li[0].mlp[11]].shape[1] : 0;
+  if (rank == 0 || rank > 8) L.err = L.err.empty() ? "HadamardMLP conditioning rank outside 1..8" : L.err;
+  long a_pre = L.floats(sc[0], c.layers), a_post = L.floats(sc[1], c.layers), a_res = L.floats(sc[2], c.layers);
+  long b_pre = L.floats(sc[3], c.layers * c.lanes), b_post = L.floats(sc[4], c.layers * c.lanes);
+  long b_res = L.floats(sc[5], c.layers * c.lanes * c.lanes);
+  std::vector<long> etaps(c.sites.size());
+  for (size_t s = 0; s < c.sites.size(); ++s) etaps[s] = L.floats(etap[s], c.e_taps * d);
+  long fnorm = L.floats(fn, d);
+  long p1 = L.floats(perm[0], n), p2 = L.floats(perm[1], n);
+  if (!L.err.empty()) {
+    *err = L.err;
+    return nullptr;
+  }
+  std::vector<uint32_t> perms(2 * n);
+  for (size_t i = 0; i < n; ++i) {
+    perms[i] = (uint32_t)L.arena[p1 + i];  // `x as u32`, v3.rs:474-478
+    perms[n + i] = (uint32_t)L.arena[p2 + i];
+    if (perms[i] >= n || perms[n + i] >= n) {
+      *err = "hadamard permutation entry out of range";
+      return nullptr;
+    }
+  }
+  // RoPE table [2][max_seq][half] with the reference's f32 formula (model.rs:378-393).
+  const size_t half = c.qk / 2;
+  std::vector<float> rope(2 * c.max_seq * half);
+  for (size_t i = 0; i < half; ++i) {
+    float freq = 1.0f / powf(c.rope_theta, (float)(2 * i) / (float)c.qk);
+    for (size_t p = 0; p < c.max_seq; ++p) {
+      float ang = (float)p * freq;
+      rope[p * half + i] = cosf(ang);
+      rope[c.max_seq * half + p * half + i] = sinf(ang);
+    }
+  }
+  e = cudaMalloc(&E->d_params, L.arena.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(E->d_params, L.arena.data(), L.arena.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&E->d_perm, perms.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(E->d_perm, perms.data(), perms.size() * 4, cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&E->d_rope, rope.size() * 4);
+  if (e == cudaSuccess) e = cudaMemcpy(E->d_rope, rope.data(), rope.size() * 4, cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("uploading parameters", e);
+    return nullptr;
+  }
+  const float* P = E->d_params;
+  auto pp = [&](long off) -> const float* { return off >= 0 ? P + off : nullptr; };
+  // CQ tensors.
+  bool okc = L.cq(emb, E->d_blob, &E->emb) && L.cq(phi[0], E->d_blob, &E->phi_pre) &&
+             L.cq(phi[1], E->d_blob, &E->phi_post) && L.cq(phi[2], E->d_blob, &E->phi_res);
+  E->qkvg.resize(c.layers);
+  E->outp.resize(c.layers);
+  for (size_t l = 0; okc && l < c.layers; ++l) {
+    CqMat q, k, v, g;
+    okc = L.cq(li[l].q, E->d_blob, &q) && L.cq(li[l].k, E->d_blob, &k) && L.cq(li[l].v, E->d_blob, &v) &&
+          L.cq(li[l].gate, E->d_blob, &g) && L.cq(li[l].out, E->d_blob, &E->outp[l]);
+    std::memset(&E->qkvg[l], 0, sizeof(CqMat));
+    okc = okc && concat(&E->qkvg[l], q, err) && concat(&E->qkvg[l], k, err) && concat(&E->qkvg[l], v, err) &&
+          concat(&E->qkvg[l], g, err);
+  }
+  E->eng_kv.resize(c.sites.size());
+  E->eng_tables.resize(c.sites.size());
+  for (size_t s = 0; okc && s < c.sites.size(); ++s) {
+    CqMat k, v;
+    okc = L.cq(et[s], E->d_blob, &E->eng_tables[s]) && L.cq(ek[s], E->d_blob, &k) && L.cq(ev[s], E->d_blob, &v);
+    std::memset(&E->eng_kv[s], 0, sizeof(CqMat));
+    okc = okc && concat(&E->eng_kv[s], k, err) && concat(&E->eng_kv[s], v, err);
+  }
+  if (!okc) {
+    if (err->empty()) *err = L.err;
+    return nullptr;
+  }
+  if (!c.sites.empty()) {
+    e = cudaMalloc(&E->d_tables, c.sites.size() * sizeof(CqMat));
+    if (e == cudaSuccess)
+      e = cudaMemcpy(E->d_tables, E->eng_tables.data(), c.sites.size() * sizeof(CqMat), cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("uploading engram tables", e);
+      return nullptr;
+    }
+  }
+  E->lp.resize(c.layers);
+  E->mp.resize(c.layers);
+  E->site_of.assign(c.layers, -1);
+  for (size_t s = 0; s < c.sites.size(); ++s)
+    if ((size_t)c.sites[s] < c.layers) E->site_of[c.sites[s]] = (int)s;
+  for (size_t l = 0; l < c.layers; ++l) {
+    LayerParams& x = E->lp[l];
+    const LOff& o = lo[l];
+    x.norm_in = pp(o.norm_in);
+    x.q_taps = c.taps ? pp(o.qt) : nullptr;
+    x.k_taps = c.taps ? pp(o.kt) : nullptr;
+    x.v_taps = c.taps ? pp(o.vt) : nullptr;
+    x.q_norm = pp(o.qn);
+    x.k_norm = pp(o.kn);
+    x.post_norm = pp(o.post);
+    x.pre_hada = pp(o.pre);
+    x.attn_gate = o.agate;
+    x.d1 = pp(o.mlp[0]);
+    x.d2 = pp(o.mlp[1]);
+    x.b2 = pp(o.mlp[2]);
+    x.d3 = pp(o.mlp[3]);
+    x.d4 = pp(o.mlp[4]);
+    x.w1a = pp(o.mlp[5]);
+    x.w1b = pp(o.mlp[6]);
+    x.w2a = pp(o.mlp[7]);
+    x.w2b = pp(o.mlp[8]);
+    x.w3a = pp(o.mlp[9]);
+    x.w3b = pp(o.mlp[10]);
+    x.cond_v = pp(o.mlp[11]);
+    x.cond_u = pp(o.mlp[12]);
+    x.window = (int)c.span(l);
+    MhcParams& m = E->mp[l];
+    m.a_pre = L.arena[a_pre + l];
+    m.a_post = L.arena[a_post + l];
+    m.a_res = L.arena[a_res + l];
+    m.b_pre = P + b_pre + l * c.lanes;
+    m.b_post = P + b_post + l * c.lanes;
+    m.b_res = P + b_res + l * c.lanes * c.lanes;
+  }
+  for (size_t s = 0; s < c.sites.size(); ++s) E->eng_taps.push_back(P + etaps[s]);
+  E->final_norm = P + fnorm;
+
+  Geo& g = E->G;
+  g.d = (int)d;
+  g.heads = (int)c.heads;
+  g.kvh = (int)c.kvh;
+  g.qk = (int)c.qk;
+  g.vh = (int)c.vh;
+  g.layers = (int)c.layers;
+  g.lanes = (int)c.lanes;
+  g.hada_n = (int)n;
+  g.ba = (int)ba;
+  g.bb = (int)bb;
+  g.taps = (int)c.taps;
+  g.window = (int)c.window;
+  g.max_seq = (int)c.max_seq;
+  g.vocab = (int)c.vocab;
+  g.logit_rows = (int)c.logit_rows();
+  g.q_dim = (int)qd;
+  g.k_dim = (int)kd;
+  g.v_dim = (int)vd;
+  g.o_dim = (int)od;
+  g.qkv_dim = (int)(qd + kd + vd);
+  g.proj_dim = (int)(qd + kd + vd + od);
+  g.e_tables = (int)c.e_tables;
+  g.e_heads = (int)c.e_heads;
+  g.e_slots = (int)c.e_slots;
+  g.e_sub = (int)c.e_sub;
+  g.e_taps = (int)c.e_taps;
+  g.e_dil = (int)c.e_dil;
+  int mo = 1;
+  for (int o : c.orders) mo = std::max(mo, o);
+  g.e_maxorder = mo;
+  g.e_reach = (int)((c.e_taps > 0 ? c.e_taps - 1 : 0) * c.e_dil);
+  g.e_stride = (int)(c.e_seed_heads == 0 ? c.e_heads : c.e_seed_heads);
+  g.n_orders = (int)c.orders.size();
+  g.n_sites = (int)c.sites.size();
+  for (int k = 0; k < 4; ++k) g.orders[k] = k < (int)c.orders.size() ? c.orders[k] : 0;
+  g.cond_rank = (int)rank;
+  g.embed_scale = sqrtf((float)d);  // model.rs:131
+  if (mo > 4) {
+    *err = "engram order above 4 exceeds the token ring";
+    return nullptr;
+  }
+  return E.release();
+}
+
+Engine::~Engine() {
+  if (stream) cudaStreamSynchronize(stream);
+  ws.release();
+  if (d_blob) cudaFree(d_blob);
+  if (d_params) cudaFree(d_params);
+  if (d_perm) cudaFree(d_perm);
+  if (d_rope) cudaFree(d_rope);
+  if (d_tables) cudaFree(d_tables);
+  if (stream) cudaStreamDestroy(stream);
+}
+
+// ------------------------------------------------------------------ sessions
+static size_t kv_elem_bytes(const Session* s) { return s->int8 ? 1 : 4; }
+
+static cudaError_t alloc_layer(const Engine* E, bool int8, int slots, int cap, LayerKV* L) {
+  const Geo& g = E->G;
+  const size_t eb = int8 ? 1 : 4;
+  std::memset(L, 0, sizeof(*L));
+  L->slots = slots;
+  L->cap = cap;
+  NB_TRY(cudaMalloc(&L->k, std::max<size_t>((size_t)g.kvh * slots * g.qk * eb, 16)));
+  NB_TRY(cudaMalloc(&L->v, std::max<size_t>((size_t)g.kvh * slots * g.vh * eb, 16)));
+  NB_TRY(cudaMemset(L->k, 0, (size_t)g.kvh * slots * g.qk * eb));
+  NB_TRY(cudaMemset(L->v, 0, (size_t)g.kvh * slots * g.vh * eb));
+  if (int8) {
+    NB_TRY(cudaMalloc(&L->ks, std::max<size_t>((size_t)g.kvh * slots * 4, 16)));
+    NB_TRY(cudaMalloc(&L->vs, std::max<size_t>((size_t)g.kvh * slots * 4, 16)));
+    NB_TRY(cudaMemset(L->ks, 0, (size_t)g.kvh * slots * 4));
+    NB_TRY(cudaMemset(L->vs, 0, (size_t)g.kvh * slots * 4));
+  }
+  return cudaSuccess;
+}
+
+static void free_layer(LayerKV* L) {
+  if (L->k) cudaFree(L->k);
+  if (L->v) cudaFree(L->v);
+  if (L->ks) cudaFree(L->ks);
+  if (L->vs) cudaFree(L->vs);
+  std::memset(L, 0, sizeof(*L));
+}
+
+Session::~Session() {
+  if (eng) cudaStreamSynchronize(eng->stream);
+  for (LayerKV& l : layers) free_layer(&l);
+  if (d_layers) cudaFree(d_layers);
+  if (d_desc) cudaFree(d_desc);
+  if (d_state) cudaFree(d_state);
+}
+
+size_t Session::bytes() const {  // as V3Cache::bytes counts (cache.rs:255-268)
+  size_t t = state_bytes;
+  const Geo& g = eng->G;
+  for (const LayerKV& l : layers)
+    t += (size_t)g.kvh * l.slots * (g.qk + g.vh) * kv_elem_bytes(this) + (int8 ? (size_t)g.kvh * l.slots * 8 : 0);
+  return t;
+}
+
+Session* Engine::new_session(size_t hint, bool int8, std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  std::unique_ptr<Session> s(new Session());
+  s->eng = this;
+  s->int8 = int8;
+  hint = std::min(std::max<size_t>(hint, 1), cfg.max_seq);  // cache.rs:178
+  s->hint = hint;
+  s->layers.resize(cfg.layers);
+  for (size_t l = 0; l < cfg.layers; ++l) {
+    size_t w = cfg.span(l);
+    int cap = (int)(w ? std::min(w, cfg.max_seq) : cfg.max_seq);
+    int slots = (int)std::min<size_t>(hint, (size_t)cap);
+    cudaError_t e = alloc_layer(this, int8, slots, cap, &s->layers[l]);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("allocating the KV cache", e);
+      return nullptr;
+    }
+  }
+  const size_t tl = G.taps > 0 ? G.taps - 1 : 0;
+  const size_t qkv_tail = cfg.layers * tl * G.qkv_dim, eng_tail = (size_t)G.n_sites * G.e_reach * G.d;
+  s->state_bytes = (qkv_tail + eng_tail) * 4 + 4 * 4;
+  SessDesc h{};
+  cudaError_t e = cudaMalloc(&s->d_state, s->state_bytes);
+  if (e == cudaSuccess) e = cudaMemset(s->d_state, 0, s->state_bytes);
+  if (e == cudaSuccess) e = cudaMalloc(&s->d_layers, cfg.layers * sizeof(LayerKV));
+  if (e == cudaSuccess)
+    e = cudaMemcpy(s->d_layers, s->layers.data(), cfg.layers * sizeof(LayerKV), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&s->d_desc, sizeof(SessDesc));
+  if (e != cudaSuccess) {
+    *err = cuda_msg("allocating session state", e);
+    return nullptr;
+  }
+  h.pos = 0;
+  h.int8 = int8 ? 1 : 0;
+  h.layers = s->d_layers;
+  h.qkv_tail = (float*)s->d_state;
+  h.eng_tail = (float*)s->d_state + qkv_tail;
+  h.toks = (uint32_t*)((float*)s->d_state + qkv_tail + eng_tail);
+  e = cudaMemcpy(s->d_desc, &h, sizeof(h), cudaMemcpyHostToDevice);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("writing the session descriptor", e);
+    return nullptr;
+  }
+  return s.release();
+}
+
+// Grow every layer ring so `pos` is addressable, doubling up to the layer's
+// cap exactly as V3Cache::ensure does (cache.rs:291-309); a local layer at its
+// window wraps instead. Old contents are kept: while a ring is below its cap
+// the slot of position p is p itself.
+bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
+  bool changed = false;
+  const size_t eb = kv_elem_bytes(s);
+  for (size_t l = 0; l < cfg.layers; ++l) {
+    LayerKV& L = s->layers[l];
+    if ((int)pos < L.slots || L.slots >= L.cap) continue;
+    int want = L.slots;
+    while ((int)pos >= want && want < L.cap) want = std::min(std::max(want * 2, want + 1), L.cap);
+    LayerKV N;
+    cudaError_t e = alloc_layer(this, s->int8, want, L.cap, &N);
+    auto copy2d = [&](void* dst, const void* src, size_t row) {
+      return cudaMemcpy2DAsync(dst, want * row, src, L.slots * row, L.slots * row, G.kvh,
+                               cudaMemcpyDeviceToDevice, stream);
+    };
+    if (e == cudaSuccess) e = copy2d(N.k, L.k, G.qk * eb);
+    if (e == cudaSuccess) e = copy2d(N.v, L.v, G.vh * eb);
+    if (e == cudaSuccess && s->int8) e = copy2d(N.ks, L.ks, 4);
+    if (e == cudaSuccess && s->int8) e = copy2d(N.vs, L.vs, 4);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+      free_layer(&N);
+      *err = cuda_msg("growing the KV ring", e);
+      return false;
+    }
+    free_layer(&L);
+    L = N;
+    changed = true;
+  }
+  if (changed) {
+    cudaError_t e = cudaMemcpyAsync(s->d_layers, s->layers.data(), cfg.layers * sizeof(LayerKV),
+                                    cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("updating the session descriptor", e);
+      return false;
+    }
+    epoch++;
+  }
+  return true;
+}
+
+// ------------------------------------------------------------------ forward
+cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8) {
+  const int M = rb.M, d = G.d, S = G.n_sites;
+  const int dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
+  if (S > 0) {
+    NB_TRY(launch_engram_gather(G, d_tables, rb, ws.fetched, st));
+    for (int s = 0; s < S; ++s)
+      NB_TRY(cq_project(eng_kv[s], ws.fetched + (size_t)s * d, S * d, M, ws.ekv + (size_t)s * 2 * d,
+                        S * 2 * d, 0, 2 * d, st));
+    NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, ws.ekv, ws.evc, st));
+  }
+  NB_TRY(launch_embed(G, emb, rb, ws.lanes, st));
+  for (int l = 0; l < G.layers; ++l) {
+    NB_TRY(launch_layer_pre(G, l, rb, ws.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
+                            site_of[l], ws.ekv, ws.evc, ws.u, ws.bx, ws.xh, ws.gates, st));
+    NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st));
+    NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, st));
+    NB_TRY(launch_attention(G, l, rb, lp[l], ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, ws.attn, st, int8 ? 1 : 0));
+    NB_TRY(launch_attn_finish(G, rb, ws.attn, ws.proj, ws.oh, st));
+    NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st));
+    NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, ws.projo, ws.u, ws.bx,
+                             ws.gates, ws.lanes, st));
+  }
+  NB_TRY(launch_final(G, rb, ws.lanes, final_norm, ws.lm_in, st));
+  return cudaSuccess;
+}
+
+// Tied head over logit_rows (model.rs:358-374, :942-978) and the greedy pick.
+cudaError_t Engine::head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
+                         cudaStream_t st) {
+  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st));
+  if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
+  return cudaSuccess;
+}
+
+static bool ensure_logits(Engine* E, size_t rows, std::string* err) {
+  if (rows <= E->ws.last_cap) return true;
+  if (E->ws.logits) cudaFree(E->ws.logits);
+  if (E->ws.lm_last) cudaFree(E->ws.lm_last);
+  E->ws.logits = nullptr;
+  E->ws.lm_last = nullptr;
+  size_t cap = std::max(rows, E->ws.last_cap * 2);
+  cudaError_t e = cudaMalloc(&E->ws.logits, cap * E->G.logit_rows * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&E->ws.lm_last, cap * ((E->G.d + 127) / 128 * 128) * 4);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("allocating logits", e);
+    E->ws.last_cap = 0;
+    return false;
+  }
+  E->ws.last_cap = cap;
+  E->epoch++;
+  return true;
+}
+
+static constexpr size_t MAX_PREFILL_ROWS = 16384;
+
+bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_t* lens, size_t n,
+                     float* logits, uint32_t* picks, std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  if (n == 0) return true;
+  for (size_t i = 0; i < n; ++i) {
+    if (!ss[i] || ss[i]->eng != this) {
+      *err = "session does not belong to this handle";
+      return false;
+    }
+    if (ss[i]->pos != 0) {
+      *err = "prefill needs a fresh session (position 0)";
+      return false;
+    }
+    if (lens[i] == 0 || lens[i] > cfg.max_seq) {
+      *err = "prompt length must be in 1..max_seq_len";
+      return false;
+    }
+    if (ss[i]->int8 != ss[0]->int8) {
+      *err = "a batch must share one KV precision";
+      return false;
+    }
+  }
+  const int dpad = (G.d + 127) / 128 * 128;
+  size_t i0 = 0;
+  while (i0 < n) {
+    // Group whole prompts so one forward holds at most MAX_PREFILL_ROWS rows.
+    size_t i1 = i0, rows = 0;
+    while (i1 < n && (i1 == i0 || rows + lens[i1] <= MAX_PREFILL_ROWS)) rows += lens[i1++];
+    for (size_t i = i0; i < i1; ++i)
+      if (!ensure_slots(ss[i], lens[i] - 1, err)) return false;
+    if (!ensure_ws(rows, err) || !ensure_logits(this, i1 - i0, err)) return false;
+    std::vector<RowInfo> ri(rows);
+    std::vector<uint32_t> tok(rows);
+    std::vector<int> last(i1 - i0);
+    size_t r = 0;
+    for (size_t i = i0; i < i1; ++i) {
+      for (size_t p = 0; p < lens[i]; ++p, ++r) {
+        ri[r] = RowInfo{ss[i]->d_desc, (int)p, (int)(r - p), (int)lens[i], 0};
+        tok[r] = ids[i][p];
+      }
+      last[i - i0] = (int)(r - 1);
+    }
+    cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), rows * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tok.data(), rows * 4, cudaMemcpyHostToDevice, stream);
+    RowBatch rb{ws.rows, ws.tokens, (int)rows, MODE_PREFILL};
+    if (e == cudaSuccess) e = forward(rb, stream, ss[i0]->int8);
+    if (e == cudaSuccess) e = launch_step_end(rb, stream);
+    for (size_t i = 0; e == cudaSuccess && i < i1 - i0; ++i)
+      e = cudaMemcpyAsync(ws.lm_last + i * dpad, ws.lm_in + (size_t)last[i] * dpad, dpad * 4,
+                          cudaMemcpyDeviceToDevice, stream);
+    if (e == cudaSuccess) e = head(ws.lm_last, dpad, (int)(i1 - i0), ws.logits, ws.next, stream);
+    if (e == cudaSuccess && logits)
+      e = cudaMemcpyAsync(logits + i0 * G.logit_rows, ws.logits, (i1 - i0) * G.logit_rows * 4,
+                          cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess && picks)
+      e = cudaMemcpyAsync(picks + i0, ws.next, (i1 - i0) * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("prefill", e);
+      return false;
+    }
+    for (size_t i = i0; i < i1; ++i) ss[i]->pos = lens[i];
+    i0 = i1;
+  }
+  return true;
+}
+
+bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float* logits,
+                    uint32_t* picks, std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  if (n == 0) return true;
+  for (size_t i = 0; i < n; ++i) {
+    if (!ss[i] || ss[i]->eng != this) {
+      *err = "session does not belong to this handle";
+      return false;
+    }
+    if (ss[i]->int8 != ss[0]->int8) {
+      *err = "a batch must share one KV precision";
+      return false;
+    }
+    if (ss[i]->pos >= cfg.max_seq) {
+      *err = "session reached max_seq_len";
+      return false;
+    }
+    for (size_t j = 0; j < i; ++j)
+      if (ss[j] == ss[i]) {
+        *err = "a session appears twice in one decode batch";
+        return false;
+      }
+    if (!ensure_slots(ss[i], ss[i]->pos, err)) return false;
+  }
+  if (!ensure_ws(n, err) || !ensure_logits(this, n, err)) return false;
+  std::vector<RowInfo> ri(n);
+  for (size_t i = 0; i < n; ++i) ri[i] = RowInfo{ss[i]->d_desc, (int)ss[i]->pos, -1, -1, 0};
+  const int dpad = (G.d + 127) / 128 * 128;
+  cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), n * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tokens, n * 4, cudaMemcpyHostToDevice, stream);
+  RowBatch rb{ws.rows, ws.tokens, (int)n, MODE_DECODE};
+  if (e == cudaSuccess) e = forward(rb, stream, ss[0]->int8);
+  if (e == cudaSuccess) e = launch_step_end(rb, stream);
+  if (e == cudaSuccess) e = head(ws.lm_in, dpad, (int)n, ws.logits, ws.next, stream);
+  if (e == cudaSuccess && logits)
+    e = cudaMemcpyAsync(logits, ws.logits, n * G.logit_rows * 4, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess && picks) e = cudaMemcpyAsync(picks, ws.next, n * 4, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("decode step", e);
+    return false;
+  }
+  for (size_t i = 0; i < n; ++i) ss[i]->pos += 1;
+  return true;
+}
+
+// ------------------------------------------------------------------ batches
+Batch::~Batch() {
+  if (graph) cudaGraphExecDestroy(graph);
+  if (d_sess) cudaFree(d_sess);
+  if (d_tok) cudaFree(d_tok);
+  if (d_next) cudaFree(d_next);
+}
+
+Batch* Engine::new_batch(Session* const* ss, size_t n, std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  if (n == 0) {
+    *err = "empty batch";
+    return nullptr;
+  }
+  std::unique_ptr<Batch> b(new Batch());
+  b->eng = this;
+  std::vector<SessDesc*> descs(n);
+  for (size_t i = 0; i < n; ++i) {
+    if (!ss[i] || ss[i]->eng != this) {
+      *err = "session does not belong to this handle";
+      return nullptr;
+    }
+    if (ss[i]->int8 != ss[0]->int8) {
+      *err = "a batch must share one KV precision";
+      return nullptr;
+    }
+    for (size_t j = 0; j < i; ++j)
+      if (ss[j] == ss[i]) {
+        *err = "a session appears twice in one batch";
+        return nullptr;
+      }
+    descs[i] = ss[i]->d_desc;
+  }
+  b->sessions.assign(ss, ss + n);
+  b->int8 = ss[0]->int8;
+  cudaError_t e = cudaMalloc(&b->d_sess, n * sizeof(SessDesc*));
+  if (e == cudaSuccess) e = cudaMemcpy(b->d_sess, descs.data(), n * sizeof(SessDesc*), cudaMemcpyHostToDevice);
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_tok, n * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&b->d_next, n * 4);
+  if (e == cudaSuccess) e = cudaMemset(b->d_tok, 0, n * 4);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("allocating the batch", e);
+    return nullptr;
+  }
+  return b.release();
+}
+
+bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, bool use_graph,
+                                 std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  const size_t n = b->sessions.size();
+  for (Session* s : b->sessions) {
+    if (s->pos >= cfg.max_seq) {
+      *err = "session reached max_seq_len";
+      return false;
+    }
+    if (!ensure_slots(s, s->pos, err)) return false;
+  }
+  if (!ensure_ws(n, err)) return false;
+  const int dpad = (G.d + 127) / 128 * 128;
+  float* lg = d_logits;
+  if (!lg) {
+    if (!ensure_logits(this, n, err)) return false;
+    lg = ws.logits;
+  }
+  RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
+  auto body = [&](cudaStream_t s) -> cudaError_t {
+    NB_TRY(launch_step_begin(rb, b->d_sess, s));
+    NB_TRY(forward(rb, s, b->int8));
+    NB_TRY(launch_step_end(rb, s));
+    NB_TRY(head(ws.lm_in, dpad, (int)n, lg, b->d_next, s));
+    return cudaSuccess;
+  };
+  cudaError_t e = cudaSuccess;
+  // The graph bakes in workspace and ring pointers: it is rebuilt whenever one
+  // of them changed (epoch) or the logits target changed. A rebuild is preceded
+  // by one eager step at the same epoch, so every one-time setup (shared-memory
+  // opt-ins) has happened before capture begins.
+  const bool graph_ok = b->graph && b->graph_epoch == epoch && b->graph_logits == (d_logits != nullptr);
+  if (use_graph && graph_ok) {
+    e = cudaGraphLaunch(b->graph, st);
+  } else if (use_graph && b->warm_epoch == epoch) {
+    if (b->graph) {
+      cudaGraphExecDestroy(b->graph);
+      b->graph = nullptr;
+    }
+    cudaGraph_t g = nullptr;
+    e = cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal);
+    if (e == cudaSuccess) {
+      cudaError_t eb = body(st);
+      e = cudaStreamEndCapture(st, &g);
+      if (eb != cudaSuccess) e = eb;
+    }
+    if (e == cudaSuccess) e = cudaGraphInstantiate(&b->graph, g, 0);
+    if (g) cudaGraphDestroy(g);
+    if (e == cudaSuccess) {
+      b->graph_epoch = epoch;
+      b->graph_logits = d_logits != nullptr;
+      e = cudaGraphLaunch(b->graph, st);
+    }
+  } else {
+    e = body(st);
+    if (use_graph) b->warm_epoch = epoch;
+  }
+  if (e != cudaSuccess) {
+    *err = cuda_msg("batched decode step", e);
+    return false;
+  }
+  for (Session* s : b->sessions) s->pos += 1;
+  return true;
+}
+
+}  // namespace nb

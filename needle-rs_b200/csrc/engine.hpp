@@ -1,0 +1,137 @@
+// Needle-3 engine on one B200: the GPU counterpart of the reference's
+// V3Model + V3Cache + V3Engine (crates/needle-core/src/v3/model.rs,
+// v3/cache.rs, crates/needle-infer/src/v3_engine.rs).
+#pragma once
+#include <cuda_runtime.h>
+
+#include <memory>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "kernels.hpp"
+
+namespace nb {
+
+struct Record {  // crates/needle-infer/src/cact.rs:398-425
+  uint8_t dtype = 0, ndim = 0;
+  uint32_t shape[4] = {0, 0, 0, 0};
+  uint64_t offset = 0, nbytes = 0;
+  uint32_t group = 0, bits = 0;
+};
+
+struct HostConfig {  // crates/needle-core/src/v3/config.rs:44-73
+  size_t vocab = 0, out_vocab = 0, d = 0, heads = 0, kvh = 0, layers = 0, qk = 0, vh = 0,
+         max_seq = 0, hada_n = 0, lanes = 0, window = 0, taps = 0;
+  std::vector<int> global_layers;
+  std::vector<int> orders, sites;
+  size_t e_slots = 0, e_sub = 0, e_tables = 0, e_heads = 0, e_taps = 0, e_dil = 0, e_seed_heads = 0;
+  float rope_theta = 0.f;
+  uint32_t kv_window = 0, kv_bits = 0;
+  size_t num_tensors = 0;
+  bool has_heads = false;
+  size_t logit_rows() const { return out_vocab == 0 ? vocab : out_vocab; }
+  bool is_global(size_t l) const;
+  size_t span(size_t l) const;  // 0 = unbounded
+  size_t kv_bytes_at(size_t seq_len, bool int8) const;  // config.rs:234-272
+};
+
+class Engine;
+
+// One generation session: the device-resident counterpart of V3Cache.
+class Session {
+ public:
+  ~Session();
+  Engine* eng = nullptr;
+  bool int8 = false;
+  size_t hint = 0;
+  size_t pos = 0;                 // host mirror of SessDesc::pos
+  SessDesc* d_desc = nullptr;     // device descriptor
+  LayerKV* d_layers = nullptr;    // device array [layers]
+  std::vector<LayerKV> layers;    // host mirror
+  void* d_state = nullptr;        // tails + token ring
+  size_t state_bytes = 0;
+  size_t bytes() const;           // device bytes held, as V3Cache::bytes counts them
+};
+
+struct Workspace {
+  size_t cap = 0;  // rows
+  size_t last_cap = 0;
+  float *lanes = nullptr, *u = nullptr, *bx = nullptr, *xh = nullptr, *proj = nullptr,
+        *qpost = nullptr, *attn = nullptr, *oh = nullptr, *projo = nullptr, *gates = nullptr,
+        *fetched = nullptr, *ekv = nullptr, *evc = nullptr, *lm_in = nullptr, *pks = nullptr,
+        *pvs = nullptr, *logits = nullptr, *lm_last = nullptr;
+  void *pk = nullptr, *pv = nullptr;
+  RowInfo* rows = nullptr;
+  uint32_t *tokens = nullptr, *next = nullptr;
+  int* last_rows = nullptr;
+  void release();
+};
+
+// A fixed set of sessions decoded together. Owns the device array of session
+// descriptors and a CUDA graph of one decode step, replayed while the set and
+// the ring capacities stay the same.
+class Batch {
+ public:
+  ~Batch();
+  Engine* eng = nullptr;
+  std::vector<Session*> sessions;
+  SessDesc** d_sess = nullptr;
+  bool int8 = false;
+  cudaGraphExec_t graph = nullptr;
+  bool graph_logits = false;
+  uint64_t graph_epoch = 0;
+  uint64_t warm_epoch = 0;
+  uint32_t* d_tok = nullptr;   // [n] token fed this step
+  uint32_t* d_next = nullptr;  // [n] greedy pick of this step
+};
+
+class Engine {
+ public:
+  static Engine* load(const uint8_t* data, size_t len, std::string* err);
+  ~Engine();
+
+  HostConfig cfg;
+  Geo G{};
+  int device = 0;
+  cudaStream_t stream = nullptr;
+  std::mutex mu;
+
+  Session* new_session(size_t hint, bool int8, std::string* err);
+  // Whole-prompt prefill of fresh sessions (model.rs:512-523). Writes the last
+  // position's logits (host, [n][logit_rows]) and/or greedy picks (host, [n]).
+  bool prefill(Session* const* ss, const uint32_t* const* ids, const size_t* lens, size_t n,
+               float* logits, uint32_t* picks, std::string* err);
+  // One decode step for each session (model.rs:150-375), host buffers.
+  bool decode(Session* const* ss, const uint32_t* tokens, size_t n, float* logits,
+              uint32_t* picks, std::string* err);
+  // Device-resident decode step over a batch: reads b->d_tok, writes b->d_next
+  // and (when logits != nullptr) logits [n][logit_rows] on the device.
+  bool decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, bool use_graph,
+                           std::string* err);
+  Batch* new_batch(Session* const* ss, size_t n, std::string* err);
+
+  // --- weights on the device
+  uint8_t* d_blob = nullptr;
+  float* d_params = nullptr;
+  uint32_t* d_perm = nullptr;
+  float* d_rope = nullptr;
+  CqMat emb{}, phi_pre{}, phi_post{}, phi_res{};
+  std::vector<CqMat> qkvg, outp, eng_kv, eng_tables;
+  CqMat* d_tables = nullptr;
+  std::vector<LayerParams> lp;
+  std::vector<MhcParams> mp;
+  std::vector<const float*> eng_taps;
+  std::vector<int> site_of;
+  const float* final_norm = nullptr;
+  Workspace ws;
+  uint64_t epoch = 1;  // bumped whenever a session's device layout changes
+
+  bool ensure_ws(size_t rows, std::string* err);
+  bool ensure_slots(Session* s, size_t pos, std::string* err);
+  cudaError_t forward(const RowBatch& rb, cudaStream_t st, bool int8);
+  cudaError_t head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
+                   cudaStream_t st);
+};
+
+}  // namespace nb

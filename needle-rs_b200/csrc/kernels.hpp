@@ -10,7 +10,7 @@ namespace nb {
 struct Geo {
   int d, heads, kvh, qk, vh, layers, lanes, hada_n, ba, bb, taps, window, max_seq, vocab, logit_rows;
   int q_dim, k_dim, v_dim, o_dim, qkv_dim, proj_dim;
-  int e_tables, e_heads, e_slots, e_sub, e_taps, e_dil, e_maxorder, e_reach, n_orders, n_sites;
+  int e_tables, e_heads, e_slots, e_sub, e_taps, e_dil, e_maxorder, e_reach, e_stride, n_orders, n_sites;
   int orders[4];
   int cond_rank;
   float embed_scale;
@@ -41,6 +41,9 @@ struct RowBatch {
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                        int nrows, cudaStream_t st, int force_path = 0);
 
+cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out,
+                              cudaStream_t st);
+
 cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, float* lanes,
                          cudaStream_t st);
 cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBatch& rb,
@@ -57,7 +60,7 @@ cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const Laye
                             void* pv, float* pks, float* pvs, cudaStream_t st);
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                              const float* qpost, const void* pk, const void* pv, const float* pks,
-                             const float* pvs, float* attn, cudaStream_t st);
+                             const float* pvs, float* attn, cudaStream_t st, int int8);
 cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, const float* attn,
                                const float* proj, float* oh, cudaStream_t st);
 cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,

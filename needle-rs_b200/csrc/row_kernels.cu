@@ -1,0 +1,797 @@
+// Per-row kernels of the Needle-3 forward: one CTA per activation row, where a
+// row is one (session, position) pair, so the same kernels serve batch-1
+// decode, batched multi-session decode and whole-prompt prefill.
+//
+// Each kernel cites the reference function it restates. Reductions run as
+// warp/block trees instead of the reference's sequential sums, so results
+// match the CPU path to f32 rounding rather than bit for bit; the integer work
+// (index unpacking, Engram hashing, int8 quantisation) is exact.
+#include <cuda_runtime.h>
+
+#include "common.cuh"
+#include "kernels.hpp"
+#include "launch_util.hpp"
+
+namespace nb {
+
+constexpr float EPS = 1e-6f;  // crates/needle-core/src/kernels.rs:11, norm.rs:6
+
+// Decode one 128-element quantisation group of a CQ row into `out`
+// (levels[idx] * norm, cq.rs:791-809); each lane writes elements lane*4..+3.
+__device__ __forceinline__ void decode_group_lane(const CqMat& W, const uint8_t* row, float norm,
+                                                  int g, float (&v)[4]) {
+  const int lane = threadIdx.x & 31;
+  const int mask = (1 << W.bits) - 1;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    int e = g * 128 + lane * 4 + i;
+    int bit = e * W.bits;
+    int code = (row[bit >> 3] >> (bit & 7)) & mask;
+    v[i] = W.levels[code] * norm;
+  }
+}
+
+// ---------------------------------------------------------------- embedding
+// model.rs:196-203: dequantize_row (levels*norm, inverse rotation) then
+// * sqrt(d_model), broadcast into every mHC lane.
+__global__ void embed_kernel(Geo G, CqMat emb, RowBatch rb, float* __restrict__ lanes) {
+  const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  uint32_t tok = rb.tokens[r];
+  if (tok > (uint32_t)(G.vocab - 1)) tok = G.vocab - 1;  // clamp_token, model.rs:533
+  const uint8_t* row = emb.seg[0].packed + (size_t)tok * emb.row_bytes;
+  const __half* nrm = emb.seg[0].norms + (size_t)tok * emb.groups;
+  float* out = lanes + (size_t)r * G.lanes * G.d;
+  for (int g = wid; g < emb.groups; g += nw) {
+    float v[4];
+    decode_group_lane(emb, row, __half2float(nrm[g]), g, v);
+    fwht128_warp(v);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      int c = g * 128 + lane * 4 + i;
+      if (c < G.d) {
+        float x = v[i] * G.embed_scale;
+        for (int l = 0; l < G.lanes; ++l) out[l * G.d + c] = x;
+      }
+    }
+  }
+}
+
+cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, float* lanes,
+                         cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  embed_kernel<<<rb.M, 256, 0, st>>>(G, emb, rb, lanes);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- Engram
+// engram.rs:31-61 (hash) and :66-69 (validity), model.rs:158-191 / :420-471
+// (gather). The fetched row feeds key/value projections whose prepare_input
+// rotates it again; the rotation is an involution, so the projection input is
+// the decoded codes levels[idx]*norm directly and both rotations are skipped.
+__global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, RowBatch rb,
+                                     float* __restrict__ fetched) {
+  const int r = blockIdx.x, site = blockIdx.y;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const RowInfo ri = rb.rows[r];
+  const int p = ri.pos;
+  const CqMat& T = tables[site];
+  float* out = fetched + ((size_t)r * G.n_sites + site) * G.d;
+  for (int t = wid; t < G.e_tables; t += nw) {
+    const int oi = t / G.e_heads, h = t % G.e_heads;
+    const int order = G.orders[oi];
+    float v[4] = {0.f, 0.f, 0.f, 0.f};
+    if (p + 1 >= order) {  // ngram_valid
+      uint32_t acc = 0x9E3779B9u * (uint32_t)(oi * G.e_stride + h + 1);
+      for (int j = 0; j < order; ++j) {
+        uint32_t tok;
+        if (j > p)
+          tok = 0;
+        else if (j == 0)
+          tok = rb.tokens[r];
+        else if (rb.mode == MODE_PREFILL)
+          tok = rb.tokens[r - j];
+        else
+          tok = ri.s->toks[(p - j) & 3];
+        acc = (acc ^ tok) * 0x01000193u;
+      }
+      acc ^= acc >> 15;
+      const uint32_t slot = acc % (uint32_t)G.e_slots;
+      const size_t trow = (size_t)t * G.e_slots + slot;
+      const uint8_t* row = T.seg[0].packed + trow * T.row_bytes;
+      decode_group_lane(T, row, __half2float(T.seg[0].norms[trow * T.groups]), 0, v);
+    }
+    reinterpret_cast<float4*>(out + t * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+  }
+}
+
+cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBatch& rb,
+                                 float* fetched, cudaStream_t st) {
+  if (rb.M <= 0 || G.n_sites == 0) return cudaSuccess;
+  dim3 grid(rb.M, G.n_sites);
+  engram_gather_kernel<<<grid, 256, 0, st>>>(G, tables, rb, fetched);
+  return cudaGetLastError();
+}
+
+// value_conv (engram.rs:89-106) / engram_conv_step (cache.rs:444-479): dilated
+// causal conv of the raw Engram values, gated until p >= j*max_order. Prefill
+// rows read earlier raw values from the batch and seed the tail ring with the
+// last `reach` raw rows; decode rows read the ring and then overwrite the slot
+// of p-reach with this position's raw value.
+struct EngTaps {
+  const float* t[16];
+};
+
+__global__ void engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float* __restrict__ ekv,
+                                   float* __restrict__ evc) {
+  const int r = blockIdx.x, site = blockIdx.y;
+  const RowInfo ri = rb.rows[r];
+  const int p = ri.pos, reach = G.e_reach;
+  const float* tp = taps.t[site];
+  const size_t kv_ld = (size_t)G.n_sites * 2 * G.d;
+  const float* raw_here = ekv + (size_t)r * kv_ld + (size_t)site * 2 * G.d + G.d;
+  float* tail = ri.s->eng_tail + (size_t)site * reach * G.d;
+  for (int c = threadIdx.x; c < G.d; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < G.e_taps; ++j) {
+      const int back = j * G.e_dil;
+      if (back > p || p < j * G.e_maxorder) continue;
+      float val;
+      if (back == 0)
+        val = raw_here[c];
+      else if (rb.mode == MODE_PREFILL)
+        val = ekv[(size_t)(r - back) * kv_ld + (size_t)site * 2 * G.d + G.d + c];
+      else
+        val = tail[(size_t)((p - back) % reach) * G.d + c];
+      acc += tp[j * G.d + c] * val;
+    }
+    evc[((size_t)r * G.n_sites + site) * G.d + c] = acc;
+    if (reach > 0) {
+      const bool seed = rb.mode == MODE_DECODE || p >= ri.len - reach;
+      if (seed) tail[(size_t)(p % reach) * G.d + c] = raw_here[c];
+    }
+  }
+}
+
+cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const RowBatch& rb,
+                               const float* ekv, float* evc, cudaStream_t st) {
+  if (rb.M <= 0 || G.n_sites == 0) return cudaSuccess;
+  if (G.n_sites > 16) return cudaErrorInvalidValue;
+  EngTaps t;
+  for (int i = 0; i < G.n_sites; ++i) t.t[i] = taps[i];
+  dim3 grid(rb.M, G.n_sites);
+  engram_conv_kernel<<<grid, 256, 0, st>>>(G, t, rb, ekv, evc);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- mHC pre
+// Sinkhorn (kernels.rs:46-85) on an n x n matrix held one element per lane
+// (n in {1, 2, 4}); rows are lane groups of n, columns lanes with stride n.
+__device__ __forceinline__ float sinkhorn_lane(float m, int n) {
+  const int lane = threadIdx.x & 31;
+  const bool in = lane < n * n;
+  for (int it = 0; it < 20; ++it) {
+    float mx = in ? m : -INFINITY;
+    for (int o = 1; o < n; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float e = in ? expf(m - mx) : 0.f;
+    for (int o = 1; o < n; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    float lse = isfinite(mx) ? mx + logf(e) : mx;
+    m = m - lse;
+    mx = in ? m : -INFINITY;
+    for (int o = n; o < n * n; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    e = in ? expf(m - mx) : 0.f;
+    for (int o = n; o < n * n; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    m = m - (mx + logf(e));
+  }
+  return expf(m);
+}
+
+// Dot of one CQ row (4- or 2-bit) with a prepared activation in shared memory,
+// one warp. Returns the full sum in every lane.
+__device__ __forceinline__ float cq_row_dot_warp(const CqMat& W, int row_index, const float* xs) {
+  const int lane = threadIdx.x & 31;
+  int local, s = 0, base = 0;
+  for (int i = 0; i < W.nseg - 1; ++i)
+    if (row_index >= base + W.seg[i].rows) {
+      base += W.seg[i].rows;
+      s = i + 1;
+    }
+  local = row_index - base;
+  const uint8_t* row = W.seg[s].packed + (size_t)local * W.row_bytes;
+  const __half* nrm = W.seg[s].norms + (size_t)local * W.groups;
+  const int E = 128 / W.bits;  // elements per 16-byte chunk
+  const int mask = (1 << W.bits) - 1;
+  const int per_byte = 8 / W.bits;
+  float acc = 0.f;
+  for (int c = lane; c < W.row_bytes / 16; c += 32) {
+    uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + c);
+    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+    const int k0 = c * E;
+    float part = 0.f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      for (int b = 0; b < 4 * per_byte; ++b) {
+        int code = (wd[q] >> (b * W.bits)) & mask;
+        part += W.levels[code] * xs[k0 + q * 4 * per_byte + b];
+      }
+    acc += __half2float(nrm[k0 / 128]) * part;
+  }
+  return warp_sum(acc);
+}
+
+// mhc.rs:79-102 (mix_down) with the gate and Sinkhorn of mhc.rs:109-130, the
+// Engram gate (engram.rs:112-132) and the pre-attention norm + rotation of the
+// q|k|v|gate input (model.rs:230-262). phi_post / phi_res read the same
+// rms_unit(lanes) as phi_pre (the lanes are unchanged until scatter_up,
+// model.rs:241 vs :332), so all three projections run here.
+__global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes,
+                                 CqMat phi_pre, CqMat phi_post, CqMat phi_res, MhcParams mp,
+                                 const float* __restrict__ norm_in, int site,
+                                 const float* __restrict__ ekv, const float* __restrict__ evc,
+                                 float* __restrict__ u_out, float* __restrict__ bx_out,
+                                 float* __restrict__ xh_out, float* __restrict__ gates) {
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x;
+  const int n = G.lanes, d = G.d, W = n * d;
+  const int Wp = phi_pre.in_pad;
+  float* L = sm;                 // [W]
+  float* X = L + W;              // [Wp]
+  float* bx = X + Wp;            // [d]
+  float* hb = bx + d;            // [d] (h, rounded up to a multiple of 128)
+  const int dpad = (d + 127) / 128 * 128;
+  float* phi = hb + dpad;        // [32]
+  float* red = phi + 32;         // [32]
+  float* gsm = red + 32;         // [4 + 4 + 16]
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+
+  const float* lr = lanes + (size_t)r * W;
+  float ss = 0.f;
+  for (int i = tid; i < W; i += blockDim.x) {
+    float v = lr[i];
+    L[i] = v;
+    ss += v * v;
+  }
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)W + EPS);  // rms_unit_to, kernels.rs:32
+  for (int i = tid; i < Wp; i += blockDim.x) X[i] = i < W ? L[i] * inv : 0.f;
+  __syncthreads();
+  fwht_groups_warp(X, Wp / 128);
+  __syncthreads();
+  // 2n + n^2 projected gate rows of this layer.
+  const int nrow = 2 * n + n * n;
+  for (int k = wid; k < nrow; k += nw) {
+    float v;
+    if (k < n)
+      v = cq_row_dot_warp(phi_pre, li * n + k, X);
+    else if (k < 2 * n)
+      v = cq_row_dot_warp(phi_post, li * n + (k - n), X);
+    else
+      v = cq_row_dot_warp(phi_res, li * n * n + (k - 2 * n), X);
+    if (lane == 0) phi[k] = v;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    const int act = li % n;
+    if (lane < n) {
+      float pre_off = lane == act ? 4.0f : -4.0f;    // mhc.rs:56
+      float post_off = lane == act ? 0.0f : -4.0f;   // mhc.rs:65
+      gsm[lane] = sigmoidf_(mp.a_pre * phi[lane] + mp.b_pre[lane] + pre_off);
+      gsm[n + lane] = 2.0f * sigmoidf_(mp.a_post * phi[n + lane] + mp.b_post[lane] + post_off);
+    }
+    float m = lane < n * n ? mp.a_res * phi[2 * n + lane] + mp.b_res[lane] : 0.f;
+    float hres = sinkhorn_lane(m, n);
+    if (lane < n * n) gsm[2 * n + lane] = hres;
+  }
+  __syncthreads();
+  float* gout = gates + (size_t)r * 24;
+  if (tid < n + n * n) gout[tid] = gsm[n + tid];  // hpost[n], hres[n*n]
+  // u = sum_i hpre_i * lane_i (mix_down), bx = u (+ Engram).
+  for (int c = tid; c < d; c += blockDim.x) {
+    float acc = 0.f;
+    for (int l = 0; l < n; ++l) acc += gsm[l] * L[l * d + c];
+    bx[c] = acc;
+    u_out[(size_t)r * d + c] = acc;
+  }
+  __syncthreads();
+  if (site >= 0) {
+    const size_t kv_ld = (size_t)G.n_sites * 2 * d;
+    const float* ek = ekv + (size_t)r * kv_ld + (size_t)site * 2 * d;
+    const float* ev = evc + ((size_t)r * G.n_sites + site) * d;
+    float sx = 0.f, sk = 0.f, sd = 0.f;
+    for (int c = tid; c < d; c += blockDim.x) {
+      float x = bx[c], k = ek[c];
+      sx += x * x;
+      sk += k * k;
+      sd += x * k;
+    }
+    sx = block_sum(sx, red);
+    sk = block_sum(sk, red);
+    sd = block_sum(sd, red);
+    const float ux = 1.0f / sqrtf(sx / (float)d + 1e-6f);
+    const float uk = 1.0f / sqrtf(sk / (float)d + 1e-6f);
+    const float alpha = sigmoidf_(sd * ux * uk / sqrtf((float)d));
+    for (int c = tid; c < d; c += blockDim.x) bx[c] += alpha * ev[c];
+    __syncthreads();
+  }
+  float s2 = 0.f;
+  for (int c = tid; c < d; c += blockDim.x) s2 += bx[c] * bx[c];
+  s2 = block_sum(s2, red);
+  const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
+  for (int c = tid; c < dpad; c += blockDim.x) {
+    hb[c] = c < d ? (1.0f + norm_in[c]) * bx[c] * inv2 : 0.f;
+    if (c < d) bx_out[(size_t)r * d + c] = bx[c];
+  }
+  __syncthreads();
+  fwht_groups_warp(hb, dpad / 128);
+  __syncthreads();
+  for (int c = tid; c < dpad; c += blockDim.x) xh_out[(size_t)r * dpad + c] = hb[c];
+}
+
+cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
+                             const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
+                             const MhcParams& mp, const float* norm_in, int site, const float* ekv,
+                             const float* evc, float* u, float* bx, float* xh, float* gates,
+                             cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
+  const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24) * sizeof(float);
+  cudaError_t e = allow_smem((const void*)layer_pre_kernel, smem);
+  if (e != cudaSuccess) return e;
+  layer_pre_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in,
+                                            site, ekv, evc, u, bx, xh, gates);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- Q/K/V post-processing
+// Causal depthwise conv (attention.rs:82-100, cache.rs:401-438), ZCRMS norm +
+// half-split RoPE (attention.rs:107-143), int8 query fake-quant (model.rs:289-293)
+// and quantize-on-append of K/V (cache.rs:346-377, quant_into :100-106).
+//
+// Quantisation is bit-exact with the reference on identical inputs: IEEE
+// absmax/127 and 1/scale, roundf (half away from zero), clamp [-128, 127].
+__device__ __forceinline__ float quant_scale_warp(float a0, float a1, float* inv) {
+  float am = warp_max(fmaxf(fabsf(a0), fabsf(a1)));
+  float scale = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
+  *inv = __fdiv_rn(1.0f, scale);
+  return scale;
+}
+__device__ __forceinline__ float q8(float x, float inv) {
+  float q = roundf(__fmul_rn(x, inv));
+  return fminf(fmaxf(q, -128.0f), 127.0f);
+}
+
+__global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
+                                const float* __restrict__ rope_cs, const float* __restrict__ proj,
+                                float* __restrict__ qpost, void* pk, void* pv, float* pks,
+                                float* pvs) {
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x;
+  const RowInfo ri = rb.rows[r];
+  const int p = ri.pos;
+  const int qd = G.q_dim, kd = G.k_dim, vd = G.v_dim, qkv = G.qkv_dim;
+  const int taps = G.taps, tl = taps > 0 ? taps - 1 : 0;
+  const float* raw = proj + (size_t)r * G.proj_dim;
+  float* tail = tl ? ri.s->qkv_tail + (size_t)li * tl * qkv : nullptr;
+  for (int c = threadIdx.x; c < qkv; c += blockDim.x) {
+    const float* tp;
+    int dim, cc;
+    if (c < qd) {
+      tp = lp.q_taps; dim = qd; cc = c;
+    } else if (c < qd + kd) {
+      tp = lp.k_taps; dim = kd; cc = c - qd;
+    } else {
+      tp = lp.v_taps; dim = vd; cc = c - qd - kd;
+    }
+    float x = raw[c];
+    float acc = x;
+    if (taps > 0) {
+      acc = tp[cc] * x;
+      for (int j = 1; j < taps; ++j) {
+        if (j > p) break;
+        float prev = rb.mode == MODE_PREFILL ? proj[(size_t)(r - j) * G.proj_dim + c]
+                                             : tail[(size_t)((p - j) % tl) * qkv + c];
+        acc += tp[j * dim + cc] * prev;
+      }
+      if (tl && (rb.mode == MODE_DECODE || p >= ri.len - tl)) tail[(size_t)(p % tl) * qkv + c] = x;
+    }
+    sm[c] = acc;
+  }
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  const int half = G.qk / 2;
+  const float* cs = rope_cs + (size_t)p * half;                     // cos
+  const float* sn = rope_cs + (size_t)G.max_seq * half + (size_t)p * half;  // sin
+  const bool int8 = ri.s->int8 != 0;
+  const bool prefill = rb.mode == MODE_PREFILL;
+  const LayerKV kv = ri.s->layers[li];
+  const int slot = p % kv.slots;
+  const bool to_ring = !prefill || p >= ri.len - kv.slots;
+  const int ntask = G.heads + 2 * G.kvh;
+  for (int t = wid; t < ntask; t += nw) {
+    if (t < G.heads + G.kvh) {
+      // q head t, or k head t-heads: norm + rope.
+      const bool isq = t < G.heads;
+      const int h = isq ? t : t - G.heads;
+      float* x = sm + (isq ? h * G.qk : qd + h * G.qk);
+      const float* sc = isq ? lp.q_norm : lp.k_norm;
+      float x1 = lane < half ? x[lane] : 0.f, x2 = lane < half ? x[half + lane] : 0.f;
+      float sq = warp_sum(x1 * x1 + x2 * x2);
+      float rms = sqrtf(sq / (float)G.qk + 1e-6f);
+      if (lane < half) {
+        x1 = (1.0f + sc[lane]) * x1 / rms;
+        x2 = (1.0f + sc[half + lane]) * x2 / rms;
+        float c = cs[lane], s = sn[lane];
+        float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
+        x1 = y1;
+        x2 = y2;
+      }
+      if (isq) {
+        if (int8) {
+          float inv, scale = quant_scale_warp(x1, x2, &inv);
+          x1 = q8(x1, inv) * scale;
+          x2 = q8(x2, inv) * scale;
+        }
+        if (lane < half) {
+          qpost[(size_t)r * qd + h * G.qk + lane] = x1;
+          qpost[(size_t)r * qd + h * G.qk + half + lane] = x2;
+        }
+      } else if (int8) {
+        float inv, scale = quant_scale_warp(x1, x2, &inv);
+        int8_t a = (int8_t)q8(x1, inv), b = (int8_t)q8(x2, inv);
+        if (lane < half) {
+          if (prefill) {
+            int8_t* d8 = (int8_t*)pk + ((size_t)r * G.kvh + h) * G.qk;
+            d8[lane] = a;
+            d8[half + lane] = b;
+          }
+          if (to_ring) {
+            int8_t* d8 = (int8_t*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
+            d8[lane] = a;
+            d8[half + lane] = b;
+          }
+        }
+        if (lane == 0) {
+          if (prefill) pks[(size_t)r * G.kvh + h] = scale;
+          if (to_ring) kv.ks[(size_t)h * kv.slots + slot] = scale;
+        }
+      } else if (lane < half) {
+        if (prefill) {
+          float* df = (float*)pk + ((size_t)r * G.kvh + h) * G.qk;
+          df[lane] = x1;
+          df[half + lane] = x2;
+        }
+        if (to_ring) {
+          float* df = (float*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
+          df[lane] = x1;
+          df[half + lane] = x2;
+        }
+      }
+    } else {
+      // v head: conv output only, then store (quantised in int8 mode).
+      const int h = t - G.heads - G.kvh;
+      const float* x = sm + qd + kd + h * G.vh;
+      const int vhalf = G.vh / 2;
+      float x1 = lane < vhalf ? x[lane] : 0.f, x2 = lane < vhalf ? x[vhalf + lane] : 0.f;
+      if (int8) {
+        float inv, scale = quant_scale_warp(x1, x2, &inv);
+        int8_t a = (int8_t)q8(x1, inv), b = (int8_t)q8(x2, inv);
+        if (lane < vhalf) {
+          if (prefill) {
+            int8_t* d8 = (int8_t*)pv + ((size_t)r * G.kvh + h) * G.vh;
+            d8[lane] = a;
+            d8[vhalf + lane] = b;
+          }
+          if (to_ring) {
+            int8_t* d8 = (int8_t*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
+            d8[lane] = a;
+            d8[vhalf + lane] = b;
+          }
+        }
+        if (lane == 0) {
+          if (prefill) pvs[(size_t)r * G.kvh + h] = scale;
+          if (to_ring) kv.vs[(size_t)h * kv.slots + slot] = scale;
+        }
+      } else if (lane < vhalf) {
+        if (prefill) {
+          float* df = (float*)pv + ((size_t)r * G.kvh + h) * G.vh;
+          df[lane] = x1;
+          df[vhalf + lane] = x2;
+        }
+        if (to_ring) {
+          float* df = (float*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
+          df[lane] = x1;
+          df[vhalf + lane] = x2;
+        }
+      }
+    }
+  }
+}
+
+cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                            const float* rope_cs, const float* proj, float* qpost, void* pk,
+                            void* pv, float* pks, float* pvs, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  if (G.qk > 64 || G.vh > 64 || (G.qk & 1) || (G.vh & 1)) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)G.qkv_dim * sizeof(float);
+  qkv_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs);
+  return cudaGetLastError();
+}
+
+// attention output * sigmoid(gate) (model.rs:305-308), then the rotation of
+// out_proj's prepare_input.
+__global__ void attn_finish_kernel(Geo G, const float* __restrict__ attn, const float* __restrict__ proj,
+                                   float* __restrict__ oh) {
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x;
+  const int od = G.o_dim, opad = (od + 127) / 128 * 128;
+  const float* gate = proj + (size_t)r * G.proj_dim + G.qkv_dim;
+  for (int i = threadIdx.x; i < opad; i += blockDim.x)
+    sm[i] = i < od ? attn[(size_t)r * od + i] * sigmoidf_(gate[i]) : 0.f;
+  __syncthreads();
+  fwht_groups_warp(sm, opad / 128);
+  __syncthreads();
+  for (int i = threadIdx.x; i < opad; i += blockDim.x) oh[(size_t)r * opad + i] = sm[i];
+}
+
+cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, const float* attn,
+                               const float* proj, float* oh, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  const int opad = (G.o_dim + 127) / 128 * 128;
+  attn_finish_kernel<<<rb.M, 256, opad * sizeof(float), st>>>(G, attn, proj, oh);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- block tail
+// model.rs:309-356: post_norm + gated residual, pre_hada norm, HadamardMLP
+// (v3/kernels.rs:119-180), MLP residual, y = block - u and scatter_up
+// (mhc.rs:109-158) back into the lanes.
+__device__ void kron_apply_block(const float* z, const float* __restrict__ a,
+                                 const float* __restrict__ b, int ba, int bb, float* tmp, float* As,
+                                 float* Bs, float* out) {
+  // out[k][l] = sum_j (sum_i z[i][j] a[i][k]) b[j][l]  (kernels.rs:41-78)
+  for (int i = threadIdx.x; i < ba * ba; i += blockDim.x) As[i] = a[i];
+  for (int i = threadIdx.x; i < bb * bb; i += blockDim.x) Bs[i] = b[i];
+  __syncthreads();
+  for (int e = threadIdx.x; e < ba * bb; e += blockDim.x) {
+    int k = e / bb, j = e % bb;
+    float acc = 0.f;
+    for (int i = 0; i < ba; ++i) acc += z[i * bb + j] * As[i * ba + k];
+    tmp[e] = acc;
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < ba * bb; e += blockDim.x) {
+    int k = e / bb, l = e % bb;
+    float acc = 0.f;
+    for (int j = 0; j < bb; ++j) acc += tmp[k * bb + j] * Bs[j * bb + l];
+    out[e] = acc;
+  }
+  __syncthreads();
+}
+
+__global__ void layer_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
+                                  const uint32_t* __restrict__ p1, const uint32_t* __restrict__ p2,
+                                  const float* __restrict__ projo, const float* __restrict__ u,
+                                  const float* __restrict__ bx_in, const float* __restrict__ gates,
+                                  float* __restrict__ lanes) {
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x;
+  const int d = G.d, n = G.hada_n, nl = G.lanes;
+  float* s1 = sm;             // [d]
+  float* t = s1 + d;          // [d]
+  float* cond = t + d;        // [n]
+  float* z = cond + n;        // [n]
+  float* buf = z + n;         // [n]
+  float* tmp = buf + n;       // [n]
+  float* As = tmp + n;        // [ba*ba]
+  float* Bs = As + G.ba * G.ba;  // [bb*bb]
+  float* red = Bs + G.bb * G.bb; // [32]
+  float* pr = red + 32;          // [8]
+  float* gs = pr + 8;            // [24]
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const float* po = projo + (size_t)r * d;
+  const float* bx = bx_in + (size_t)r * d;
+  if (tid < nl + nl * nl) gs[tid] = gates[(size_t)r * 24 + tid];
+  float ss = 0.f;
+  for (int c = tid; c < d; c += blockDim.x) ss += po[c] * po[c];
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)d + EPS);
+  const float ag = sigmoidf_(lp.attn_gate);
+  for (int c = tid; c < d; c += blockDim.x) s1[c] = bx[c] + ag * ((1.0f + lp.post_norm[c]) * po[c] * inv);
+  __syncthreads();
+  float s2 = 0.f;
+  for (int c = tid; c < d; c += blockDim.x) s2 += s1[c] * s1[c];
+  s2 = block_sum(s2, red);
+  const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);
+  for (int c = tid; c < d; c += blockDim.x) t[c] = (1.0f + lp.pre_hada[c]) * s1[c] * inv2;
+  __syncthreads();
+  // cond = 1 + softmax(t . cond_v) . cond_u   (rank <= 8)
+  const int rk = G.cond_rank;
+  if (wid < rk) {
+    float acc = 0.f;
+    for (int i = lane; i < d; i += 32) acc += t[i] * lp.cond_v[i * rk + wid];
+    acc = warp_sum(acc);
+    if (lane == 0) pr[wid] = acc;
+  }
+  __syncthreads();
+  if (tid == 0) {
+    float mx = -INFINITY;
+    for (int j = 0; j < rk; ++j) mx = fmaxf(mx, pr[j]);
+    float sum = 0.f;
+    for (int j = 0; j < rk; ++j) {
+      pr[j] = expf(pr[j] - mx);
+      sum += pr[j];
+    }
+    for (int j = 0; j < rk; ++j) pr[j] = pr[j] / sum;
+  }
+  __syncthreads();
+  for (int c = tid; c < n; c += blockDim.x) {
+    float cv = 1.0f;
+    for (int j = 0; j < rk; ++j)
+      if (pr[j] != 0.0f) cv += pr[j] * lp.cond_u[j * n + c];
+    cond[c] = cv;
+    z[c] = (c < d ? t[c] : 0.f) * lp.d1[c];
+  }
+  __syncthreads();
+  kron_apply_block(z, lp.w1a, lp.w1b, G.ba, G.bb, tmp, As, Bs, buf);
+  for (int c = tid; c < n; c += blockDim.x) {
+    float v = lp.d2[c] * cond[c] * buf[p1[c]] + lp.b2[c];
+    z[c] = v * sigmoidf_(v);  // silu, ops.rs:118
+  }
+  __syncthreads();
+  kron_apply_block(z, lp.w2a, lp.w2b, G.ba, G.bb, tmp, As, Bs, buf);
+  for (int c = tid; c < n; c += blockDim.x) z[c] = buf[p2[c]] * lp.d3[c];
+  __syncthreads();
+  kron_apply_block(z, lp.w3a, lp.w3b, G.ba, G.bb, tmp, As, Bs, buf);
+  // bx += mlp; y = bx - u; lanes' = hres . lanes + hpost * y
+  float* lr = lanes + (size_t)r * nl * d;
+  const float* ur = u + (size_t)r * d;
+  for (int c = tid; c < d; c += blockDim.x) {
+    float b2 = s1[c] + buf[c] * lp.d4[c];
+    float y = b2 - ur[c];
+    float lv[4];
+    for (int j = 0; j < nl; ++j) lv[j] = lr[j * d + c];
+    for (int i = 0; i < nl; ++i) {
+      float acc = 0.f;
+      for (int j = 0; j < nl; ++j) acc += gs[nl + i * nl + j] * lv[j];
+      lr[i * d + c] = acc + gs[i] * y;
+    }
+  }
+}
+
+cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                              const uint32_t* p1, const uint32_t* p2, const float* projo,
+                              const float* u, float* bx, const float* gates, float* lanes,
+                              cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  if (G.lanes > 4 || G.cond_rank > 8) return cudaErrorInvalidValue;
+  const size_t smem = (size_t)(2 * G.d + 4 * G.hada_n + G.ba * G.ba + G.bb * G.bb + 32 + 8 + 24) * sizeof(float);
+  cudaError_t e = allow_smem((const void*)layer_post_kernel, smem);
+  if (e != cudaSuccess) return e;
+  layer_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, p1, p2, projo, u, bx, gates, lanes);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- head
+// model.rs:358-374: lane mean, final ZCRMS norm, rotation for the tied head.
+__global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float* __restrict__ fnorm,
+                             float* __restrict__ lm_in) {
+  extern __shared__ __align__(16) float sm[];
+  float* red = sm;
+  float* x = sm + 32;
+  const int r = blockIdx.x, d = G.d, dpad = (d + 127) / 128 * 128;
+  const float* lr = lanes + (size_t)r * G.lanes * d;
+  float ss = 0.f;
+  for (int c = threadIdx.x; c < d; c += blockDim.x) {
+    float a = 0.f;
+    for (int l = 0; l < G.lanes; ++l) a += lr[l * d + c];
+    a = a / (float)G.lanes;
+    x[c] = a;
+    ss += a * a;
+  }
+  ss = block_sum(ss, red);
+  const float inv = 1.0f / sqrtf(ss / (float)d + EPS);
+  for (int c = threadIdx.x; c < dpad; c += blockDim.x) x[c] = c < d ? (1.0f + fnorm[c]) * x[c] * inv : 0.f;
+  __syncthreads();
+  fwht_groups_warp(x, dpad / 128);
+  __syncthreads();
+  for (int c = threadIdx.x; c < dpad; c += blockDim.x) lm_in[(size_t)r * dpad + c] = x[c];
+}
+
+cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
+                         const float* final_norm, float* lm_in, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  const int dpad = (G.d + 127) / 128 * 128;
+  final_kernel<<<rb.M, 256, (32 + dpad) * sizeof(float), st>>>(G, lanes, final_norm, lm_in);
+  return cudaGetLastError();
+}
+
+// Greedy pick: the first maximum, as argmax (v3_engine.rs:410-420) keeps the
+// lowest index on ties and never picks a NaN.
+__global__ void argmax_kernel(const float* __restrict__ logits, int n, int ld, uint32_t* out) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  const int r = blockIdx.x;
+  const float* x = logits + (size_t)r * ld;
+  float best = -INFINITY;
+  int idx = 0x7fffffff;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    float v = x[i];
+    if (v > best || (v == best && i < idx)) {
+      best = v;
+      idx = i;
+    }
+  }
+  for (int o = 16; o > 0; o >>= 1) {
+    float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+    if (ov > best || (ov == best && oi < idx)) {
+      best = ov;
+      idx = oi;
+    }
+  }
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (lane == 0) {
+    bv[wid] = best;
+    bi[wid] = idx;
+  }
+  __syncthreads();
+  if (wid == 0) {
+    best = lane < nw ? bv[lane] : -INFINITY;
+    idx = lane < nw ? bi[lane] : 0x7fffffff;
+    for (int o = 16; o > 0; o >>= 1) {
+      float ov = __shfl_xor_sync(0xffffffffu, best, o);
+      int oi = __shfl_xor_sync(0xffffffffu, idx, o);
+      if (ov > best || (ov == best && oi < idx)) {
+        best = ov;
+        idx = oi;
+      }
+    }
+    if (lane == 0) out[r] = idx == 0x7fffffff ? 0u : (uint32_t)idx;
+  }
+}
+
+cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  argmax_kernel<<<M, 256, 0, st>>>(logits, n, ld, out);
+  return cudaGetLastError();
+}
+
+// ---------------------------------------------------------------- step bookkeeping
+__global__ void step_begin_kernel(RowInfo* rows, SessDesc* const* sess, int M) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= M) return;
+  SessDesc* s = sess[i];
+  rows[i].s = s;
+  rows[i].pos = s->pos;
+  rows[i].base = -1;
+  rows[i].len = -1;
+}
+
+cudaError_t launch_step_begin(const RowBatch& rb, SessDesc* const* sess, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  step_begin_kernel<<<(rb.M + 127) / 128, 128, 0, st>>>(rb.rows, sess, rb.M);
+  return cudaGetLastError();
+}
+
+// Decode: record the token in the history ring and advance (cache.rs:276, :530).
+// Prefill: seed the ring with the last tokens and set the position (cache.rs:505-520).
+__global__ void step_end_kernel(RowBatch rb) {
+  int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= rb.M) return;
+  RowInfo ri = rb.rows[i];
+  if (rb.mode == MODE_DECODE) {
+    ri.s->toks[ri.pos & 3] = rb.tokens[i];
+    ri.s->pos = ri.pos + 1;
+  } else {
+    if (ri.pos >= ri.len - 4) ri.s->toks[ri.pos & 3] = rb.tokens[i];
+    if (ri.pos == ri.len - 1) ri.s->pos = ri.len;
+  }
+}
+
+cudaError_t launch_step_end(const RowBatch& rb, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  step_end_kernel<<<(rb.M + 127) / 128, 128, 0, st>>>(rb);
+  return cudaGetLastError();
+}
+
+}  // namespace nb
