@@ -143,6 +143,10 @@ uint32_t *needle_v3_batch_next(NeedleV3Batch *batch);
 bool needle_v3_batch_step(NeedleV3Batch *batch, float *d_logits, void *stream, bool use_graph);
 /* Copy `next` into `tokens` on `stream` (feed the greedy picks back). */
 bool needle_v3_batch_feed_next(NeedleV3Batch *batch, void *stream);
+/* Synchronous host copies: set the tokens of the next step from host memory,
+ * or read the picks of the last step into host memory ([n] each). */
+bool needle_v3_batch_set_tokens(NeedleV3Batch *batch, const uint32_t *tokens);
+bool needle_v3_batch_get_next(NeedleV3Batch *batch, uint32_t *next);
 
 /* Geometry: vocab, out_vocab, d_model, heads, kv_heads, layers, qk, v_head,
  * max_seq, hada_n, lanes, window, conv_taps, logit_rows (14 int64). */

@@ -538,6 +538,38 @@ bool needle_v3_batch_feed_next(NeedleV3Batch* b, void* stream) {
   return true;
 }
 
+static bool batch_copy(NeedleV3Batch* b, void* dst, const void* src, cudaMemcpyKind kind) {
+  nb::Engine* E = b->h->eng.get();
+  cudaError_t e = cudaMemcpyAsync(dst, src, b->b->sessions.size() * 4, kind, E->stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(E->stream);
+  if (e != cudaSuccess) {
+    set_err(std::string("batch token copy: ") + cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
+
+bool needle_v3_batch_set_tokens(NeedleV3Batch* b, const uint32_t* tokens) {
+  clear_err();
+  if (!b || !tokens) {
+    set_err("batch or tokens was null");
+    return false;
+  }
+  // The batch's previous step may run on another stream: wait for the device.
+  cudaDeviceSynchronize();
+  return batch_copy(b, b->b->d_tok, tokens, cudaMemcpyHostToDevice);
+}
+
+bool needle_v3_batch_get_next(NeedleV3Batch* b, uint32_t* next) {
+  clear_err();
+  if (!b || !next) {
+    set_err("batch or next was null");
+    return false;
+  }
+  cudaDeviceSynchronize();
+  return batch_copy(b, next, b->b->d_next, cudaMemcpyDeviceToHost);
+}
+
 bool needle_v3_geometry(NeedleV3Handle* h, int64_t* out) {
   clear_err();
   if (!h || !out) {

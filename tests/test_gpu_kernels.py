@@ -1,0 +1,222 @@
+"""GPU parity of the single kernels, through the C ABI (nd_* entry points),
+against the CPU oracle on identical seeded inputs.
+
+Tolerances: index unpacking and int8 quantisation are bit-exact; f32 dot
+products are compared at max|diff| <= 2e-5 * max(1, max|y|) because the GPU
+sums in a different order than the reference's 8-lane loop.
+"""
+import numpy as np
+import pytest
+from conftest import cact_pack, nb, orc
+
+pytestmark = pytest.mark.gpu
+
+
+def dev(torch, a):
+    return torch.from_numpy(np.ascontiguousarray(a)).cuda()
+
+
+def make_weight(torch, out, inp, bits, seed, codebook):
+    rng = np.random.default_rng(seed)
+    idx, norms = cact_pack.random_cq(rng, out, inp, bits)
+    blob = cact_pack.cq_blob(idx, norms, bits)
+    d = dev(torch, np.frombuffer(blob, np.uint8).copy())
+    in_pad = idx.shape[1]
+    packed_ptr = d.data_ptr()
+    norms_ptr = packed_ptr + out * in_pad * bits // 8
+    w = orc.CqWeight(blob, out, inp, bits, codebook)
+    return d, packed_ptr, norms_ptr, w, idx, norms
+
+
+def close(a, b, tol=2e-5):
+    scale = max(1.0, float(np.abs(b).max()))
+    return float(np.abs(a - b).max()) <= tol * scale
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_cq_prepare_is_bit_exact(cuda, bits):
+    torch = cuda
+    rng = np.random.default_rng(0)
+    for inp in (768, 3072, 200):
+        x = rng.normal(size=(3, inp)).astype(np.float32)
+        in_pad = -(-inp // 128) * 128
+        xg = dev(torch, x)
+        xh = torch.zeros(3, in_pad, device="cuda")
+        nb.cq_prepare(xg.data_ptr(), 3, inp, xh.data_ptr(), in_pad)
+        cb = cact_pack.lloyd_codebook()
+        _, _, _, w, _, _ = make_weight(torch, 4, inp, bits, 0, cb)
+        want = np.stack([w.prepare(r) for r in x])
+        assert np.array_equal(xh.cpu().numpy(), want)  # same butterflies, same order
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_cq_index_unpacking_is_bit_exact(cuda, bits):
+    """With one-hot rotated inputs the kernel returns norm * level[idx[r, k]]
+    for every row: the recovered indices must equal the packed ones."""
+    torch = cuda
+    cb = cact_pack.lloyd_codebook()
+    out, inp = 300, 768
+    d, pp, npp, w, idx, norms = make_weight(torch, out, inp, bits, 1, cb)
+    levels = cact_pack.codebook_levels(cb, bits)
+    ks = np.arange(0, inp, 7)[:8]
+    for path in (1, 2):
+        xh = np.zeros((8, inp), np.float32)
+        xh[np.arange(8), ks] = 1.0
+        y = torch.zeros(8, out, device="cuda")
+        nb.cq_project(pp, npp, out, inp, bits, levels, dev(torch, xh).data_ptr(), inp, 8, y.data_ptr(), out,
+                      path=path)
+        torch.cuda.synchronize()
+        yn = y.cpu().numpy()
+        for m, k in enumerate(ks):
+            want = (norms[:, k // 128].astype(np.float32) * levels[idx[:, k]]).astype(np.float32)
+            assert np.array_equal(yn[m], want), (path, k)
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("shape", [(3072, 768), (1568, 768), (768, 768), (8192, 768), (24, 3072), (1000, 300)])
+def test_cq_gemv_matches_oracle(cuda, bits, shape):
+    torch = cuda
+    out, inp = shape
+    cb = cact_pack.random_codebook(np.random.default_rng(9))  # BASELINE config 0 codebook
+    d, pp, npp, w, _, _ = make_weight(torch, out, inp, bits, 2, cb)
+    levels = cact_pack.codebook_levels(cb, bits)
+    rng = np.random.default_rng(3)
+    for M in (1, 2, 3, 5, 8):
+        x = rng.normal(size=(M, inp)).astype(np.float32)
+        xh = np.stack([w.prepare(r) for r in x])
+        y = torch.zeros(M, out, device="cuda")
+        nb.cq_project(pp, npp, out, inp, bits, levels, dev(torch, xh).data_ptr(), xh.shape[1], M, y.data_ptr(),
+                      out, path=1)
+        torch.cuda.synchronize()
+        want = w.matmul_prepared(xh)
+        assert close(y.cpu().numpy(), want), (M, float(np.abs(y.cpu().numpy() - want).max()))
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("n_out", [768, 2304, 3072])
+def test_cq_gemm_matches_oracle_config1(cuda, bits, n_out):
+    """X [512, 768], W [N, 768]."""
+    torch = cuda
+    cb = cact_pack.random_codebook(np.random.default_rng(9))
+    d, pp, npp, w, _, _ = make_weight(torch, n_out, 768, bits, 4, cb)
+    levels = cact_pack.codebook_levels(cb, bits)
+    x = np.random.default_rng(5).normal(size=(512, 768)).astype(np.float32)
+    xg = dev(torch, x)
+    xh = torch.zeros(512, 768, device="cuda")
+    nb.cq_prepare(xg.data_ptr(), 512, 768, xh.data_ptr(), 768)
+    y = torch.zeros(512, n_out, device="cuda")
+    nb.cq_project(pp, npp, n_out, 768, bits, levels, xh.data_ptr(), 768, 512, y.data_ptr(), n_out)
+    torch.cuda.synchronize()
+    want = w.matmul_prepared(np.stack([w.prepare(r) for r in x]))
+    assert close(y.cpu().numpy(), want)
+
+
+def test_cq_row_ranges_and_ragged_sizes(cuda):
+    torch = cuda
+    cb = cact_pack.lloyd_codebook()
+    d, pp, npp, w, _, _ = make_weight(torch, 80, 3072, 4, 6, cb)
+    levels = cact_pack.codebook_levels(cb, 4)
+    x = np.random.default_rng(1).normal(size=(67, 3072)).astype(np.float32)
+    xh = np.stack([w.prepare(r) for r in x])
+    for M, row0, nrows, path in ((1, 4, 4, 0), (1, 16, 16, 0), (67, 40, 24, 0), (67, 0, 80, 2), (9, 3, 61, 0)):
+        y = torch.zeros(M, nrows, device="cuda")
+        nb.cq_project(pp, npp, 80, 3072, 4, levels, dev(torch, xh[:M]).data_ptr(), 3072, M, y.data_ptr(), nrows,
+                      row0=row0, nrows=nrows, path=path)
+        torch.cuda.synchronize()
+        assert close(y.cpu().numpy(), w.matmul_prepared(xh[:M], row0, nrows))
+
+
+def test_cq_rejects_bad_arguments(cuda):
+    torch = cuda
+    cb = cact_pack.lloyd_codebook()
+    d, pp, npp, w, _, _ = make_weight(torch, 8, 128, 2, 0, cb)
+    xh = torch.zeros(1, 128, device="cuda")
+    y = torch.zeros(1, 8, device="cuda")
+    with pytest.raises(nb.NeedleError):
+        nb.cq_project(pp, npp, 8, 128, 2, cb[:4], xh.data_ptr(), 128, 1, y.data_ptr(), 8, row0=4, nrows=8)
+    with pytest.raises(nb.NeedleError):
+        nb.cq_project(pp, npp, 8, 128, 3, cb[4:12], xh.data_ptr(), 128, 1, y.data_ptr(), 8)
+
+
+# ------------------------------------------------------------------ int8 KV
+def test_kv_quant_is_bit_exact(cuda):
+    import json
+    import os
+    from conftest import GOLDEN
+    torch = cuda
+    rng = np.random.default_rng(0)
+    rows = [(rng.normal(size=48) * 10 ** rng.uniform(-4, 4)).astype(np.float32) for _ in range(3000)]
+    with open(os.path.join(GOLDEN, "kv_quant_vectors.json")) as f:
+        for case in json.load(f)["cases"]:
+            rows += list(np.array(case["in"], np.float32).reshape(-1, case["dim"]))
+    for dim in (48, 64):
+        sel = [r[:dim] if len(r) >= dim else np.pad(r, (0, dim - len(r))) for r in rows]
+        x = np.stack(sel).astype(np.float32)
+        q = torch.zeros(x.shape, dtype=torch.int8, device="cuda")
+        s = torch.zeros(len(x), device="cuda")
+        nb.kv_quant(dev(torch, x).data_ptr(), len(x), dim, q.data_ptr(), s.data_ptr())
+        torch.cuda.synchronize()
+        want = [orc.quant_into(r) for r in x]
+        assert np.array_equal(q.cpu().numpy(), np.stack([w[0] for w in want]))
+        assert np.array_equal(s.cpu().numpy(), np.array([w[1] for w in want], np.float32))
+
+
+@pytest.mark.parametrize("int8", [True, False])
+def test_attend_step_config2(cuda, int8):
+    """64 sessions, context 512, 12 query heads (qk 48),
+    2 KV heads (v 64), K/V N(0,1) quantised per (position, head), q fake-quantised."""
+    torch = cuda
+    B, S, H, KVH, QK, VH = 64, 512, 12, 2, 48, 64
+    rng = np.random.default_rng(0)
+    q = rng.normal(size=(B, H, QK)).astype(np.float32)
+    k = rng.normal(size=(B, S, KVH, QK)).astype(np.float32)
+    v = rng.normal(size=(B, S, KVH, VH)).astype(np.float32)
+    lo = np.zeros(B, np.int32)
+    hi = np.full(B, S - 1, np.int32)
+    if int8:
+        q = np.stack([np.stack([orc.fake_quant(h) for h in s]) for s in q])
+        kq = np.zeros(k.shape, np.int8)
+        vq = np.zeros(v.shape, np.int8)
+        ks = np.zeros((B, S, KVH), np.float32)
+        vs = np.zeros((B, S, KVH), np.float32)
+        for b in range(B):
+            for p in range(S):
+                for h in range(KVH):
+                    kq[b, p, h], ks[b, p, h] = orc.quant_into(k[b, p, h])
+                    vq[b, p, h], vs[b, p, h] = orc.quant_into(v[b, p, h])
+        args = (dev(torch, kq), dev(torch, vq), dev(torch, ks), dev(torch, vs))
+    else:
+        args = (dev(torch, k), dev(torch, v), None, None)
+    out = torch.zeros(B, H * VH, device="cuda")
+    nb.attend_step(dev(torch, q).data_ptr(), args[0].data_ptr(), args[1].data_ptr(),
+                   args[2].data_ptr() if int8 else None, args[3].data_ptr() if int8 else None, int8, S,
+                   dev(torch, lo).data_ptr(), dev(torch, hi).data_ptr(), B, H, KVH, QK, VH, out.data_ptr())
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b in range(0, B, 7):
+        if int8:
+            want = orc.attend_step(q[b].ravel(), S, 0, S - 1, H, KVH, QK, VH, kq=kq[b].ravel(), ks=ks[b].ravel(),
+                                   vq=vq[b].ravel(), vs=vs[b].ravel())
+        else:
+            want = orc.attend_step(q[b].ravel(), S, 0, S - 1, H, KVH, QK, VH, k=k[b].ravel(), v=v[b].ravel())
+        assert close(got[b], want, 1e-4)
+
+
+def test_attend_step_ring_wrap_and_ragged_ranges(cuda):
+    torch = cuda
+    B, S, H, KVH, QK, VH = 5, 17, 4, 2, 48, 64
+    rng = np.random.default_rng(1)
+    q = rng.normal(size=(B, H, QK)).astype(np.float32)
+    k = rng.normal(size=(B, S, KVH, QK)).astype(np.float32)
+    v = rng.normal(size=(B, S, KVH, VH)).astype(np.float32)
+    ranges = [(0, 0), (0, 9), (3, 16), (5, 5), (20, 36)]  # the last wraps the 17-slot ring
+    lo = np.array([r[0] for r in ranges], np.int32)
+    hi = np.array([r[1] for r in ranges], np.int32)
+    out = torch.zeros(B, H * VH, device="cuda")
+    nb.attend_step(dev(torch, q).data_ptr(), dev(torch, k).data_ptr(), dev(torch, v).data_ptr(), None, None, 0, S,
+                   dev(torch, lo).data_ptr(), dev(torch, hi).data_ptr(), B, H, KVH, QK, VH, out.data_ptr())
+    torch.cuda.synchronize()
+    got = out.cpu().numpy()
+    for b, (l, h) in enumerate(ranges):
+        want = orc.attend_step(q[b].ravel(), S, l, h, H, KVH, QK, VH, k=k[b].ravel(), v=v[b].ravel())
+        assert close(got[b], want, 1e-4)

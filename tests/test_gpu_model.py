@@ -1,0 +1,136 @@
+"""GPU engine parity: full Needle-3 forward through the C ABI against the CPU
+oracle on the same seeded containers and prompts.
+
+Bar: logits within 1e-3 of the oracle relative to the
+logit RMS, and token-exact greedy output, for f32 and int8 KV caches.
+"""
+import numpy as np
+import pytest
+from conftest import nb, orc
+
+pytestmark = pytest.mark.gpu
+
+REL = 1e-3
+
+
+def rel_err(a, b):
+    return float(np.abs(a - b).max() / np.sqrt(np.mean(b.astype(np.float64) ** 2)))
+
+
+def test_geometry_and_sizes_match(tiny_gpu, tiny_oracle, full_gpu, full_oracle):
+    for g, o in ((tiny_gpu, tiny_oracle), (full_gpu, full_oracle)):
+        assert g.geometry == o.geometry
+        for n in (1, 7, 512, 1025, 8192):
+            for int8 in (False, True):
+                assert g.kv_bytes(n, int8) == o.kv_bytes(n, int8)
+    assert full_gpu.max_seq_len() == 8192 and full_gpu.num_layers() == 20
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_tiny_prefill_then_decode(tiny_gpu, tiny_oracle, int8):
+    """Tiny geometry: window 8 with ring wrap, global layers, two Engram sites,
+    logit_rows < vocab. Prompt 20, then 30 decode steps fed the oracle's tokens."""
+    toks = np.random.default_rng(11).integers(1, 512, 20).astype(np.uint32)
+    g = tiny_gpu.session(8, int8)  # small hint: global rings must grow
+    o = tiny_oracle.session(8, int8)
+    lg, lo = g.prefill(toks), o.prefill(toks)
+    assert rel_err(lg, lo) < REL
+    for _ in range(30):
+        t = int(np.argmax(lo))
+        assert int(np.argmax(lg)) == t
+        lg, lo = g.decode_step(t), o.decode_step(t)
+        assert rel_err(lg, lo) < REL
+    assert g.pos == o.pos == 50
+    for li in range(4):
+        assert g.slots(li) == o.slots(li)
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_decode_steps_match_prefill_on_gpu(tiny_gpu, int8):
+    toks = np.random.default_rng(2).integers(1, 512, 24).astype(np.uint32)
+    s = tiny_gpu.session(24, int8)
+    s.prefill(toks[:4])
+    for t in toks[4:-1]:
+        s.decode_step(t)
+    stepped = s.decode_step(toks[-1])
+    p = tiny_gpu.session(24, int8)
+    assert rel_err(stepped, p.prefill(toks)) < 1e-4
+
+
+@pytest.mark.parametrize("int8", [False, True])
+def test_full_config3_token_exact(full_gpu, full_oracle, int8):
+    """shipped geometry, 256-token prompt of ids in [1, 8192),
+    greedy decode of 64 tokens, f32 and int8 KV."""
+    prompt = np.random.default_rng(0).integers(1, 8192, 256).astype(np.uint32)
+    want_tokens, want_logits = orc.greedy(full_oracle, prompt, 64, int8)
+    s = full_gpu.session(320, int8)
+    lg = s.prefill(prompt)
+    worst = rel_err(lg, want_logits[0])
+    got = []
+    for i in range(64):
+        t = int(np.argmax(lg))
+        got.append(t)
+        lg = s.decode_step(int(want_tokens[i]))
+        worst = max(worst, rel_err(lg, want_logits[i + 1]))
+    assert worst < REL, worst
+    assert np.array_equal(np.array(got, np.uint32), want_tokens)
+    ids = full_gpu.generate_ids(prompt, 64, kv_int8=int8)
+    assert np.array_equal(ids, want_tokens)
+
+
+def test_batched_sessions_match_single_sessions(full_gpu):
+    rng = np.random.default_rng(3)
+    prompts = [rng.integers(1, 8192, n).astype(np.uint32) for n in (5, 40, 17, 64, 9, 33, 12, 70, 21, 3)]
+    for int8 in (False, True):
+        singles = [full_gpu.session(128, int8) for _ in prompts]
+        ref = [s.prefill(p) for s, p in zip(singles, prompts)]
+        batch = [full_gpu.session(128, int8) for _ in prompts]
+        lg, picks = full_gpu.prefill_batch(batch, prompts)
+        for a, b in zip(lg, ref):
+            assert rel_err(a, b) < 1e-4
+        assert np.array_equal(picks, np.array([int(np.argmax(r)) for r in ref]))
+        toks = picks
+        for _ in range(6):
+            lg, picks = full_gpu.decode_batch(batch, toks)
+            ref = [s.decode_step(int(t)) for s, t in zip(singles, toks)]
+            for a, b in zip(lg, ref):
+                assert rel_err(a, b) < 1e-4
+            toks = picks
+
+
+def test_device_batch_graph_matches_eager(full_gpu, cuda):
+    """The CUDA-graph replay of a batched decode step gives the same tokens and
+    logits as the eager launch sequence (and both match single sessions)."""
+    torch = cuda
+    rng = np.random.default_rng(4)
+    prompts = [rng.integers(1, 8192, 24).astype(np.uint32) for _ in range(12)]
+    outs = []
+    for use_graph in (False, True):
+        ss = [full_gpu.session(64, True) for _ in prompts]
+        _, picks = full_gpu.prefill_batch(ss, prompts, logits=False)
+        b = full_gpu.batch(ss)
+        b.set_tokens(picks)
+        logits = torch.zeros(12, full_gpu.logit_rows, device="cuda")
+        seq = []
+        for _ in range(8):
+            b.step(logits.data_ptr(), use_graph=use_graph)
+            b.feed_next()
+            torch.cuda.synchronize()
+            seq.append((b.get_next(), logits.cpu().numpy().copy()))
+        outs.append(seq)
+        assert all(s.pos == 24 + 8 for s in ss)
+    for (ta, la), (tb, lb) in zip(*outs):
+        assert np.array_equal(ta, tb)
+        assert np.array_equal(la, lb)
+
+
+def test_engine_errors_are_reported(full_gpu):
+    s = full_gpu.session(8)
+    s.prefill(np.arange(1, 5, dtype=np.uint32))
+    with pytest.raises(nb.NeedleError, match="fresh session"):
+        s.prefill(np.arange(1, 5, dtype=np.uint32))
+    a, b = full_gpu.session(8, False), full_gpu.session(8, True)
+    with pytest.raises(nb.NeedleError, match="precision"):
+        full_gpu.prefill_batch([a, b], [[1, 2], [3, 4]])
+    with pytest.raises(nb.NeedleError):
+        full_gpu.session(8).prefill(np.ones(8193, np.uint32))
