@@ -148,6 +148,14 @@ bool needle_v3_batch_feed_next(NeedleV3Batch *batch, void *stream);
 bool needle_v3_batch_set_tokens(NeedleV3Batch *batch, const uint32_t *tokens);
 bool needle_v3_batch_get_next(NeedleV3Batch *batch, uint32_t *next);
 
+/* One eager decode step of the batch with CUDA events between kernel groups
+ * (advances every session by one position like needle_v3_batch_step). Writes
+ * milliseconds per group to ms[12] — engram, embed, layer_pre, qkvg
+ * projection, qkv_post, attention, attention finish, out projection,
+ * layer_post, final norm, LM head, bookkeeping — and this library's kernel
+ * launch count for the step to *launches. Synchronous. */
+bool needle_v3_batch_profile(NeedleV3Batch *batch, float *ms, int *launches);
+
 /* Geometry: vocab, out_vocab, d_model, heads, kv_heads, layers, qk, v_head,
  * max_seq, hada_n, lanes, window, conv_taps, logit_rows (14 int64). */
 bool needle_v3_geometry(NeedleV3Handle *handle, int64_t *out14);

@@ -73,6 +73,7 @@ def lib() -> C.CDLL:
         "needle_v3_batch_step": (b, [vp, vp, vp, b]),
         "needle_v3_batch_feed_next": (b, [vp, vp]),
         "needle_v3_batch_set_tokens": (b, [vp, vp]),
+        "needle_v3_batch_profile": (b, [vp, vp, vp]),
         "needle_v3_batch_get_next": (b, [vp, vp]),
         "needle_v3_geometry": (b, [vp, vp]),
         "needle_v3_device": (C.c_int, [vp]),
@@ -286,6 +287,17 @@ class Batch:
         assert len(t) == len(self.sessions)
         if not lib().needle_v3_batch_set_tokens(self._b, t.ctypes.data):
             _fail("needle_v3_batch_set_tokens")
+
+    PROFILE_KINDS = ("engram", "embed", "layer_pre", "qkvg_proj", "qkv_post", "attention", "attn_finish",
+                     "out_proj", "layer_post", "final", "lm_head", "bookkeeping")
+
+    def profile(self):
+        """One eager step with per-kernel-group timing: ({kind: ms}, launches)."""
+        ms = np.zeros(12, np.float32)
+        n = C.c_int(0)
+        if not lib().needle_v3_batch_profile(self._b, ms.ctypes.data, C.addressof(n)):
+            _fail("needle_v3_batch_profile")
+        return dict(zip(self.PROFILE_KINDS, (float(x) for x in ms))), n.value
 
     def get_next(self) -> np.ndarray:
         out = np.zeros(len(self.sessions), np.uint32)

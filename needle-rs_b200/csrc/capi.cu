@@ -16,14 +16,14 @@
 #include "engine.hpp"
 
 struct NeedleV3Handle {
-  std::unique_ptr<nb::Engine> eng;
+  std::shared_ptr<nb::Engine> eng;
 };
 struct NeedleV3Session {
-  NeedleV3Handle* h;
+  std::shared_ptr<nb::Engine> eng;  // keeps the engine alive until this object is freed
   std::unique_ptr<nb::Session> s;
 };
 struct NeedleV3Batch {
-  NeedleV3Handle* h;
+  std::shared_ptr<nb::Engine> eng;  // keeps the engine alive until this object is freed
   std::unique_ptr<nb::Batch> b;
 };
 
@@ -293,7 +293,7 @@ NeedleV3Session* needle_v3_session_new(NeedleV3Handle* h, size_t hint, bool kv_i
     return nullptr;
   }
   NeedleV3Session* r = new NeedleV3Session();
-  r->h = h;
+  r->eng = h->eng;
   r->s.reset(s);
   return r;
 }
@@ -339,7 +339,7 @@ static bool check_sessions(NeedleV3Handle* h, NeedleV3Session* const* ss, size_t
   }
   out->resize(n);
   for (size_t i = 0; i < n; ++i) {
-    if (!ss[i] || ss[i]->h != h) {
+    if (!ss[i] || ss[i]->eng != h->eng) {
       set_err("session was null or belongs to another handle");
       return false;
     }
@@ -480,7 +480,7 @@ NeedleV3Batch* needle_v3_batch_new(NeedleV3Handle* h, NeedleV3Session* const* ss
     return nullptr;
   }
   NeedleV3Batch* r = new NeedleV3Batch();
-  r->h = h;
+  r->eng = h->eng;
   r->b.reset(b);
   return r;
 }
@@ -511,7 +511,7 @@ bool needle_v3_batch_step(NeedleV3Batch* b, float* d_logits, void* stream, bool 
     set_err("batch was null");
     return false;
   }
-  nb::Engine* E = b->h->eng.get();
+  nb::Engine* E = b->eng.get();
   cudaStream_t st = stream ? (cudaStream_t)stream : E->stream;
   std::string err;
   if (!E->decode_batch_device(b->b.get(), d_logits, st, use_graph, &err)) {
@@ -527,7 +527,7 @@ bool needle_v3_batch_feed_next(NeedleV3Batch* b, void* stream) {
     set_err("batch was null");
     return false;
   }
-  nb::Engine* E = b->h->eng.get();
+  nb::Engine* E = b->eng.get();
   cudaStream_t st = stream ? (cudaStream_t)stream : E->stream;
   cudaError_t e = cudaMemcpyAsync(b->b->d_tok, b->b->d_next, b->b->sessions.size() * 4,
                                   cudaMemcpyDeviceToDevice, st);
@@ -538,8 +538,22 @@ bool needle_v3_batch_feed_next(NeedleV3Batch* b, void* stream) {
   return true;
 }
 
+bool needle_v3_batch_profile(NeedleV3Batch* b, float* ms, int* launches) {
+  clear_err();
+  if (!b || !ms || !launches) {
+    set_err("batch, ms or launches was null");
+    return false;
+  }
+  std::string err;
+  if (!b->eng->profile_batch_step(b->b.get(), ms, launches, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
 static bool batch_copy(NeedleV3Batch* b, void* dst, const void* src, cudaMemcpyKind kind) {
-  nb::Engine* E = b->h->eng.get();
+  nb::Engine* E = b->eng.get();
   cudaError_t e = cudaMemcpyAsync(dst, src, b->b->sessions.size() * 4, kind, E->stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(E->stream);
   if (e != cudaSuccess) {
@@ -586,6 +600,30 @@ bool needle_v3_geometry(NeedleV3Handle* h, int64_t* out) {
 }
 
 int needle_v3_device(NeedleV3Handle* h) { return h ? h->eng->device : -1; }
+
+// Copies one engine workspace buffer (the last forward's intermediates) to the
+// host, for debugging and tests: 0 xh, 1 proj, 2 qpost, 3 attn, 4 oh, 5 projo,
+// 6 prefill keys (f32), 7 prefill values (f32), 8 lanes, 9 u, 10 bx, 11 lm_in.
+bool needle_v3_debug_buffer(NeedleV3Handle* h, int which, float* out, size_t count) {
+  clear_err();
+  if (!h || !out) {
+    set_err("handle or out was null");
+    return false;
+  }
+  nb::Workspace& w = h->eng->ws;
+  const void* src[] = {w.xh, w.proj, w.qpost, w.attn, w.oh, w.projo, w.pk, w.pv, w.lanes, w.u, w.bx, w.lm_in};
+  if (which < 0 || which >= (int)(sizeof(src) / sizeof(src[0])) || !src[which]) {
+    set_err("no such buffer");
+    return false;
+  }
+  cudaError_t e = cudaStreamSynchronize(h->eng->stream);
+  if (e == cudaSuccess) e = cudaMemcpy(out, src[which], count * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    set_err(cudaGetErrorString(e));
+    return false;
+  }
+  return true;
+}
 
 // ------------------------------------------------------------------ Part 3
 int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, int bits,

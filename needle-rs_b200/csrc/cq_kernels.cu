@@ -58,11 +58,13 @@ __device__ __forceinline__ void build_lut_smem(const CqMat& W, float* lut) {
   }
 }
 
+// Segment holding logical row r: walk the segments in order and stop at the
+// first one whose end lies beyond r.
 __device__ __forceinline__ int find_seg(const CqMat& W, int r, int* local) {
   int s = 0, base = 0;
 #pragma unroll
-  for (int i = 0; i < MAX_SEG; ++i) {
-    if (i < W.nseg - 1 && r >= base + W.seg[i].rows) {
+  for (int i = 0; i < MAX_SEG - 1; ++i) {
+    if (s == i && i < W.nseg - 1 && r >= base + W.seg[i].rows) {
       base += W.seg[i].rows;
       s = i + 1;
     }

@@ -712,7 +712,23 @@ bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
 }
 
 // ------------------------------------------------------------------ forward
-cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8) {
+cudaError_t Prof::mark(int kind, cudaStream_t st, int nlaunch) {
+  launches += nlaunch;
+  if (used == marks.size()) {
+    cudaEvent_t ev;
+    NB_TRY(cudaEventCreate(&ev));
+    marks.push_back({kind, ev});
+  }
+  marks[used].first = kind;
+  NB_TRY(cudaEventRecord(marks[used].second, st));
+  ++used;
+  return cudaSuccess;
+}
+
+#define NB_MARK(kind, n) \
+  if (prof) NB_TRY(prof->mark(kind, st, n))
+
+cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, Prof* prof) {
   const int M = rb.M, d = G.d, S = G.n_sites;
   const int dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   if (S > 0) {
@@ -721,28 +737,40 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8) {
       NB_TRY(cq_project(eng_kv[s], ws.fetched + (size_t)s * d, S * d, M, ws.ekv + (size_t)s * 2 * d,
                         S * 2 * d, 0, 2 * d, st));
     NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, ws.ekv, ws.evc, st));
+    NB_MARK(PK_ENGRAM, S + 2);
   }
   NB_TRY(launch_embed(G, emb, rb, ws.lanes, st));
+  NB_MARK(PK_EMBED, 1);
   for (int l = 0; l < G.layers; ++l) {
     NB_TRY(launch_layer_pre(G, l, rb, ws.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
                             site_of[l], ws.ekv, ws.evc, ws.u, ws.bx, ws.xh, ws.gates, st));
+    NB_MARK(PK_LAYER_PRE, 1);
     NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st));
+    NB_MARK(PK_QKVG, 1);
     NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, st));
+    NB_MARK(PK_QKV_POST, 1);
     NB_TRY(launch_attention(G, l, rb, lp[l], ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, ws.attn, st, int8 ? 1 : 0));
+    NB_MARK(PK_ATTN, 1);
     NB_TRY(launch_attn_finish(G, rb, ws.attn, ws.proj, ws.oh, st));
+    NB_MARK(PK_ATTN_FINISH, 1);
     NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st));
+    NB_MARK(PK_OUT_PROJ, 1);
     NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, ws.projo, ws.u, ws.bx,
                              ws.gates, ws.lanes, st));
+    NB_MARK(PK_LAYER_POST, 1);
   }
   NB_TRY(launch_final(G, rb, ws.lanes, final_norm, ws.lm_in, st));
+  NB_MARK(PK_FINAL, 1);
   return cudaSuccess;
 }
 
 // Tied head over logit_rows (model.rs:358-374, :942-978) and the greedy pick.
 cudaError_t Engine::head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
-                         cudaStream_t st) {
+                         cudaStream_t st, Prof* prof) {
   NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st));
+  NB_MARK(PK_HEAD, 1);
   if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
+  NB_MARK(PK_BOOK, picks ? 1 : 0);
   return cudaSuccess;
 }
 
@@ -992,6 +1020,50 @@ bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, boo
     *err = cuda_msg("batched decode step", e);
     return false;
   }
+  for (Session* s : b->sessions) s->pos += 1;
+  return true;
+}
+
+bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  const size_t n = b->sessions.size();
+  for (Session* s : b->sessions) {
+    if (s->pos >= cfg.max_seq) {
+      *err = "session reached max_seq_len";
+      return false;
+    }
+    if (!ensure_slots(s, s->pos, err)) return false;
+  }
+  if (!ensure_ws(n, err) || !ensure_logits(this, n, err)) return false;
+  const int dpad = (G.d + 127) / 128 * 128;
+  RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
+  Prof prof;
+  cudaStream_t st = stream;
+  auto run = [&]() -> cudaError_t {
+    Prof* p = &prof;
+    NB_TRY(p->mark(PK_BOOK, st, 0));
+    NB_TRY(launch_step_begin(rb, b->d_sess, st));
+    NB_TRY(p->mark(PK_BOOK, st, 1));
+    NB_TRY(forward(rb, st, b->int8, p));
+    NB_TRY(launch_step_end(rb, st));
+    NB_TRY(p->mark(PK_BOOK, st, 1));
+    NB_TRY(head(ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p));
+    return cudaStreamSynchronize(st);
+  };
+  cudaError_t e = run();
+  for (int k = 0; k < PK_COUNT; ++k) ms[k] = 0.f;
+  for (size_t i = 1; e == cudaSuccess && i < prof.used; ++i) {
+    float t = 0.f;
+    e = cudaEventElapsedTime(&t, prof.marks[i - 1].second, prof.marks[i].second);
+    ms[prof.marks[i].first] += t;
+  }
+  for (auto& m : prof.marks) cudaEventDestroy(m.second);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("profiled decode step", e);
+    return false;
+  }
+  *launches = prof.launches;
   for (Session* s : b->sessions) s->pos += 1;
   return true;
 }

@@ -86,9 +86,27 @@ class Batch {
   uint32_t* d_next = nullptr;  // [n] greedy pick of this step
 };
 
+// Kernel groups of one forward, for per-kernel timing.
+enum ProfKind {
+  PK_ENGRAM = 0, PK_EMBED, PK_LAYER_PRE, PK_QKVG, PK_QKV_POST, PK_ATTN, PK_ATTN_FINISH, PK_OUT_PROJ,
+  PK_LAYER_POST, PK_FINAL, PK_HEAD, PK_BOOK, PK_COUNT
+};
+
+// Events recorded after each launch group of a step; `launches` counts this
+// library's kernel launches.
+struct Prof {
+  std::vector<std::pair<int, cudaEvent_t>> marks;
+  size_t used = 0;
+  int launches = 0;
+  cudaError_t mark(int kind, cudaStream_t st, int nlaunch);
+};
+
 class Engine {
  public:
   static Engine* load(const uint8_t* data, size_t len, std::string* err);
+  // One decode step of `b`, eager, with events between kernel groups; writes
+  // per-kind milliseconds (PK_COUNT floats) and the number of launches.
+  bool profile_batch_step(Batch* b, float* ms, int* launches, std::string* err);
   ~Engine();
 
   HostConfig cfg;
@@ -129,9 +147,9 @@ class Engine {
 
   bool ensure_ws(size_t rows, std::string* err);
   bool ensure_slots(Session* s, size_t pos, std::string* err);
-  cudaError_t forward(const RowBatch& rb, cudaStream_t st, bool int8);
+  cudaError_t forward(const RowBatch& rb, cudaStream_t st, bool int8, Prof* prof = nullptr);
   cudaError_t head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
-                   cudaStream_t st);
+                   cudaStream_t st, Prof* prof = nullptr);
 };
 
 }  // namespace nb

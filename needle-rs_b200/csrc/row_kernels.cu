@@ -191,11 +191,11 @@ __device__ __forceinline__ float sinkhorn_lane(float m, int n) {
 __device__ __forceinline__ float cq_row_dot_warp(const CqMat& W, int row_index, const float* xs) {
   const int lane = threadIdx.x & 31;
   int local, s = 0, base = 0;
-  for (int i = 0; i < W.nseg - 1; ++i)
-    if (row_index >= base + W.seg[i].rows) {
-      base += W.seg[i].rows;
-      s = i + 1;
-    }
+  for (int i = 0; i < W.nseg - 1; ++i) {
+    if (row_index < base + W.seg[i].rows) break;
+    base += W.seg[i].rows;
+    s = i + 1;
+  }
   local = row_index - base;
   const uint8_t* row = W.seg[s].packed + (size_t)local * W.row_bytes;
   const __half* nrm = W.seg[s].norms + (size_t)local * W.groups;

@@ -179,6 +179,7 @@ void* orc_session_new(void* mp, size_t hint, int int8) {
   return new V3Cache(((V3Model*)mp)->cfg, hint, int8 ? KvPrecision::Int8 : KvPrecision::F32);
 }
 void orc_session_free(void* s) { delete (V3Cache*)s; }
+void* orc_session_clone(void* s) { return new V3Cache(*(V3Cache*)s); }
 size_t orc_session_pos(void* s) { return ((V3Cache*)s)->pos; }
 size_t orc_session_bytes(void* s) { return ((V3Cache*)s)->bytes(); }
 size_t orc_session_slots(void* s, size_t li) { return ((V3Cache*)s)->layers[li].slots; }

@@ -26,14 +26,15 @@ def build():
 def lib():
     global _lib
     if _lib is None:
-        if not os.path.exists(LIB_PATH):
-            build()
+        if not os.path.exists(LIB_PATH) or os.environ.get("NEEDLE_ORACLE_REBUILD", "1") == "1":
+            build()  # make is incremental: a no-op when the library is current
         _lib = C.CDLL(LIB_PATH)
         vp, sz = C.c_void_p, C.c_size_t
         for name, res, args in [
             ("orc_cq_new", vp, [vp, sz, sz, sz, sz, C.c_int, vp, C.c_char_p, sz]),
             ("orc_model_load", vp, [C.c_char_p, sz, C.c_char_p, sz]),
             ("orc_session_new", vp, [vp, sz, C.c_int]),
+            ("orc_session_clone", vp, [vp]),
             ("orc_quant_into", C.c_float, [vp, vp, sz]),
             ("orc_f16_to_f32", C.c_float, [C.c_uint16]),
             ("orc_cq_in_padded", sz, [vp]),
@@ -217,9 +218,12 @@ class Model:
 
 
 class Session:
-    def __init__(self, m: Model, hint: int, int8: bool):
+    def __init__(self, m: Model, hint: int, int8: bool, handle=None):
         self.m = m
-        self.h = lib().orc_session_new(m.h, hint, int(int8))
+        self.h = handle if handle is not None else lib().orc_session_new(m.h, hint, int(int8))
+
+    def clone(self):
+        return Session(self.m, 0, False, handle=lib().orc_session_clone(self.h))
 
     def __del__(self):
         if getattr(self, "h", None):

@@ -63,7 +63,8 @@ def test_cq_index_unpacking_is_bit_exact(cuda, bits):
         xh = np.zeros((8, inp), np.float32)
         xh[np.arange(8), ks] = 1.0
         y = torch.zeros(8, out, device="cuda")
-        nb.cq_project(pp, npp, out, inp, bits, levels, dev(torch, xh).data_ptr(), inp, 8, y.data_ptr(), out,
+        xd = dev(torch, xh)
+        nb.cq_project(pp, npp, out, inp, bits, levels, xd.data_ptr(), inp, 8, y.data_ptr(), out,
                       path=path)
         torch.cuda.synchronize()
         yn = y.cpu().numpy()
@@ -85,7 +86,8 @@ def test_cq_gemv_matches_oracle(cuda, bits, shape):
         x = rng.normal(size=(M, inp)).astype(np.float32)
         xh = np.stack([w.prepare(r) for r in x])
         y = torch.zeros(M, out, device="cuda")
-        nb.cq_project(pp, npp, out, inp, bits, levels, dev(torch, xh).data_ptr(), xh.shape[1], M, y.data_ptr(),
+        xd = dev(torch, xh)
+        nb.cq_project(pp, npp, out, inp, bits, levels, xd.data_ptr(), xh.shape[1], M, y.data_ptr(),
                       out, path=1)
         torch.cuda.synchronize()
         want = w.matmul_prepared(xh)
@@ -120,7 +122,8 @@ def test_cq_row_ranges_and_ragged_sizes(cuda):
     xh = np.stack([w.prepare(r) for r in x])
     for M, row0, nrows, path in ((1, 4, 4, 0), (1, 16, 16, 0), (67, 40, 24, 0), (67, 0, 80, 2), (9, 3, 61, 0)):
         y = torch.zeros(M, nrows, device="cuda")
-        nb.cq_project(pp, npp, 80, 3072, 4, levels, dev(torch, xh[:M]).data_ptr(), 3072, M, y.data_ptr(), nrows,
+        xd = dev(torch, xh[:M])
+        nb.cq_project(pp, npp, 80, 3072, 4, levels, xd.data_ptr(), 3072, M, y.data_ptr(), nrows,
                       row0=row0, nrows=nrows, path=path)
         torch.cuda.synchronize()
         assert close(y.cpu().numpy(), w.matmul_prepared(xh[:M], row0, nrows))
@@ -154,7 +157,8 @@ def test_kv_quant_is_bit_exact(cuda):
         x = np.stack(sel).astype(np.float32)
         q = torch.zeros(x.shape, dtype=torch.int8, device="cuda")
         s = torch.zeros(len(x), device="cuda")
-        nb.kv_quant(dev(torch, x).data_ptr(), len(x), dim, q.data_ptr(), s.data_ptr())
+        xd = dev(torch, x)
+        nb.kv_quant(xd.data_ptr(), len(x), dim, q.data_ptr(), s.data_ptr())
         torch.cuda.synchronize()
         want = [orc.quant_into(r) for r in x]
         assert np.array_equal(q.cpu().numpy(), np.stack([w[0] for w in want]))
@@ -188,9 +192,10 @@ def test_attend_step_config2(cuda, int8):
     else:
         args = (dev(torch, k), dev(torch, v), None, None)
     out = torch.zeros(B, H * VH, device="cuda")
-    nb.attend_step(dev(torch, q).data_ptr(), args[0].data_ptr(), args[1].data_ptr(),
+    qd, lod, hid = dev(torch, q), dev(torch, lo), dev(torch, hi)  # keep the device copies alive
+    nb.attend_step(qd.data_ptr(), args[0].data_ptr(), args[1].data_ptr(),
                    args[2].data_ptr() if int8 else None, args[3].data_ptr() if int8 else None, int8, S,
-                   dev(torch, lo).data_ptr(), dev(torch, hi).data_ptr(), B, H, KVH, QK, VH, out.data_ptr())
+                   lod.data_ptr(), hid.data_ptr(), B, H, KVH, QK, VH, out.data_ptr())
     torch.cuda.synchronize()
     got = out.cpu().numpy()
     for b in range(0, B, 7):
@@ -213,8 +218,9 @@ def test_attend_step_ring_wrap_and_ragged_ranges(cuda):
     lo = np.array([r[0] for r in ranges], np.int32)
     hi = np.array([r[1] for r in ranges], np.int32)
     out = torch.zeros(B, H * VH, device="cuda")
-    nb.attend_step(dev(torch, q).data_ptr(), dev(torch, k).data_ptr(), dev(torch, v).data_ptr(), None, None, 0, S,
-                   dev(torch, lo).data_ptr(), dev(torch, hi).data_ptr(), B, H, KVH, QK, VH, out.data_ptr())
+    keep = [dev(torch, a) for a in (q, k, v, lo, hi)]  # keep the device copies alive until the kernel ran
+    nb.attend_step(keep[0].data_ptr(), keep[1].data_ptr(), keep[2].data_ptr(), None, None, 0, S,
+                   keep[3].data_ptr(), keep[4].data_ptr(), B, H, KVH, QK, VH, out.data_ptr())
     torch.cuda.synchronize()
     got = out.cpu().numpy()
     for b, (l, h) in enumerate(ranges):
