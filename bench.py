@@ -1,0 +1,419 @@
+"""Benchmark: Needle-3 batched decode tokens/s on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
+
+Workload (config 4): 4096 independent sessions in total, split evenly across
+the ranks (one process per GPU, no collective on the data path), each prefilled
+with a 1024-token prompt of uniform random ids in [1, 8192) (seed = session
+index), int8 KV cache, then decoded greedily. A step is one decode position for
+every local session. `value` is whole-box decode tokens/s with the step's
+inputs (tokens, KV rings, weights) resident in HBM, timed with CUDA events on
+the launch stream, max over ranks; `e2e` is the same metric through the host
+API (host tokens in, host picks out every step).
+
+The model is a random-init container with the shipped Needle-3 geometry written
+by the seeded packer (no checkpoint is available offline).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+PKG_DIR = os.path.join(ROOT, "needle-rs_b200")
+PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+HBM_FALLBACK, BF16_FALLBACK = 6650.0, 1590.0
+
+
+def pkg():
+    if "needle_b200" in sys.modules:
+        return sys.modules["needle_b200"]
+    spec = importlib.util.spec_from_file_location(
+        "needle_b200", os.path.join(PKG_DIR, "__init__.py"), submodule_search_locations=[PKG_DIR])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["needle_b200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def container(seed: int = 0) -> bytes:
+    from needle_b200 import cact_pack
+    cache = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"needle3_random_seed{seed}.cact")
+    if os.path.exists(cache):
+        return open(cache, "rb").read()
+    raw = cact_pack.build_container(cact_pack.shipped(), seed=seed)
+    tmp = f"{cache}.{os.getpid()}"
+    with open(tmp, "wb") as f:
+        f.write(raw)
+    os.replace(tmp, cache)
+    return raw
+
+
+def peaks():
+    if os.path.exists(PEAKS):
+        with open(PEAKS) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    return HBM_FALLBACK, BF16_FALLBACK, "fallback"
+
+
+def prompt(i: int, n: int) -> np.ndarray:
+    return np.random.default_rng(i).integers(1, 8192, n).astype(np.uint32)
+
+
+# ------------------------------------------------------------------ clocks
+class Clocks:
+    """nvidia-smi sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu, self.rows, self.proc = gpu, [], None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.rows.append([x.strip() for x in line.split(",")])
+
+    def __exit__(self, *a):
+        if self.proc:
+            time.sleep(0.3)
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        if not self.rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in self.rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in self.rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[k] for r in self.rows for k in range(4) if len(r) > 4 + k and r[4 + k] == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(self.rows)}
+
+
+# ------------------------------------------------------------------ CPU baseline (oracle port)
+def cpu_decode_sample(raw: bytes, ctx: int, steps: int, sessions: int | None = None):
+    """The oracle (C++ restatement of the reference CPU path) decoding `sessions`
+    int8 sessions at context `ctx` in parallel, one host thread each: one
+    session is prefilled (all cores), cloned, then every clone decodes
+    `steps` tokens. Returns (tok/s, threads, seconds, sample text)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    ncpu = os.cpu_count() or 1
+    n = sessions or ncpu
+    m = orc.Model(raw)
+    orc.set_threads(ncpu)
+    base = m.session(ctx + steps + 1, True)
+    base.prefill(prompt(0, ctx))
+    clones = [base.clone() for _ in range(n)]
+    orc.set_threads(1)
+    toks = prompt(1, steps)
+
+    def run(s):
+        for t in toks:
+            s.decode_step(int(t))
+
+    threads = [threading.Thread(target=run, args=(s,)) for s in clones]
+    t0 = time.perf_counter()
+    for th in threads:
+        th.start()
+    for th in threads:
+        th.join()
+    dt = time.perf_counter() - t0
+    orc.set_threads(ncpu)
+    tps = n * steps / dt
+    return tps, n, dt, f"{n} int8 sessions at context {ctx}, {steps} decode steps each, one host thread per session"
+
+
+def reference_arm(args):
+    """--impl reference: the reference's CPU path on the host cores. The Rust
+    reference cannot be built here (no Rust toolchain), so its C++ restatement
+    (oracle/) is timed, with all host threads."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    raw = container(0)
+    ncpu = os.cpu_count() or 1
+    ctx = 1024
+    # Each step: every host thread decodes one token of its own session.
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    m = orc.Model(raw)
+    orc.set_threads(ncpu)
+    base = m.session(ctx + args.steps + args.warmup + 2, True)
+    base.prefill(prompt(0, ctx))
+    clones = [base.clone() for _ in range(ncpu)]
+    orc.set_threads(1)
+
+    def one_step(t):
+        ths = [threading.Thread(target=s.decode_step, args=(t,)) for s in clones]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+
+    for i in range(args.warmup):
+        one_step(100 + i)
+    t0 = time.perf_counter()
+    for i in range(args.steps):
+        one_step(200 + i)
+    dt = time.perf_counter() - t0
+    value = ncpu * args.steps / dt
+    sample = (f"{ncpu} int8 sessions at context {ctx} (oracle C++ port of the reference CPU path, "
+              f"one host thread per session), {args.steps} timed steps")
+    print(json.dumps({
+        "impl": "reference", "metric": "decode tok/s (config 4: batched int8-KV sessions, ctx 1024)",
+        "value": round(value, 2), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32+int8", "data": "synthetic",
+        "config": {"workload": "config4-decode", "sessions": ncpu, "prompt_len": ctx, "kv": "int8"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tok/s", "cores": ncpu, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "reference Rust path unavailable on this box (no Rust toolchain); oracle port timed instead",
+    }))
+
+
+# ------------------------------------------------------------------ GPU arm
+def gemv_bandwidth(nb, torch, stream):
+    """BASELINE config 0 GEMV ([3072, 768] 2-bit, M=1) as a stream of launches:
+    L2-resident (same weights each launch) and HBM (a ring of distinct weight
+    copies larger than twice L2). Returns GB/s of algorithmic bytes."""
+    from needle_b200 import cact_pack
+    rng = np.random.default_rng(0)
+    cb = cact_pack.random_codebook(rng)
+    idx, norms = cact_pack.random_cq(rng, 3072, 768, 2)
+    blob = np.frombuffer(cact_pack.cq_blob(idx, norms, 2), np.uint8)
+    nbytes = len(blob)
+    algo = 3072 * 192 + 3072 * 6 * 2 + 768 * 4 + 3072 * 4 + 16  # 642,064 B per GEMV
+    stride = (nbytes + 255) // 256 * 256
+    copies = max(8, int(2.2 * 126e6 / stride))
+    ring = torch.zeros(copies * stride, dtype=torch.uint8, device="cuda")
+    one = torch.from_numpy(blob.copy()).cuda()
+    for c in range(copies):
+        ring[c * stride:c * stride + nbytes].copy_(one)
+    xh = torch.randn(1, 768, device="cuda")
+    y = torch.zeros(1, 3072, device="cuda")
+    lv = cact_pack.codebook_levels(cb, 2)
+    base = ring.data_ptr()
+    out = {}
+    for name, ncopy in (("l2", 1), ("hbm", copies)):
+        reps = 400
+
+        def launches():
+            s = torch.cuda.current_stream().cuda_stream  # the capture stream inside graph capture
+            for r in range(reps):
+                p = base + (r % ncopy) * stride
+                nb.cq_project(p, p + 3072 * 192, 3072, 768, 2, lv, xh.data_ptr(), 768, 1, y.data_ptr(), 3072,
+                              stream=s)
+        launches()
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            launches()
+        g.replay()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(3):
+            g.replay()
+        e1.record()
+        torch.cuda.synchronize()
+        per = e0.elapsed_time(e1) / (3 * reps) * 1e-3
+        out[name] = {"us_per_gemv": round(per * 1e6, 3), "gbs": round(algo / per / 1e9, 1)}
+        del g
+    # L2 copy bandwidth on this box (a 32 MB buffer, read + write), the L2 roofline denominator.
+    a = torch.empty(8 << 20, dtype=torch.float32, device="cuda")
+    b = torch.empty_like(a)
+    for _ in range(5):
+        b.copy_(a)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(50):
+        b.copy_(a)
+    e1.record()
+    torch.cuda.synchronize()
+    out["l2_copy_gbs_measured"] = round(2 * a.numel() * 4 * 50 / (e0.elapsed_time(e1) * 1e-3) / 1e9, 1)
+    out["algorithmic_bytes_per_gemv"] = algo
+    out["weight_ring_copies"] = copies
+    return out
+
+
+def attn_bytes_per_step(cfg, n_sessions, pos):
+    """Algorithmic HBM bytes of the 20 decode-attention launches of one step at
+    position `pos` (int8: per position and KV head 48 + 64 code bytes + two f32
+    scales; plus q in and the head outputs out)."""
+    total = 0
+    for l in range(cfg["layers"]):
+        glob = l in (4, 9, 14, 19)
+        span = pos + 1 if glob else min(pos + 1, cfg["window"])
+        per_sess = span * cfg["kv_heads"] * (cfg["qk_head_dim"] + cfg["v_head_dim"] + 8)
+        per_sess += cfg["heads"] * cfg["qk_head_dim"] * 4 + cfg["heads"] * cfg["v_head_dim"] * 4
+        total += per_sess * n_sessions
+    return total
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=16)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--sessions", type=int, default=4096, help="total sessions (config 4: 4096)")
+    ap.add_argument("--prompt", type=int, default=1024)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        return reference_arm(args)
+
+    import torch
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+    nb = pkg()
+    raw = container(0)
+    eng = nb.V3Engine.from_bytes(raw)
+    geo = eng.geometry
+    per = args.sessions // world
+    s0 = rank * per
+    gen_budget = 2 * (args.warmup + args.steps) + 4
+    hint = args.prompt + max(128, gen_budget)
+    sessions = [eng.session(hint, True) for _ in range(per)]
+    # ---- prefill (setup, timed for the record)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    group = max(1, 16384 // args.prompt)
+    picks = np.zeros(per, np.uint32)
+    for g0 in range(0, per, group):
+        ss = sessions[g0:g0 + group]
+        _, pk = eng.prefill_batch(ss, [prompt(s0 + g0 + i, args.prompt) for i in range(len(ss))], logits=False)
+        picks[g0:g0 + len(ss)] = pk
+    torch.cuda.synchronize()
+    prefill_s = time.perf_counter() - t0
+    stream = torch.cuda.current_stream()
+    st = stream.cuda_stream
+    batch = eng.batch(sessions)
+    batch.set_tokens(picks)
+    # ---- device-resident decode (CUDA-graph replay), value
+    for _ in range(args.warmup):
+        batch.step(None, stream=st)
+        batch.feed_next(stream=st)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(stream)
+        for _ in range(args.steps):
+            batch.step(None, stream=st)
+            batch.feed_next(stream=st)
+        e1.record(stream)
+        torch.cuda.synchronize()
+    dev_s = e0.elapsed_time(e1) * 1e-3
+    if dist:
+        t = torch.tensor([dev_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dev_s = float(t.item())
+        torch.cuda.synchronize()
+    value = args.sessions * args.steps / dev_s if world > 1 else per * args.steps / dev_s
+    # ---- per-kernel profile of one step (eager, events between kernel groups)
+    prof, launches = batch.profile()
+    pos_now = sessions[0].pos - 1
+    # ---- end to end through the host API: host tokens in, host picks out
+    toks = batch.get_next()
+    for _ in range(args.warmup):
+        _, toks = eng.decode_batch(sessions, toks, logits=False)
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        _, toks = eng.decode_batch(sessions, toks, logits=False)
+    e2e_s = time.perf_counter() - t0
+    if dist:
+        t = torch.tensor([e2e_s], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_s = float(t.item())
+    e2e = args.sessions * args.steps / e2e_s if world > 1 else per * args.steps / e2e_s
+    hbm, bf16, src = peaks()
+    attn_ms = prof["attention"] / geo["layers"]
+    abytes = attn_bytes_per_step(geo, per, pos_now) / geo["layers"]
+    achieved = abytes / (attn_ms * 1e-3) / 1e9
+    extra = {}
+    if rank == 0:
+        extra["gemv_config0"] = gemv_bandwidth(nb, torch, st)
+        if not args.no_cpu_baseline:
+            tps, cores, secs, sample = cpu_decode_sample(raw, args.prompt, 8)
+            extra["cpu_baseline"] = {"value": round(tps, 3), "unit": "tok/s", "cores": cores, "kind": "port",
+                                     "sample": sample + f" ({secs:.1f} s)"}
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    step_ms = dev_s / args.steps * 1e3
+    total_prof = sum(prof.values())
+    line = {
+        "metric": "decode tok/s (config 4: batched int8-KV sessions, 1024-token prompts)",
+        "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f32 (int8 KV)", "data": "synthetic (seeded random-init container, shipped Needle-3 geometry)",
+        "config": {"workload": "config4-decode", "sessions": args.sessions, "sessions_per_gpu": per,
+                   "prompt_len": args.prompt, "kv": "int8", "context_at_timing": pos_now,
+                   "l2": "inputs larger than L2 (int8 KV of all sessions)", "graph": "one CUDA graph per step",
+                   "prefill_s": round(prefill_s, 2),
+                   "prefill_tok_per_s_per_gpu": round(per * args.prompt / prefill_s, 1)},
+        "roofline": {"kernel": "decode attention (int8 KV)", "bound": "hbm", "achieved": round(achieved, 1),
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                     "peak_source": src, "algorithmic_bytes_per_launch": int(abytes),
+                     "launch_ms": round(attn_ms, 4)},
+        "profile_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
+        "profile_share": {k: round(v / total_prof, 4) for k, v in prof.items()} if total_prof else {},
+        "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * per,
+                "d2h_bytes_per_step": 4 * per},
+        "gpu_launches": launches * args.steps,
+        "clocks": clk.summary(),
+    }
+    line.update(extra)
+    print(json.dumps(line))
+
+
+if __name__ == "__main__":
+    main()

@@ -576,39 +576,38 @@ Engine::~Engine() {
 // ------------------------------------------------------------------ sessions
 static size_t kv_elem_bytes(const Session* s) { return s->int8 ? 1 : 4; }
 
-static cudaError_t alloc_layer(const Engine* E, bool int8, int slots, int cap, LayerKV* L) {
-  const Geo& g = E->G;
+// Bytes of one layer's KV ring at `slots` (each array 256-byte aligned).
+static size_t layer_bytes(const Geo& g, bool int8, int slots) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  const size_t eb = int8 ? 1 : 4;
+  size_t b = al((size_t)g.kvh * slots * g.qk * eb) + al((size_t)g.kvh * slots * g.vh * eb);
+  if (int8) b += 2 * al((size_t)g.kvh * slots * 4);
+  return b;
+}
+
+// Point L's arrays into `base` (layer_bytes(...) bytes, zeroed by the caller).
+static void carve_layer(const Geo& g, bool int8, int slots, int cap, uint8_t* base, LayerKV* L) {
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
   const size_t eb = int8 ? 1 : 4;
   std::memset(L, 0, sizeof(*L));
   L->slots = slots;
   L->cap = cap;
-  NB_TRY(cudaMalloc(&L->k, std::max<size_t>((size_t)g.kvh * slots * g.qk * eb, 16)));
-  NB_TRY(cudaMalloc(&L->v, std::max<size_t>((size_t)g.kvh * slots * g.vh * eb, 16)));
-  NB_TRY(cudaMemset(L->k, 0, (size_t)g.kvh * slots * g.qk * eb));
-  NB_TRY(cudaMemset(L->v, 0, (size_t)g.kvh * slots * g.vh * eb));
+  L->k = base;
+  base += al((size_t)g.kvh * slots * g.qk * eb);
+  L->v = base;
+  base += al((size_t)g.kvh * slots * g.vh * eb);
   if (int8) {
-    NB_TRY(cudaMalloc(&L->ks, std::max<size_t>((size_t)g.kvh * slots * 4, 16)));
-    NB_TRY(cudaMalloc(&L->vs, std::max<size_t>((size_t)g.kvh * slots * 4, 16)));
-    NB_TRY(cudaMemset(L->ks, 0, (size_t)g.kvh * slots * 4));
-    NB_TRY(cudaMemset(L->vs, 0, (size_t)g.kvh * slots * 4));
+    L->ks = (float*)base;
+    base += al((size_t)g.kvh * slots * 4);
+    L->vs = (float*)base;
   }
-  return cudaSuccess;
-}
-
-static void free_layer(LayerKV* L) {
-  if (L->k) cudaFree(L->k);
-  if (L->v) cudaFree(L->v);
-  if (L->ks) cudaFree(L->ks);
-  if (L->vs) cudaFree(L->vs);
-  std::memset(L, 0, sizeof(*L));
 }
 
 Session::~Session() {
   if (eng) cudaStreamSynchronize(eng->stream);
-  for (LayerKV& l : layers) free_layer(&l);
-  if (d_layers) cudaFree(d_layers);
-  if (d_desc) cudaFree(d_desc);
-  if (d_state) cudaFree(d_state);
+  for (size_t l = 0; l < layers.size(); ++l)
+    if (l < owned.size() && owned[l] && layers[l].k) cudaFree(layers[l].k);
+  if (d_arena) cudaFree(d_arena);
 }
 
 size_t Session::bytes() const {  // as V3Cache::bytes counts (cache.rs:255-268)
@@ -628,37 +627,52 @@ Session* Engine::new_session(size_t hint, bool int8, std::string* err) {
   hint = std::min(std::max<size_t>(hint, 1), cfg.max_seq);  // cache.rs:178
   s->hint = hint;
   s->layers.resize(cfg.layers);
+  s->owned.assign(cfg.layers, 0);
+  // One device arena per session: every layer's ring, the conv/Engram tails and
+  // token ring, the per-layer descriptor array and the session descriptor.
+  auto al = [](size_t x) { return (x + 255) / 256 * 256; };
+  std::vector<int> slots(cfg.layers), caps(cfg.layers);
+  size_t total = 0;
   for (size_t l = 0; l < cfg.layers; ++l) {
     size_t w = cfg.span(l);
-    int cap = (int)(w ? std::min(w, cfg.max_seq) : cfg.max_seq);
-    int slots = (int)std::min<size_t>(hint, (size_t)cap);
-    cudaError_t e = alloc_layer(this, int8, slots, cap, &s->layers[l]);
-    if (e != cudaSuccess) {
-      *err = cuda_msg("allocating the KV cache", e);
-      return nullptr;
-    }
+    caps[l] = (int)(w ? std::min(w, cfg.max_seq) : cfg.max_seq);
+    slots[l] = (int)std::min<size_t>(hint, (size_t)caps[l]);
+    total += layer_bytes(G, int8, slots[l]);
   }
   const size_t tl = G.taps > 0 ? G.taps - 1 : 0;
   const size_t qkv_tail = cfg.layers * tl * G.qkv_dim, eng_tail = (size_t)G.n_sites * G.e_reach * G.d;
   s->state_bytes = (qkv_tail + eng_tail) * 4 + 4 * 4;
-  SessDesc h{};
-  cudaError_t e = cudaMalloc(&s->d_state, s->state_bytes);
-  if (e == cudaSuccess) e = cudaMemset(s->d_state, 0, s->state_bytes);
-  if (e == cudaSuccess) e = cudaMalloc(&s->d_layers, cfg.layers * sizeof(LayerKV));
-  if (e == cudaSuccess)
-    e = cudaMemcpy(s->d_layers, s->layers.data(), cfg.layers * sizeof(LayerKV), cudaMemcpyHostToDevice);
-  if (e == cudaSuccess) e = cudaMalloc(&s->d_desc, sizeof(SessDesc));
+  const size_t state_off = total;
+  total += al(s->state_bytes);
+  const size_t layers_off = total;
+  total += al(cfg.layers * sizeof(LayerKV));
+  const size_t desc_off = total;
+  total += al(sizeof(SessDesc));
+  cudaError_t e = cudaMalloc(&s->d_arena, total);
+  if (e == cudaSuccess) e = cudaMemsetAsync(s->d_arena, 0, total, stream);
   if (e != cudaSuccess) {
-    *err = cuda_msg("allocating session state", e);
+    *err = cuda_msg("allocating the session", e);
     return nullptr;
   }
+  uint8_t* base = (uint8_t*)s->d_arena;
+  size_t off = 0;
+  for (size_t l = 0; l < cfg.layers; ++l) {
+    carve_layer(G, int8, slots[l], caps[l], base + off, &s->layers[l]);
+    off += layer_bytes(G, int8, slots[l]);
+  }
+  s->d_state = base + state_off;
+  s->d_layers = (LayerKV*)(base + layers_off);
+  s->d_desc = (SessDesc*)(base + desc_off);
+  SessDesc h{};
   h.pos = 0;
   h.int8 = int8 ? 1 : 0;
   h.layers = s->d_layers;
   h.qkv_tail = (float*)s->d_state;
   h.eng_tail = (float*)s->d_state + qkv_tail;
   h.toks = (uint32_t*)((float*)s->d_state + qkv_tail + eng_tail);
-  e = cudaMemcpy(s->d_desc, &h, sizeof(h), cudaMemcpyHostToDevice);
+  e = cudaMemcpyAsync(s->d_layers, s->layers.data(), cfg.layers * sizeof(LayerKV), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(s->d_desc, &h, sizeof(h), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   if (e != cudaSuccess) {
     *err = cuda_msg("writing the session descriptor", e);
     return nullptr;
@@ -679,7 +693,11 @@ bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
     int want = L.slots;
     while ((int)pos >= want && want < L.cap) want = std::min(std::max(want * 2, want + 1), L.cap);
     LayerKV N;
-    cudaError_t e = alloc_layer(this, s->int8, want, L.cap, &N);
+    void* mem = nullptr;
+    const size_t nb_ = layer_bytes(G, s->int8, want);
+    cudaError_t e = cudaMalloc(&mem, nb_);
+    if (e == cudaSuccess) e = cudaMemsetAsync(mem, 0, nb_, stream);
+    if (e == cudaSuccess) carve_layer(G, s->int8, want, L.cap, (uint8_t*)mem, &N);
     auto copy2d = [&](void* dst, const void* src, size_t row) {
       return cudaMemcpy2DAsync(dst, want * row, src, L.slots * row, L.slots * row, G.kvh,
                                cudaMemcpyDeviceToDevice, stream);
@@ -690,12 +708,13 @@ bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
     if (e == cudaSuccess && s->int8) e = copy2d(N.vs, L.vs, 4);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
     if (e != cudaSuccess) {
-      free_layer(&N);
+      if (mem) cudaFree(mem);
       *err = cuda_msg("growing the KV ring", e);
       return false;
     }
-    free_layer(&L);
+    if (s->owned[l]) cudaFree(L.k);  // a ring grown earlier owns its allocation
     L = N;
+    s->owned[l] = 1;
     changed = true;
   }
   if (changed) {

@@ -49,7 +49,9 @@ class Session {
   SessDesc* d_desc = nullptr;     // device descriptor
   LayerKV* d_layers = nullptr;    // device array [layers]
   std::vector<LayerKV> layers;    // host mirror
-  void* d_state = nullptr;        // tails + token ring
+  void* d_state = nullptr;        // tails + token ring (inside the arena)
+  void* d_arena = nullptr;        // one allocation holding the initial rings, state and descriptors
+  std::vector<char> owned;        // layer ring grown into its own allocation
   size_t state_bytes = 0;
   size_t bytes() const;           // device bytes held, as V3Cache::bytes counts them
 };
