@@ -326,7 +326,10 @@ def main():
         picks[g0:g0 + len(ss)] = pk
     torch.cuda.synchronize()
     prefill_s = time.perf_counter() - t0
-    stream = torch.cuda.current_stream()
+    # A dedicated stream: handle 0 (the legacy default stream) means "the
+    # engine's own stream" to the C ABI, and events must sit on the launch stream.
+    stream = torch.cuda.Stream()
+    torch.cuda.set_stream(stream)
     st = stream.cuda_stream
     batch = eng.batch(sessions)
     batch.set_tokens(picks)
