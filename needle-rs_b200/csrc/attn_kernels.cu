@@ -5,10 +5,21 @@
 // kv_head = h / repeat, scale 1/sqrt(qk_head_dim), softmax with max
 // subtraction, then P.V. The int8 reader follows Int8View (:191-216): the
 // per-(position, kv head) key scale multiplies the integer-valued dot and the
-// value scale multiplies the softmax weight. The softmax runs online over
-// tiles of positions (one CTA per (row, kv head)), so sums are reassociated
-// relative to the reference's two-pass loop; the result agrees to f32 rounding.
+// value scale multiplies the softmax weight.
+//
+// Structure (split-position / "flash-decode"): one CTA per (row, KV head,
+// split). A row's range [lo, hi] is cut into `nsplit` equal parts; each CTA
+// streams its part in chunks of 128 positions through a double-buffered
+// cp.async pipeline (keys, values and their scales in shared memory), keeps an
+// online softmax per query head and writes an unnormalised partial
+// (max, sum, P.V) per head. A combine step (fused into attn_finish for the
+// forward, attn_combine for the standalone entry) merges the splits. All query
+// heads of a KV head share one CTA, so each key/value byte is read from HBM
+// once per row. Sums are reassociated relative to the reference's two-pass
+// loop; results agree to f32 rounding.
 #include <cuda_runtime.h>
+
+#include <algorithm>
 
 #include "common.cuh"
 #include "kernels.hpp"
@@ -16,12 +27,13 @@
 
 namespace nb {
 
-constexpr int AT_TILE = 128;
+constexpr int CH = 128;        // positions per chunk
+constexpr int AT_THREADS = 128;
 constexpr int AT_MAXREP = 8;
 
-// Where keys/values of one (row, kv head) live. Element (position n, kv head
-// kh) of keys is at k + idx(n) * k_row + kh * k_head (in elements), with
-// idx(n) = n % slots for a ring and base + n for the prefill scratch.
+// Where keys/values of one (row, KV head) live: element (position n, KV head
+// kh) of keys is at k + idx(n) * k_row + kh * k_head (elements), idx(n) = n %
+// slots for a ring and base + n for the prefill scratch.
 struct AttnSrc {
   const void* k;
   const void* v;
@@ -32,157 +44,250 @@ struct AttnSrc {
   int base;
 };
 
-template <bool INT8, int QK>
-__device__ void attend_core(const float* qs, int rep, int vh, const AttnSrc& src, int kh,
-                            int lo, int hi, float scale, float* __restrict__ out, float* sm) {
-  float* S = sm;                          // [rep][AT_TILE]
-  float* Vs = S + AT_MAXREP * AT_TILE;    // [AT_TILE][vh]
-  float* vsc = Vs + AT_TILE * vh;         // [AT_TILE]
-  float* mrun = vsc + AT_TILE;            // [AT_MAXREP]
-  float* lrun = mrun + AT_MAXREP;
-  float* cr = lrun + AT_MAXREP;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
-  if (tid < AT_MAXREP) {
-    mrun[tid] = -INFINITY;
-    lrun[tid] = 0.f;
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  int n = valid ? 16 : 0;  // src-size 0: zero-fill, nothing read
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  int n = valid ? 4 : 0;
+  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
+}
+__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
+template <int N>
+__device__ __forceinline__ void cp_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+template <bool INT8, int QK, int VH>
+struct AttnTile {
+  static constexpr int ES = INT8 ? 1 : 4;
+  static constexpr int KB = CH * QK * ES;  // key bytes per chunk
+  static constexpr int VB = CH * VH * ES;  // value bytes per chunk
+  static constexpr int KP = QK * ES / 16;  // 16-byte pieces per key row
+  static constexpr int VP = VH * ES / 16;
+  static constexpr int G = AT_THREADS / (VH / 4);  // position groups in P.V
+};
+
+template <bool INT8, int QK, int VH>
+struct __align__(16) AttnSmem {
+  using T = AttnTile<INT8, QK, VH>;
+  uint8_t kbuf[2][T::KB];
+  uint8_t vbuf[2][T::VB];
+  float ksc[2][CH];
+  float vsc[2][CH];
+  float q[AT_MAXREP * QK];
+  float P[CH][AT_MAXREP + 1];  // scores, then weights; padded row
+  float m[AT_MAXREP], l[AT_MAXREP], corr[AT_MAXREP];
+  float red[T::G][AT_MAXREP][VH];
+};
+
+// Issue the cp.async copies of one chunk [n0, n0 + CH) clipped at hi.
+template <bool INT8, int QK, int VH>
+__device__ __forceinline__ void issue_chunk(AttnSmem<INT8, QK, VH>& S, int buf, const AttnSrc& src,
+                                            int kh, int n0, int hi) {
+  using T = AttnTile<INT8, QK, VH>;
+  const char* kb = (const char*)src.k;
+  const char* vb = (const char*)src.v;
+  for (int j = threadIdx.x; j < CH * T::KP; j += AT_THREADS) {
+    const int i = j / T::KP, pc = j % T::KP, n = n0 + i;
+    const bool ok = n <= hi;
+    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    cp_async16(S.kbuf[buf] + i * QK * T::ES + pc * 16,
+               kb + (idx * src.k_row + kh * src.k_head) * T::ES + pc * 16, ok);
   }
-  const int nout = rep * vh;
-  float acc0 = 0.f, acc1 = 0.f;  // outputs tid and tid + blockDim.x
-  const int hsplit = (rep + 1) / 2;
-  for (int n0 = lo; n0 <= hi; n0 += AT_TILE) {
+  for (int j = threadIdx.x; j < CH * T::VP; j += AT_THREADS) {
+    const int i = j / T::VP, pc = j % T::VP, n = n0 + i;
+    const bool ok = n <= hi;
+    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    cp_async16(S.vbuf[buf] + i * VH * T::ES + pc * 16,
+               vb + (idx * src.v_row + kh * src.v_head) * T::ES + pc * 16, ok);
+  }
+  if (INT8) {
+    for (int i = threadIdx.x; i < CH; i += AT_THREADS) {
+      const int n = n0 + i;
+      const bool ok = n <= hi;
+      const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+      cp_async4(&S.ksc[buf][i], src.ks + idx * src.s_row + kh * src.s_head, ok);
+      cp_async4(&S.vsc[buf][i], src.vs + idx * src.s_row + kh * src.s_head, ok);
+    }
+  }
+}
+
+// One CTA: query heads [kh*rep, kh*rep + rep) of one row over positions
+// [a, b] (inclusive; empty when a > b). Writes the partial to `part`:
+// rep maxima, rep sums, rep x VH unnormalised outputs.
+template <bool INT8, int QK, int VH>
+__device__ void attend_part(AttnSmem<INT8, QK, VH>& S, const float* __restrict__ qrow, int rep,
+                            const AttnSrc& src, int kh, int a, int b, float scale,
+                            float* __restrict__ part) {
+  using T = AttnTile<INT8, QK, VH>;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  for (int i = tid; i < rep * QK; i += AT_THREADS) S.q[i] = qrow[i];
+  if (tid < AT_MAXREP) {
+    S.m[tid] = -INFINITY;
+    S.l[tid] = 0.f;
+  }
+  constexpr int DQ = VH / 4;  // d-quads
+  const int dq = tid % DQ, grp = tid / DQ;
+  float acc[AT_MAXREP][4];
+#pragma unroll
+  for (int h = 0; h < AT_MAXREP; ++h)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) acc[h][e] = 0.f;
+  const int nch = a <= b ? (b - a) / CH + 1 : 0;
+  if (nch > 0) {
+    issue_chunk<INT8, QK, VH>(S, 0, src, kh, a, b);
+    cp_commit();
+  }
+  for (int c = 0; c < nch; ++c) {
+    const int buf = c & 1;
+    if (c + 1 < nch) {
+      issue_chunk<INT8, QK, VH>(S, buf ^ 1, src, kh, a + (c + 1) * CH, b);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
     __syncthreads();
-    // ---- scores: position n0 + (tid % TILE); head half tid / TILE.
+    // ---- scores: thread = position
     {
-      const int t = tid % AT_TILE, half = tid / AT_TILE;
-      const int n = n0 + t;
-      const int h0 = half * hsplit, h1 = min(rep, h0 + hsplit);
-      if (n <= hi) {
-        const long idx = src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n);
-        float kv[QK];
-        if (INT8) {
-          const int8_t* kp = (const int8_t*)src.k + idx * src.k_row + kh * src.k_head;
+      const int n = a + c * CH + tid;
+      float kv[QK];
+      if (INT8) {
+        const int8_t* kr = reinterpret_cast<const int8_t*>(S.kbuf[buf]) + tid * QK;
 #pragma unroll
-          for (int i = 0; i < QK; i += 16) {
-            int4 w = *reinterpret_cast<const int4*>(kp + i);
-            const int8_t* b = reinterpret_cast<const int8_t*>(&w);
+        for (int i = 0; i < QK; i += 16) {
+          int4 w = *reinterpret_cast<const int4*>(kr + i);
+          const int8_t* bb = reinterpret_cast<const int8_t*>(&w);
 #pragma unroll
-            for (int j = 0; j < 16; ++j) kv[i + j] = (float)b[j];
-          }
-        } else {
-          const float* kp = (const float*)src.k + idx * src.k_row + kh * src.k_head;
-#pragma unroll
-          for (int i = 0; i < QK; i += 4) {
-            float4 w = *reinterpret_cast<const float4*>(kp + i);
-            kv[i] = w.x;
-            kv[i + 1] = w.y;
-            kv[i + 2] = w.z;
-            kv[i + 3] = w.w;
-          }
-        }
-        const float ksc = INT8 ? src.ks[idx * src.s_row + kh * src.s_head] : 1.0f;
-        for (int h = h0; h < h1; ++h) {
-          float a = 0.f;
-#pragma unroll
-          for (int i = 0; i < QK; ++i) a += qs[h * QK + i] * kv[i];
-          if (INT8) a = a * ksc;
-          S[h * AT_TILE + t] = a * scale;
+          for (int j = 0; j < 16; ++j) kv[i + j] = (float)bb[j];
         }
       } else {
-        for (int h = h0; h < h1; ++h) S[h * AT_TILE + t] = -INFINITY;
+        const float* kr = reinterpret_cast<const float*>(S.kbuf[buf]) + tid * QK;
+#pragma unroll
+        for (int i = 0; i < QK; i += 4) {
+          float4 w = *reinterpret_cast<const float4*>(kr + i);
+          kv[i] = w.x;
+          kv[i + 1] = w.y;
+          kv[i + 2] = w.z;
+          kv[i + 3] = w.w;
+        }
       }
-    }
-    // ---- value tile
-    for (int e = tid; e < AT_TILE * vh; e += blockDim.x) {
-      const int t = e / vh, dd = e % vh;
-      const int n = n0 + t;
-      float val = 0.f;
-      if (n <= hi) {
-        const long idx = src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n);
-        if (INT8)
-          val = (float)((const int8_t*)src.v)[idx * src.v_row + kh * src.v_head + dd];
-        else
-          val = ((const float*)src.v)[idx * src.v_row + kh * src.v_head + dd];
-        if (INT8 && dd == 0) vsc[t] = src.vs[idx * src.s_row + kh * src.s_head];
-      } else if (dd == 0) {
-        vsc[t] = 0.f;
+      const float ksc = INT8 ? S.ksc[buf][tid] : 1.0f;
+      const bool ok = n <= b;
+#pragma unroll
+      for (int h = 0; h < AT_MAXREP; ++h) {
+        if (h < rep) {
+          float s = 0.f;
+#pragma unroll
+          for (int i = 0; i < QK; ++i) s += S.q[h * QK + i] * kv[i];
+          if (INT8) s = s * ksc;
+          S.P[tid][h] = ok ? s * scale : -INFINITY;
+        }
       }
-      Vs[e] = val;
     }
     __syncthreads();
-    // ---- online softmax update per head
-    for (int h = wid; h < rep; h += nw) {
+    // ---- online softmax per head (one warp per head)
+    for (int h = wid; h < rep; h += AT_THREADS / 32) {
       float mx = -INFINITY;
-      for (int t = lane; t < AT_TILE; t += 32) mx = fmaxf(mx, S[h * AT_TILE + t]);
+#pragma unroll
+      for (int j = 0; j < CH / 32; ++j) mx = fmaxf(mx, S.P[lane + 32 * j][h]);
       mx = warp_max(mx);
-      const float mold = mrun[h];
-      const float mnew = fmaxf(mold, mx);
+      const float mold = S.m[h], mnew = fmaxf(mold, mx);
       float sum = 0.f;
-      for (int t = lane; t < AT_TILE; t += 32) {
-        float s = S[h * AT_TILE + t];
-        float pv = s == -INFINITY ? 0.f : expf(s - mnew);
-        S[h * AT_TILE + t] = pv;
-        sum += pv;
+#pragma unroll
+      for (int j = 0; j < CH / 32; ++j) {
+        const int i = lane + 32 * j;
+        const float s = S.P[i][h];
+        const float p = s == -INFINITY ? 0.f : expf(s - mnew);
+        sum += p;
+        S.P[i][h] = INT8 ? p * S.vsc[buf][i] : p;
       }
       sum = warp_sum(sum);
       if (lane == 0) {
-        const float c = mold == -INFINITY ? 0.f : expf(mold - mnew);
-        cr[h] = c;
-        lrun[h] = lrun[h] * c + sum;
-        mrun[h] = mnew;
+        const float cr = mold == -INFINITY ? 0.f : expf(mold - mnew);
+        S.corr[h] = cr;
+        S.l[h] = S.l[h] * cr + sum;
+        S.m[h] = mnew;
       }
     }
     __syncthreads();
-    // ---- P.V
+    // ---- P.V: thread = (position group, d-quad), all heads
 #pragma unroll
-    for (int rep2 = 0; rep2 < 2; ++rep2) {
-      const int o = tid + rep2 * blockDim.x;
-      if (o < nout) {
-        const int h = o / vh, dd = o % vh;
-        float a = 0.f;
-        const float* P = S + h * AT_TILE;
-        if (INT8) {
-          for (int t = 0; t < AT_TILE; ++t) a += (P[t] * vsc[t]) * Vs[t * vh + dd];
-        } else {
-          for (int t = 0; t < AT_TILE; ++t) a += P[t] * Vs[t * vh + dd];
-        }
-        if (rep2 == 0)
-          acc0 = acc0 * cr[h] + a;
-        else
-          acc1 = acc1 * cr[h] + a;
+    for (int h = 0; h < AT_MAXREP; ++h)
+      if (h < rep) {
+        const float cr = S.corr[h];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) acc[h][e] *= cr;
       }
-    }
-  }
-  __syncthreads();
+    for (int i = grp; i < CH; i += T::G) {
+      float v4[4];
+      if (INT8) {
+        const int w = *reinterpret_cast<const int*>(S.vbuf[buf] + i * VH + dq * 4);
+        v4[0] = (float)(int8_t)(w & 0xff);
+        v4[1] = (float)(int8_t)((w >> 8) & 0xff);
+        v4[2] = (float)(int8_t)((w >> 16) & 0xff);
+        v4[3] = (float)(int8_t)((w >> 24) & 0xff);
+      } else {
+        const float4 w = *reinterpret_cast<const float4*>(S.vbuf[buf] + (i * VH + dq * 4) * 4);
+        v4[0] = w.x;
+        v4[1] = w.y;
+        v4[2] = w.z;
+        v4[3] = w.w;
+      }
 #pragma unroll
-  for (int rep2 = 0; rep2 < 2; ++rep2) {
-    const int o = tid + rep2 * blockDim.x;
-    if (o < nout) {
-      const int h = o / vh;
-      out[o] = (rep2 == 0 ? acc0 : acc1) / lrun[h];
+      for (int h = 0; h < AT_MAXREP; ++h)
+        if (h < rep) {
+          const float p = S.P[i][h];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) acc[h][e] += p * v4[e];
+        }
     }
+    __syncthreads();
+  }
+  // ---- reduce the position groups and write the partial
+#pragma unroll
+  for (int h = 0; h < AT_MAXREP; ++h)
+    if (h < rep)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S.red[grp][h][dq * 4 + e] = acc[h][e];
+  __syncthreads();
+  for (int o = tid; o < rep * VH; o += AT_THREADS) {
+    const int h = o / VH, d = o % VH;
+    float s = 0.f;
+    for (int g = 0; g < T::G; ++g) s += S.red[g][h][d];
+    part[2 * rep + o] = s;
+  }
+  if (tid < rep) {
+    part[tid] = S.m[tid];
+    part[rep + tid] = S.l[tid];
   }
 }
 
-static size_t attn_smem(int vh) {
-  return (size_t)(AT_MAXREP * AT_TILE + AT_TILE * vh + AT_TILE + 3 * AT_MAXREP + AT_MAXREP * 64) * sizeof(float);
+// Split z of `nsplit` equal, chunk-aligned parts of [lo, hi].
+__device__ __forceinline__ void split_range(int lo, int hi, int nsplit, int z, int* a, int* b) {
+  const int len = hi - lo + 1;
+  int spl = (len + nsplit - 1) / nsplit;
+  spl = (spl + CH - 1) / CH * CH;
+  *a = lo + z * spl;
+  *b = min(hi, lo + (z + 1) * spl - 1);
 }
 
-// Forward-pass attention: one CTA per (row, kv head).
-template <bool INT8, int QK>
-__global__ void __launch_bounds__(256) layer_attn_kernel(Geo G, int li, RowBatch rb, int window,
-                                                         const float* __restrict__ qpost,
-                                                         const void* pk, const void* pv,
-                                                         const float* pks, const float* pvs,
-                                                         float* __restrict__ attn) {
-  extern __shared__ __align__(16) float sm[];
-  const int r = blockIdx.x, kh = blockIdx.y;
+// Forward-pass attention: grid (rows, kv_heads, nsplit).
+template <bool INT8, int QK, int VH>
+__global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, RowBatch rb, int window,
+                                                                int nsplit, const float* __restrict__ qpost,
+                                                                const void* pk, const void* pv,
+                                                                const float* pks, const float* pvs,
+                                                                float* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  auto& S = *reinterpret_cast<AttnSmem<INT8, QK, VH>*>(smraw);
+  const int r = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
   const int rep = G.heads / G.kvh;
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos;
-  float* qs = sm;  // [rep][qk]
-  float* rest = sm + AT_MAXREP * 64;
-  for (int i = threadIdx.x; i < rep * G.qk; i += blockDim.x)
-    qs[i] = qpost[(size_t)r * G.q_dim + (size_t)kh * rep * G.qk + i];
   int lo = (window > 0 && p + 1 > window) ? p + 1 - window : 0;
   AttnSrc src;
   if (rb.mode == MODE_PREFILL) {
@@ -190,10 +295,10 @@ __global__ void __launch_bounds__(256) layer_attn_kernel(Geo G, int li, RowBatch
     src.v = pv;
     src.ks = pks;
     src.vs = pvs;
-    src.k_row = (long)G.kvh * G.qk;
-    src.k_head = G.qk;
-    src.v_row = (long)G.kvh * G.vh;
-    src.v_head = G.vh;
+    src.k_row = (long)G.kvh * QK;
+    src.k_head = QK;
+    src.v_row = (long)G.kvh * VH;
+    src.v_head = VH;
     src.s_row = G.kvh;
     src.s_head = 1;
     src.slots = 0;
@@ -204,10 +309,10 @@ __global__ void __launch_bounds__(256) layer_attn_kernel(Geo G, int li, RowBatch
     src.v = kv.v;
     src.ks = kv.ks;
     src.vs = kv.vs;
-    src.k_row = G.qk;
-    src.k_head = (long)kv.slots * G.qk;
-    src.v_row = G.vh;
-    src.v_head = (long)kv.slots * G.vh;
+    src.k_row = QK;
+    src.k_head = (long)kv.slots * QK;
+    src.v_row = VH;
+    src.v_head = (long)kv.slots * VH;
     src.s_row = 1;
     src.s_head = kv.slots;
     src.slots = kv.slots;
@@ -215,117 +320,187 @@ __global__ void __launch_bounds__(256) layer_attn_kernel(Geo G, int li, RowBatch
     const int floor = p + 1 > kv.slots ? p + 1 - kv.slots : 0;  // cache.rs:322-331
     lo = max(lo, floor);
   }
-  __syncthreads();
-  const float scale = 1.0f / sqrtf((float)G.qk);
-  attend_core<INT8, QK>(qs, rep, G.vh, src, kh, lo, p, scale,
-                    attn + (size_t)r * G.o_dim + (size_t)kh * rep * G.vh, rest);
+  int a, b;
+  split_range(lo, p, nsplit, z, &a, &b);
+  const int pw = rep * (VH + 2);
+  attend_part<INT8, QK, VH>(S, qpost + (size_t)r * G.q_dim + (size_t)kh * rep * QK, rep, src, kh, a, b,
+                            1.0f / sqrtf((float)QK), part + (((size_t)r * G.kvh + kh) * nsplit + z) * pw);
 }
 
-cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+int attn_nsplit(int rows, int kvh, int max_span) {
+  // Enough CTAs to cover the 148 SMs several times; never more splits than chunks.
+  const int target = 148 * 6;
+  int ns = (target + rows * kvh - 1) / (rows * kvh);
+  ns = std::max(1, std::min(ns, (max_span + CH - 1) / CH));
+  return std::min(ns, 64);
+}
+
+size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit) {
+  return (size_t)rows * kvh * nsplit * (heads / kvh) * (vh + 2);
+}
+
+template <bool INT8, int QK, int VH>
+static cudaError_t launch_layer_attn_t(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
+                                       const float* qpost, const void* pk, const void* pv, const float* pks,
+                                       const float* pvs, float* part, cudaStream_t st) {
+  const size_t smem = sizeof(AttnSmem<INT8, QK, VH>);
+  auto k = layer_attn_kernel<INT8, QK, VH>;
+  cudaError_t e = allow_smem((const void*)k, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(rb.M, G.kvh, nsplit);
+  k<<<grid, AT_THREADS, smem, st>>>(G, li, rb, window, nsplit, qpost, pk, pv, pks, pvs, part);
+  return cudaGetLastError();
+}
+
+cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const void* pk, const void* pv, const float* pks,
-                             const float* pvs, float* attn, cudaStream_t st, int int8) {
+                             const float* pvs, float* part, cudaStream_t st, int int8) {
   if (rb.M <= 0) return cudaSuccess;
   const int rep = G.heads / G.kvh;
-  if (rep > AT_MAXREP || G.qk > 64 || G.vh > 64 || G.qk % 16 || rep * G.vh > 512)
-    return cudaErrorInvalidValue;
-  const size_t smem = attn_smem(G.vh);
-  dim3 grid(rb.M, G.kvh);
-#define NB_ATTN_LAUNCH(I8, Q)                                                                   \
-  {                                                                                            \
-    auto k = layer_attn_kernel<I8, Q>;                                                         \
-    cudaError_t e = allow_smem((const void*)k, smem);                                         \
-    if (e != cudaSuccess) return e;                                                            \
-    k<<<grid, 256, smem, st>>>(G, li, rb, lp.window, qpost, pk, pv, pks, pvs, attn);           \
+  if (rep > AT_MAXREP || nsplit < 1) return cudaErrorInvalidValue;
+#define NB_ATT(I8, Q, V) \
+  return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, st)
+  const int key = G.qk * 2 + (int8 ? 1 : 0);
+  if (G.vh == 64) {
+    switch (key) {
+      case 32: NB_ATT(false, 16, 64);
+      case 33: NB_ATT(true, 16, 64);
+      case 64: NB_ATT(false, 32, 64);
+      case 65: NB_ATT(true, 32, 64);
+      case 96: NB_ATT(false, 48, 64);
+      case 97: NB_ATT(true, 48, 64);
+      case 128: NB_ATT(false, 64, 64);
+      case 129: NB_ATT(true, 64, 64);
+    }
+  } else if (G.vh == 32) {
+    switch (key) {
+      case 32: NB_ATT(false, 16, 32);
+      case 33: NB_ATT(true, 16, 32);
+      case 64: NB_ATT(false, 32, 32);
+      case 65: NB_ATT(true, 32, 32);
+      case 96: NB_ATT(false, 48, 32);
+      case 97: NB_ATT(true, 48, 32);
+      case 128: NB_ATT(false, 64, 32);
+      case 129: NB_ATT(true, 64, 32);
+    }
   }
-  switch (G.qk * 2 + (int8 ? 1 : 0)) {
-    case 32: NB_ATTN_LAUNCH(false, 16) break;
-    case 33: NB_ATTN_LAUNCH(true, 16) break;
-    case 64: NB_ATTN_LAUNCH(false, 32) break;
-    case 65: NB_ATTN_LAUNCH(true, 32) break;
-    case 96: NB_ATTN_LAUNCH(false, 48) break;
-    case 97: NB_ATTN_LAUNCH(true, 48) break;
-    case 128: NB_ATTN_LAUNCH(false, 64) break;
-    case 129: NB_ATTN_LAUNCH(true, 64) break;
-    default: return cudaErrorInvalidValue;
+#undef NB_ATT
+  return cudaErrorInvalidValue;
+}
+
+// Merge the split partials of one (row, head): softmax over all positions.
+__device__ __forceinline__ float combine_head(const float* __restrict__ part, int nsplit, int rep, int vh,
+                                              int hl, int d) {
+  const int pw = rep * (vh + 2);
+  float M = -INFINITY;
+  for (int z = 0; z < nsplit; ++z) M = fmaxf(M, part[z * pw + hl]);
+  float L = 0.f, o = 0.f;
+  for (int z = 0; z < nsplit; ++z) {
+    const float mz = part[z * pw + hl];
+    if (mz == -INFINITY) continue;
+    const float w = expf(mz - M);
+    L += w * part[z * pw + rep + hl];
+    o += w * part[z * pw + 2 * rep + hl * vh + d];
   }
-#undef NB_ATTN_LAUNCH
-  return cudaGetLastError();
+  return o / L;
 }
 
 // Standalone batched decode attention: B independent
 // sessions whose rings use the reference's layout k [slots][kv_heads][qk],
 // v [slots][kv_heads][vh], scales [slots][kv_heads], session b at offset
 // b * slots * kv_heads * (qk | vh | 1).
-template <bool INT8, int QK>
-__global__ void __launch_bounds__(256) attend_step_kernel(const float* __restrict__ q, const void* k,
-                                                          const void* v, const float* ks,
-                                                          const float* vs, int slots,
-                                                          const int* __restrict__ lo,
-                                                          const int* __restrict__ hi, int heads,
-                                                          int kvh, int qk, int vh,
-                                                          float* __restrict__ out) {
-  extern __shared__ __align__(16) float sm[];
-  const int b = blockIdx.x, kh = blockIdx.y;
+template <bool INT8, int QK, int VH>
+__global__ void __launch_bounds__(AT_THREADS) attend_step_kernel(const float* __restrict__ q, const void* k,
+                                                                 const void* v, const float* ks, const float* vs,
+                                                                 int slots, const int* __restrict__ lo,
+                                                                 const int* __restrict__ hi, int heads, int kvh,
+                                                                 int nsplit, float* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  auto& S = *reinterpret_cast<AttnSmem<INT8, QK, VH>*>(smraw);
+  const int bi = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
   const int rep = heads / kvh;
-  float* qs = sm;
-  float* rest = sm + AT_MAXREP * 64;
-  for (int i = threadIdx.x; i < rep * qk; i += blockDim.x)
-    qs[i] = q[(size_t)b * heads * qk + (size_t)kh * rep * qk + i];
+  const size_t es = INT8 ? 1 : 4;
   AttnSrc src;
-  const size_t esz = INT8 ? 1 : 4;
-  src.k = (const char*)k + (size_t)b * slots * kvh * qk * esz;
-  src.v = (const char*)v + (size_t)b * slots * kvh * vh * esz;
-  src.ks = INT8 ? ks + (size_t)b * slots * kvh : nullptr;
-  src.vs = INT8 ? vs + (size_t)b * slots * kvh : nullptr;
-  src.k_row = (long)kvh * qk;
-  src.k_head = qk;
-  src.v_row = (long)kvh * vh;
-  src.v_head = vh;
+  src.k = (const char*)k + (size_t)bi * slots * kvh * QK * es;
+  src.v = (const char*)v + (size_t)bi * slots * kvh * VH * es;
+  src.ks = INT8 ? ks + (size_t)bi * slots * kvh : nullptr;
+  src.vs = INT8 ? vs + (size_t)bi * slots * kvh : nullptr;
+  src.k_row = (long)kvh * QK;
+  src.k_head = QK;
+  src.v_row = (long)kvh * VH;
+  src.v_head = VH;
   src.s_row = kvh;
   src.s_head = 1;
   src.slots = slots;
   src.base = 0;
-  __syncthreads();
-  attend_core<INT8, QK>(qs, rep, vh, src, kh, lo[b], hi[b], 1.0f / sqrtf((float)qk),
-                    out + (size_t)b * heads * vh + (size_t)kh * rep * vh, rest);
+  int a, b;
+  split_range(lo[bi], hi[bi], nsplit, z, &a, &b);
+  const int pw = rep * (VH + 2);
+  attend_part<INT8, QK, VH>(S, q + (size_t)bi * heads * QK + (size_t)kh * rep * QK, rep, src, kh, a, b,
+                            1.0f / sqrtf((float)QK), part + (((size_t)bi * kvh + kh) * nsplit + z) * pw);
+}
+
+__global__ void attn_combine_kernel(const float* __restrict__ part, int heads, int kvh, int vh, int nsplit,
+                                    float* __restrict__ out) {
+  const int bi = blockIdx.x, rep = heads / kvh, pw = rep * (vh + 2);
+  for (int o = threadIdx.x; o < heads * vh; o += blockDim.x) {
+    const int h = o / vh, d = o % vh, kh = h / rep, hl = h % rep;
+    out[(size_t)bi * heads * vh + o] =
+        combine_head(part + ((size_t)bi * kvh + kh) * nsplit * pw, nsplit, rep, vh, hl, d);
+  }
+}
+
+template <bool INT8, int QK, int VH>
+static cudaError_t launch_step_t(const float* q, const void* k, const void* v, const float* ks, const float* vs,
+                                 int slots, const int* lo, const int* hi, int B, int heads, int kvh, int nsplit,
+                                 float* part, cudaStream_t st) {
+  const size_t smem = sizeof(AttnSmem<INT8, QK, VH>);
+  auto kk = attend_step_kernel<INT8, QK, VH>;
+  cudaError_t e = allow_smem((const void*)kk, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(B, kvh, nsplit);
+  kk<<<grid, AT_THREADS, smem, st>>>(q, k, v, ks, vs, slots, lo, hi, heads, kvh, nsplit, part);
+  return cudaGetLastError();
 }
 
 cudaError_t launch_attend_step(const float* q, const void* k, const void* v, const float* ks,
                                const float* vs, int int8, int slots, const int* lo, const int* hi,
-                               int B, int heads, int kvh, int qk, int vh, float* out,
-                               cudaStream_t st) {
+                               int B, int heads, int kvh, int qk, int vh, int nsplit, float* part,
+                               float* out, cudaStream_t st) {
   if (B <= 0) return cudaSuccess;
-  if (kvh <= 0 || heads % kvh) return cudaErrorInvalidValue;
-  const int rep = heads / kvh;
-  if (rep > AT_MAXREP || qk > 64 || vh > 64 || qk % 16 || rep * vh > 512 || slots <= 0)
-    return cudaErrorInvalidValue;
-  const size_t smem = attn_smem(vh);
-  dim3 grid(B, kvh);
-#define NB_STEP_LAUNCH(I8, Q)                                                                   \
-  {                                                                                            \
-    auto kk = attend_step_kernel<I8, Q>;                                                       \
-    cudaError_t e = allow_smem((const void*)kk, smem);                                        \
-    if (e != cudaSuccess) return e;                                                            \
-    kk<<<grid, 256, smem, st>>>(q, k, v, ks, vs, slots, lo, hi, heads, kvh, qk, vh, out);      \
+  if (kvh <= 0 || heads % kvh || heads / kvh > AT_MAXREP || slots <= 0 || nsplit < 1) return cudaErrorInvalidValue;
+  cudaError_t e = cudaErrorInvalidValue;
+#define NB_STEP(I8, Q, V) \
+  e = launch_step_t<I8, Q, V>(q, k, v, ks, vs, slots, lo, hi, B, heads, kvh, nsplit, part, st)
+  const int key = qk * 2 + (int8 ? 1 : 0);
+  if (vh == 64) {
+    if (key == 32) NB_STEP(false, 16, 64);
+    else if (key == 33) NB_STEP(true, 16, 64);
+    else if (key == 64) NB_STEP(false, 32, 64);
+    else if (key == 65) NB_STEP(true, 32, 64);
+    else if (key == 96) NB_STEP(false, 48, 64);
+    else if (key == 97) NB_STEP(true, 48, 64);
+    else if (key == 128) NB_STEP(false, 64, 64);
+    else if (key == 129) NB_STEP(true, 64, 64);
+  } else if (vh == 32) {
+    if (key == 32) NB_STEP(false, 16, 32);
+    else if (key == 33) NB_STEP(true, 16, 32);
+    else if (key == 64) NB_STEP(false, 32, 32);
+    else if (key == 65) NB_STEP(true, 32, 32);
+    else if (key == 96) NB_STEP(false, 48, 32);
+    else if (key == 97) NB_STEP(true, 48, 32);
+    else if (key == 128) NB_STEP(false, 64, 32);
+    else if (key == 129) NB_STEP(true, 64, 32);
   }
-  switch (qk * 2 + (int8 ? 1 : 0)) {
-    case 32: NB_STEP_LAUNCH(false, 16) break;
-    case 33: NB_STEP_LAUNCH(true, 16) break;
-    case 64: NB_STEP_LAUNCH(false, 32) break;
-    case 65: NB_STEP_LAUNCH(true, 32) break;
-    case 96: NB_STEP_LAUNCH(false, 48) break;
-    case 97: NB_STEP_LAUNCH(true, 48) break;
-    case 128: NB_STEP_LAUNCH(false, 64) break;
-    case 129: NB_STEP_LAUNCH(true, 64) break;
-    default: return cudaErrorInvalidValue;
-  }
-#undef NB_STEP_LAUNCH
+#undef NB_STEP
+  if (e != cudaSuccess) return e;
+  attn_combine_kernel<<<B, 256, 0, st>>>(part, heads, kvh, vh, nsplit, out);
   return cudaGetLastError();
 }
 
-// quant_into (crates/needle-core/src/v3/cache.rs:100-106) over `rows` head
-// vectors of `dim` <= 64: one warp per vector. Bit-exact: IEEE division for
-// the scale and its reciprocal, roundf half away from zero, clamp [-128, 127].
+// quant_into (crates/needle-core/src/v3/cache.rs:100-106) over `rows` vectors of
+// `dim` <= 64: one warp per vector. Bit-exact: IEEE division for the scale and
+// its reciprocal, roundf half away from zero, clamp [-128, 127].
 __global__ void kv_quant_kernel(const float* __restrict__ x, int rows, int dim, int8_t* __restrict__ q,
                                 float* __restrict__ scales) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
@@ -347,6 +522,37 @@ cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float*
   if (dim <= 0 || dim > 64) return cudaErrorInvalidValue;
   const int warps = 8;
   kv_quant_kernel<<<(rows + warps - 1) / warps, warps * 32, 0, st>>>(x, rows, dim, q, scales);
+  return cudaGetLastError();
+}
+
+// Combine of the forward's attention partials, fused with the output gate
+// (model.rs:305-308) and the rotation of out_proj's prepare_input.
+__global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ part,
+                                   const float* __restrict__ proj, float* __restrict__ oh) {
+  extern __shared__ __align__(16) float sm[];
+  const int r = blockIdx.x;
+  const int od = G.o_dim, opad = (od + 127) / 128 * 128, rep = G.heads / G.kvh, pw = rep * (G.vh + 2);
+  const float* gate = proj + (size_t)r * G.proj_dim + G.qkv_dim;
+  for (int i = threadIdx.x; i < opad; i += blockDim.x) {
+    float v = 0.f;
+    if (i < od) {
+      const int h = i / G.vh, d = i % G.vh, kh = h / rep, hl = h % rep;
+      v = combine_head(part + ((size_t)r * G.kvh + kh) * nsplit * pw, nsplit, rep, G.vh, hl, d) *
+          sigmoidf_(gate[i]);
+    }
+    sm[i] = v;
+  }
+  __syncthreads();
+  fwht_groups_warp(sm, opad / 128);
+  __syncthreads();
+  for (int i = threadIdx.x; i < opad; i += blockDim.x) oh[(size_t)r * opad + i] = sm[i];
+}
+
+cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
+                               const float* proj, float* oh, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  const int opad = (G.o_dim + 127) / 128 * 128;
+  attn_finish_kernel<<<rb.M, 256, opad * sizeof(float), st>>>(G, nsplit, part, proj, oh);
   return cudaGetLastError();
 }
 

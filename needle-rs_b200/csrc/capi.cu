@@ -648,8 +648,18 @@ int nd_attend_step(const float* q, const void* k, const void* v, const float* ks
                    int int8, int slots, const int* lo, const int* hi, int B, int heads, int kv_heads,
                    int qk, int vh, float* out, void* stream) {
   if (!q || !k || !v || !lo || !hi || !out || (int8 && (!ks || !vs))) return nd_status(cudaErrorInvalidValue);
-  return nd_status(nb::launch_attend_step(q, k, v, ks, vs, int8, slots, lo, hi, B, heads, kv_heads, qk,
-                                          vh, out, (cudaStream_t)stream));
+  if (B <= 0) return 0;
+  if (kv_heads <= 0 || heads % kv_heads || slots <= 0) return nd_status(cudaErrorInvalidValue);
+  // Split partials live in stream-ordered scratch: allocated and released on
+  // `stream`, so concurrent calls on different streams never share it.
+  cudaStream_t st = (cudaStream_t)stream;
+  const int ns = nb::attn_nsplit(B, kv_heads, slots);
+  float* part = nullptr;
+  cudaError_t e = cudaMallocAsync((void**)&part, nb::attn_part_floats(B, heads, kv_heads, vh, ns) * 4, st);
+  if (e != cudaSuccess) return nd_status(e);
+  e = nb::launch_attend_step(q, k, v, ks, vs, int8, slots, lo, hi, B, heads, kv_heads, qk, vh, ns, part, out, st);
+  cudaError_t f = cudaFreeAsync(part, st);
+  return nd_status(e != cudaSuccess ? e : f);
 }
 
 const char* nd_last_error(void) { return g_nd_err.c_str(); }

@@ -62,6 +62,7 @@ void Workspace::release() {
   for (void* p : ps)
     if (p) cudaFree(p);
   if (logits) cudaFree(logits);
+  if (part) cudaFree(part);
   if (lm_last) cudaFree(lm_last);
   *this = Workspace();
 }
@@ -98,6 +99,24 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
     }
   }
   ws.cap = cap;
+  epoch++;
+  return true;
+}
+
+bool Engine::ensure_part(size_t rows, int nsplit, std::string* err) {
+  const size_t need = attn_part_floats((int)rows, G.heads, G.kvh, G.vh, nsplit);
+  if (need <= ws.part_cap) return true;
+  cudaStreamSynchronize(stream);
+  if (ws.part) cudaFree(ws.part);
+  ws.part = nullptr;
+  const size_t cap = std::max(need, ws.part_cap * 2);
+  cudaError_t e = cudaMalloc(&ws.part, cap * 4);
+  if (e != cudaSuccess) {
+    ws.part_cap = 0;
+    *err = cuda_msg("allocating attention partials", e);
+    return false;
+  }
+  ws.part_cap = cap;
   epoch++;
   return true;
 }
@@ -747,7 +766,7 @@ cudaError_t Prof::mark(int kind, cudaStream_t st, int nlaunch) {
 #define NB_MARK(kind, n) \
   if (prof) NB_TRY(prof->mark(kind, st, n))
 
-cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, Prof* prof) {
+cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof) {
   const int M = rb.M, d = G.d, S = G.n_sites;
   const int dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   if (S > 0) {
@@ -768,9 +787,9 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, Prof
     NB_MARK(PK_QKVG, 1);
     NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, st));
     NB_MARK(PK_QKV_POST, 1);
-    NB_TRY(launch_attention(G, l, rb, lp[l], ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, ws.attn, st, int8 ? 1 : 0));
+    NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, ws.part, st, int8 ? 1 : 0));
     NB_MARK(PK_ATTN, 1);
-    NB_TRY(launch_attn_finish(G, rb, ws.attn, ws.proj, ws.oh, st));
+    NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
     NB_MARK(PK_ATTN_FINISH, 1);
     NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st));
     NB_MARK(PK_OUT_PROJ, 1);
@@ -845,7 +864,10 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
     while (i1 < n && (i1 == i0 || rows + lens[i1] <= MAX_PREFILL_ROWS)) rows += lens[i1++];
     for (size_t i = i0; i < i1; ++i)
       if (!ensure_slots(ss[i], lens[i] - 1, err)) return false;
-    if (!ensure_ws(rows, err) || !ensure_logits(this, i1 - i0, err)) return false;
+    size_t maxlen = 0;
+    for (size_t i = i0; i < i1; ++i) maxlen = std::max(maxlen, lens[i]);
+    const int ns = attn_nsplit((int)rows, G.kvh, (int)maxlen);
+    if (!ensure_ws(rows, err) || !ensure_logits(this, i1 - i0, err) || !ensure_part(rows, ns, err)) return false;
     std::vector<RowInfo> ri(rows);
     std::vector<uint32_t> tok(rows);
     std::vector<int> last(i1 - i0);
@@ -860,7 +882,7 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
     cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), rows * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tok.data(), rows * 4, cudaMemcpyHostToDevice, stream);
     RowBatch rb{ws.rows, ws.tokens, (int)rows, MODE_PREFILL};
-    if (e == cudaSuccess) e = forward(rb, stream, ss[i0]->int8);
+    if (e == cudaSuccess) e = forward(rb, stream, ss[i0]->int8, ns);
     if (e == cudaSuccess) e = launch_step_end(rb, stream);
     for (size_t i = 0; e == cudaSuccess && i < i1 - i0; ++i)
       e = cudaMemcpyAsync(ws.lm_last + i * dpad, ws.lm_in + (size_t)last[i] * dpad, dpad * 4,
@@ -907,14 +929,17 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
       }
     if (!ensure_slots(ss[i], ss[i]->pos, err)) return false;
   }
-  if (!ensure_ws(n, err) || !ensure_logits(this, n, err)) return false;
+  size_t maxpos = 0;
+  for (size_t i = 0; i < n; ++i) maxpos = std::max(maxpos, ss[i]->pos);
+  const int ns = attn_nsplit((int)n, G.kvh, (int)maxpos + 1);
+  if (!ensure_ws(n, err) || !ensure_logits(this, n, err) || !ensure_part(n, ns, err)) return false;
   std::vector<RowInfo> ri(n);
   for (size_t i = 0; i < n; ++i) ri[i] = RowInfo{ss[i]->d_desc, (int)ss[i]->pos, -1, -1, 0};
   const int dpad = (G.d + 127) / 128 * 128;
   cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), n * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
   if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tokens, n * 4, cudaMemcpyHostToDevice, stream);
   RowBatch rb{ws.rows, ws.tokens, (int)n, MODE_DECODE};
-  if (e == cudaSuccess) e = forward(rb, stream, ss[0]->int8);
+  if (e == cudaSuccess) e = forward(rb, stream, ss[0]->int8, ns);
   if (e == cudaSuccess) e = launch_step_end(rb, stream);
   if (e == cudaSuccess) e = head(ws.lm_in, dpad, (int)n, ws.logits, ws.next, stream);
   if (e == cudaSuccess && logits)
@@ -989,7 +1014,14 @@ bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, boo
     }
     if (!ensure_slots(s, s->pos, err)) return false;
   }
-  if (!ensure_ws(n, err)) return false;
+  size_t maxpos = 0;
+  for (Session* s : b->sessions) maxpos = std::max(maxpos, s->pos);
+  const int ns = attn_nsplit((int)n, G.kvh, (int)maxpos + 1);
+  if (ns != b->nsplit) {  // a different split count changes the launch shapes
+    b->nsplit = ns;
+    b->graph_epoch = 0;
+  }
+  if (!ensure_ws(n, err) || !ensure_part(n, ns, err)) return false;
   const int dpad = (G.d + 127) / 128 * 128;
   float* lg = d_logits;
   if (!lg) {
@@ -999,7 +1031,7 @@ bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, boo
   RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
   auto body = [&](cudaStream_t s) -> cudaError_t {
     NB_TRY(launch_step_begin(rb, b->d_sess, s));
-    NB_TRY(forward(rb, s, b->int8));
+    NB_TRY(forward(rb, s, b->int8, ns));
     NB_TRY(launch_step_end(rb, s));
     NB_TRY(head(ws.lm_in, dpad, (int)n, lg, b->d_next, s));
     return cudaSuccess;
@@ -1054,7 +1086,10 @@ bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string*
     }
     if (!ensure_slots(s, s->pos, err)) return false;
   }
-  if (!ensure_ws(n, err) || !ensure_logits(this, n, err)) return false;
+  size_t maxpos = 0;
+  for (Session* s : b->sessions) maxpos = std::max(maxpos, s->pos);
+  const int ns = attn_nsplit((int)n, G.kvh, (int)maxpos + 1);
+  if (!ensure_ws(n, err) || !ensure_logits(this, n, err) || !ensure_part(n, ns, err)) return false;
   const int dpad = (G.d + 127) / 128 * 128;
   RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
   Prof prof;
@@ -1064,7 +1099,7 @@ bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string*
     NB_TRY(p->mark(PK_BOOK, st, 0));
     NB_TRY(launch_step_begin(rb, b->d_sess, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
-    NB_TRY(forward(rb, st, b->int8, p));
+    NB_TRY(forward(rb, st, b->int8, ns, p));
     NB_TRY(launch_step_end(rb, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
     NB_TRY(head(ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p));

@@ -67,6 +67,8 @@ struct Workspace {
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;
   int* last_rows = nullptr;
+  float* part = nullptr;  // attention split partials
+  size_t part_cap = 0;    // floats
   void release();
 };
 
@@ -84,6 +86,7 @@ class Batch {
   bool graph_logits = false;
   uint64_t graph_epoch = 0;
   uint64_t warm_epoch = 0;
+  int nsplit = 0;              // attention splits baked into the graph
   uint32_t* d_tok = nullptr;   // [n] token fed this step
   uint32_t* d_next = nullptr;  // [n] greedy pick of this step
 };
@@ -148,8 +151,9 @@ class Engine {
   uint64_t epoch = 1;  // bumped whenever a session's device layout changes
 
   bool ensure_ws(size_t rows, std::string* err);
+  bool ensure_part(size_t rows, int nsplit, std::string* err);
   bool ensure_slots(Session* s, size_t pos, std::string* err);
-  cudaError_t forward(const RowBatch& rb, cudaStream_t st, bool int8, Prof* prof = nullptr);
+  cudaError_t forward(const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof = nullptr);
   cudaError_t head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                    cudaStream_t st, Prof* prof = nullptr);
 };

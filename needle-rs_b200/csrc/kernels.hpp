@@ -58,10 +58,14 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                             const float* rope_cs, const float* proj, float* qpost, void* pk,
                             void* pv, float* pks, float* pvs, cudaStream_t st);
-cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+// Attention writes per-(row, KV head, split) partials; attn_finish merges the
+// splits, applies the output gate and rotates for out_proj.
+int attn_nsplit(int rows, int kvh, int max_span);
+size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit);
+cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const void* pk, const void* pv, const float* pks,
-                             const float* pvs, float* attn, cudaStream_t st, int int8);
-cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, const float* attn,
+                             const float* pvs, float* part, cudaStream_t st, int int8);
+cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
                                const float* proj, float* oh, cudaStream_t st);
 cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                               const uint32_t* p1, const uint32_t* p2, const float* projo,
@@ -78,9 +82,10 @@ cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float*
                             cudaStream_t st);
 // Standalone batched decode attention over caller-provided rings
 // (attention.rs:300-377): B independent sessions, each with its own [lo, hi].
+// `part` is scratch of attn_part_floats(B, heads, kvh, vh, nsplit) floats.
 cudaError_t launch_attend_step(const float* q, const void* k, const void* v, const float* ks,
                                const float* vs, int int8, int slots, const int* lo, const int* hi,
-                               int B, int heads, int kvh, int qk, int vh, float* out,
-                               cudaStream_t st);
+                               int B, int heads, int kvh, int qk, int vh, int nsplit, float* part,
+                               float* out, cudaStream_t st);
 
 }  // namespace nb

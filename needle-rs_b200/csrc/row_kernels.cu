@@ -517,30 +517,6 @@ cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const Laye
   return cudaGetLastError();
 }
 
-// attention output * sigmoid(gate) (model.rs:305-308), then the rotation of
-// out_proj's prepare_input.
-__global__ void attn_finish_kernel(Geo G, const float* __restrict__ attn, const float* __restrict__ proj,
-                                   float* __restrict__ oh) {
-  extern __shared__ __align__(16) float sm[];
-  const int r = blockIdx.x;
-  const int od = G.o_dim, opad = (od + 127) / 128 * 128;
-  const float* gate = proj + (size_t)r * G.proj_dim + G.qkv_dim;
-  for (int i = threadIdx.x; i < opad; i += blockDim.x)
-    sm[i] = i < od ? attn[(size_t)r * od + i] * sigmoidf_(gate[i]) : 0.f;
-  __syncthreads();
-  fwht_groups_warp(sm, opad / 128);
-  __syncthreads();
-  for (int i = threadIdx.x; i < opad; i += blockDim.x) oh[(size_t)r * opad + i] = sm[i];
-}
-
-cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, const float* attn,
-                               const float* proj, float* oh, cudaStream_t st) {
-  if (rb.M <= 0) return cudaSuccess;
-  const int opad = (G.o_dim + 127) / 128 * 128;
-  attn_finish_kernel<<<rb.M, 256, opad * sizeof(float), st>>>(G, attn, proj, oh);
-  return cudaGetLastError();
-}
-
 // ---------------------------------------------------------------- block tail
 // model.rs:309-356: post_norm + gated residual, pre_hada norm, HadamardMLP
 // (v3/kernels.rs:119-180), MLP residual, y = block - u and scatter_up
