@@ -191,6 +191,23 @@ int nd_attend_step(const float *q, const void *k, const void *v, const float *ks
                    int int8, int slots, const int *lo, const int *hi, int B, int heads, int kv_heads,
                    int qk, int vh, float *out, void *stream);
 
+/* Allocation-free nd_attend_step. No counterpart in the reference (its CPU
+ * code never allocates device memory). For callers that cannot allocate device
+ * memory — a runtime that reserved the GPU's memory for its own pool, or a
+ * latency-critical path that must not make an allocation call — the split
+ * partials use a fixed 4 MiB device array compiled into this library (held by
+ * every GPU that loads the library until exit) instead of per-call scratch.
+ * Requests needing more than 1048576 floats of partials even with a single
+ * position split (B * heads * (vh + 2) floats) fail with cudaErrorInvalidValue
+ * and a message in nd_last_error(). The first call on each device looks up the
+ * array's device address; make that first call before any stream capture.
+ * All calls on a device share the array and keep the last call's contents:
+ * calls whose kernels overlap on the GPU race and must be serialised.
+ * Arguments and result as nd_attend_step. */
+int nd_attend_step_noalloc(const float *q, const void *k, const void *v, const float *ks,
+                           const float *vs, int int8, int slots, const int *lo, const int *hi,
+                           int B, int heads, int kv_heads, int qk, int vh, float *out, void *stream);
+
 /* Returns the cudaError_t of the last nd_* failure on this thread as text. */
 const char *nd_last_error(void);
 

@@ -20,6 +20,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "kernels.hpp"
@@ -556,4 +557,81 @@ cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, con
   return cudaGetLastError();
 }
 
+
+// ---------------------------------------------------------------------------
+// Allocation-free form of the standalone decode attention.
+//
+// Some callers cannot allocate device memory at all: a serving runtime that has
+// reserved the GPU's memory for its own pool up front (so a cudaMalloc or
+// cudaMallocAsync from inside a plugin fails, or fragments that pool), or code
+// on a latency-critical path that must not make any allocation call. For them
+// nd_attend_step_noalloc keeps the split partials in a fixed array compiled
+// into this library instead of allocating them per call.
+//
+// The array holds NB_NOALLOC_SCRATCH_FLOATS floats (4 MiB). Every GPU that loads
+// the library holds it until the process exits. All calls on a device share it
+// and it keeps the last call's contents; each call overwrites every partial it
+// later reads, so nothing has to start at zero. Calls whose kernels overlap on
+// the GPU (different streams, or graphs replayed concurrently) race on the
+// array: serialise them.
+constexpr size_t NB_NOALLOC_SCRATCH_FLOATS = (size_t)1 << 20;
+static __device__ __align__(256) float g_attn_noalloc_scratch[NB_NOALLOC_SCRATCH_FLOATS];
+
+namespace {
+std::mutex g_noalloc_mu;
+float* g_noalloc_ptr[256] = {};  // device address of the array, per device ordinal
+
+// In host code the array's name stands for a host-side shadow, not a device
+// address; the device address is looked up once per device, with that device
+// current.
+cudaError_t noalloc_scratch(float** out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= 256) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lk(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    g_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return cudaSuccess;
+}
+}  // namespace
+
 }  // namespace nb
+
+extern "C" int nd_attend_step_noalloc(const float* q, const void* k, const void* v, const float* ks,
+                                      const float* vs, int int8, int slots, const int* lo, const int* hi,
+                                      int B, int heads, int kv_heads, int qk, int vh, float* out,
+                                      void* stream) {
+  using namespace nb;
+  if (!q || !k || !v || !lo || !hi || !out || (int8 && (!ks || !vs)) || kv_heads <= 0 || heads % kv_heads ||
+      slots <= 0 || vh <= 0) {
+    nd_record_error(cudaErrorInvalidValue, "nd_attend_step_noalloc: invalid argument");
+    return (int)cudaErrorInvalidValue;
+  }
+  if (B <= 0) return 0;
+  // Fewer position splits need less scratch; the result does not depend on the
+  // split count beyond f32 rounding. Reject what one split cannot fit.
+  int ns = attn_nsplit(B, kv_heads, slots);
+  while (ns > 1 && attn_part_floats(B, heads, kv_heads, vh, ns) > NB_NOALLOC_SCRATCH_FLOATS) --ns;
+  if (attn_part_floats(B, heads, kv_heads, vh, ns) > NB_NOALLOC_SCRATCH_FLOATS) {
+    nd_record_error(cudaErrorInvalidValue,
+                    "nd_attend_step_noalloc: B * heads * (v_head_dim + 2) floats exceed the fixed 4 MiB "
+                    "scratch (1048576 floats); use nd_attend_step or a smaller batch");
+    return (int)cudaErrorInvalidValue;
+  }
+  float* part = nullptr;
+  cudaError_t e = noalloc_scratch(&part);
+  if (e == cudaSuccess)
+    e = launch_attend_step(q, k, v, ks, vs, int8, slots, lo, hi, B, heads, kv_heads, qk, vh, ns, part, out,
+                           (cudaStream_t)stream);
+  if (e != cudaSuccess) {
+    nd_record_error(e, nullptr);
+    return (int)e;
+  }
+  return 0;
+}

@@ -665,3 +665,13 @@ int nd_attend_step(const float* q, const void* k, const void* v, const float* ks
 const char* nd_last_error(void) { return g_nd_err.c_str(); }
 
 }  // extern "C"
+
+namespace nb {
+void nd_record_error(cudaError_t e, const char* msg) {
+  g_nd_err = msg ? std::string(msg) : std::string(cudaGetErrorName(e)) + ": " + cudaGetErrorString(e);
+}
+}  // namespace nb
+
+extern "C" {
+
+}  // extern "C"

@@ -77,6 +77,9 @@ cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* o
 cudaError_t launch_step_begin(const RowBatch& rb, SessDesc* const* sess, cudaStream_t st);
 cudaError_t launch_step_end(const RowBatch& rb, cudaStream_t st);
 
+// Records the text returned by nd_last_error() (msg, or the CUDA error's name).
+void nd_record_error(cudaError_t e, const char* msg);
+
 // Standalone int8 quantiser of head vectors (cache.rs:100-106), bit-exact.
 cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float* scales,
                             cudaStream_t st);
