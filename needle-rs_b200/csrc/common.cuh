@@ -146,4 +146,26 @@ __device__ __forceinline__ void fwht_groups_warp(float* buf, int n128) {
 
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
+// Packed row and norms of logical row r of a (multi-segment) CQ matrix.
+__device__ __forceinline__ void cq_row_ptr(const CqMat& W, int r, const uint8_t** row, const __half** nrm) {
+  int s = 0, base = 0;
+#pragma unroll
+  for (int i = 0; i < MAX_SEG - 1; ++i) {
+    if (s == i && i < W.nseg - 1 && r >= base + W.seg[i].rows) {
+      base += W.seg[i].rows;
+      s = i + 1;
+    }
+  }
+  *row = W.seg[s].packed + (size_t)(r - base) * W.row_bytes;
+  *nrm = W.seg[s].norms + (size_t)(r - base) * W.groups;
+}
+
+// Codes of elements g*128 + lane*4 .. +3 of a packed row, code i at bits
+// [i*bits, (i+1)*bits) of the result (LSB-first bitstream, cq.rs:908-925):
+// two bytes per lane at 4 bits, one byte at 2 bits.
+__device__ __forceinline__ uint32_t cq_quad_codes(const uint8_t* row, int bits, int g, int lane) {
+  if (bits == 4) return __ldg(reinterpret_cast<const uint16_t*>(row + g * 64) + lane);
+  return __ldg(row + g * 32 + lane);
+}
+
 }  // namespace nb

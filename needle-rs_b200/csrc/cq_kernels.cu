@@ -173,7 +173,9 @@ __global__ void __launch_bounds__(256) cq_gemm_simt_kernel(CqMat W, const float*
   __shared__ __align__(16) float Ws[GB_KS][GB_N + GB_PAD];
   __shared__ __align__(16) float Xs[GB_KS][GB_M + GB_PAD];
   __shared__ float Ns[GB_N];
+  __shared__ float lev[16];
   const int tid = threadIdx.x;
+  if (tid < 16) lev[tid] = W.levels[tid];
   const int n_base = blockIdx.x * GB_N, m_base = blockIdx.y * GB_M;
   const int tn = (tid % 16) * 4, tm = (tid / 16) * 4;
   constexpr int P = 8 / BITS;
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(256) cq_gemm_simt_kernel(CqMat W, const float*
       for (int bi = tid / GB_N; bi < BPS; bi += 256 / GB_N) {
         uint8_t byte = my_row ? my_row[(size_t)g * BPG + hk * BPS + bi] : 0;
 #pragma unroll
-        for (int j = 0; j < P; ++j) Ws[bi * P + j][my_nl] = W.levels[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
+        for (int j = 0; j < P; ++j) Ws[bi * P + j][my_nl] = lev[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
       }
       if (hk == 0 && tid < GB_N) Ns[tid] = my_norm ? __half2float(my_norm[g]) : 0.f;
       for (int i = tid; i < GB_M * (GB_KS / 4); i += 256) {

@@ -18,23 +18,27 @@ constexpr float EPS = 1e-6f;  // crates/needle-core/src/kernels.rs:11, norm.rs:6
 
 // Decode one 128-element quantisation group of a CQ row into `out`
 // (levels[idx] * norm, cq.rs:791-809); each lane writes elements lane*4..+3.
-__device__ __forceinline__ void decode_group_lane(const CqMat& W, const uint8_t* row, float norm,
-                                                  int g, float (&v)[4]) {
+// `lev` is the tensor's level table in shared memory.
+__device__ __forceinline__ void decode_group_lane(const CqMat& W, const float* lev, const uint8_t* row,
+                                                  float norm, int g, float (&v)[4]) {
   const int lane = threadIdx.x & 31;
-  const int mask = (1 << W.bits) - 1;
+  const int bits = W.bits, mask = (1 << bits) - 1;
+  const uint32_t c = cq_quad_codes(row, bits, g, lane);
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    int e = g * 128 + lane * 4 + i;
-    int bit = e * W.bits;
-    int code = (row[bit >> 3] >> (bit & 7)) & mask;
-    v[i] = W.levels[code] * norm;
-  }
+  for (int i = 0; i < 4; ++i) v[i] = lev[(c >> (i * bits)) & mask] * norm;
+}
+
+__device__ __forceinline__ void load_levels(const CqMat& W, float* lev) {
+  if (threadIdx.x < 16) lev[threadIdx.x] = W.levels[threadIdx.x];
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------- embedding
 // model.rs:196-203: dequantize_row (levels*norm, inverse rotation) then
 // * sqrt(d_model), broadcast into every mHC lane.
 __global__ void embed_kernel(Geo G, CqMat emb, RowBatch rb, float* __restrict__ lanes) {
+  __shared__ float lev[16];
+  load_levels(emb, lev);
   const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   uint32_t tok = rb.tokens[r];
@@ -44,7 +48,7 @@ __global__ void embed_kernel(Geo G, CqMat emb, RowBatch rb, float* __restrict__ 
   float* out = lanes + (size_t)r * G.lanes * G.d;
   for (int g = wid; g < emb.groups; g += nw) {
     float v[4];
-    decode_group_lane(emb, row, __half2float(nrm[g]), g, v);
+    decode_group_lane(emb, lev, row, __half2float(nrm[g]), g, v);
     fwht128_warp(v);
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -76,6 +80,8 @@ __global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, Ro
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos;
   const CqMat& T = tables[site];
+  __shared__ float lev[16];
+  load_levels(T, lev);
   float* out = fetched + ((size_t)r * G.n_sites + site) * G.d;
   for (int t = wid; t < G.e_tables; t += nw) {
     const int oi = t / G.e_heads, h = t % G.e_heads;
@@ -99,7 +105,7 @@ __global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, Ro
       const uint32_t slot = acc % (uint32_t)G.e_slots;
       const size_t trow = (size_t)t * G.e_slots + slot;
       const uint8_t* row = T.seg[0].packed + trow * T.row_bytes;
-      decode_group_lane(T, row, __half2float(T.seg[0].norms[trow * T.groups]), 0, v);
+      decode_group_lane(T, lev, row, __half2float(T.seg[0].norms[trow * T.groups]), 0, v);
     }
     reinterpret_cast<float4*>(out + t * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
   }
@@ -187,36 +193,41 @@ __device__ __forceinline__ float sinkhorn_lane(float m, int n) {
 }
 
 // Dot of one CQ row (4- or 2-bit) with a prepared activation in shared memory,
-// one warp. Returns the full sum in every lane.
-__device__ __forceinline__ float cq_row_dot_warp(const CqMat& W, int row_index, const float* xs) {
+// one warp; lane l covers elements g*128 + l*4 .. +3 of every group, so the
+// float4 reads of `xs` are conflict-free. `lev` is the matrix's level table in
+// shared memory. The norm multiplies the lane's part of each group dot, as
+// cq.rs:666-672 applies `norm * group_dot`. Returns the sum in every lane.
+__device__ __forceinline__ float cq_row_dot_warp(const CqMat& W, int row_index, const float* lev,
+                                                 const float* xs) {
   const int lane = threadIdx.x & 31;
-  int local, s = 0, base = 0;
-  for (int i = 0; i < W.nseg - 1; ++i) {
-    if (row_index < base + W.seg[i].rows) break;
-    base += W.seg[i].rows;
-    s = i + 1;
-  }
-  local = row_index - base;
-  const uint8_t* row = W.seg[s].packed + (size_t)local * W.row_bytes;
-  const __half* nrm = W.seg[s].norms + (size_t)local * W.groups;
-  const int E = 128 / W.bits;  // elements per 16-byte chunk
-  const int mask = (1 << W.bits) - 1;
-  const int per_byte = 8 / W.bits;
+  const uint8_t* row;
+  const __half* nrm;
+  cq_row_ptr(W, row_index, &row, &nrm);
+  const int bits = W.bits, mask = (1 << bits) - 1;
   float acc = 0.f;
-  for (int c = lane; c < W.row_bytes / 16; c += 32) {
-    uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + c);
-    const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-    const int k0 = c * E;
-    float part = 0.f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q)
-      for (int b = 0; b < 4 * per_byte; ++b) {
-        int code = (wd[q] >> (b * W.bits)) & mask;
-        part += W.levels[code] * xs[k0 + q * 4 * per_byte + b];
-      }
-    acc += __half2float(nrm[k0 / 128]) * part;
+#pragma unroll 4
+  for (int g = 0; g < W.groups; ++g) {
+    const uint32_t c = cq_quad_codes(row, bits, g, lane);
+    const float4 x = reinterpret_cast<const float4*>(xs + g * 128)[lane];
+    float p = lev[c & mask] * x.x;
+    p += lev[(c >> bits) & mask] * x.y;
+    p += lev[(c >> (2 * bits)) & mask] * x.z;
+    p += lev[(c >> (3 * bits)) & mask] * x.w;
+    acc += __half2float(nrm[g]) * p;
   }
   return warp_sum(acc);
+}
+
+// The level tables of the three mHC projections, copied to shared memory so a
+// lane-dependent lookup is a bank-parallel shared load.
+__device__ __forceinline__ void load_phi_levels(const CqMat& a, const CqMat& b, const CqMat& c, float* lev) {
+  const int t = threadIdx.x;
+  if (t < 16)
+    lev[t] = a.levels[t];
+  else if (t < 32)
+    lev[t] = b.levels[t - 16];
+  else if (t < 48)
+    lev[t] = c.levels[t - 32];
 }
 
 // mhc.rs:79-102 (mix_down) with the gate and Sinkhorn of mhc.rs:109-130, the
@@ -242,8 +253,10 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
   float* phi = hb + dpad;        // [32]
   float* red = phi + 32;         // [32]
   float* gsm = red + 32;         // [4 + 4 + 16]
+  float* lev = gsm + 24;         // [3][16] level tables of phi_pre, phi_post, phi_res
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
 
+  load_phi_levels(phi_pre, phi_post, phi_res, lev);
   const float* lr = lanes + (size_t)r * W;
   float ss = 0.f;
   for (int i = tid; i < W; i += blockDim.x) {
@@ -262,11 +275,11 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
   for (int k = wid; k < nrow; k += nw) {
     float v;
     if (k < n)
-      v = cq_row_dot_warp(phi_pre, li * n + k, X);
+      v = cq_row_dot_warp(phi_pre, li * n + k, lev, X);
     else if (k < 2 * n)
-      v = cq_row_dot_warp(phi_post, li * n + (k - n), X);
+      v = cq_row_dot_warp(phi_post, li * n + (k - n), lev + 16, X);
     else
-      v = cq_row_dot_warp(phi_res, li * n * n + (k - 2 * n), X);
+      v = cq_row_dot_warp(phi_res, li * n * n + (k - 2 * n), lev + 32, X);
     if (lane == 0) phi[k] = v;
   }
   __syncthreads();
@@ -327,14 +340,254 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
   for (int c = tid; c < dpad; c += blockDim.x) xh_out[(size_t)r * dpad + c] = hb[c];
 }
 
+// The same computation for many rows: PT_M rows per CTA so each mHC weight
+// group is decoded once for PT_M rows instead of once per row.
+//
+// Phase 1 streams the lanes of the tile one 128-wide group at a time: each
+// warp loads two rows' group, accumulates their sums of squares and rotates it
+// (FWHT) into a shared tile; then warp w dots the tile with outputs w, w+8 and
+// w+16 of the 2n + n^2 projected rows, lane l covering group elements
+// l*4..l*4+3. The rotation is linear, so the rms_unit scale (kernels.rs:32) is
+// applied to the finished dot products rather than to the lanes first. The
+// next group's lanes are loaded while the current one is consumed.
+// Phase 2 (one warp per row, no block barriers): gates and Sinkhorn, mix_down
+// re-reading the tile's lanes (L2-resident), the Engram gate, the ZCRMS norm
+// and the rotation of the attention input, exactly as the per-row kernel.
+constexpr int PT_M = 16;   // rows per CTA
+constexpr int PT_DQ = 8;   // d_model / 128 supported on this path
+
+__global__ void __launch_bounds__(256, 2)
+layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes, CqMat phi_pre,
+                       CqMat phi_post, CqMat phi_res, MhcParams mp, const float* __restrict__ norm_in,
+                       int site, const float* __restrict__ ekv, const float* __restrict__ evc,
+                       float* __restrict__ u_out, float* __restrict__ bx_out, float* __restrict__ xh_out,
+                       float* __restrict__ gates) {
+  __shared__ __align__(16) float Xs[PT_M][128];
+  __shared__ float lev[48];
+  __shared__ float phi_s[PT_M][24];
+  __shared__ float ss_s[PT_M];
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const int n = G.lanes, d = G.d, W = n * d, nrow = 2 * n + n * n;
+  const int m0 = blockIdx.x * PT_M;
+  const int rows = min(PT_M, rb.M - m0);
+  const int ngroups = W / 128;
+  load_phi_levels(phi_pre, phi_post, phi_res, lev);
+
+  // This warp's projected rows: o = wid + 8j.
+  const uint8_t* wrow[3];
+  const __half* wnrm[3];
+  int wbits[3], wlev[3];
+  bool wok[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int o = wid + 8 * j;
+    wok[j] = o < nrow;
+    wrow[j] = nullptr;
+    wnrm[j] = nullptr;
+    wbits[j] = 4;
+    wlev[j] = 0;
+    if (!wok[j]) continue;
+    if (o < n) {
+      cq_row_ptr(phi_pre, li * n + o, &wrow[j], &wnrm[j]);
+      wbits[j] = phi_pre.bits;
+      wlev[j] = 0;
+    } else if (o < 2 * n) {
+      cq_row_ptr(phi_post, li * n + (o - n), &wrow[j], &wnrm[j]);
+      wbits[j] = phi_post.bits;
+      wlev[j] = 16;
+    } else {
+      cq_row_ptr(phi_res, li * n * n + (o - 2 * n), &wrow[j], &wnrm[j]);
+      wbits[j] = phi_res.bits;
+      wlev[j] = 32;
+    }
+  }
+
+  // Rows wid and wid + 8 of the tile are loaded and rotated by this warp.
+  const bool okA = wid < rows, okB = wid + 8 < rows;
+  const float* lrA = lanes + (size_t)(m0 + wid) * W + lane * 4;
+  const float* lrB = lanes + (size_t)(m0 + wid + 8) * W + lane * 4;
+  const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 nA = okA ? __ldg(reinterpret_cast<const float4*>(lrA)) : z4;
+  float4 nB = okB ? __ldg(reinterpret_cast<const float4*>(lrB)) : z4;
+  float ssA = 0.f, ssB = 0.f;
+  float acc[3][PT_M];
+#pragma unroll
+  for (int j = 0; j < 3; ++j)
+#pragma unroll
+    for (int m = 0; m < PT_M; ++m) acc[j][m] = 0.f;
+  __syncthreads();  // level tables
+
+  for (int g = 0; g < ngroups; ++g) {
+    const float4 cA = nA, cB = nB;
+    if (g + 1 < ngroups) {
+      if (okA) nA = __ldg(reinterpret_cast<const float4*>(lrA + (g + 1) * 128));
+      if (okB) nB = __ldg(reinterpret_cast<const float4*>(lrB + (g + 1) * 128));
+    }
+    uint32_t wc[3];
+    float wn[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      wc[j] = wok[j] ? cq_quad_codes(wrow[j], wbits[j], g, lane) : 0u;
+      wn[j] = wok[j] ? __half2float(wnrm[j][g]) : 0.f;
+    }
+    {
+      float v[4] = {cA.x, cA.y, cA.z, cA.w};
+      ssA += v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+      fwht128_warp(v);
+      reinterpret_cast<float4*>(Xs[wid])[lane] = make_float4(v[0], v[1], v[2], v[3]);
+      float u[4] = {cB.x, cB.y, cB.z, cB.w};
+      ssB += u[0] * u[0] + u[1] * u[1] + u[2] * u[2] + u[3] * u[3];
+      fwht128_warp(u);
+      reinterpret_cast<float4*>(Xs[wid + 8])[lane] = make_float4(u[0], u[1], u[2], u[3]);
+    }
+    __syncthreads();
+    float w4[3][4];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int b = wbits[j], mask = (1 << b) - 1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) w4[j][i] = wn[j] * lev[wlev[j] + ((wc[j] >> (i * b)) & mask)];
+    }
+#pragma unroll
+    for (int m = 0; m < PT_M; ++m) {
+      if (m < rows) {
+        const float4 x = reinterpret_cast<const float4*>(Xs[m])[lane];
+#pragma unroll
+        for (int j = 0; j < 3; ++j)
+          acc[j][m] += w4[j][0] * x.x + w4[j][1] * x.y + w4[j][2] * x.z + w4[j][3] * x.w;
+      }
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+#pragma unroll
+    for (int m = 0; m < PT_M; ++m) {
+      const float v = warp_sum(acc[j][m]);
+      if (lane == 0 && wok[j] && m < rows) phi_s[m][wid + 8 * j] = v;
+    }
+  }
+  ssA = warp_sum(ssA);
+  ssB = warp_sum(ssB);
+  if (lane == 0) {
+    if (okA) ss_s[wid] = ssA;
+    if (okB) ss_s[wid + 8] = ssB;
+  }
+  __syncthreads();
+
+  const int nq = d / 128, act = li % n;
+  for (int m = wid; m < rows; m += 8) {
+    const int r = m0 + m;
+    const float inv = 1.0f / sqrtf(ss_s[m] / (float)W + EPS);  // rms_unit_to, kernels.rs:32
+    float hpre = 0.f, hpost = 0.f;
+    if (lane < n) {
+      const float pre_off = lane == act ? 4.0f : -4.0f;   // mhc.rs:56
+      const float post_off = lane == act ? 0.0f : -4.0f;  // mhc.rs:65
+      hpre = sigmoidf_(mp.a_pre * (phi_s[m][lane] * inv) + mp.b_pre[lane] + pre_off);
+      hpost = 2.0f * sigmoidf_(mp.a_post * (phi_s[m][n + lane] * inv) + mp.b_post[lane] + post_off);
+    }
+    const float mres = lane < n * n ? mp.a_res * (phi_s[m][2 * n + lane] * inv) + mp.b_res[lane] : 0.f;
+    const float hres = sinkhorn_lane(mres, n);
+    float* gout = gates + (size_t)r * 24;
+    if (lane < n) gout[lane] = hpost;
+    if (lane < n * n) gout[n + lane] = hres;
+    float hp[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) hp[l] = __shfl_sync(0xffffffffu, hpre, l);
+    // mix_down (mhc.rs:79-102)
+    const float* lr = lanes + (size_t)r * W + lane * 4;
+    float bxv[PT_DQ][4];
+#pragma unroll
+    for (int q = 0; q < PT_DQ; ++q) {
+      if (q >= nq) continue;
+      float a[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int l = 0; l < n; ++l) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(lr + l * d + q * 128));
+        a[0] += hp[l] * t.x;
+        a[1] += hp[l] * t.y;
+        a[2] += hp[l] * t.z;
+        a[3] += hp[l] * t.w;
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i) bxv[q][i] = a[i];
+      reinterpret_cast<float4*>(u_out + (size_t)r * d + q * 128)[lane] = make_float4(a[0], a[1], a[2], a[3]);
+    }
+    if (site >= 0) {  // Engram gate, engram.rs:112-132
+      const size_t kv_ld = (size_t)G.n_sites * 2 * d;
+      const float* ek = ekv + (size_t)r * kv_ld + (size_t)site * 2 * d + lane * 4;
+      const float* ev = evc + ((size_t)r * G.n_sites + site) * d + lane * 4;
+      float sx = 0.f, sk = 0.f, sd = 0.f;
+#pragma unroll
+      for (int q = 0; q < PT_DQ; ++q) {
+        if (q >= nq) continue;
+        const float4 t = __ldg(reinterpret_cast<const float4*>(ek + q * 128));
+        const float kk[4] = {t.x, t.y, t.z, t.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          sx += bxv[q][i] * bxv[q][i];
+          sk += kk[i] * kk[i];
+          sd += bxv[q][i] * kk[i];
+        }
+      }
+      sx = warp_sum(sx);
+      sk = warp_sum(sk);
+      sd = warp_sum(sd);
+      const float ux = 1.0f / sqrtf(sx / (float)d + 1e-6f);
+      const float uk = 1.0f / sqrtf(sk / (float)d + 1e-6f);
+      const float alpha = sigmoidf_(sd * ux * uk / sqrtf((float)d));
+#pragma unroll
+      for (int q = 0; q < PT_DQ; ++q) {
+        if (q >= nq) continue;
+        const float4 t = __ldg(reinterpret_cast<const float4*>(ev + q * 128));
+        bxv[q][0] += alpha * t.x;
+        bxv[q][1] += alpha * t.y;
+        bxv[q][2] += alpha * t.z;
+        bxv[q][3] += alpha * t.w;
+      }
+    }
+    float s2 = 0.f;
+#pragma unroll
+    for (int q = 0; q < PT_DQ; ++q) {
+      if (q >= nq) continue;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) s2 += bxv[q][i] * bxv[q][i];
+    }
+    s2 = warp_sum(s2);
+    const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
+#pragma unroll
+    for (int q = 0; q < PT_DQ; ++q) {
+      if (q >= nq) continue;
+      const int c0 = q * 128 + lane * 4;
+      reinterpret_cast<float4*>(bx_out + (size_t)r * d + q * 128)[lane] =
+          make_float4(bxv[q][0], bxv[q][1], bxv[q][2], bxv[q][3]);
+      const float4 ni = __ldg(reinterpret_cast<const float4*>(norm_in + c0));
+      float h[4] = {(1.0f + ni.x) * bxv[q][0] * inv2, (1.0f + ni.y) * bxv[q][1] * inv2,
+                    (1.0f + ni.z) * bxv[q][2] * inv2, (1.0f + ni.w) * bxv[q][3] * inv2};
+      fwht128_warp(h);
+      reinterpret_cast<float4*>(xh_out + (size_t)r * d + q * 128)[lane] = make_float4(h[0], h[1], h[2], h[3]);
+    }
+  }
+}
+
+// Rows at which the tiled kernel takes over from one CTA per row.
+constexpr int PT_MIN_ROWS = 512;
+
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                              const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
                              const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                              const float* evc, float* u, float* bx, float* xh, float* gates,
                              cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
+  const int nrow = 2 * G.lanes + G.lanes * G.lanes;
+  const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
+                        (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0;
+  if (rb.M >= PT_MIN_ROWS && tiled_ok) {
+    layer_pre_tiled_kernel<<<(rb.M + PT_M - 1) / PT_M, 256, 0, st>>>(
+        G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates);
+    return cudaGetLastError();
+  }
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
-  const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24) * sizeof(float);
+  const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48) * sizeof(float);
   cudaError_t e = allow_smem((const void*)layer_pre_kernel, smem);
   if (e != cudaSuccess) return e;
   layer_pre_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in,
@@ -544,6 +797,54 @@ __device__ void kron_apply_block(const float* z, const float* __restrict__ a,
   __syncthreads();
 }
 
+// The same contraction register-tiled for ba, bb multiples of 4: each thread
+// produces four consecutive k of one column j (stage 1) or l (stage 2), so a
+// step reads one broadcast float4 and one per-lane float for four FMAs. The
+// intermediate is stored transposed, tmpT[j][k] with row stride ba + 4 so the
+// float4 stores of consecutive j hit distinct banks. Sums run over i and j in
+// the same ascending order as kron_apply_block.
+__device__ void kron_apply_block4(const float* z, const float* __restrict__ a,
+                                  const float* __restrict__ b, int ba, int bb, float* tmpT, float* As,
+                                  float* Bs, float* out) {
+  for (int i = threadIdx.x; i < ba * ba; i += blockDim.x) As[i] = a[i];
+  for (int i = threadIdx.x; i < bb * bb; i += blockDim.x) Bs[i] = b[i];
+  __syncthreads();
+  const int nq = (ba / 4) * bb, ts = ba + 4;
+  for (int e = threadIdx.x; e < nq; e += blockDim.x) {
+    const int j = e % bb, k0 = (e / bb) * 4;
+    float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+#pragma unroll 8
+    for (int i = 0; i < ba; ++i) {
+      const float zv = z[i * bb + j];
+      const float4 av = *reinterpret_cast<const float4*>(As + i * ba + k0);
+      a0 += zv * av.x;
+      a1 += zv * av.y;
+      a2 += zv * av.z;
+      a3 += zv * av.w;
+    }
+    *reinterpret_cast<float4*>(tmpT + j * ts + k0) = make_float4(a0, a1, a2, a3);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < nq; e += blockDim.x) {
+    const int l = e % bb, k0 = (e / bb) * 4;
+    float o0 = 0.f, o1 = 0.f, o2 = 0.f, o3 = 0.f;
+#pragma unroll 8
+    for (int j = 0; j < bb; ++j) {
+      const float bv = Bs[j * bb + l];
+      const float4 tv = *reinterpret_cast<const float4*>(tmpT + j * ts + k0);
+      o0 += tv.x * bv;
+      o1 += tv.y * bv;
+      o2 += tv.z * bv;
+      o3 += tv.w * bv;
+    }
+    out[(k0 + 0) * bb + l] = o0;
+    out[(k0 + 1) * bb + l] = o1;
+    out[(k0 + 2) * bb + l] = o2;
+    out[(k0 + 3) * bb + l] = o3;
+  }
+  __syncthreads();
+}
+
 __global__ void layer_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
                                   const uint32_t* __restrict__ p1, const uint32_t* __restrict__ p2,
                                   const float* __restrict__ projo, const float* __restrict__ u,
@@ -557,13 +858,20 @@ __global__ void layer_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
   float* cond = t + d;        // [n]
   float* z = cond + n;        // [n]
   float* buf = z + n;         // [n]
-  float* tmp = buf + n;       // [n]
-  float* As = tmp + n;        // [ba*ba]
+  float* tmp = buf + n;       // [n + 4*bb]
+  float* As = tmp + n + 4 * G.bb;  // [ba*ba]
   float* Bs = As + G.ba * G.ba;  // [bb*bb]
   float* red = Bs + G.bb * G.bb; // [32]
   float* pr = red + 32;          // [8]
   float* gs = pr + 8;            // [24]
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  const bool k4 = (G.ba % 4) == 0 && (G.bb % 4) == 0 && (d % 2) == 0;
+  auto kron = [&](const float* a, const float* b) {
+    if (k4)
+      kron_apply_block4(z, a, b, G.ba, G.bb, tmp, As, Bs, buf);
+    else
+      kron_apply_block(z, a, b, G.ba, G.bb, tmp, As, Bs, buf);
+  };
   const float* po = projo + (size_t)r * d;
   const float* bx = bx_in + (size_t)r * d;
   if (tid < nl + nl * nl) gs[tid] = gates[(size_t)r * 24 + tid];
@@ -608,16 +916,16 @@ __global__ void layer_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
     z[c] = (c < d ? t[c] : 0.f) * lp.d1[c];
   }
   __syncthreads();
-  kron_apply_block(z, lp.w1a, lp.w1b, G.ba, G.bb, tmp, As, Bs, buf);
+  kron(lp.w1a, lp.w1b);
   for (int c = tid; c < n; c += blockDim.x) {
     float v = lp.d2[c] * cond[c] * buf[p1[c]] + lp.b2[c];
     z[c] = v * sigmoidf_(v);  // silu, ops.rs:118
   }
   __syncthreads();
-  kron_apply_block(z, lp.w2a, lp.w2b, G.ba, G.bb, tmp, As, Bs, buf);
+  kron(lp.w2a, lp.w2b);
   for (int c = tid; c < n; c += blockDim.x) z[c] = buf[p2[c]] * lp.d3[c];
   __syncthreads();
-  kron_apply_block(z, lp.w3a, lp.w3b, G.ba, G.bb, tmp, As, Bs, buf);
+  kron(lp.w3a, lp.w3b);
   // bx += mlp; y = bx - u; lanes' = hres . lanes + hpost * y
   float* lr = lanes + (size_t)r * nl * d;
   const float* ur = u + (size_t)r * d;
@@ -640,7 +948,8 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
                               cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   if (G.lanes > 4 || G.cond_rank > 8) return cudaErrorInvalidValue;
-  const size_t smem = (size_t)(2 * G.d + 4 * G.hada_n + G.ba * G.ba + G.bb * G.bb + 32 + 8 + 24) * sizeof(float);
+  const size_t smem =
+      (size_t)(2 * G.d + 4 * G.hada_n + 4 * G.bb + G.ba * G.ba + G.bb * G.bb + 32 + 8 + 24) * sizeof(float);
   cudaError_t e = allow_smem((const void*)layer_post_kernel, smem);
   if (e != cudaSuccess) return e;
   layer_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, p1, p2, projo, u, bx, gates, lanes);

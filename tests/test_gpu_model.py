@@ -110,6 +110,23 @@ def test_batched_sessions_match_single_sessions(full_gpu):
             toks = picks
 
 
+@pytest.mark.parametrize("int8", [False, True])
+def test_large_prefill_batch_matches_oracle(full_gpu, full_oracle, int8):
+    """A batched prefill of 700 rows takes the many-row kernels (the tiled mHC
+    pre-projection engages from 512 rows); every session's last logits and its
+    next decode step match the oracle."""
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(1, 8192, n).astype(np.uint32) for n in (300, 200, 150, 50)]
+    ss = [full_gpu.session(320, int8) for _ in prompts]
+    lg, picks = full_gpu.prefill_batch(ss, prompts)
+    for p, s, a, t in zip(prompts, ss, lg, picks):
+        o = full_oracle.session(320, int8)
+        b = o.prefill(p)
+        assert rel_err(a, b) < tol(int8)
+        assert int(t) == int(np.argmax(b))
+        assert rel_err(s.decode_step(int(t)), o.decode_step(int(t))) < tol(int8)
+
+
 def test_device_batch_graph_matches_eager(full_gpu, cuda):
     """The CUDA-graph replay of a batched decode step gives the same tokens and
     logits as the eager launch sequence (and both match single sessions)."""
