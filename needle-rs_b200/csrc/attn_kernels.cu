@@ -276,17 +276,14 @@ __device__ __forceinline__ void split_range(int lo, int hi, int nsplit, int z, i
   *b = min(hi, lo + (z + 1) * spl - 1);
 }
 
-// Forward-pass attention: grid (rows, kv_heads, nsplit).
-template <bool INT8, int QK, int VH>
-__global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, RowBatch rb, int window,
-                                                                int nsplit, const float* __restrict__ qpost,
-                                                                const void* pk, const void* pv,
-                                                                const float* pks, const float* pvs,
-                                                                float* __restrict__ part) {
-  extern __shared__ __align__(16) unsigned char smraw[];
-  auto& S = *reinterpret_cast<AttnSmem<INT8, QK, VH>*>(smraw);
-  const int r = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
-  const int rep = G.heads / G.kvh;
+// Keys/values of row r for the forward pass: the prefill scratch ([row][kv
+// head][dim], linear from the session's first row) or the session's head-major
+// ring. Sets the first visible position lo (local window, ring floor) and the
+// row's position p.
+template <int QK, int VH>
+__device__ __forceinline__ AttnSrc layer_src(const Geo& G, int li, const RowBatch& rb, int r, int window,
+                                             const void* pk, const void* pv, const float* pks,
+                                             const float* pvs, int* lo_out, int* p_out) {
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos;
   int lo = (window > 0 && p + 1 > window) ? p + 1 - window : 0;
@@ -321,11 +318,346 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
     const int floor = p + 1 > kv.slots ? p + 1 - kv.slots : 0;  // cache.rs:322-331
     lo = max(lo, floor);
   }
+  *lo_out = lo;
+  *p_out = p;
+  return src;
+}
+
+// Forward-pass attention: grid (rows, kv_heads, nsplit).
+template <bool INT8, int QK, int VH>
+__global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, RowBatch rb, int window,
+                                                                int nsplit, const float* __restrict__ qpost,
+                                                                const void* pk, const void* pv,
+                                                                const float* pks, const float* pvs,
+                                                                float* __restrict__ part) {
+  extern __shared__ __align__(16) unsigned char smraw[];
+  auto& S = *reinterpret_cast<AttnSmem<INT8, QK, VH>*>(smraw);
+  const int r = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
+  const int rep = G.heads / G.kvh;
+  int lo, p;
+  const AttnSrc src = layer_src<QK, VH>(G, li, rb, r, window, pk, pv, pks, pvs, &lo, &p);
   int a, b;
   split_range(lo, p, nsplit, z, &a, &b);
   const int pw = rep * (VH + 2);
   attend_part<INT8, QK, VH>(S, qpost + (size_t)r * G.q_dim + (size_t)kh * rep * QK, rep, src, kh, a, b,
                             1.0f / sqrtf((float)QK), part + (((size_t)r * G.kvh + kh) * nsplit + z) * pw);
+}
+
+// ----------------------------------------------------------------------------
+// int8 KV on the tensor cores.
+//
+// In int8 mode the query is fake-quantised (model.rs:289-293): q = code * qs
+// with integer codes, so q.k = qs * sum(code * k8) and the key dot is an exact
+// integer product, run as mma.sync s8 x s8 -> s32 (m16n8k32 / m16n8k16) with
+// the query heads of one KV head as the 16 rows (rows >= rep are zero) and
+// positions as columns. The score is then (dot * qs) * ks * scale, as the
+// reference's f32 dot times the key scale (attention.rs:191-216) up to f32
+// rounding of the query product.
+//
+// P.V runs as m16n8k16 f16 MMAs with f32 accumulation: int8 values are exact
+// in f16, and each weight p * vs is split into an f16 high part and an f16
+// remainder (two MMAs), which keeps about 22 bits of the weight. The score
+// fragment layout of the first MMA is the A-fragment layout of the second, so
+// the weights never leave registers. Values are widened to f16 in shared
+// memory (bias trick: byte ^ 0x80 placed under exponent byte 0x64 is 1024 +
+// u in f16; subtracting 1152 gives the signed value) and fed by ldmatrix.trans.
+//
+// Each of the four warps of a CTA owns every fourth 32-position block of the
+// CTA's range with its own cp.async double buffer and its own online softmax,
+// so the main loop has no block-wide barrier; the warps merge at the end and
+// the CTA writes the same (max, sum, P.V) partial as the f32 kernel.
+// ----------------------------------------------------------------------------
+constexpr int WB = 32;  // positions per warp block
+
+template <int QK, int VH>
+struct MmaTile {
+  // Key row stride in shared memory: conflict-free 32-bit fragment loads.
+  static constexpr int KS = QK == 16 ? 16 : (QK % 32 == 0 ? QK + 16 : QK);
+  static constexpr int KP = QK / 16;   // 16-byte pieces per key row
+  static constexpr int VP = VH / 16;   // 16-byte pieces per value row
+  static constexpr int VHS = VH + 8;   // f16 value row stride (halves): conflict-free ldmatrix
+  static constexpr int NT = VH / 8;    // P.V n-tiles
+  static constexpr int NK32 = QK / 32; // m16n8k32 steps of the key dot
+  static constexpr bool K16 = (QK % 32) != 0;
+};
+
+template <int QK, int VH>
+struct __align__(16) MmaWarpSmem {
+  using T = MmaTile<QK, VH>;
+  int8_t k[2][WB * T::KS];
+  int8_t v[2][WB * VH];
+  float ks[2][WB];
+  float vs[2][WB];
+  __half vh[WB * T::VHS];
+};
+
+__device__ __forceinline__ void mma_s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ void mma_f16_k16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+
+// Four signed bytes -> two f16 pairs (exact).
+__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t* lo, uint32_t* hi) {
+  const uint32_t u = w ^ 0x80808080u;
+  const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
+  uint32_t a = __byte_perm(u, 0x64646464u, 0x5140), b = __byte_perm(u, 0x64646464u, 0x5342);
+  __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), bias);
+  __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), bias);
+  *lo = *reinterpret_cast<uint32_t*>(&ha);
+  *hi = *reinterpret_cast<uint32_t*>(&hb);
+}
+
+__device__ __forceinline__ uint32_t pack_h2(float x, float y) {
+  __half2 h = __floats2half2_rn(x, y);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// cp.async of one warp block [n0, n0 + WB) clipped at hi (zero-filled beyond).
+template <int QK, int VH>
+__device__ __forceinline__ void mma_issue(MmaWarpSmem<QK, VH>& W, int buf, const AttnSrc& src, int kh,
+                                          int n0, int hi, int lane) {
+  using T = MmaTile<QK, VH>;
+  const int8_t* kb = (const int8_t*)src.k;
+  const int8_t* vb = (const int8_t*)src.v;
+#pragma unroll
+  for (int j = lane; j < WB * T::KP; j += 32) {
+    const int i = j / T::KP, pc = j % T::KP, n = n0 + i;
+    const bool ok = n <= hi;
+    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    cp_async16(W.k[buf] + i * T::KS + pc * 16, kb + idx * src.k_row + kh * src.k_head + pc * 16, ok);
+  }
+#pragma unroll
+  for (int j = lane; j < WB * T::VP; j += 32) {
+    const int i = j / T::VP, pc = j % T::VP, n = n0 + i;
+    const bool ok = n <= hi;
+    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    cp_async16(W.v[buf] + i * VH + pc * 16, vb + idx * src.v_row + kh * src.v_head + pc * 16, ok);
+  }
+  {
+    const int n = n0 + lane;
+    const bool ok = n <= hi;
+    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    cp_async4(&W.ks[buf][lane], src.ks + idx * src.s_row + kh * src.s_head, ok);
+    cp_async4(&W.vs[buf][lane], src.vs + idx * src.s_row + kh * src.s_head, ok);
+  }
+}
+
+template <int QK, int VH>
+__global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, RowBatch rb, int window, int nsplit,
+                                                            const int8_t* __restrict__ q8,
+                                                            const float* __restrict__ q8s, const void* pk,
+                                                            const void* pv, const float* pks, const float* pvs,
+                                                            float* __restrict__ part) {
+  using T = MmaTile<QK, VH>;
+  using WS = MmaWarpSmem<QK, VH>;
+  extern __shared__ __align__(16) unsigned char smraw[];
+  const int r = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  const int g = lane >> 2, t = lane & 3;
+  WS& W = reinterpret_cast<WS*>(smraw)[wid];
+  const int rep = G.heads / G.kvh;
+  int lo, p;
+  const AttnSrc src = layer_src<QK, VH>(G, li, rb, r, window, pk, pv, pks, pvs, &lo, &p);
+  int a, b;
+  split_range(lo, p, nsplit, z, &a, &b);
+  const float scale = 1.0f / sqrtf((float)QK);
+
+  // Query codes of head g of this KV head as A fragments (rows >= rep zero).
+  const bool hv = g < rep;
+  const int8_t* qr = q8 + (size_t)r * G.q_dim + (size_t)(kh * rep + (hv ? g : 0)) * QK;
+  uint32_t qa[T::NK32 > 0 ? T::NK32 : 1][4];
+  uint32_t qa16 = 0;
+#pragma unroll
+  for (int s = 0; s < T::NK32; ++s) {
+    qa[s][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + s * 32 + t * 4)) : 0u;
+    qa[s][1] = 0u;
+    qa[s][2] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + s * 32 + 16 + t * 4)) : 0u;
+    qa[s][3] = 0u;
+  }
+  if (T::K16) qa16 = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + T::NK32 * 32 + t * 4)) : 0u;
+  const float qs = hv ? q8s[(size_t)r * G.heads + kh * rep + g] : 0.f;
+
+  float m = -INFINITY, l = 0.f;
+  float o[T::NT][4];
+#pragma unroll
+  for (int i = 0; i < T::NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+
+  const int nblk = a <= b ? (b - a) / WB + 1 : 0;
+  const int mine = nblk > wid ? (nblk - wid + 3) / 4 : 0;  // blocks wid, wid + 4, ...
+  if (mine > 0) {
+    mma_issue<QK, VH>(W, 0, src, kh, a + wid * WB, b, lane);
+    cp_commit();
+  }
+  for (int c = 0; c < mine; ++c) {
+    const int buf = c & 1;
+    const int n0 = a + (wid + 4 * c) * WB;
+    if (c + 1 < mine) {
+      mma_issue<QK, VH>(W, buf ^ 1, src, kh, n0 + 4 * WB, b, lane);
+      cp_commit();
+      cp_wait<1>();
+    } else {
+      cp_wait<0>();
+    }
+    __syncwarp();
+    // ---- values to f16 (each lane widens 16-byte pieces)
+#pragma unroll
+    for (int j = lane; j < WB * T::VP; j += 32) {
+      const int i = j / T::VP, c0 = (j % T::VP) * 16;
+      const uint4 w = *reinterpret_cast<const uint4*>(W.v[buf] + i * VH + c0);
+      uint4 h0, h1;
+      i8x4_to_h2x2(w.x, &h0.x, &h0.y);
+      i8x4_to_h2x2(w.y, &h0.z, &h0.w);
+      i8x4_to_h2x2(w.z, &h1.x, &h1.y);
+      i8x4_to_h2x2(w.w, &h1.z, &h1.w);
+      *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0) = h0;
+      *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0 + 8) = h1;
+    }
+    // ---- integer key dots: n-tile j covers positions j*8 .. j*8+7
+    float sc[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      int d[4] = {0, 0, 0, 0};
+      const int8_t* kr = W.k[buf] + (j * 8 + g) * T::KS;
+#pragma unroll
+      for (int s = 0; s < T::NK32; ++s)
+        mma_s8_k32(d, qa[s], *reinterpret_cast<const uint32_t*>(kr + s * 32 + t * 4),
+                   *reinterpret_cast<const uint32_t*>(kr + s * 32 + 16 + t * 4));
+      if (T::K16) mma_s8_k16(d, qa16, 0u, *reinterpret_cast<const uint32_t*>(kr + T::NK32 * 32 + t * 4));
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int i = j * 8 + t * 2 + e;
+        sc[j * 2 + e] = n0 + i <= b ? (float)d[e] * qs * W.ks[buf][i] * scale : -INFINITY;
+      }
+    }
+    // ---- online softmax of row g over this block (the four lanes of a row
+    // hold 8 positions each)
+    float mx = sc[0];
+#pragma unroll
+    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, sc[i]);
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(m, mx);
+    const float corr = m == -INFINITY ? 0.f : expf(m - mnew);
+    float pw[8], sum = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float pe = sc[i] == -INFINITY ? 0.f : expf(sc[i] - mnew);
+      sum += pe;
+      pw[i] = pe * W.vs[buf][(i >> 1) * 8 + t * 2 + (i & 1)];
+    }
+    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+    l = l * corr + sum;
+    m = mnew;
+#pragma unroll
+    for (int i = 0; i < T::NT; ++i) {
+      o[i][0] *= corr;
+      o[i][1] *= corr;
+    }
+    __syncwarp();  // f16 values visible to every lane
+    // ---- P.V: k-step kk covers positions kk*16 .. kk*16+15 (score n-tiles 2kk, 2kk+1)
+#pragma unroll
+    for (int kk = 0; kk < 2; ++kk) {
+      uint32_t ah[4], al[4];
+      const float x0 = pw[4 * kk], x1 = pw[4 * kk + 1], x2 = pw[4 * kk + 2], x3 = pw[4 * kk + 3];
+      ah[0] = pack_h2(x0, x1);
+      ah[2] = pack_h2(x2, x3);
+      ah[1] = ah[3] = 0u;
+      {
+        const __half2 h0 = *reinterpret_cast<const __half2*>(&ah[0]);
+        const __half2 h2 = *reinterpret_cast<const __half2*>(&ah[2]);
+        al[0] = pack_h2(x0 - __low2float(h0), x1 - __high2float(h0));
+        al[2] = pack_h2(x2 - __low2float(h2), x3 - __high2float(h2));
+        al[1] = al[3] = 0u;
+      }
+      const int mat = lane >> 3, row = lane & 7;
+#pragma unroll
+      for (int np = 0; np < T::NT / 2; ++np) {
+        uint32_t bf[4];
+        ldsm_x4_trans(bf, W.vh + (kk * 16 + (mat & 1) * 8 + row) * T::VHS + np * 16 + (mat >> 1) * 8);
+        mma_f16_k16(o[2 * np], ah, bf[0], bf[1]);
+        mma_f16_k16(o[2 * np], al, bf[0], bf[1]);
+        mma_f16_k16(o[2 * np + 1], ah, bf[2], bf[3]);
+        mma_f16_k16(o[2 * np + 1], al, bf[2], bf[3]);
+      }
+    }
+    __syncwarp();  // before the next block overwrites the f16 values
+  }
+
+  // ---- merge the four warps (shared memory reused) and write the partial
+  __syncthreads();
+  float* Wm = reinterpret_cast<float*>(smraw);  // [4][8]
+  float* Wl = Wm + 32;                           // [4][8]
+  float* Wo = Wl + 32;                           // [4][8][VH]
+  if (hv) {
+    if (t == 0) {
+      Wm[wid * 8 + g] = m;
+      Wl[wid * 8 + g] = l;
+    }
+#pragma unroll
+    for (int i = 0; i < T::NT; ++i) {
+      Wo[(wid * 8 + g) * VH + i * 8 + t * 2] = o[i][0];
+      Wo[(wid * 8 + g) * VH + i * 8 + t * 2 + 1] = o[i][1];
+    }
+  }
+  __syncthreads();
+  const int pwid = rep * (VH + 2);
+  float* out = part + (((size_t)r * G.kvh + kh) * nsplit + z) * pwid;
+  for (int i = threadIdx.x; i < rep * (VH + 2); i += blockDim.x) {
+    const int h = i < 2 * rep ? i % rep : (i - 2 * rep) / VH;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, Wm[w * 8 + h]);
+    float acc = 0.f;
+    if (i < rep) {
+      acc = M;
+    } else if (M != -INFINITY) {
+#pragma unroll
+      for (int w = 0; w < 4; ++w) {
+        const float mw = Wm[w * 8 + h];
+        if (mw == -INFINITY) continue;
+        const float f = expf(mw - M);
+        acc += f * (i < 2 * rep ? Wl[w * 8 + h] : Wo[(w * 8 + h) * VH + (i - 2 * rep) % VH]);
+      }
+    }
+    out[i] = acc;
+  }
+}
+
+template <int QK, int VH>
+static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
+                                        const int8_t* q8, const float* q8s, const void* pk, const void* pv,
+                                        const float* pks, const float* pvs, float* part, cudaStream_t st) {
+  using WS = MmaWarpSmem<QK, VH>;
+  const size_t smem = std::max(4 * sizeof(WS), (size_t)(64 + 4 * 8 * VH) * sizeof(float));
+  auto k = layer_attn_i8_kernel<QK, VH>;
+  cudaError_t e = allow_smem((const void*)k, smem);
+  if (e != cudaSuccess) return e;
+  dim3 grid(rb.M, G.kvh, nsplit);
+  k<<<grid, 128, smem, st>>>(G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part);
+  return cudaGetLastError();
 }
 
 int attn_nsplit(int rows, int kvh, int max_span) {
@@ -354,11 +686,34 @@ static cudaError_t launch_layer_attn_t(const Geo& G, int li, const RowBatch& rb,
 }
 
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
-                             const float* qpost, const void* pk, const void* pv, const float* pks,
-                             const float* pvs, float* part, cudaStream_t st, int int8) {
+                             const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
+                             const void* pv, const float* pks, const float* pvs, float* part,
+                             cudaStream_t st, int int8) {
   if (rb.M <= 0) return cudaSuccess;
   const int rep = G.heads / G.kvh;
   if (rep > AT_MAXREP || nsplit < 1) return cudaErrorInvalidValue;
+  if (int8) {
+    if (!q8 || !q8s) return cudaErrorInvalidValue;
+#define NB_ATI(Q, V) \
+  return launch_layer_attn_i8<Q, V>(G, li, rb, lp.window, nsplit, q8, q8s, pk, pv, pks, pvs, part, st)
+    if (G.vh == 64) {
+      switch (G.qk) {
+        case 16: NB_ATI(16, 64);
+        case 32: NB_ATI(32, 64);
+        case 48: NB_ATI(48, 64);
+        case 64: NB_ATI(64, 64);
+      }
+    } else if (G.vh == 32) {
+      switch (G.qk) {
+        case 16: NB_ATI(16, 32);
+        case 32: NB_ATI(32, 32);
+        case 48: NB_ATI(48, 32);
+        case 64: NB_ATI(64, 32);
+      }
+    }
+#undef NB_ATI
+    return cudaErrorInvalidValue;
+  }
 #define NB_ATT(I8, Q, V) \
   return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, st)
   const int key = G.qk * 2 + (int8 ? 1 : 0);

@@ -602,7 +602,7 @@ bool needle_v3_geometry(NeedleV3Handle* h, int64_t* out) {
 int needle_v3_device(NeedleV3Handle* h) { return h ? h->eng->device : -1; }
 
 // Copies one engine workspace buffer (the last forward's intermediates) to the
-// host, for debugging and tests: 0 xh, 1 proj, 2 qpost, 3 attn, 4 oh, 5 projo,
+// host, for debugging and tests: 0 xh, 1 proj, 2 qpost, 3 int8 query scales, 4 oh, 5 projo,
 // 6 prefill keys (f32), 7 prefill values (f32), 8 lanes, 9 u, 10 bx, 11 lm_in.
 bool needle_v3_debug_buffer(NeedleV3Handle* h, int which, float* out, size_t count) {
   clear_err();
@@ -611,7 +611,7 @@ bool needle_v3_debug_buffer(NeedleV3Handle* h, int which, float* out, size_t cou
     return false;
   }
   nb::Workspace& w = h->eng->ws;
-  const void* src[] = {w.xh, w.proj, w.qpost, w.attn, w.oh, w.projo, w.pk, w.pv, w.lanes, w.u, w.bx, w.lm_in};
+  const void* src[] = {w.xh, w.proj, w.qpost, w.q8s, w.oh, w.projo, w.pk, w.pv, w.lanes, w.u, w.bx, w.lm_in};
   if (which < 0 || which >= (int)(sizeof(src) / sizeof(src[0])) || !src[which]) {
     set_err("no such buffer");
     return false;

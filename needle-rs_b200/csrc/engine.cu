@@ -57,7 +57,7 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
-  void* ps[] = {lanes, u, bx, xh, proj, qpost, attn, oh, projo, gates, fetched, ekv, evc, lm_in,
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, oh, projo, gates, fetched, ekv, evc, lm_in,
                 pks, pvs, pk, pv, rows, tokens, next, last_rows};
   for (void* p : ps)
     if (p) cudaFree(p);
@@ -81,7 +81,8 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
       {(void**)&ws.lanes, cap * G.lanes * d * 4},   {(void**)&ws.u, cap * d * 4},
       {(void**)&ws.bx, cap * d * 4},                {(void**)&ws.xh, cap * dpad * 4},
       {(void**)&ws.proj, cap * G.proj_dim * 4},     {(void**)&ws.qpost, cap * G.q_dim * 4},
-      {(void**)&ws.attn, cap * G.o_dim * 4},        {(void**)&ws.oh, cap * opad * 4},
+      {(void**)&ws.q8s, cap * G.heads * 4},         {(void**)&ws.q8, cap * G.q_dim},
+      {(void**)&ws.oh, cap * opad * 4},
       {(void**)&ws.projo, cap * d * 4},             {(void**)&ws.gates, cap * 24 * 4},
       {(void**)&ws.fetched, cap * S * d * 4},       {(void**)&ws.ekv, cap * S * 2 * d * 4},
       {(void**)&ws.evc, cap * S * d * 4},           {(void**)&ws.lm_in, cap * dpad * 4},
@@ -785,9 +786,11 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_MARK(PK_LAYER_PRE, 1);
     NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st));
     NB_MARK(PK_QKVG, 1);
-    NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, st));
+    NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs,
+                           int8 ? ws.q8 : nullptr, int8 ? ws.q8s : nullptr, st));
     NB_MARK(PK_QKV_POST, 1);
-    NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs, ws.part, st, int8 ? 1 : 0));
+    NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, ws.qpost, ws.q8, ws.q8s, ws.pk, ws.pv, ws.pks, ws.pvs,
+                            ws.part, st, int8 ? 1 : 0));
     NB_MARK(PK_ATTN, 1);
     NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
     NB_MARK(PK_ATTN_FINISH, 1);

@@ -60,10 +60,11 @@ struct Workspace {
   size_t cap = 0;  // rows
   size_t last_cap = 0;
   float *lanes = nullptr, *u = nullptr, *bx = nullptr, *xh = nullptr, *proj = nullptr,
-        *qpost = nullptr, *attn = nullptr, *oh = nullptr, *projo = nullptr, *gates = nullptr,
+        *qpost = nullptr, *q8s = nullptr, *oh = nullptr, *projo = nullptr, *gates = nullptr,
         *fetched = nullptr, *ekv = nullptr, *evc = nullptr, *lm_in = nullptr, *pks = nullptr,
         *pvs = nullptr, *logits = nullptr, *lm_last = nullptr;
   void *pk = nullptr, *pv = nullptr;
+  int8_t* q8 = nullptr;  // int8 mode: query codes [rows][heads][qk], scales in q8s [rows][heads]
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;
   int* last_rows = nullptr;

@@ -55,16 +55,22 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
                              const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                              const float* evc, float* u, float* bx, float* xh, float* gates,
                              cudaStream_t st);
+// In int8 mode q8out / q8s (when non-null) receive the query's int8 codes
+// [M][heads][qk] and per-head scales [M][heads].
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                             const float* rope_cs, const float* proj, float* qpost, void* pk,
-                            void* pv, float* pks, float* pvs, cudaStream_t st);
+                            void* pv, float* pks, float* pvs, int8_t* q8out, float* q8s,
+                            cudaStream_t st);
 // Attention writes per-(row, KV head, split) partials; attn_finish merges the
 // splits, applies the output gate and rotates for out_proj.
 int attn_nsplit(int rows, int kvh, int max_span);
 size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit);
+// int8 = 1 runs the tensor-core kernel on the query codes q8 / q8s;
+// int8 = 0 the f32 kernel on qpost.
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
-                             const float* qpost, const void* pk, const void* pv, const float* pks,
-                             const float* pvs, float* part, cudaStream_t st, int int8);
+                             const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
+                             const void* pv, const float* pks, const float* pvs, float* part,
+                             cudaStream_t st, int int8);
 cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
                                const float* proj, float* oh, cudaStream_t st);
 cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,

@@ -616,7 +616,7 @@ __device__ __forceinline__ float q8(float x, float inv) {
 __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
                                 const float* __restrict__ rope_cs, const float* __restrict__ proj,
                                 float* __restrict__ qpost, void* pk, void* pv, float* pks,
-                                float* pvs) {
+                                float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x;
   const RowInfo ri = rb.rows[r];
@@ -680,9 +680,17 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
       }
       if (isq) {
         if (int8) {
+          // The codes and scale also go to q8out / q8s for the integer score
+          // path of the int8 attention; code * scale is the fake-quantised query.
           float inv, scale = quant_scale_warp(x1, x2, &inv);
-          x1 = q8(x1, inv) * scale;
-          x2 = q8(x2, inv) * scale;
+          const float c1 = q8(x1, inv), c2 = q8(x2, inv);
+          if (q8out && lane < half) {
+            q8out[(size_t)r * qd + h * G.qk + lane] = (int8_t)c1;
+            q8out[(size_t)r * qd + h * G.qk + half + lane] = (int8_t)c2;
+          }
+          if (q8out && lane == 0) q8s[(size_t)r * G.heads + h] = scale;
+          x1 = c1 * scale;
+          x2 = c2 * scale;
         }
         if (lane < half) {
           qpost[(size_t)r * qd + h * G.qk + lane] = x1;
@@ -762,11 +770,11 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
 
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                             const float* rope_cs, const float* proj, float* qpost, void* pk,
-                            void* pv, float* pks, float* pvs, cudaStream_t st) {
+                            void* pv, float* pks, float* pvs, int8_t* q8out, float* q8s, cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   if (G.qk > 64 || G.vh > 64 || (G.qk & 1) || (G.vh & 1)) return cudaErrorInvalidValue;
   const size_t smem = (size_t)G.qkv_dim * sizeof(float);
-  qkv_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs);
+  qkv_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
   return cudaGetLastError();
 }
 
