@@ -168,7 +168,9 @@ int needle_v3_device(NeedleV3Handle *handle);
  * reading one `.cact` CQ blob in place: `packed` = rows*in_pad*bits/8 bytes,
  * `norms` = rows*(in_pad/128) FP16 (cq.rs:181-238). `levels` = the 2^bits
  * codebook entries (host). xh is the rotated input (prepare_input, cq.rs:264),
- * [M][ldx] f32. path: 0 auto, 1 GEMV (M <= 8), 2 tiled GEMM. Replaces
+ * [M][ldx] f32. path: 0 auto, 1 GEMV (M <= 8), 2 tiled SIMT GEMM, 3 tensor-core
+ * GEMM (tcgen05; chosen by path 0 for M > 8; uses stream-ordered scratch of
+ * 4*M*(in_pad + 1) bytes). Replaces
  * CqWeight::matvec_rows_prepared / matmul_rows_prepared (cq.rs:301, :446). */
 int nd_cq_project(const void *packed, const void *norms, int rows, int in_feat, int bits,
                   const float *levels, const float *xh, int ldx, int M, float *y, int ldy,

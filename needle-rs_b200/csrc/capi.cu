@@ -580,7 +580,13 @@ bool needle_v3_batch_get_next(NeedleV3Batch* b, uint32_t* next) {
     set_err("batch or next was null");
     return false;
   }
+  cudaSetDevice(b->eng->device);
   cudaDeviceSynchronize();
+  int flag = 0;
+  if (nb::umma_take_error(&flag) == cudaSuccess && flag) {
+    set_err("a tensor-core projection of an earlier step gave up a bounded wait; its results are invalid");
+    return false;
+  }
   return batch_copy(b, next, b->b->d_next, cudaMemcpyDeviceToHost);
 }
 
@@ -632,7 +638,22 @@ int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, 
   if (!packed || !norms || !levels || !xh || !y || rows <= 0 || in_feat <= 0 || (bits != 2 && bits != 4))
     return nd_status(cudaErrorInvalidValue);
   nb::CqMat W = make_cq(packed, norms, rows, in_feat, bits, levels);
-  return nd_status(nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, (cudaStream_t)stream, path));
+  cudaStream_t st = (cudaStream_t)stream;
+  const bool tensor_cores = path == 3 || (path == 0 && M > 8 && nb::umma_supported(W));
+  if (!tensor_cores || M <= 0) return nd_status(nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, st, path));
+  // The split activations live in stream-ordered scratch, released on `stream`.
+  nb::GemmScratch gs;
+  gs.elems = (size_t)M * W.in_pad;
+  void* mem = nullptr;
+  cudaError_t e = cudaMallocAsync(&mem, gs.elems * 2 * sizeof(__half) + (size_t)M * sizeof(float), st);
+  if (e != cudaSuccess) return nd_status(e);
+  gs.hi = (__half*)mem;
+  gs.lo = gs.hi + gs.elems;
+  gs.inv = reinterpret_cast<float*>(gs.lo + gs.elems);
+  gs.rows = (size_t)M;
+  e = nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, st, path, &gs);
+  cudaError_t f = cudaFreeAsync(mem, st);
+  return nd_status(e != cudaSuccess ? e : f);
 }
 
 int nd_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out, void* stream) {

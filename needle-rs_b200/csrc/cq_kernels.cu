@@ -336,10 +336,19 @@ cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int
 }
 
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                       int nrows, cudaStream_t st, int force_path) {
+                       int nrows, cudaStream_t st, int force_path, const GemmScratch* gs) {
   if (M <= 0 || nrows <= 0) return cudaSuccess;
   if (!cq_args_ok(W, xh, ldx) || row0 < 0 || row0 + nrows > W.rows) return cudaErrorInvalidValue;
   if (force_path == 1 && M > 8) return cudaErrorInvalidValue;
+  if (force_path < 0 || force_path > 3) return cudaErrorInvalidValue;
+  const bool scratch_ok = gs && gs->hi && gs->lo && gs->inv && gs->elems >= (size_t)M * W.in_pad &&
+                          gs->rows >= (size_t)M;
+  if (force_path == 3) {
+    if (!scratch_ok) return cudaErrorInvalidValue;
+    return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs);
+  }
+  if (force_path == 0 && M > 8 && scratch_ok && umma_supported(W))
+    return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs);
   if (force_path == 2)
     return W.bits == 2 ? launch_gemm_simt<2>(W, xh, ldx, M, y, ldy, row0, nrows, st)
                        : launch_gemm_simt<4>(W, xh, ldx, M, y, ldy, row0, nrows, st);

@@ -57,7 +57,7 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
-  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, oh, projo, gates, fetched, ekv, evc, lm_in,
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, oh, projo, gates, fetched, ekv, evc, lm_in,
                 pks, pvs, pk, pv, rows, tokens, next, last_rows};
   for (void* p : ps)
     if (p) cudaFree(p);
@@ -74,6 +74,7 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
   ws.release();
   const size_t d = G.d, dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   const size_t S = std::max(1, G.n_sites);
+  const size_t kmax = std::max(dpad, opad);  // widest input of a projection
   struct A {
     void** p;
     size_t bytes;
@@ -82,6 +83,8 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
       {(void**)&ws.bx, cap * d * 4},                {(void**)&ws.xh, cap * dpad * 4},
       {(void**)&ws.proj, cap * G.proj_dim * 4},     {(void**)&ws.qpost, cap * G.q_dim * 4},
       {(void**)&ws.q8s, cap * G.heads * 4},         {(void**)&ws.q8, cap * G.q_dim},
+      {(void**)&ws.ahi, cap * kmax * 2},            {(void**)&ws.alo, cap * kmax * 2},
+      {(void**)&ws.ainv, cap * 4},
       {(void**)&ws.oh, cap * opad * 4},
       {(void**)&ws.projo, cap * d * 4},             {(void**)&ws.gates, cap * 24 * 4},
       {(void**)&ws.fetched, cap * S * d * 4},       {(void**)&ws.ekv, cap * S * 2 * d * 4},
@@ -99,6 +102,11 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
       return false;
     }
   }
+  ws.gs.hi = ws.ahi;
+  ws.gs.lo = ws.alo;
+  ws.gs.inv = ws.ainv;
+  ws.gs.elems = cap * kmax;
+  ws.gs.rows = cap;
   ws.cap = cap;
   epoch++;
   return true;
@@ -376,6 +384,9 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
   // Device upload of the container.
   cudaError_t e = cudaGetDevice(&E->device);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking);
+  if (e == cudaSuccess) e = umma_error_ptr(&E->d_wait_flag);
+  if (e == cudaSuccess) e = cudaMallocHost(&E->h_wait_flag, sizeof(int));
+  if (e == cudaSuccess) *E->h_wait_flag = 0;
   if (e == cudaSuccess) e = cudaMalloc(&E->d_blob, len);
   if (e == cudaSuccess) e = cudaMemcpy(E->d_blob, raw, len, cudaMemcpyHostToDevice);
   if (e != cudaSuccess) {
@@ -590,7 +601,20 @@ Engine::~Engine() {
   if (d_perm) cudaFree(d_perm);
   if (d_rope) cudaFree(d_rope);
   if (d_tables) cudaFree(d_tables);
+  if (h_wait_flag) cudaFreeHost(h_wait_flag);
   if (stream) cudaStreamDestroy(stream);
+}
+
+cudaError_t Engine::queue_wait_flag(cudaStream_t st) {
+  return cudaMemcpyAsync(h_wait_flag, d_wait_flag, sizeof(int), cudaMemcpyDeviceToHost, st);
+}
+
+cudaError_t Engine::wait_status(cudaStream_t st) {
+  if (!*h_wait_flag) return cudaSuccess;
+  *h_wait_flag = 0;
+  cudaError_t e = cudaMemsetAsync(d_wait_flag, 0, sizeof(int), st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e == cudaSuccess ? cudaErrorTimeout : e;
 }
 
 // ------------------------------------------------------------------ sessions
@@ -774,7 +798,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_TRY(launch_engram_gather(G, d_tables, rb, ws.fetched, st));
     for (int s = 0; s < S; ++s)
       NB_TRY(cq_project(eng_kv[s], ws.fetched + (size_t)s * d, S * d, M, ws.ekv + (size_t)s * 2 * d,
-                        S * 2 * d, 0, 2 * d, st));
+                        S * 2 * d, 0, 2 * d, st, 0, &ws.gs));
     NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, ws.ekv, ws.evc, st));
     NB_MARK(PK_ENGRAM, S + 2);
   }
@@ -784,7 +808,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_TRY(launch_layer_pre(G, l, rb, ws.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
                             site_of[l], ws.ekv, ws.evc, ws.u, ws.bx, ws.xh, ws.gates, st));
     NB_MARK(PK_LAYER_PRE, 1);
-    NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st));
+    NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st, 0, &ws.gs));
     NB_MARK(PK_QKVG, 1);
     NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs,
                            int8 ? ws.q8 : nullptr, int8 ? ws.q8s : nullptr, st));
@@ -794,7 +818,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_MARK(PK_ATTN, 1);
     NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
     NB_MARK(PK_ATTN_FINISH, 1);
-    NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st));
+    NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st, 0, &ws.gs));
     NB_MARK(PK_OUT_PROJ, 1);
     NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, ws.projo, ws.u, ws.bx,
                              ws.gates, ws.lanes, st));
@@ -808,7 +832,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
 // Tied head over logit_rows (model.rs:358-374, :942-978) and the greedy pick.
 cudaError_t Engine::head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                          cudaStream_t st, Prof* prof) {
-  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st));
+  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &ws.gs));
   NB_MARK(PK_HEAD, 1);
   if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
   NB_MARK(PK_BOOK, picks ? 1 : 0);
@@ -896,7 +920,9 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
                           cudaMemcpyDeviceToHost, stream);
     if (e == cudaSuccess && picks)
       e = cudaMemcpyAsync(picks + i0, ws.next, (i1 - i0) * 4, cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = queue_wait_flag(stream);
     if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e == cudaSuccess) e = wait_status(stream);
     if (e != cudaSuccess) {
       *err = cuda_msg("prefill", e);
       return false;
@@ -948,7 +974,9 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   if (e == cudaSuccess && logits)
     e = cudaMemcpyAsync(logits, ws.logits, n * G.logit_rows * 4, cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess && picks) e = cudaMemcpyAsync(picks, ws.next, n * 4, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess) e = queue_wait_flag(stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess) e = wait_status(stream);
   if (e != cudaSuccess) {
     *err = cuda_msg("decode step", e);
     return false;

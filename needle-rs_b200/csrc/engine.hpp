@@ -65,6 +65,9 @@ struct Workspace {
         *pvs = nullptr, *logits = nullptr, *lm_last = nullptr;
   void *pk = nullptr, *pv = nullptr;
   int8_t* q8 = nullptr;  // int8 mode: query codes [rows][heads][qk], scales in q8s [rows][heads]
+  __half *ahi = nullptr, *alo = nullptr;  // tensor-core projections: split activations
+  float* ainv = nullptr;                  // and their inverse row scales
+  GemmScratch gs;
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;
   int* last_rows = nullptr;
@@ -150,6 +153,13 @@ class Engine {
   const float* final_norm = nullptr;
   Workspace ws;
   uint64_t epoch = 1;  // bumped whenever a session's device layout changes
+  int* d_wait_flag = nullptr;  // tensor-core GEMM: a bounded wait expired (device flag)
+  int* h_wait_flag = nullptr;  // pinned host copy, refreshed before each synchronous return
+
+  // Queues the copy of the device wait flag on `st`; after the stream is
+  // synchronised, wait_status() turns a raised flag into an error and clears it.
+  cudaError_t queue_wait_flag(cudaStream_t st);
+  cudaError_t wait_status(cudaStream_t st);
 
   bool ensure_ws(size_t rows, std::string* err);
   bool ensure_part(size_t rows, int nsplit, std::string* err);

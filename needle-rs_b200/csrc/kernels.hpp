@@ -1,5 +1,6 @@
 // Host-side launch interface of the Needle-3 B200 kernels.
 #pragma once
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
 #include "common.cuh"
@@ -38,8 +39,29 @@ struct RowBatch {
   int mode;
 };
 
+// Scratch of the tensor-core path: the activations split into f16 high parts
+// and remainders, `elems` (>= M * in_pad) halves each, 16-byte aligned, and
+// `rows` (>= M) inverse row scales.
+struct GemmScratch {
+  __half* hi = nullptr;
+  __half* lo = nullptr;
+  float* inv = nullptr;
+  size_t elems = 0;
+  size_t rows = 0;
+};
+
+// force_path: 0 automatic (GEMV for M <= 8, else the tensor cores when `gs`
+// holds enough scratch, else the SIMT GEMM), 1 GEMV, 2 SIMT GEMM, 3 tensor cores.
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                       int nrows, cudaStream_t st, int force_path = 0);
+                       int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr);
+bool umma_supported(const CqMat& W);
+cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
+                            int nrows, cudaStream_t st, const GemmScratch& gs);
+// Reads and clears the device flag raised when a bounded wait of the
+// tensor-core GEMM expired (*flag != 0).
+cudaError_t umma_take_error(int* flag);
+// Device address of that flag on the current device.
+cudaError_t umma_error_ptr(int** p);
 
 cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out,
                               cudaStream_t st);

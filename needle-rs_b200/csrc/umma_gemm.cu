@@ -1,0 +1,500 @@
+// Codebook-quantized projection on the 5th-generation tensor cores (tcgen05).
+//
+// y[m][o] = sum_g norm[o,g] * sum_{k in g} level[idx[o,k]] * xh[m,k]   (cq.rs:632-679)
+//
+// for many activation rows. The tensor cores multiply f16 operands into f32
+// accumulators held in tensor memory (TMEM). To keep f32 accuracy both
+// operands are split into an f16 high part and an f16 remainder,
+// x = x_hi + x_lo and level = l_hi + l_lo, and per 128-element group
+//     main = sum x_hi * l_hi        corr = sum (x_hi * l_lo + x_lo * l_hi)
+// accumulate in two TMEM accumulators (f16 products are exact; the dropped
+// x_lo * l_lo term and the remainders' rounding leave ~2^-22 per product).
+// The tensor cores' f32 accumulation truncates toward zero, so the
+// accumulators only ever span one group: after each group the epilogue warps
+// read them and add norm * (main + corr) into f32 registers with
+// round-to-nearest, the same norm-times-group-dot structure as the reference.
+// Activation rows and the level table are scaled by powers of two that keep
+// every f16 remainder in the normal range; the epilogue undoes them exactly.
+//
+// One CTA computes 128 activation rows x 128 weight rows with 14 warps:
+//   * warp 12 loads [128 rows x 64 k] tiles of the split activations (made by
+//     split_f16_kernel) with TMA and 128-byte swizzle into a 3-stage ring, and
+//     owns the TMEM allocation;
+//   * warps 0-3 read the packed `.cact` codes straight from the container (one
+//     weight row per thread) and decode them into level hi / lo tiles in the
+//     same swizzled K-major layout;
+//   * warp 13 (one thread) issues tcgen05.mma kind::f16 M=128 N=128 K=16, three
+//     per K step, into the group's accumulator pair; groups alternate between
+//     two pairs so one is drained while the other fills;
+//   * warps 4-11 drain the accumulators (warp w reads TMEM lanes 32*(w%4)..,
+//     columns of half (w-4)/4) and store y.
+// Every wait on an mbarrier is bounded in time; on expiry the CTA raises a
+// device error flag, stops, waits (bounded) for its issued copies and MMAs,
+// frees its TMEM and returns, and the host reports the flag.
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.hpp"
+#include "launch_util.hpp"
+
+namespace nb {
+
+__device__ int g_umma_error;  // nonzero once a bounded wait in the tensor-core GEMM gave up
+
+namespace {
+
+constexpr int UM = 128;          // activation rows per CTA (MMA M)
+constexpr int UN = 128;          // weight rows per CTA (MMA N)
+constexpr int UK = 64;           // K per stage: 64 f16 = one 128-byte swizzle row
+constexpr int USTAGES = 3;
+constexpr int UGMAX = 32;        // groups of 128 supported (in_pad <= 4096)
+constexpr int UTHREADS = 448;    // warps 0-3 weights, 4-11 epilogue, 12 TMA + TMEM, 13 MMA
+constexpr uint32_t TILE = 128 * 128;        // bytes of one [128 rows][128 B] tile
+constexpr uint32_t STAGE_BYTES = 4 * TILE;  // A hi, A lo, B hi, B lo
+constexpr uint32_t NSM_BYTES = UGMAX * UN * 4;  // norm * level scale, [group][weight row]
+constexpr size_t UMMA_SMEM = 1024 + USTAGES * STAGE_BYTES + NSM_BYTES + 64 + 256;
+constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every wait: one second
+
+__device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ unsigned long long now_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(su32(bar)), "r"(count));
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(su32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(su32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(su32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar`. Gives up after WAIT_NS or as soon as
+// another role of the CTA gave up (`abort`), returning false.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
+  if (mbar_try(bar, parity)) return true;
+  const unsigned long long t0 = now_ns();
+  while (true) {
+    if (mbar_try(bar, parity)) return true;
+    if (*abort) return false;
+    if (now_ns() - t0 > WAIT_NS) {
+      *abort = 1;
+      atomicExch(&g_umma_error, 1);
+      return false;
+    }
+  }
+}
+
+// Drain wait used on the abort path: ignores the abort flag, bounded in time.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
+  const unsigned long long t0 = now_ns();
+  while (!mbar_try(bar, parity) && now_ns() - t0 <= WAIT_NS) {
+  }
+}
+
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, uint64_t* bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];" ::"r"(
+          su32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(su32(bar)), "r"(x), "r"(y)
+      : "memory");
+}
+
+// K-major operand tile, 128-byte swizzle: rows of 128 B, 8-row atoms 1024 B
+// apart (stride byte offset), start address in 16-byte units.
+__device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
+  const uint64_t start = (su32(tile) & 0x3FFFF) >> 4;
+  return start | (uint64_t)(1024 >> 4) << 32 | (uint64_t)1 << 46 | (uint64_t)2 << 61;
+}
+
+// kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both K-major.
+constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(UN >> 3) << 17) | ((uint32_t)(UM >> 4) << 24);
+
+__device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accum));
+}
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+        "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// f32 -> (f16 high part, f16 remainder), packed as lo16 = hi, hi16 = remainder.
+__device__ __forceinline__ uint32_t split_h(float x) {
+  const __half h = __float2half_rn(x);
+  const __half l = __float2half_rn(x - __half2float(h));
+  return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
+}
+
+// Power of two that brings max|v| into [2^13, 2^14) (1 for an all-zero row).
+__device__ __forceinline__ int row_exp(float amax) {
+  if (!(amax > 0.f) || !isfinite(amax)) return 0;
+  int e;
+  frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
+  return 14 - e;
+}
+
+// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile.
+__device__ __forceinline__ uint32_t sw_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
+
+template <int BITS>
+__global__ void __launch_bounds__(UTHREADS, 1)
+cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
+               const float* __restrict__ ainv, int M, float* __restrict__ y, int ldy, int row0, int nrows) {
+  extern __shared__ unsigned char smraw[];
+  unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
+  float* nsm = reinterpret_cast<float*>(sm + USTAGES * STAGE_BYTES);
+  uint32_t* ltab = reinterpret_cast<uint32_t*>(sm + USTAGES * STAGE_BYTES + NSM_BYTES);  // [16] level hi|lo
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + USTAGES * STAGE_BYTES + NSM_BYTES + 64);  // weights written
+  uint64_t* afull = full + USTAGES;   // activation tiles landed (TMA transaction bytes)
+  uint64_t* empty = afull + USTAGES;  // stage consumed by the MMAs
+  uint64_t* tfull = empty + USTAGES;  // [2] a group's accumulator pair is complete
+  uint64_t* tempty = tfull + 2;       // [2] the pair has been drained
+  uint64_t* drainb = tempty + 2;      // every MMA of the CTA has completed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drainb + 1);
+  volatile uint32_t* abort = tmem_slot + 1;
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int n0 = blockIdx.x * UN, m0 = blockIdx.y * UM;
+  const int nk = W.in_pad / UK, ng = W.in_pad / 128;
+
+  // Level scale: a power of two putting max|level| in [2^13, 2^14).
+  float lmax = 0.f;
+#pragma unroll
+  for (int i = 0; i < (1 << BITS); ++i) lmax = fmaxf(lmax, fabsf(W.levels[i]));
+  const int le = row_exp(lmax);
+
+  if (tid == 0) {
+    for (int s = 0; s < USTAGES; ++s) {
+      mbar_init(&full[s], 4);   // the four weight warps
+      mbar_init(&afull[s], 1);  // the TMA thread's expect_tx arrive
+      mbar_init(&empty[s], 1);  // one tcgen05.commit
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&tfull[b], 1);   // one tcgen05.commit
+      mbar_init(&tempty[b], 8);  // the eight epilogue warps
+    }
+    mbar_init(drainb, 1);
+    *abort = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  }
+  if (tid < 16) ltab[tid] = split_h(ldexpf(W.levels[tid < (1 << BITS) ? tid : 0], le));
+  if (warp == 12) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
+                 "r"(512));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp < 4) {
+    // ------------------------------------------------ weight producer
+    const int nl = tid;  // weight row of this thread within the tile
+    const int n = n0 + nl;
+    const bool valid = n < nrows;
+    const uint8_t* row = nullptr;
+    const __half* nrm = nullptr;
+    if (valid) cq_row_ptr(W, row0 + n, &row, &nrm);
+    const float linv = ldexpf(1.f, -le);
+    for (int g = 0; g < ng; ++g) nsm[g * UN + nl] = valid ? __half2float(nrm[g]) * linv : 0.f;
+    asm volatile("bar.sync 1, 384;" ::: "memory");  // norms visible to the epilogue warps
+    uint32_t t0 = 0, t1 = 0, l0 = 0, l1 = 0;  // 2-bit tables: hi pairs, lo pairs
+    if (BITS == 2) {
+      t0 = __byte_perm(ltab[0], ltab[1], 0x5410);
+      t1 = __byte_perm(ltab[2], ltab[3], 0x5410);
+      l0 = __byte_perm(ltab[0], ltab[1], 0x7632);
+      l1 = __byte_perm(ltab[2], ltab[3], 0x7632);
+    }
+    for (int kb = 0; kb < nk; ++kb) {
+      const int s = kb % USTAGES;
+      const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
+      uint4 c0 = make_uint4(0, 0, 0, 0), c1 = make_uint4(0, 0, 0, 0);
+      if (valid) {
+        const uint4* src = reinterpret_cast<const uint4*>(row + (size_t)kb * (UK * BITS / 8));
+        c0 = __ldg(src);
+        if (BITS == 4) c1 = __ldg(src + 1);
+      }
+      if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
+      unsigned char* bh = sm + s * STAGE_BYTES + 2 * TILE;
+      unsigned char* bl = bh + TILE;
+      const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
+#pragma unroll
+      for (int ch = 0; ch < 8; ++ch) {  // 8 chunks of 8 elements
+        uint32_t hv[4], lv[4];
+        if (BITS == 2) {
+          const uint32_t bits16 = (cw[ch >> 1] >> ((ch & 1) * 16)) & 0xFFFFu;
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            // Two 2-bit codes c0, c1 select bytes 2c..2c+1 of the 4-entry tables.
+            const uint32_t x = (bits16 >> (4 * p)) & 0xFu;
+            const uint32_t sel = (x & 3u) * 0x22u + (x & 0xCu) * 0x880u + 0x1010u;
+            hv[p] = __byte_perm(t0, t1, sel);
+            lv[p] = __byte_perm(l0, l1, sel);
+          }
+        } else {
+          const uint32_t w32 = cw[ch];
+#pragma unroll
+          for (int p = 0; p < 4; ++p) {
+            const uint32_t a = ltab[(w32 >> (8 * p)) & 0xFu];
+            const uint32_t b = ltab[(w32 >> (8 * p + 4)) & 0xFu];
+            hv[p] = __byte_perm(a, b, 0x5410);
+            lv[p] = __byte_perm(a, b, 0x7632);
+          }
+        }
+        const uint32_t off = sw_off(nl, ch);
+        *reinterpret_cast<uint4*>(bh + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
+        *reinterpret_cast<uint4*>(bl + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
+      }
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&full[s]);
+    }
+  } else if (warp < 12) {
+    // ------------------------------------------------ epilogue: drain each group
+    const int q = warp & 3, h = (warp - 4) >> 2;  // TMEM lane quarter, column half
+    asm volatile("bar.sync 1, 384;" ::: "memory");
+    float acc[64];
+#pragma unroll
+    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < ng; ++g) {
+      const int b = g & 1;
+      if (!mbar_wait(&tfull[b], (uint32_t)(g >> 1) & 1u, abort)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint32_t tm = tmem + ((uint32_t)(q * 32) << 16) + b * 256 + h * 64;
+      const float* ng_ = nsm + g * UN + h * 64;
+#pragma unroll
+      for (int cb = 0; cb < 4; ++cb) {
+        uint32_t r[16], c[16];
+        tmem_ld16(tm + cb * 16, r);
+        tmem_ld16(tm + 128 + cb * 16, c);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          acc[cb * 16 + i] += ng_[cb * 16 + i] * (__uint_as_float(r[i]) + __uint_as_float(c[i]));
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+    }
+    const int m = m0 + q * 32 + lane;
+    if (ok && m < M) {
+      const float ai = ainv[m];
+      float* yr = y + (size_t)m * ldy + n0 + h * 64;
+      const int lim = nrows - (n0 + h * 64);
+      const bool vec = lim >= 64 && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
+      if (vec) {
+#pragma unroll
+        for (int i = 0; i < 64; i += 4)
+          *reinterpret_cast<float4*>(yr + i) =
+              make_float4(acc[i] * ai, acc[i + 1] * ai, acc[i + 2] * ai, acc[i + 3] * ai);
+      } else {
+#pragma unroll
+        for (int i = 0; i < 64; ++i)
+          if (i < lim) yr[i] = acc[i] * ai;
+      }
+    }
+  } else if (warp == 12) {
+    // ------------------------------------------------ activation producer (TMA)
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < nk; ++kb) {
+        const int s = kb % USTAGES;
+        const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
+        unsigned char* ah = sm + s * STAGE_BYTES;
+        mbar_arrive_tx(&afull[s], 2 * TILE);
+        tma_load_2d(ah, &mapAh, &afull[s], kb * UK, m0);
+        tma_load_2d(ah + TILE, &mapAl, &afull[s], kb * UK, m0);
+        ++issued;
+      }
+      if (*abort) {  // let the copies already issued land before the CTA exits
+        for (int kb = issued - USTAGES > 0 ? issued - USTAGES : 0; kb < issued; ++kb)
+          mbar_drain(&afull[kb % USTAGES], (uint32_t)(kb / USTAGES) & 1u);
+      }
+    }
+  } else {
+    // ------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      int kb = 0;
+      bool ok = true;
+      for (int g = 0; g < ng && ok; ++g) {
+        const int b = g & 1;
+        if (!mbar_wait(&tempty[b], ((uint32_t)(g >> 1) & 1u) ^ 1u, abort)) break;
+        tc_fence_after();
+        const uint32_t dmain = tmem + b * 256, dcorr = dmain + 128;
+        for (int j = 0; j < 2; ++j, ++kb) {
+          const int s = kb % USTAGES;
+          const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
+          if (!mbar_wait(&afull[s], ph, abort) || !mbar_wait(&full[s], ph, abort)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          unsigned char* st = sm + s * STAGE_BYTES;
+          const uint64_t dah = sw128_desc(st), dal = sw128_desc(st + TILE);
+          const uint64_t dbh = sw128_desc(st + 2 * TILE), dbl = sw128_desc(st + 3 * TILE);
+#pragma unroll
+          for (int kk = 0; kk < UK / 16; ++kk) {
+            const uint64_t o = (uint64_t)(kk * 2);  // 32 bytes along K, in 16-byte units
+            const uint32_t acc = (j | kk) != 0;     // a group starts from zero
+            umma_f16(dmain, dah + o, dbh + o, acc);
+            umma_f16(dcorr, dah + o, dbl + o, acc);
+            umma_f16(dcorr, dal + o, dbh + o, 1);
+          }
+          umma_commit(&empty[s]);
+        }
+        if (ok) umma_commit(&tfull[b]);
+      }
+      // Every issued MMA completes before TMEM is freed.
+      umma_commit(drainb);
+      mbar_drain(drainb, 0);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 12) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// f32 activations [M][ldx] -> row-scaled f16 high parts and remainders
+// [M][K] and the inverse row scales [M]. One warp per row.
+__global__ void split_f16_kernel(const float* __restrict__ x, int ldx, int M, int K, __half* __restrict__ hi,
+                                 __half* __restrict__ lo, float* __restrict__ inv) {
+  const int lane = threadIdx.x & 31;
+  const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (m >= M) return;
+  const float* xr = x + (size_t)m * ldx;
+  float amax = 0.f;
+  for (int c = lane * 4; c < K; c += 128) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + c);
+    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
+  }
+  amax = warp_max(amax);
+  const int e = row_exp(amax);
+  const float sc = ldexpf(1.f, e);
+  if (lane == 0) inv[m] = ldexpf(1.f, -e);
+  for (int c = lane * 8; c < K; c += 256) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + c);
+    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
+    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t p = split_h(v[2 * j] * sc), q = split_h(v[2 * j + 1] * sc);
+      h[j] = __byte_perm(p, q, 0x5410);
+      l[j] = __byte_perm(p, q, 0x7632);
+    }
+    *reinterpret_cast<uint4*>(hi + (size_t)m * K + c) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(lo + (size_t)m * K + c) = make_uint4(l[0], l[1], l[2], l[3]);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map of an f16 [M][K] row-major array: box [128 rows][64 k], 128-byte swizzle.
+bool make_map(CUtensorMap* map, const __half* base, int M, int K) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)UK, (cuuint32_t)UM};
+  const cuuint32_t estr[2] = {1, 1};
+  return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+}  // namespace
+
+bool umma_supported(const CqMat& W) {
+  return W.group == 128 && (W.bits == 2 || W.bits == 4) && W.in_pad % 128 == 0 && W.in_pad <= UGMAX * 128;
+}
+
+cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
+                            int nrows, cudaStream_t st, const GemmScratch& gs) {
+  const int K = W.in_pad;
+  if (!umma_supported(W) || !gs.hi || !gs.lo || !gs.inv || gs.elems < (size_t)M * K || gs.rows < (size_t)M)
+    return cudaErrorInvalidValue;
+  if ((reinterpret_cast<uintptr_t>(gs.hi) | reinterpret_cast<uintptr_t>(gs.lo)) & 15) return cudaErrorInvalidValue;
+  split_f16_kernel<<<(M + 7) / 8, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv);
+  cudaError_t e0 = cudaGetLastError();
+  if (e0 != cudaSuccess) return e0;
+  CUtensorMap mh, ml;
+  if (!make_map(&mh, gs.hi, M, K) || !make_map(&ml, gs.lo, M, K)) return cudaErrorNotSupported;
+  auto kern = W.bits == 2 ? cq_umma_kernel<2> : cq_umma_kernel<4>;
+  cudaError_t e = allow_smem((const void*)kern, UMMA_SMEM);
+  if (e != cudaSuccess) return e;
+  dim3 grid((nrows + UN - 1) / UN, (M + UM - 1) / UM);
+  kern<<<grid, UTHREADS, UMMA_SMEM, st>>>(W, mh, ml, gs.inv, M, y, ldy, row0, nrows);
+  return cudaGetLastError();
+}
+
+cudaError_t umma_error_ptr(int** p) { return cudaGetSymbolAddress((void**)p, g_umma_error); }
+
+cudaError_t umma_take_error(int* flag) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_umma_error, sizeof(int));
+  if (e == cudaSuccess && v) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_umma_error, &zero, sizeof(int));
+  }
+  *flag = v;
+  return e;
+}
+
+}  // namespace nb

@@ -113,6 +113,53 @@ def test_cq_gemm_matches_oracle_config1(cuda, bits, n_out):
     assert close(y.cpu().numpy(), want)
 
 
+@pytest.mark.parametrize("bits", [2, 4])
+@pytest.mark.parametrize("shape", [(812, 768), (768, 768), (300, 3072), (8192, 768)])
+def test_cq_tensor_core_gemm_matches_oracle(cuda, bits, shape):
+    """The tcgen05 path (path 3: f16 hi/lo split, three MMAs into TMEM) against
+    the oracle for ragged row counts (partial 128-row tiles) and partial
+    128-output tiles."""
+    torch = cuda
+    out, inp = shape
+    cb = cact_pack.random_codebook(np.random.default_rng(9))
+    d, pp, npp, w, _, _ = make_weight(torch, out, inp, bits, 7, cb)
+    levels = cact_pack.codebook_levels(cb, bits)
+    rng = np.random.default_rng(11)
+    for M in (9, 128, 200, 1000):
+        x = rng.normal(size=(M, inp)).astype(np.float32)
+        xh = np.stack([w.prepare(r) for r in x])
+        y = torch.zeros(M, out, device="cuda")
+        xd = dev(torch, xh)
+        nb.cq_project(pp, npp, out, inp, bits, levels, xd.data_ptr(), xh.shape[1], M, y.data_ptr(), out,
+                      path=3)
+        torch.cuda.synchronize()
+        want = w.matmul_prepared(xh)
+        got = y.cpu().numpy()
+        assert close(got, want), (M, float(np.abs(got - want).max()))
+
+
+@pytest.mark.parametrize("bits", [2, 4])
+def test_cq_tensor_core_unpacking_matches_levels(cuda, bits):
+    """One-hot rotated inputs through the tensor-core path return
+    norm * level[idx] per row to the precision of the hi/lo split."""
+    torch = cuda
+    cb = cact_pack.lloyd_codebook()
+    out, inp = 300, 768
+    d, pp, npp, w, idx, norms = make_weight(torch, out, inp, bits, 1, cb)
+    levels = cact_pack.codebook_levels(cb, bits)
+    ks = np.arange(0, inp, 7)[:16]
+    xh = np.zeros((16, inp), np.float32)
+    xh[np.arange(16), ks] = 1.0
+    y = torch.zeros(16, out, device="cuda")
+    xd = dev(torch, xh)
+    nb.cq_project(pp, npp, out, inp, bits, levels, xd.data_ptr(), inp, 16, y.data_ptr(), out, path=3)
+    torch.cuda.synchronize()
+    yn = y.cpu().numpy()
+    for m, k in enumerate(ks):
+        want = (norms[:, k // 128].astype(np.float32) * levels[idx[:, k]]).astype(np.float32)
+        assert np.allclose(yn[m], want, rtol=1e-6, atol=1e-9), k
+
+
 def test_cq_row_ranges_and_ragged_sizes(cuda):
     torch = cuda
     cb = cact_pack.lloyd_codebook()
@@ -120,7 +167,8 @@ def test_cq_row_ranges_and_ragged_sizes(cuda):
     levels = cact_pack.codebook_levels(cb, 4)
     x = np.random.default_rng(1).normal(size=(67, 3072)).astype(np.float32)
     xh = np.stack([w.prepare(r) for r in x])
-    for M, row0, nrows, path in ((1, 4, 4, 0), (1, 16, 16, 0), (67, 40, 24, 0), (67, 0, 80, 2), (9, 3, 61, 0)):
+    for M, row0, nrows, path in ((1, 4, 4, 0), (1, 16, 16, 0), (67, 40, 24, 0), (67, 0, 80, 2), (9, 3, 61, 0),
+                                 (67, 40, 24, 3), (9, 3, 61, 3)):
         y = torch.zeros(M, nrows, device="cuda")
         xd = dev(torch, xh[:M])
         nb.cq_project(pp, npp, 80, 3072, 4, levels, xd.data_ptr(), 3072, M, y.data_ptr(), nrows,

@@ -25,6 +25,15 @@ def tol(int8, small_heads=False):
     return (REL_INT8 * (3 if small_heads else 1)) if int8 else REL
 
 
+def tol_pair(int8):
+    """GPU-against-GPU bar for two launch shapes of the same input (single
+    sessions against one batch): the shapes may take different projection
+    kernels (f32 GEMV at <= 8 rows, tensor cores above) and attention splits,
+    and in int8 mode each side can flip KV codes independently; each side is
+    held to REL_INT8 against the oracle, so the two differ by at most twice it."""
+    return 2 * REL_INT8 if int8 else 2e-4
+
+
 def rel_err(a, b):
     return float(np.abs(a - b).max() / np.sqrt(np.mean(b.astype(np.float64) ** 2)))
 
@@ -99,14 +108,14 @@ def test_batched_sessions_match_single_sessions(full_gpu):
         batch = [full_gpu.session(128, int8) for _ in prompts]
         lg, picks = full_gpu.prefill_batch(batch, prompts)
         for a, b in zip(lg, ref):
-            assert rel_err(a, b) < (tol(int8) if int8 else 2e-4)
+            assert rel_err(a, b) < tol_pair(int8)
         assert np.array_equal(picks, np.array([int(np.argmax(r)) for r in ref]))
         toks = picks
         for _ in range(6):
             lg, picks = full_gpu.decode_batch(batch, toks)
             ref = [s.decode_step(int(t)) for s, t in zip(singles, toks)]
             for a, b in zip(lg, ref):
-                assert rel_err(a, b) < (tol(int8) if int8 else 2e-4)
+                assert rel_err(a, b) < tol_pair(int8)
             toks = picks
 
 
