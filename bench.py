@@ -265,6 +265,30 @@ def gemv_bandwidth(nb, torch, stream):
     return out
 
 
+def attn_traffic_per_unit():
+    """DRAM bytes per (position, KV head) of the decode attention kernel from
+    the committed ncu summary (dram__bytes_read.sum + dram__bytes_write.sum of
+    one captured launch divided by its units), or None when absent."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "decode_attention_int8.md")) as f:
+            for line in f:
+                if line.startswith("traffic_bytes_per_position_kvhead:"):
+                    return float(line.split(":")[1])
+    except OSError:
+        pass
+    return None
+
+
+def attn_units_per_step(cfg, n_sessions, pos):
+    """(position, KV head) pairs the 20 attention launches of one step read."""
+    total = 0
+    for l in range(cfg["layers"]):
+        glob = l in (4, 9, 14, 19)
+        span = pos + 1 if glob else min(pos + 1, cfg["window"])
+        total += span * cfg["kv_heads"] * n_sessions
+    return total
+
+
 def attn_bytes_per_step(cfg, n_sessions, pos):
     """Algorithmic HBM bytes of the 20 decode-attention launches of one step at
     position `pos` (int8: per position and KV head 48 + 64 code bytes + two f32
@@ -379,6 +403,8 @@ def main():
     attn_ms = prof["attention"] / geo["layers"]
     abytes = attn_bytes_per_step(geo, per, pos_now) / geo["layers"]
     achieved = abytes / (attn_ms * 1e-3) / 1e9
+    tpu = attn_traffic_per_unit()
+    traffic = round(tpu * attn_units_per_step(geo, per, pos_now) / geo["layers"]) if tpu else None
     extra = {}
     if rank == 0:
         extra["gemv_config0"] = gemv_bandwidth(nb, torch, st)
@@ -404,7 +430,8 @@ def main():
                    "prefill_s": round(prefill_s, 2),
                    "prefill_tok_per_s_per_gpu": round(per * args.prompt / prefill_s, 1)},
         "roofline": {"kernel": "decode attention (int8 KV)", "bound": "hbm", "achieved": round(achieved, 1),
-                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": None,
+                     "peak": hbm, "unit": "GB/s", "frac": round(achieved / hbm, 4), "traffic": traffic,
+                     "traffic_source": "ncu dram bytes per (position, KV head), profiles/decode_attention_int8.md",
                      "peak_source": src, "algorithmic_bytes_per_launch": int(abytes),
                      "launch_ms": round(attn_ms, 4)},
         "profile_ms_per_step": {k: round(v, 4) for k, v in prof.items()},

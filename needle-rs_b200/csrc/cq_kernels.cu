@@ -335,6 +335,14 @@ cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int
   return cudaGetLastError();
 }
 
+int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path) {
+  if (M <= 0) return 0;
+  const bool scratch_ok = gs && gs->hi && gs->lo && gs->inv && gs->elems >= (size_t)M * W.in_pad &&
+                          gs->rows >= (size_t)M;
+  if (force_path == 3 || (force_path == 0 && M > 8 && scratch_ok && umma_supported(W))) return 2;
+  return 1;
+}
+
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                        int nrows, cudaStream_t st, int force_path, const GemmScratch* gs) {
   if (M <= 0 || nrows <= 0) return cudaSuccess;

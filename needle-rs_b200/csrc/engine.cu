@@ -800,7 +800,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
       NB_TRY(cq_project(eng_kv[s], ws.fetched + (size_t)s * d, S * d, M, ws.ekv + (size_t)s * 2 * d,
                         S * 2 * d, 0, 2 * d, st, 0, &ws.gs));
     NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, ws.ekv, ws.evc, st));
-    NB_MARK(PK_ENGRAM, S + 2);
+    NB_MARK(PK_ENGRAM, S * cq_launches(eng_kv[0], M, &ws.gs) + 2);
   }
   NB_TRY(launch_embed(G, emb, rb, ws.lanes, st));
   NB_MARK(PK_EMBED, 1);
@@ -809,7 +809,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
                             site_of[l], ws.ekv, ws.evc, ws.u, ws.bx, ws.xh, ws.gates, st));
     NB_MARK(PK_LAYER_PRE, 1);
     NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st, 0, &ws.gs));
-    NB_MARK(PK_QKVG, 1);
+    NB_MARK(PK_QKVG, cq_launches(qkvg[l], M, &ws.gs));
     NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs,
                            int8 ? ws.q8 : nullptr, int8 ? ws.q8s : nullptr, st));
     NB_MARK(PK_QKV_POST, 1);
@@ -819,7 +819,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
     NB_MARK(PK_ATTN_FINISH, 1);
     NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st, 0, &ws.gs));
-    NB_MARK(PK_OUT_PROJ, 1);
+    NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &ws.gs));
     NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, ws.projo, ws.u, ws.bx,
                              ws.gates, ws.lanes, st));
     NB_MARK(PK_LAYER_POST, 1);
@@ -833,7 +833,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
 cudaError_t Engine::head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                          cudaStream_t st, Prof* prof) {
   NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &ws.gs));
-  NB_MARK(PK_HEAD, 1);
+  NB_MARK(PK_HEAD, cq_launches(emb, M, &ws.gs));
   if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
   NB_MARK(PK_BOOK, picks ? 1 : 0);
   return cudaSuccess;

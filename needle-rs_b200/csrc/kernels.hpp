@@ -55,6 +55,9 @@ struct GemmScratch {
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                        int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr);
 bool umma_supported(const CqMat& W);
+// Kernel launches cq_project makes for these arguments (2 on the tensor-core
+// path: the activation split and the GEMM).
+int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path = 0);
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                             int nrows, cudaStream_t st, const GemmScratch& gs);
 // Reads and clears the device flag raised when a bounded wait of the
