@@ -45,21 +45,6 @@ struct AttnSrc {
   int base;
 };
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
-  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  int n = valid ? 16 : 0;  // src-size 0: zero-fill, nothing read
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
-}
-__device__ __forceinline__ void cp_async4(void* smem, const void* gmem, bool valid) {
-  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
-  int n = valid ? 4 : 0;
-  asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gmem), "r"(n));
-}
-__device__ __forceinline__ void cp_commit() { asm volatile("cp.async.commit_group;\n" ::); }
-template <int N>
-__device__ __forceinline__ void cp_wait() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
-}
 
 template <bool INT8, int QK, int VH>
 struct AttnTile {
@@ -91,17 +76,25 @@ __device__ __forceinline__ void issue_chunk(AttnSmem<INT8, QK, VH>& S, int buf, 
   using T = AttnTile<INT8, QK, VH>;
   const char* kb = (const char*)src.k;
   const char* vb = (const char*)src.v;
+  // Storage index of position n0 + i: one modulo per chunk, then a wrap test.
+  const int idx0 = src.slots > 0 ? n0 % src.slots : src.base + n0;
+  auto index = [&](int i) -> long {
+    if (src.slots == 0) return (long)idx0 + i;
+    const int v = idx0 + i;
+    if (src.slots >= CH) return v >= src.slots ? v - src.slots : v;
+    return v % src.slots;
+  };
   for (int j = threadIdx.x; j < CH * T::KP; j += AT_THREADS) {
     const int i = j / T::KP, pc = j % T::KP, n = n0 + i;
     const bool ok = n <= hi;
-    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    const long idx = ok ? index(i) : 0;
     cp_async16(S.kbuf[buf] + i * QK * T::ES + pc * 16,
                kb + (idx * src.k_row + kh * src.k_head) * T::ES + pc * 16, ok);
   }
   for (int j = threadIdx.x; j < CH * T::VP; j += AT_THREADS) {
     const int i = j / T::VP, pc = j % T::VP, n = n0 + i;
     const bool ok = n <= hi;
-    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    const long idx = ok ? index(i) : 0;
     cp_async16(S.vbuf[buf] + i * VH * T::ES + pc * 16,
                vb + (idx * src.v_row + kh * src.v_head) * T::ES + pc * 16, ok);
   }
@@ -109,7 +102,7 @@ __device__ __forceinline__ void issue_chunk(AttnSmem<INT8, QK, VH>& S, int buf, 
     for (int i = threadIdx.x; i < CH; i += AT_THREADS) {
       const int n = n0 + i;
       const bool ok = n <= hi;
-      const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+      const long idx = ok ? index(i) : 0;
       cp_async4(&S.ksc[buf][i], src.ks + idx * src.s_row + kh * src.s_head, ok);
       cp_async4(&S.vsc[buf][i], src.vs + idx * src.s_row + kh * src.s_head, ok);
     }
@@ -392,20 +385,20 @@ struct __align__(16) MmaWarpSmem {
 };
 
 __device__ __forceinline__ void mma_s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k32.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 __device__ __forceinline__ void mma_s8_k16(int (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.s32.s8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
       : "+r"(d[0]), "+r"(d[1]), "+r"(d[2]), "+r"(d[3])
       : "r"(a0), "r"(a1), "r"(b0));
 }
 __device__ __forceinline__ void mma_f16_k16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};\n"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -434,31 +427,40 @@ __device__ __forceinline__ uint32_t pack_h2(float x, float y) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Storage index of position n0 + i of a block, i in [0, WB): one modulo per
+// block (idx0 = n0 mod slots), then a wrap test per position.
+__device__ __forceinline__ long block_index(const AttnSrc& src, int idx0, int i) {
+  if (src.slots == 0) return (long)idx0 + i;
+  int v = idx0 + i;
+  if (src.slots >= WB) return v >= src.slots ? v - src.slots : v;
+  return v % src.slots;  // rings shorter than a block (tiny geometries only)
+}
+
 // cp.async of one warp block [n0, n0 + WB) clipped at hi (zero-filled beyond).
 template <int QK, int VH>
 __device__ __forceinline__ void mma_issue(MmaWarpSmem<QK, VH>& W, int buf, const AttnSrc& src, int kh,
                                           int n0, int hi, int lane) {
   using T = MmaTile<QK, VH>;
-  const int8_t* kb = (const int8_t*)src.k;
-  const int8_t* vb = (const int8_t*)src.v;
+  const int8_t* kb = (const int8_t*)src.k + kh * src.k_head;
+  const int8_t* vb = (const int8_t*)src.v + kh * src.v_head;
+  const int idx0 = src.slots > 0 ? n0 % src.slots : src.base + n0;
 #pragma unroll
   for (int j = lane; j < WB * T::KP; j += 32) {
-    const int i = j / T::KP, pc = j % T::KP, n = n0 + i;
-    const bool ok = n <= hi;
-    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
-    cp_async16(W.k[buf] + i * T::KS + pc * 16, kb + idx * src.k_row + kh * src.k_head + pc * 16, ok);
+    const int i = j / T::KP, pc = j % T::KP;
+    const bool ok = n0 + i <= hi;
+    const long idx = ok ? block_index(src, idx0, i) : 0;
+    cp_async16(W.k[buf] + i * T::KS + pc * 16, kb + idx * src.k_row + pc * 16, ok);
   }
 #pragma unroll
   for (int j = lane; j < WB * T::VP; j += 32) {
-    const int i = j / T::VP, pc = j % T::VP, n = n0 + i;
-    const bool ok = n <= hi;
-    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
-    cp_async16(W.v[buf] + i * VH + pc * 16, vb + idx * src.v_row + kh * src.v_head + pc * 16, ok);
+    const int i = j / T::VP, pc = j % T::VP;
+    const bool ok = n0 + i <= hi;
+    const long idx = ok ? block_index(src, idx0, i) : 0;
+    cp_async16(W.v[buf] + i * VH + pc * 16, vb + idx * src.v_row + pc * 16, ok);
   }
   {
-    const int n = n0 + lane;
-    const bool ok = n <= hi;
-    const long idx = ok ? (src.slots > 0 ? (long)(n % src.slots) : (long)(src.base + n)) : 0;
+    const bool ok = n0 + lane <= hi;
+    const long idx = ok ? block_index(src, idx0, lane) : 0;
     cp_async4(&W.ks[buf][lane], src.ks + idx * src.s_row + kh * src.s_head, ok);
     cp_async4(&W.vs[buf][lane], src.vs + idx * src.s_row + kh * src.s_head, ok);
   }
@@ -535,22 +537,33 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
       *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0 + 8) = h1;
     }
     // ---- integer key dots: n-tile j covers positions j*8 .. j*8+7
+    // (consecutive MMAs target different n-tiles, so they do not wait on each other)
     float sc[8];
+    int d[4][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      int d[4] = {0, 0, 0, 0};
-      const int8_t* kr = W.k[buf] + (j * 8 + g) * T::KS;
+    for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0;
 #pragma unroll
-      for (int s = 0; s < T::NK32; ++s)
-        mma_s8_k32(d, qa[s], *reinterpret_cast<const uint32_t*>(kr + s * 32 + t * 4),
+    for (int s = 0; s < T::NK32; ++s)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int8_t* kr = W.k[buf] + (j * 8 + g) * T::KS;
+        mma_s8_k32(d[j], qa[s], *reinterpret_cast<const uint32_t*>(kr + s * 32 + t * 4),
                    *reinterpret_cast<const uint32_t*>(kr + s * 32 + 16 + t * 4));
-      if (T::K16) mma_s8_k16(d, qa16, 0u, *reinterpret_cast<const uint32_t*>(kr + T::NK32 * 32 + t * 4));
+      }
+    if (T::K16) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int8_t* kr = W.k[buf] + (j * 8 + g) * T::KS;
+        mma_s8_k16(d[j], qa16, 0u, *reinterpret_cast<const uint32_t*>(kr + T::NK32 * 32 + t * 4));
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int i = j * 8 + t * 2 + e;
-        sc[j * 2 + e] = n0 + i <= b ? (float)d[e] * qs * W.ks[buf][i] * scale : -INFINITY;
+        sc[j * 2 + e] = n0 + i <= b ? (float)d[j][e] * qs * W.ks[buf][i] * scale : -INFINITY;
       }
-    }
     // ---- online softmax of row g over this block (the four lanes of a row
     // hold 8 positions each)
     float mx = sc[0];
@@ -593,14 +606,19 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
         al[1] = al[3] = 0u;
       }
       const int mat = lane >> 3, row = lane & 7;
+      uint32_t bf[T::NT / 2][4];
+#pragma unroll
+      for (int np = 0; np < T::NT / 2; ++np)
+        ldsm_x4_trans(bf[np], W.vh + (kk * 16 + (mat & 1) * 8 + row) * T::VHS + np * 16 + (mat >> 1) * 8);
 #pragma unroll
       for (int np = 0; np < T::NT / 2; ++np) {
-        uint32_t bf[4];
-        ldsm_x4_trans(bf, W.vh + (kk * 16 + (mat & 1) * 8 + row) * T::VHS + np * 16 + (mat >> 1) * 8);
-        mma_f16_k16(o[2 * np], ah, bf[0], bf[1]);
-        mma_f16_k16(o[2 * np], al, bf[0], bf[1]);
-        mma_f16_k16(o[2 * np + 1], ah, bf[2], bf[3]);
-        mma_f16_k16(o[2 * np + 1], al, bf[2], bf[3]);
+        mma_f16_k16(o[2 * np], ah, bf[np][0], bf[np][1]);
+        mma_f16_k16(o[2 * np + 1], ah, bf[np][2], bf[np][3]);
+      }
+#pragma unroll
+      for (int np = 0; np < T::NT / 2; ++np) {
+        mma_f16_k16(o[2 * np], al, bf[np][0], bf[np][1]);
+        mma_f16_k16(o[2 * np + 1], al, bf[np][2], bf[np][3]);
       }
     }
     __syncwarp();  // before the next block overwrites the f16 values
@@ -887,17 +905,35 @@ __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ 
                                    const float* __restrict__ proj, float* __restrict__ oh) {
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x;
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int od = G.o_dim, opad = (od + 127) / 128 * 128, rep = G.heads / G.kvh, pw = rep * (G.vh + 2);
   const float* gate = proj + (size_t)r * G.proj_dim + G.qkv_dim;
-  for (int i = threadIdx.x; i < opad; i += blockDim.x) {
-    float v = 0.f;
-    if (i < od) {
-      const int h = i / G.vh, d = i % G.vh, kh = h / rep, hl = h % rep;
-      v = combine_head(part + ((size_t)r * G.kvh + kh) * nsplit * pw, nsplit, rep, G.vh, hl, d) *
-          sigmoidf_(gate[i]);
+  // One warp per head: the split weights exp(m_z - M) and 1/L are formed once
+  // per head (lanes over splits), then each lane merges its value dimensions.
+  for (int h = wid; h < G.heads; h += nw) {
+    const int kh = h / rep, hl = h % rep;
+    const float* base = part + ((size_t)r * G.kvh + kh) * nsplit * pw;
+    float M = -INFINITY;
+    for (int z = lane; z < nsplit; z += 32) M = fmaxf(M, base[z * pw + hl]);
+    M = warp_max(M);
+    float L = 0.f;
+    for (int z = lane; z < nsplit; z += 32) {
+      const float mz = base[z * pw + hl];
+      if (mz != -INFINITY) L += expf(mz - M) * base[z * pw + rep + hl];
     }
-    sm[i] = v;
+    L = warp_sum(L);
+    for (int dd = lane; dd < G.vh; dd += 32) {
+      float o = 0.f;
+      for (int z = 0; z < nsplit; ++z) {
+        const float mz = base[z * pw + hl];
+        if (mz == -INFINITY) continue;
+        o += expf(mz - M) * base[z * pw + 2 * rep + hl * G.vh + dd];
+      }
+      const int i = h * G.vh + dd;
+      sm[i] = o / L * sigmoidf_(gate[i]);
+    }
   }
+  for (int i = od + threadIdx.x; i < opad; i += blockDim.x) sm[i] = 0.f;
   __syncthreads();
   fwht_groups_warp(sm, opad / 128);
   __syncthreads();

@@ -9,6 +9,7 @@
 #include <cstring>
 #include <fstream>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -103,6 +104,37 @@ nb::CqMat make_cq(const void* packed, const void* norms, int rows, int in_feat, 
   W.bits = bits;
   for (int i = 0; i < (1 << bits) && i < 16; ++i) W.levels[i] = levels[i];
   return W;
+}
+
+// Stream-ordered scratch of the nd_* entry points comes from a library-owned
+// memory pool per device whose release threshold keeps freed memory reserved,
+// so repeated calls reuse it instead of mapping new memory each time.
+cudaError_t scratch_alloc(void** p, size_t bytes, cudaStream_t st) {
+  static std::mutex mu;
+  static std::vector<cudaMemPool_t> pools;
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  cudaMemPool_t pool = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    if ((int)pools.size() <= dev) pools.resize(dev + 1, nullptr);
+    if (!pools[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      e = cudaMemPoolCreate(&pools[dev], &props);
+      if (e != cudaSuccess) {
+        pools[dev] = nullptr;
+        return e;
+      }
+      uint64_t keep = UINT64_MAX;
+      cudaMemPoolSetAttribute(pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+    }
+    pool = pools[dev];
+  }
+  return cudaMallocFromPoolAsync(p, bytes, pool, st);
 }
 
 // SplitMix64 and temperature sampling as crates/needle-infer/src/v3_engine.rs:422-464.
@@ -642,14 +674,18 @@ int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, 
   const bool tensor_cores = path == 3 || (path == 0 && M > 8 && nb::umma_supported(W));
   if (!tensor_cores || M <= 0) return nd_status(nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, st, path));
   // The split activations live in stream-ordered scratch, released on `stream`.
+  if (nrows <= 0 || row0 < 0 || row0 + nrows > rows) return nd_status(cudaErrorInvalidValue);
   nb::GemmScratch gs;
   gs.elems = (size_t)M * W.in_pad;
+  gs.welems = (size_t)nrows * W.in_pad;
   void* mem = nullptr;
-  cudaError_t e = cudaMallocAsync(&mem, gs.elems * 2 * sizeof(__half) + (size_t)M * sizeof(float), st);
+  cudaError_t e = scratch_alloc(&mem, (gs.elems + gs.welems) * 2 * sizeof(__half) + (size_t)M * sizeof(float), st);
   if (e != cudaSuccess) return nd_status(e);
   gs.hi = (__half*)mem;
   gs.lo = gs.hi + gs.elems;
-  gs.inv = reinterpret_cast<float*>(gs.lo + gs.elems);
+  gs.whi = gs.lo + gs.elems;
+  gs.wlo = gs.whi + gs.welems;
+  gs.inv = reinterpret_cast<float*>(gs.wlo + gs.welems);
   gs.rows = (size_t)M;
   e = nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, st, path, &gs);
   cudaError_t f = cudaFreeAsync(mem, st);
@@ -676,7 +712,7 @@ int nd_attend_step(const float* q, const void* k, const void* v, const float* ks
   cudaStream_t st = (cudaStream_t)stream;
   const int ns = nb::attn_nsplit(B, kv_heads, slots);
   float* part = nullptr;
-  cudaError_t e = cudaMallocAsync((void**)&part, nb::attn_part_floats(B, heads, kv_heads, vh, ns) * 4, st);
+  cudaError_t e = scratch_alloc((void**)&part, nb::attn_part_floats(B, heads, kv_heads, vh, ns) * 4, st);
   if (e != cudaSuccess) return nd_status(e);
   e = nb::launch_attend_step(q, k, v, ks, vs, int8, slots, lo, hi, B, heads, kv_heads, qk, vh, ns, part, out, st);
   cudaError_t f = cudaFreeAsync(part, st);

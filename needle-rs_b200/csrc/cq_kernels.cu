@@ -335,11 +335,15 @@ cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int
   return cudaGetLastError();
 }
 
+static bool umma_scratch_ok(const CqMat& W, int M, int nrows, const GemmScratch* gs) {
+  return gs && gs->hi && gs->lo && gs->inv && gs->whi && gs->wlo && gs->elems >= (size_t)M * W.in_pad &&
+         gs->rows >= (size_t)M && gs->welems >= (size_t)nrows * W.in_pad;
+}
+
 int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path) {
   if (M <= 0) return 0;
-  const bool scratch_ok = gs && gs->hi && gs->lo && gs->inv && gs->elems >= (size_t)M * W.in_pad &&
-                          gs->rows >= (size_t)M;
-  if (force_path == 3 || (force_path == 0 && M > 8 && scratch_ok && umma_supported(W))) return 2;
+  if (force_path == 3 || (force_path == 0 && M > 8 && umma_scratch_ok(W, M, W.rows, gs) && umma_supported(W)))
+    return 3;
   return 1;
 }
 
@@ -349,8 +353,7 @@ cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y
   if (!cq_args_ok(W, xh, ldx) || row0 < 0 || row0 + nrows > W.rows) return cudaErrorInvalidValue;
   if (force_path == 1 && M > 8) return cudaErrorInvalidValue;
   if (force_path < 0 || force_path > 3) return cudaErrorInvalidValue;
-  const bool scratch_ok = gs && gs->hi && gs->lo && gs->inv && gs->elems >= (size_t)M * W.in_pad &&
-                          gs->rows >= (size_t)M;
+  const bool scratch_ok = umma_scratch_ok(W, M, nrows, gs);
   if (force_path == 3) {
     if (!scratch_ok) return cudaErrorInvalidValue;
     return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs);

@@ -57,7 +57,7 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
-  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, oh, projo, gates, fetched, ekv, evc, lm_in,
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, whi, wlo, oh, projo, gates, fetched, ekv, evc, lm_in,
                 pks, pvs, pk, pv, rows, tokens, next, last_rows};
   for (void* p : ps)
     if (p) cudaFree(p);
@@ -75,6 +75,7 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
   const size_t d = G.d, dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   const size_t S = std::max(1, G.n_sites);
   const size_t kmax = std::max(dpad, opad);  // widest input of a projection
+  const size_t wmax = std::max<size_t>(std::max<size_t>(G.logit_rows, G.proj_dim), 2 * d);  // most weight rows
   struct A {
     void** p;
     size_t bytes;
@@ -85,6 +86,7 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
       {(void**)&ws.q8s, cap * G.heads * 4},         {(void**)&ws.q8, cap * G.q_dim},
       {(void**)&ws.ahi, cap * kmax * 2},            {(void**)&ws.alo, cap * kmax * 2},
       {(void**)&ws.ainv, cap * 4},
+      {(void**)&ws.whi, wmax * kmax * 2},           {(void**)&ws.wlo, wmax * kmax * 2},
       {(void**)&ws.oh, cap * opad * 4},
       {(void**)&ws.projo, cap * d * 4},             {(void**)&ws.gates, cap * 24 * 4},
       {(void**)&ws.fetched, cap * S * d * 4},       {(void**)&ws.ekv, cap * S * 2 * d * 4},
@@ -107,6 +109,9 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
   ws.gs.inv = ws.ainv;
   ws.gs.elems = cap * kmax;
   ws.gs.rows = cap;
+  ws.gs.whi = ws.whi;
+  ws.gs.wlo = ws.wlo;
+  ws.gs.welems = wmax * kmax;
   ws.cap = cap;
   epoch++;
   return true;

@@ -67,6 +67,7 @@ struct Workspace {
   int8_t* q8 = nullptr;  // int8 mode: query codes [rows][heads][qk], scales in q8s [rows][heads]
   __half *ahi = nullptr, *alo = nullptr;  // tensor-core projections: split activations
   float* ainv = nullptr;                  // and their inverse row scales
+  __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
   GemmScratch gs;
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;

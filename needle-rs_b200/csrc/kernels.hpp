@@ -39,8 +39,8 @@ struct RowBatch {
   int mode;
 };
 
-// Scratch of the tensor-core path: the activations split into f16 high parts
-// and remainders, `elems` (>= M * in_pad) halves each, 16-byte aligned, and
+// Scratch of the tensor-core path (16-byte aligned): the activations split
+// into f16 high parts and remainders, `elems` (>= M * in_pad) halves each, and
 // `rows` (>= M) inverse row scales.
 struct GemmScratch {
   __half* hi = nullptr;
@@ -48,6 +48,11 @@ struct GemmScratch {
   float* inv = nullptr;
   size_t elems = 0;
   size_t rows = 0;
+  // The weight rows' levels expanded to f16 high parts and remainders,
+  // `welems` (>= nrows * in_pad) halves each.
+  __half* whi = nullptr;
+  __half* wlo = nullptr;
+  size_t welems = 0;
 };
 
 // force_path: 0 automatic (GEMV for M <= 8, else the tensor cores when `gs`
@@ -55,8 +60,8 @@ struct GemmScratch {
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                        int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr);
 bool umma_supported(const CqMat& W);
-// Kernel launches cq_project makes for these arguments (2 on the tensor-core
-// path: the activation split and the GEMM).
+// Kernel launches cq_project makes for these arguments (3 on the tensor-core
+// path: the activation split, the level expansion and the GEMM).
 int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path = 0);
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                             int nrows, cudaStream_t st, const GemmScratch& gs);

@@ -8,6 +8,8 @@
 // (index unpacking, Engram hashing, int8 quantisation) is exact.
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.hpp"
 #include "launch_util.hpp"
@@ -349,7 +351,9 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
 // w+16 of the 2n + n^2 projected rows, lane l covering group elements
 // l*4..l*4+3. The rotation is linear, so the rms_unit scale (kernels.rs:32) is
 // applied to the finished dot products rather than to the lanes first. The
-// next group's lanes are loaded while the current one is consumed.
+// next group's lanes are loaded while the current one is consumed. The CTA's
+// 2n + n^2 packed weight rows and their norms are copied to shared memory once
+// at the start, so the group loop reads no weights from global memory.
 // Phase 2 (one warp per row, no block barriers): gates and Sinkhorn, mix_down
 // re-reading the tile's lanes (L2-resident), the Engram gate, the ZCRMS norm
 // and the rotation of the attention input, exactly as the per-row kernel.
@@ -361,45 +365,43 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
                        CqMat phi_post, CqMat phi_res, MhcParams mp, const float* __restrict__ norm_in,
                        int site, const float* __restrict__ ekv, const float* __restrict__ evc,
                        float* __restrict__ u_out, float* __restrict__ bx_out, float* __restrict__ xh_out,
-                       float* __restrict__ gates) {
+                       float* __restrict__ gates, int rbmax, int gmax) {
   __shared__ __align__(16) float Xs[PT_M][128];
   __shared__ float lev[48];
   __shared__ float phi_s[PT_M][24];
   __shared__ float ss_s[PT_M];
+  extern __shared__ __align__(16) unsigned char pt_dyn[];  // [nrow][rbmax] codes, [nrow][gmax] norms
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int n = G.lanes, d = G.d, W = n * d, nrow = 2 * n + n * n;
   const int m0 = blockIdx.x * PT_M;
   const int rows = min(PT_M, rb.M - m0);
   const int ngroups = W / 128;
   load_phi_levels(phi_pre, phi_post, phi_res, lev);
+  float* nsm = reinterpret_cast<float*>(pt_dyn + (size_t)nrow * rbmax);
+
+  // Stage the packed rows and norms of all 2n + n^2 projected rows.
+  for (int o = 0; o < nrow; ++o) {
+    const CqMat& Mx = o < n ? phi_pre : (o < 2 * n ? phi_post : phi_res);
+    const int r = o < n ? li * n + o : (o < 2 * n ? li * n + (o - n) : li * n * n + (o - 2 * n));
+    const uint8_t* prow;
+    const __half* pn;
+    cq_row_ptr(Mx, r, &prow, &pn);
+    for (int i = tid; i < Mx.row_bytes / 16; i += blockDim.x)
+      cp_async16(pt_dyn + (size_t)o * rbmax + i * 16, prow + i * 16, true);
+    for (int g = tid; g < Mx.groups; g += blockDim.x) nsm[o * gmax + g] = __half2float(pn[g]);
+  }
+  cp_commit();
+  cp_wait<0>();
 
   // This warp's projected rows: o = wid + 8j.
-  const uint8_t* wrow[3];
-  const __half* wnrm[3];
   int wbits[3], wlev[3];
   bool wok[3];
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
     const int o = wid + 8 * j;
     wok[j] = o < nrow;
-    wrow[j] = nullptr;
-    wnrm[j] = nullptr;
-    wbits[j] = 4;
-    wlev[j] = 0;
-    if (!wok[j]) continue;
-    if (o < n) {
-      cq_row_ptr(phi_pre, li * n + o, &wrow[j], &wnrm[j]);
-      wbits[j] = phi_pre.bits;
-      wlev[j] = 0;
-    } else if (o < 2 * n) {
-      cq_row_ptr(phi_post, li * n + (o - n), &wrow[j], &wnrm[j]);
-      wbits[j] = phi_post.bits;
-      wlev[j] = 16;
-    } else {
-      cq_row_ptr(phi_res, li * n * n + (o - 2 * n), &wrow[j], &wnrm[j]);
-      wbits[j] = phi_res.bits;
-      wlev[j] = 32;
-    }
+    wbits[j] = !wok[j] ? 4 : (o < n ? phi_pre.bits : (o < 2 * n ? phi_post.bits : phi_res.bits));
+    wlev[j] = !wok[j] ? 0 : (o < n ? 0 : (o < 2 * n ? 16 : 32));
   }
 
   // Rows wid and wid + 8 of the tile are loaded and rotated by this warp.
@@ -415,7 +417,7 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
   for (int j = 0; j < 3; ++j)
 #pragma unroll
     for (int m = 0; m < PT_M; ++m) acc[j][m] = 0.f;
-  __syncthreads();  // level tables
+  __syncthreads();  // level tables, staged rows and norms
 
   for (int g = 0; g < ngroups; ++g) {
     const float4 cA = nA, cB = nB;
@@ -427,8 +429,12 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
     float wn[3];
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      wc[j] = wok[j] ? cq_quad_codes(wrow[j], wbits[j], g, lane) : 0u;
-      wn[j] = wok[j] ? __half2float(wnrm[j][g]) : 0.f;
+      const int o = wid + 8 * j;
+      const unsigned char* cr = pt_dyn + (size_t)(wok[j] ? o : 0) * rbmax;
+      wc[j] = !wok[j] ? 0u
+                      : (wbits[j] == 4 ? (uint32_t)reinterpret_cast<const uint16_t*>(cr + g * 64)[lane]
+                                       : (uint32_t)cr[g * 32 + lane]);
+      wn[j] = wok[j] ? nsm[o * gmax + g] : 0.f;
     }
     {
       float v[4] = {cA.x, cA.y, cA.z, cA.w};
@@ -582,8 +588,13 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
   const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
                         (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0;
   if (rb.M >= PT_MIN_ROWS && tiled_ok) {
-    layer_pre_tiled_kernel<<<(rb.M + PT_M - 1) / PT_M, 256, 0, st>>>(
-        G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates);
+    const int rbmax = std::max(phi_pre.row_bytes, std::max(phi_post.row_bytes, phi_res.row_bytes));
+    const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
+    const size_t dyn = (size_t)nrow * rbmax + (size_t)nrow * gmax * 4;
+    cudaError_t e = allow_smem((const void*)layer_pre_tiled_kernel, dyn);
+    if (e != cudaSuccess) return e;
+    layer_pre_tiled_kernel<<<(rb.M + PT_M - 1) / PT_M, 256, dyn, st>>>(
+        G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates, rbmax, gmax);
     return cudaGetLastError();
   }
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;

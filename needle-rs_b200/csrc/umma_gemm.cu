@@ -16,18 +16,21 @@
 // Activation rows and the level table are scaled by powers of two that keep
 // every f16 remainder in the normal range; the epilogue undoes them exactly.
 //
-// One CTA computes 128 activation rows x 128 weight rows with 14 warps:
-//   * warp 12 loads [128 rows x 64 k] tiles of the split activations (made by
-//     split_f16_kernel) with TMA and 128-byte swizzle into a 3-stage ring, and
-//     owns the TMEM allocation;
-//   * warps 0-3 read the packed `.cact` codes straight from the container (one
-//     weight row per thread) and decode them into level hi / lo tiles in the
-//     same swizzled K-major layout;
-//   * warp 13 (one thread) issues tcgen05.mma kind::f16 M=128 N=128 K=16, three
+// Per call, cq_expand_kernel reads the packed `.cact` codes of the requested
+// rows in place and writes their level high parts and remainders as f16
+// [rows][in_pad] tiles (4 bytes per weight, L2-resident for the GEMM that
+// follows), once, instead of once per 128-row activation tile; the group
+// norms stay in the container and are applied by the epilogue.
+//
+// One CTA computes 128 activation rows x 128 weight rows with 10 warps:
+//   * warp 8 loads [128 rows x 64 k] tiles of the split activations (made by
+//     split_f16_kernel) and of the expanded levels with TMA and 128-byte
+//     swizzle into a 3-stage ring, and owns the TMEM allocation;
+//   * warp 9 (one thread) issues tcgen05.mma kind::f16 M=128 N=128 K=16, three
 //     per K step, into the group's accumulator pair; groups alternate between
 //     two pairs so one is drained while the other fills;
-//   * warps 4-11 drain the accumulators (warp w reads TMEM lanes 32*(w%4)..,
-//     columns of half (w-4)/4) and store y.
+//   * warps 0-7 drain the accumulators (warp w reads TMEM lanes 32*(w%4)..,
+//     columns of half w/4) and store y.
 // Every wait on an mbarrier is bounded in time; on expiry the CTA raises a
 // device error flag, stops, waits (bounded) for its issued copies and MMAs,
 // frees its TMEM and returns, and the host reports the flag.
@@ -36,6 +39,8 @@
 #include <cuda_runtime.h>
 #include <cudaTypedefs.h>
 
+#include <algorithm>
+#include <cmath>
 #include <mutex>
 
 #include "common.cuh"
@@ -53,11 +58,11 @@ constexpr int UN = 128;          // weight rows per CTA (MMA N)
 constexpr int UK = 64;           // K per stage: 64 f16 = one 128-byte swizzle row
 constexpr int USTAGES = 3;
 constexpr int UGMAX = 32;        // groups of 128 supported (in_pad <= 4096)
-constexpr int UTHREADS = 448;    // warps 0-3 weights, 4-11 epilogue, 12 TMA + TMEM, 13 MMA
+constexpr int UTHREADS = 320;    // warps 0-7 epilogue, 8 TMA + TMEM, 9 MMA
 constexpr uint32_t TILE = 128 * 128;        // bytes of one [128 rows][128 B] tile
 constexpr uint32_t STAGE_BYTES = 4 * TILE;  // A hi, A lo, B hi, B lo
 constexpr uint32_t NSM_BYTES = UGMAX * UN * 4;  // norm * level scale, [group][weight row]
-constexpr size_t UMMA_SMEM = 1024 + USTAGES * STAGE_BYTES + NSM_BYTES + 64 + 256;
+constexpr size_t UMMA_SMEM = 1024 + USTAGES * STAGE_BYTES + NSM_BYTES + 256;
 constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every wait: one second
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -90,11 +95,15 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
 }
 
 // Wait for phase `parity` of `bar`. Gives up after WAIT_NS or as soon as
-// another role of the CTA gave up (`abort`), returning false.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort) {
+// another role of the CTA gave up (`abort`), returning false. Between polls a
+// waiter sleeps `backoff_ns` so waiting warps leave the issue slots to the
+// warps that decode weights on the same schedulers.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+                                          unsigned backoff_ns = 0) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
   while (true) {
+    if (backoff_ns) __nanosleep(backoff_ns);
     if (mbar_try(bar, parity)) return true;
     if (*abort) return false;
     if (now_ns() - t0 > WAIT_NS) {
@@ -112,7 +121,6 @@ __device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity) {
   }
 }
 
-__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -170,20 +178,17 @@ __device__ __forceinline__ int row_exp(float amax) {
   return 14 - e;
 }
 
-// Byte offset of 16-byte chunk c of row r in a 128-byte-swizzled tile.
-__device__ __forceinline__ uint32_t sw_off(int r, int c) { return (uint32_t)(r * 128 + ((c ^ (r & 7)) << 4)); }
 
-template <int BITS>
 __global__ void __launch_bounds__(UTHREADS, 1)
 cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
-               const float* __restrict__ ainv, int M, float* __restrict__ y, int ldy, int row0, int nrows) {
+               const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
+               const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
+               int nrows) {
   extern __shared__ unsigned char smraw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   float* nsm = reinterpret_cast<float*>(sm + USTAGES * STAGE_BYTES);
-  uint32_t* ltab = reinterpret_cast<uint32_t*>(sm + USTAGES * STAGE_BYTES + NSM_BYTES);  // [16] level hi|lo
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + USTAGES * STAGE_BYTES + NSM_BYTES + 64);  // weights written
-  uint64_t* afull = full + USTAGES;   // activation tiles landed (TMA transaction bytes)
-  uint64_t* empty = afull + USTAGES;  // stage consumed by the MMAs
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + USTAGES * STAGE_BYTES + NSM_BYTES);  // stage landed
+  uint64_t* empty = full + USTAGES;   // stage consumed by the MMAs
   uint64_t* tfull = empty + USTAGES;  // [2] a group's accumulator pair is complete
   uint64_t* tempty = tfull + 2;       // [2] the pair has been drained
   uint64_t* drainb = tempty + 2;      // every MMA of the CTA has completed
@@ -194,16 +199,9 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   const int n0 = blockIdx.x * UN, m0 = blockIdx.y * UM;
   const int nk = W.in_pad / UK, ng = W.in_pad / 128;
 
-  // Level scale: a power of two putting max|level| in [2^13, 2^14).
-  float lmax = 0.f;
-#pragma unroll
-  for (int i = 0; i < (1 << BITS); ++i) lmax = fmaxf(lmax, fabsf(W.levels[i]));
-  const int le = row_exp(lmax);
-
   if (tid == 0) {
     for (int s = 0; s < USTAGES; ++s) {
-      mbar_init(&full[s], 4);   // the four weight warps
-      mbar_init(&afull[s], 1);  // the TMA thread's expect_tx arrive
+      mbar_init(&full[s], 1);   // the TMA thread's expect_tx arrive
       mbar_init(&empty[s], 1);  // one tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
@@ -214,8 +212,19 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (tid < 16) ltab[tid] = split_h(ldexpf(W.levels[tid < (1 << BITS) ? tid : 0], le));
-  if (warp == 12) {
+  // Group norms of the tile's weight rows (times the inverse level scale).
+  for (int i = tid; i < ng * UN; i += UTHREADS) {
+    const int g = i / UN, nl = i % UN;
+    float v = 0.f;
+    if (n0 + nl < nrows) {
+      const uint8_t* prow;
+      const __half* pn;
+      cq_row_ptr(W, row0 + n0 + nl, &prow, &pn);
+      v = __half2float(pn[g]) * linv;
+    }
+    nsm[i] = v;
+  }
+  if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
                  "r"(512));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
@@ -225,79 +234,16 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 4) {
-    // ------------------------------------------------ weight producer
-    const int nl = tid;  // weight row of this thread within the tile
-    const int n = n0 + nl;
-    const bool valid = n < nrows;
-    const uint8_t* row = nullptr;
-    const __half* nrm = nullptr;
-    if (valid) cq_row_ptr(W, row0 + n, &row, &nrm);
-    const float linv = ldexpf(1.f, -le);
-    for (int g = 0; g < ng; ++g) nsm[g * UN + nl] = valid ? __half2float(nrm[g]) * linv : 0.f;
-    asm volatile("bar.sync 1, 384;" ::: "memory");  // norms visible to the epilogue warps
-    uint32_t t0 = 0, t1 = 0, l0 = 0, l1 = 0;  // 2-bit tables: hi pairs, lo pairs
-    if (BITS == 2) {
-      t0 = __byte_perm(ltab[0], ltab[1], 0x5410);
-      t1 = __byte_perm(ltab[2], ltab[3], 0x5410);
-      l0 = __byte_perm(ltab[0], ltab[1], 0x7632);
-      l1 = __byte_perm(ltab[2], ltab[3], 0x7632);
-    }
-    for (int kb = 0; kb < nk; ++kb) {
-      const int s = kb % USTAGES;
-      const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
-      uint4 c0 = make_uint4(0, 0, 0, 0), c1 = make_uint4(0, 0, 0, 0);
-      if (valid) {
-        const uint4* src = reinterpret_cast<const uint4*>(row + (size_t)kb * (UK * BITS / 8));
-        c0 = __ldg(src);
-        if (BITS == 4) c1 = __ldg(src + 1);
-      }
-      if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
-      unsigned char* bh = sm + s * STAGE_BYTES + 2 * TILE;
-      unsigned char* bl = bh + TILE;
-      const uint32_t cw[8] = {c0.x, c0.y, c0.z, c0.w, c1.x, c1.y, c1.z, c1.w};
-#pragma unroll
-      for (int ch = 0; ch < 8; ++ch) {  // 8 chunks of 8 elements
-        uint32_t hv[4], lv[4];
-        if (BITS == 2) {
-          const uint32_t bits16 = (cw[ch >> 1] >> ((ch & 1) * 16)) & 0xFFFFu;
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            // Two 2-bit codes c0, c1 select bytes 2c..2c+1 of the 4-entry tables.
-            const uint32_t x = (bits16 >> (4 * p)) & 0xFu;
-            const uint32_t sel = (x & 3u) * 0x22u + (x & 0xCu) * 0x880u + 0x1010u;
-            hv[p] = __byte_perm(t0, t1, sel);
-            lv[p] = __byte_perm(l0, l1, sel);
-          }
-        } else {
-          const uint32_t w32 = cw[ch];
-#pragma unroll
-          for (int p = 0; p < 4; ++p) {
-            const uint32_t a = ltab[(w32 >> (8 * p)) & 0xFu];
-            const uint32_t b = ltab[(w32 >> (8 * p + 4)) & 0xFu];
-            hv[p] = __byte_perm(a, b, 0x5410);
-            lv[p] = __byte_perm(a, b, 0x7632);
-          }
-        }
-        const uint32_t off = sw_off(nl, ch);
-        *reinterpret_cast<uint4*>(bh + off) = make_uint4(hv[0], hv[1], hv[2], hv[3]);
-        *reinterpret_cast<uint4*>(bl + off) = make_uint4(lv[0], lv[1], lv[2], lv[3]);
-      }
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&full[s]);
-    }
-  } else if (warp < 12) {
+  if (warp < 8) {
     // ------------------------------------------------ epilogue: drain each group
-    const int q = warp & 3, h = (warp - 4) >> 2;  // TMEM lane quarter, column half
-    asm volatile("bar.sync 1, 384;" ::: "memory");
+    const int q = warp & 3, h = warp >> 2;  // TMEM lane quarter, column half
     float acc[64];
 #pragma unroll
     for (int i = 0; i < 64; ++i) acc[i] = 0.f;
     bool ok = true;
     for (int g = 0; g < ng; ++g) {
       const int b = g & 1;
-      if (!mbar_wait(&tfull[b], (uint32_t)(g >> 1) & 1u, abort)) {
+      if (!mbar_wait(&tfull[b], (uint32_t)(g >> 1) & 1u, abort, 128)) {
         ok = false;
         break;
       }
@@ -335,23 +281,25 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
           if (i < lim) yr[i] = acc[i] * ai;
       }
     }
-  } else if (warp == 12) {
-    // ------------------------------------------------ activation producer (TMA)
+  } else if (warp == 8) {
+    // ------------------------------------------------ operand producer (TMA)
     if (lane == 0) {
       int issued = 0;
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % USTAGES;
         const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
-        unsigned char* ah = sm + s * STAGE_BYTES;
-        mbar_arrive_tx(&afull[s], 2 * TILE);
-        tma_load_2d(ah, &mapAh, &afull[s], kb * UK, m0);
-        tma_load_2d(ah + TILE, &mapAl, &afull[s], kb * UK, m0);
+        unsigned char* st = sm + s * STAGE_BYTES;
+        mbar_arrive_tx(&full[s], 4 * TILE);
+        tma_load_2d(st, &mapAh, &full[s], kb * UK, m0);
+        tma_load_2d(st + TILE, &mapAl, &full[s], kb * UK, m0);
+        tma_load_2d(st + 2 * TILE, &mapBh, &full[s], kb * UK, n0);
+        tma_load_2d(st + 3 * TILE, &mapBl, &full[s], kb * UK, n0);
         ++issued;
       }
       if (*abort) {  // let the copies already issued land before the CTA exits
         for (int kb = issued - USTAGES > 0 ? issued - USTAGES : 0; kb < issued; ++kb)
-          mbar_drain(&afull[kb % USTAGES], (uint32_t)(kb / USTAGES) & 1u);
+          mbar_drain(&full[kb % USTAGES], (uint32_t)(kb / USTAGES) & 1u);
       }
     }
   } else {
@@ -367,7 +315,7 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
         for (int j = 0; j < 2; ++j, ++kb) {
           const int s = kb % USTAGES;
           const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
-          if (!mbar_wait(&afull[s], ph, abort) || !mbar_wait(&full[s], ph, abort)) {
+          if (!mbar_wait(&full[s], ph, abort)) {
             ok = false;
             break;
           }
@@ -394,9 +342,40 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 12) {
+  if (warp == 8) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+  }
+}
+
+// Level high parts and remainders of rows [row0, row0 + nrows) of a CQ
+// matrix, decoded from the packed codes (cq.rs:908-925) and scaled by 2^le:
+// hi / lo [nrows][in_pad] f16. One thread per 8 weights.
+template <int BITS>
+__global__ void cq_expand_kernel(CqMat W, int row0, int nrows, int le, __half* __restrict__ whi,
+                                 __half* __restrict__ wlo) {
+  __shared__ uint32_t tab[16];  // level * 2^le as (hi | lo << 16)
+  if (threadIdx.x < 16) tab[threadIdx.x] = split_h(ldexpf(W.levels[threadIdx.x < (1 << BITS) ? threadIdx.x : 0], le));
+  __syncthreads();
+  const int per_row = W.in_pad / 8;
+  const long total = (long)nrows * per_row;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int n = (int)(i / per_row), c = (int)(i % per_row);
+    const uint8_t* prow;
+    const __half* pn;
+    cq_row_ptr(W, row0 + n, &prow, &pn);
+    uint32_t code = BITS == 2 ? (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(prow) + c)
+                              : __ldg(reinterpret_cast<const uint32_t*>(prow) + c);
+    uint32_t h[4], l[4];
+#pragma unroll
+    for (int p = 0; p < 4; ++p) {
+      const uint32_t a = tab[(code >> (2 * p * BITS)) & ((1u << BITS) - 1)];
+      const uint32_t b = tab[(code >> ((2 * p + 1) * BITS)) & ((1u << BITS) - 1)];
+      h[p] = __byte_perm(a, b, 0x5410);
+      l[p] = __byte_perm(a, b, 0x7632);
+    }
+    *reinterpret_cast<uint4*>(whi + (size_t)n * W.in_pad + c * 8) = make_uint4(h[0], h[1], h[2], h[3]);
+    *reinterpret_cast<uint4*>(wlo + (size_t)n * W.in_pad + c * 8) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
@@ -468,19 +447,43 @@ bool umma_supported(const CqMat& W) {
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                             int nrows, cudaStream_t st, const GemmScratch& gs) {
   const int K = W.in_pad;
-  if (!umma_supported(W) || !gs.hi || !gs.lo || !gs.inv || gs.elems < (size_t)M * K || gs.rows < (size_t)M)
+  if (!umma_supported(W) || !gs.hi || !gs.lo || !gs.inv || !gs.whi || !gs.wlo || gs.elems < (size_t)M * K ||
+      gs.rows < (size_t)M || gs.welems < (size_t)nrows * K)
     return cudaErrorInvalidValue;
-  if ((reinterpret_cast<uintptr_t>(gs.hi) | reinterpret_cast<uintptr_t>(gs.lo)) & 15) return cudaErrorInvalidValue;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(gs.hi) | reinterpret_cast<uintptr_t>(gs.lo) |
+                       reinterpret_cast<uintptr_t>(gs.whi) | reinterpret_cast<uintptr_t>(gs.wlo);
+  if (al & 15) return cudaErrorInvalidValue;
+  // Level scale: a power of two putting max|level| in [2^13, 2^14).
+  float lmax = 0.f;
+  for (int i = 0; i < (1 << W.bits); ++i) lmax = std::max(lmax, std::fabs(W.levels[i]));
+  int le = 0;
+  if (lmax > 0.f && std::isfinite(lmax)) {
+    int e;
+    std::frexp(lmax, &e);
+    le = 14 - e;
+  }
   split_f16_kernel<<<(M + 7) / 8, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv);
-  cudaError_t e0 = cudaGetLastError();
-  if (e0 != cudaSuccess) return e0;
-  CUtensorMap mh, ml;
-  if (!make_map(&mh, gs.hi, M, K) || !make_map(&ml, gs.lo, M, K)) return cudaErrorNotSupported;
-  auto kern = W.bits == 2 ? cq_umma_kernel<2> : cq_umma_kernel<4>;
-  cudaError_t e = allow_smem((const void*)kern, UMMA_SMEM);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  {
+    const long total = (long)nrows * (K / 8);
+    const int blocks = (int)std::min<long>((total + 255) / 256, 148L * 8);
+    if (W.bits == 2)
+      cq_expand_kernel<2><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, gs.wlo);
+    else
+      cq_expand_kernel<4><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, gs.wlo);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+  }
+  CUtensorMap mah, mal, mbh, mbl;
+  if (!make_map(&mah, gs.hi, M, K) || !make_map(&mal, gs.lo, M, K) || !make_map(&mbh, gs.whi, nrows, K) ||
+      !make_map(&mbl, gs.wlo, nrows, K))
+    return cudaErrorNotSupported;
+  e = allow_smem((const void*)cq_umma_kernel, UMMA_SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid((nrows + UN - 1) / UN, (M + UM - 1) / UM);
-  kern<<<grid, UTHREADS, UMMA_SMEM, st>>>(W, mh, ml, gs.inv, M, y, ldy, row0, nrows);
+  cq_umma_kernel<<<grid, UTHREADS, UMMA_SMEM, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy,
+                                                    row0, nrows);
   return cudaGetLastError();
 }
 
