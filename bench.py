@@ -265,6 +265,135 @@ def gemv_bandwidth(nb, torch, stream):
     return out
 
 
+def _event_us(torch, fn, reps):
+    """Mean device time of fn() in microseconds (CUDA events on the current stream, warm)."""
+    fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps * 1e3
+
+
+def kernel_configs(nb, torch, raw, hbm, bf16):
+    """BASELINE configs 1-3 on this GPU beside the oracle (the C++ restatement
+    of the reference CPU path) on the host cores, each on a bounded sample."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as orc
+    from needle_b200 import cact_pack
+    ncpu = os.cpu_count() or 1
+    orc.set_threads(ncpu)
+    st = torch.cuda.current_stream().cuda_stream
+    out = {}
+    # ---- config 1: X [512, 768] x W [N, 768] 2-bit g128 (tensor-core path)
+    rng = np.random.default_rng(0)
+    cb = cact_pack.random_codebook(rng)
+    lv = cact_pack.codebook_levels(cb, 2)
+    x = rng.normal(size=(512, 768)).astype(np.float32)
+    c1 = {}
+    for n_out in (768, 2304, 3072):
+        idx, norms = cact_pack.random_cq(np.random.default_rng(n_out), n_out, 768, 2)
+        blob = cact_pack.cq_blob(idx, norms, 2)
+        w = orc.CqWeight(blob, n_out, 768, 2, cb)
+        xh = np.stack([w.prepare(r) for r in x])
+        d = torch.from_numpy(np.frombuffer(blob, np.uint8).copy()).cuda()
+        xd = torch.from_numpy(xh).cuda()
+        y = torch.zeros(512, n_out, device="cuda")
+        us = _event_us(torch, lambda: nb.cq_project(d.data_ptr(), d.data_ptr() + n_out * 192, n_out, 768, 2, lv,
+                                                    xd.data_ptr(), 768, 512, y.data_ptr(), n_out, stream=st), 50)
+        flop = 2 * 512 * 768 * n_out
+        t0 = time.perf_counter()
+        w.matmul_prepared(xh)
+        cpu_s = time.perf_counter() - t0
+        c1[str(n_out)] = {"us": round(us, 2), "tflops": round(flop / us / 1e6, 2),
+                          "frac_of_bf16_peak": round(flop / us / 1e6 / bf16, 4),
+                          "cpu_us": round(cpu_s * 1e6, 1), "cpu_cores": ncpu}
+    out["config1_gemm"] = {"metric": "X[512,768] x W[N,768] 2-bit CQ projection (tensor cores, f16 hi/lo split)",
+                           "roofline": "tensor (bf16 dense peak, measured)", "by_n": c1}
+    # ---- config 2: standalone int8 decode attention, 64 sessions x ctx 512
+    B, S, H, KVH, QK, VH = 64, 512, 12, 2, 48, 64
+    r2 = np.random.default_rng(0)
+    q = r2.normal(size=(B, H, QK)).astype(np.float32)
+    kf = r2.normal(size=(B, S, KVH, QK)).astype(np.float32)
+    vf = r2.normal(size=(B, S, KVH, VH)).astype(np.float32)
+    kq = np.zeros((B, S, KVH, QK), np.int8)
+    vq = np.zeros((B, S, KVH, VH), np.int8)
+    ks = np.zeros((B, S, KVH), np.float32)
+    vs = np.zeros((B, S, KVH), np.float32)
+    for b in range(B):
+        for s in range(S):
+            for h in range(KVH):
+                kq[b, s, h], ks[b, s, h] = orc.quant_into(kf[b, s, h])
+                vq[b, s, h], vs[b, s, h] = orc.quant_into(vf[b, s, h])
+    qf = np.stack([np.stack([orc.fake_quant(q[b, h]) for h in range(H)]) for b in range(B)]).astype(np.float32)
+    dv = {k_: torch.from_numpy(np.ascontiguousarray(a)).cuda() for k_, a in
+          dict(q=qf, k=kq, v=vq, ks=ks, vs=vs, lo=np.zeros(B, np.int32), hi=np.full(B, S - 1, np.int32)).items()}
+    o2 = torch.zeros(B, H * VH, device="cuda")
+    us = _event_us(torch, lambda: nb.attend_step(dv["q"].data_ptr(), dv["k"].data_ptr(), dv["v"].data_ptr(),
+                                                 dv["ks"].data_ptr(), dv["vs"].data_ptr(), True, S,
+                                                 dv["lo"].data_ptr(), dv["hi"].data_ptr(), B, H, KVH, QK, VH,
+                                                 o2.data_ptr(), stream=st), 100)
+    algo = B * (S * KVH * (QK + VH + 8) + H * QK * 4 + H * VH * 4)
+    t0 = time.perf_counter()
+    for b in range(B):
+        orc.attend_step(qf[b].ravel(), S, 0, S - 1, H, KVH, QK, VH, kq=kq[b], ks=ks[b], vq=vq[b], vs=vs[b])
+    cpu_s = time.perf_counter() - t0
+    out["config2_attention"] = {"metric": "int8 decode attention, 64 sessions x ctx 512 (nd_attend_step)",
+                                "us": round(us, 2), "algorithmic_bytes": algo,
+                                "gbs": round(algo / us / 1e3, 1), "frac_of_hbm_peak": round(algo / us / 1e3 / hbm, 4),
+                                "note": "8.2 MB fits in L2; the HBM figure is the conservative denominator",
+                                "cpu_us": round(cpu_s * 1e6, 1), "cpu_cores": 1}
+    # ---- config 3: batch 1, 256-token prompt, 64 greedy tokens, f32 and int8 KV
+    eng1 = nb.V3Engine.from_bytes(raw)
+    p3 = prompt(0, 256)
+    c3 = {}
+    m = orc.Model(raw)
+    for int8 in (False, True):
+        eng1.generate_ids(p3, 64, kv_int8=int8)  # warm
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        s = eng1.session(320, int8)
+        s.prefill(p3)
+        torch.cuda.synchronize()
+        pre_s = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        ids = eng1.generate_ids(p3, 64, kv_int8=int8)
+        gen_s = time.perf_counter() - t0
+        # device-resident batch-1 decode: one session stepped as a CUDA-graph batch
+        s2 = eng1.session(320, int8)
+        _, pk = eng1.prefill_batch([s2], [p3], logits=False)
+        bt = eng1.batch([s2])
+        bt.set_tokens(pk)
+        for _ in range(3):
+            bt.step(None, stream=st)
+            bt.feed_next(stream=st)
+        us_tok = _event_us(torch, lambda: (bt.step(None, stream=st), bt.feed_next(stream=st)), 40)
+        # oracle: prefill + 64 decode steps, all host cores
+        so = m.session(320, int8)
+        t0 = time.perf_counter()
+        so.prefill(p3)
+        cpu_pre = time.perf_counter() - t0
+        t0 = time.perf_counter()
+        tok = int(np.argmax(so.decode_step(int(ids[0]))))
+        for i in range(1, 16):
+            so.decode_step(int(ids[i]))
+        cpu_dec = (time.perf_counter() - t0) / 16
+        c3["int8" if int8 else "f32"] = {
+            "prefill_ms": round(pre_s * 1e3, 2), "generate_64_tok_per_s_host_api": round(64 / gen_s, 1),
+            "decode_us_per_token_graph": round(us_tok, 1), "decode_tok_per_s_graph": round(1e6 / us_tok, 1),
+            "cpu_prefill_ms": round(cpu_pre * 1e3, 1), "cpu_decode_tok_per_s": round(1 / cpu_dec, 1),
+            "cpu_cores": ncpu, "cpu_sample": "oracle prefill of the 256-token prompt + 16 decode steps"}
+        del bt, s, s2, so
+    out["config3_batch1"] = {"metric": "batch-1 forward: 256-token prompt, greedy decode",
+                             "roofline": "L2 / latency (17.6 MB of weights per token stay L2-resident)",
+                             "by_kv": c3}
+    del eng1, m
+    return out
+
+
 def attn_traffic_per_unit():
     """DRAM bytes per (position, KV head) of the decode attention kernel from
     the committed ncu summary (dram__bytes_read.sum + dram__bytes_write.sum of
@@ -312,6 +441,7 @@ def main():
     ap.add_argument("--sessions", type=int, default=4096, help="total sessions (config 4: 4096)")
     ap.add_argument("--prompt", type=int, default=1024)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-configs", action="store_true", help="skip the BASELINE config 1-3 measurements")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -334,8 +464,9 @@ def main():
     raw = container(0)
     eng = nb.V3Engine.from_bytes(raw)
     geo = eng.geometry
-    per = args.sessions // world
-    s0 = rank * per
+    from needle_b200.shard import max_over_ranks, session_range
+    s0, s1 = session_range(args.sessions, world, rank)
+    per = s1 - s0
     gen_budget = 2 * (args.warmup + args.steps) + 4
     hint = args.prompt + max(128, gen_budget)
     sessions = [eng.session(hint, True) for _ in range(per)]
@@ -373,13 +504,9 @@ def main():
             batch.feed_next(stream=st)
         e1.record(stream)
         torch.cuda.synchronize()
-    dev_s = e0.elapsed_time(e1) * 1e-3
-    if dist:
-        t = torch.tensor([dev_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        dev_s = float(t.item())
-        torch.cuda.synchronize()
-    value = args.sessions * args.steps / dev_s if world > 1 else per * args.steps / dev_s
+    dev_s = max_over_ranks(e0.elapsed_time(e1) * 1e-3, dist, "cuda")
+    torch.cuda.synchronize()
+    value = args.sessions * args.steps / dev_s
     # ---- per-kernel profile of one step (eager, events between kernel groups)
     prof, launches = batch.profile()
     pos_now = sessions[0].pos - 1
@@ -393,12 +520,8 @@ def main():
     t0 = time.perf_counter()
     for _ in range(args.steps):
         _, toks = eng.decode_batch(sessions, toks, logits=False)
-    e2e_s = time.perf_counter() - t0
-    if dist:
-        t = torch.tensor([e2e_s], device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_s = float(t.item())
-    e2e = args.sessions * args.steps / e2e_s if world > 1 else per * args.steps / e2e_s
+    e2e_s = max_over_ranks(time.perf_counter() - t0, dist, "cuda")
+    e2e = args.sessions * args.steps / e2e_s
     hbm, bf16, src = peaks()
     attn_ms = prof["attention"] / geo["layers"]
     abytes = attn_bytes_per_step(geo, per, pos_now) / geo["layers"]
@@ -408,6 +531,8 @@ def main():
     extra = {}
     if rank == 0:
         extra["gemv_config0"] = gemv_bandwidth(nb, torch, st)
+        if not args.no_configs:
+            extra["configs"] = kernel_configs(nb, torch, raw, hbm, bf16)
         if not args.no_cpu_baseline:
             tps, cores, secs, sample = cpu_decode_sample(raw, args.prompt, 8)
             extra["cpu_baseline"] = {"value": round(tps, 3), "unit": "tok/s", "cores": cores, "kind": "port",

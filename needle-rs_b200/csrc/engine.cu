@@ -552,6 +552,26 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
   }
   for (size_t s = 0; s < c.sites.size(); ++s) E->eng_taps.push_back(P + etaps[s]);
   E->final_norm = P + fnorm;
+  // HadamardMLP weight fragments for the tensor-core block tail.
+  for (size_t l = 0; l < c.layers; ++l) E->lp[l].hfrag = nullptr;
+  if (hada_tc_supported((int)ba, (int)bb)) {
+    const size_t fw = hada_frag_words((int)ba);
+    std::vector<uint32_t> frags(fw * c.layers);
+    for (size_t l = 0; l < c.layers; ++l) {
+      const LOff& o = lo[l];
+      // Stage order per Kronecker pair: B^T (w*b) then A^T (w*a).
+      const float* mats[6] = {&L.arena[o.mlp[6]], &L.arena[o.mlp[5]], &L.arena[o.mlp[8]],
+                              &L.arena[o.mlp[7]], &L.arena[o.mlp[10]], &L.arena[o.mlp[9]]};
+      hada_frags(mats, (int)ba, frags.data() + l * fw, E->lp[l].hinv);
+    }
+    e = cudaMalloc(&E->d_hfrag, frags.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(E->d_hfrag, frags.data(), frags.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("uploading HadamardMLP fragments", e);
+      return nullptr;
+    }
+    for (size_t l = 0; l < c.layers; ++l) E->lp[l].hfrag = E->d_hfrag + l * fw;
+  }
 
   Geo& g = E->G;
   g.d = (int)d;
@@ -605,6 +625,7 @@ Engine::~Engine() {
   if (d_params) cudaFree(d_params);
   if (d_perm) cudaFree(d_perm);
   if (d_rope) cudaFree(d_rope);
+  if (d_hfrag) cudaFree(d_hfrag);
   if (d_tables) cudaFree(d_tables);
   if (h_wait_flag) cudaFreeHost(h_wait_flag);
   if (stream) cudaStreamDestroy(stream);

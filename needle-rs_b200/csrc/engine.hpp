@@ -144,6 +144,7 @@ class Engine {
   float* d_params = nullptr;
   uint32_t* d_perm = nullptr;
   float* d_rope = nullptr;
+  uint32_t* d_hfrag = nullptr;  // HadamardMLP weight fragments, all layers
   CqMat emb{}, phi_pre{}, phi_post{}, phi_res{};
   std::vector<CqMat> qkvg, outp, eng_kv, eng_tables;
   CqMat* d_tables = nullptr;

@@ -23,6 +23,12 @@ struct LayerParams {
   float attn_gate;
   const float *d1, *d2, *b2, *d3, *d4, *w1a, *w1b, *w2a, *w2b, *w3a, *w3b, *cond_v, *cond_u;
   int window;  // attention span, 0 = unbounded (config.rs:216)
+  // HadamardMLP weight fragments for the tensor-core tail (B^T and A^T of the
+  // three Kronecker pairs, high parts and remainders in mma lane order) and
+  // their inverse power-of-two scales; null when the factors are not square
+  // 16x16 or 32x32.
+  const uint32_t* hfrag;
+  float hinv[6];
 };
 
 struct MhcParams {
@@ -107,6 +113,13 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
                               const uint32_t* p1, const uint32_t* p2, const float* projo,
                               const float* u, float* bx, const float* gates, float* lanes,
                               cudaStream_t st);
+// Tensor-core block tail (post_kernels.cu) and the host-side fragment builder.
+bool hada_tc_supported(int ba, int bb);
+size_t hada_frag_words(int D);
+void hada_frags(const float* const* mats, int D, uint32_t* out, float* inv);
+cudaError_t launch_layer_post_tc(const Geo& G, const RowBatch& rb, const LayerParams& lp, const uint32_t* p1,
+                                 const uint32_t* p2, const float* projo, const float* u, float* bx,
+                                 const float* gates, float* lanes, cudaStream_t st);
 cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
                          const float* final_norm, float* lm_in, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st);

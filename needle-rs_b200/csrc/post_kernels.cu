@@ -1,0 +1,473 @@
+// Block tail of a Needle-3 layer with the HadamardMLP on the tensor cores.
+//
+// model.rs:309-356: post_norm + gated residual, pre_hada norm, the
+// HadamardMLP (v3/kernels.rs:119-180), MLP residual, y = block - u and
+// scatter_up (mhc.rs:109-158) back into the lanes. One warp per activation row.
+//
+// Each Kronecker apply out = A^T Z B (kernels.rs:41-78; Z is the 1024-vector
+// as a D x D matrix, D = 32 on the shipped geometry) runs as two D x D x D
+// products on mma.sync m16n8k16 (f16 in, f32 accumulate):
+//   stage 1   T^T[l][i] = sum_j B[j][l] Z[i][j]     (A operand B^T, B operand Z^T)
+//   stage 2   out[k][l] = sum_i A[i][k] T[i][l]     (A operand A^T, B operand T)
+// Computing stage 1 transposed makes its accumulator fragments exactly the B
+// fragments of stage 2, so T never leaves registers. Every operand is split
+// into an f16 high part and remainder (x_hi*w_hi + x_hi*w_lo + x_lo*w_hi) after
+// a power-of-two scale that keeps the remainders normal; each accumulator sums
+// only K = D products over 3 * D/16 MMAs, so the tensor cores' truncating
+// accumulation stays at f32 rounding level. The weight fragments (high part
+// and remainder, in mma lane order) are built once at load time.
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstring>
+#include <vector>
+
+#include "common.cuh"
+#include "kernels.hpp"
+#include "launch_util.hpp"
+
+namespace nb {
+
+namespace {
+
+constexpr float EPS = 1e-6f;  // kernels.rs:11, norm.rs:6
+
+__host__ __device__ inline int pow2_exp(float amax) {
+  // Power of two that brings max|v| into [2^13, 2^14) (0 for an all-zero input).
+  if (!(amax > 0.f) || !std::isfinite(amax)) return 0;
+  int e;
+  std::frexp(amax, &e);
+  return 14 - e;
+}
+
+__device__ __forceinline__ uint32_t split_h2(float x, float y, uint32_t* lo) {
+  const __half2 h = __floats2half2_rn(x, y);
+  const __half2 l = __floats2half2_rn(x - __low2float(h), y - __high2float(h));
+  *lo = *reinterpret_cast<const uint32_t*>(&l);
+  return *reinterpret_cast<const uint32_t*>(&h);
+}
+
+__device__ __forceinline__ void mma16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Padded D x (D + 4) storage of a D x D matrix: element c = r * D + s at
+// r * (D + 4) + s, so fragment loads of consecutive rows hit distinct banks.
+template <int D>
+__device__ __forceinline__ int pad_idx(int c) {
+  return (c / D) * (D + 4) + c % D;
+}
+
+// One Kronecker apply for this warp. zb: the input, each element packed as
+// (f16 high part | f16 remainder << 16) in padded layout, the true value being
+// the stored one times invz. fb receives the f32 output in padded layout.
+// fB / fA: weight fragments of B^T and A^T (true weight = fragment * inv).
+template <int D>
+__device__ void kron_tc(const uint32_t* __restrict__ fB, float invB, const uint32_t* __restrict__ fA,
+                        float invA, const uint32_t* zb, float invz, float* fb) {
+  constexpr int MT = D / 16, NT = D / 8, KS = D / 16, P = D + 4;
+  const int lane = threadIdx.x & 31, g = lane >> 2, t = lane & 3;
+  float c1[MT][NT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) c1[m][n][0] = c1[m][n][1] = c1[m][n][2] = c1[m][n][3] = 0.f;
+  // ---- stage 1: T^T[l][i] = sum_j Bt[l][j] Z^T[j][i]
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const uint32_t* zr = zb + (8 * n + g) * P + 16 * ks + 2 * t;
+      const uint2 e01 = *reinterpret_cast<const uint2*>(zr);
+      const uint2 e89 = *reinterpret_cast<const uint2*>(zr + 8);
+      bh[n][0] = __byte_perm(e01.x, e01.y, 0x5410);
+      bl[n][0] = __byte_perm(e01.x, e01.y, 0x7632);
+      bh[n][1] = __byte_perm(e89.x, e89.y, 0x5410);
+      bl[n][1] = __byte_perm(e89.x, e89.y, 0x7632);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint4* fr = reinterpret_cast<const uint4*>(fB + ((m * KS + ks) * 32 + lane) * 8);
+      const uint4 h4 = __ldg(fr), l4 = __ldg(fr + 1);
+      const uint32_t ah[4] = {h4.x, h4.y, h4.z, h4.w}, al[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma16816(c1[m][n], ah, bh[n][0], bh[n][1]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma16816(c1[m][n], ah, bl[n][0], bl[n][1]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma16816(c1[m][n], al, bh[n][0], bh[n][1]);
+    }
+  }
+  // ---- rescale T for the f16 split of stage 2
+  float amax = 0.f;
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) amax = fmaxf(amax, fabsf(c1[m][n][e]));
+  amax = warp_max(amax);
+  const int et = pow2_exp(amax);
+  const float st = ldexpf(1.f, et);
+  // ---- stage 2: out[k][l] = sum_i At[k][i] T[i][l]; B (i, l) = c1 tile (l/16, i/8)
+  float c2[MT][NT][4];
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) c2[m][n][0] = c2[m][n][1] = c2[m][n][2] = c2[m][n][3] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < KS; ++ks) {
+    uint32_t bh[NT][2], bl[NT][2];
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int m1 = n >> 1, h = (n & 1) * 2;  // rows l = 8n + g of c1 m-tile n/2
+      bh[n][0] = split_h2(c1[m1][2 * ks][h] * st, c1[m1][2 * ks][h + 1] * st, &bl[n][0]);
+      bh[n][1] = split_h2(c1[m1][2 * ks + 1][h] * st, c1[m1][2 * ks + 1][h + 1] * st, &bl[n][1]);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+      const uint4* fr = reinterpret_cast<const uint4*>(fA + ((m * KS + ks) * 32 + lane) * 8);
+      const uint4 h4 = __ldg(fr), l4 = __ldg(fr + 1);
+      const uint32_t ah[4] = {h4.x, h4.y, h4.z, h4.w}, al[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma16816(c2[m][n], ah, bh[n][0], bh[n][1]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma16816(c2[m][n], ah, bl[n][0], bl[n][1]);
+#pragma unroll
+      for (int n = 0; n < NT; ++n) mma16816(c2[m][n], al, bh[n][0], bh[n][1]);
+    }
+  }
+  const float inv = invz * invB * ldexpf(1.f, -et) * invA;
+#pragma unroll
+  for (int m = 0; m < MT; ++m)
+#pragma unroll
+    for (int n = 0; n < NT; ++n) {
+      const int k = 16 * m + g, l = 8 * n + 2 * t;
+      *reinterpret_cast<float2*>(fb + k * P + l) = make_float2(c2[m][n][0] * inv, c2[m][n][1] * inv);
+      *reinterpret_cast<float2*>(fb + (k + 8) * P + l) = make_float2(c2[m][n][2] * inv, c2[m][n][3] * inv);
+    }
+  __syncwarp();
+}
+
+// Converts this warp's row, held as f32 in zb (padded layout), to packed
+// f16 high part | remainder with the power-of-two scale of `amax`; returns the
+// inverse scale.
+template <int D>
+__device__ __forceinline__ float pack_row(uint32_t* zb, float amax) {
+  constexpr int N = D * D;
+  const int lane = threadIdx.x & 31;
+  const int e = pow2_exp(amax);
+  const float s = ldexpf(1.f, e);
+  for (int c = lane; c < N; c += 32) {
+    const int pi = pad_idx<D>(c);
+    const float x = __uint_as_float(zb[pi]) * s;
+    const __half h = __float2half_rn(x);
+    const __half l = __float2half_rn(x - __half2float(h));
+    zb[pi] = (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
+  }
+  __syncwarp();
+  return ldexpf(1.f, -e);
+}
+
+constexpr int PW = 8;       // rows (warps) per CTA
+constexpr int PT = PW * 32;  // threads
+
+template <int D>
+struct PostSmem {
+  static constexpr int P = D + 4;
+  uint32_t zb[PW][D * P];  // Kronecker input (f32 while built, then f16 hi|lo)
+  float fb[PW][D * P];     // Kronecker output
+  float pr[PW][8];         // conditioning weights per row
+  float part[PW][PW][8];   // per-warp partial sums: [warp][row][j]
+  float amax[PW][PW];      // per-warp partial maxima: [warp][row]
+  float inv2[PW];
+};
+
+// Block max over the eight warps of per-row partials red[warp][row].
+__device__ __forceinline__ float rows_max(float (*red)[PW], int row) {
+  float m = 0.f;
+#pragma unroll
+  for (int w = 0; w < PW; ++w) m = fmaxf(m, red[w][row]);
+  return m;
+}
+
+// The CTA owns PW consecutive rows. Phases alternate between element-parallel
+// work (thread tid covers elements tid, tid + PT, ... of every row, so each
+// parameter element is loaded once per PW rows) and one Kronecker apply per
+// warp on its own row.
+template <int D>
+__global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, LayerParams lp,
+                                                           const uint32_t* __restrict__ p1,
+                                                           const uint32_t* __restrict__ p2,
+                                                           const float* __restrict__ projo,
+                                                           const float* __restrict__ u,
+                                                           const float* __restrict__ bx_in,
+                                                           const float* __restrict__ gates,
+                                                           float* __restrict__ lanes) {
+  constexpr int N = D * D;
+  extern __shared__ __align__(16) unsigned char post_smem[];
+  auto& S = *reinterpret_cast<PostSmem<D>*>(post_smem);
+  float* s1all = reinterpret_cast<float*>(post_smem + sizeof(PostSmem<D>));  // [PW][d]
+  const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+  const int r0 = blockIdx.x * PW;
+  const int nrow = min(PW, rb.M - r0);
+  const int d = G.d, nl = G.lanes, rk = G.cond_rank;
+
+  // ---- per row (warp w): post_norm + gated residual (model.rs:309-316), s1 and its rms
+  if (w < nrow) {
+    const int r = r0 + w;
+    const float* po = projo + (size_t)r * d;
+    const float* bx = bx_in + (size_t)r * d;
+    float* s1 = s1all + (size_t)w * d;
+    float ss = 0.f;
+#pragma unroll 4
+    for (int c = lane; c < d; c += 32) ss += po[c] * po[c];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)d + EPS);
+    const float ag = sigmoidf_(lp.attn_gate);
+    float s2 = 0.f;
+#pragma unroll 4
+    for (int c = lane; c < d; c += 32) {
+      const float v = bx[c] + ag * ((1.0f + lp.post_norm[c]) * po[c] * inv);
+      s1[c] = v;
+      s2 += v * v;
+    }
+    s2 = warp_sum(s2);
+    if (lane == 0) S.inv2[w] = 1.0f / sqrtf(s2 / (float)d + EPS);
+  }
+  __syncthreads();
+  // ---- element-parallel: t = pre_hada norm, z = t * d1, logits t . cond_v
+  {
+    float acc[PW][8], mz[PW];
+#pragma unroll
+    for (int i = 0; i < PW; ++i) {
+      mz[i] = 0.f;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    }
+    for (int c = tid; c < N; c += PT) {
+      const int pi = pad_idx<D>(c);
+      if (c < d) {
+        const float ph = 1.0f + lp.pre_hada[c], dd = lp.d1[c];
+        float cv[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cv[j] = j < rk ? lp.cond_v[c * rk + j] : 0.f;
+#pragma unroll
+        for (int i = 0; i < PW; ++i) {
+          if (i >= nrow) break;
+          const float tc = ph * s1all[i * d + c] * S.inv2[i];
+#pragma unroll
+          for (int j = 0; j < 8; ++j) acc[i][j] += tc * cv[j];
+          const float z = tc * dd;
+          mz[i] = fmaxf(mz[i], fabsf(z));
+          S.zb[i][pi] = __float_as_uint(z);
+        }
+      } else {
+#pragma unroll
+        for (int i = 0; i < PW; ++i) S.zb[i][pi] = 0u;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PW; ++i) {
+      const float m = warp_max(mz[i]);
+      if (lane == 0) S.amax[w][i] = m;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const float v = warp_sum(acc[i][j]);
+        if (lane == 0) S.part[w][i][j] = v;
+      }
+    }
+  }
+  __syncthreads();
+  // conditioning softmax per row (one lane per row)
+  if (tid < nrow) {
+    float lg[8], mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      float v = 0.f;
+#pragma unroll
+      for (int ww = 0; ww < PW; ++ww) v += S.part[ww][tid][j];
+      lg[j] = v;
+      if (j < rk) mx = fmaxf(mx, v);
+    }
+    float sum = 0.f;
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+      if (j < rk) {
+        lg[j] = expf(lg[j] - mx);
+        sum += lg[j];
+      }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) S.pr[tid][j] = j < rk ? lg[j] / sum : 0.f;
+  }
+  constexpr int FR = (D / 16) * (D / 16) * 32 * 8;  // u32 per weight fragment block
+  // ---- Kronecker 1 (warp per row)
+  if (w < nrow) {
+    const float iz = pack_row<D>(S.zb[w], rows_max(S.amax, w));
+    kron_tc<D>(lp.hfrag, lp.hinv[0], lp.hfrag + FR, lp.hinv[1], S.zb[w], iz, S.fb[w]);
+  }
+  __syncthreads();
+  // ---- element-parallel: silu(d2 * cond * out[p1] + b2), cond = 1 + pr . cond_u
+  {
+    float mz[PW];
+#pragma unroll
+    for (int i = 0; i < PW; ++i) mz[i] = 0.f;
+    for (int c = tid; c < N; c += PT) {
+      float cu[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cu[j] = j < rk ? lp.cond_u[j * N + c] : 0.f;
+      const float d2 = lp.d2[c], b2 = lp.b2[c];
+      const int src = pad_idx<D>(p1[c]), pi = pad_idx<D>(c);
+#pragma unroll
+      for (int i = 0; i < PW; ++i) {
+        if (i >= nrow) break;
+        float cv = 1.0f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j)
+          if (j < rk && S.pr[i][j] != 0.0f) cv += S.pr[i][j] * cu[j];
+        const float v = d2 * cv * S.fb[i][src] + b2;
+        const float z = v * sigmoidf_(v);  // silu, ops.rs:118
+        mz[i] = fmaxf(mz[i], fabsf(z));
+        S.zb[i][pi] = __float_as_uint(z);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PW; ++i) {
+      const float m = warp_max(mz[i]);
+      if (lane == 0) S.amax[w][i] = m;
+    }
+  }
+  __syncthreads();
+  // ---- Kronecker 2
+  if (w < nrow) {
+    const float iz = pack_row<D>(S.zb[w], rows_max(S.amax, w));
+    kron_tc<D>(lp.hfrag + 2 * FR, lp.hinv[2], lp.hfrag + 3 * FR, lp.hinv[3], S.zb[w], iz, S.fb[w]);
+  }
+  __syncthreads();
+  // ---- element-parallel: out[p2] * d3
+  {
+    float mz[PW];
+#pragma unroll
+    for (int i = 0; i < PW; ++i) mz[i] = 0.f;
+    for (int c = tid; c < N; c += PT) {
+      const float d3 = lp.d3[c];
+      const int src = pad_idx<D>(p2[c]), pi = pad_idx<D>(c);
+#pragma unroll
+      for (int i = 0; i < PW; ++i) {
+        if (i >= nrow) break;
+        const float z = S.fb[i][src] * d3;
+        mz[i] = fmaxf(mz[i], fabsf(z));
+        S.zb[i][pi] = __float_as_uint(z);
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < PW; ++i) {
+      const float m = warp_max(mz[i]);
+      if (lane == 0) S.amax[w][i] = m;
+    }
+  }
+  __syncthreads();
+  // ---- Kronecker 3
+  if (w < nrow) {
+    const float iz = pack_row<D>(S.zb[w], rows_max(S.amax, w));
+    kron_tc<D>(lp.hfrag + 4 * FR, lp.hinv[4], lp.hfrag + 5 * FR, lp.hinv[5], S.zb[w], iz, S.fb[w]);
+  }
+  __syncthreads();
+  // ---- element-parallel: MLP residual, y = block - u, scatter_up into the lanes
+  for (int c = tid; c < d; c += PT) {
+    const float d4 = lp.d4[c];
+    const int pi = pad_idx<D>(c);
+#pragma unroll
+    for (int i = 0; i < PW; ++i) {
+      if (i >= nrow) break;
+      const int r = r0 + i;
+      const float* gs = gates + (size_t)r * 24;
+      const float b2v = s1all[i * d + c] + S.fb[i][pi] * d4;
+      const float y = b2v - u[(size_t)r * d + c];
+      float* lr = lanes + (size_t)r * nl * d;
+      float lv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) lv[j] = j < nl ? lr[j * d + c] : 0.f;
+#pragma unroll
+      for (int a = 0; a < 4; ++a) {
+        if (a >= nl) break;
+        float accv = 0.f;
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          if (j < nl) accv += gs[nl + a * nl + j] * lv[j];
+        lr[a * d + c] = accv + gs[a] * y;
+      }
+    }
+  }
+}
+
+// Weight fragments of one D x D matrix W used as the mma A operand with
+// element (m, k) = W[k][m], scaled by 2^e: [D/16][D/16][32 lanes][4 hi, 4 lo].
+void frag_block(const float* W, int D, int e, uint32_t* out) {
+  const int MT = D / 16, KS = D / 16;
+  const float s = std::ldexp(1.f, e);
+  for (int mt = 0; mt < MT; ++mt)
+    for (int ks = 0; ks < KS; ++ks)
+      for (int lane = 0; lane < 32; ++lane) {
+        const int g = lane >> 2, t = lane & 3;
+        auto el = [&](int m, int k) { return W[k * D + m] * s; };
+        const int m0 = 16 * mt + g, k0 = 16 * ks + 2 * t;
+        const float v[8] = {el(m0, k0),     el(m0, k0 + 1),     el(m0 + 8, k0),     el(m0 + 8, k0 + 1),
+                            el(m0, k0 + 8), el(m0, k0 + 9), el(m0 + 8, k0 + 8), el(m0 + 8, k0 + 9)};
+        uint32_t* o = out + ((mt * KS + ks) * 32 + lane) * 8;
+        for (int i = 0; i < 4; ++i) {
+          const __half h0 = __float2half_rn(v[2 * i]), h1 = __float2half_rn(v[2 * i + 1]);
+          const __half l0 = __float2half_rn(v[2 * i] - __half2float(h0));
+          const __half l1 = __float2half_rn(v[2 * i + 1] - __half2float(h1));
+          o[i] = (uint32_t)__half_as_ushort(h0) | ((uint32_t)__half_as_ushort(h1) << 16);
+          o[4 + i] = (uint32_t)__half_as_ushort(l0) | ((uint32_t)__half_as_ushort(l1) << 16);
+        }
+      }
+}
+
+}  // namespace
+
+bool hada_tc_supported(int ba, int bb) { return ba == bb && (ba == 16 || ba == 32); }
+
+size_t hada_frag_words(int D) { return 6 * (size_t)(D / 16) * (D / 16) * 32 * 8; }
+
+void hada_frags(const float* const* mats, int D, uint32_t* out, float* inv) {
+  const size_t fr = hada_frag_words(D) / 6;
+  for (int i = 0; i < 6; ++i) {
+    float amax = 0.f;
+    for (int k = 0; k < D * D; ++k) amax = std::fmax(amax, std::fabs(mats[i][k]));
+    const int e = pow2_exp(amax);
+    frag_block(mats[i], D, e, out + i * fr);
+    inv[i] = std::ldexp(1.f, -e);
+  }
+}
+
+cudaError_t launch_layer_post_tc(const Geo& G, const RowBatch& rb, const LayerParams& lp, const uint32_t* p1,
+                                 const uint32_t* p2, const float* projo, const float* u, float* bx,
+                                 const float* gates, float* lanes, cudaStream_t st) {
+  if (rb.M <= 0) return cudaSuccess;
+  if (!lp.hfrag || G.lanes > 4 || G.cond_rank > 8 || G.cond_rank < 1 || G.ba != G.bb || G.hada_n < G.d)
+    return cudaErrorInvalidValue;
+  const dim3 grid((rb.M + PW - 1) / PW);
+  if (G.ba == 32) {
+    const size_t smem = sizeof(PostSmem<32>) + (size_t)PW * G.d * 4;
+    cudaError_t e = allow_smem((const void*)layer_post_tc_kernel<32>, smem);
+    if (e != cudaSuccess) return e;
+    layer_post_tc_kernel<32><<<grid, PW * 32, smem, st>>>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes);
+  } else if (G.ba == 16) {
+    const size_t smem = sizeof(PostSmem<16>) + (size_t)PW * G.d * 4;
+    cudaError_t e = allow_smem((const void*)layer_post_tc_kernel<16>, smem);
+    if (e != cudaSuccess) return e;
+    layer_post_tc_kernel<16><<<grid, PW * 32, smem, st>>>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes);
+  } else {
+    return cudaErrorInvalidValue;
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace nb

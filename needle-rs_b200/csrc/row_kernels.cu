@@ -966,6 +966,7 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
                               const float* u, float* bx, const float* gates, float* lanes,
                               cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
+  if (lp.hfrag) return launch_layer_post_tc(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
   if (G.lanes > 4 || G.cond_rank > 8) return cudaErrorInvalidValue;
   const size_t smem =
       (size_t)(2 * G.d + 4 * G.hada_n + 4 * G.bb + G.ba * G.ba + G.bb * G.bb + 32 + 8 + 24) * sizeof(float);
