@@ -904,6 +904,7 @@ cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float*
 __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ part,
                                    const float* __restrict__ proj, float* __restrict__ oh) {
   extern __shared__ __align__(16) float sm[];
+  __shared__ float wsm[8][64];  // per-warp split weights (nsplit <= 64)
   const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int od = G.o_dim, opad = (od + 127) / 128 * 128, rep = G.heads / G.kvh, pw = rep * (G.vh + 2);
@@ -919,19 +920,21 @@ __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ 
     float L = 0.f;
     for (int z = lane; z < nsplit; z += 32) {
       const float mz = base[z * pw + hl];
-      if (mz != -INFINITY) L += expf(mz - M) * base[z * pw + rep + hl];
+      const float wz = mz == -INFINITY ? 0.f : expf(mz - M);  // split weight
+      wsm[wid][z] = wz;
+      L += wz * base[z * pw + rep + hl];
     }
     L = warp_sum(L);
+    __syncwarp();
+#pragma unroll 2
     for (int dd = lane; dd < G.vh; dd += 32) {
       float o = 0.f;
-      for (int z = 0; z < nsplit; ++z) {
-        const float mz = base[z * pw + hl];
-        if (mz == -INFINITY) continue;
-        o += expf(mz - M) * base[z * pw + 2 * rep + hl * G.vh + dd];
-      }
+#pragma unroll 4
+      for (int z = 0; z < nsplit; ++z) o += wsm[wid][z] * base[z * pw + 2 * rep + hl * G.vh + dd];
       const int i = h * G.vh + dd;
       sm[i] = o / L * sigmoidf_(gate[i]);
     }
+    __syncwarp();
   }
   for (int i = od + threadIdx.x; i < opad; i += blockDim.x) sm[i] = 0.f;
   __syncthreads();
@@ -944,6 +947,7 @@ cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, con
                                const float* proj, float* oh, cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   const int opad = (G.o_dim + 127) / 128 * 128;
+  if (nsplit > 64) return cudaErrorInvalidValue;  // the kernel's split-weight buffer
   attn_finish_kernel<<<rb.M, 256, opad * sizeof(float), st>>>(G, nsplit, part, proj, oh);
   return cudaGetLastError();
 }

@@ -47,14 +47,19 @@ struct ChunkTraits<4> {
 
 __host__ __device__ inline int padded_len(int in_pad, int E) { return in_pad + (in_pad / E) * 4; }
 
+// `lev` is a 16-float scratch in shared memory for the level table, so the
+// byte table is built with bank-parallel shared loads instead of lane-divergent
+// parameter-space lookups.
 template <int BITS>
-__device__ __forceinline__ void build_lut_smem(const CqMat& W, float* lut) {
+__device__ __forceinline__ void build_lut_smem(const CqMat& W, float* lut, float* lev) {
   using T = ChunkTraits<BITS>;
+  if (threadIdx.x < 16) lev[threadIdx.x] = W.levels[threadIdx.x];
+  __syncthreads();
   const int total = 256 * T::COPIES;
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
     int byte = i / T::COPIES;
 #pragma unroll
-    for (int j = 0; j < T::P; ++j) lut[i * T::P + j] = W.levels[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
+    for (int j = 0; j < T::P; ++j) lut[i * T::P + j] = lev[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
   }
 }
 
@@ -85,7 +90,8 @@ __global__ void __launch_bounds__(256) cq_gemv_kernel(CqMat W, const float* __re
   for (int m = 0; m < M; ++m)
     for (int k = threadIdx.x; k < W.in_pad; k += blockDim.x)
       xs[m * plen + k + (k / T::E) * 4] = xh[(size_t)m * ldx + k];
-  build_lut_smem<BITS>(W, lut);
+  __shared__ float lev[16];
+  build_lut_smem<BITS>(W, lut, lev);
   __syncthreads();
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;

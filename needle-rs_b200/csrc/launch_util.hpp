@@ -21,8 +21,12 @@ inline cudaError_t allow_smem(const void* kern, size_t smem) {
   auto key = std::make_pair(kern, dev);
   auto it = done.find(key);
   if (it != done.end() && it->second >= smem) return cudaSuccess;
-  // Opt in to the B200 per-block maximum once; later launches need no call.
-  const size_t want = 227 * 1024;
+  // Opt in to the B200 per-block maximum (227 KB, static shared memory
+  // included) once; later launches need no call.
+  cudaFuncAttributes fa;
+  e = cudaFuncGetAttributes(&fa, kern);
+  if (e != cudaSuccess) return e;
+  const size_t want = 227 * 1024 - fa.sharedSizeBytes;
   if (smem > want) return cudaErrorInvalidValue;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)want);
   if (e == cudaSuccess) done[key] = want;

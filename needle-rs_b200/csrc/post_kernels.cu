@@ -178,7 +178,7 @@ constexpr int PW = 8;       // rows (warps) per CTA
 constexpr int PT = PW * 32;  // threads
 
 template <int D>
-struct PostSmem {
+struct __align__(16) PostSmem {
   static constexpr int P = D + 4;
   uint32_t zb[PW][D * P];  // Kronecker input (f32 while built, then f16 hi|lo)
   float fb[PW][D * P];     // Kronecker output
@@ -186,6 +186,7 @@ struct PostSmem {
   float part[PW][PW][8];   // per-warp partial sums: [warp][row][j]
   float amax[PW][PW];      // per-warp partial maxima: [warp][row]
   float inv2[PW];
+  float gs[PW][24];        // gates per row: hpost [nl], hres [nl * nl]
 };
 
 // Block max over the eight warps of per-row partials red[warp][row].
@@ -218,30 +219,40 @@ __global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, L
   const int nrow = min(PW, rb.M - r0);
   const int d = G.d, nl = G.lanes, rk = G.cond_rank;
 
+  // Gates of the CTA's rows: hpost [nl], hres [nl * nl] (written by layer_pre).
+  if (tid < PW * 24) S.gs[tid / 24][tid % 24] = (tid / 24 < nrow) ? gates[(size_t)(r0 + tid / 24) * 24 + tid % 24] : 0.f;
   // ---- per row (warp w): post_norm + gated residual (model.rs:309-316), s1 and its rms
   if (w < nrow) {
     const int r = r0 + w;
-    const float* po = projo + (size_t)r * d;
-    const float* bx = bx_in + (size_t)r * d;
-    float* s1 = s1all + (size_t)w * d;
+    const float4* po = reinterpret_cast<const float4*>(projo + (size_t)r * d);
+    const float4* bx = reinterpret_cast<const float4*>(bx_in + (size_t)r * d);
+    const float4* pn = reinterpret_cast<const float4*>(lp.post_norm);
+    float4* s1 = reinterpret_cast<float4*>(s1all + (size_t)w * d);
+    const int d4 = d / 4;
     float ss = 0.f;
-#pragma unroll 4
-    for (int c = lane; c < d; c += 32) ss += po[c] * po[c];
+#pragma unroll 2
+    for (int c = lane; c < d4; c += 32) {
+      const float4 v = po[c];
+      ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+    }
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)d + EPS);
     const float ag = sigmoidf_(lp.attn_gate);
     float s2 = 0.f;
-#pragma unroll 4
-    for (int c = lane; c < d; c += 32) {
-      const float v = bx[c] + ag * ((1.0f + lp.post_norm[c]) * po[c] * inv);
+#pragma unroll 2
+    for (int c = lane; c < d4; c += 32) {
+      const float4 p = po[c], x = bx[c], q = pn[c];
+      const float4 v = make_float4(x.x + ag * ((1.0f + q.x) * p.x * inv), x.y + ag * ((1.0f + q.y) * p.y * inv),
+                                   x.z + ag * ((1.0f + q.z) * p.z * inv), x.w + ag * ((1.0f + q.w) * p.w * inv));
       s1[c] = v;
-      s2 += v * v;
+      s2 += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
     }
     s2 = warp_sum(s2);
     if (lane == 0) S.inv2[w] = 1.0f / sqrtf(s2 / (float)d + EPS);
   }
   __syncthreads();
-  // ---- element-parallel: t = pre_hada norm, z = t * d1, logits t . cond_v
+  // ---- element-parallel, four elements per thread: t = pre_hada norm,
+  // z = t * d1, logits t . cond_v
   {
     float acc[PW][8], mz[PW];
 #pragma unroll
@@ -250,26 +261,38 @@ __global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, L
 #pragma unroll
       for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
     }
-    for (int c = tid; c < N; c += PT) {
-      const int pi = pad_idx<D>(c);
-      if (c < d) {
-        const float ph = 1.0f + lp.pre_hada[c], dd = lp.d1[c];
-        float cv[8];
+    for (int c0 = 4 * tid; c0 < N; c0 += 4 * PT) {
+      const int pi = pad_idx<D>(c0);  // c0..c0+3 stay in one padded row
+      if (c0 < d) {
+        const float4 ph4 = *reinterpret_cast<const float4*>(lp.pre_hada + c0);
+        const float4 d14 = *reinterpret_cast<const float4*>(lp.d1 + c0);
+        const float ph[4] = {1.0f + ph4.x, 1.0f + ph4.y, 1.0f + ph4.z, 1.0f + ph4.w};
+        const float dd[4] = {d14.x, d14.y, d14.z, d14.w};
+        float cv[4][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cv[j] = j < rk ? lp.cond_v[c * rk + j] : 0.f;
+        for (int e = 0; e < 4; ++e)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) cv[e][j] = j < rk ? lp.cond_v[(c0 + e) * rk + j] : 0.f;
 #pragma unroll
         for (int i = 0; i < PW; ++i) {
           if (i >= nrow) break;
-          const float tc = ph * s1all[i * d + c] * S.inv2[i];
+          const float4 sv = *reinterpret_cast<const float4*>(s1all + i * d + c0);
+          const float s1v[4] = {sv.x, sv.y, sv.z, sv.w};
+          float z[4];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) acc[i][j] += tc * cv[j];
-          const float z = tc * dd;
-          mz[i] = fmaxf(mz[i], fabsf(z));
-          S.zb[i][pi] = __float_as_uint(z);
+          for (int e = 0; e < 4; ++e) {
+            const float tc = ph[e] * s1v[e] * S.inv2[i];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc[i][j] += tc * cv[e][j];
+            z[e] = tc * dd[e];
+            mz[i] = fmaxf(mz[i], fabsf(z[e]));
+          }
+          *reinterpret_cast<uint4*>(&S.zb[i][pi]) =
+              make_uint4(__float_as_uint(z[0]), __float_as_uint(z[1]), __float_as_uint(z[2]), __float_as_uint(z[3]));
         }
       } else {
 #pragma unroll
-        for (int i = 0; i < PW; ++i) S.zb[i][pi] = 0u;
+        for (int i = 0; i < PW; ++i) *reinterpret_cast<uint4*>(&S.zb[i][pi]) = make_uint4(0u, 0u, 0u, 0u);
       }
     }
 #pragma unroll
@@ -317,23 +340,38 @@ __global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, L
     float mz[PW];
 #pragma unroll
     for (int i = 0; i < PW; ++i) mz[i] = 0.f;
-    for (int c = tid; c < N; c += PT) {
-      float cu[8];
+    for (int c0 = 4 * tid; c0 < N; c0 += 4 * PT) {
+      float cu[8][4];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) cu[j] = j < rk ? lp.cond_u[j * N + c] : 0.f;
-      const float d2 = lp.d2[c], b2 = lp.b2[c];
-      const int src = pad_idx<D>(p1[c]), pi = pad_idx<D>(c);
+      for (int j = 0; j < 8; ++j) {
+        const float4 t = j < rk ? *reinterpret_cast<const float4*>(lp.cond_u + j * N + c0) : make_float4(0, 0, 0, 0);
+        cu[j][0] = t.x;
+        cu[j][1] = t.y;
+        cu[j][2] = t.z;
+        cu[j][3] = t.w;
+      }
+      const float4 d24 = *reinterpret_cast<const float4*>(lp.d2 + c0);
+      const float4 b24 = *reinterpret_cast<const float4*>(lp.b2 + c0);
+      const uint4 pp = *reinterpret_cast<const uint4*>(p1 + c0);
+      const float d2[4] = {d24.x, d24.y, d24.z, d24.w}, b2[4] = {b24.x, b24.y, b24.z, b24.w};
+      const int src[4] = {pad_idx<D>(pp.x), pad_idx<D>(pp.y), pad_idx<D>(pp.z), pad_idx<D>(pp.w)};
+      const int pi = pad_idx<D>(c0);
 #pragma unroll
       for (int i = 0; i < PW; ++i) {
         if (i >= nrow) break;
-        float cv = 1.0f;
+        float z[4];
 #pragma unroll
-        for (int j = 0; j < 8; ++j)
-          if (j < rk && S.pr[i][j] != 0.0f) cv += S.pr[i][j] * cu[j];
-        const float v = d2 * cv * S.fb[i][src] + b2;
-        const float z = v * sigmoidf_(v);  // silu, ops.rs:118
-        mz[i] = fmaxf(mz[i], fabsf(z));
-        S.zb[i][pi] = __float_as_uint(z);
+        for (int e = 0; e < 4; ++e) {
+          float cv = 1.0f;
+#pragma unroll
+          for (int j = 0; j < 8; ++j)
+            if (j < rk && S.pr[i][j] != 0.0f) cv += S.pr[i][j] * cu[j][e];
+          const float v = d2[e] * cv * S.fb[i][src[e]] + b2[e];
+          z[e] = v * sigmoidf_(v);  // silu, ops.rs:118
+          mz[i] = fmaxf(mz[i], fabsf(z[e]));
+        }
+        *reinterpret_cast<uint4*>(&S.zb[i][pi]) =
+            make_uint4(__float_as_uint(z[0]), __float_as_uint(z[1]), __float_as_uint(z[2]), __float_as_uint(z[3]));
       }
     }
 #pragma unroll
@@ -354,15 +392,23 @@ __global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, L
     float mz[PW];
 #pragma unroll
     for (int i = 0; i < PW; ++i) mz[i] = 0.f;
-    for (int c = tid; c < N; c += PT) {
-      const float d3 = lp.d3[c];
-      const int src = pad_idx<D>(p2[c]), pi = pad_idx<D>(c);
+    for (int c0 = 4 * tid; c0 < N; c0 += 4 * PT) {
+      const float4 d34 = *reinterpret_cast<const float4*>(lp.d3 + c0);
+      const uint4 pp = *reinterpret_cast<const uint4*>(p2 + c0);
+      const float d3[4] = {d34.x, d34.y, d34.z, d34.w};
+      const int src[4] = {pad_idx<D>(pp.x), pad_idx<D>(pp.y), pad_idx<D>(pp.z), pad_idx<D>(pp.w)};
+      const int pi = pad_idx<D>(c0);
 #pragma unroll
       for (int i = 0; i < PW; ++i) {
         if (i >= nrow) break;
-        const float z = S.fb[i][src] * d3;
-        mz[i] = fmaxf(mz[i], fabsf(z));
-        S.zb[i][pi] = __float_as_uint(z);
+        float z[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          z[e] = S.fb[i][src[e]] * d3[e];
+          mz[i] = fmaxf(mz[i], fabsf(z[e]));
+        }
+        *reinterpret_cast<uint4*>(&S.zb[i][pi]) =
+            make_uint4(__float_as_uint(z[0]), __float_as_uint(z[1]), __float_as_uint(z[2]), __float_as_uint(z[3]));
       }
     }
 #pragma unroll
@@ -379,28 +425,35 @@ __global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, L
   }
   __syncthreads();
   // ---- element-parallel: MLP residual, y = block - u, scatter_up into the lanes
-  for (int c = tid; c < d; c += PT) {
-    const float d4 = lp.d4[c];
-    const int pi = pad_idx<D>(c);
+  for (int c0 = 4 * tid; c0 < d; c0 += 4 * PT) {
+    const float4 d44 = *reinterpret_cast<const float4*>(lp.d4 + c0);
+    const int pi = pad_idx<D>(c0);
 #pragma unroll
     for (int i = 0; i < PW; ++i) {
       if (i >= nrow) break;
       const int r = r0 + i;
-      const float* gs = gates + (size_t)r * 24;
-      const float b2v = s1all[i * d + c] + S.fb[i][pi] * d4;
-      const float y = b2v - u[(size_t)r * d + c];
-      float* lr = lanes + (size_t)r * nl * d;
-      float lv[4];
+      const float4 sv = *reinterpret_cast<const float4*>(s1all + i * d + c0);
+      const float4 fv = *reinterpret_cast<const float4*>(&S.fb[i][pi]);
+      const float4 uv = *reinterpret_cast<const float4*>(u + (size_t)r * d + c0);
+      const float y[4] = {sv.x + fv.x * d44.x - uv.x, sv.y + fv.y * d44.y - uv.y, sv.z + fv.z * d44.z - uv.z,
+                          sv.w + fv.w * d44.w - uv.w};
+      float* lr = lanes + (size_t)r * nl * d + c0;
+      float4 lv[4];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) lv[j] = j < nl ? lr[j * d + c] : 0.f;
+      for (int j = 0; j < 4; ++j) lv[j] = j < nl ? *reinterpret_cast<const float4*>(lr + j * d) : make_float4(0, 0, 0, 0);
 #pragma unroll
       for (int a = 0; a < 4; ++a) {
         if (a >= nl) break;
-        float accv = 0.f;
+        float o[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j)
-          if (j < nl) accv += gs[nl + a * nl + j] * lv[j];
-        lr[a * d + c] = accv + gs[a] * y;
+        for (int e = 0; e < 4; ++e) {
+          float accv = 0.f;
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            if (j < nl) accv += S.gs[i][nl + a * nl + j] * (&lv[j].x)[e];
+          o[e] = accv + S.gs[i][a] * y[e];
+        }
+        *reinterpret_cast<float4*>(lr + a * d) = make_float4(o[0], o[1], o[2], o[3]);
       }
     }
   }

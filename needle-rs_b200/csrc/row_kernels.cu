@@ -139,6 +139,7 @@ __global__ void engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float
   const size_t kv_ld = (size_t)G.n_sites * 2 * G.d;
   const float* raw_here = ekv + (size_t)r * kv_ld + (size_t)site * 2 * G.d + G.d;
   float* tail = ri.s->eng_tail + (size_t)site * reach * G.d;
+#pragma unroll 4
   for (int c = threadIdx.x; c < G.d; c += blockDim.x) {
     float acc = 0.f;
     for (int j = 0; j < G.e_taps; ++j) {
@@ -173,26 +174,29 @@ cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const Row
 }
 
 // ---------------------------------------------------------------- mHC pre
-// Sinkhorn (kernels.rs:46-85) on an n x n matrix held one element per lane
-// (n in {1, 2, 4}); rows are lane groups of n, columns lanes with stride n.
-__device__ __forceinline__ float sinkhorn_lane(float m, int n) {
+// Sinkhorn (kernels.rs:46-85) in the log domain on an n x n matrix held one
+// element per lane (n in {1, 2, 4}); rows are lane groups of n, columns lanes
+// with stride n. The 20 dependent log-sum-exp rounds use the hardware
+// exponential and logarithm (__expf/__logf, ~1e-6 relative).
+__device__ __forceinline__ float sinkhorn_lane_fast(float m, int n) {
   const int lane = threadIdx.x & 31;
   const bool in = lane < n * n;
   for (int it = 0; it < 20; ++it) {
     float mx = in ? m : -INFINITY;
     for (int o = 1; o < n; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    float e = in ? expf(m - mx) : 0.f;
+    float e = in ? __expf(m - mx) : 0.f;
     for (int o = 1; o < n; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
-    float lse = isfinite(mx) ? mx + logf(e) : mx;
+    float lse = isfinite(mx) ? mx + __logf(e) : mx;
     m = m - lse;
     mx = in ? m : -INFINITY;
     for (int o = n; o < n * n; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
-    e = in ? expf(m - mx) : 0.f;
+    e = in ? __expf(m - mx) : 0.f;
     for (int o = n; o < n * n; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
-    m = m - (mx + logf(e));
+    m = m - (mx + __logf(e));
   }
-  return expf(m);
+  return __expf(m);
 }
+
 
 // Dot of one CQ row (4- or 2-bit) with a prepared activation in shared memory,
 // one warp; lane l covers elements g*128 + l*4 .. +3 of every group, so the
@@ -220,6 +224,25 @@ __device__ __forceinline__ float cq_row_dot_warp(const CqMat& W, int row_index, 
   return warp_sum(acc);
 }
 
+// cq_row_dot_warp over a packed row and its norms staged in shared memory.
+__device__ __forceinline__ float cq_row_dot_staged(const unsigned char* row, const float* nrm, int bits,
+                                                   int groups, const float* lev, const float* xs) {
+  const int lane = threadIdx.x & 31, mask = (1 << bits) - 1;
+  float acc = 0.f;
+#pragma unroll 4
+  for (int g = 0; g < groups; ++g) {
+    const uint32_t c = bits == 4 ? (uint32_t)reinterpret_cast<const uint16_t*>(row + g * 64)[lane]
+                                 : (uint32_t)row[g * 32 + lane];
+    const float4 x = reinterpret_cast<const float4*>(xs + g * 128)[lane];
+    float p = lev[c & mask] * x.x;
+    p += lev[(c >> bits) & mask] * x.y;
+    p += lev[(c >> (2 * bits)) & mask] * x.z;
+    p += lev[(c >> (3 * bits)) & mask] * x.w;
+    acc += nrm[g] * p;
+  }
+  return warp_sum(acc);
+}
+
 // The level tables of the three mHC projections, copied to shared memory so a
 // lane-dependent lookup is a bank-parallel shared load.
 __device__ __forceinline__ void load_phi_levels(const CqMat& a, const CqMat& b, const CqMat& c, float* lev) {
@@ -232,6 +255,25 @@ __device__ __forceinline__ void load_phi_levels(const CqMat& a, const CqMat& b, 
     lev[t] = c.levels[t - 32];
 }
 
+// Packed row, norms, row bytes and groups of projected row o of layer li:
+// o < n phi_pre, o < 2n phi_post, else phi_res (mhc.rs:56-70).
+__device__ __forceinline__ void phi_row(int o, int li, int n, const CqMat& a, const CqMat& b, const CqMat& c,
+                                        const uint8_t** row, const __half** nrm, int* rb, int* groups) {
+  if (o < n) {
+    cq_row_ptr(a, li * n + o, row, nrm);
+    *rb = a.row_bytes;
+    *groups = a.groups;
+  } else if (o < 2 * n) {
+    cq_row_ptr(b, li * n + (o - n), row, nrm);
+    *rb = b.row_bytes;
+    *groups = b.groups;
+  } else {
+    cq_row_ptr(c, li * n * n + (o - 2 * n), row, nrm);
+    *rb = c.row_bytes;
+    *groups = c.groups;
+  }
+}
+
 // mhc.rs:79-102 (mix_down) with the gate and Sinkhorn of mhc.rs:109-130, the
 // Engram gate (engram.rs:112-132) and the pre-attention norm + rotation of the
 // q|k|v|gate input (model.rs:230-262). phi_post / phi_res read the same
@@ -242,7 +284,8 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
                                  const float* __restrict__ norm_in, int site,
                                  const float* __restrict__ ekv, const float* __restrict__ evc,
                                  float* __restrict__ u_out, float* __restrict__ bx_out,
-                                 float* __restrict__ xh_out, float* __restrict__ gates) {
+                                 float* __restrict__ xh_out, float* __restrict__ gates, int rbmax,
+                                 int gmax) {
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x;
   const int n = G.lanes, d = G.d, W = n * d;
@@ -256,11 +299,40 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
   float* red = phi + 32;         // [32]
   float* gsm = red + 32;         // [4 + 4 + 16]
   float* lev = gsm + 24;         // [3][16] level tables of phi_pre, phi_post, phi_res
+  const int nrow = 2 * n + n * n;
+  float* nsm = lev + 48;                                    // [nrow][gmax] norms
+  unsigned char* csm = reinterpret_cast<unsigned char*>(  // [nrow][rbmax] codes, 16-byte aligned
+      (reinterpret_cast<uintptr_t>(nsm + nrow * gmax) + 15) & ~uintptr_t(15));
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
 
   load_phi_levels(phi_pre, phi_post, phi_res, lev);
+  // The 2n + n^2 packed rows travel by cp.async while the lanes are normalised
+  // and rotated below; every (row, chunk) and (row, group) is independent.
+  {
+    const int cpr = rbmax / 16;
+    for (int i = tid; i < nrow * cpr; i += blockDim.x) {
+      const int o = i / cpr, ch = i % cpr;
+      const uint8_t* prow;
+      const __half* pn;
+      int rbo, go;
+      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      if (ch * 16 < rbo) cp_async16(csm + (size_t)o * rbmax + ch * 16, prow + ch * 16, true);
+    }
+    cp_commit();
+#pragma unroll 4
+    for (int i = tid; i < nrow * gmax; i += blockDim.x) {
+      const int o = i / gmax, g = i % gmax;
+      const uint8_t* prow;
+      const __half* pn;
+      int rbo, go;
+      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      nsm[i] = g < go ? __half2float(pn[g]) : 0.f;
+    }
+  }
+
   const float* lr = lanes + (size_t)r * W;
   float ss = 0.f;
+#pragma unroll 4
   for (int i = tid; i < W; i += blockDim.x) {
     float v = lr[i];
     L[i] = v;
@@ -271,75 +343,124 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
   for (int i = tid; i < Wp; i += blockDim.x) X[i] = i < W ? L[i] * inv : 0.f;
   __syncthreads();
   fwht_groups_warp(X, Wp / 128);
+  cp_wait<0>();
   __syncthreads();
-  // 2n + n^2 projected gate rows of this layer.
-  const int nrow = 2 * n + n * n;
-  for (int k = wid; k < nrow; k += nw) {
-    float v;
-    if (k < n)
-      v = cq_row_dot_warp(phi_pre, li * n + k, lev, X);
-    else if (k < 2 * n)
-      v = cq_row_dot_warp(phi_post, li * n + (k - n), lev + 16, X);
-    else
-      v = cq_row_dot_warp(phi_res, li * n * n + (k - 2 * n), lev + 32, X);
-    if (lane == 0) phi[k] = v;
+  // 2n + n^2 projected gate rows of this layer, from the staged rows: warp w
+  // dots rows w, w + nw, w + 2nw together, sharing each activation load.
+  {
+    float acc[3] = {0.f, 0.f, 0.f};
+    int bits[3], lvo[3];
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const int k = wid + j * nw;
+      bits[j] = k < n ? phi_pre.bits : (k < 2 * n ? phi_post.bits : phi_res.bits);
+      lvo[j] = k < n ? 0 : (k < 2 * n ? 16 : 32);
+    }
+    const int groups = phi_pre.groups;  // the three mHC matrices share in_feat = lanes * d_model
+#pragma unroll 2
+    for (int g = 0; g < groups; ++g) {
+      const float4 x = reinterpret_cast<const float4*>(X + g * 128)[lane];
+#pragma unroll
+      for (int j = 0; j < 3; ++j) {
+        const int k = wid + j * nw;
+        if (k >= nrow) continue;
+        const unsigned char* row = csm + (size_t)k * rbmax;
+        const int b = bits[j], mask = (1 << b) - 1;
+        const uint32_t c = b == 4 ? (uint32_t)reinterpret_cast<const uint16_t*>(row + g * 64)[lane]
+                                  : (uint32_t)row[g * 32 + lane];
+        const float* lv = lev + lvo[j];
+        float p = lv[c & mask] * x.x;
+        p += lv[(c >> b) & mask] * x.y;
+        p += lv[(c >> (2 * b)) & mask] * x.z;
+        p += lv[(c >> (3 * b)) & mask] * x.w;
+        acc[j] += nsm[k * gmax + g] * p;
+      }
+    }
+#pragma unroll
+    for (int j = 0; j < 3; ++j) {
+      const float v = warp_sum(acc[j]);
+      const int k = wid + j * nw;
+      if (lane == 0 && k < nrow) phi[k] = v;
+    }
   }
   __syncthreads();
+  // Warp 0 forms the gates; the mix-down gate releases warps 1.. (named
+  // barrier 1) while warp 0 runs Sinkhorn, which nothing below depends on.
+  const int nwo = nw - 1, wo = wid - 1, to = tid - 32, NT = blockDim.x - 32;
   if (wid == 0) {
     const int act = li % n;
+    float hpost = 0.f;
     if (lane < n) {
-      float pre_off = lane == act ? 4.0f : -4.0f;    // mhc.rs:56
-      float post_off = lane == act ? 0.0f : -4.0f;   // mhc.rs:65
+      const float pre_off = lane == act ? 4.0f : -4.0f;   // mhc.rs:56
+      const float post_off = lane == act ? 0.0f : -4.0f;  // mhc.rs:65
       gsm[lane] = sigmoidf_(mp.a_pre * phi[lane] + mp.b_pre[lane] + pre_off);
-      gsm[n + lane] = 2.0f * sigmoidf_(mp.a_post * phi[n + lane] + mp.b_post[lane] + post_off);
+      hpost = 2.0f * sigmoidf_(mp.a_post * phi[n + lane] + mp.b_post[lane] + post_off);
     }
-    float m = lane < n * n ? mp.a_res * phi[2 * n + lane] + mp.b_res[lane] : 0.f;
-    float hres = sinkhorn_lane(m, n);
-    if (lane < n * n) gsm[2 * n + lane] = hres;
+    __syncwarp();
+    asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
+    const float m = lane < n * n ? mp.a_res * phi[2 * n + lane] + mp.b_res[lane] : 0.f;
+    const float hres = sinkhorn_lane_fast(m, n);
+    float* gout = gates + (size_t)r * 24;
+    if (lane < n) gout[lane] = hpost;
+    if (lane < n * n) gout[n + lane] = hres;
+    return;
   }
-  __syncthreads();
-  float* gout = gates + (size_t)r * 24;
-  if (tid < n + n * n) gout[tid] = gsm[n + tid];  // hpost[n], hres[n*n]
+  asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+  // Warps 1..: reductions over NT threads on named barrier 2.
+  auto gsum = [&](float v) {
+    v = warp_sum(v);
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+    if (lane == 0) red[wo] = v;
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+    return warp_sum(lane < nwo ? red[lane] : 0.f);
+  };
   // u = sum_i hpre_i * lane_i (mix_down), bx = u (+ Engram).
-  for (int c = tid; c < d; c += blockDim.x) {
+#pragma unroll 4
+  for (int c = to; c < d; c += NT) {
     float acc = 0.f;
     for (int l = 0; l < n; ++l) acc += gsm[l] * L[l * d + c];
     bx[c] = acc;
     u_out[(size_t)r * d + c] = acc;
   }
-  __syncthreads();
+  asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
   if (site >= 0) {
     const size_t kv_ld = (size_t)G.n_sites * 2 * d;
     const float* ek = ekv + (size_t)r * kv_ld + (size_t)site * 2 * d;
     const float* ev = evc + ((size_t)r * G.n_sites + site) * d;
     float sx = 0.f, sk = 0.f, sd = 0.f;
-    for (int c = tid; c < d; c += blockDim.x) {
+#pragma unroll 4
+    for (int c = to; c < d; c += NT) {
       float x = bx[c], k = ek[c];
       sx += x * x;
       sk += k * k;
       sd += x * k;
     }
-    sx = block_sum(sx, red);
-    sk = block_sum(sk, red);
-    sd = block_sum(sd, red);
+    sx = gsum(sx);
+    sk = gsum(sk);
+    sd = gsum(sd);
     const float ux = 1.0f / sqrtf(sx / (float)d + 1e-6f);
     const float uk = 1.0f / sqrtf(sk / (float)d + 1e-6f);
     const float alpha = sigmoidf_(sd * ux * uk / sqrtf((float)d));
-    for (int c = tid; c < d; c += blockDim.x) bx[c] += alpha * ev[c];
-    __syncthreads();
+#pragma unroll 4
+    for (int c = to; c < d; c += NT) bx[c] += alpha * ev[c];
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
   }
   float s2 = 0.f;
-  for (int c = tid; c < d; c += blockDim.x) s2 += bx[c] * bx[c];
-  s2 = block_sum(s2, red);
+  for (int c = to; c < d; c += NT) s2 += bx[c] * bx[c];
+  s2 = gsum(s2);
   const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
-  for (int c = tid; c < dpad; c += blockDim.x) {
+#pragma unroll 4
+  for (int c = to; c < dpad; c += NT) {
     hb[c] = c < d ? (1.0f + norm_in[c]) * bx[c] * inv2 : 0.f;
     if (c < d) bx_out[(size_t)r * d + c] = bx[c];
   }
-  __syncthreads();
-  fwht_groups_warp(hb, dpad / 128);
-  __syncthreads();
-  for (int c = tid; c < dpad; c += blockDim.x) xh_out[(size_t)r * dpad + c] = hb[c];
+  asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+  for (int g = wo; g < dpad / 128; g += nwo) {
+    float4 v = reinterpret_cast<float4*>(hb + g * 128)[lane];
+    float x[4] = {v.x, v.y, v.z, v.w};
+    fwht128_warp(x);
+    reinterpret_cast<float4*>(xh_out + (size_t)r * dpad + g * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+  }
 }
 
 // The same computation for many rows: PT_M rows per CTA so each mHC weight
@@ -493,7 +614,7 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
       hpost = 2.0f * sigmoidf_(mp.a_post * (phi_s[m][n + lane] * inv) + mp.b_post[lane] + post_off);
     }
     const float mres = lane < n * n ? mp.a_res * (phi_s[m][2 * n + lane] * inv) + mp.b_res[lane] : 0.f;
-    const float hres = sinkhorn_lane(mres, n);
+    const float hres = sinkhorn_lane_fast(mres, n);
     float* gout = gates + (size_t)r * 24;
     if (lane < n) gout[lane] = hpost;
     if (lane < n * n) gout[n + lane] = hres;
@@ -585,11 +706,11 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
                              cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   const int nrow = 2 * G.lanes + G.lanes * G.lanes;
+  const int rbmax = std::max(phi_pre.row_bytes, std::max(phi_post.row_bytes, phi_res.row_bytes));
+  const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
   const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
                         (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0;
   if (rb.M >= PT_MIN_ROWS && tiled_ok) {
-    const int rbmax = std::max(phi_pre.row_bytes, std::max(phi_post.row_bytes, phi_res.row_bytes));
-    const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
     const size_t dyn = (size_t)nrow * rbmax + (size_t)nrow * gmax * 4;
     cudaError_t e = allow_smem((const void*)layer_pre_tiled_kernel, dyn);
     if (e != cudaSuccess) return e;
@@ -598,11 +719,12 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
     return cudaGetLastError();
   }
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
-  const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48) * sizeof(float);
+  const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48 + nrow * gmax) * sizeof(float) +
+                      (size_t)nrow * rbmax + 16;
   cudaError_t e = allow_smem((const void*)layer_pre_kernel, smem);
   if (e != cudaSuccess) return e;
   layer_pre_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in,
-                                            site, ekv, evc, u, bx, xh, gates);
+                                            site, ekv, evc, u, bx, xh, gates, rbmax, gmax);
   return cudaGetLastError();
 }
 
@@ -636,6 +758,7 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
   const int taps = G.taps, tl = taps > 0 ? taps - 1 : 0;
   const float* raw = proj + (size_t)r * G.proj_dim;
   float* tail = tl ? ri.s->qkv_tail + (size_t)li * tl * qkv : nullptr;
+#pragma unroll 4
   for (int c = threadIdx.x; c < qkv; c += blockDim.x) {
     const float* tp;
     int dim, cc;
@@ -986,6 +1109,7 @@ __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float
   const int r = blockIdx.x, d = G.d, dpad = (d + 127) / 128 * 128;
   const float* lr = lanes + (size_t)r * G.lanes * d;
   float ss = 0.f;
+#pragma unroll 4
   for (int c = threadIdx.x; c < d; c += blockDim.x) {
     float a = 0.f;
     for (int l = 0; l < G.lanes; ++l) a += lr[l * d + c];
