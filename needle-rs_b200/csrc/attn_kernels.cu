@@ -471,7 +471,8 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
                                                             const int8_t* __restrict__ q8,
                                                             const float* __restrict__ q8s, const void* pk,
                                                             const void* pv, const float* pks, const float* pvs,
-                                                            float* __restrict__ part) {
+                                                            float* __restrict__ part, const float* __restrict__ proj,
+                                                            float* __restrict__ oh, int* __restrict__ cnt) {
   using T = MmaTile<QK, VH>;
   using WS = MmaWarpSmem<QK, VH>;
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -624,7 +625,7 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
     __syncwarp();  // before the next block overwrites the f16 values
   }
 
-  // ---- merge the four warps (shared memory reused) and write the partial
+  // ---- merge the four warps (shared memory reused)
   __syncthreads();
   float* Wm = reinterpret_cast<float*>(smraw);  // [4][8]
   float* Wl = Wm + 32;                           // [4][8]
@@ -642,8 +643,8 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
   }
   __syncthreads();
   const int pwid = rep * (VH + 2);
-  float* out = part + (((size_t)r * G.kvh + kh) * nsplit + z) * pwid;
-  for (int i = threadIdx.x; i < rep * (VH + 2); i += blockDim.x) {
+  float* C = Wo + 4 * 8 * VH;  // this CTA's partial: rep maxima, rep sums, rep x VH outputs
+  for (int i = threadIdx.x; i < pwid; i += blockDim.x) {
     const int h = i < 2 * rep ? i % rep : (i - 2 * rep) / VH;
     float M = -INFINITY;
 #pragma unroll
@@ -660,22 +661,88 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
         acc += f * (i < 2 * rep ? Wl[w * 8 + h] : Wo[(w * 8 + h) * VH + (i - 2 * rep) % VH]);
       }
     }
-    out[i] = acc;
+    C[i] = acc;
+  }
+  __syncthreads();
+  float* out = part + (((size_t)r * G.kvh + kh) * nsplit + z) * pwid;
+  if (!oh || nsplit > 1)
+    for (int i = threadIdx.x; i < pwid; i += blockDim.x) out[i] = C[i];
+  if (!oh) return;  // the separate attn_finish kernel combines and rotates
+  // ---- finish this (row, KV head): softmax merge over the splits, output
+  // gate, rotation of its rep * VH outputs (whole 128-wide groups) into oh.
+  const float* ps = C;  // one split: this CTA's partial
+  int ns = 1;
+  if (nsplit > 1) {
+    // The last CTA of the row's KV head to arrive combines all splits.
+    __shared__ int last;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      last = atomicAdd(&cnt[(size_t)r * G.kvh + kh], 1) == nsplit - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    ps = part + ((size_t)r * G.kvh + kh) * nsplit * pwid;
+    ns = nsplit;
+  }
+  float* Fw = C + pwid;        // [rep][64] split weights exp(m_z - M)
+  float* FL = Fw + rep * 64;   // [rep] 1 / sum
+  float* Fo = FL + 8;          // [rep * VH] gated outputs
+  if (threadIdx.x < rep) {
+    const int h = threadIdx.x;
+    float M = -INFINITY;
+    for (int zz = 0; zz < ns; ++zz) M = fmaxf(M, ps[zz * pwid + h]);
+    float L = 0.f;
+    for (int zz = 0; zz < ns; ++zz) {
+      const float mz = ps[zz * pwid + h];
+      const float wz = mz == -INFINITY ? 0.f : expf(mz - M);
+      Fw[h * 64 + zz] = wz;
+      L += wz * ps[zz * pwid + rep + h];
+    }
+    FL[h] = 1.0f / L;
+  }
+  __syncthreads();
+  const float* gate = proj + (size_t)r * G.proj_dim + G.qkv_dim + (size_t)kh * rep * VH;
+#pragma unroll 3
+  for (int i = threadIdx.x; i < rep * VH; i += blockDim.x) {
+    const int h = i / VH;
+    float acc = 0.f;
+    for (int zz = 0; zz < ns; ++zz) acc += Fw[h * 64 + zz] * ps[zz * pwid + 2 * rep + i];
+    Fo[i] = acc * FL[h] * sigmoidf_(gate[i]);
+  }
+  if (nsplit > 1 && threadIdx.x == 0) cnt[(size_t)r * G.kvh + kh] = 0;  // ready for the next launch
+  __syncthreads();
+  const int opad = (G.o_dim + 127) / 128 * 128;
+  float* ohr = oh + (size_t)r * opad + (size_t)kh * rep * VH;
+  for (int gg = wid; gg < rep * VH / 128; gg += 4) {
+    const float4 v = reinterpret_cast<const float4*>(Fo + gg * 128)[lane];
+    float x[4] = {v.x, v.y, v.z, v.w};
+    fwht128_warp(x);
+    reinterpret_cast<float4*>(ohr + gg * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
   }
 }
 
 template <int QK, int VH>
 static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
                                         const int8_t* q8, const float* q8s, const void* pk, const void* pv,
-                                        const float* pks, const float* pvs, float* part, cudaStream_t st) {
+                                        const float* pks, const float* pvs, float* part, const float* proj,
+                                        float* oh, int* cnt, cudaStream_t st) {
   using WS = MmaWarpSmem<QK, VH>;
-  const size_t smem = std::max(4 * sizeof(WS), (size_t)(64 + 4 * 8 * VH) * sizeof(float));
+  const int rep = G.heads / G.kvh;
+  const size_t fin = (size_t)(64 + 4 * 8 * VH + rep * (VH + 2) + rep * 64 + 8 + rep * VH) * sizeof(float);
+  const size_t smem = std::max(4 * sizeof(WS), fin);
   auto k = layer_attn_i8_kernel<QK, VH>;
   cudaError_t e = allow_smem((const void*)k, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(rb.M, G.kvh, nsplit);
-  k<<<grid, 128, smem, st>>>(G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part);
+  k<<<grid, 128, smem, st>>>(G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, cnt);
   return cudaGetLastError();
+}
+
+bool attn_fuses_finish(const Geo& G, int int8) {
+  const int rep = G.heads / G.kvh;
+  return int8 && (rep * G.vh) % 128 == 0 && rep <= 8;
 }
 
 int attn_nsplit(int rows, int kvh, int max_span) {
@@ -706,14 +773,19 @@ static cudaError_t launch_layer_attn_t(const Geo& G, int li, const RowBatch& rb,
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
                              const void* pv, const float* pks, const float* pvs, float* part,
-                             cudaStream_t st, int int8) {
+                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt) {
   if (rb.M <= 0) return cudaSuccess;
   const int rep = G.heads / G.kvh;
   if (rep > AT_MAXREP || nsplit < 1) return cudaErrorInvalidValue;
   if (int8) {
     if (!q8 || !q8s) return cudaErrorInvalidValue;
-#define NB_ATI(Q, V) \
-  return launch_layer_attn_i8<Q, V>(G, li, rb, lp.window, nsplit, q8, q8s, pk, pv, pks, pvs, part, st)
+    // With proj, oh and cnt the kernel also finishes (attn_fuses_finish);
+    // without them it leaves the partials to attn_finish.
+    const bool fuse = proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64;
+    if (!fuse) proj = nullptr, oh = nullptr, cnt = nullptr;
+#define NB_ATI(Q, V)                                                                                         \
+  return launch_layer_attn_i8<Q, V>(G, li, rb, lp.window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, \
+                                    cnt, st)
     if (G.vh == 64) {
       switch (G.qk) {
         case 16: NB_ATI(16, 64);

@@ -57,7 +57,7 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
-  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, whi, wlo, oh, projo, gates, fetched, ekv, evc, lm_in,
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, whi, wlo, cnt, oh, projo, gates, fetched, ekv, evc, lm_in,
                 pks, pvs, pk, pv, rows, tokens, next, last_rows};
   for (void* p : ps)
     if (p) cudaFree(p);
@@ -85,7 +85,7 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
       {(void**)&ws.proj, cap * G.proj_dim * 4},     {(void**)&ws.qpost, cap * G.q_dim * 4},
       {(void**)&ws.q8s, cap * G.heads * 4},         {(void**)&ws.q8, cap * G.q_dim},
       {(void**)&ws.ahi, cap * kmax * 2},            {(void**)&ws.alo, cap * kmax * 2},
-      {(void**)&ws.ainv, cap * 4},
+      {(void**)&ws.ainv, cap * 4},                  {(void**)&ws.cnt, cap * G.kvh * 4},
       {(void**)&ws.whi, wmax * kmax * 2},           {(void**)&ws.wlo, wmax * kmax * 2},
       {(void**)&ws.oh, cap * opad * 4},
       {(void**)&ws.projo, cap * d * 4},             {(void**)&ws.gates, cap * 24 * 4},
@@ -101,6 +101,14 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
     if (e != cudaSuccess) {
       ws.release();
       *err = cuda_msg("workspace allocation", e);
+      return false;
+    }
+  }
+  {
+    cudaError_t e = cudaMemset(ws.cnt, 0, cap * G.kvh * 4);  // attention split counters start at zero
+    if (e != cudaSuccess) {
+      ws.release();
+      *err = cuda_msg("workspace initialisation", e);
       return false;
     }
   }
@@ -839,11 +847,12 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs,
                            int8 ? ws.q8 : nullptr, int8 ? ws.q8s : nullptr, st));
     NB_MARK(PK_QKV_POST, 1);
+    const bool fused = attn_fuses_finish(G, int8 ? 1 : 0) && nsplit <= 64;
     NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, ws.qpost, ws.q8, ws.q8s, ws.pk, ws.pv, ws.pks, ws.pvs,
-                            ws.part, st, int8 ? 1 : 0));
+                            ws.part, st, int8 ? 1 : 0, ws.proj, ws.oh, ws.cnt));
     NB_MARK(PK_ATTN, 1);
-    NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
-    NB_MARK(PK_ATTN_FINISH, 1);
+    if (!fused) NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
+    NB_MARK(PK_ATTN_FINISH, fused ? 0 : 1);
     NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st, 0, &ws.gs));
     NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &ws.gs));
     NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, ws.projo, ws.u, ws.bx,

@@ -68,6 +68,7 @@ struct Workspace {
   __half *ahi = nullptr, *alo = nullptr;  // tensor-core projections: split activations
   float* ainv = nullptr;                  // and their inverse row scales
   __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
+  int* cnt = nullptr;  // attention split-arrival counters [rows][kv heads], zero between launches
   GemmScratch gs;
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;

@@ -103,10 +103,15 @@ int attn_nsplit(int rows, int kvh, int max_span);
 size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit);
 // int8 = 1 runs the tensor-core kernel on the query codes q8 / q8s;
 // int8 = 0 the f32 kernel on qpost.
+// int8 = 1 with proj / oh / cnt (per-row, per-KV-head counters, zero-initialised)
+// and attn_fuses_finish(): the kernel also merges the splits, gates and
+// rotates into oh, so attn_finish is not launched.
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
                              const void* pv, const float* pks, const float* pvs, float* part,
-                             cudaStream_t st, int int8);
+                             cudaStream_t st, int int8, const float* proj = nullptr, float* oh = nullptr,
+                             int* cnt = nullptr);
+bool attn_fuses_finish(const Geo& G, int int8);
 cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
                                const float* proj, float* oh, cudaStream_t st);
 cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
