@@ -485,7 +485,8 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
   const AttnSrc src = layer_src<QK, VH>(G, li, rb, r, window, pk, pv, pks, pvs, &lo, &p);
   int a, b;
   split_range(lo, p, nsplit, z, &a, &b);
-  const float scale = 1.0f / sqrtf((float)QK);
+  // Scores are kept in base-2 units (times log2 e) so the softmax uses exp2f.
+  const float scale = 1.0f / sqrtf((float)QK) * 1.44269504088896341f;
 
   // Query codes of head g of this KV head as A fragments (rows >= rep zero).
   const bool hv = g < rep;
@@ -573,11 +574,11 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     const float mnew = fmaxf(m, mx);
-    const float corr = m == -INFINITY ? 0.f : expf(m - mnew);
+    const float corr = m == -INFINITY ? 0.f : exp2f(m - mnew);
     float pw[8], sum = 0.f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      const float pe = sc[i] == -INFINITY ? 0.f : expf(sc[i] - mnew);
+      const float pe = sc[i] == -INFINITY ? 0.f : exp2f(sc[i] - mnew);
       sum += pe;
       pw[i] = pe * W.vs[buf][(i >> 1) * 8 + t * 2 + (i & 1)];
     }
@@ -657,7 +658,7 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
       for (int w = 0; w < 4; ++w) {
         const float mw = Wm[w * 8 + h];
         if (mw == -INFINITY) continue;
-        const float f = expf(mw - M);
+        const float f = exp2f(mw - M);
         acc += f * (i < 2 * rep ? Wl[w * 8 + h] : Wo[(w * 8 + h) * VH + (i - 2 * rep) % VH]);
       }
     }
@@ -665,8 +666,10 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
   }
   __syncthreads();
   float* out = part + (((size_t)r * G.kvh + kh) * nsplit + z) * pwid;
+  // The separate attn_finish kernel expects natural-log maxima.
   if (!oh || nsplit > 1)
-    for (int i = threadIdx.x; i < pwid; i += blockDim.x) out[i] = C[i];
+    for (int i = threadIdx.x; i < pwid; i += blockDim.x)
+      out[i] = (!oh && i < rep && C[i] != -INFINITY) ? C[i] * 0.69314718055994531f : C[i];
   if (!oh) return;  // the separate attn_finish kernel combines and rotates
   // ---- finish this (row, KV head): softmax merge over the splits, output
   // gate, rotation of its rep * VH outputs (whole 128-wide groups) into oh.
@@ -696,7 +699,7 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
     float L = 0.f;
     for (int zz = 0; zz < ns; ++zz) {
       const float mz = ps[zz * pwid + h];
-      const float wz = mz == -INFINITY ? 0.f : expf(mz - M);
+      const float wz = mz == -INFINITY ? 0.f : exp2f(mz - M);
       Fw[h * 64 + zz] = wz;
       L += wz * ps[zz * pwid + rep + h];
     }

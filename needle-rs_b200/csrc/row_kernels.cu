@@ -178,6 +178,27 @@ cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const Row
 // element per lane (n in {1, 2, 4}); rows are lane groups of n, columns lanes
 // with stride n. The 20 dependent log-sum-exp rounds use the hardware
 // exponential and logarithm (__expf/__logf, ~1e-6 relative).
+// Two independent matrices per warp, one per 16-lane half (lanes 16.. hold the
+// second); the shuffle distances (< n * n <= 16) stay inside a half.
+__device__ __forceinline__ float sinkhorn_half_fast(float m, int n) {
+  const int hl = threadIdx.x & 15;
+  const bool in = hl < n * n;
+  for (int it = 0; it < 20; ++it) {
+    float mx = in ? m : -INFINITY;
+    for (int o = 1; o < n; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    float e = in ? __expf(m - mx) : 0.f;
+    for (int o = 1; o < n; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    float lse = isfinite(mx) ? mx + __logf(e) : mx;
+    m = m - lse;
+    mx = in ? m : -INFINITY;
+    for (int o = n; o < n * n; o <<= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+    e = in ? __expf(m - mx) : 0.f;
+    for (int o = n; o < n * n; o <<= 1) e += __shfl_xor_sync(0xffffffffu, e, o);
+    m = m - (mx + __logf(e));
+  }
+  return __expf(m);
+}
+
 __device__ __forceinline__ float sinkhorn_lane_fast(float m, int n) {
   const int lane = threadIdx.x & 31;
   const bool in = lane < n * n;
@@ -491,6 +512,8 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
   __shared__ float lev[48];
   __shared__ float phi_s[PT_M][24];
   __shared__ float ss_s[PT_M];
+  __shared__ float hp_s[PT_M][4];      // mix-down gates per row
+  __shared__ float red3[8][PT_M][3];   // per-warp partial sums per row
   extern __shared__ __align__(16) unsigned char pt_dyn[];  // [nrow][rbmax] codes, [nrow][gmax] norms
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int n = G.lanes, d = G.d, W = n * d, nrow = 2 * n + n * n;
@@ -500,19 +523,30 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
   load_phi_levels(phi_pre, phi_post, phi_res, lev);
   float* nsm = reinterpret_cast<float*>(pt_dyn + (size_t)nrow * rbmax);
 
-  // Stage the packed rows and norms of all 2n + n^2 projected rows.
-  for (int o = 0; o < nrow; ++o) {
-    const CqMat& Mx = o < n ? phi_pre : (o < 2 * n ? phi_post : phi_res);
-    const int r = o < n ? li * n + o : (o < 2 * n ? li * n + (o - n) : li * n * n + (o - 2 * n));
-    const uint8_t* prow;
-    const __half* pn;
-    cq_row_ptr(Mx, r, &prow, &pn);
-    for (int i = tid; i < Mx.row_bytes / 16; i += blockDim.x)
-      cp_async16(pt_dyn + (size_t)o * rbmax + i * 16, prow + i * 16, true);
-    for (int g = tid; g < Mx.groups; g += blockDim.x) nsm[o * gmax + g] = __half2float(pn[g]);
+  // Stage the packed rows and norms of all 2n + n^2 projected rows; every
+  // (row, chunk) and (row, group) is independent.
+  {
+    const int cpr = rbmax / 16;
+    for (int i = tid; i < nrow * cpr; i += blockDim.x) {
+      const int o = i / cpr, ch = i % cpr;
+      const uint8_t* prow;
+      const __half* pn;
+      int rbo, go;
+      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      if (ch * 16 < rbo) cp_async16(pt_dyn + (size_t)o * rbmax + ch * 16, prow + ch * 16, true);
+    }
+    cp_commit();
+#pragma unroll 4
+    for (int i = tid; i < nrow * gmax; i += blockDim.x) {
+      const int o = i / gmax, g = i % gmax;
+      const uint8_t* prow;
+      const __half* pn;
+      int rbo, go;
+      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      nsm[i] = g < go ? __half2float(pn[g]) : 0.f;
+    }
+    cp_wait<0>();
   }
-  cp_commit();
-  cp_wait<0>();
 
   // This warp's projected rows: o = wid + 8j.
   int wbits[3], wlev[3];
@@ -602,97 +636,128 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
   }
   __syncthreads();
 
-  const int nq = d / 128, act = li % n;
-  for (int m = wid; m < rows; m += 8) {
-    const int r = m0 + m;
-    const float inv = 1.0f / sqrtf(ss_s[m] / (float)W + EPS);  // rms_unit_to, kernels.rs:32
+  // ---- gates: warp w forms rows w and w + 8 at once, one per 16-lane half
+  // (the Sinkhorn shuffles stay inside a half).
+  {
+    const int half = lane >> 4, hl = lane & 15;
+    const int m = wid + 8 * half;
+    const bool live = m < rows;
+    const int act = li % n;
+    const float inv = live ? 1.0f / sqrtf(ss_s[m] / (float)W + EPS) : 0.f;  // rms_unit_to, kernels.rs:32
     float hpre = 0.f, hpost = 0.f;
-    if (lane < n) {
-      const float pre_off = lane == act ? 4.0f : -4.0f;   // mhc.rs:56
-      const float post_off = lane == act ? 0.0f : -4.0f;  // mhc.rs:65
-      hpre = sigmoidf_(mp.a_pre * (phi_s[m][lane] * inv) + mp.b_pre[lane] + pre_off);
-      hpost = 2.0f * sigmoidf_(mp.a_post * (phi_s[m][n + lane] * inv) + mp.b_post[lane] + post_off);
+    if (live && hl < n) {
+      const float pre_off = hl == act ? 4.0f : -4.0f;   // mhc.rs:56
+      const float post_off = hl == act ? 0.0f : -4.0f;  // mhc.rs:65
+      hpre = sigmoidf_(mp.a_pre * (phi_s[m][hl] * inv) + mp.b_pre[hl] + pre_off);
+      hpost = 2.0f * sigmoidf_(mp.a_post * (phi_s[m][n + hl] * inv) + mp.b_post[hl] + post_off);
     }
-    const float mres = lane < n * n ? mp.a_res * (phi_s[m][2 * n + lane] * inv) + mp.b_res[lane] : 0.f;
-    const float hres = sinkhorn_lane_fast(mres, n);
-    float* gout = gates + (size_t)r * 24;
-    if (lane < n) gout[lane] = hpost;
-    if (lane < n * n) gout[n + lane] = hres;
-    float hp[4];
-#pragma unroll
-    for (int l = 0; l < 4; ++l) hp[l] = __shfl_sync(0xffffffffu, hpre, l);
-    // mix_down (mhc.rs:79-102)
-    const float* lr = lanes + (size_t)r * W + lane * 4;
-    float bxv[PT_DQ][4];
-#pragma unroll
-    for (int q = 0; q < PT_DQ; ++q) {
-      if (q >= nq) continue;
-      float a[4] = {0.f, 0.f, 0.f, 0.f};
-      for (int l = 0; l < n; ++l) {
-        const float4 t = __ldg(reinterpret_cast<const float4*>(lr + l * d + q * 128));
-        a[0] += hp[l] * t.x;
-        a[1] += hp[l] * t.y;
-        a[2] += hp[l] * t.z;
-        a[3] += hp[l] * t.w;
+    const float mres = (live && hl < n * n) ? mp.a_res * (phi_s[m][2 * n + hl] * inv) + mp.b_res[hl] : 0.f;
+    const float hres = sinkhorn_half_fast(mres, n);
+    if (live) {
+      float* gout = gates + (size_t)(m0 + m) * 24;
+      if (hl < n) {
+        gout[hl] = hpost;
+        hp_s[m][hl] = hpre;
       }
-#pragma unroll
-      for (int i = 0; i < 4; ++i) bxv[q][i] = a[i];
-      reinterpret_cast<float4*>(u_out + (size_t)r * d + q * 128)[lane] = make_float4(a[0], a[1], a[2], a[3]);
+      if (hl < n * n) gout[n + hl] = hres;
     }
-    if (site >= 0) {  // Engram gate, engram.rs:112-132
-      const size_t kv_ld = (size_t)G.n_sites * 2 * d;
-      const float* ek = ekv + (size_t)r * kv_ld + (size_t)site * 2 * d + lane * 4;
-      const float* ev = evc + ((size_t)r * G.n_sites + site) * d + lane * 4;
-      float sx = 0.f, sk = 0.f, sd = 0.f;
+  }
+  __syncthreads();
+  // ---- element-parallel over the tile: warp w holds 128-wide group w of every
+  // row (lane l elements 128w + 4l .. +3), so the final rotation needs no
+  // shared memory. mix_down (mhc.rs:79-102), Engram gate (engram.rs:112-132),
+  // ZCRMS norm (norm.rs:23) and the rotation of the attention input.
+  const int nq = d / 128;
+  const bool act_w = wid < nq;
+  const int c0 = wid * 128 + lane * 4;
+  float bxv[PT_M][4];
 #pragma unroll
-      for (int q = 0; q < PT_DQ; ++q) {
-        if (q >= nq) continue;
-        const float4 t = __ldg(reinterpret_cast<const float4*>(ek + q * 128));
-        const float kk[4] = {t.x, t.y, t.z, t.w};
+  for (int m = 0; m < PT_M; ++m) {
+    bxv[m][0] = bxv[m][1] = bxv[m][2] = bxv[m][3] = 0.f;
+    if (!act_w || m >= rows) continue;
+    const float* lr = lanes + (size_t)(m0 + m) * W + c0;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int l = 0; l < n; ++l) {
+      const float4 t = __ldg(reinterpret_cast<const float4*>(lr + l * d));
+      const float h = hp_s[m][l];
+      a.x += h * t.x;
+      a.y += h * t.y;
+      a.z += h * t.z;
+      a.w += h * t.w;
+    }
+    bxv[m][0] = a.x;
+    bxv[m][1] = a.y;
+    bxv[m][2] = a.z;
+    bxv[m][3] = a.w;
+    *reinterpret_cast<float4*>(u_out + (size_t)(m0 + m) * d + c0) = a;
+  }
+  if (site >= 0) {
+    const size_t kv_ld = (size_t)G.n_sites * 2 * d;
+#pragma unroll
+    for (int m = 0; m < PT_M; ++m) {
+      float sx = 0.f, sk = 0.f, sd = 0.f;
+      if (act_w && m < rows) {
+        const size_t r = m0 + m;
+        const float4 kk = __ldg(reinterpret_cast<const float4*>(ekv + r * kv_ld + (size_t)site * 2 * d + c0));
+        const float k4[4] = {kk.x, kk.y, kk.z, kk.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          sx += bxv[q][i] * bxv[q][i];
-          sk += kk[i] * kk[i];
-          sd += bxv[q][i] * kk[i];
+          sx += bxv[m][i] * bxv[m][i];
+          sk += k4[i] * k4[i];
+          sd += bxv[m][i] * k4[i];
         }
       }
       sx = warp_sum(sx);
       sk = warp_sum(sk);
       sd = warp_sum(sd);
+      if (lane == 0) {
+        red3[wid][m][0] = sx;
+        red3[wid][m][1] = sk;
+        red3[wid][m][2] = sd;
+      }
+    }
+    __syncthreads();
+#pragma unroll
+    for (int m = 0; m < PT_M; ++m) {
+      if (!act_w || m >= rows) continue;
+      float sx = 0.f, sk = 0.f, sd = 0.f;
+      for (int w = 0; w < nq; ++w) {
+        sx += red3[w][m][0];
+        sk += red3[w][m][1];
+        sd += red3[w][m][2];
+      }
       const float ux = 1.0f / sqrtf(sx / (float)d + 1e-6f);
       const float uk = 1.0f / sqrtf(sk / (float)d + 1e-6f);
       const float alpha = sigmoidf_(sd * ux * uk / sqrtf((float)d));
-#pragma unroll
-      for (int q = 0; q < PT_DQ; ++q) {
-        if (q >= nq) continue;
-        const float4 t = __ldg(reinterpret_cast<const float4*>(ev + q * 128));
-        bxv[q][0] += alpha * t.x;
-        bxv[q][1] += alpha * t.y;
-        bxv[q][2] += alpha * t.z;
-        bxv[q][3] += alpha * t.w;
-      }
+      const float4 ev = __ldg(reinterpret_cast<const float4*>(evc + ((size_t)(m0 + m) * G.n_sites + site) * d + c0));
+      bxv[m][0] += alpha * ev.x;
+      bxv[m][1] += alpha * ev.y;
+      bxv[m][2] += alpha * ev.z;
+      bxv[m][3] += alpha * ev.w;
     }
-    float s2 = 0.f;
+    __syncthreads();
+  }
 #pragma unroll
-    for (int q = 0; q < PT_DQ; ++q) {
-      if (q >= nq) continue;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) s2 += bxv[q][i] * bxv[q][i];
-    }
+  for (int m = 0; m < PT_M; ++m) {
+    float s2 = bxv[m][0] * bxv[m][0] + bxv[m][1] * bxv[m][1] + bxv[m][2] * bxv[m][2] + bxv[m][3] * bxv[m][3];
     s2 = warp_sum(s2);
-    const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
+    if (lane == 0) red3[wid][m][0] = s2;
+  }
+  __syncthreads();
+  if (!act_w) return;
+  const float4 ni = __ldg(reinterpret_cast<const float4*>(norm_in + c0));
 #pragma unroll
-    for (int q = 0; q < PT_DQ; ++q) {
-      if (q >= nq) continue;
-      const int c0 = q * 128 + lane * 4;
-      reinterpret_cast<float4*>(bx_out + (size_t)r * d + q * 128)[lane] =
-          make_float4(bxv[q][0], bxv[q][1], bxv[q][2], bxv[q][3]);
-      const float4 ni = __ldg(reinterpret_cast<const float4*>(norm_in + c0));
-      float h[4] = {(1.0f + ni.x) * bxv[q][0] * inv2, (1.0f + ni.y) * bxv[q][1] * inv2,
-                    (1.0f + ni.z) * bxv[q][2] * inv2, (1.0f + ni.w) * bxv[q][3] * inv2};
-      fwht128_warp(h);
-      reinterpret_cast<float4*>(xh_out + (size_t)r * d + q * 128)[lane] = make_float4(h[0], h[1], h[2], h[3]);
-    }
+  for (int m = 0; m < PT_M; ++m) {
+    if (m >= rows) break;
+    float s2 = 0.f;
+    for (int w = 0; w < nq; ++w) s2 += red3[w][m][0];
+    const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
+    const size_t r = m0 + m;
+    *reinterpret_cast<float4*>(bx_out + r * d + c0) = make_float4(bxv[m][0], bxv[m][1], bxv[m][2], bxv[m][3]);
+    float h[4] = {(1.0f + ni.x) * bxv[m][0] * inv2, (1.0f + ni.y) * bxv[m][1] * inv2,
+                  (1.0f + ni.z) * bxv[m][2] * inv2, (1.0f + ni.w) * bxv[m][3] * inv2};
+    fwht128_warp(h);
+    *reinterpret_cast<float4*>(xh_out + r * d + c0) = make_float4(h[0], h[1], h[2], h[3]);
   }
 }
 
@@ -758,6 +823,41 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
   const int taps = G.taps, tl = taps > 0 ? taps - 1 : 0;
   const float* raw = proj + (size_t)r * G.proj_dim;
   float* tail = tl ? ri.s->qkv_tail + (size_t)li * tl * qkv : nullptr;
+  // Four channels per thread when every segment width is a multiple of 4.
+  if ((qd | kd | vd) % 4 == 0) {
+    const int slot_here = tl ? p % tl : 0;
+    for (int c = 4 * threadIdx.x; c < qkv; c += 4 * blockDim.x) {
+      const float* tp;
+      int dim, cc;
+      if (c < qd) {
+        tp = lp.q_taps; dim = qd; cc = c;
+      } else if (c < qd + kd) {
+        tp = lp.k_taps; dim = kd; cc = c - qd;
+      } else {
+        tp = lp.v_taps; dim = vd; cc = c - qd - kd;
+      }
+      const float4 x = *reinterpret_cast<const float4*>(raw + c);
+      float4 acc = x;
+      if (taps > 0) {
+        const float4 t0 = *reinterpret_cast<const float4*>(tp + cc);
+        acc = make_float4(t0.x * x.x, t0.y * x.y, t0.z * x.z, t0.w * x.w);
+        for (int j = 1; j < taps; ++j) {
+          if (j > p) break;
+          const float4 pv = *reinterpret_cast<const float4*>(
+              rb.mode == MODE_PREFILL ? proj + (size_t)(r - j) * G.proj_dim + c
+                                      : tail + (size_t)((p - j) % tl) * qkv + c);
+          const float4 tj = *reinterpret_cast<const float4*>(tp + j * dim + cc);
+          acc.x += tj.x * pv.x;
+          acc.y += tj.y * pv.y;
+          acc.z += tj.z * pv.z;
+          acc.w += tj.w * pv.w;
+        }
+        if (tl && (rb.mode == MODE_DECODE || p >= ri.len - tl))
+          *reinterpret_cast<float4*>(tail + (size_t)slot_here * qkv + c) = x;
+      }
+      *reinterpret_cast<float4*>(sm + c) = acc;
+    }
+  } else
 #pragma unroll 4
   for (int c = threadIdx.x; c < qkv; c += blockDim.x) {
     const float* tp;
