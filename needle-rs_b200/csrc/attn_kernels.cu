@@ -342,18 +342,21 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
 // In int8 mode the query is fake-quantised (model.rs:289-293): q = code * qs
 // with integer codes, so q.k = qs * sum(code * k8) and the key dot is an exact
 // integer product, run as mma.sync s8 x s8 -> s32 (m16n8k32 / m16n8k16) with
-// the query heads of one KV head as the 16 rows (rows >= rep are zero) and
-// positions as columns. The score is then (dot * qs) * ks * scale, as the
-// reference's f32 dot times the key scale (attention.rs:191-216) up to f32
-// rounding of the query product.
+// positions as the 16 rows (keys straight from shared memory as A) and the
+// query heads of one KV head as the 8 columns (their codes held in registers
+// as B; columns >= rep are zero). The score is then dot * (qs * scale) * ks,
+// the reference's f32 dot times the key scale (attention.rs:191-216) up to
+// f32 rounding of the products.
 //
-// P.V runs as m16n8k16 f16 MMAs with f32 accumulation: int8 values are exact
-// in f16, and each weight p * vs is split into an f16 high part and an f16
-// remainder (two MMAs), which keeps about 22 bits of the weight. The score
-// fragment layout of the first MMA is the A-fragment layout of the second, so
-// the weights never leave registers. Values are widened to f16 in shared
-// memory (bias trick: byte ^ 0x80 placed under exponent byte 0x64 is 1024 +
-// u in f16; subtracting 1152 gives the signed value) and fed by ldmatrix.trans.
+// P.V runs transposed, O^T = V^T P^T, as m16n8k16 f16 MMAs with f32
+// accumulation: value dimensions are the 16 rows (V^T fed by ldmatrix.trans
+// from f16 values in shared memory), heads the 8 columns. int8 values are exact
+// in f16 (bias trick: byte ^ 0x80 placed under exponent byte 0x64 is 1024 + u
+// in f16; subtracting 1152 gives the signed value), and each weight p * vs is
+// split into an f16 high part and an f16 remainder (two MMAs), which keeps
+// about 22 bits of the weight. The weights leave the score fragment as
+// [position][head] 8x8 blocks; movmatrix.trans turns each into the
+// [head][position] pairs of the B fragment, so they never touch memory.
 //
 // Each of the four warps of a CTA owns every fourth 32-position block of the
 // CTA's range with its own cp.async double buffer and its own online softmax,
@@ -409,6 +412,14 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(s));
+}
+
+// Transpose of an 8x8 b16 matrix held in the accumulator-fragment layout
+// (lane 4r + c/2 holds row r, columns c and c + 1).
+__device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  return y;
 }
 
 // Four signed bytes -> two f16 pairs (exact).
@@ -488,25 +499,37 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
   // Scores are kept in base-2 units (times log2 e) so the softmax uses exp2f.
   const float scale = 1.0f / sqrtf((float)QK) * 1.44269504088896341f;
 
-  // Query codes of head g of this KV head as A fragments (rows >= rep zero).
+  // Query codes as the B operand of the key MMAs: column n of B is query head
+  // kh * rep + n (columns >= rep are zero), so lane (g, t) holds head g's
+  // codes at k = 4t.. of each 16-wide half of a 32-wide k step.
   const bool hv = g < rep;
   const int8_t* qr = q8 + (size_t)r * G.q_dim + (size_t)(kh * rep + (hv ? g : 0)) * QK;
-  uint32_t qa[T::NK32 > 0 ? T::NK32 : 1][4];
-  uint32_t qa16 = 0;
+  uint32_t qb[T::NK32 > 0 ? T::NK32 : 1][2];
+  uint32_t qb16 = 0;
 #pragma unroll
   for (int s = 0; s < T::NK32; ++s) {
-    qa[s][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + s * 32 + t * 4)) : 0u;
-    qa[s][1] = 0u;
-    qa[s][2] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + s * 32 + 16 + t * 4)) : 0u;
-    qa[s][3] = 0u;
+    qb[s][0] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + s * 32 + t * 4)) : 0u;
+    qb[s][1] = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + s * 32 + 16 + t * 4)) : 0u;
   }
-  if (T::K16) qa16 = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + T::NK32 * 32 + t * 4)) : 0u;
-  const float qs = hv ? q8s[(size_t)r * G.heads + kh * rep + g] : 0.f;
-
-  float m = -INFINITY, l = 0.f;
-  float o[T::NT][4];
+  if (T::K16) qb16 = hv ? __ldg(reinterpret_cast<const uint32_t*>(qr + T::NK32 * 32 + t * 4)) : 0u;
+  // This lane's score columns are heads 2t and 2t + 1: the query scale times
+  // the softmax scale for each (zero for padding columns).
+  float qsc[2];
 #pragma unroll
-  for (int i = 0; i < T::NT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
+  for (int e = 0; e < 2; ++e) {
+    const int h = 2 * t + e;
+    qsc[e] = h < rep ? q8s[(size_t)r * G.heads + kh * rep + h] * scale : 0.f;
+  }
+
+  // Running max and this lane's share of the sum for heads 2t, 2t + 1.
+  float m[2] = {-INFINITY, -INFINITY}, l[2] = {0.f, 0.f};
+  // O^T accumulators: m-tile mt covers value dims mt*16 .. mt*16+15; lane
+  // (g, t) holds dims mt*16+g (regs 0, 1) and mt*16+g+8 (regs 2, 3) of heads
+  // 2t (regs 0, 2) and 2t + 1 (regs 1, 3).
+  constexpr int MT = VH / 16;
+  float o[MT][4];
+#pragma unroll
+  for (int i = 0; i < MT; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
 
   const int nblk = a <= b ? (b - a) / WB + 1 : 0;
   const int mine = nblk > wid ? (nblk - wid + 3) / 4 : 0;  // blocks wid, wid + 4, ...
@@ -538,92 +561,111 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
       *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0) = h0;
       *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0 + 8) = h1;
     }
-    // ---- integer key dots: n-tile j covers positions j*8 .. j*8+7
-    // (consecutive MMAs target different n-tiles, so they do not wait on each other)
-    float sc[8];
-    int d[4][4];
+    // ---- integer key dots, positions as rows: m-tile j covers positions
+    // j*16 .. j*16+15; d[j] = (pos g, heads 2t, 2t+1), (pos g+8, same heads)
+    int d[2][4];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0;
+    for (int j = 0; j < 2; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0;
 #pragma unroll
     for (int s = 0; s < T::NK32; ++s)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int8_t* kr = W.k[buf] + (j * 8 + g) * T::KS;
-        mma_s8_k32(d[j], qa[s], *reinterpret_cast<const uint32_t*>(kr + s * 32 + t * 4),
-                   *reinterpret_cast<const uint32_t*>(kr + s * 32 + 16 + t * 4));
+      for (int j = 0; j < 2; ++j) {
+        const int8_t* k0 = W.k[buf] + (j * 16 + g) * T::KS + s * 32 + t * 4;
+        const int8_t* k1 = k0 + 8 * T::KS;
+        const uint32_t ka[4] = {*reinterpret_cast<const uint32_t*>(k0), *reinterpret_cast<const uint32_t*>(k1),
+                                *reinterpret_cast<const uint32_t*>(k0 + 16),
+                                *reinterpret_cast<const uint32_t*>(k1 + 16)};
+        mma_s8_k32(d[j], ka, qb[s][0], qb[s][1]);
       }
     if (T::K16) {
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const int8_t* kr = W.k[buf] + (j * 8 + g) * T::KS;
-        mma_s8_k16(d[j], qa16, 0u, *reinterpret_cast<const uint32_t*>(kr + T::NK32 * 32 + t * 4));
+      for (int j = 0; j < 2; ++j) {
+        const int8_t* k0 = W.k[buf] + (j * 16 + g) * T::KS + T::NK32 * 32 + t * 4;
+        mma_s8_k16(d[j], *reinterpret_cast<const uint32_t*>(k0),
+                   *reinterpret_cast<const uint32_t*>(k0 + 8 * T::KS), qb16);
       }
     }
+    // Score i of this lane: position j*16 + g + 8*hf (i = 4j + 2hf + e), head 2t + e.
+    float sc[8];
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
+    for (int j = 0; j < 2; ++j)
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int i = j * 8 + t * 2 + e;
-        sc[j * 2 + e] = n0 + i <= b ? (float)d[j][e] * qs * W.ks[buf][i] * scale : -INFINITY;
+      for (int hf = 0; hf < 2; ++hf) {
+        const int pi = j * 16 + hf * 8 + g;
+        const float ksv = W.ks[buf][pi];
+        const bool ok = n0 + pi <= b;
+#pragma unroll
+        for (int e = 0; e < 2; ++e)
+          sc[4 * j + 2 * hf + e] = ok ? (float)d[j][2 * hf + e] * qsc[e] * ksv : -INFINITY;
       }
-    // ---- online softmax of row g over this block (the four lanes of a row
-    // hold 8 positions each)
-    float mx = sc[0];
+    // ---- online softmax per head (column): the 8 lanes sharing t hold
+    // the block's 32 positions of heads 2t, 2t + 1
+    float corr[2], mz[2];
 #pragma unroll
-    for (int i = 1; i < 8; ++i) mx = fmaxf(mx, sc[i]);
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-    const float mnew = fmaxf(m, mx);
-    const float corr = m == -INFINITY ? 0.f : exp2f(m - mnew);
-    float pw[8], sum = 0.f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float pe = sc[i] == -INFINITY ? 0.f : exp2f(sc[i] - mnew);
-      sum += pe;
-      pw[i] = pe * W.vs[buf][(i >> 1) * 8 + t * 2 + (i & 1)];
+    for (int e = 0; e < 2; ++e) {
+      float mx = fmaxf(fmaxf(sc[e], sc[2 + e]), fmaxf(sc[4 + e], sc[6 + e]));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+      const float mnew = fmaxf(m[e], mx);
+      mz[e] = mnew == -INFINITY ? 0.f : mnew;  // every position so far masked: weights are 0
+      corr[e] = exp2f(m[e] - mz[e]);
+      m[e] = mnew;
     }
-    sum += __shfl_xor_sync(0xffffffffu, sum, 1);
-    sum += __shfl_xor_sync(0xffffffffu, sum, 2);
-    l = l * corr + sum;
-    m = mnew;
+    float pw[8];
 #pragma unroll
-    for (int i = 0; i < T::NT; ++i) {
-      o[i][0] *= corr;
-      o[i][1] *= corr;
+    for (int i = 0; i < 8; ++i) pw[i] = exp2f(sc[i] - mz[i & 1]);
+#pragma unroll
+    for (int e = 0; e < 2; ++e) l[e] = l[e] * corr[e] + ((pw[e] + pw[2 + e]) + (pw[4 + e] + pw[6 + e]));
+#pragma unroll
+    for (int j = 0; j < 2; ++j)
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const float vsv = W.vs[buf][j * 16 + hf * 8 + g];
+        pw[4 * j + 2 * hf] *= vsv;
+        pw[4 * j + 2 * hf + 1] *= vsv;
+      }
+#pragma unroll
+    for (int i = 0; i < MT; ++i) {
+      o[i][0] *= corr[0];
+      o[i][1] *= corr[1];
+      o[i][2] *= corr[0];
+      o[i][3] *= corr[1];
     }
     __syncwarp();  // f16 values visible to every lane
-    // ---- P.V: k-step kk covers positions kk*16 .. kk*16+15 (score n-tiles 2kk, 2kk+1)
+    // ---- O^T += V^T P^T: k-step j covers positions j*16 .. j*16+15. The
+    // weights (f16 high part and remainder) of 8 positions x 8 heads sit in
+    // the score fragment as [position][head]; movmatrix.trans turns each into
+    // the [head][position] pairs of the B fragment.
 #pragma unroll
-    for (int kk = 0; kk < 2; ++kk) {
-      uint32_t ah[4], al[4];
-      const float x0 = pw[4 * kk], x1 = pw[4 * kk + 1], x2 = pw[4 * kk + 2], x3 = pw[4 * kk + 3];
-      ah[0] = pack_h2(x0, x1);
-      ah[2] = pack_h2(x2, x3);
-      ah[1] = ah[3] = 0u;
-      {
-        const __half2 h0 = *reinterpret_cast<const __half2*>(&ah[0]);
-        const __half2 h2 = *reinterpret_cast<const __half2*>(&ah[2]);
-        al[0] = pack_h2(x0 - __low2float(h0), x1 - __high2float(h0));
-        al[2] = pack_h2(x2 - __low2float(h2), x3 - __high2float(h2));
-        al[1] = al[3] = 0u;
+    for (int j = 0; j < 2; ++j) {
+      uint32_t bh[2], bl[2];
+#pragma unroll
+      for (int hf = 0; hf < 2; ++hf) {
+        const float x0 = pw[4 * j + 2 * hf], x1 = pw[4 * j + 2 * hf + 1];
+        const uint32_t h = pack_h2(x0, x1);
+        const __half2 hh = *reinterpret_cast<const __half2*>(&h);
+        const uint32_t lw = pack_h2(x0 - __low2float(hh), x1 - __high2float(hh));
+        bh[hf] = movmatrix_t(h);
+        bl[hf] = movmatrix_t(lw);
       }
-      const int mat = lane >> 3, row = lane & 7;
-      uint32_t bf[T::NT / 2][4];
+      const int mi = lane >> 3, ri = lane & 7;
 #pragma unroll
-      for (int np = 0; np < T::NT / 2; ++np)
-        ldsm_x4_trans(bf[np], W.vh + (kk * 16 + (mat & 1) * 8 + row) * T::VHS + np * 16 + (mat >> 1) * 8);
-#pragma unroll
-      for (int np = 0; np < T::NT / 2; ++np) {
-        mma_f16_k16(o[2 * np], ah, bf[np][0], bf[np][1]);
-        mma_f16_k16(o[2 * np + 1], ah, bf[np][2], bf[np][3]);
-      }
-#pragma unroll
-      for (int np = 0; np < T::NT / 2; ++np) {
-        mma_f16_k16(o[2 * np], al, bf[np][0], bf[np][1]);
-        mma_f16_k16(o[2 * np + 1], al, bf[np][2], bf[np][3]);
+      for (int mt = 0; mt < MT; ++mt) {
+        uint32_t va[4];
+        ldsm_x4_trans(va, W.vh + (j * 16 + (mi >> 1) * 8 + ri) * T::VHS + mt * 16 + (mi & 1) * 8);
+        mma_f16_k16(o[mt], va, bh[0], bh[1]);
+        mma_f16_k16(o[mt], va, bl[0], bl[1]);
       }
     }
     __syncwarp();  // before the next block overwrites the f16 values
+  }
+  // Sum each head's share over the 8 lanes holding it.
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 4);
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 8);
+    l[e] += __shfl_xor_sync(0xffffffffu, l[e], 16);
   }
 
   // ---- merge the four warps (shared memory reused)
@@ -631,15 +673,18 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
   float* Wm = reinterpret_cast<float*>(smraw);  // [4][8]
   float* Wl = Wm + 32;                           // [4][8]
   float* Wo = Wl + 32;                           // [4][8][VH]
-  if (hv) {
-    if (t == 0) {
-      Wm[wid * 8 + g] = m;
-      Wl[wid * 8 + g] = l;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const int h = 2 * t + e;
+    if (h >= rep) continue;
+    if (g == 0) {
+      Wm[wid * 8 + h] = m[e];
+      Wl[wid * 8 + h] = l[e];
     }
 #pragma unroll
-    for (int i = 0; i < T::NT; ++i) {
-      Wo[(wid * 8 + g) * VH + i * 8 + t * 2] = o[i][0];
-      Wo[(wid * 8 + g) * VH + i * 8 + t * 2 + 1] = o[i][1];
+    for (int mt = 0; mt < MT; ++mt) {
+      Wo[(wid * 8 + h) * VH + mt * 16 + g] = o[mt][e];
+      Wo[(wid * 8 + h) * VH + mt * 16 + g + 8] = o[mt][2 + e];
     }
   }
   __syncthreads();
