@@ -385,6 +385,7 @@ struct __align__(16) MmaWarpSmem {
   float ks[2][WB];
   float vs[2][WB];
   __half vh[WB * T::VHS];
+  uint64_t bar[2];  // bulk-copy completion of buffer 0 / 1
 };
 
 __device__ __forceinline__ void mma_s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -477,13 +478,84 @@ __device__ __forceinline__ void mma_issue(MmaWarpSmem<QK, VH>& W, int buf, const
   }
 }
 
+// ---- bulk copies for ring sources whose per-head rows are contiguous.
+constexpr unsigned long long ATTN_WAIT_NS = 1000000000ull;  // bound of every wait: one second
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ bool mbar_try_parity(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for phase `parity` of `bar`, giving up after ATTN_WAIT_NS.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
+  if (mbar_try_parity(bar, parity)) return true;
+  unsigned long long t0, t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+  while (true) {
+    if (mbar_try_parity(bar, parity)) return true;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    if (t - t0 > ATTN_WAIT_NS) return false;
+  }
+}
+
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst)),
+      "l"(src), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Keys and values of one warp block [n0, n0 + WB) clipped at hi, as at most
+// two contiguous pieces per operand (the ring wraps at most once: slots >= WB)
+// copied by lane 0 and completing on W.bar[buf]; the scales go by cp.async
+// (zero-filled past hi). Rows past hi keep stale bytes: their scores are
+// masked and their value scales are zero, so they contribute nothing.
+template <int QK, int VH>
+__device__ __forceinline__ void mma_issue_bulk(MmaWarpSmem<QK, VH>& W, int buf, const AttnSrc& src, int kh,
+                                               int n0, int hi, int lane) {
+  const int cnt = min(WB, hi - n0 + 1);
+  const int idx0 = n0 % src.slots;
+  if (lane == 0) {
+    const int c1 = min(cnt, src.slots - idx0);
+    const int8_t* kb = (const int8_t*)src.k + kh * src.k_head;
+    const int8_t* vb = (const int8_t*)src.v + kh * src.v_head;
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(&W.bar[buf])),
+                 "r"((uint32_t)cnt * (QK + VH))
+                 : "memory");
+    bulk_g2s(W.k[buf], kb + (long)idx0 * QK, (uint32_t)c1 * QK, &W.bar[buf]);
+    bulk_g2s(W.v[buf], vb + (long)idx0 * VH, (uint32_t)c1 * VH, &W.bar[buf]);
+    if (cnt > c1) {
+      bulk_g2s(W.k[buf] + c1 * QK, kb, (uint32_t)(cnt - c1) * QK, &W.bar[buf]);
+      bulk_g2s(W.v[buf] + c1 * VH, vb, (uint32_t)(cnt - c1) * VH, &W.bar[buf]);
+    }
+  }
+  const bool ok = lane < cnt;
+  int idx = idx0 + lane;
+  idx = idx >= src.slots ? idx - src.slots : idx;
+  idx = ok ? idx : 0;
+  cp_async4(&W.ks[buf][lane], src.ks + (long)idx * src.s_row + kh * src.s_head, ok);
+  cp_async4(&W.vs[buf][lane], src.vs + (long)idx * src.s_row + kh * src.s_head, ok);
+}
+
 template <int QK, int VH>
 __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, RowBatch rb, int window, int nsplit,
                                                             const int8_t* __restrict__ q8,
                                                             const float* __restrict__ q8s, const void* pk,
                                                             const void* pv, const float* pks, const float* pvs,
                                                             float* __restrict__ part, const float* __restrict__ proj,
-                                                            float* __restrict__ oh, int* __restrict__ cnt) {
+                                                            float* __restrict__ oh, int* __restrict__ cnt,
+                                                            int* __restrict__ werr) {
   using T = MmaTile<QK, VH>;
   using WS = MmaWarpSmem<QK, VH>;
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -533,19 +605,43 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
 
   const int nblk = a <= b ? (b - a) / WB + 1 : 0;
   const int mine = nblk > wid ? (nblk - wid + 3) / 4 : 0;  // blocks wid, wid + 4, ...
-  if (mine > 0) {
-    mma_issue<QK, VH>(W, 0, src, kh, a + wid * WB, b, lane);
-    cp_commit();
+  // Ring rows of one KV head are contiguous: lane 0 moves a block with bulk
+  // copies. Other sources (the prefill scratch interleaves KV heads) and padded
+  // key rows go by per-lane cp.async.
+  const bool bulk = src.slots >= WB && T::KS == QK;
+  if (bulk) {
+    if (lane == 0) {
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&W.bar[0])));
+      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&W.bar[1])));
+      asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
   }
+  auto issue = [&](int buf, int n0) {
+    if (bulk)
+      mma_issue_bulk<QK, VH>(W, buf, src, kh, n0, b, lane);
+    else
+      mma_issue<QK, VH>(W, buf, src, kh, n0, b, lane);
+    cp_commit();
+  };
+  bool failed = false;
+  if (mine > 0) issue(0, a + wid * WB);
   for (int c = 0; c < mine; ++c) {
     const int buf = c & 1;
     const int n0 = a + (wid + 4 * c) * WB;
     if (c + 1 < mine) {
-      mma_issue<QK, VH>(W, buf ^ 1, src, kh, n0 + 4 * WB, b, lane);
-      cp_commit();
+      issue(buf ^ 1, n0 + 4 * WB);
       cp_wait<1>();
     } else {
       cp_wait<0>();
+    }
+    if (bulk && !__all_sync(0xffffffffu, mbar_wait_bounded(&W.bar[buf], (uint32_t)(c >> 1) & 1u))) {
+      // The copy never completed: report it, let the copies in flight land
+      // (bounded) and leave this warp's partial empty.
+      if (lane == 0) atomicExch(werr, 2);
+      if (c + 1 < mine) mbar_wait_bounded(&W.bar[buf ^ 1], (uint32_t)((c + 1) >> 1) & 1u);
+      failed = true;
+      break;
     }
     __syncwarp();
     // ---- values to f16 (each lane widens 16-byte pieces)
@@ -659,6 +755,14 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
       }
     }
     __syncwarp();  // before the next block overwrites the f16 values
+  }
+  if (failed) {
+    m[0] = m[1] = -INFINITY;
+    l[0] = l[1] = 0.f;
+  }
+  if (bulk && lane == 0) {  // the barriers' memory is reused by the merge below
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&W.bar[0])) : "memory");
+    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&W.bar[1])) : "memory");
   }
   // Sum each head's share over the 8 lanes holding it.
 #pragma unroll
@@ -775,7 +879,7 @@ template <int QK, int VH>
 static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
                                         const int8_t* q8, const float* q8s, const void* pk, const void* pv,
                                         const float* pks, const float* pvs, float* part, const float* proj,
-                                        float* oh, int* cnt, cudaStream_t st) {
+                                        float* oh, int* cnt, int* werr, cudaStream_t st) {
   using WS = MmaWarpSmem<QK, VH>;
   const int rep = G.heads / G.kvh;
   const size_t fin = (size_t)(64 + 4 * 8 * VH + rep * (VH + 2) + rep * 64 + 8 + rep * VH) * sizeof(float);
@@ -784,7 +888,7 @@ static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb
   cudaError_t e = allow_smem((const void*)k, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(rb.M, G.kvh, nsplit);
-  k<<<grid, 128, smem, st>>>(G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, cnt);
+  k<<<grid, 128, smem, st>>>(G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, cnt, werr);
   return cudaGetLastError();
 }
 
@@ -821,19 +925,19 @@ static cudaError_t launch_layer_attn_t(const Geo& G, int li, const RowBatch& rb,
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
                              const void* pv, const float* pks, const float* pvs, float* part,
-                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt) {
+                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt, int* werr) {
   if (rb.M <= 0) return cudaSuccess;
   const int rep = G.heads / G.kvh;
   if (rep > AT_MAXREP || nsplit < 1) return cudaErrorInvalidValue;
   if (int8) {
-    if (!q8 || !q8s) return cudaErrorInvalidValue;
+    if (!q8 || !q8s || !werr) return cudaErrorInvalidValue;
     // With proj, oh and cnt the kernel also finishes (attn_fuses_finish);
     // without them it leaves the partials to attn_finish.
     const bool fuse = proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64;
     if (!fuse) proj = nullptr, oh = nullptr, cnt = nullptr;
 #define NB_ATI(Q, V)                                                                                         \
   return launch_layer_attn_i8<Q, V>(G, li, rb, lp.window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, \
-                                    cnt, st)
+                                    cnt, werr, st)
     if (G.vh == 64) {
       switch (G.qk) {
         case 16: NB_ATI(16, 64);

@@ -849,7 +849,7 @@ cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int 
     NB_MARK(PK_QKV_POST, 1);
     const bool fused = attn_fuses_finish(G, int8 ? 1 : 0) && nsplit <= 64;
     NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, ws.qpost, ws.q8, ws.q8s, ws.pk, ws.pv, ws.pks, ws.pvs,
-                            ws.part, st, int8 ? 1 : 0, ws.proj, ws.oh, ws.cnt));
+                            ws.part, st, int8 ? 1 : 0, ws.proj, ws.oh, ws.cnt, d_wait_flag));
     NB_MARK(PK_ATTN, 1);
     if (!fused) NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
     NB_MARK(PK_ATTN_FINISH, fused ? 0 : 1);

@@ -156,7 +156,7 @@ class Engine {
   const float* final_norm = nullptr;
   Workspace ws;
   uint64_t epoch = 1;  // bumped whenever a session's device layout changes
-  int* d_wait_flag = nullptr;  // tensor-core GEMM: a bounded wait expired (device flag)
+  int* d_wait_flag = nullptr;  // tensor-core GEMM or int8 attention: a bounded wait expired (device flag)
   int* h_wait_flag = nullptr;  // pinned host copy, refreshed before each synchronous return
 
   // Queues the copy of the device wait flag on `st`; after the stream is

@@ -106,11 +106,12 @@ size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit);
 // int8 = 1 with proj / oh / cnt (per-row, per-KV-head counters, zero-initialised)
 // and attn_fuses_finish(): the kernel also merges the splits, gates and
 // rotates into oh, so attn_finish is not launched.
+// werr: device flag set to 2 when a bounded wait of the int8 kernel's copies
+// expired (required for int8 = 1).
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
                              const void* pv, const float* pks, const float* pvs, float* part,
-                             cudaStream_t st, int int8, const float* proj = nullptr, float* oh = nullptr,
-                             int* cnt = nullptr);
+                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt, int* werr);
 bool attn_fuses_finish(const Geo& G, int int8);
 cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
                                const float* proj, float* oh, cudaStream_t st);
