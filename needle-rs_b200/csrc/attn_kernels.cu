@@ -323,6 +323,7 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
                                                                 const void* pk, const void* pv,
                                                                 const float* pks, const float* pvs,
                                                                 float* __restrict__ part) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   extern __shared__ __align__(16) unsigned char smraw[];
   auto& S = *reinterpret_cast<AttnSmem<INT8, QK, VH>*>(smraw);
   const int r = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
@@ -413,6 +414,15 @@ __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
                : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                : "r"(s));
+}
+
+// 2^x by the hardware approximation (PTX ex2.approx.ftz.f32, relative error
+// about 2^-22); used for softmax weights, whose arguments are <= 0 and whose
+// sum is >= 1, so flushing denormal results to zero changes nothing material.
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
 }
 
 // Transpose of an 8x8 b16 matrix held in the accumulator-fragment layout
@@ -556,6 +566,7 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
                                                             float* __restrict__ part, const float* __restrict__ proj,
                                                             float* __restrict__ oh, int* __restrict__ cnt,
                                                             int* __restrict__ werr) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   using T = MmaTile<QK, VH>;
   using WS = MmaWarpSmem<QK, VH>;
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -705,12 +716,12 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float mnew = fmaxf(m[e], mx);
       mz[e] = mnew == -INFINITY ? 0.f : mnew;  // every position so far masked: weights are 0
-      corr[e] = exp2f(m[e] - mz[e]);
+      corr[e] = ex2_fast(m[e] - mz[e]);
       m[e] = mnew;
     }
     float pw[8];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pw[i] = exp2f(sc[i] - mz[i & 1]);
+    for (int i = 0; i < 8; ++i) pw[i] = ex2_fast(sc[i] - mz[i & 1]);
 #pragma unroll
     for (int e = 0; e < 2; ++e) l[e] = l[e] * corr[e] + ((pw[e] + pw[2 + e]) + (pw[4 + e] + pw[6 + e]));
 #pragma unroll
@@ -1127,6 +1138,7 @@ cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float*
 // (model.rs:305-308) and the rotation of out_proj's prepare_input.
 __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ part,
                                    const float* __restrict__ proj, float* __restrict__ oh) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   extern __shared__ __align__(16) float sm[];
   __shared__ float wsm[8][64];  // per-warp split weights (nsplit <= 64)
   const int r = blockIdx.x;

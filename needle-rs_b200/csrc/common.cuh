@@ -161,6 +161,15 @@ __device__ __forceinline__ void cp_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
 }
 
+// Programmatic dependent launch. A kernel launched with the programmatic
+// stream-serialization attribute may start while the previous kernel in the
+// stream is still running; pdl_wait() blocks until that kernel has completed
+// and its memory is visible (a no-op for a normal launch), so everything a
+// kernel reads or writes that another kernel touches comes after it.
+// pdl_trigger() lets the next such kernel be scheduled early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
 
 // Packed row and norms of logical row r of a (multi-segment) CQ matrix.

@@ -21,47 +21,36 @@ namespace nb {
 // ----------------------------------------------------------------------------
 // GEMV: MT activation rows at most (the batch-1 decode path and small batches).
 //
-// Each output row is split over LPR lanes; lane `sub` of a row reads the row's
-// 16-byte chunks sub, sub+LPR, ... with 128-bit loads, so a warp reads
-// 32/LPR rows x LPR*16 contiguous bytes per instruction. The codebook is
-// expanded into a byte-indexed table in shared memory (one table entry decodes
-// all indices of a packed byte, the GPU form of cq.rs:932-964), replicated so
-// the lanes of one shared-memory phase hit distinct banks. The activation rows
-// sit in shared memory with a 4-float pad after every chunk-sized block so that
-// lanes working on different chunks of the same row hit different banks.
+// At these sizes the kernel is latency-bound, so it is ordered around the
+// critical path: each lane first issues the 128-bit loads of its row chunks
+// and their FP16 norms (weights never change, so this happens before waiting
+// on the kernel that produced the activation), then the CTA builds the byte
+// table of the codebook (one entry decodes every index of a packed byte, the
+// GPU form of cq.rs:932-964; 4 KB for 2-bit, 2 KB for 4-bit), waits for the
+// producer (programmatic dependent launch) and stages the activation rows.
+// Each output row is split over LPR lanes: lane `sub` of a row takes the row's
+// 16-byte chunks sub, sub+LPR, ... The activation rows sit in shared memory
+// with a 4-float pad after every chunk-sized block so that lanes working on
+// different chunks of the same row hit different banks. 128-thread CTAs keep
+// the grid wide: a [3072, 768] 2-bit matrix spreads over 192 CTAs.
 // ----------------------------------------------------------------------------
 template <int BITS>
 struct ChunkTraits;
 template <>
 struct ChunkTraits<2> {
-  static constexpr int E = 64;       // elements per 16-byte chunk
-  static constexpr int P = 4;        // levels per byte
-  static constexpr int COPIES = 8;   // LUT copies (LDS.128: 8 lanes per phase)
+  static constexpr int E = 64;  // elements per 16-byte chunk
+  static constexpr int P = 4;   // levels per byte
 };
 template <>
 struct ChunkTraits<4> {
   static constexpr int E = 32;
   static constexpr int P = 2;
-  static constexpr int COPIES = 16;  // LDS.64: 16 lanes per phase
 };
 
-__host__ __device__ inline int padded_len(int in_pad, int E) { return in_pad + (in_pad / E) * 4; }
+constexpr int GV_THREADS = 128;
+constexpr int GV_PRE = 2;  // chunks per lane fetched before the producer wait
 
-// `lev` is a 16-float scratch in shared memory for the level table, so the
-// byte table is built with bank-parallel shared loads instead of lane-divergent
-// parameter-space lookups.
-template <int BITS>
-__device__ __forceinline__ void build_lut_smem(const CqMat& W, float* lut, float* lev) {
-  using T = ChunkTraits<BITS>;
-  if (threadIdx.x < 16) lev[threadIdx.x] = W.levels[threadIdx.x];
-  __syncthreads();
-  const int total = 256 * T::COPIES;
-  for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    int byte = i / T::COPIES;
-#pragma unroll
-    for (int j = 0; j < T::P; ++j) lut[i * T::P + j] = lev[(byte >> (j * BITS)) & ((1 << BITS) - 1)];
-  }
-}
+__host__ __device__ inline int padded_len(int in_pad, int E) { return in_pad + (in_pad / E) * 4; }
 
 // Segment holding logical row r: walk the segments in order and stop at the
 // first one whose end lies beyond r.
@@ -78,76 +67,111 @@ __device__ __forceinline__ int find_seg(const CqMat& W, int r, int* local) {
   return s;
 }
 
+// Dot of one 16-byte chunk (chunk index c) with the MT staged activation rows.
+template <int BITS, int MT>
+__device__ __forceinline__ void gemv_chunk(const uint4 w, float nv, int c, const float* lut, const float* xs,
+                                           int plen, int M, float (&acc)[MT]) {
+  using T = ChunkTraits<BITS>;
+  const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
+  float part[MT];
+#pragma unroll
+  for (int m = 0; m < MT; ++m) part[m] = 0.f;
+  const float* xc = xs + c * (T::E + 4);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+#pragma unroll
+    for (int bb = 0; bb < 4; ++bb) {
+      const int byte = (wd[q] >> (8 * bb)) & 0xff;
+      const int e0 = (q * 4 + bb) * T::P;
+      if (BITS == 2) {
+        const float4 lv = *reinterpret_cast<const float4*>(lut + byte * 4);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < M) {
+            const float4 xv = *reinterpret_cast<const float4*>(xc + m * plen + e0);
+            part[m] += lv.x * xv.x + lv.y * xv.y + lv.z * xv.z + lv.w * xv.w;
+          }
+        }
+      } else {
+        const float2 lv = *reinterpret_cast<const float2*>(lut + byte * 2);
+#pragma unroll
+        for (int m = 0; m < MT; ++m) {
+          if (m < M) {
+            const float2 xv = *reinterpret_cast<const float2*>(xc + m * plen + e0);
+            part[m] += lv.x * xv.x + lv.y * xv.y;
+          }
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int m = 0; m < MT; ++m) acc[m] += nv * part[m];
+}
+
 template <int BITS, int LPR, int MT>
-__global__ void __launch_bounds__(256) cq_gemv_kernel(CqMat W, const float* __restrict__ xh, int ldx,
-                                                      int M, float* __restrict__ y, int ldy,
-                                                      int row0, int nrows) {
+__global__ void __launch_bounds__(GV_THREADS) cq_gemv_kernel(CqMat W, const float* __restrict__ xh, int ldx,
+                                                             int M, float* __restrict__ y, int ldy, int row0,
+                                                             int nrows) {
   using T = ChunkTraits<BITS>;
   extern __shared__ __align__(16) float smem[];
-  const int plen = padded_len(W.in_pad, T::E);
-  float* xs = smem;                       // [MT][plen]
-  float* lut = smem + MT * plen;          // [256 * COPIES * P]
-  for (int m = 0; m < M; ++m)
-    for (int k = threadIdx.x; k < W.in_pad; k += blockDim.x)
-      xs[m * plen + k + (k / T::E) * 4] = xh[(size_t)m * ldx + k];
   __shared__ float lev[16];
-  build_lut_smem<BITS>(W, lut, lev);
-  __syncthreads();
-
+  const int plen = padded_len(W.in_pad, T::E);
+  float* lut = smem;                // [256 * P]
+  float* xs = smem + 256 * T::P;    // [MT][plen]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  const int rows_per_warp = 32 / LPR;
   const int sub = lane % LPR;
-  const int r = (blockIdx.x * (blockDim.x >> 5) + warp) * rows_per_warp + lane / LPR;
+  const int r = (blockIdx.x * (GV_THREADS / 32) + warp) * (32 / LPR) + lane / LPR;
   const bool active = r < nrows;
+  const int nchunks = W.row_bytes / 16;
+  const uint8_t* row = nullptr;
+  const __half* nrm = nullptr;
+  if (active) {
+    int local;
+    const int s = find_seg(W, row0 + r, &local);
+    row = W.seg[s].packed + (size_t)local * W.row_bytes;
+    nrm = W.seg[s].norms + (size_t)local * W.groups;
+  }
+  // 1. this lane's first chunks and their norms
+  uint4 wpre[GV_PRE];
+  float npre[GV_PRE];
+#pragma unroll
+  for (int j = 0; j < GV_PRE; ++j) {
+    const int c = sub + j * LPR;
+    const bool ok = active && c < nchunks;
+    wpre[j] = ok ? __ldg(reinterpret_cast<const uint4*>(row) + c) : make_uint4(0u, 0u, 0u, 0u);
+    npre[j] = ok ? __half2float(nrm[c * T::E / W.group]) : 0.f;
+  }
+  // 2. byte table
+  if (threadIdx.x < 16) lev[threadIdx.x] = W.levels[threadIdx.x];
+  __syncthreads();
+  for (int i = threadIdx.x; i < 256; i += GV_THREADS) {
+#pragma unroll
+    for (int j = 0; j < T::P; ++j) lut[i * T::P + j] = lev[(i >> (j * BITS)) & ((1 << BITS) - 1)];
+  }
+  // 3. the activation rows, written by the previous kernel
+  pdl_wait();
+  const int q4 = W.in_pad / 4;
+  for (int m = 0; m < M; ++m)
+    for (int i = threadIdx.x; i < q4; i += GV_THREADS) {
+      const int k = i * 4;
+      *reinterpret_cast<float4*>(xs + m * plen + k + (k / T::E) * 4) =
+          *reinterpret_cast<const float4*>(xh + (size_t)m * ldx + k);
+    }
+  __syncthreads();
+  pdl_trigger();
+
   float acc[MT];
 #pragma unroll
   for (int m = 0; m < MT; ++m) acc[m] = 0.f;
   if (active) {
-    int local;
-    int s = find_seg(W, row0 + r, &local);
-    const uint8_t* row = W.seg[s].packed + (size_t)local * W.row_bytes;
-    const __half* nrm = W.seg[s].norms + (size_t)local * W.groups;
-    const int nchunks = W.row_bytes / 16;
-    const int copy = lane % T::COPIES;
-    for (int c = sub; c < nchunks; c += LPR) {
-      uint4 w = __ldg(reinterpret_cast<const uint4*>(row) + c);
-      const int k0 = c * T::E;
-      const float nv = __half2float(nrm[k0 / W.group]);
-      const uint32_t wd[4] = {w.x, w.y, w.z, w.w};
-      float part[MT];
 #pragma unroll
-      for (int m = 0; m < MT; ++m) part[m] = 0.f;
-      const float* xc = xs + c * (T::E + 4);
-#pragma unroll
-      for (int q = 0; q < 4; ++q) {
-#pragma unroll
-        for (int bb = 0; bb < 4; ++bb) {
-          const int byte = (wd[q] >> (8 * bb)) & 0xff;
-          const int e0 = (q * 4 + bb) * T::P;
-          if (BITS == 2) {
-            const float4 lv = *reinterpret_cast<const float4*>(lut + (byte * T::COPIES + copy) * 4);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              if (m < M) {
-                const float4 xv = *reinterpret_cast<const float4*>(xc + m * plen + e0);
-                part[m] += lv.x * xv.x + lv.y * xv.y + lv.z * xv.z + lv.w * xv.w;
-              }
-            }
-          } else {
-            const float2 lv = *reinterpret_cast<const float2*>(lut + (byte * T::COPIES + copy) * 2);
-#pragma unroll
-            for (int m = 0; m < MT; ++m) {
-              if (m < M) {
-                const float2 xv = *reinterpret_cast<const float2*>(xc + m * plen + e0);
-                part[m] += lv.x * xv.x + lv.y * xv.y;
-              }
-            }
-          }
-        }
-      }
-#pragma unroll
-      for (int m = 0; m < MT; ++m) acc[m] += nv * part[m];
+    for (int j = 0; j < GV_PRE; ++j) {
+      const int c = sub + j * LPR;
+      if (c < nchunks) gemv_chunk<BITS, MT>(wpre[j], npre[j], c, lut, xs, plen, M, acc);
     }
+    for (int c = sub + GV_PRE * LPR; c < nchunks; c += LPR)
+      gemv_chunk<BITS, MT>(__ldg(reinterpret_cast<const uint4*>(row) + c), __half2float(nrm[c * T::E / W.group]),
+                           c, lut, xs, plen, M, acc);
   }
 #pragma unroll
   for (int m = 0; m < MT; ++m) {
@@ -264,26 +288,26 @@ template <int BITS, int LPR, int MT>
 static cudaError_t launch_gemv(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
                                int row0, int nrows, cudaStream_t st) {
   using T = ChunkTraits<BITS>;
-  const int threads = 256;
-  const int rows_per_cta = (threads / 32) * (32 / LPR);
+  const int rows_per_cta = (GV_THREADS / 32) * (32 / LPR);
   const int grid = (nrows + rows_per_cta - 1) / rows_per_cta;
-  const size_t smem = (size_t)(MT * padded_len(W.in_pad, T::E) + 256 * T::COPIES * T::P) * sizeof(float);
+  const size_t smem = (size_t)(256 * T::P + MT * padded_len(W.in_pad, T::E)) * sizeof(float);
   auto kern = cq_gemv_kernel<BITS, LPR, MT>;
   cudaError_t e = allow_smem((const void*)kern, smem);
   if (e != cudaSuccess) return e;
-  kern<<<grid, threads, smem, st>>>(W, xh, ldx, M, y, ldy, row0, nrows);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(GV_THREADS), smem, st, W, xh, ldx, M, y, ldy, row0, nrows);
 }
 
 template <int BITS, int MT>
 static cudaError_t gemv_lpr(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
                             int row0, int nrows, cudaStream_t st) {
-  // Lanes per row: keep a few chunks per lane so every load is issued up front.
+  // Lanes per row: at most two chunks per lane, so every load is in flight
+  // before the producer wait.
   const int nchunks = W.row_bytes / 16;
-  if (nchunks <= 8) return launch_gemv<BITS, 2, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
-  if (nchunks <= 16) return launch_gemv<BITS, 4, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
-  if (nchunks <= 32) return launch_gemv<BITS, 8, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
-  return launch_gemv<BITS, 16, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (nchunks <= 4) return launch_gemv<BITS, 2, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (nchunks <= 8) return launch_gemv<BITS, 4, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (nchunks <= 16) return launch_gemv<BITS, 8, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  if (nchunks <= 32) return launch_gemv<BITS, 16, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
+  return launch_gemv<BITS, 32, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
 }
 
 template <int BITS>

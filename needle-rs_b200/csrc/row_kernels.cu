@@ -77,6 +77,7 @@ cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, flo
 // the decoded codes levels[idx]*norm directly and both rotations are skipped.
 __global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, RowBatch rb,
                                      float* __restrict__ fetched) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   const int r = blockIdx.x, site = blockIdx.y;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const RowInfo ri = rb.rows[r];
@@ -307,6 +308,7 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
                                  float* __restrict__ u_out, float* __restrict__ bx_out,
                                  float* __restrict__ xh_out, float* __restrict__ gates, int rbmax,
                                  int gmax) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x;
   const int n = G.lanes, d = G.d, W = n * d;
@@ -508,6 +510,7 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
                        int site, const float* __restrict__ ekv, const float* __restrict__ evc,
                        float* __restrict__ u_out, float* __restrict__ bx_out, float* __restrict__ xh_out,
                        float* __restrict__ gates, int rbmax, int gmax) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   __shared__ __align__(16) float Xs[PT_M][128];
   __shared__ float lev[48];
   __shared__ float phi_s[PT_M][24];
@@ -1203,6 +1206,7 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
 // model.rs:358-374: lane mean, final ZCRMS norm, rotation for the tied head.
 __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float* __restrict__ fnorm,
                              float* __restrict__ lm_in) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   extern __shared__ __align__(16) float sm[];
   float* red = sm;
   float* x = sm + 32;
