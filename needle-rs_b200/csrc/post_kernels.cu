@@ -174,10 +174,9 @@ __device__ __forceinline__ float pack_row(uint32_t* zb, float amax) {
   return ldexpf(1.f, -e);
 }
 
-constexpr int PW = 8;       // rows (warps) per CTA
-constexpr int PT = PW * 32;  // threads
-
-template <int D>
+// PW rows per CTA, one warp per row (PW * 32 threads): 8, or 2 for mid-size
+// batches (four times the CTAs, so the SMs fill).
+template <int D, int PW>
 struct __align__(16) PostSmem {
   static constexpr int P = D + 4;
   uint32_t zb[PW][D * P];  // Kronecker input (f32 while built, then f16 hi|lo)
@@ -189,7 +188,8 @@ struct __align__(16) PostSmem {
   float gs[PW][24];        // gates per row: hpost [nl], hres [nl * nl]
 };
 
-// Block max over the eight warps of per-row partials red[warp][row].
+// Block max over the PW warps of per-row partials red[warp][row].
+template <int PW>
 __device__ __forceinline__ float rows_max(float (*red)[PW], int row) {
   float m = 0.f;
 #pragma unroll
@@ -201,8 +201,8 @@ __device__ __forceinline__ float rows_max(float (*red)[PW], int row) {
 // work (thread tid covers elements tid, tid + PT, ... of every row, so each
 // parameter element is loaded once per PW rows) and one Kronecker apply per
 // warp on its own row.
-template <int D>
-__global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, LayerParams lp,
+template <int D, int PW>
+__global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch rb, LayerParams lp,
                                                            const uint32_t* __restrict__ p1,
                                                            const uint32_t* __restrict__ p2,
                                                            const float* __restrict__ projo,
@@ -211,9 +211,10 @@ __global__ void __launch_bounds__(PT) layer_post_tc_kernel(Geo G, RowBatch rb, L
                                                            const float* __restrict__ gates,
                                                            float* __restrict__ lanes) {
   constexpr int N = D * D;
+  constexpr int PT = PW * 32;  // threads
   extern __shared__ __align__(16) unsigned char post_smem[];
-  auto& S = *reinterpret_cast<PostSmem<D>*>(post_smem);
-  float* s1all = reinterpret_cast<float*>(post_smem + sizeof(PostSmem<D>));  // [PW][d]
+  auto& S = *reinterpret_cast<PostSmem<D, PW>*>(post_smem);
+  float* s1all = reinterpret_cast<float*>(post_smem + sizeof(PostSmem<D, PW>));  // [PW][d]
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int r0 = blockIdx.x * PW;
   const int nrow = min(PW, rb.M - r0);
@@ -500,27 +501,32 @@ void hada_frags(const float* const* mats, int D, uint32_t* out, float* inv) {
   }
 }
 
+template <int D, int PW>
+static cudaError_t post_tc(const Geo& G, const RowBatch& rb, const LayerParams& lp, const uint32_t* p1,
+                           const uint32_t* p2, const float* projo, const float* u, float* bx, const float* gates,
+                           float* lanes, cudaStream_t st) {
+  const size_t smem = sizeof(PostSmem<D, PW>) + (size_t)PW * G.d * 4;
+  auto k = layer_post_tc_kernel<D, PW>;
+  cudaError_t e = allow_smem((const void*)k, smem);
+  if (e != cudaSuccess) return e;
+  k<<<(rb.M + PW - 1) / PW, PW * 32, smem, st>>>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes);
+  return cudaGetLastError();
+}
+
 cudaError_t launch_layer_post_tc(const Geo& G, const RowBatch& rb, const LayerParams& lp, const uint32_t* p1,
                                  const uint32_t* p2, const float* projo, const float* u, float* bx,
                                  const float* gates, float* lanes, cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   if (!lp.hfrag || G.lanes > 4 || G.cond_rank > 8 || G.cond_rank < 1 || G.ba != G.bb || G.hada_n < G.d)
     return cudaErrorInvalidValue;
-  const dim3 grid((rb.M + PW - 1) / PW);
-  if (G.ba == 32) {
-    const size_t smem = sizeof(PostSmem<32>) + (size_t)PW * G.d * 4;
-    cudaError_t e = allow_smem((const void*)layer_post_tc_kernel<32>, smem);
-    if (e != cudaSuccess) return e;
-    layer_post_tc_kernel<32><<<grid, PW * 32, smem, st>>>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes);
-  } else if (G.ba == 16) {
-    const size_t smem = sizeof(PostSmem<16>) + (size_t)PW * G.d * 4;
-    cudaError_t e = allow_smem((const void*)layer_post_tc_kernel<16>, smem);
-    if (e != cudaSuccess) return e;
-    layer_post_tc_kernel<16><<<grid, PW * 32, smem, st>>>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes);
-  } else {
-    return cudaErrorInvalidValue;
-  }
-  return cudaGetLastError();
+  // 2-row CTAs between 128 and 2048 rows fill the SMs; below that a row's
+  // element phases run faster on 8 warps, above it 8-row CTAs already fill them.
+  const bool small = rb.M >= 128 && rb.M < 2048;
+  if (G.ba == 32) return small ? post_tc<32, 2>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st)
+                               : post_tc<32, 8>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
+  if (G.ba == 16) return small ? post_tc<16, 2>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st)
+                               : post_tc<16, 8>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
+  return cudaErrorInvalidValue;
 }
 
 }  // namespace nb

@@ -501,9 +501,11 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
 // Phase 2 (one warp per row, no block barriers): gates and Sinkhorn, mix_down
 // re-reading the tile's lanes (L2-resident), the Engram gate, the ZCRMS norm
 // and the rotation of the attention input, exactly as the per-row kernel.
-constexpr int PT_M = 16;   // rows per CTA
 constexpr int PT_DQ = 8;   // d_model / 128 supported on this path
 
+// PT_M rows per CTA: 16 for large batches, 4 for small ones (four times the
+// CTAs, shorter per-CTA loops).
+template <int PT_M>
 __global__ void __launch_bounds__(256, 2)
 layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes, CqMat phi_pre,
                        CqMat phi_post, CqMat phi_res, MhcParams mp, const float* __restrict__ norm_in,
@@ -594,11 +596,14 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
                                        : (uint32_t)cr[g * 32 + lane]);
       wn[j] = wok[j] ? nsm[o * gmax + g] : 0.f;
     }
-    {
+    // Tile rows wid and wid + 8 exist only below PT_M (warp-uniform tests).
+    if (wid < PT_M) {
       float v[4] = {cA.x, cA.y, cA.z, cA.w};
       ssA += v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
       fwht128_warp(v);
       reinterpret_cast<float4*>(Xs[wid])[lane] = make_float4(v[0], v[1], v[2], v[3]);
+    }
+    if (wid + 8 < PT_M) {
       float u[4] = {cB.x, cB.y, cB.z, cB.w};
       ssB += u[0] * u[0] + u[1] * u[1] + u[2] * u[2] + u[3] * u[3];
       fwht128_warp(u);
@@ -765,7 +770,23 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
 }
 
 // Rows at which the tiled kernel takes over from one CTA per row.
-constexpr int PT_MIN_ROWS = 512;
+constexpr int PRE_TILED_MIN_ROWS = 2;
+
+template <int PT_M>
+static cudaError_t launch_pre_tiled(const Geo& G, int li, const RowBatch& rb, const float* lanes,
+                                    const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
+                                    const MhcParams& mp, const float* norm_in, int site, const float* ekv,
+                                    const float* evc, float* u, float* bx, float* xh, float* gates, int rbmax,
+                                    int gmax, cudaStream_t st) {
+  const int nrow = 2 * G.lanes + G.lanes * G.lanes;
+  const size_t dyn = (size_t)nrow * rbmax + (size_t)nrow * gmax * 4;
+  auto k = layer_pre_tiled_kernel<PT_M>;
+  cudaError_t e = allow_smem((const void*)k, dyn);
+  if (e != cudaSuccess) return e;
+  k<<<(rb.M + PT_M - 1) / PT_M, 256, dyn, st>>>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site,
+                                                ekv, evc, u, bx, xh, gates, rbmax, gmax);
+  return cudaGetLastError();
+}
 
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                              const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
@@ -778,14 +799,12 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
   const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
   const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
                         (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0;
-  if (rb.M >= PT_MIN_ROWS && tiled_ok) {
-    const size_t dyn = (size_t)nrow * rbmax + (size_t)nrow * gmax * 4;
-    cudaError_t e = allow_smem((const void*)layer_pre_tiled_kernel, dyn);
-    if (e != cudaSuccess) return e;
-    layer_pre_tiled_kernel<<<(rb.M + PT_M - 1) / PT_M, 256, dyn, st>>>(
-        G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates, rbmax, gmax);
-    return cudaGetLastError();
-  }
+  if (tiled_ok && rb.M >= 2048)
+    return launch_pre_tiled<16>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx,
+                                xh, gates, rbmax, gmax, st);
+  if (tiled_ok && rb.M >= PRE_TILED_MIN_ROWS)
+    return launch_pre_tiled<4>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx,
+                               xh, gates, rbmax, gmax, st);
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
   const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48 + nrow * gmax) * sizeof(float) +
                       (size_t)nrow * rbmax + 16;
