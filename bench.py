@@ -278,6 +278,29 @@ def _event_us(torch, fn, reps):
     return e0.elapsed_time(e1) / reps * 1e3
 
 
+def _graph_us(torch, call, reps):
+    """Mean device time in microseconds of call(stream) replayed from a CUDA
+    graph holding `reps` calls (host launch overhead excluded)."""
+    s = torch.cuda.current_stream().cuda_stream
+    call(s)  # first call: one-time set-up outside the capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        cs = torch.cuda.current_stream().cuda_stream
+        for _ in range(reps):
+            call(cs)
+    g.replay()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(3):
+        g.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    del g
+    return e0.elapsed_time(e1) / (3 * reps) * 1e3
+
+
 def kernel_configs(nb, torch, raw, hbm, bf16):
     """BASELINE configs 1-3 on this GPU beside the oracle (the C++ restatement
     of the reference CPU path) on the host cores, each on a bounded sample."""
@@ -302,8 +325,8 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
         d = torch.from_numpy(np.frombuffer(blob, np.uint8).copy()).cuda()
         xd = torch.from_numpy(xh).cuda()
         y = torch.zeros(512, n_out, device="cuda")
-        us = _event_us(torch, lambda: nb.cq_project(d.data_ptr(), d.data_ptr() + n_out * 192, n_out, 768, 2, lv,
-                                                    xd.data_ptr(), 768, 512, y.data_ptr(), n_out, stream=st), 50)
+        us = _graph_us(torch, lambda s: nb.cq_project(d.data_ptr(), d.data_ptr() + n_out * 192, n_out, 768, 2, lv,
+                                                      xd.data_ptr(), 768, 512, y.data_ptr(), n_out, stream=s), 50)
         flop = 2 * 512 * 768 * n_out
         t0 = time.perf_counter()
         w.matmul_prepared(xh)
@@ -311,7 +334,8 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
         c1[str(n_out)] = {"us": round(us, 2), "tflops": round(flop / us / 1e6, 2),
                           "frac_of_bf16_peak": round(flop / us / 1e6 / bf16, 4),
                           "cpu_us": round(cpu_s * 1e6, 1), "cpu_cores": ncpu}
-    out["config1_gemm"] = {"metric": "X[512,768] x W[N,768] 2-bit CQ projection (tensor cores, f16 hi/lo split)",
+    out["config1_gemm"] = {"metric": "X[512,768] x W[N,768] 2-bit CQ projection (tensor cores, f16 hi/lo split), "
+                                     "device time per call from a CUDA graph of 50 calls",
                            "roofline": "tensor (bf16 dense peak, measured)", "by_n": c1}
     # ---- config 2: standalone int8 decode attention, 64 sessions x ctx 512
     B, S, H, KVH, QK, VH = 64, 512, 12, 2, 48, 64
@@ -332,16 +356,17 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
     dv = {k_: torch.from_numpy(np.ascontiguousarray(a)).cuda() for k_, a in
           dict(q=qf, k=kq, v=vq, ks=ks, vs=vs, lo=np.zeros(B, np.int32), hi=np.full(B, S - 1, np.int32)).items()}
     o2 = torch.zeros(B, H * VH, device="cuda")
-    us = _event_us(torch, lambda: nb.attend_step(dv["q"].data_ptr(), dv["k"].data_ptr(), dv["v"].data_ptr(),
-                                                 dv["ks"].data_ptr(), dv["vs"].data_ptr(), True, S,
-                                                 dv["lo"].data_ptr(), dv["hi"].data_ptr(), B, H, KVH, QK, VH,
-                                                 o2.data_ptr(), stream=st), 100)
+    us = _graph_us(torch, lambda s: nb.attend_step(dv["q"].data_ptr(), dv["k"].data_ptr(), dv["v"].data_ptr(),
+                                                   dv["ks"].data_ptr(), dv["vs"].data_ptr(), True, S,
+                                                   dv["lo"].data_ptr(), dv["hi"].data_ptr(), B, H, KVH, QK, VH,
+                                                   o2.data_ptr(), stream=s), 50)
     algo = B * (S * KVH * (QK + VH + 8) + H * QK * 4 + H * VH * 4)
     t0 = time.perf_counter()
     for b in range(B):
         orc.attend_step(qf[b].ravel(), S, 0, S - 1, H, KVH, QK, VH, kq=kq[b], ks=ks[b], vq=vq[b], vs=vs[b])
     cpu_s = time.perf_counter() - t0
-    out["config2_attention"] = {"metric": "int8 decode attention, 64 sessions x ctx 512 (nd_attend_step)",
+    out["config2_attention"] = {"metric": "int8 decode attention, 64 sessions x ctx 512 (nd_attend_step), "
+                                          "device time per call from a CUDA graph of 50 calls",
                                 "us": round(us, 2), "algorithmic_bytes": algo,
                                 "gbs": round(algo / us / 1e3, 1), "frac_of_hbm_peak": round(algo / us / 1e3 / hbm, 4),
                                 "note": "8.2 MB fits in L2; the HBM figure is the conservative denominator",

@@ -269,11 +269,22 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
         const float4 d14 = *reinterpret_cast<const float4*>(lp.d1 + c0);
         const float ph[4] = {1.0f + ph4.x, 1.0f + ph4.y, 1.0f + ph4.z, 1.0f + ph4.w};
         const float dd[4] = {d14.x, d14.y, d14.z, d14.w};
+        // cond_v rows c0..c0+3 ([d][rk] row-major): 4 * rk consecutive floats.
         float cv[4][8];
+        if (rk == 8) {
+          const float4* cv4 = reinterpret_cast<const float4*>(lp.cond_v + (size_t)c0 * 8);
 #pragma unroll
-        for (int e = 0; e < 4; ++e)
+          for (int e = 0; e < 4; ++e) {
+            const float4 a = __ldg(cv4 + 2 * e), b = __ldg(cv4 + 2 * e + 1);
+            cv[e][0] = a.x, cv[e][1] = a.y, cv[e][2] = a.z, cv[e][3] = a.w;
+            cv[e][4] = b.x, cv[e][5] = b.y, cv[e][6] = b.z, cv[e][7] = b.w;
+          }
+        } else {
 #pragma unroll
-          for (int j = 0; j < 8; ++j) cv[e][j] = j < rk ? lp.cond_v[(c0 + e) * rk + j] : 0.f;
+          for (int e = 0; e < 4; ++e)
+#pragma unroll
+            for (int j = 0; j < 8; ++j) cv[e][j] = j < rk ? lp.cond_v[(c0 + e) * rk + j] : 0.f;
+        }
 #pragma unroll
         for (int i = 0; i < PW; ++i) {
           if (i >= nrow) break;
@@ -298,11 +309,12 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
     }
 #pragma unroll
     for (int i = 0; i < PW; ++i) {
+      if (i >= nrow) break;  // rows past the batch are never read
       const float m = warp_max(mz[i]);
       if (lane == 0) S.amax[w][i] = m;
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float v = warp_sum(acc[i][j]);
+        const float v = j < rk ? warp_sum(acc[i][j]) : 0.f;
         if (lane == 0) S.part[w][i][j] = v;
       }
     }
@@ -337,6 +349,10 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
   }
   __syncthreads();
   // ---- element-parallel: silu(d2 * cond * out[p1] + b2), cond = 1 + pr . cond_u
+  // (kernels.rs:146-160; a conditioning rank whose weight is exactly zero is
+  // skipped, as the reference skips it). A row's weights and their nonzero
+  // mask are read once per row; silu(v) = v / (1 + e^-v) with the hardware
+  // exponential and division (~2 ulp each).
   {
     float mz[PW];
 #pragma unroll
@@ -345,30 +361,41 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
       float cu[8][4];
 #pragma unroll
       for (int j = 0; j < 8; ++j) {
-        const float4 t = j < rk ? *reinterpret_cast<const float4*>(lp.cond_u + j * N + c0) : make_float4(0, 0, 0, 0);
+        const float4 t = j < rk ? __ldg(reinterpret_cast<const float4*>(lp.cond_u + j * N + c0)) : make_float4(0, 0, 0, 0);
         cu[j][0] = t.x;
         cu[j][1] = t.y;
         cu[j][2] = t.z;
         cu[j][3] = t.w;
       }
-      const float4 d24 = *reinterpret_cast<const float4*>(lp.d2 + c0);
-      const float4 b24 = *reinterpret_cast<const float4*>(lp.b2 + c0);
-      const uint4 pp = *reinterpret_cast<const uint4*>(p1 + c0);
+      const float4 d24 = __ldg(reinterpret_cast<const float4*>(lp.d2 + c0));
+      const float4 b24 = __ldg(reinterpret_cast<const float4*>(lp.b2 + c0));
+      const uint4 pp = __ldg(reinterpret_cast<const uint4*>(p1 + c0));
       const float d2[4] = {d24.x, d24.y, d24.z, d24.w}, b2[4] = {b24.x, b24.y, b24.z, b24.w};
       const int src[4] = {pad_idx<D>(pp.x), pad_idx<D>(pp.y), pad_idx<D>(pp.z), pad_idx<D>(pp.w)};
       const int pi = pad_idx<D>(c0);
 #pragma unroll
       for (int i = 0; i < PW; ++i) {
         if (i >= nrow) break;
+        float pr[8];
+        unsigned nz = 0;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          pr[j] = S.pr[i][j];
+          nz |= (j < rk && pr[j] != 0.0f) ? 1u << j : 0u;
+        }
+        float cv[4] = {1.0f, 1.0f, 1.0f, 1.0f};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          if (nz & (1u << j)) {  // the same for every thread of the CTA
+#pragma unroll
+            for (int e = 0; e < 4; ++e) cv[e] += pr[j] * cu[j][e];
+          }
+        }
         float z[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
-          float cv = 1.0f;
-#pragma unroll
-          for (int j = 0; j < 8; ++j)
-            if (j < rk && S.pr[i][j] != 0.0f) cv += S.pr[i][j] * cu[j][e];
-          const float v = d2[e] * cv * S.fb[i][src[e]] + b2[e];
-          z[e] = v * sigmoidf_(v);  // silu, ops.rs:118
+          const float v = d2[e] * cv[e] * S.fb[i][src[e]] + b2[e];
+          z[e] = __fdividef(v, 1.0f + __expf(-v));  // silu, ops.rs:118
           mz[i] = fmaxf(mz[i], fabsf(z[e]));
         }
         *reinterpret_cast<uint4*>(&S.zb[i][pi]) =
@@ -377,6 +404,7 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
     }
 #pragma unroll
     for (int i = 0; i < PW; ++i) {
+      if (i >= nrow) break;
       const float m = warp_max(mz[i]);
       if (lane == 0) S.amax[w][i] = m;
     }
@@ -414,6 +442,7 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
     }
 #pragma unroll
     for (int i = 0; i < PW; ++i) {
+      if (i >= nrow) break;
       const float m = warp_max(mz[i]);
       if (lane == 0) S.amax[w][i] = m;
     }

@@ -15,6 +15,9 @@
 // round-to-nearest, the same norm-times-group-dot structure as the reference.
 // Activation rows and the level table are scaled by powers of two that keep
 // every f16 remainder in the normal range; the epilogue undoes them exactly.
+// When every scaled level is itself an f16 value (codebooks stored as f16
+// numbers, as the packer writes them), the level remainders are zero: that
+// form skips their tile and their MMA, two MMAs per K step instead of three.
 //
 // Per call, cq_expand_kernel reads the packed `.cact` codes of the requested
 // rows in place and writes their level high parts and remainders as f16
@@ -179,6 +182,10 @@ __device__ __forceinline__ int row_exp(float amax) {
 }
 
 
+// EXACT: every level times the level scale is an f16 value, so the level
+// remainders are zero and only x_hi * l_hi and x_lo * l_hi are issued (two
+// MMAs per K step, no remainder tile).
+template <bool EXACT>
 __global__ void __launch_bounds__(UTHREADS, 1)
 cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
@@ -290,11 +297,11 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
         const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
         unsigned char* st = sm + s * STAGE_BYTES;
-        mbar_arrive_tx(&full[s], 4 * TILE);
+        mbar_arrive_tx(&full[s], (EXACT ? 3 : 4) * TILE);
         tma_load_2d(st, &mapAh, &full[s], kb * UK, m0);
         tma_load_2d(st + TILE, &mapAl, &full[s], kb * UK, m0);
         tma_load_2d(st + 2 * TILE, &mapBh, &full[s], kb * UK, n0);
-        tma_load_2d(st + 3 * TILE, &mapBl, &full[s], kb * UK, n0);
+        if (!EXACT) tma_load_2d(st + 3 * TILE, &mapBl, &full[s], kb * UK, n0);
         ++issued;
       }
       if (*abort) {  // let the copies already issued land before the CTA exits
@@ -328,8 +335,12 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
             const uint64_t o = (uint64_t)(kk * 2);  // 32 bytes along K, in 16-byte units
             const uint32_t acc = (j | kk) != 0;     // a group starts from zero
             umma_f16(dmain, dah + o, dbh + o, acc);
-            umma_f16(dcorr, dah + o, dbl + o, acc);
-            umma_f16(dcorr, dal + o, dbh + o, 1);
+            if (EXACT) {
+              umma_f16(dcorr, dal + o, dbh + o, acc);
+            } else {
+              umma_f16(dcorr, dah + o, dbl + o, acc);
+              umma_f16(dcorr, dal + o, dbh + o, 1);
+            }
           }
           umma_commit(&empty[s]);
         }
@@ -350,7 +361,8 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
 
 // Level high parts and remainders of rows [row0, row0 + nrows) of a CQ
 // matrix, decoded from the packed codes (cq.rs:908-925) and scaled by 2^le:
-// hi / lo [nrows][in_pad] f16. One thread per 8 weights.
+// hi / lo [nrows][in_pad] f16 (no remainders when wlo is null: exact levels).
+// One thread per 8 weights.
 template <int BITS>
 __global__ void cq_expand_kernel(CqMat W, int row0, int nrows, int le, __half* __restrict__ whi,
                                  __half* __restrict__ wlo) {
@@ -375,7 +387,7 @@ __global__ void cq_expand_kernel(CqMat W, int row0, int nrows, int le, __half* _
       l[p] = __byte_perm(a, b, 0x7632);
     }
     *reinterpret_cast<uint4*>(whi + (size_t)n * W.in_pad + c * 8) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(wlo + (size_t)n * W.in_pad + c * 8) = make_uint4(l[0], l[1], l[2], l[3]);
+    if (wlo) *reinterpret_cast<uint4*>(wlo + (size_t)n * W.in_pad + c * 8) = make_uint4(l[0], l[1], l[2], l[3]);
   }
 }
 
@@ -462,16 +474,23 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
     std::frexp(lmax, &e);
     le = 14 - e;
   }
+  // Exact levels: every scaled level survives the round trip through f16.
+  bool exact = true;
+  for (int i = 0; i < (1 << W.bits); ++i) {
+    const float v = std::ldexp(W.levels[i], le);
+    if (__half2float(__float2half_rn(v)) != v) exact = false;
+  }
   split_f16_kernel<<<(M + 7) / 8, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   {
     const long total = (long)nrows * (K / 8);
     const int blocks = (int)std::min<long>((total + 255) / 256, 148L * 8);
+    __half* wlo = exact ? nullptr : gs.wlo;
     if (W.bits == 2)
-      cq_expand_kernel<2><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, gs.wlo);
+      cq_expand_kernel<2><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, wlo);
     else
-      cq_expand_kernel<4><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, gs.wlo);
+      cq_expand_kernel<4><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, wlo);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -479,11 +498,12 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
   if (!make_map(&mah, gs.hi, M, K) || !make_map(&mal, gs.lo, M, K) || !make_map(&mbh, gs.whi, nrows, K) ||
       !make_map(&mbl, gs.wlo, nrows, K))
     return cudaErrorNotSupported;
-  e = allow_smem((const void*)cq_umma_kernel, UMMA_SMEM);
+  auto kern = exact ? cq_umma_kernel<true> : cq_umma_kernel<false>;
+  e = allow_smem((const void*)kern, UMMA_SMEM);
   if (e != cudaSuccess) return e;
   dim3 grid((nrows + UN - 1) / UN, (M + UM - 1) / UM);
-  cq_umma_kernel<<<grid, UTHREADS, UMMA_SMEM, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy,
-                                                    row0, nrows);
+  kern<<<grid, UTHREADS, UMMA_SMEM, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy, row0,
+                                          nrows);
   return cudaGetLastError();
 }
 

@@ -115,13 +115,19 @@ def test_cq_gemm_matches_oracle_config1(cuda, bits, n_out):
 
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("shape", [(812, 768), (768, 768), (300, 3072), (8192, 768)])
-def test_cq_tensor_core_gemm_matches_oracle(cuda, bits, shape):
-    """The tcgen05 path (path 3: f16 hi/lo split, three MMAs into TMEM) against
-    the oracle for ragged row counts (partial 128-row tiles) and partial
-    128-output tiles."""
+@pytest.mark.parametrize("levels_kind", ["f16", "f32"])
+def test_cq_tensor_core_gemm_matches_oracle(cuda, bits, shape, levels_kind):
+    """The tcgen05 path (path 3) against the oracle for ragged row counts
+    (partial 128-row tiles) and partial 128-output tiles. f16 codebook entries
+    take the exact-level form (two MMAs per K step); plain f32 entries need the
+    level remainders too (three MMAs)."""
     torch = cuda
     out, inp = shape
-    cb = cact_pack.random_codebook(np.random.default_rng(9))
+    if levels_kind == "f16":
+        cb = cact_pack.random_codebook(np.random.default_rng(9))
+    else:
+        cb = (np.random.default_rng(9).normal(0.0, 0.02, 28) / np.sqrt(128)).astype(np.float32)
+        assert not np.array_equal(cb, cact_pack.f16_round(cb))
     d, pp, npp, w, _, _ = make_weight(torch, out, inp, bits, 7, cb)
     levels = cact_pack.codebook_levels(cb, bits)
     rng = np.random.default_rng(11)
