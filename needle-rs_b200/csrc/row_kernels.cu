@@ -833,12 +833,16 @@ __device__ __forceinline__ float q8(float x, float inv) {
   return fminf(fmaxf(q, -128.0f), 127.0f);
 }
 
-__global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
-                                const float* __restrict__ rope_cs, const float* __restrict__ proj,
-                                float* __restrict__ qpost, void* pk, void* pv, float* pks,
-                                float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
-  extern __shared__ __align__(16) float sm[];
-  const int r = blockIdx.x;
+// One activation row, handled by the whole CTA (WARP = false: the conv phase
+// over every thread, the heads spread over the warps) or by one warp (WARP =
+// true: many rows per CTA, for large batches). `sm` holds qkv_dim floats.
+template <bool WARP>
+__device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                                             const float* __restrict__ rope_cs, const float* __restrict__ proj,
+                                             float* __restrict__ qpost, void* pk, void* pv, float* pks, float* pvs,
+                                             int8_t* __restrict__ q8out, float* __restrict__ q8s, int r, float* sm) {
+  const int tix = WARP ? (int)(threadIdx.x & 31) : (int)threadIdx.x;
+  const int nthr = WARP ? 32 : (int)blockDim.x;
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos;
   const int qd = G.q_dim, kd = G.k_dim, vd = G.v_dim, qkv = G.qkv_dim;
@@ -848,7 +852,7 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
   // Four channels per thread when every segment width is a multiple of 4.
   if ((qd | kd | vd) % 4 == 0) {
     const int slot_here = tl ? p % tl : 0;
-    for (int c = 4 * threadIdx.x; c < qkv; c += 4 * blockDim.x) {
+    for (int c = 4 * tix; c < qkv; c += 4 * nthr) {
       const float* tp;
       int dim, cc;
       if (c < qd) {
@@ -881,7 +885,7 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
     }
   } else
 #pragma unroll 4
-  for (int c = threadIdx.x; c < qkv; c += blockDim.x) {
+  for (int c = tix; c < qkv; c += nthr) {
     const float* tp;
     int dim, cc;
     if (c < qd) {
@@ -905,8 +909,11 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
     }
     sm[c] = acc;
   }
-  __syncthreads();
-  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  if (WARP)
+    __syncwarp();
+  else
+    __syncthreads();
+  const int lane = threadIdx.x & 31, wid = WARP ? 0 : (int)(threadIdx.x >> 5), nw = WARP ? 1 : (int)(blockDim.x >> 5);
   const int half = G.qk / 2;
   const float* cs = rope_cs + (size_t)p * half;                     // cos
   const float* sn = rope_cs + (size_t)G.max_seq * half + (size_t)p * half;  // sin
@@ -1024,11 +1031,40 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
   }
 }
 
+__global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
+                                const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv,
+                                float* pks, float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
+  extern __shared__ __align__(16) float sm[];
+  qkv_post_row<false>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, blockIdx.x, sm);
+}
+
+// Large batches: one warp per row, QP_ROWS rows per CTA, each warp with its
+// own qkv_dim-float slice of shared memory.
+constexpr int QP_ROWS = 8;
+__global__ void __launch_bounds__(QP_ROWS * 32)
+qkv_post_rows_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
+                     const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv, float* pks,
+                     float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
+  extern __shared__ __align__(16) float sm[];
+  const int w = threadIdx.x >> 5, r = blockIdx.x * QP_ROWS + w;
+  if (r >= rb.M) return;
+  const int stride = (G.qkv_dim + 3) / 4 * 4;
+  qkv_post_row<true>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, r, sm + (size_t)w * stride);
+}
+
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                             const float* rope_cs, const float* proj, float* qpost, void* pk,
                             void* pv, float* pks, float* pvs, int8_t* q8out, float* q8s, cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   if (G.qk > 64 || G.vh > 64 || (G.qk & 1) || (G.vh & 1)) return cudaErrorInvalidValue;
+  if (rb.M >= 2048) {  // enough rows that the per-row head loop of one warp overlaps across warps
+    const size_t smem = (size_t)QP_ROWS * ((G.qkv_dim + 3) / 4 * 4) * sizeof(float);
+    cudaError_t e = allow_smem((const void*)qkv_post_rows_kernel, smem);
+    if (e != cudaSuccess) return e;
+    qkv_post_rows_kernel<<<(rb.M + QP_ROWS - 1) / QP_ROWS, QP_ROWS * 32, smem, st>>>(
+        G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
+    return cudaGetLastError();
+  }
   const size_t smem = (size_t)G.qkv_dim * sizeof(float);
   qkv_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
   return cudaGetLastError();
