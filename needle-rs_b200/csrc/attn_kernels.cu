@@ -350,17 +350,19 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
 // f32 rounding of the products.
 //
 // P.V runs transposed, O^T = V^T P^T, as m16n8k16 f16 MMAs with f32
-// accumulation: value dimensions are the 16 rows (V^T fed by ldmatrix.trans
-// from f16 values in shared memory), heads the 8 columns. int8 values are exact
-// in f16 (bias trick: byte ^ 0x80 placed under exponent byte 0x64 is 1024 + u
-// in f16; subtracting 1152 gives the signed value), and each weight p * vs is
-// split into an f16 high part and an f16 remainder (two MMAs), which keeps
-// about 22 bits of the weight. The weights leave the score fragment as
-// [position][head] 8x8 blocks; movmatrix.trans turns each into the
-// [head][position] pairs of the B fragment, so they never touch memory.
+// accumulation: value dimensions are the 16 rows, heads the 8 columns. V^T
+// comes straight from the int8 values in shared memory by ldmatrix.trans of
+// byte pairs; each register splits into an even-dimension and an
+// odd-dimension fragment, widened exactly to f16 (bias trick: byte ^ 0x80
+// placed under exponent byte 0x64 is 1024 + u in f16; subtracting 1152 gives
+// the signed value). Each weight p * vs is split into an f16 high part and an
+// f16 remainder (two MMAs), which keeps about 22 bits of the weight. The
+// weights leave the score fragment as [position][head] 8x8 blocks;
+// movmatrix.trans turns each into the [head][position] pairs of the B
+// fragment, so they never touch memory.
 //
 // Each of the four warps of a CTA owns every fourth 32-position block of the
-// CTA's range with its own cp.async double buffer and its own online softmax,
+// CTA's range with its own three-block buffer and its own online softmax,
 // so the main loop has no block-wide barrier; the warps merge at the end and
 // the CTA writes the same (max, sum, P.V) partial as the f32 kernel.
 // ----------------------------------------------------------------------------
@@ -372,21 +374,21 @@ struct MmaTile {
   static constexpr int KS = QK == 16 ? 16 : (QK % 32 == 0 ? QK + 16 : QK);
   static constexpr int KP = QK / 16;   // 16-byte pieces per key row
   static constexpr int VP = VH / 16;   // 16-byte pieces per value row
-  static constexpr int VHS = VH + 8;   // f16 value row stride (halves): conflict-free ldmatrix
   static constexpr int NT = VH / 8;    // P.V n-tiles
   static constexpr int NK32 = QK / 32; // m16n8k32 steps of the key dot
   static constexpr bool K16 = (QK % 32) != 0;
 };
 
+constexpr int NBUF = 3;  // per-warp block buffers: two blocks in flight while one is consumed
+
 template <int QK, int VH>
 struct __align__(16) MmaWarpSmem {
   using T = MmaTile<QK, VH>;
-  int8_t k[2][WB * T::KS];
-  int8_t v[2][WB * VH];
-  float ks[2][WB];
-  float vs[2][WB];
-  __half vh[WB * T::VHS];
-  uint64_t bar[2];  // bulk-copy completion of buffer 0 / 1
+  int8_t k[NBUF][WB * T::KS];
+  int8_t v[NBUF][WB * VH];
+  float ks[NBUF][WB];
+  float vs[NBUF][WB];
+  uint64_t bar[NBUF];  // bulk-copy completion of each buffer
 };
 
 __device__ __forceinline__ void mma_s8_k32(int (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
@@ -433,15 +435,17 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   return y;
 }
 
-// Four signed bytes -> two f16 pairs (exact).
-__device__ __forceinline__ void i8x4_to_h2x2(uint32_t w, uint32_t* lo, uint32_t* hi) {
+// Bytes (a0, a1, b0, b1) of two adjacent positions' dimension pair ->
+// f16 pairs (a0, b0) and (a1, b1) (exact), for V^T fragments read by
+// ldmatrix.trans straight from the int8 values.
+__device__ __forceinline__ void i8pairs_to_h2(uint32_t w, uint32_t* even, uint32_t* odd) {
   const uint32_t u = w ^ 0x80808080u;
   const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
-  uint32_t a = __byte_perm(u, 0x64646464u, 0x5140), b = __byte_perm(u, 0x64646464u, 0x5342);
+  uint32_t a = __byte_perm(u, 0x64646464u, 0x4240), b = __byte_perm(u, 0x64646464u, 0x4341);
   __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), bias);
   __half2 hb = __hsub2(*reinterpret_cast<__half2*>(&b), bias);
-  *lo = *reinterpret_cast<uint32_t*>(&ha);
-  *hi = *reinterpret_cast<uint32_t*>(&hb);
+  *even = *reinterpret_cast<uint32_t*>(&ha);
+  *odd = *reinterpret_cast<uint32_t*>(&hb);
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float x, float y) {
@@ -622,52 +626,43 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
   const bool bulk = src.slots >= WB && T::KS == QK;
   if (bulk) {
     if (lane == 0) {
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&W.bar[0])));
-      asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&W.bar[1])));
+#pragma unroll
+      for (int i = 0; i < NBUF; ++i) asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;" ::"r"(smem_u32(&W.bar[i])));
       asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
     }
     __syncwarp();
   }
-  auto issue = [&](int buf, int n0) {
-    if (bulk)
-      mma_issue_bulk<QK, VH>(W, buf, src, kh, n0, b, lane);
-    else
-      mma_issue<QK, VH>(W, buf, src, kh, n0, b, lane);
+  // Block c of this warp (position a + (wid + 4c) * WB) goes to buffer c % NBUF;
+  // one cp.async commit group per block (empty past the last) keeps the
+  // group count uniform.
+  auto issue = [&](int c) {
+    if (c < mine) {
+      const int n0 = a + (wid + 4 * c) * WB;
+      if (bulk)
+        mma_issue_bulk<QK, VH>(W, c % NBUF, src, kh, n0, b, lane);
+      else
+        mma_issue<QK, VH>(W, c % NBUF, src, kh, n0, b, lane);
+    }
     cp_commit();
   };
   bool failed = false;
-  if (mine > 0) issue(0, a + wid * WB);
+#pragma unroll
+  for (int c = 0; c < NBUF - 1; ++c) issue(c);
   for (int c = 0; c < mine; ++c) {
-    const int buf = c & 1;
+    const int buf = c % NBUF;
     const int n0 = a + (wid + 4 * c) * WB;
-    if (c + 1 < mine) {
-      issue(buf ^ 1, n0 + 4 * WB);
-      cp_wait<1>();
-    } else {
-      cp_wait<0>();
-    }
-    if (bulk && !__all_sync(0xffffffffu, mbar_wait_bounded(&W.bar[buf], (uint32_t)(c >> 1) & 1u))) {
+    issue(c + NBUF - 1);
+    cp_wait<NBUF - 1>();
+    if (bulk && !__all_sync(0xffffffffu, mbar_wait_bounded(&W.bar[buf], (uint32_t)(c / NBUF) & 1u))) {
       // The copy never completed: report it, let the copies in flight land
       // (bounded) and leave this warp's partial empty.
       if (lane == 0) atomicExch(werr, 2);
-      if (c + 1 < mine) mbar_wait_bounded(&W.bar[buf ^ 1], (uint32_t)((c + 1) >> 1) & 1u);
+      for (int cc = c + 1; cc < c + NBUF && cc < mine; ++cc)
+        mbar_wait_bounded(&W.bar[cc % NBUF], (uint32_t)(cc / NBUF) & 1u);
       failed = true;
       break;
     }
     __syncwarp();
-    // ---- values to f16 (each lane widens 16-byte pieces)
-#pragma unroll
-    for (int j = lane; j < WB * T::VP; j += 32) {
-      const int i = j / T::VP, c0 = (j % T::VP) * 16;
-      const uint4 w = *reinterpret_cast<const uint4*>(W.v[buf] + i * VH + c0);
-      uint4 h0, h1;
-      i8x4_to_h2x2(w.x, &h0.x, &h0.y);
-      i8x4_to_h2x2(w.y, &h0.z, &h0.w);
-      i8x4_to_h2x2(w.z, &h1.x, &h1.y);
-      i8x4_to_h2x2(w.w, &h1.z, &h1.w);
-      *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0) = h0;
-      *reinterpret_cast<uint4*>(W.vh + i * T::VHS + c0 + 8) = h1;
-    }
     // ---- integer key dots, positions as rows: m-tile j covers positions
     // j*16 .. j*16+15; d[j] = (pos g, heads 2t, 2t+1), (pos g+8, same heads)
     int d[2][4];
@@ -756,24 +751,35 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
         bh[hf] = movmatrix_t(h);
         bl[hf] = movmatrix_t(lw);
       }
+      // V^T straight from the int8 values: ldmatrix.trans of 8x8 b16 tiles
+      // (b16 = a pair of adjacent dimensions), matrix mi covering positions
+      // j*16 + (mi >> 1)*8 .. +7 and dimension pairs hq*16 + (mi & 1)*8 .. +7.
+      // Each register splits into an even-dimension and an odd-dimension A
+      // fragment: m-tile 2hq + par has row g = dimension hq*32 + 2g + par and
+      // row g + 8 = dimension hq*32 + 16 + 2g + par.
       const int mi = lane >> 3, ri = lane & 7;
 #pragma unroll
-      for (int mt = 0; mt < MT; ++mt) {
-        uint32_t va[4];
-        ldsm_x4_trans(va, W.vh + (j * 16 + (mi >> 1) * 8 + ri) * T::VHS + mt * 16 + (mi & 1) * 8);
-        mma_f16_k16(o[mt], va, bh[0], bh[1]);
-        mma_f16_k16(o[mt], va, bl[0], bl[1]);
+      for (int hq = 0; hq < VH / 32; ++hq) {
+        uint32_t vr[4], ae[4], ao[4];
+        ldsm_x4_trans(vr, W.v[buf] + (j * 16 + (mi >> 1) * 8 + ri) * VH + hq * 32 + (mi & 1) * 16);
+#pragma unroll
+        for (int k = 0; k < 4; ++k) i8pairs_to_h2(vr[k], &ae[k], &ao[k]);
+        mma_f16_k16(o[2 * hq], ae, bh[0], bh[1]);
+        mma_f16_k16(o[2 * hq], ae, bl[0], bl[1]);
+        mma_f16_k16(o[2 * hq + 1], ao, bh[0], bh[1]);
+        mma_f16_k16(o[2 * hq + 1], ao, bl[0], bl[1]);
       }
     }
-    __syncwarp();  // before the next block overwrites the f16 values
+    __syncwarp();  // before a later block overwrites this buffer
   }
   if (failed) {
     m[0] = m[1] = -INFINITY;
     l[0] = l[1] = 0.f;
   }
   if (bulk && lane == 0) {  // the barriers' memory is reused by the merge below
-    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&W.bar[0])) : "memory");
-    asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&W.bar[1])) : "memory");
+#pragma unroll
+    for (int i = 0; i < NBUF; ++i)
+      asm volatile("mbarrier.inval.shared::cta.b64 [%0];" ::"r"(smem_u32(&W.bar[i])) : "memory");
   }
   // Sum each head's share over the 8 lanes holding it.
 #pragma unroll
@@ -798,8 +804,9 @@ __global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, Ro
     }
 #pragma unroll
     for (int mt = 0; mt < MT; ++mt) {
-      Wo[(wid * 8 + h) * VH + mt * 16 + g] = o[mt][e];
-      Wo[(wid * 8 + h) * VH + mt * 16 + g + 8] = o[mt][2 + e];
+      const int d0 = (mt >> 1) * 32 + 2 * g + (mt & 1);  // dimension of row g (row g + 8: d0 + 16)
+      Wo[(wid * 8 + h) * VH + d0] = o[mt][e];
+      Wo[(wid * 8 + h) * VH + d0 + 16] = o[mt][2 + e];
     }
   }
   __syncthreads();
