@@ -718,10 +718,14 @@ Session* Engine::new_session(size_t hint, bool int8, std::string* err) {
     total += layer_bytes(G, int8, slots[l]);
   }
   const size_t tl = G.taps > 0 ? G.taps - 1 : 0;
-  const size_t qkv_tail = cfg.layers * tl * G.qkv_dim, eng_tail = (size_t)G.n_sites * G.e_reach * G.d;
-  s->state_bytes = (qkv_tail + eng_tail) * 4 + 4 * 4;
+  // The Engram tails start at the Q/K/V tail count rounded up to four floats
+  // (16-byte aligned for float4 access); the byte count (V3Cache::bytes)
+  // excludes that padding.
+  const size_t qkv_n = cfg.layers * tl * G.qkv_dim, eng_tail = (size_t)G.n_sites * G.e_reach * G.d;
+  const size_t qkv_tail = (qkv_n + 3) / 4 * 4;
+  s->state_bytes = (qkv_n + eng_tail) * 4 + 4 * 4;
   const size_t state_off = total;
-  total += al(s->state_bytes);
+  total += al((qkv_tail + eng_tail) * 4 + 4 * 4);
   const size_t layers_off = total;
   total += al(cfg.layers * sizeof(LayerKV));
   const size_t desc_off = total;

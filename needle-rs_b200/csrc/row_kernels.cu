@@ -131,35 +131,43 @@ struct EngTaps {
   const float* t[16];
 };
 
+// One CTA per row covering every site, four channels per thread-step (the
+// row descriptor and the session's tail pointer are read once per row).
 __global__ void engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float* __restrict__ ekv,
                                    float* __restrict__ evc) {
-  const int r = blockIdx.x, site = blockIdx.y;
+  const int r = blockIdx.x;
   const RowInfo ri = rb.rows[r];
-  const int p = ri.pos, reach = G.e_reach;
-  const float* tp = taps.t[site];
-  const size_t kv_ld = (size_t)G.n_sites * 2 * G.d;
-  const float* raw_here = ekv + (size_t)r * kv_ld + (size_t)site * 2 * G.d + G.d;
-  float* tail = ri.s->eng_tail + (size_t)site * reach * G.d;
-#pragma unroll 4
-  for (int c = threadIdx.x; c < G.d; c += blockDim.x) {
-    float acc = 0.f;
+  const int p = ri.pos, reach = G.e_reach, d = G.d, d4 = d / 4;
+  const size_t kv_ld = (size_t)G.n_sites * 2 * d;
+  float* tails = ri.s->eng_tail;
+  const bool seed = reach > 0 && (rb.mode == MODE_DECODE || p >= ri.len - reach);
+  const float* row_kv = ekv + (size_t)r * kv_ld;
+  for (int i = threadIdx.x; i < G.n_sites * d4; i += blockDim.x) {
+    const int site = i / d4, c = (i % d4) * 4;
+    const float* tp = taps.t[site];
+    const float4 raw = *reinterpret_cast<const float4*>(row_kv + (size_t)site * 2 * d + d + c);
+    float* tail = tails + (size_t)site * reach * d;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int j = 0; j < G.e_taps; ++j) {
       const int back = j * G.e_dil;
       if (back > p || p < j * G.e_maxorder) continue;
-      float val;
+      float4 val;
       if (back == 0)
-        val = raw_here[c];
+        val = raw;
       else if (rb.mode == MODE_PREFILL)
-        val = ekv[(size_t)(r - back) * kv_ld + (size_t)site * 2 * G.d + G.d + c];
+        val = *reinterpret_cast<const float4*>(ekv + (size_t)(r - back) * kv_ld + (size_t)site * 2 * d + d + c);
       else
-        val = tail[(size_t)((p - back) % reach) * G.d + c];
-      acc += tp[j * G.d + c] * val;
+        val = *reinterpret_cast<const float4*>(tail + (size_t)((p - back) % reach) * d + c);
+      const float4 t = *reinterpret_cast<const float4*>(tp + (size_t)j * d + c);
+      acc.x += t.x * val.x;
+      acc.y += t.y * val.y;
+      acc.z += t.z * val.z;
+      acc.w += t.w * val.w;
     }
-    evc[((size_t)r * G.n_sites + site) * G.d + c] = acc;
-    if (reach > 0) {
-      const bool seed = rb.mode == MODE_DECODE || p >= ri.len - reach;
-      if (seed) tail[(size_t)(p % reach) * G.d + c] = raw_here[c];
-    }
+    *reinterpret_cast<float4*>(evc + ((size_t)r * G.n_sites + site) * d + c) = acc;
+    // The slot written here is the one tap j = reach / dil read above (same
+    // thread, same channels), so the read comes first.
+    if (seed) *reinterpret_cast<float4*>(tail + (size_t)(p % reach) * d + c) = raw;
   }
 }
 
@@ -169,8 +177,8 @@ cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const Row
   if (G.n_sites > 16) return cudaErrorInvalidValue;
   EngTaps t;
   for (int i = 0; i < G.n_sites; ++i) t.t[i] = taps[i];
-  dim3 grid(rb.M, G.n_sites);
-  engram_conv_kernel<<<grid, 256, 0, st>>>(G, t, rb, ekv, evc);
+  if (G.d % 4) return cudaErrorInvalidValue;
+  engram_conv_kernel<<<rb.M, 256, 0, st>>>(G, t, rb, ekv, evc);
   return cudaGetLastError();
 }
 
