@@ -156,6 +156,13 @@ class Engine {
   const float* final_norm = nullptr;
   Workspace ws;
   uint64_t epoch = 1;  // bumped whenever a session's device layout changes
+  // Graph of the host-API decode step (forward, step end, head), replayed
+  // while the row count, split count, KV precision and epoch are unchanged;
+  // the step's rows and tokens are copied in before it, the picks out after.
+  cudaGraphExec_t dec_graph = nullptr;
+  uint64_t dec_graph_epoch = 0, dec_warm_epoch = 0;
+  size_t dec_n = 0;
+  int dec_ns = 0, dec_int8 = -1;
   int* d_wait_flag = nullptr;  // tensor-core GEMM or int8 attention: a bounded wait expired (device flag)
   int* h_wait_flag = nullptr;  // pinned host copy, refreshed before each synchronous return
 
