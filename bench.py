@@ -31,6 +31,7 @@ import numpy as np
 ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "needle-rs_b200")
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
+METRIC = "decode tok/s (config 4: batched int8-KV sessions, 1024-token prompts)"
 HBM_FALLBACK, BF16_FALLBACK = 6650.0, 1590.0
 
 
@@ -46,6 +47,7 @@ def pkg():
 
 
 def container(seed: int = 0) -> bytes:
+    pkg()  # registers the package (the CUDA library itself loads only on first use)
     from needle_b200 import cact_pack
     cache = os.path.join(os.environ.get("TMPDIR", "/tmp"), f"needle3_random_seed{seed}.cact")
     if os.path.exists(cache):
@@ -187,11 +189,12 @@ def reference_arm(args):
     sample = (f"{ncpu} int8 sessions at context {ctx} (oracle C++ port of the reference CPU path, "
               f"one host thread per session), {args.steps} timed steps")
     print(json.dumps({
-        "impl": "reference", "metric": "decode tok/s (config 4: batched int8-KV sessions, ctx 1024)",
+        "impl": "reference", "metric": METRIC,
         "value": round(value, 2), "unit": "tok/s", "n_gpus": args.gpus, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 3), "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32+int8", "data": "synthetic",
-        "config": {"workload": "config4-decode", "sessions": ncpu, "prompt_len": ctx, "kv": "int8"},
+        "config": {"workload": "config4-decode", "sessions": args.sessions, "prompt_len": args.prompt, "kv": "int8",
+                   "sample": f"{ncpu} sessions at context {ctx} per timed step (one host thread each)"},
         "cpu_baseline": {"value": round(value, 2), "unit": "tok/s", "cores": ncpu, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(value, 2), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -570,7 +573,7 @@ def main():
     step_ms = dev_s / args.steps * 1e3
     total_prof = sum(prof.values())
     line = {
-        "metric": "decode tok/s (config 4: batched int8-KV sessions, 1024-token prompts)",
+        "metric": METRIC,
         "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(step_ms, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "f32 (int8 KV)", "data": "synthetic (seeded random-init container, shipped Needle-3 geometry)",
