@@ -486,7 +486,7 @@ def main():
         import datetime
 
         import torch.distributed as dist
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
                                 device_id=torch.device("cuda", local))
     nb = pkg()
     raw = container(0)
@@ -557,7 +557,7 @@ def main():
     tpu = attn_traffic_per_unit()
     traffic = round(tpu * attn_units_per_step(geo, per, pos_now) / geo["layers"]) if tpu else None
     extra = {}
-    if rank == 0:
+    if world == 1:  # the BASELINE config 0-3 lines and the CPU baseline are single-GPU items
         extra["gemv_config0"] = gemv_bandwidth(nb, torch, st)
         if not args.no_configs:
             extra["configs"] = kernel_configs(nb, torch, raw, hbm, bf16)
