@@ -67,11 +67,11 @@ void Workspace::release() {
   *this = Workspace();
 }
 
-bool Engine::ensure_ws(size_t rows, std::string* err) {
-  if (rows <= ws.cap) return true;
+bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
+  if (rows <= w.cap) return true;
   cudaStreamSynchronize(stream);
-  size_t cap = std::max(rows, ws.cap * 2);
-  ws.release();
+  size_t cap = std::max(rows, w.cap * 2);
+  w.release();
   const size_t d = G.d, dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   const size_t S = std::max(1, G.n_sites);
   const size_t kmax = std::max(dpad, opad);  // widest input of a projection
@@ -80,65 +80,65 @@ bool Engine::ensure_ws(size_t rows, std::string* err) {
     void** p;
     size_t bytes;
   } allocs[] = {
-      {(void**)&ws.lanes, cap * G.lanes * d * 4},   {(void**)&ws.u, cap * d * 4},
-      {(void**)&ws.bx, cap * d * 4},                {(void**)&ws.xh, cap * dpad * 4},
-      {(void**)&ws.proj, cap * G.proj_dim * 4},     {(void**)&ws.qpost, cap * G.q_dim * 4},
-      {(void**)&ws.q8s, cap * G.heads * 4},         {(void**)&ws.q8, cap * G.q_dim},
-      {(void**)&ws.ahi, cap * kmax * 2},            {(void**)&ws.alo, cap * kmax * 2},
-      {(void**)&ws.ainv, cap * 4},                  {(void**)&ws.cnt, cap * G.kvh * 4},
-      {(void**)&ws.whi, wmax * kmax * 2},           {(void**)&ws.wlo, wmax * kmax * 2},
-      {(void**)&ws.oh, cap * opad * 4},
-      {(void**)&ws.projo, cap * d * 4},             {(void**)&ws.gates, cap * 24 * 4},
-      {(void**)&ws.fetched, cap * S * d * 4},       {(void**)&ws.ekv, cap * S * 2 * d * 4},
-      {(void**)&ws.evc, cap * S * d * 4},           {(void**)&ws.lm_in, cap * dpad * 4},
-      {(void**)&ws.pk, cap * G.kvh * G.qk * 4},     {(void**)&ws.pv, cap * G.kvh * G.vh * 4},
-      {(void**)&ws.pks, cap * G.kvh * 4},           {(void**)&ws.pvs, cap * G.kvh * 4},
-      {(void**)&ws.rows, cap * sizeof(RowInfo)},    {(void**)&ws.tokens, cap * 4},
-      {(void**)&ws.next, cap * 4},                  {(void**)&ws.last_rows, cap * 4},
+      {(void**)&w.lanes, cap * G.lanes * d * 4},   {(void**)&w.u, cap * d * 4},
+      {(void**)&w.bx, cap * d * 4},                {(void**)&w.xh, cap * dpad * 4},
+      {(void**)&w.proj, cap * G.proj_dim * 4},     {(void**)&w.qpost, cap * G.q_dim * 4},
+      {(void**)&w.q8s, cap * G.heads * 4},         {(void**)&w.q8, cap * G.q_dim},
+      {(void**)&w.ahi, cap * kmax * 2},            {(void**)&w.alo, cap * kmax * 2},
+      {(void**)&w.ainv, cap * 4},                  {(void**)&w.cnt, cap * G.kvh * 4},
+      {(void**)&w.whi, wmax * kmax * 2},           {(void**)&w.wlo, wmax * kmax * 2},
+      {(void**)&w.oh, cap * opad * 4},
+      {(void**)&w.projo, cap * d * 4},             {(void**)&w.gates, cap * 24 * 4},
+      {(void**)&w.fetched, cap * S * d * 4},       {(void**)&w.ekv, cap * S * 2 * d * 4},
+      {(void**)&w.evc, cap * S * d * 4},           {(void**)&w.lm_in, cap * dpad * 4},
+      {(void**)&w.pk, cap * G.kvh * G.qk * 4},     {(void**)&w.pv, cap * G.kvh * G.vh * 4},
+      {(void**)&w.pks, cap * G.kvh * 4},           {(void**)&w.pvs, cap * G.kvh * 4},
+      {(void**)&w.rows, cap * sizeof(RowInfo)},    {(void**)&w.tokens, cap * 4},
+      {(void**)&w.next, cap * 4},                  {(void**)&w.last_rows, cap * 4},
   };
   for (auto& a : allocs) {
     cudaError_t e = cudaMalloc(a.p, std::max<size_t>(a.bytes, 256));
     if (e != cudaSuccess) {
-      ws.release();
+      w.release();
       *err = cuda_msg("workspace allocation", e);
       return false;
     }
   }
   {
-    cudaError_t e = cudaMemset(ws.cnt, 0, cap * G.kvh * 4);  // attention split counters start at zero
+    cudaError_t e = cudaMemset(w.cnt, 0, cap * G.kvh * 4);  // attention split counters start at zero
     if (e != cudaSuccess) {
-      ws.release();
+      w.release();
       *err = cuda_msg("workspace initialisation", e);
       return false;
     }
   }
-  ws.gs.hi = ws.ahi;
-  ws.gs.lo = ws.alo;
-  ws.gs.inv = ws.ainv;
-  ws.gs.elems = cap * kmax;
-  ws.gs.rows = cap;
-  ws.gs.whi = ws.whi;
-  ws.gs.wlo = ws.wlo;
-  ws.gs.welems = wmax * kmax;
-  ws.cap = cap;
+  w.gs.hi = w.ahi;
+  w.gs.lo = w.alo;
+  w.gs.inv = w.ainv;
+  w.gs.elems = cap * kmax;
+  w.gs.rows = cap;
+  w.gs.whi = w.whi;
+  w.gs.wlo = w.wlo;
+  w.gs.welems = wmax * kmax;
+  w.cap = cap;
   epoch++;
   return true;
 }
 
-bool Engine::ensure_part(size_t rows, int nsplit, std::string* err) {
+bool Engine::ensure_part(Workspace& w, size_t rows, int nsplit, std::string* err) {
   const size_t need = attn_part_floats((int)rows, G.heads, G.kvh, G.vh, nsplit);
-  if (need <= ws.part_cap) return true;
+  if (need <= w.part_cap) return true;
   cudaStreamSynchronize(stream);
-  if (ws.part) cudaFree(ws.part);
-  ws.part = nullptr;
-  const size_t cap = std::max(need, ws.part_cap * 2);
-  cudaError_t e = cudaMalloc(&ws.part, cap * 4);
+  if (w.part) cudaFree(w.part);
+  w.part = nullptr;
+  const size_t cap = std::max(need, w.part_cap * 2);
+  cudaError_t e = cudaMalloc(&w.part, cap * 4);
   if (e != cudaSuccess) {
-    ws.part_cap = 0;
+    w.part_cap = 0;
     *err = cuda_msg("allocating attention partials", e);
     return false;
   }
-  ws.part_cap = cap;
+  w.part_cap = cap;
   epoch++;
   return true;
 }
@@ -830,70 +830,70 @@ cudaError_t Prof::mark(int kind, cudaStream_t st, int nlaunch) {
 #define NB_MARK(kind, n) \
   if (prof) NB_TRY(prof->mark(kind, st, n))
 
-cudaError_t Engine::forward(const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof) {
+cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof) {
   const int M = rb.M, d = G.d, S = G.n_sites;
   const int dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   if (S > 0) {
-    NB_TRY(launch_engram_gather(G, d_tables, rb, ws.fetched, st));
+    NB_TRY(launch_engram_gather(G, d_tables, rb, w.fetched, st));
     for (int s = 0; s < S; ++s)
-      NB_TRY(cq_project(eng_kv[s], ws.fetched + (size_t)s * d, S * d, M, ws.ekv + (size_t)s * 2 * d,
-                        S * 2 * d, 0, 2 * d, st, 0, &ws.gs));
-    NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, ws.ekv, ws.evc, st));
-    NB_MARK(PK_ENGRAM, S * cq_launches(eng_kv[0], M, &ws.gs) + 2);
+      NB_TRY(cq_project(eng_kv[s], w.fetched + (size_t)s * d, S * d, M, w.ekv + (size_t)s * 2 * d,
+                        S * 2 * d, 0, 2 * d, st, 0, &w.gs));
+    NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, w.ekv, w.evc, st));
+    NB_MARK(PK_ENGRAM, S * cq_launches(eng_kv[0], M, &w.gs) + 2);
   }
-  NB_TRY(launch_embed(G, emb, rb, ws.lanes, st));
+  NB_TRY(launch_embed(G, emb, rb, w.lanes, st));
   NB_MARK(PK_EMBED, 1);
   for (int l = 0; l < G.layers; ++l) {
-    NB_TRY(launch_layer_pre(G, l, rb, ws.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
-                            site_of[l], ws.ekv, ws.evc, ws.u, ws.bx, ws.xh, ws.gates, st));
+    NB_TRY(launch_layer_pre(G, l, rb, w.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
+                            site_of[l], w.ekv, w.evc, w.u, w.bx, w.xh, w.gates, st));
     NB_MARK(PK_LAYER_PRE, 1);
-    NB_TRY(cq_project(qkvg[l], ws.xh, dpad, M, ws.proj, G.proj_dim, 0, G.proj_dim, st, 0, &ws.gs));
-    NB_MARK(PK_QKVG, cq_launches(qkvg[l], M, &ws.gs));
-    NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, ws.proj, ws.qpost, ws.pk, ws.pv, ws.pks, ws.pvs,
-                           int8 ? ws.q8 : nullptr, int8 ? ws.q8s : nullptr, st));
+    NB_TRY(cq_project(qkvg[l], w.xh, dpad, M, w.proj, G.proj_dim, 0, G.proj_dim, st, 0, &w.gs));
+    NB_MARK(PK_QKVG, cq_launches(qkvg[l], M, &w.gs));
+    NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, w.proj, w.qpost, w.pk, w.pv, w.pks, w.pvs,
+                           int8 ? w.q8 : nullptr, int8 ? w.q8s : nullptr, st));
     NB_MARK(PK_QKV_POST, 1);
     const bool fused = attn_fuses_finish(G, int8 ? 1 : 0) && nsplit <= 64;
-    NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, ws.qpost, ws.q8, ws.q8s, ws.pk, ws.pv, ws.pks, ws.pvs,
-                            ws.part, st, int8 ? 1 : 0, ws.proj, ws.oh, ws.cnt, d_wait_flag));
+    NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, w.qpost, w.q8, w.q8s, w.pk, w.pv, w.pks, w.pvs,
+                            w.part, st, int8 ? 1 : 0, w.proj, w.oh, w.cnt, d_wait_flag));
     NB_MARK(PK_ATTN, 1);
-    if (!fused) NB_TRY(launch_attn_finish(G, rb, nsplit, ws.part, ws.proj, ws.oh, st));
+    if (!fused) NB_TRY(launch_attn_finish(G, rb, nsplit, w.part, w.proj, w.oh, st));
     NB_MARK(PK_ATTN_FINISH, fused ? 0 : 1);
-    NB_TRY(cq_project(outp[l], ws.oh, opad, M, ws.projo, d, 0, d, st, 0, &ws.gs));
-    NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &ws.gs));
-    NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, ws.projo, ws.u, ws.bx,
-                             ws.gates, ws.lanes, st));
+    NB_TRY(cq_project(outp[l], w.oh, opad, M, w.projo, d, 0, d, st, 0, &w.gs));
+    NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &w.gs));
+    NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, w.projo, w.u, w.bx,
+                             w.gates, w.lanes, st));
     NB_MARK(PK_LAYER_POST, 1);
   }
-  NB_TRY(launch_final(G, rb, ws.lanes, final_norm, ws.lm_in, st));
+  NB_TRY(launch_final(G, rb, w.lanes, final_norm, w.lm_in, st));
   NB_MARK(PK_FINAL, 1);
   return cudaSuccess;
 }
 
 // Tied head over logit_rows (model.rs:358-374, :942-978) and the greedy pick.
-cudaError_t Engine::head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
+cudaError_t Engine::head(Workspace& w, const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                          cudaStream_t st, Prof* prof) {
-  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &ws.gs));
-  NB_MARK(PK_HEAD, cq_launches(emb, M, &ws.gs));
+  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &w.gs));
+  NB_MARK(PK_HEAD, cq_launches(emb, M, &w.gs));
   if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
   NB_MARK(PK_BOOK, picks ? 1 : 0);
   return cudaSuccess;
 }
 
-static bool ensure_logits(Engine* E, size_t rows, std::string* err) {
-  if (rows <= E->ws.last_cap) return true;
-  if (E->ws.logits) cudaFree(E->ws.logits);
-  if (E->ws.lm_last) cudaFree(E->ws.lm_last);
-  E->ws.logits = nullptr;
-  E->ws.lm_last = nullptr;
-  size_t cap = std::max(rows, E->ws.last_cap * 2);
-  cudaError_t e = cudaMalloc(&E->ws.logits, cap * E->G.logit_rows * 4);
-  if (e == cudaSuccess) e = cudaMalloc(&E->ws.lm_last, cap * ((E->G.d + 127) / 128 * 128) * 4);
+static bool ensure_logits(Engine* E, Workspace& w, size_t rows, std::string* err) {
+  if (rows <= w.last_cap) return true;
+  if (w.logits) cudaFree(w.logits);
+  if (w.lm_last) cudaFree(w.lm_last);
+  w.logits = nullptr;
+  w.lm_last = nullptr;
+  size_t cap = std::max(rows, w.last_cap * 2);
+  cudaError_t e = cudaMalloc(&w.logits, cap * E->G.logit_rows * 4);
+  if (e == cudaSuccess) e = cudaMalloc(&w.lm_last, cap * ((E->G.d + 127) / 128 * 128) * 4);
   if (e != cudaSuccess) {
     *err = cuda_msg("allocating logits", e);
-    E->ws.last_cap = 0;
+    w.last_cap = 0;
     return false;
   }
-  E->ws.last_cap = cap;
+  w.last_cap = cap;
   E->epoch++;
   return true;
 }
@@ -934,7 +934,7 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
     size_t maxlen = 0;
     for (size_t i = i0; i < i1; ++i) maxlen = std::max(maxlen, lens[i]);
     const int ns = attn_nsplit((int)rows, G.kvh, (int)maxlen);
-    if (!ensure_ws(rows, err) || !ensure_logits(this, i1 - i0, err) || !ensure_part(rows, ns, err)) return false;
+    if (!ensure_ws(ws, rows, err) || !ensure_logits(this, ws, i1 - i0, err) || !ensure_part(ws, rows, ns, err)) return false;
     std::vector<RowInfo> ri(rows);
     std::vector<uint32_t> tok(rows);
     std::vector<int> last(i1 - i0);
@@ -949,12 +949,12 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
     cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), rows * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tok.data(), rows * 4, cudaMemcpyHostToDevice, stream);
     RowBatch rb{ws.rows, ws.tokens, (int)rows, MODE_PREFILL};
-    if (e == cudaSuccess) e = forward(rb, stream, ss[i0]->int8, ns);
+    if (e == cudaSuccess) e = forward(ws, rb, stream, ss[i0]->int8, ns);
     if (e == cudaSuccess) e = launch_step_end(rb, stream);
     for (size_t i = 0; e == cudaSuccess && i < i1 - i0; ++i)
       e = cudaMemcpyAsync(ws.lm_last + i * dpad, ws.lm_in + (size_t)last[i] * dpad, dpad * 4,
                           cudaMemcpyDeviceToDevice, stream);
-    if (e == cudaSuccess) e = head(ws.lm_last, dpad, (int)(i1 - i0), ws.logits, ws.next, stream);
+    if (e == cudaSuccess) e = head(ws, ws.lm_last, dpad, (int)(i1 - i0), ws.logits, ws.next, stream);
     if (e == cudaSuccess && logits)
       e = cudaMemcpyAsync(logits + i0 * G.logit_rows, ws.logits, (i1 - i0) * G.logit_rows * 4,
                           cudaMemcpyDeviceToHost, stream);
@@ -1004,7 +1004,7 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   size_t maxpos = 0;
   for (size_t i = 0; i < n; ++i) maxpos = std::max(maxpos, ss[i]->pos);
   const int ns = attn_nsplit((int)n, G.kvh, (int)maxpos + 1);
-  if (!ensure_ws(n, err) || !ensure_logits(this, n, err) || !ensure_part(n, ns, err)) return false;
+  if (!ensure_ws(ws, n, err) || !ensure_logits(this, ws, n, err) || !ensure_part(ws, n, ns, err)) return false;
   std::vector<RowInfo> ri(n);
   for (size_t i = 0; i < n; ++i) ri[i] = RowInfo{ss[i]->d_desc, (int)ss[i]->pos, -1, -1, 0};
   const int dpad = (G.d + 127) / 128 * 128;
@@ -1013,9 +1013,9 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   RowBatch rb{ws.rows, ws.tokens, (int)n, MODE_DECODE};
   const int int8 = ss[0]->int8 ? 1 : 0;
   auto body = [&](cudaStream_t s) -> cudaError_t {
-    NB_TRY(forward(rb, s, int8, ns));
+    NB_TRY(forward(ws, rb, s, int8, ns));
     NB_TRY(launch_step_end(rb, s));
-    return head(ws.lm_in, dpad, (int)n, ws.logits, ws.next, s);
+    return head(ws, ws.lm_in, dpad, (int)n, ws.logits, ws.next, s);
   };
   // Replay the captured step while its shapes and buffers are unchanged; a
   // new shape or epoch first runs one eager step (one-time set-up such as
@@ -1137,19 +1137,19 @@ bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, boo
     b->nsplit = ns;
     b->graph_epoch = 0;
   }
-  if (!ensure_ws(n, err) || !ensure_part(n, ns, err)) return false;
+  if (!ensure_ws(ws, n, err) || !ensure_part(ws, n, ns, err)) return false;
   const int dpad = (G.d + 127) / 128 * 128;
   float* lg = d_logits;
   if (!lg) {
-    if (!ensure_logits(this, n, err)) return false;
+    if (!ensure_logits(this, ws, n, err)) return false;
     lg = ws.logits;
   }
   RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
   auto body = [&](cudaStream_t s) -> cudaError_t {
     NB_TRY(launch_step_begin(rb, b->d_sess, s));
-    NB_TRY(forward(rb, s, b->int8, ns));
+    NB_TRY(forward(ws, rb, s, b->int8, ns));
     NB_TRY(launch_step_end(rb, s));
-    NB_TRY(head(ws.lm_in, dpad, (int)n, lg, b->d_next, s));
+    NB_TRY(head(ws, ws.lm_in, dpad, (int)n, lg, b->d_next, s));
     return cudaSuccess;
   };
   cudaError_t e = cudaSuccess;
@@ -1205,7 +1205,7 @@ bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string*
   size_t maxpos = 0;
   for (Session* s : b->sessions) maxpos = std::max(maxpos, s->pos);
   const int ns = attn_nsplit((int)n, G.kvh, (int)maxpos + 1);
-  if (!ensure_ws(n, err) || !ensure_logits(this, n, err) || !ensure_part(n, ns, err)) return false;
+  if (!ensure_ws(ws, n, err) || !ensure_logits(this, ws, n, err) || !ensure_part(ws, n, ns, err)) return false;
   const int dpad = (G.d + 127) / 128 * 128;
   RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
   Prof prof;
@@ -1215,10 +1215,10 @@ bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string*
     NB_TRY(p->mark(PK_BOOK, st, 0));
     NB_TRY(launch_step_begin(rb, b->d_sess, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
-    NB_TRY(forward(rb, st, b->int8, ns, p));
+    NB_TRY(forward(ws, rb, st, b->int8, ns, p));
     NB_TRY(launch_step_end(rb, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
-    NB_TRY(head(ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p));
+    NB_TRY(head(ws, ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p));
     return cudaStreamSynchronize(st);
   };
   cudaError_t e = run();

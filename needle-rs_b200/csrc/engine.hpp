@@ -171,11 +171,12 @@ class Engine {
   cudaError_t queue_wait_flag(cudaStream_t st);
   cudaError_t wait_status(cudaStream_t st);
 
-  bool ensure_ws(size_t rows, std::string* err);
-  bool ensure_part(size_t rows, int nsplit, std::string* err);
+  bool ensure_ws(Workspace& w, size_t rows, std::string* err);
+  bool ensure_part(Workspace& w, size_t rows, int nsplit, std::string* err);
   bool ensure_slots(Session* s, size_t pos, std::string* err);
-  cudaError_t forward(const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof = nullptr);
-  cudaError_t head(const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
+  cudaError_t forward(Workspace& w, const RowBatch& rb, cudaStream_t st, bool int8, int nsplit,
+                      Prof* prof = nullptr);
+  cudaError_t head(Workspace& w, const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                    cudaStream_t st, Prof* prof = nullptr);
 };
 
