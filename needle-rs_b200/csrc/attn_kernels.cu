@@ -362,7 +362,7 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
 // fragment, so they never touch memory.
 //
 // Each of the four warps of a CTA owns every fourth 32-position block of the
-// CTA's range with its own three-block buffer and its own online softmax,
+// CTA's range with its own double block buffer and its own online softmax,
 // so the main loop has no block-wide barrier; the warps merge at the end and
 // the CTA writes the same (max, sum, P.V) partial as the f32 kernel.
 // ----------------------------------------------------------------------------
@@ -379,7 +379,7 @@ struct MmaTile {
   static constexpr bool K16 = (QK % 32) != 0;
 };
 
-constexpr int NBUF = 3;  // per-warp block buffers: two blocks in flight while one is consumed
+constexpr int NBUF = 2;  // per-warp block buffers: one block in flight while one is consumed (five CTAs per SM)
 
 template <int QK, int VH>
 struct __align__(16) MmaWarpSmem {
@@ -563,7 +563,7 @@ __device__ __forceinline__ void mma_issue_bulk(MmaWarpSmem<QK, VH>& W, int buf, 
 }
 
 template <int QK, int VH>
-__global__ void __launch_bounds__(128, 4) layer_attn_i8_kernel(Geo G, int li, RowBatch rb, int window, int nsplit,
+__global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, RowBatch rb, int window, int nsplit,
                                                             const int8_t* __restrict__ q8,
                                                             const float* __restrict__ q8s, const void* pk,
                                                             const void* pv, const float* pks, const float* pvs,
