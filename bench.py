@@ -250,6 +250,19 @@ def gemv_bandwidth(nb, torch, stream):
         per = e0.elapsed_time(e1) / (3 * reps) * 1e-3
         out[name] = {"us_per_gemv": round(per * 1e6, 3), "gbs": round(algo / per / 1e9, 1)}
         del g
+    # The same kernel streaming a matrix twice the size of L2 ([rows, 768] 2-bit,
+    # random codes, unit norms): the row-block loop amortises the per-CTA set-up,
+    # so this is the kernel's own bandwidth, which config 0's size cannot show.
+    big = int(2.2 * 126e6 / 192) // 16 * 16
+    packed = torch.randint(0, 256, (big * 192,), dtype=torch.uint8, device="cuda")
+    norms = torch.ones(big * 6, dtype=torch.float16, device="cuda")
+    ybig = torch.zeros(1, big, device="cuda")
+    us = _graph_us(torch, lambda s: nb.cq_project(packed.data_ptr(), norms.data_ptr(), big, 768, 2, lv, xh.data_ptr(),
+                                                  768, 1, ybig.data_ptr(), big, stream=s), 10)
+    sbytes = big * 192 + big * 6 * 2 + 768 * 4 + big * 4
+    out["stream"] = {"rows": big, "us_per_gemv": round(us, 2), "algorithmic_bytes": sbytes,
+                     "gbs": round(sbytes / us / 1e3, 1)}
+    del packed, norms, ybig
     # L2 copy bandwidth on this box (a 32 MB buffer, read + write), the L2 roofline denominator.
     a = torch.empty(8 << 20, dtype=torch.float32, device="cuda")
     b = torch.empty_like(a)

@@ -12,6 +12,8 @@
 // 2-bit byte holds indices 4b..4b+3 at bits 0-1, 2-3, 4-5, 6-7).
 #include <cuda_runtime.h>
 
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.hpp"
 #include "launch_util.hpp"
@@ -49,6 +51,7 @@ struct ChunkTraits<4> {
 
 constexpr int GV_THREADS = 128;
 constexpr int GV_PRE = 2;  // chunks per lane fetched before the producer wait
+constexpr int GV_MAX_CTAS = 148 * 8;  // grid cap: row blocks beyond it loop inside the CTAs
 
 __host__ __device__ inline int padded_len(int in_pad, int E) { return in_pad + (in_pad / E) * 4; }
 
@@ -120,27 +123,35 @@ __global__ void __launch_bounds__(GV_THREADS) cq_gemv_kernel(CqMat W, const floa
   float* xs = smem + 256 * T::P;    // [MT][plen]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int sub = lane % LPR;
-  const int r = (blockIdx.x * (GV_THREADS / 32) + warp) * (32 / LPR) + lane / LPR;
-  const bool active = r < nrows;
+  const int rows_per_block = (GV_THREADS / 32) * (32 / LPR);
+  const int nblocks = (nrows + rows_per_block - 1) / rows_per_block;
   const int nchunks = W.row_bytes / 16;
-  const uint8_t* row = nullptr;
-  const __half* nrm = nullptr;
-  if (active) {
-    int local;
-    const int s = find_seg(W, row0 + r, &local);
-    row = W.seg[s].packed + (size_t)local * W.row_bytes;
-    nrm = W.seg[s].norms + (size_t)local * W.groups;
-  }
-  // 1. this lane's first chunks and their norms
-  uint4 wpre[GV_PRE];
-  float npre[GV_PRE];
+  // This lane's row in row block `blk` and its first GV_PRE chunks and norms.
+  auto fetch = [&](int blk, uint4 (&w)[GV_PRE], float (&nv)[GV_PRE], const uint8_t** row, const __half** nrm) {
+    const int r = blk * rows_per_block + warp * (32 / LPR) + lane / LPR;
+    *row = nullptr;
+    *nrm = nullptr;
+    if (blk < nblocks && r < nrows) {
+      int local;
+      const int s = find_seg(W, row0 + r, &local);
+      *row = W.seg[s].packed + (size_t)local * W.row_bytes;
+      *nrm = W.seg[s].norms + (size_t)local * W.groups;
+    }
 #pragma unroll
-  for (int j = 0; j < GV_PRE; ++j) {
-    const int c = sub + j * LPR;
-    const bool ok = active && c < nchunks;
-    wpre[j] = ok ? __ldg(reinterpret_cast<const uint4*>(row) + c) : make_uint4(0u, 0u, 0u, 0u);
-    npre[j] = ok ? __half2float(nrm[c * T::E / W.group]) : 0.f;
-  }
+    for (int j = 0; j < GV_PRE; ++j) {
+      const int c = sub + j * LPR;
+      const bool ok = *row && c < nchunks;
+      w[j] = ok ? __ldg(reinterpret_cast<const uint4*>(*row) + c) : make_uint4(0u, 0u, 0u, 0u);
+      nv[j] = ok ? __half2float((*nrm)[c * T::E / W.group]) : 0.f;
+    }
+  };
+  // 1. this lane's first chunks (weights never change, so they are fetched
+  // before waiting on the producer of xh)
+  uint4 wcur[GV_PRE];
+  float ncur[GV_PRE];
+  const uint8_t* row;
+  const __half* nrm;
+  fetch(blockIdx.x, wcur, ncur, &row, &nrm);
   // 2. byte table
   if (threadIdx.x < 16) lev[threadIdx.x] = W.levels[threadIdx.x];
   __syncthreads();
@@ -160,28 +171,45 @@ __global__ void __launch_bounds__(GV_THREADS) cq_gemv_kernel(CqMat W, const floa
   __syncthreads();
   pdl_trigger();
 
-  float acc[MT];
+  // 4. row blocks blockIdx.x, + gridDim.x, ...: the next block's first chunks
+  // are in flight while this block's dots run.
+  for (int blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    uint4 wnext[GV_PRE];
+    float nnext[GV_PRE];
+    const uint8_t* rnext;
+    const __half* nrnext;
+    fetch(blk + gridDim.x, wnext, nnext, &rnext, &nrnext);
+    float acc[MT];
 #pragma unroll
-  for (int m = 0; m < MT; ++m) acc[m] = 0.f;
-  if (active) {
+    for (int m = 0; m < MT; ++m) acc[m] = 0.f;
+    if (row) {
+#pragma unroll
+      for (int j = 0; j < GV_PRE; ++j) {
+        const int c = sub + j * LPR;
+        if (c < nchunks) gemv_chunk<BITS, MT>(wcur[j], ncur[j], c, lut, xs, plen, M, acc);
+      }
+      for (int c = sub + GV_PRE * LPR; c < nchunks; c += LPR)
+        gemv_chunk<BITS, MT>(__ldg(reinterpret_cast<const uint4*>(row) + c), __half2float(nrm[c * T::E / W.group]),
+                             c, lut, xs, plen, M, acc);
+    }
+#pragma unroll
+    for (int m = 0; m < MT; ++m) {
+#pragma unroll
+      for (int o = LPR / 2; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+    }
+    const int r = blk * rows_per_block + warp * (32 / LPR) + lane / LPR;
+    if (row && sub == 0) {
+#pragma unroll
+      for (int m = 0; m < MT; ++m)
+        if (m < M) y[(size_t)m * ldy + r] = acc[m];
+    }
 #pragma unroll
     for (int j = 0; j < GV_PRE; ++j) {
-      const int c = sub + j * LPR;
-      if (c < nchunks) gemv_chunk<BITS, MT>(wpre[j], npre[j], c, lut, xs, plen, M, acc);
+      wcur[j] = wnext[j];
+      ncur[j] = nnext[j];
     }
-    for (int c = sub + GV_PRE * LPR; c < nchunks; c += LPR)
-      gemv_chunk<BITS, MT>(__ldg(reinterpret_cast<const uint4*>(row) + c), __half2float(nrm[c * T::E / W.group]),
-                           c, lut, xs, plen, M, acc);
-  }
-#pragma unroll
-  for (int m = 0; m < MT; ++m) {
-#pragma unroll
-    for (int o = LPR / 2; o > 0; o >>= 1) acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-  }
-  if (active && sub == 0) {
-#pragma unroll
-    for (int m = 0; m < MT; ++m)
-      if (m < M) y[(size_t)m * ldy + r] = acc[m];
+    row = rnext;
+    nrm = nrnext;
   }
 }
 
@@ -289,7 +317,9 @@ static cudaError_t launch_gemv(const CqMat& W, const float* xh, int ldx, int M, 
                                int row0, int nrows, cudaStream_t st) {
   using T = ChunkTraits<BITS>;
   const int rows_per_cta = (GV_THREADS / 32) * (32 / LPR);
-  const int grid = (nrows + rows_per_cta - 1) / rows_per_cta;
+  // One row block per CTA for small matrices; large ones loop over row blocks
+  // (the byte table and the activation are staged once per CTA).
+  const int grid = std::min((nrows + rows_per_cta - 1) / rows_per_cta, GV_MAX_CTAS);
   const size_t smem = (size_t)(256 * T::P + MT * padded_len(W.in_pad, T::E)) * sizeof(float);
   auto kern = cq_gemv_kernel<BITS, LPR, MT>;
   cudaError_t e = allow_smem((const void*)kern, smem);
