@@ -214,6 +214,90 @@ __global__ void __launch_bounds__(GV_THREADS) cq_gemv_kernel(CqMat W, const floa
 }
 
 // ----------------------------------------------------------------------------
+// GEMV for one activation row: partial-sum table per nibble position.
+//
+// After the activation arrives, the CTA builds, for every nibble position p of
+// the packed row (2 codes of 2 bits, or 1 code of 4 bits) and every nibble
+// value n, T[p][n] = sum_j level[code_j(n)] * xh[p * E + j] (16 floats per
+// position: 24 KB for a 2-bit row of 768). Each lane then owns one output row:
+// it reads its packed bytes 16 at a time and adds T[p][nibble] per nibble,
+// applying the FP16 norm per quantisation group (cq.rs:666-672 structure). The
+// lanes of a warp walk their rows in lockstep, so one table read touches one
+// 16-float row of T: distinct nibbles fall in distinct banks and equal ones
+// broadcast, so the table reads never conflict. Compared with decoding levels
+// and re-reading the activation (32 B of shared memory per 4 codes), a nibble
+// costs one 4-byte table read and one add.
+// ----------------------------------------------------------------------------
+constexpr int G1_THREADS = 128;
+
+template <int BITS>
+__global__ void __launch_bounds__(G1_THREADS) cq_gemv1_kernel(CqMat W, const float* __restrict__ xh,
+                                                              float* __restrict__ y, int row0, int nrows) {
+  constexpr int EN = 4 / BITS;                 // codes per nibble
+  constexpr int CPG = 128 * BITS / 8 / 16;     // 16-byte chunks per quantisation group of 128
+  extern __shared__ __align__(16) float T[];   // [npos][16]
+  __shared__ float lev[16];
+  const int npos = W.in_pad / EN;
+  const int nchunks = W.row_bytes / 16;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int nblocks = (nrows + G1_THREADS - 1) / G1_THREADS;
+  if (threadIdx.x < 16) lev[threadIdx.x] = W.levels[threadIdx.x];
+  __syncthreads();
+  pdl_wait();  // xh is written by the previous kernel
+  for (int e = threadIdx.x; e < npos * 16; e += G1_THREADS) {
+    const int pos = e >> 4, n = e & 15;
+    float v = 0.f;
+#pragma unroll
+    for (int j = 0; j < EN; ++j) v += lev[(n >> (j * BITS)) & ((1 << BITS) - 1)] * __ldg(xh + pos * EN + j);
+    T[e] = v;
+  }
+  __syncthreads();
+  pdl_trigger();
+  for (int blk = blockIdx.x; blk < nblocks; blk += gridDim.x) {
+    const int r = blk * G1_THREADS + warp * 32 + lane;
+    if (r >= nrows) continue;
+    int local;
+    const int s = find_seg(W, row0 + r, &local);
+    const uint4* row = reinterpret_cast<const uint4*>(W.seg[s].packed + (size_t)local * W.row_bytes);
+    const __half* nrm = W.seg[s].norms + (size_t)local * W.groups;
+    // Four independent partial sums (one per 32-bit word of a chunk) keep four
+    // table reads and adds in flight per lane.
+    float total = 0.f, gp[4] = {0.f, 0.f, 0.f, 0.f};
+    uint4 w = __ldg(row);
+    for (int c = 0; c < nchunks; ++c) {
+      const uint4 cur = w;
+      if (c + 1 < nchunks) w = __ldg(row + c + 1);
+      const uint32_t wd[4] = {cur.x, cur.y, cur.z, cur.w};
+      const float* tc = T + (size_t)c * 32 * 16;  // 32 nibble positions per chunk
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int q = 0; q < 4; ++q) gp[q] += tc[(q * 8 + i) * 16 + ((wd[q] >> (4 * i)) & 15)];
+      if ((c + 1) % CPG == 0) {
+        total += __half2float(nrm[c / CPG]) * ((gp[0] + gp[1]) + (gp[2] + gp[3]));
+        gp[0] = gp[1] = gp[2] = gp[3] = 0.f;
+      }
+    }
+    y[r] = total;
+  }
+}
+
+template <int BITS>
+static cudaError_t launch_gemv1(const CqMat& W, const float* xh, float* y, int row0, int nrows, cudaStream_t st) {
+  const size_t smem = (size_t)(W.in_pad * BITS / 4) * 16 * sizeof(float);
+  const int grid = std::min((nrows + G1_THREADS - 1) / G1_THREADS, GV_MAX_CTAS);
+  auto kern = cq_gemv1_kernel<BITS>;
+  cudaError_t e = allow_smem((const void*)kern, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(grid), dim3(G1_THREADS), smem, st, W, xh, y, row0, nrows);
+}
+
+// Table size the one-row GEMV may stage (shared memory per CTA), and the row
+// count from which it is used.
+constexpr size_t G1_MAX_TABLE_BYTES = 100 * 1024;
+constexpr int G1_MIN_ROWS = 16384;
+
+// ----------------------------------------------------------------------------
 // SIMT GEMM for many activation rows (prefill, batched decode).
 // Tile: 64 weight rows x 64 activation rows, K stepped one quantisation group
 // (128) at a time. The group's packed bytes are decoded once into shared memory
@@ -351,6 +435,10 @@ static cudaError_t launch_gemm_simt(const CqMat& W, const float* xh, int ldx, in
 template <int BITS>
 static cudaError_t project_bits(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
                                 int row0, int nrows, cudaStream_t st) {
+  // Large one-row products stream through the table kernel; smaller ones are
+  // latency-bound and take the kernel above, whose set-up is shorter.
+  if (M == 1 && nrows >= G1_MIN_ROWS && (size_t)W.in_pad * BITS / 4 * 16 * sizeof(float) <= G1_MAX_TABLE_BYTES)
+    return launch_gemv1<BITS>(W, xh, y, row0, nrows, st);
   if (M <= 1) return gemv_lpr<BITS, 1>(W, xh, ldx, M, y, ldy, row0, nrows, st);
   if (M <= 2) return gemv_lpr<BITS, 2>(W, xh, ldx, M, y, ldy, row0, nrows, st);
   if (M <= 4) return gemv_lpr<BITS, 4>(W, xh, ldx, M, y, ldy, row0, nrows, st);

@@ -77,8 +77,9 @@ def test_cq_index_unpacking_is_bit_exact(cuda, bits):
 @pytest.mark.parametrize("shape", [(3072, 768), (1568, 768), (768, 768), (8192, 768), (24, 3072), (1000, 300),
                                    (20000, 768)])
 def test_cq_gemv_matches_oracle(cuda, bits, shape):
-    """(20000, 768) has more row blocks than the GEMV grid, so CTAs loop over
-    row blocks."""
+    """(20000, 768): one activation row takes the partial-sum table kernel
+    (16384 rows and more); two to eight rows have more row blocks than the GEMV
+    grid, so CTAs loop over row blocks."""
     torch = cuda
     out, inp = shape
     cb = cact_pack.random_codebook(np.random.default_rng(9))  # BASELINE config 0 codebook
