@@ -59,13 +59,23 @@ namespace {
 constexpr int UM = 128;          // activation rows per CTA (MMA M)
 constexpr int UN = 128;          // weight rows per CTA (MMA N)
 constexpr int UK = 64;           // K per stage: 64 f16 = one 128-byte swizzle row
-constexpr int USTAGES = 3;
+// Pipeline stages and stage bytes: the three-MMA form carries four tiles per
+// stage (A hi, A lo, B hi, B lo) in three stages; the exact-level form three
+// tiles (no B remainder) in four stages of the same shared memory, one more
+// stage of loads in flight ahead of the MMAs.
+template <bool EXACT>
+struct Pipe {
+  static constexpr int STAGES = EXACT ? 4 : 3;
+  static constexpr uint32_t STAGE_BYTES = (EXACT ? 3u : 4u) * 128u * 128u;
+};
 constexpr int UGMAX = 32;        // groups of 128 supported (in_pad <= 4096)
 constexpr int UTHREADS = 320;    // warps 0-7 epilogue, 8 TMA + TMEM, 9 MMA
 constexpr uint32_t TILE = 128 * 128;        // bytes of one [128 rows][128 B] tile
-constexpr uint32_t STAGE_BYTES = 4 * TILE;  // A hi, A lo, B hi, B lo
 constexpr uint32_t NSM_BYTES = UGMAX * UN * 4;  // norm * level scale, [group][weight row]
-constexpr size_t UMMA_SMEM = 1024 + USTAGES * STAGE_BYTES + NSM_BYTES + 256;
+template <bool EXACT>
+constexpr size_t umma_smem() {
+  return 1024 + (size_t)Pipe<EXACT>::STAGES * Pipe<EXACT>::STAGE_BYTES + NSM_BYTES + 256;
+}
 constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every wait: one second
 
 __device__ __forceinline__ uint32_t su32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
@@ -191,6 +201,8 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
                const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
                int nrows) {
+  constexpr int USTAGES = Pipe<EXACT>::STAGES;
+  constexpr uint32_t STAGE_BYTES = Pipe<EXACT>::STAGE_BYTES;
   extern __shared__ unsigned char smraw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   float* nsm = reinterpret_cast<float*>(sm + USTAGES * STAGE_BYTES);
@@ -499,11 +511,11 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
       !make_map(&mbl, gs.wlo, nrows, K))
     return cudaErrorNotSupported;
   auto kern = exact ? cq_umma_kernel<true> : cq_umma_kernel<false>;
-  e = allow_smem((const void*)kern, UMMA_SMEM);
+  const size_t smem = exact ? umma_smem<true>() : umma_smem<false>();
+  e = allow_smem((const void*)kern, smem);
   if (e != cudaSuccess) return e;
   dim3 grid((nrows + UN - 1) / UN, (M + UM - 1) / UM);
-  kern<<<grid, UTHREADS, UMMA_SMEM, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy, row0,
-                                          nrows);
+  kern<<<grid, UTHREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy, row0, nrows);
   return cudaGetLastError();
 }
 
