@@ -231,18 +231,6 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  // Group norms of the tile's weight rows (times the inverse level scale).
-  for (int i = tid; i < ng * UN; i += UTHREADS) {
-    const int g = i / UN, nl = i % UN;
-    float v = 0.f;
-    if (n0 + nl < nrows) {
-      const uint8_t* prow;
-      const __half* pn;
-      cq_row_ptr(W, row0 + n0 + nl, &prow, &pn);
-      v = __half2float(pn[g]) * linv;
-    }
-    nsm[i] = v;
-  }
   if (warp == 8) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
                  "r"(512));
@@ -255,6 +243,18 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
 
   if (warp < 8) {
     // ------------------------------------------------ epilogue: drain each group
+    // Group norms of the tile's weight rows (times the inverse level scale),
+    // one weight row per thread, built while the first stages load; the
+    // eight epilogue warps meet on named barrier 1 before the first drain.
+    for (int nl = tid; nl < UN; nl += 256) {
+      const __half* pn = nullptr;
+      if (n0 + nl < nrows) {
+        const uint8_t* prow;
+        cq_row_ptr(W, row0 + n0 + nl, &prow, &pn);
+      }
+      for (int g = 0; g < ng; ++g) nsm[g * UN + nl] = pn ? __half2float(pn[g]) * linv : 0.f;
+    }
+    asm volatile("bar.sync 1, 256;" ::: "memory");
     const int q = warp & 3, h = warp >> 2;  // TMEM lane quarter, column half
     float acc[64];
 #pragma unroll
