@@ -491,7 +491,7 @@ static bool umma_scratch_ok(const CqMat& W, int M, int nrows, const GemmScratch*
 int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path) {
   if (M <= 0) return 0;
   if (force_path == 3 || (force_path == 0 && M > 8 && umma_scratch_ok(W, M, W.rows, gs) && umma_supported(W)))
-    return 3;
+    return 2;  // operand preparation + tensor-core GEMM
   return 1;
 }
 

@@ -19,19 +19,20 @@
 // numbers, as the packer writes them), the level remainders are zero: that
 // form skips their tile and their MMA, two MMAs per K step instead of three.
 //
-// Per call, cq_expand_kernel reads the packed `.cact` codes of the requested
-// rows in place and writes their level high parts and remainders as f16
-// [rows][in_pad] tiles (4 bytes per weight, L2-resident for the GEMM that
-// follows), once, instead of once per 128-row activation tile; the group
-// norms stay in the container and are applied by the epilogue.
+// Per call, one preparation launch (umma_prep_kernel) splits the activation
+// rows and reads the packed `.cact` codes of the requested weight rows in
+// place, writing their level high parts (and remainders) as f16
+// [rows][in_pad] tiles (L2-resident for the GEMM that follows), once, instead
+// of once per 128-row activation tile; the group norms stay in the container
+// and are applied by the epilogue.
 //
 // One CTA computes 128 activation rows x 128 weight rows with 10 warps:
-//   * warp 8 loads [128 rows x 64 k] tiles of the split activations (made by
-//     split_f16_kernel) and of the expanded levels with TMA and 128-byte
-//     swizzle into a 3-stage ring, and owns the TMEM allocation;
-//   * warp 9 (one thread) issues tcgen05.mma kind::f16 M=128 N=128 K=16, three
-//     per K step, into the group's accumulator pair; groups alternate between
-//     two pairs so one is drained while the other fills;
+//   * warp 8 loads [128 rows x 64 k] tiles of the split activations and of the
+//     expanded levels with TMA and 128-byte swizzle into a ring of four
+//     (three with level remainders) stages, and owns the TMEM allocation;
+//   * warp 9 (one thread) issues tcgen05.mma kind::f16 M=128 N=128 K=16, two
+//     (three) per K step, into the group's accumulator pair; groups alternate
+//     between two pairs so one is drained while the other fills;
 //   * warps 0-7 drain the accumulators (warp w reads TMEM lanes 32*(w%4)..,
 //     columns of half w/4) and store y.
 // Every wait on an mbarrier is bounded in time; on expiry the CTA raises a
@@ -374,16 +375,16 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
 // Level high parts and remainders of rows [row0, row0 + nrows) of a CQ
 // matrix, decoded from the packed codes (cq.rs:908-925) and scaled by 2^le:
 // hi / lo [nrows][in_pad] f16 (no remainders when wlo is null: exact levels).
-// One thread per 8 weights.
+// One thread per 8 weights; block `blk` of `nblk` strides over the rows.
 template <int BITS>
-__global__ void cq_expand_kernel(CqMat W, int row0, int nrows, int le, __half* __restrict__ whi,
-                                 __half* __restrict__ wlo) {
+__device__ __forceinline__ void expand_levels(const CqMat& W, int row0, int nrows, int le, __half* __restrict__ whi,
+                                              __half* __restrict__ wlo, int blk, int nblk) {
   __shared__ uint32_t tab[16];  // level * 2^le as (hi | lo << 16)
   if (threadIdx.x < 16) tab[threadIdx.x] = split_h(ldexpf(W.levels[threadIdx.x < (1 << BITS) ? threadIdx.x : 0], le));
   __syncthreads();
   const int per_row = W.in_pad / 8;
   const long total = (long)nrows * per_row;
-  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+  for (long i = blk * (long)blockDim.x + threadIdx.x; i < total; i += (long)nblk * blockDim.x) {
     const int n = (int)(i / per_row), c = (int)(i % per_row);
     const uint8_t* prow;
     const __half* pn;
@@ -404,11 +405,12 @@ __global__ void cq_expand_kernel(CqMat W, int row0, int nrows, int le, __half* _
 }
 
 // f32 activations [M][ldx] -> row-scaled f16 high parts and remainders
-// [M][K] and the inverse row scales [M]. One warp per row.
-__global__ void split_f16_kernel(const float* __restrict__ x, int ldx, int M, int K, __half* __restrict__ hi,
-                                 __half* __restrict__ lo, float* __restrict__ inv) {
+// [M][K] and the inverse row scales [M]. One warp per row (block `blk`: rows
+// blk * 8 ..).
+__device__ __forceinline__ void split_rows(const float* __restrict__ x, int ldx, int M, int K, __half* __restrict__ hi,
+                                           __half* __restrict__ lo, float* __restrict__ inv, int blk) {
   const int lane = threadIdx.x & 31;
-  const int m = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int m = blk * (blockDim.x >> 5) + (threadIdx.x >> 5);
   if (m >= M) return;
   const float* xr = x + (size_t)m * ldx;
   float amax = 0.f;
@@ -434,6 +436,22 @@ __global__ void split_f16_kernel(const float* __restrict__ x, int ldx, int M, in
     *reinterpret_cast<uint4*>(hi + (size_t)m * K + c) = make_uint4(h[0], h[1], h[2], h[3]);
     *reinterpret_cast<uint4*>(lo + (size_t)m * K + c) = make_uint4(l[0], l[1], l[2], l[3]);
   }
+}
+
+// Both operand preparations of one projection in one launch (they are
+// independent): blocks below `split_blocks` split activation rows (split_f16),
+// the others expand level tiles (cq_expand).
+template <int BITS>
+__global__ void __launch_bounds__(256) umma_prep_kernel(const float* __restrict__ x, int ldx, int M, int K,
+                                                        __half* __restrict__ hi, __half* __restrict__ lo,
+                                                        float* __restrict__ inv, int split_blocks, CqMat W, int row0,
+                                                        int nrows, int le, __half* __restrict__ whi,
+                                                        __half* __restrict__ wlo) {
+  if ((int)blockIdx.x < split_blocks) {
+    split_rows(x, ldx, M, K, hi, lo, inv, blockIdx.x);
+    return;
+  }
+  expand_levels<BITS>(W, row0, nrows, le, whi, wlo, blockIdx.x - split_blocks, gridDim.x - split_blocks);
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -492,17 +510,18 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
     const float v = std::ldexp(W.levels[i], le);
     if (__half2float(__float2half_rn(v)) != v) exact = false;
   }
-  split_f16_kernel<<<(M + 7) / 8, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
+  cudaError_t e;
   {
+    const int split_blocks = (M + 7) / 8;
     const long total = (long)nrows * (K / 8);
-    const int blocks = (int)std::min<long>((total + 255) / 256, 148L * 8);
+    const int eblocks = (int)std::min<long>((total + 255) / 256, 148L * 8);
     __half* wlo = exact ? nullptr : gs.wlo;
     if (W.bits == 2)
-      cq_expand_kernel<2><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, wlo);
+      umma_prep_kernel<2><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv, split_blocks,
+                                                                  W, row0, nrows, le, gs.whi, wlo);
     else
-      cq_expand_kernel<4><<<blocks, 256, 0, st>>>(W, row0, nrows, le, gs.whi, wlo);
+      umma_prep_kernel<4><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv, split_blocks,
+                                                                  W, row0, nrows, le, gs.whi, wlo);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
