@@ -37,8 +37,9 @@ typedef struct NeedleV3Handle NeedleV3Handle;
 /* needle.h:370 / v3.rs:63-77. NULL on failure; free with needle_v3_free(). */
 NeedleV3Handle *needle_v3_load(const char *cact_path);
 
-/* needle.h:382 / v3.rs:109-128. This build serves the full depth only:
- * `layers` must equal the container's layer count, anything else fails. */
+/* needle.h:382 / v3.rs:109-128. The `layers`-block rung of the intelligence
+ * ladder, sliced at load (v3.rs:656-745); the container's own depth loads it
+ * unchanged. NULL for a depth outside 2..num_layers. */
 NeedleV3Handle *needle_v3_load_with_depth(const char *cact_path, size_t layers);
 
 /* needle.h:385 / v3.rs:135-138. 0 for NULL. */
@@ -89,6 +90,10 @@ const char *needle_last_error(void);
 
 typedef struct NeedleV3Session NeedleV3Session;
 typedef struct NeedleV3Batch NeedleV3Batch;
+
+/* needle_v3_load_with_depth from a container already in memory
+ * (V3Engine::from_bytes_with_depth, v3_engine.rs:140-143). */
+NeedleV3Handle *needle_v3_load_bytes_with_depth(const unsigned char *data, size_t len, size_t layers);
 
 /* A per-generation KV cache on the device (V3Cache::with_precision,
  * cache.rs:177-238): `hint` sizes the first allocation, rings grow on demand. */

@@ -44,6 +44,7 @@ def lib() -> C.CDLL:
         "needle_v3_load": (vp, [C.c_char_p]),
         "needle_v3_load_bytes": (vp, [C.c_char_p, sz]),
         "needle_v3_load_with_depth": (vp, [C.c_char_p, sz]),
+        "needle_v3_load_bytes_with_depth": (vp, [C.c_char_p, sz, sz]),
         "needle_v3_num_layers": (sz, [vp]),
         "needle_v3_run": (vp, [vp, C.c_char_p, C.c_char_p]),
         "needle_v3_run_json": (vp, [vp, C.c_char_p, C.c_char_p]),
@@ -122,17 +123,30 @@ class V3Engine:
         self.logit_rows = self.geometry["logit_rows"]
 
     @classmethod
-    def from_bytes(cls, raw: bytes) -> "V3Engine":
-        h = lib().needle_v3_load_bytes(raw, len(raw))
-        if not h:
-            _fail("needle_v3_load_bytes")
+    def from_bytes(cls, raw: bytes, depth: int | None = None) -> "V3Engine":
+        """`depth` loads that rung of the intelligence ladder
+        (from_bytes_with_depth, v3_engine.rs:140-143)."""
+        if depth is None:
+            h = lib().needle_v3_load_bytes(raw, len(raw))
+            if not h:
+                _fail("needle_v3_load_bytes")
+        else:
+            h = lib().needle_v3_load_bytes_with_depth(raw, len(raw), depth)
+            if not h:
+                _fail("needle_v3_load_bytes_with_depth")
         return cls(h)
 
     @classmethod
-    def load(cls, path: str) -> "V3Engine":
-        h = lib().needle_v3_load(path.encode())
-        if not h:
-            _fail("needle_v3_load")
+    def load(cls, path: str, depth: int | None = None) -> "V3Engine":
+        """`depth` as in load_with_depth (v3_engine.rs:132-138)."""
+        if depth is None:
+            h = lib().needle_v3_load(path.encode())
+            if not h:
+                _fail("needle_v3_load")
+        else:
+            h = lib().needle_v3_load_with_depth(path.encode(), depth)
+            if not h:
+                _fail("needle_v3_load_with_depth")
         return cls(h)
 
     def close(self):

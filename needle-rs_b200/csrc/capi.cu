@@ -42,9 +42,9 @@ void set_err(const std::string& m) {
   g_has_err = true;
 }
 
-NeedleV3Handle* load_engine(const uint8_t* data, size_t len, const std::string& what) {
+NeedleV3Handle* load_engine(const uint8_t* data, size_t len, const std::string& what, size_t depth = 0) {
   std::string err;
-  nb::Engine* e = nb::Engine::load(data, len, &err);
+  nb::Engine* e = nb::Engine::load(data, len, &err, depth);
   if (!e) {
     set_err(what + err);
     return nullptr;
@@ -191,18 +191,38 @@ NeedleV3Handle* needle_v3_load_bytes(const unsigned char* data, size_t len) {
   return load_engine(data, len, "failed to load container: ");
 }
 
-NeedleV3Handle* needle_v3_load_with_depth(const char* cact_path, size_t layers) {
+NeedleV3Handle* needle_v3_load_bytes_with_depth(const unsigned char* data, size_t len, size_t layers) {
   clear_err();
-  NeedleV3Handle* h = needle_v3_load(cact_path);
-  if (!h) return nullptr;
-  if (layers != h->eng->cfg.layers) {
-    set_err(std::string("failed to load ") + cact_path + " at " + std::to_string(layers) +
-            " layers: this GPU engine serves the full depth (" + std::to_string(h->eng->cfg.layers) +
-            " layers) only");
-    delete h;
+  if (!data) {
+    set_err("data was null");
     return nullptr;
   }
-  return h;
+  const std::string what = "failed to load container at " + std::to_string(layers) + " layers: ";
+  if (layers == 0) {
+    set_err(what + "depth is outside the ladder");
+    return nullptr;
+  }
+  return load_engine(data, len, what, layers);
+}
+
+NeedleV3Handle* needle_v3_load_with_depth(const char* cact_path, size_t layers) {
+  clear_err();
+  if (!cact_path) {
+    set_err("cact_path was null or not UTF-8");
+    return nullptr;
+  }
+  const std::string what = std::string("failed to load ") + cact_path + " at " + std::to_string(layers) + " layers: ";
+  std::vector<uint8_t> raw;
+  if (!read_file(cact_path, &raw)) {
+    set_err(what + "cannot read file");
+    return nullptr;
+  }
+  // 0 is not a rung (the engine reads 0 as "every block").
+  if (layers == 0) {
+    set_err(what + "depth is outside the ladder");
+    return nullptr;
+  }
+  return load_engine(raw.data(), raw.size(), what, layers);
 }
 
 size_t needle_v3_num_layers(NeedleV3Handle* h) {

@@ -229,7 +229,31 @@ bool concat(CqMat* dst, const CqMat& add, std::string* err) {
 }
 }  // namespace
 
-Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
+// The intelligence ladder (ladder.rs:28-74): block 0 and the last block, then
+// repeatedly the midpoint of the widest gap between chosen blocks (the leftmost
+// gap on ties); the rung of depth k keeps the first k blocks of that order, in
+// stack order. Depths outside 2..layers are not rungs.
+static bool ladder_kept(size_t layers, size_t depth, std::vector<int>* kept) {
+  if (depth < 2 || depth > layers) return false;
+  std::vector<int> sel = {0, (int)layers - 1};
+  while (sel.size() < depth) {
+    std::vector<int> s = sel;
+    std::sort(s.begin(), s.end());
+    int at = -1, widest = 1;
+    for (size_t i = 0; i + 1 < s.size(); ++i)
+      if (s[i + 1] - s[i] > widest) {
+        widest = s[i + 1] - s[i];
+        at = (int)i;
+      }
+    if (at < 0) break;
+    sel.push_back((s[at] + s[at + 1]) / 2);
+  }
+  std::sort(sel.begin(), sel.end());
+  *kept = sel;
+  return sel.size() == depth;
+}
+
+Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t depth) {
   if (!raw) {
     *err = "data was null";
     return nullptr;
@@ -331,6 +355,19 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
       c.heads * c.vh % 128 || c.out_vocab > c.vocab) {
     *err = "geometry outside what this GPU path supports";
     return nullptr;
+  }
+  // Blocks this engine runs, by source block in the container: all of them, or
+  // a ladder rung. Tensors are read at the container's depth and selected
+  // below; nothing is re-quantised.
+  std::vector<int> src;
+  const bool rung = depth != 0 && depth != c.layers;
+  if (rung) {
+    if (!ladder_kept(c.layers, depth, &src)) {
+      *err = "depth is outside the ladder";
+      return nullptr;
+    }
+  } else {
+    for (size_t l = 0; l < c.layers; ++l) src.push_back((int)l);
   }
 
   // Canon walk (v3.rs:236-332).
@@ -483,6 +520,29 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
     *err = cuda_msg("uploading parameters", e);
     return nullptr;
   }
+  // config_at_depth (v3.rs:620-640): kept blocks renumbered contiguously; the
+  // global layers and Engram sites follow them, a site surviving exactly when
+  // its block does. ssrc maps each kept site to its source site.
+  std::vector<int> ssrc;
+  if (rung) {
+    auto pos = [&](int l) {
+      auto it = std::find(src.begin(), src.end(), l);
+      return it == src.end() ? -1 : (int)(it - src.begin());
+    };
+    std::vector<int> gl, st;
+    for (int l : c.global_layers)
+      if (pos(l) >= 0) gl.push_back(pos(l));
+    for (size_t s = 0; s < c.sites.size(); ++s)
+      if (pos(c.sites[s]) >= 0) {
+        st.push_back(pos(c.sites[s]));
+        ssrc.push_back((int)s);
+      }
+    c.layers = src.size();
+    c.global_layers = gl;
+    c.sites = st;
+  } else {
+    for (size_t s = 0; s < c.sites.size(); ++s) ssrc.push_back((int)s);
+  }
   const float* P = E->d_params;
   auto pp = [&](long off) -> const float* { return off >= 0 ? P + off : nullptr; };
   // CQ tensors.
@@ -492,8 +552,9 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
   E->outp.resize(c.layers);
   for (size_t l = 0; okc && l < c.layers; ++l) {
     CqMat q, k, v, g;
-    okc = L.cq(li[l].q, E->d_blob, &q) && L.cq(li[l].k, E->d_blob, &k) && L.cq(li[l].v, E->d_blob, &v) &&
-          L.cq(li[l].gate, E->d_blob, &g) && L.cq(li[l].out, E->d_blob, &E->outp[l]);
+    const LayerIdx& x = li[src[l]];
+    okc = L.cq(x.q, E->d_blob, &q) && L.cq(x.k, E->d_blob, &k) && L.cq(x.v, E->d_blob, &v) &&
+          L.cq(x.gate, E->d_blob, &g) && L.cq(x.out, E->d_blob, &E->outp[l]);
     std::memset(&E->qkvg[l], 0, sizeof(CqMat));
     okc = okc && concat(&E->qkvg[l], q, err) && concat(&E->qkvg[l], k, err) && concat(&E->qkvg[l], v, err) &&
           concat(&E->qkvg[l], g, err);
@@ -502,7 +563,8 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
   E->eng_tables.resize(c.sites.size());
   for (size_t s = 0; okc && s < c.sites.size(); ++s) {
     CqMat k, v;
-    okc = L.cq(et[s], E->d_blob, &E->eng_tables[s]) && L.cq(ek[s], E->d_blob, &k) && L.cq(ev[s], E->d_blob, &v);
+    const int o = ssrc[s];
+    okc = L.cq(et[o], E->d_blob, &E->eng_tables[s]) && L.cq(ek[o], E->d_blob, &k) && L.cq(ev[o], E->d_blob, &v);
     std::memset(&E->eng_kv[s], 0, sizeof(CqMat));
     okc = okc && concat(&E->eng_kv[s], k, err) && concat(&E->eng_kv[s], v, err);
   }
@@ -526,7 +588,7 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
     if ((size_t)c.sites[s] < c.layers) E->site_of[c.sites[s]] = (int)s;
   for (size_t l = 0; l < c.layers; ++l) {
     LayerParams& x = E->lp[l];
-    const LOff& o = lo[l];
+    const LOff& o = lo[src[l]];
     x.norm_in = pp(o.norm_in);
     x.q_taps = c.taps ? pp(o.qt) : nullptr;
     x.k_taps = c.taps ? pp(o.kt) : nullptr;
@@ -551,14 +613,16 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
     x.cond_u = pp(o.mlp[12]);
     x.window = (int)c.span(l);
     MhcParams& m = E->mp[l];
-    m.a_pre = L.arena[a_pre + l];
-    m.a_post = L.arena[a_post + l];
-    m.a_res = L.arena[a_res + l];
-    m.b_pre = P + b_pre + l * c.lanes;
-    m.b_post = P + b_post + l * c.lanes;
-    m.b_res = P + b_res + l * c.lanes * c.lanes;
+    const size_t sl = (size_t)src[l];
+    m.a_pre = L.arena[a_pre + sl];
+    m.a_post = L.arena[a_post + sl];
+    m.a_res = L.arena[a_res + sl];
+    m.b_pre = P + b_pre + sl * c.lanes;
+    m.b_post = P + b_post + sl * c.lanes;
+    m.b_res = P + b_res + sl * c.lanes * c.lanes;
+    m.phi_layer = src[l];  // the lane matrices keep the container's rows
   }
-  for (size_t s = 0; s < c.sites.size(); ++s) E->eng_taps.push_back(P + etaps[s]);
+  for (size_t s = 0; s < c.sites.size(); ++s) E->eng_taps.push_back(P + etaps[ssrc[s]]);
   E->final_norm = P + fnorm;
   // HadamardMLP weight fragments for the tensor-core block tail.
   for (size_t l = 0; l < c.layers; ++l) E->lp[l].hfrag = nullptr;
@@ -566,7 +630,7 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err) {
     const size_t fw = hada_frag_words((int)ba);
     std::vector<uint32_t> frags(fw * c.layers);
     for (size_t l = 0; l < c.layers; ++l) {
-      const LOff& o = lo[l];
+      const LOff& o = lo[src[l]];
       // Stage order per Kronecker pair: B^T (w*b) then A^T (w*a).
       const float* mats[6] = {&L.arena[o.mlp[6]], &L.arena[o.mlp[5]], &L.arena[o.mlp[8]],
                               &L.arena[o.mlp[7]], &L.arena[o.mlp[10]], &L.arena[o.mlp[9]]};

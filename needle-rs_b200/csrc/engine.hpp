@@ -114,7 +114,9 @@ struct Prof {
 
 class Engine {
  public:
-  static Engine* load(const uint8_t* data, size_t len, std::string* err);
+  // depth 0 (or the container's own depth) loads every block; 2..layers-1
+  // loads that rung of the intelligence ladder (v3.rs:656-745).
+  static Engine* load(const uint8_t* data, size_t len, std::string* err, size_t depth = 0);
   // One decode step of `b`, eager, with events between kernel groups; writes
   // per-kind milliseconds (PK_COUNT floats) and the number of launches.
   bool profile_batch_step(Batch* b, float* ms, int* launches, std::string* err);

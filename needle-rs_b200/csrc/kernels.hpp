@@ -34,6 +34,10 @@ struct LayerParams {
 struct MhcParams {
   float a_pre, a_post, a_res;
   const float *b_pre, *b_post, *b_res;  // this layer's slices
+  // Layer whose rows of the mHC lane matrices this block reads: the block's
+  // own index, or its index in the full stack for a ladder rung sliced at
+  // load (v3.rs:656-745; the active lane still follows the sliced index).
+  int phi_layer;
 };
 
 enum RowMode { MODE_DECODE = 0, MODE_PREFILL = 1 };

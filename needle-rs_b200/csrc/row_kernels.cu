@@ -346,7 +346,7 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
       const uint8_t* prow;
       const __half* pn;
       int rbo, go;
-      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      phi_row(o, mp.phi_layer, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
       if (ch * 16 < rbo) cp_async16(csm + (size_t)o * rbmax + ch * 16, prow + ch * 16, true);
     }
     cp_commit();
@@ -356,7 +356,7 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
       const uint8_t* prow;
       const __half* pn;
       int rbo, go;
-      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      phi_row(o, mp.phi_layer, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
       nsm[i] = g < go ? __half2float(pn[g]) : 0.f;
     }
   }
@@ -545,7 +545,7 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
       const uint8_t* prow;
       const __half* pn;
       int rbo, go;
-      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      phi_row(o, mp.phi_layer, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
       if (ch * 16 < rbo) cp_async16(pt_dyn + (size_t)o * rbmax + ch * 16, prow + ch * 16, true);
     }
     cp_commit();
@@ -555,7 +555,7 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
       const uint8_t* prow;
       const __half* pn;
       int rbo, go;
-      phi_row(o, li, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
+      phi_row(o, mp.phi_layer, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
       nsm[i] = g < go ? __half2float(pn[g]) : 0.f;
     }
     cp_wait<0>();

@@ -157,6 +157,44 @@ void* orc_model_load(const uint8_t* data, size_t len, char* err, size_t errlen) 
   return m;
 }
 void orc_model_free(void* m) { delete (V3Model*)m; }
+// The `depth`-block rung of a full-depth container (v3.rs:656-745).
+void* orc_model_load_depth(const uint8_t* data, size_t len, size_t depth, char* err, size_t errlen) {
+  V3Model* m = new V3Model();
+  std::string e = load_model(data, len, m);
+  if (e.empty()) e = slice_to_depth(m, depth);
+  if (!e.empty()) {
+    put_err(err, errlen, e);
+    delete m;
+    return nullptr;
+  }
+  return m;
+}
+// ladder.rs:28: writes num_layers entries.
+void orc_ladder_order(size_t num_layers, int64_t* out) {
+  std::vector<size_t> o = ladder_order(num_layers);
+  for (size_t i = 0; i < o.size(); ++i) out[i] = (int64_t)o[i];
+}
+// ladder.rs:67: writes depth entries and returns 1, or returns 0 outside the ladder.
+int orc_ladder_layers(size_t num_layers, size_t depth, int64_t* out) {
+  std::vector<size_t> k;
+  if (!ladder_layer_indices(num_layers, depth, &k)) return 0;
+  for (size_t i = 0; i < k.size(); ++i) out[i] = (int64_t)k[i];
+  return 1;
+}
+// Global layers and Engram sites of the model (rungs renumber them): counts
+// first, then the lists; returns the number of entries written.
+int orc_model_layer_roles(void* mp, int64_t* out, int cap) {
+  const V3Config& c = ((V3Model*)mp)->cfg;
+  int w = 0;
+  if (cap < 2) return 0;
+  out[w++] = (int64_t)c.global_layers.size();
+  out[w++] = (int64_t)c.engram.sites.size();
+  for (size_t l : c.global_layers)
+    if (w < cap) out[w++] = (int64_t)l;
+  for (size_t l : c.engram.sites)
+    if (w < cap) out[w++] = (int64_t)l;
+  return w;
+}
 // vocab, out_vocab, d_model, heads, kv_heads, layers, qk, vh, max_seq, hada_n, lanes,
 // window, conv_taps, logit_rows
 void orc_model_geom(void* mp, int64_t* out) {

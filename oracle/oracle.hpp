@@ -62,6 +62,7 @@ struct CqWeight {  // cq.rs:117-141
                             float* y) const;                                   // cq.rs:446
   void dequantize_row(size_t o, float* out) const;                             // cq.rs:763
   void decode_group(const uint8_t* row, size_t g, float norm, float* buf) const;  // cq.rs:791
+  bool select_rows(const std::vector<size_t>& rows, CqWeight* out) const;          // cq.rs:151
 
  private:
   void matvec_rows_serial(const float* xh, size_t row_start, float* y, size_t rows) const;
@@ -272,5 +273,10 @@ constexpr uint8_t DT_FP16 = 1, DT_FP32 = 2, DT_CQ = 3, DT_RAW = 4;
 // Parse container bytes and build the model (cact.rs:990-1030, v3.rs:25-484).
 // Returns an empty string on success, else a message.
 std::string load_model(const uint8_t* raw, size_t len, V3Model* out);
+
+// ---------------------------------------------------------------- v3/ladder.rs, v3.rs:620-745
+std::vector<size_t> ladder_order(size_t num_layers);                                   // ladder.rs:28
+bool ladder_layer_indices(size_t num_layers, size_t depth, std::vector<size_t>* kept);  // ladder.rs:67
+std::string slice_to_depth(V3Model* m, size_t depth);  // v3.rs:656, on a model loaded at full depth
 
 }  // namespace oracle

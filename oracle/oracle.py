@@ -33,6 +33,10 @@ def lib():
         for name, res, args in [
             ("orc_cq_new", vp, [vp, sz, sz, sz, sz, C.c_int, vp, C.c_char_p, sz]),
             ("orc_model_load", vp, [C.c_char_p, sz, C.c_char_p, sz]),
+            ("orc_model_load_depth", vp, [C.c_char_p, sz, sz, C.c_char_p, sz]),
+            ("orc_ladder_order", None, [sz, vp]),
+            ("orc_ladder_layers", C.c_int, [sz, sz, vp]),
+            ("orc_model_layer_roles", C.c_int, [vp, vp, C.c_int]),
             ("orc_session_new", vp, [vp, sz, C.c_int]),
             ("orc_session_clone", vp, [vp]),
             ("orc_quant_into", C.c_float, [vp, vp, sz]),
@@ -180,11 +184,30 @@ def ngram_valid(p, table, orders, heads):
     return bool(lib().orc_ngram_valid(p, table, P(o), len(o), heads))
 
 
+def ladder_order(num_layers: int):
+    """ladder.rs:28: the order blocks join the ladder."""
+    out = np.zeros(max(num_layers, 1), np.int64)
+    lib().orc_ladder_order(C.c_size_t(num_layers), P(out))
+    return [int(x) for x in out[:num_layers]]
+
+
+def ladder_layers(num_layers: int, depth: int):
+    """ladder.rs:67: the blocks a rung keeps, ascending, or None outside 2..=num_layers."""
+    out = np.zeros(max(depth, 1), np.int64)
+    if not lib().orc_ladder_layers(num_layers, depth, P(out)):
+        return None
+    return [int(x) for x in out[:depth]]
+
+
 class Model:
-    def __init__(self, raw: bytes):
+    def __init__(self, raw: bytes, depth: int | None = None):
+        """The full model, or the `depth`-block rung sliced at load (v3.rs:656)."""
         err = C.create_string_buffer(256)
         self.raw = raw
-        self.h = lib().orc_model_load(raw, len(raw), err, 256)
+        if depth is None:
+            self.h = lib().orc_model_load(raw, len(raw), err, 256)
+        else:
+            self.h = lib().orc_model_load_depth(raw, len(raw), depth, err, 256)
         if not self.h:
             raise ValueError(err.value.decode())
         g = np.zeros(14, np.int64)
@@ -203,6 +226,13 @@ class Model:
         out = np.zeros((len(ids), self.rows), np.float32)
         lib().orc_forward_sequence(C.c_void_p(self.h), P(ids), C.c_size_t(len(ids)), P(out))
         return out
+
+    def layer_roles(self):
+        """(global-attention layers, Engram sites) of this model's stack."""
+        out = np.zeros(64, np.int64)
+        lib().orc_model_layer_roles(C.c_void_p(self.h), P(out), 64)
+        ng, ns = int(out[0]), int(out[1])
+        return [int(x) for x in out[2:2 + ng]], [int(x) for x in out[2 + ng:2 + ng + ns]]
 
     def kv_bytes(self, seq_len, int8):
         return lib().orc_model_kv_bytes(self.h, seq_len, int(int8))

@@ -11,6 +11,10 @@ the reference checkout; the committed fixtures are what the tests read).
   needle3.cact (the reference's `tests/cact_v3_vectors.json`): record dtypes,
   shapes, groups, widths and byte sizes, which pin the container canon and the
   CQ size arithmetic.
+* ladder_rungs.json — the reference's `tests/v3_ladder_rungs.json` (the
+  intelligence ladder of a 20-block model: block order and, per depth, the
+  kept blocks, renumbered global layers and Engram sites; gated by
+  crates/needle-infer/tests/v3_ladder_slice.rs:39-68), copied unchanged.
 * numpy_ref_{tiny,full}.npz — logits of the reference's own numpy model
   (`tools/needle3_reference.py`, imported from the reference checkout) on
   seeded synthetic containers written by needle-rs_b200/cact_pack.py. The
@@ -30,7 +34,15 @@ sys.path.insert(0, os.path.join(ROOT, "needle-rs_b200"))
 import cact_pack  # noqa: E402
 
 
+def copy_ladder(ref_root):
+    with open(os.path.join(ref_root, "tests", "v3_ladder_rungs.json")) as f:
+        lad = json.load(f)
+    with open(os.path.join(HERE, "ladder_rungs.json"), "w") as f:
+        json.dump(lad, f)
+
+
 def main(ref_root):
+    copy_ladder(ref_root)
     with open(os.path.join(ref_root, "tests", "v3_kv_quant_vectors.json")) as f:
         kv = json.load(f)
     with open(os.path.join(HERE, "kv_quant_vectors.json"), "w") as f:
