@@ -233,6 +233,37 @@ bool concat(CqMat* dst, const CqMat& add, std::string* err) {
 // repeatedly the midpoint of the widest gap between chosen blocks (the leftmost
 // gap on ties); the rung of depth k keeps the first k blocks of that order, in
 // stack order. Depths outside 2..layers are not rungs.
+// One row of a single-tensor CQ matrix as dense f32 weights, each 128-group
+// rotated: H (norm_g * levels[codes]) with H the normalised Walsh-Hadamard
+// matrix of the group (natural order, symmetric), so that
+// dense . x == norm_g * (levels . H x), the CQ dot of cq.rs:666-672. Computed
+// in double from the container's host bytes and rounded once.
+static void cq_dense_row(const uint8_t* raw, const uint8_t* d_blob, const CqMat& m, int row, float* out) {
+  const uint8_t* codes = raw + (m.seg[0].packed - d_blob) + (size_t)row * m.row_bytes;
+  const uint8_t* nb = raw + (reinterpret_cast<const uint8_t*>(m.seg[0].norms) - d_blob) + (size_t)row * m.groups * 2;
+  const int bits = m.bits, mask = (1 << bits) - 1;
+  double v[128];
+  for (int g = 0; g < m.groups; ++g) {
+    __half_raw hr;
+    hr.x = (unsigned short)(nb[2 * g] | (nb[2 * g + 1] << 8));
+    const double norm = (double)__half2float(__half(hr));
+    for (int j = 0; j < 128; ++j) {
+      const size_t bit = (size_t)(g * 128 + j) * bits;
+      const int c = (codes[bit / 8] >> (bit % 8)) & mask;
+      v[j] = (double)m.levels[c] * norm;
+    }
+    for (int h = 1; h < 128; h <<= 1)
+      for (int i = 0; i < 128; i += 2 * h)
+        for (int j = i; j < i + h; ++j) {
+          const double a = v[j], b = v[j + h];
+          v[j] = a + b;
+          v[j + h] = a - b;
+        }
+    const double sc = 1.0 / std::sqrt(128.0);
+    for (int j = 0; j < 128; ++j) out[g * 128 + j] = (float)(v[j] * sc);
+  }
+}
+
 static bool ladder_kept(size_t layers, size_t depth, std::vector<int>* kept) {
   if (depth < 2 || depth > layers) return false;
   std::vector<int> sel = {0, (int)layers - 1};
@@ -622,6 +653,26 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     m.b_res = P + b_res + sl * c.lanes * c.lanes;
     m.phi_layer = src[l];  // the lane matrices keep the container's rows
   }
+  // Dense rotated mHC lane-matrix rows for the tiled layer-pre kernel, every
+  // container layer (a rung addresses them through its source blocks).
+  {
+    const size_t nr = 2 * c.lanes + c.lanes * c.lanes, Wd = c.lanes * d, PL = (size_t)E->phi_pre.rows / c.lanes;
+    std::vector<float> dense(PL * nr * Wd);
+    for (size_t l = 0; l < PL; ++l)
+      for (size_t o = 0; o < nr; ++o) {
+        float* dst = dense.data() + (l * nr + o) * Wd;
+        if (o < c.lanes) cq_dense_row(raw, E->d_blob, E->phi_pre, (int)(l * c.lanes + o), dst);
+        else if (o < 2 * c.lanes) cq_dense_row(raw, E->d_blob, E->phi_post, (int)(l * c.lanes + o - c.lanes), dst);
+        else cq_dense_row(raw, E->d_blob, E->phi_res, (int)(l * c.lanes * c.lanes + o - 2 * c.lanes), dst);
+      }
+    e = cudaMalloc(&E->d_phid, dense.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(E->d_phid, dense.data(), dense.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("uploading the mHC lane matrices", e);
+      return nullptr;
+    }
+    for (size_t l = 0; l < c.layers; ++l) E->mp[l].phi_dense = E->d_phid + (size_t)src[l] * nr * Wd;
+  }
   for (size_t s = 0; s < c.sites.size(); ++s) E->eng_taps.push_back(P + etaps[ssrc[s]]);
   E->final_norm = P + fnorm;
   // HadamardMLP weight fragments for the tensor-core block tail.
@@ -699,6 +750,7 @@ Engine::~Engine() {
   if (d_perm) cudaFree(d_perm);
   if (d_rope) cudaFree(d_rope);
   if (d_hfrag) cudaFree(d_hfrag);
+  if (d_phid) cudaFree(d_phid);
   if (d_tables) cudaFree(d_tables);
   if (h_wait_flag) cudaFreeHost(h_wait_flag);
   if (stream) cudaStreamDestroy(stream);

@@ -148,6 +148,7 @@ class Engine {
   uint32_t* d_perm = nullptr;
   float* d_rope = nullptr;
   uint32_t* d_hfrag = nullptr;  // HadamardMLP weight fragments, all layers
+  float* d_phid = nullptr;      // mHC lane-matrix rows, dequantised and rotated, all container layers
   CqMat emb{}, phi_pre{}, phi_post{}, phi_res{};
   std::vector<CqMat> qkvg, outp, eng_kv, eng_tables;
   CqMat* d_tables = nullptr;

@@ -38,6 +38,9 @@ struct MhcParams {
   // own index, or its index in the full stack for a ladder rung sliced at
   // load (v3.rs:656-745; the active lane still follows the sliced index).
   int phi_layer;
+  // This block's 2n + n^2 rows of the lane matrices, dequantised and rotated
+  // per 128-group at load: [2n + n^2][lanes * d_model] f32 (tiled path).
+  const float* phi_dense;
 };
 
 enum RowMode { MODE_DECODE = 0, MODE_PREFILL = 1 };

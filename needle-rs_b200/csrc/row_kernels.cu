@@ -495,146 +495,106 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
 }
 
 // The same computation for many rows: PT_M rows per CTA so each mHC weight
-// group is decoded once for PT_M rows instead of once per row.
+// row is read once for PT_M rows instead of once per row.
 //
-// Phase 1 streams the lanes of the tile one 128-wide group at a time: each
-// warp loads two rows' group, accumulates their sums of squares and rotates it
-// (FWHT) into a shared tile; then warp w dots the tile with outputs w, w+8 and
-// w+16 of the 2n + n^2 projected rows, lane l covering group elements
-// l*4..l*4+3. The rotation is linear, so the rms_unit scale (kernels.rs:32) is
-// applied to the finished dot products rather than to the lanes first. The
-// next group's lanes are loaded while the current one is consumed. The CTA's
-// 2n + n^2 packed weight rows and their norms are copied to shared memory once
-// at the start, so the group loop reads no weights from global memory.
+// Phase 1 streams the lanes of the tile one 128-wide group at a time through a
+// PT_S-stage cp.async ring in shared memory, and warp w dots every row of the
+// tile with outputs w, w+8 and w+16 of the 2n + n^2 projected rows, lane l
+// covering group elements l*4..l*4+3. The weights are the mHC lane matrices
+// dequantised and rotated once at load (MhcParams::phi_dense, f32): the CQ dot
+// norm * (levels . H x) (cq.rs:666-672) equals (H (norm * levels)) . x for the
+// symmetric group rotation H, so the lanes need no rotation here. The rms_unit
+// scale (kernels.rs:32) is applied to the finished dot products rather than to
+// the lanes first. Each warp keeps the next group's weights in flight.
 // Phase 2 (one warp per row, no block barriers): gates and Sinkhorn, mix_down
 // re-reading the tile's lanes (L2-resident), the Engram gate, the ZCRMS norm
 // and the rotation of the attention input, exactly as the per-row kernel.
 constexpr int PT_DQ = 8;   // d_model / 128 supported on this path
+constexpr int PT_S = 4;    // lane-group stages in flight
 
 // PT_M rows per CTA: 16 for large batches, 4 for small ones (four times the
 // CTAs, shorter per-CTA loops).
 template <int PT_M>
 __global__ void __launch_bounds__(256, 2)
-layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes, CqMat phi_pre,
-                       CqMat phi_post, CqMat phi_res, MhcParams mp, const float* __restrict__ norm_in,
-                       int site, const float* __restrict__ ekv, const float* __restrict__ evc,
-                       float* __restrict__ u_out, float* __restrict__ bx_out, float* __restrict__ xh_out,
-                       float* __restrict__ gates, int rbmax, int gmax) {
+layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes, MhcParams mp,
+                       const float* __restrict__ norm_in, int site, const float* __restrict__ ekv,
+                       const float* __restrict__ evc, float* __restrict__ u_out, float* __restrict__ bx_out,
+                       float* __restrict__ xh_out, float* __restrict__ gates) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
-  __shared__ __align__(16) float Xs[PT_M][128];
-  __shared__ float lev[48];
+  __shared__ __align__(16) float Xr[PT_S][PT_M][128];
   __shared__ float phi_s[PT_M][24];
   __shared__ float ss_s[PT_M];
   __shared__ float hp_s[PT_M][4];      // mix-down gates per row
   __shared__ float red3[8][PT_M][3];   // per-warp partial sums per row
-  extern __shared__ __align__(16) unsigned char pt_dyn[];  // [nrow][rbmax] codes, [nrow][gmax] norms
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
   const int n = G.lanes, d = G.d, W = n * d, nrow = 2 * n + n * n;
   const int m0 = blockIdx.x * PT_M;
   const int rows = min(PT_M, rb.M - m0);
   const int ngroups = W / 128;
-  load_phi_levels(phi_pre, phi_post, phi_res, lev);
-  float* nsm = reinterpret_cast<float*>(pt_dyn + (size_t)nrow * rbmax);
 
-  // Stage the packed rows and norms of all 2n + n^2 projected rows; every
-  // (row, chunk) and (row, group) is independent.
-  {
-    const int cpr = rbmax / 16;
-    for (int i = tid; i < nrow * cpr; i += blockDim.x) {
-      const int o = i / cpr, ch = i % cpr;
-      const uint8_t* prow;
-      const __half* pn;
-      int rbo, go;
-      phi_row(o, mp.phi_layer, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
-      if (ch * 16 < rbo) cp_async16(pt_dyn + (size_t)o * rbmax + ch * 16, prow + ch * 16, true);
-    }
-    cp_commit();
-#pragma unroll 4
-    for (int i = tid; i < nrow * gmax; i += blockDim.x) {
-      const int o = i / gmax, g = i % gmax;
-      const uint8_t* prow;
-      const __half* pn;
-      int rbo, go;
-      phi_row(o, mp.phi_layer, n, phi_pre, phi_post, phi_res, &prow, &pn, &rbo, &go);
-      nsm[i] = g < go ? __half2float(pn[g]) : 0.f;
-    }
-    cp_wait<0>();
-  }
+  // Ring stage s <- group g of every tile row (rows past the batch zero-filled).
+  auto issue = [&](int g) {
+    if (g < ngroups)
+      for (int i = tid; i < PT_M * 32; i += blockDim.x) {
+        const int m = i >> 5, c = (i & 31) * 4;
+        const float* src = lanes + (size_t)(m0 + (m < rows ? m : 0)) * W + g * 128 + c;
+        cp_async16(&Xr[g % PT_S][m][c], src, m < rows);
+      }
+    cp_commit();  // one group per call, empty past the end, so the wait counts stay fixed
+  };
+#pragma unroll
+  for (int g = 0; g < PT_S - 1; ++g) issue(g);
 
-  // This warp's projected rows: o = wid + 8j.
-  int wbits[3], wlev[3];
+  // This warp's projected rows: o = wid + 8j, each a [W] row of dense weights.
   bool wok[3];
+  const float* wrow[3];
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
     const int o = wid + 8 * j;
     wok[j] = o < nrow;
-    wbits[j] = !wok[j] ? 4 : (o < n ? phi_pre.bits : (o < 2 * n ? phi_post.bits : phi_res.bits));
-    wlev[j] = !wok[j] ? 0 : (o < n ? 0 : (o < 2 * n ? 16 : 32));
+    wrow[j] = mp.phi_dense + (size_t)(wok[j] ? o : 0) * W + lane * 4;
   }
-
-  // Rows wid and wid + 8 of the tile are loaded and rotated by this warp.
-  const bool okA = wid < rows, okB = wid + 8 < rows;
-  const float* lrA = lanes + (size_t)(m0 + wid) * W + lane * 4;
-  const float* lrB = lanes + (size_t)(m0 + wid + 8) * W + lane * 4;
   const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
-  float4 nA = okA ? __ldg(reinterpret_cast<const float4*>(lrA)) : z4;
-  float4 nB = okB ? __ldg(reinterpret_cast<const float4*>(lrB)) : z4;
+  float4 wn[3];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) wn[j] = wok[j] ? __ldg(reinterpret_cast<const float4*>(wrow[j])) : z4;
   float ssA = 0.f, ssB = 0.f;
   float acc[3][PT_M];
 #pragma unroll
   for (int j = 0; j < 3; ++j)
 #pragma unroll
     for (int m = 0; m < PT_M; ++m) acc[j][m] = 0.f;
-  __syncthreads();  // level tables, staged rows and norms
 
   for (int g = 0; g < ngroups; ++g) {
-    const float4 cA = nA, cB = nB;
-    if (g + 1 < ngroups) {
-      if (okA) nA = __ldg(reinterpret_cast<const float4*>(lrA + (g + 1) * 128));
-      if (okB) nB = __ldg(reinterpret_cast<const float4*>(lrB + (g + 1) * 128));
-    }
-    uint32_t wc[3];
-    float wn[3];
+    issue(g + PT_S - 1);
+    float4 wc[3];
 #pragma unroll
     for (int j = 0; j < 3; ++j) {
-      const int o = wid + 8 * j;
-      const unsigned char* cr = pt_dyn + (size_t)(wok[j] ? o : 0) * rbmax;
-      wc[j] = !wok[j] ? 0u
-                      : (wbits[j] == 4 ? (uint32_t)reinterpret_cast<const uint16_t*>(cr + g * 64)[lane]
-                                       : (uint32_t)cr[g * 32 + lane]);
-      wn[j] = wok[j] ? nsm[o * gmax + g] : 0.f;
+      wc[j] = wn[j];
+      if (wok[j] && g + 1 < ngroups) wn[j] = __ldg(reinterpret_cast<const float4*>(wrow[j] + (g + 1) * 128));
     }
+    cp_wait<PT_S - 1>();
+    __syncthreads();
+    const int s = g % PT_S;
     // Tile rows wid and wid + 8 exist only below PT_M (warp-uniform tests).
     if (wid < PT_M) {
-      float v[4] = {cA.x, cA.y, cA.z, cA.w};
-      ssA += v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
-      fwht128_warp(v);
-      reinterpret_cast<float4*>(Xs[wid])[lane] = make_float4(v[0], v[1], v[2], v[3]);
+      const float4 x = reinterpret_cast<const float4*>(Xr[s][wid])[lane];
+      ssA += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
     }
     if (wid + 8 < PT_M) {
-      float u[4] = {cB.x, cB.y, cB.z, cB.w};
-      ssB += u[0] * u[0] + u[1] * u[1] + u[2] * u[2] + u[3] * u[3];
-      fwht128_warp(u);
-      reinterpret_cast<float4*>(Xs[wid + 8])[lane] = make_float4(u[0], u[1], u[2], u[3]);
-    }
-    __syncthreads();
-    float w4[3][4];
-#pragma unroll
-    for (int j = 0; j < 3; ++j) {
-      const int b = wbits[j], mask = (1 << b) - 1;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) w4[j][i] = wn[j] * lev[wlev[j] + ((wc[j] >> (i * b)) & mask)];
+      const float4 x = reinterpret_cast<const float4*>(Xr[s][wid + 8])[lane];
+      ssB += x.x * x.x + x.y * x.y + x.z * x.z + x.w * x.w;
     }
 #pragma unroll
     for (int m = 0; m < PT_M; ++m) {
       if (m < rows) {
-        const float4 x = reinterpret_cast<const float4*>(Xs[m])[lane];
+        const float4 x = reinterpret_cast<const float4*>(Xr[s][m])[lane];
 #pragma unroll
         for (int j = 0; j < 3; ++j)
-          acc[j][m] += w4[j][0] * x.x + w4[j][1] * x.y + w4[j][2] * x.z + w4[j][3] * x.w;
+          acc[j][m] += wc[j].x * x.x + wc[j].y * x.y + wc[j].z * x.z + wc[j].w * x.w;
       }
     }
-    __syncthreads();
+    __syncthreads();  // stage s is refilled by the next iteration's issue
   }
 #pragma unroll
   for (int j = 0; j < 3; ++j) {
@@ -647,8 +607,8 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
   ssA = warp_sum(ssA);
   ssB = warp_sum(ssB);
   if (lane == 0) {
-    if (okA) ss_s[wid] = ssA;
-    if (okB) ss_s[wid + 8] = ssB;
+    if (wid < rows) ss_s[wid] = ssA;
+    if (wid + 8 < rows) ss_s[wid + 8] = ssB;
   }
   __syncthreads();
 
@@ -782,17 +742,11 @@ constexpr int PRE_TILED_MIN_ROWS = 2;
 
 template <int PT_M>
 static cudaError_t launch_pre_tiled(const Geo& G, int li, const RowBatch& rb, const float* lanes,
-                                    const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
                                     const MhcParams& mp, const float* norm_in, int site, const float* ekv,
-                                    const float* evc, float* u, float* bx, float* xh, float* gates, int rbmax,
-                                    int gmax, cudaStream_t st) {
-  const int nrow = 2 * G.lanes + G.lanes * G.lanes;
-  const size_t dyn = (size_t)nrow * rbmax + (size_t)nrow * gmax * 4;
-  auto k = layer_pre_tiled_kernel<PT_M>;
-  cudaError_t e = allow_smem((const void*)k, dyn);
-  if (e != cudaSuccess) return e;
-  k<<<(rb.M + PT_M - 1) / PT_M, 256, dyn, st>>>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site,
-                                                ekv, evc, u, bx, xh, gates, rbmax, gmax);
+                                    const float* evc, float* u, float* bx, float* xh, float* gates,
+                                    cudaStream_t st) {
+  layer_pre_tiled_kernel<PT_M><<<(rb.M + PT_M - 1) / PT_M, 256, 0, st>>>(G, li, rb, lanes, mp, norm_in, site, ekv,
+                                                                       evc, u, bx, xh, gates);
   return cudaGetLastError();
 }
 
@@ -806,13 +760,12 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
   const int rbmax = std::max(phi_pre.row_bytes, std::max(phi_post.row_bytes, phi_res.row_bytes));
   const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
   const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
-                        (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0;
+                        (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0 && mp.phi_dense &&
+                        (reinterpret_cast<uintptr_t>(mp.phi_dense) & 15) == 0;
   if (tiled_ok && rb.M >= 2048)
-    return launch_pre_tiled<16>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx,
-                                xh, gates, rbmax, gmax, st);
+    return launch_pre_tiled<16>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
   if (tiled_ok && rb.M >= PRE_TILED_MIN_ROWS)
-    return launch_pre_tiled<4>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx,
-                               xh, gates, rbmax, gmax, st);
+    return launch_pre_tiled<4>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
   const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48 + nrow * gmax) * sizeof(float) +
                       (size_t)nrow * rbmax + 16;
