@@ -188,6 +188,41 @@ struct __align__(16) PostSmem {
   float gs[PW][24];        // gates per row: hpost [nl], hres [nl * nl]
 };
 
+// One halving step of a many-value warp sum: lanes with bit `o` set keep the
+// upper H values of v[0 .. 2H), the others the lower H, each adding its
+// partner's copy of the half it keeps.
+template <int C, int H>
+__device__ __forceinline__ void halve_sum(float (&v)[C], int lane, int o) {
+  const bool up = (lane & o) != 0;
+#pragma unroll
+  for (int k = 0; k < H; ++k) {
+    const float send = up ? v[k] : v[k + H];
+    const float keep = up ? v[k + H] : v[k];
+    v[k] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+  }
+}
+
+// Warp sums of C = 64 or 16 values per lane by recursive halving (62 or 31
+// shuffles instead of 5 per value). Afterwards lane l holds the sums of values
+// 2l and 2l + 1 in v[0], v[1] (C = 64), or of value l / 2 in v[0] (C = 16).
+template <int C>
+__device__ __forceinline__ void warp_sum_many(float (&v)[C], int lane) {
+  static_assert(C == 64 || C == 16, "64 or 16 values");
+  if constexpr (C == 64) {
+    halve_sum<64, 32>(v, lane, 16);
+    halve_sum<64, 16>(v, lane, 8);
+    halve_sum<64, 8>(v, lane, 4);
+    halve_sum<64, 4>(v, lane, 2);
+    halve_sum<64, 2>(v, lane, 1);
+  } else {
+    halve_sum<16, 8>(v, lane, 16);
+    halve_sum<16, 4>(v, lane, 8);
+    halve_sum<16, 2>(v, lane, 4);
+    halve_sum<16, 1>(v, lane, 2);
+    v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  }
+}
+
 // Block max over the PW warps of per-row partials red[warp][row].
 template <int PW>
 __device__ __forceinline__ float rows_max(float (*red)[PW], int row) {
@@ -220,6 +255,14 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
   const int nrow = min(PW, rb.M - r0);
   const int d = G.d, nl = G.lanes, rk = G.cond_rank;
 
+  // The final phase re-reads this CTA's rows of u and of the lanes, which the
+  // attention's KV stream has usually pushed out of L2: start bringing them
+  // back now (a hint; nothing waits on it).
+  if (tid == 0) {
+    const unsigned ub = (unsigned)(nrow * d * 4), lb = (unsigned)(nrow * nl * d * 4);
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(u + (size_t)r0 * d), "r"(ub) : "memory");
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(lanes + (size_t)r0 * nl * d), "r"(lb) : "memory");
+  }
   // Gates of the CTA's rows: hpost [nl], hres [nl * nl] (written by layer_pre).
   if (tid < PW * 24) S.gs[tid / 24][tid % 24] = (tid / 24 < nrow) ? gates[(size_t)(r0 + tid / 24) * 24 + tid % 24] : 0.f;
   // ---- per row (warp w): post_norm + gated residual (model.rs:309-316), s1 and its rms
@@ -312,11 +355,20 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
       if (i >= nrow) break;  // rows past the batch are never read
       const float m = warp_max(mz[i]);
       if (lane == 0) S.amax[w][i] = m;
+    }
+    // Conditioning logits: all PW x 8 partial sums of the warp at once (ranks
+    // past rk and rows past the batch hold zeros).
+    float sums[PW * 8];
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        const float v = j < rk ? warp_sum(acc[i][j]) : 0.f;
-        if (lane == 0) S.part[w][i][j] = v;
-      }
+    for (int i = 0; i < PW; ++i)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) sums[i * 8 + j] = acc[i][j];
+    warp_sum_many<PW * 8>(sums, lane);
+    if constexpr (PW * 8 == 64) {
+      S.part[w][lane >> 2][(2 * lane) & 7] = sums[0];
+      S.part[w][lane >> 2][((2 * lane) & 7) + 1] = sums[1];
+    } else {
+      if ((lane & 1) == 0) S.part[w][lane >> 4][(lane >> 1) & 7] = sums[0];
     }
   }
   __syncthreads();
