@@ -722,11 +722,13 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
   __syncthreads();
   if (!act_w) return;
   const float4 ni = __ldg(reinterpret_cast<const float4*>(norm_in + c0));
+  // Rows are independent: predicated (not exited) so their latencies overlap.
 #pragma unroll
   for (int m = 0; m < PT_M; ++m) {
-    if (m >= rows) break;
+    if (m >= rows) continue;
     float s2 = 0.f;
-    for (int w = 0; w < nq; ++w) s2 += red3[w][m][0];
+#pragma unroll
+    for (int w = 0; w < PT_DQ; ++w) s2 += w < nq ? red3[w][m][0] : 0.f;
     const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
     const size_t r = m0 + m;
     *reinterpret_cast<float4*>(bx_out + r * d + c0) = make_float4(bxv[m][0], bxv[m][1], bxv[m][2], bxv[m][3]);
