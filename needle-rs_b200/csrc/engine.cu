@@ -383,7 +383,7 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
       c.heads / c.kvh > 8 || (c.qk != 16 && c.qk != 32 && c.qk != 48 && c.qk != 64) || c.vh > 64 ||
       c.vh % 2 || (c.heads / c.kvh) * c.vh > 512 || c.hada_n > 1024 || c.hada_n < c.d ||
       (c.hada_n & (c.hada_n - 1)) || c.sites.size() > 16 || c.max_seq == 0 ||
-      c.heads * c.vh % 128 || c.out_vocab > c.vocab) {
+      c.heads * c.vh % 128 || c.out_vocab > c.vocab || c.taps > (size_t)MAX_QKV_TAPS) {
     *err = "geometry outside what this GPU path supports";
     return nullptr;
   }

@@ -31,6 +31,9 @@ struct LayerParams {
   float hinv[6];
 };
 
+// Longest causal QKV conv the GPU path runs (the shipped geometry has 3 taps).
+constexpr int MAX_QKV_TAPS = 4;
+
 struct MhcParams {
   float a_pre, a_post, a_res;
   const float *b_pre, *b_post, *b_res;  // this layer's slices

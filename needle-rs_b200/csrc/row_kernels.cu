@@ -830,8 +830,11 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
       if (taps > 0) {
         const float4 t0 = *reinterpret_cast<const float4*>(tp + cc);
         acc = make_float4(t0.x * x.x, t0.y * x.y, t0.z * x.z, t0.w * x.w);
-        for (int j = 1; j < taps; ++j) {
-          if (j > p) break;
+        // Fixed trip count, predicated taps: every tap's loads are in flight
+        // together instead of one tap per memory round trip.
+#pragma unroll
+        for (int j = 1; j < MAX_QKV_TAPS; ++j) {
+          if (j >= taps || j > p) continue;
           const float4 pv = *reinterpret_cast<const float4*>(
               rb.mode == MODE_PREFILL ? proj + (size_t)(r - j) * G.proj_dim + c
                                       : tail + (size_t)((p - j) % tl) * qkv + c);
@@ -862,8 +865,9 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
     float acc = x;
     if (taps > 0) {
       acc = tp[cc] * x;
-      for (int j = 1; j < taps; ++j) {
-        if (j > p) break;
+#pragma unroll
+      for (int j = 1; j < MAX_QKV_TAPS; ++j) {
+        if (j >= taps || j > p) continue;
         float prev = rb.mode == MODE_PREFILL ? proj[(size_t)(r - j) * G.proj_dim + c]
                                              : tail[(size_t)((p - j) % tl) * qkv + c];
         acc += tp[j * dim + cc] * prev;
