@@ -358,17 +358,18 @@ __global__ void __launch_bounds__(PW * 32) layer_post_tc_kernel(Geo G, RowBatch 
     }
     // Conditioning logits: all PW x 8 partial sums of the warp at once (ranks
     // past rk and rows past the batch hold zeros).
-    float sums[PW * 8];
+    constexpr int NS = PW * 8 <= 16 ? 16 : 64;  // padded with zeros
+    float sums[NS];
 #pragma unroll
-    for (int i = 0; i < PW; ++i)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) sums[i * 8 + j] = acc[i][j];
-    warp_sum_many<PW * 8>(sums, lane);
-    if constexpr (PW * 8 == 64) {
-      S.part[w][lane >> 2][(2 * lane) & 7] = sums[0];
-      S.part[w][lane >> 2][((2 * lane) & 7) + 1] = sums[1];
+    for (int k = 0; k < NS; ++k) sums[k] = k < PW * 8 ? acc[k / 8 < PW ? k / 8 : 0][k % 8] : 0.f;
+    warp_sum_many<NS>(sums, lane);
+    if constexpr (NS == 64) {
+      if ((lane >> 2) < PW) {
+        S.part[w][lane >> 2][(2 * lane) & 7] = sums[0];
+        S.part[w][lane >> 2][((2 * lane) & 7) + 1] = sums[1];
+      }
     } else {
-      if ((lane & 1) == 0) S.part[w][lane >> 4][(lane >> 1) & 7] = sums[0];
+      if ((lane & 1) == 0 && (lane >> 4) < PW) S.part[w][lane >> 4][(lane >> 1) & 7] = sums[0];
     }
   }
   __syncthreads();
@@ -601,12 +602,17 @@ cudaError_t launch_layer_post_tc(const Geo& G, const RowBatch& rb, const LayerPa
   if (!lp.hfrag || G.lanes > 4 || G.cond_rank > 8 || G.cond_rank < 1 || G.ba != G.bb || G.hada_n < G.d)
     return cudaErrorInvalidValue;
   // 2-row CTAs between 128 and 2048 rows fill the SMs; below that a row's
-  // element phases run faster on 8 warps, above it 8-row CTAs already fill them.
+  // element phases run faster on 8 warps. From 2048 rows, 8- or 7-row CTAs
+  // (two resident per SM), whichever leaves the fewest rows on the busiest SM.
   const bool small = rb.M >= 128 && rb.M < 2048;
+  auto busiest = [&](int pw) { return ((rb.M + pw - 1) / pw + 2 * 148 - 1) / (2 * 148) * pw; };
+  const bool seven = !small && rb.M >= 2048 && busiest(7) < busiest(8);
   if (G.ba == 32) return small ? post_tc<32, 2>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st)
-                               : post_tc<32, 8>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
+                         : seven ? post_tc<32, 7>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st)
+                                 : post_tc<32, 8>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
   if (G.ba == 16) return small ? post_tc<16, 2>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st)
-                               : post_tc<16, 8>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
+                         : seven ? post_tc<16, 7>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st)
+                                 : post_tc<16, 8>(G, rb, lp, p1, p2, projo, u, bx, gates, lanes, st);
   return cudaErrorInvalidValue;
 }
 

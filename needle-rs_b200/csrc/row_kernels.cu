@@ -512,8 +512,8 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
 constexpr int PT_DQ = 8;   // d_model / 128 supported on this path
 constexpr int PT_S = 4;    // lane-group stages in flight
 
-// PT_M rows per CTA: 16 for large batches, 4 for small ones (four times the
-// CTAs, shorter per-CTA loops).
+// PT_M rows per CTA: 16 or 14 for large batches, 4 for small ones (four times
+// the CTAs, shorter per-CTA loops).
 template <int PT_M>
 __global__ void __launch_bounds__(256, 2)
 layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes, MhcParams mp,
@@ -764,8 +764,13 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
   const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
                         (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0 && mp.phi_dense &&
                         (reinterpret_cast<uintptr_t>(mp.phi_dense) & 15) == 0;
+  // From 2048 rows: 16- or 14-row tiles (two CTAs resident per SM), whichever
+  // leaves the fewest rows on the busiest SM.
+  auto busiest = [&](int pt) { return ((rb.M + pt - 1) / pt + 2 * 148 - 1) / (2 * 148) * pt; };
   if (tiled_ok && rb.M >= 2048)
-    return launch_pre_tiled<16>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
+    return busiest(14) < busiest(16)
+               ? launch_pre_tiled<14>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st)
+               : launch_pre_tiled<16>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
   if (tiled_ok && rb.M >= PRE_TILED_MIN_ROWS)
     return launch_pre_tiled<4>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;

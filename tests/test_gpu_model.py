@@ -140,6 +140,24 @@ def test_large_prefill_batch_matches_oracle(full_gpu, full_oracle, int8):
         assert rel_err(s.decode_step(int(t)), o.decode_step(int(t))) < tol(int8)
 
 
+def test_many_row_prefill_matches_oracle(full_gpu, full_oracle):
+    """A batched prefill of 2400 rows takes the large-batch tilings: 14-row
+    mHC pre-projection tiles and 7-row block-tail CTAs (the row counts that
+    balance two CTAs per SM at this size); every session's last logits, its
+    greedy pick and its next decode step match the oracle (f32 KV: the row
+    kernels do not depend on the KV precision, and f32 holds the tighter bar)."""
+    rng = np.random.default_rng(9)
+    prompts = [rng.integers(1, 8192, n).astype(np.uint32) for n in (700, 600, 650, 450)]
+    ss = [full_gpu.session(720, False) for _ in prompts]
+    lg, picks = full_gpu.prefill_batch(ss, prompts)
+    for p, s, a, t in zip(prompts, ss, lg, picks):
+        o = full_oracle.session(720, False)
+        b = o.prefill(p)
+        assert rel_err(a, b) < tol(False)
+        assert int(t) == int(np.argmax(b))
+        assert rel_err(s.decode_step(int(t)), o.decode_step(int(t))) < tol(False)
+
+
 def test_device_batch_graph_matches_eager(full_gpu, cuda):
     """The CUDA-graph replay of a batched decode step gives the same tokens and
     logits as the eager launch sequence (and both match single sessions)."""
