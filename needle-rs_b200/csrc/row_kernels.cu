@@ -1012,7 +1012,8 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp, cons
 
 // Large batches: one warp per row, QP_ROWS rows per CTA, each warp with its
 // own qkv_dim-float slice of shared memory.
-constexpr int QP_ROWS = 8;
+// Seven rows: 4096 rows make 586 CTAs, four resident on each of the 148 SMs.
+constexpr int QP_ROWS = 7;
 __global__ void __launch_bounds__(QP_ROWS * 32)
 qkv_post_rows_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
                      const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv, float* pks,
