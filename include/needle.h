@@ -50,9 +50,14 @@ NeedleV3Handle *needle_v3_load_bytes(const unsigned char *data, size_t len);
 
 /* needle.h:396 / v3.rs:153-164; needle.h:405 / v3.rs:176-187;
  * needle.h:411 / v3.rs:198-211; needle.h:417 / v3.rs:219-250;
- * needle.h:431 / v3.rs:259-281. Text-level calls: they need the container's
- * SentencePiece tokenizer record; when it is absent (as in synthetic
- * containers) they return NULL and set the last error. */
+ * needle.h:431 / v3.rs:259-281. Text-level calls (V3Engine::generate_with,
+ * v3_engine.rs:193-305): chat prompt, the container's SentencePiece tokenizer,
+ * greedy or temperature sampling on the GPU engine until </s> or <|im_end|>.
+ * run / run_json / run_stream use the defaults (256 new tokens, greedy, f32
+ * KV); run_json returns the trimmed <tool_call> payload, "" when there is
+ * none. When the container has no tokenizer record, and for generate with
+ * constrain = true (grammar-constrained decoding is not built), they return
+ * NULL and set the last error. */
 char *needle_v3_run(NeedleV3Handle *handle, const char *query, const char *tools_json);
 char *needle_v3_run_json(NeedleV3Handle *handle, const char *query, const char *tools_json);
 char *needle_v3_reasoning(NeedleV3Handle *handle, const char *text);
@@ -160,6 +165,16 @@ bool needle_v3_batch_get_next(NeedleV3Batch *batch, uint32_t *next);
  * layer_post, final norm, LM head, bookkeeping — and this library's kernel
  * launch count for the step to *launches. Synchronous. */
 bool needle_v3_batch_profile(NeedleV3Batch *batch, float *ms, int *launches);
+
+/* The container tokenizer on its own, from a RAW tokenizer blob
+ * (sp_tokenizer.rs:116-414); host only, needs no GPU. encode writes
+ * min(count, cap) ids and returns the count ((size_t)-1 on error); decode
+ * returns a string to free with needle_free_str. */
+typedef struct NeedleTokenizer NeedleTokenizer;
+NeedleTokenizer *needle_tokenizer_new(const unsigned char *blob, size_t len);
+void needle_tokenizer_free(NeedleTokenizer *tokenizer);
+size_t needle_tokenizer_encode(NeedleTokenizer *tokenizer, const char *text, uint32_t *out, size_t cap);
+char *needle_tokenizer_decode(NeedleTokenizer *tokenizer, const uint32_t *ids, size_t n);
 
 /* Geometry: vocab, out_vocab, d_model, heads, kv_heads, layers, qk, v_head,
  * max_seq, hada_n, lanes, window, conv_taps, logit_rows (14 int64). */

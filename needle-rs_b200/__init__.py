@@ -31,6 +31,53 @@ class NeedleError(RuntimeError):
     pass
 
 
+STREAM_CB = C.CFUNCTYPE(None, C.c_char_p, C.c_void_p)
+
+
+def _take_str(p) -> str | None:
+    """A char* the library allocated, as text (freed); None for NULL."""
+    if not p:
+        return None
+    try:
+        return C.string_at(p).decode("utf-8")
+    finally:
+        lib().needle_free_str(p)
+
+
+class Tokenizer:
+    """The container's SentencePiece tokenizer from its RAW blob
+    (SpTokenizer, sp_tokenizer.rs:116-414); host only."""
+
+    def __init__(self, blob: bytes):
+        self._t = lib().needle_tokenizer_new(blob, len(blob))
+        if not self._t:
+            _fail("needle_tokenizer_new")
+
+    def encode(self, text: str) -> list[int]:
+        raw = text.encode("utf-8")
+        n = lib().needle_tokenizer_encode(self._t, raw, None, 0)
+        if n == C.c_size_t(-1).value:
+            _fail("needle_tokenizer_encode")
+        out = np.zeros(max(n, 1), np.uint32)
+        lib().needle_tokenizer_encode(self._t, raw, out.ctypes.data, n)
+        return [int(x) for x in out[:n]]
+
+    def decode(self, ids) -> str:
+        a = np.ascontiguousarray(ids, np.uint32)
+        r = _take_str(lib().needle_tokenizer_decode(self._t, a.ctypes.data, len(a)))
+        if r is None:
+            _fail("needle_tokenizer_decode")
+        return r
+
+    def __del__(self):
+        try:
+            if self._t:
+                lib().needle_tokenizer_free(self._t)
+                self._t = None
+        except Exception:
+            pass
+
+
 def lib() -> C.CDLL:
     """Load (once) and declare the C ABI."""
     global _lib
@@ -50,6 +97,11 @@ def lib() -> C.CDLL:
         "needle_v3_run_json": (vp, [vp, C.c_char_p, C.c_char_p]),
         "needle_v3_reasoning": (vp, [vp, C.c_char_p]),
         "needle_v3_generate": (vp, [vp, C.c_char_p, C.c_char_p, sz, C.c_float, C.c_uint64, b, b]),
+        "needle_v3_run_stream": (vp, [vp, C.c_char_p, C.c_char_p, STREAM_CB, vp]),
+        "needle_tokenizer_new": (vp, [C.c_char_p, sz]),
+        "needle_tokenizer_free": (None, [vp]),
+        "needle_tokenizer_encode": (sz, [vp, C.c_char_p, vp, sz]),
+        "needle_tokenizer_decode": (vp, [vp, vp, sz]),
         "needle_v3_has_confidence": (b, [vp]),
         "needle_v3_confidence_for": (b, [vp, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_float)]),
         "needle_v3_kv_bytes": (sz, [vp, sz, b]),
@@ -172,6 +224,33 @@ class V3Engine:
 
     def num_layers(self) -> int:
         return lib().needle_v3_num_layers(self._h)
+
+    # ---- text level (V3Engine::run / run_json / generate / generate_with)
+    def _text(self, p, what):
+        r = _take_str(p)
+        if r is None:
+            _fail(what)
+        return r
+
+    def run(self, query: str, tools_json: str) -> str:
+        return self._text(lib().needle_v3_run(self._h, query.encode(), tools_json.encode()), "needle_v3_run")
+
+    def run_json(self, query: str, tools_json: str) -> str:
+        return self._text(lib().needle_v3_run_json(self._h, query.encode(), tools_json.encode()),
+                          "needle_v3_run_json")
+
+    def generate(self, query: str, tools_json: str, max_new_tokens: int = 0, temperature: float = 0.0,
+                 seed: int = 0, constrain: bool = False, kv_int8: bool = False) -> str:
+        return self._text(lib().needle_v3_generate(self._h, query.encode(), tools_json.encode(), max_new_tokens,
+                                                   temperature, seed, constrain, kv_int8), "needle_v3_generate")
+
+    def run_stream(self, query: str, tools_json: str, on_piece) -> str:
+        cb = STREAM_CB(lambda piece, _ud: on_piece(piece.decode("utf-8")))
+        return self._text(lib().needle_v3_run_stream(self._h, query.encode(), tools_json.encode(), cb, None),
+                          "needle_v3_run_stream")
+
+    def reasoning(self, text: str) -> str | None:
+        return _take_str(lib().needle_v3_reasoning(self._h, text.encode()))
 
     def session(self, hint: int = 1, kv_int8: bool = False) -> "Session":
         s = lib().needle_v3_session_new(self._h, hint, kv_int8)

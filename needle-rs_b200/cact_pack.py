@@ -284,7 +284,7 @@ class _Writer:
 
 
 def build_container(geom: Geometry | None = None, seed: int = 0,
-                    codebook: np.ndarray | None = None) -> bytes:
+                    codebook: np.ndarray | None = None, tokenizer: bytes | None = None) -> bytes:
     """A random-init Needle 3 container with `geom`'s geometry.
 
     Init profile (seeded, documented so parity runs are reproducible): CQ
@@ -357,6 +357,8 @@ def build_container(geom: Geometry | None = None, seed: int = 0,
         cqw(d, d, g.default_bits, 0.05)  # value_proj
         w.fp16(rng.normal(0, 0.5, (g.engram_conv_taps, d)))  # taps
     w.fp16(rng.normal(0, 0.02, d))  # final_norm
+    if tokenizer is not None:  # the RAW tokenizer record, last as in the shipped container
+        w.recs.append((DT_RAW, (), bytes(tokenizer), 0, 0))
     return w.build(g.header_words(len(w.recs)), g.rope_theta, cb)
 
 

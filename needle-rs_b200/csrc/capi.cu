@@ -75,10 +75,94 @@ char* out_string(const std::string& s) {
   return p;
 }
 
-const char* kNoText =
-    "text-level generation needs the container's SentencePiece tokenizer and prompt layer, "
-    "which this GPU build does not implement; use the token-level API "
+const char* kNoTokenizer =
+    "the container has no tokenizer record, so text-level calls cannot run; use the token-level API "
     "(needle_v3_prefill / needle_v3_decode_step / needle_v3_generate_ids)";
+
+// Defaults of V3Options (v3_engine.rs:26, :65-76) and the ids upstream fixes
+// for the stop and start tokens (v3_engine.rs:175-178).
+constexpr size_t kDefaultMaxNewTokens = 256;
+constexpr uint32_t kEosId = 1, kBosId = 2;
+
+bool utf8_ok(const char* s) {
+  if (!s) return false;
+  const std::string t(s);
+  return nb::utf8_lossy(t) == t;
+}
+
+// compact_json (prompt.rs): whitespace outside JSON strings removed.
+std::string compact_json(const std::string& s) {
+  std::string out;
+  bool in_str = false, esc = false;
+  for (char c : s) {
+    if (in_str) {
+      out += c;
+      if (esc) esc = false;
+      else if (c == '\\') esc = true;
+      else if (c == '"') in_str = false;
+      continue;
+    }
+    if (c == '"') {
+      in_str = true;
+      out += c;
+    } else if (c != ' ' && c != '\t' && c != '\n' && c != '\r') {
+      out += c;
+    }
+  }
+  return out;
+}
+
+// build_prompt (prompt.rs), no system turn: the user turn carries the compact
+// tool list between <tools> markers, then the assistant turn is opened.
+std::string build_prompt(const std::string& query, const std::string& tools_json) {
+  return "<|im_start|>user\n<tools>" + compact_json(tools_json) + "</tools>\n" + query +
+         "<|im_end|>\n<|im_start|>assistant\n";
+}
+
+// The text between `open` and `close` (to the end when unterminated), or
+// false when `open` is absent (v3_engine.rs:392-401).
+bool between(const std::string& text, const char* open, const char* close, std::string* out) {
+  size_t a = text.find(open);
+  if (a == std::string::npos) return false;
+  a += std::strlen(open);
+  const size_t b = text.find(close, a);
+  *out = text.substr(a, b == std::string::npos ? std::string::npos : b - a);
+  return true;
+}
+
+// Unicode White_Space (what Rust's str::trim removes).
+bool unicode_ws(uint32_t c) {
+  return (c >= 0x09 && c <= 0x0D) || c == 0x20 || c == 0x85 || c == 0xA0 || c == 0x1680 ||
+         (c >= 0x2000 && c <= 0x200A) || c == 0x2028 || c == 0x2029 || c == 0x202F || c == 0x205F ||
+         c == 0x3000;
+}
+
+// Code point of the well-formed UTF-8 sequence of `n` bytes at p.
+uint32_t code_point(const char* p, size_t n) {
+  const unsigned char* u = reinterpret_cast<const unsigned char*>(p);
+  if (n == 1) return u[0];
+  uint32_t c = u[0] & (0xFF >> (n + 1));
+  for (size_t k = 1; k < n; ++k) c = (c << 6) | (u[k] & 0x3F);
+  return c;
+}
+
+// Leading and trailing Unicode white space removed from UTF-8 text.
+std::string trim(const std::string& s) {
+  auto seq_len = [](unsigned char b) -> size_t { return b < 0x80 ? 1 : b < 0xE0 ? 2 : b < 0xF0 ? 3 : 4; };
+  size_t i = 0, j = s.size();
+  while (i < j) {
+    const size_t n = std::min(seq_len((unsigned char)s[i]), j - i);
+    if (!unicode_ws(code_point(s.data() + i, n))) break;
+    i += n;
+  }
+  while (j > i) {
+    size_t k = j - 1;
+    while (k > i && ((unsigned char)s[k] & 0xC0) == 0x80) --k;
+    if (!unicode_ws(code_point(s.data() + k, j - k))) break;
+    j = k;
+  }
+  return s.substr(i, j - i);
+}
 
 int nd_status(cudaError_t e) {
   if (e == cudaSuccess) return 0;
@@ -163,6 +247,95 @@ uint32_t sample(const float* logits, size_t n, float temperature, SplitMix64* rn
   }
   return (uint32_t)(n - 1);
 }
+
+struct TextOptions {
+  size_t max_new_tokens = kDefaultMaxNewTokens;
+  float temperature = 0.f;
+  uint64_t seed = 0;
+  bool kv_int8 = false;
+};
+
+// V3Engine::generate_with (v3_engine.rs:193-305) without the grammar: the chat
+// prompt as [bos] + encode(prompt), truncated to the context; one batched
+// prefill, then greedy or temperature sampling until </s>, <|im_end|>, the
+// token budget or the end of the context. Every step's newly decoded text goes
+// to `cb` (the whole run is re-decoded so byte-fallback characters split over
+// several tokens arrive whole). False with *err set on failure.
+bool generate_text(nb::Engine* E, const std::string& query, const std::string& tools, const TextOptions& o,
+                   void (*cb)(const char*, void*), void* ud, std::string* text, std::string* err) {
+  if (!E->tok) {
+    *err = kNoTokenizer;
+    return false;
+  }
+  const nb::Tokenizer& T = *E->tok;
+  uint32_t im_end = UINT32_MAX;
+  T.id_of("<|im_end|>", &im_end);
+  std::vector<uint32_t> ids = {kBosId};
+  const std::vector<uint32_t> enc = T.encode(build_prompt(query, tools));
+  ids.insert(ids.end(), enc.begin(), enc.end());
+  const size_t max = E->cfg.max_seq;
+  if (ids.size() > max) ids.resize(max);
+  const size_t budget = std::min(max - ids.size(), o.max_new_tokens);
+  std::vector<uint32_t> out;
+  text->clear();
+  if (budget == 0) return true;
+  std::unique_ptr<nb::Session> s(E->new_session(ids.size() + budget, o.kv_int8, err));
+  if (!s) return false;
+  const size_t rows = E->cfg.logit_rows();
+  std::vector<float> logits(rows);
+  float* lp = o.temperature > 0.f ? logits.data() : nullptr;
+  nb::Session* sp = s.get();
+  const uint32_t* idp[1] = {ids.data()};
+  size_t lens[1] = {ids.size()};
+  uint32_t pick = 0;
+  if (!E->prefill(&sp, idp, lens, 1, lp, &pick, err)) return false;
+  SplitMix64 rng{o.seed};
+  std::string emitted;
+  for (size_t t = 0; t < budget; ++t) {
+    const uint32_t next = lp ? sample(logits.data(), rows, o.temperature, &rng) : pick;
+    if (next == kEosId || next == im_end) break;
+    out.push_back(next);
+    const std::string full = T.decode(out.data(), out.size());
+    if (full.size() > emitted.size()) {
+      const std::string delta = full.substr(emitted.size());
+      if (cb && delta.find('\0') == std::string::npos) cb(delta.c_str(), ud);
+      emitted = full;
+    }
+    if (sp->pos >= max) break;
+    if (!E->decode(&sp, &next, 1, lp, &pick, err)) return false;
+  }
+  *text = T.decode(out.data(), out.size());
+  return true;
+}
+
+// Shared argument checks of the text calls (v3.rs:131-150): NULL or
+// non-UTF-8 strings fail with the reference's messages.
+bool text_args(NeedleV3Handle* h, const char* query, const char* tools_json) {
+  if (!h) {
+    set_err("handle was null");
+    return false;
+  }
+  if (!utf8_ok(query)) {
+    set_err("query was null or not UTF-8");
+    return false;
+  }
+  if (!utf8_ok(tools_json)) {
+    set_err("tools_json was null or not UTF-8");
+    return false;
+  }
+  return true;
+}
+
+char* text_call(NeedleV3Handle* h, const char* query, const char* tools_json, const TextOptions& o,
+                void (*cb)(const char*, void*), void* ud) {
+  if (!text_args(h, query, tools_json)) return nullptr;
+  std::string text, err;
+  if (!generate_text(h->eng.get(), query, tools_json, o, cb, ud, &text, &err)) {
+    set_err(err);
+    return nullptr;
+  }
+  return out_string(text);
+}
 }  // namespace
 
 extern "C" {
@@ -236,14 +409,20 @@ size_t needle_v3_num_layers(NeedleV3Handle* h) {
 
 char* needle_v3_run(NeedleV3Handle* h, const char* query, const char* tools_json) {
   clear_err();
-  if (!h) set_err("handle was null");
-  else if (!query || !tools_json) set_err("query or tools_json was null");
-  else set_err(kNoText);
-  return nullptr;
+  return text_call(h, query, tools_json, TextOptions(), nullptr, nullptr);
 }
 
+// The <tool_call> payload of run(), trimmed; an empty string when the model
+// emitted no call (v3.rs:171-181 returns unwrap_or_default()).
 char* needle_v3_run_json(NeedleV3Handle* h, const char* query, const char* tools_json) {
-  return needle_v3_run(h, query, tools_json);
+  clear_err();
+  if (!text_args(h, query, tools_json)) return nullptr;
+  std::string text, err, call;
+  if (!generate_text(h->eng.get(), query, tools_json, TextOptions(), nullptr, nullptr, &text, &err)) {
+    set_err(err);
+    return nullptr;
+  }
+  return out_string(between(text, "<tool_call>", "</tool_call>", &call) ? trim(call) : std::string());
 }
 
 // V3Engine::reasoning (v3_engine.rs:382-401): the text between <think> and
@@ -254,37 +433,35 @@ char* needle_v3_reasoning(NeedleV3Handle* h, const char* text) {
     set_err("handle was null");
     return nullptr;
   }
-  if (!text) {
+  if (!utf8_ok(text)) {
     set_err("text was null or not UTF-8");
     return nullptr;
   }
-  std::string s(text);
-  size_t a = s.find("<think>");
-  if (a == std::string::npos) return nullptr;
-  a += 7;
-  size_t b = s.find("</think>", a);
-  std::string mid = s.substr(a, b == std::string::npos ? std::string::npos : b - a);
-  const char* ws = " \t\n\r\f\v";
-  size_t i = mid.find_first_not_of(ws), j = mid.find_last_not_of(ws);
-  return out_string(i == std::string::npos ? std::string() : mid.substr(i, j - i + 1));
+  std::string mid;
+  if (!between(text, "<think>", "</think>", &mid)) return nullptr;
+  return out_string(trim(mid));
 }
 
 char* needle_v3_generate(NeedleV3Handle* h, const char* query, const char* tools_json,
                          size_t max_new_tokens, float temperature, uint64_t seed, bool constrain,
                          bool kv_int8) {
-  (void)max_new_tokens;
-  (void)temperature;
-  (void)seed;
-  (void)constrain;
-  (void)kv_int8;
-  return needle_v3_run(h, query, tools_json);
+  clear_err();
+  if (constrain) {
+    set_err("grammar-constrained decoding is not part of this build; pass constrain = false");
+    return nullptr;
+  }
+  TextOptions o;
+  o.max_new_tokens = max_new_tokens == 0 ? kDefaultMaxNewTokens : max_new_tokens;
+  o.temperature = temperature;
+  o.seed = seed;
+  o.kv_int8 = kv_int8;
+  return text_call(h, query, tools_json, o, nullptr, nullptr);
 }
 
 char* needle_v3_run_stream(NeedleV3Handle* h, const char* query, const char* tools_json,
                            void (*cb)(const char*, void*), void* userdata) {
-  (void)cb;
-  (void)userdata;
-  return needle_v3_run(h, query, tools_json);
+  clear_err();
+  return text_call(h, query, tools_json, TextOptions(), cb, userdata);
 }
 
 bool needle_v3_has_confidence(NeedleV3Handle* h) {
@@ -640,6 +817,58 @@ bool needle_v3_batch_get_next(NeedleV3Batch* b, uint32_t* next) {
     return false;
   }
   return batch_copy(b, next, b->b->d_next, cudaMemcpyDeviceToHost);
+}
+
+struct NeedleTokenizer {
+  std::unique_ptr<nb::Tokenizer> t;
+};
+
+NeedleTokenizer* needle_tokenizer_new(const unsigned char* blob, size_t len) {
+  clear_err();
+  if (!blob) {
+    set_err("blob was null");
+    return nullptr;
+  }
+  std::string err;
+  nb::Tokenizer* t = nb::Tokenizer::from_blob(blob, len, &err);
+  if (!t) {
+    set_err(err);
+    return nullptr;
+  }
+  NeedleTokenizer* r = new NeedleTokenizer();
+  r->t.reset(t);
+  return r;
+}
+
+void needle_tokenizer_free(NeedleTokenizer* t) { delete t; }
+
+size_t needle_tokenizer_encode(NeedleTokenizer* t, const char* text, uint32_t* out, size_t cap) {
+  clear_err();
+  if (!t) {
+    set_err("tokenizer was null");
+    return (size_t)-1;
+  }
+  if (!utf8_ok(text)) {
+    set_err("text was null or not UTF-8");
+    return (size_t)-1;
+  }
+  const std::vector<uint32_t> ids = t->t->encode(text);
+  if (out)
+    for (size_t i = 0; i < ids.size() && i < cap; ++i) out[i] = ids[i];
+  return ids.size();
+}
+
+char* needle_tokenizer_decode(NeedleTokenizer* t, const uint32_t* ids, size_t n) {
+  clear_err();
+  if (!t) {
+    set_err("tokenizer was null");
+    return nullptr;
+  }
+  if (!ids && n) {
+    set_err("ids was null");
+    return nullptr;
+  }
+  return out_string(t->t->decode(ids, n));
 }
 
 bool needle_v3_geometry(NeedleV3Handle* h, int64_t* out) {

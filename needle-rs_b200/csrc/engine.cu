@@ -331,6 +331,19 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     L.recs.push_back(r);
   }
   std::unique_ptr<Engine> E(new Engine());
+  // The tokenizer travels as the container's RAW record (cact.rs:1068-1075).
+  // A malformed one fails the load; a container without one still serves the
+  // token-level API.
+  for (size_t i = 0; i < nt; ++i)
+    if (L.recs[i].dtype == 4) {
+      std::string terr;
+      E->tok.reset(Tokenizer::from_blob(raw + L.recs[i].offset, L.recs[i].nbytes, &terr));
+      if (!E->tok) {
+        *err = "bad tokenizer record: " + terr;
+        return nullptr;
+      }
+      break;
+    }
   HostConfig& c = E->cfg;
   c.num_tensors = nt;
   c.kv_window = w[3];

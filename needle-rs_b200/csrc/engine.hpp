@@ -10,6 +10,7 @@
 #include <vector>
 
 #include "kernels.hpp"
+#include "tokenizer.hpp"
 
 namespace nb {
 
@@ -148,7 +149,9 @@ class Engine {
   uint32_t* d_perm = nullptr;
   float* d_rope = nullptr;
   uint32_t* d_hfrag = nullptr;  // HadamardMLP weight fragments, all layers
-  float* d_phid = nullptr;      // mHC lane-matrix rows, dequantised and rotated, all container layers
+  float* d_phid = nullptr;
+  // The container's tokenizer (its RAW record); null when the container has none.
+  std::unique_ptr<Tokenizer> tok;      // mHC lane-matrix rows, dequantised and rotated, all container layers
   CqMat emb{}, phi_pre{}, phi_post{}, phi_res{};
   std::vector<CqMat> qkvg, outp, eng_kv, eng_tables;
   CqMat* d_tables = nullptr;

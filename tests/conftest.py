@@ -87,5 +87,33 @@ def full_gpu(cuda, full_raw):
     return nb.V3Engine.from_bytes(full_raw)
 
 
+@pytest.fixture(scope="session")
+def sp_fixture():
+    """A SentencePiece BPE model trained with the `sentencepiece` package, as a
+    RAW tokenizer blob plus that library's ids for a set of texts
+    (tests/golden/make_tokenizer_golden.py)."""
+    import base64
+    import json
+    d = json.load(open(os.path.join(GOLDEN, "sp_bpe_tokenizer.json")))
+    d["blob"] = base64.b64decode(d["blob_b64"])
+    return d
+
+
+@pytest.fixture(scope="session")
+def text_raw(sp_fixture):
+    """The shipped-geometry container of full_raw with the fixture's tokenizer
+    appended as its RAW record, cached on disk like the others."""
+    os.makedirs(CACHE, exist_ok=True)
+    path = os.path.join(CACHE, f"shipped_tok_0_{sha256(sp_fixture['blob'])[:12]}.cact")
+    if os.path.exists(path):
+        return open(path, "rb").read()
+    raw = cact_pack.build_container(cact_pack.shipped(), seed=0, tokenizer=sp_fixture["blob"])
+    tmp = path + f".{os.getpid()}"
+    with open(tmp, "wb") as f:
+        f.write(raw)
+    os.replace(tmp, path)
+    return raw
+
+
 def sha256(b: bytes) -> str:
     return hashlib.sha256(b).hexdigest()
