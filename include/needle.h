@@ -55,9 +55,10 @@ NeedleV3Handle *needle_v3_load_bytes(const unsigned char *data, size_t len);
  * greedy or temperature sampling on the GPU engine until </s> or <|im_end|>.
  * run / run_json / run_stream use the defaults (256 new tokens, greedy, f32
  * KV); run_json returns the trimmed <tool_call> payload, "" when there is
- * none. When the container has no tokenizer record, and for generate with
- * constrain = true (grammar-constrained decoding is not built), they return
- * NULL and set the last error. */
+ * none. generate with constrain = true masks the logits inside <tool_call>
+ * spans to the declared tool names and argument keys (constrained.rs). When
+ * the container has no tokenizer record they return NULL and set the last
+ * error. */
 char *needle_v3_run(NeedleV3Handle *handle, const char *query, const char *tools_json);
 char *needle_v3_run_json(NeedleV3Handle *handle, const char *query, const char *tools_json);
 char *needle_v3_reasoning(NeedleV3Handle *handle, const char *text);
@@ -175,6 +176,13 @@ NeedleTokenizer *needle_tokenizer_new(const unsigned char *blob, size_t len);
 void needle_tokenizer_free(NeedleTokenizer *tokenizer);
 size_t needle_tokenizer_encode(NeedleTokenizer *tokenizer, const char *text, uint32_t *out, size_t cap);
 char *needle_tokenizer_decode(NeedleTokenizer *tokenizer, const uint32_t *ids, size_t n);
+/* The grammar mask (0 or -1e9 per id, `vocab` entries) that constrained
+ * decoding adds after the tool-call bytes out_bytes[0..n) have been written,
+ * for the tools declared in tools_json (ConstrainedDecoder::logit_mask,
+ * constrained.rs:431-461; unique_keys as with_unique_arg_keys). */
+bool needle_tokenizer_tool_mask(NeedleTokenizer *tokenizer, const char *tools_json,
+                                const unsigned char *out_bytes, size_t n, bool unique_keys,
+                                float *mask, size_t vocab);
 
 /* Geometry: vocab, out_vocab, d_model, heads, kv_heads, layers, qk, v_head,
  * max_seq, hada_n, lanes, window, conv_taps, logit_rows (14 int64). */

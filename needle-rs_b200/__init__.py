@@ -69,6 +69,14 @@ class Tokenizer:
             _fail("needle_tokenizer_decode")
         return r
 
+    def tool_mask(self, tools_json: str, written: bytes, vocab: int, unique_keys: bool = True) -> np.ndarray:
+        """The grammar mask after the tool-call bytes `written` (constrained.rs:431-461)."""
+        out = np.zeros(vocab, np.float32)
+        if not lib().needle_tokenizer_tool_mask(self._t, tools_json.encode(), written, len(written), unique_keys,
+                                                out.ctypes.data, vocab):
+            _fail("needle_tokenizer_tool_mask")
+        return out
+
     def __del__(self):
         try:
             if self._t:
@@ -102,6 +110,7 @@ def lib() -> C.CDLL:
         "needle_tokenizer_free": (None, [vp]),
         "needle_tokenizer_encode": (sz, [vp, C.c_char_p, vp, sz]),
         "needle_tokenizer_decode": (vp, [vp, vp, sz]),
+        "needle_tokenizer_tool_mask": (b, [vp, C.c_char_p, C.c_char_p, sz, b, vp, sz]),
         "needle_v3_has_confidence": (b, [vp]),
         "needle_v3_confidence_for": (b, [vp, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_float)]),
         "needle_v3_kv_bytes": (sz, [vp, sz, b]),

@@ -14,6 +14,7 @@
 #include <vector>
 
 #include "../../include/needle.h"
+#include "constrained.hpp"
 #include "engine.hpp"
 
 struct NeedleV3Handle {
@@ -253,14 +254,29 @@ struct TextOptions {
   float temperature = 0.f;
   uint64_t seed = 0;
   bool kv_int8 = false;
+  bool constrain = false;
 };
 
-// V3Engine::generate_with (v3_engine.rs:193-305) without the grammar: the chat
-// prompt as [bos] + encode(prompt), truncated to the context; one batched
-// prefill, then greedy or temperature sampling until </s>, <|im_end|>, the
-// token budget or the end of the context. Every step's newly decoded text goes
-// to `cb` (the whole run is re-decoded so byte-fallback characters split over
-// several tokens arrive whole). False with *err set on failure.
+// First maximum, as argmax (v3_engine.rs:410-420).
+uint32_t host_argmax(const float* v, size_t n) {
+  size_t best = 0;
+  float top = -INFINITY;
+  for (size_t i = 0; i < n; ++i)
+    if (v[i] > top) {
+      top = v[i];
+      best = i;
+    }
+  return (uint32_t)best;
+}
+
+// V3Engine::generate_with (v3_engine.rs:193-305): the chat prompt as [bos] +
+// encode(prompt), truncated to the context; one batched prefill, then greedy
+// or temperature sampling until </s>, <|im_end|>, the token budget or the end
+// of the context. With `constrain` and at least one declared tool, the logits
+// inside a <tool_call> span get the grammar mask first. Every step's newly
+// decoded text goes to `cb` (the whole run is re-decoded so byte-fallback
+// characters split over several tokens arrive whole). False with *err set on
+// failure.
 bool generate_text(nb::Engine* E, const std::string& query, const std::string& tools, const TextOptions& o,
                    void (*cb)(const char*, void*), void* ud, std::string* text, std::string* err) {
   if (!E->tok) {
@@ -282,8 +298,16 @@ bool generate_text(nb::Engine* E, const std::string& query, const std::string& t
   std::unique_ptr<nb::Session> s(E->new_session(ids.size() + budget, o.kv_int8, err));
   if (!s) return false;
   const size_t rows = E->cfg.logit_rows();
+  std::unique_ptr<nb::ConstrainedDecoder> grammar;
+  if (o.constrain) {
+    const std::vector<nb::ToolDef> defs = nb::parse_tools_json(tools);
+    if (!defs.empty()) grammar.reset(new nb::ConstrainedDecoder(defs, T.token_bytes(), true));
+  }
+  uint32_t tc_start = 0, tc_end = 0;
+  const bool has_start = T.id_of("<tool_call>", &tc_start), has_end = T.id_of("</tool_call>", &tc_end);
+  bool in_call = false;
   std::vector<float> logits(rows);
-  float* lp = o.temperature > 0.f ? logits.data() : nullptr;
+  float* lp = o.temperature > 0.f || grammar ? logits.data() : nullptr;
   nb::Session* sp = s.get();
   const uint32_t* idp[1] = {ids.data()};
   size_t lens[1] = {ids.size()};
@@ -292,9 +316,20 @@ bool generate_text(nb::Engine* E, const std::string& query, const std::string& t
   SplitMix64 rng{o.seed};
   std::string emitted;
   for (size_t t = 0; t < budget; ++t) {
-    const uint32_t next = lp ? sample(logits.data(), rows, o.temperature, &rng) : pick;
+    if (in_call && grammar) {
+      const std::vector<float> mask = grammar->logit_mask(rows);
+      for (size_t i = 0; i < rows; ++i) logits[i] += mask[i];
+    }
+    const uint32_t next = o.temperature > 0.f ? sample(logits.data(), rows, o.temperature, &rng)
+                          : lp                ? host_argmax(logits.data(), rows)
+                                              : pick;
     if (next == kEosId || next == im_end) break;
     out.push_back(next);
+    if (grammar) {
+      if (has_start && next == tc_start) in_call = true;
+      else if (has_end && next == tc_end) in_call = false;
+      else if (in_call) grammar->update(next);
+    }
     const std::string full = T.decode(out.data(), out.size());
     if (full.size() > emitted.size()) {
       const std::string delta = full.substr(emitted.size());
@@ -446,11 +481,8 @@ char* needle_v3_generate(NeedleV3Handle* h, const char* query, const char* tools
                          size_t max_new_tokens, float temperature, uint64_t seed, bool constrain,
                          bool kv_int8) {
   clear_err();
-  if (constrain) {
-    set_err("grammar-constrained decoding is not part of this build; pass constrain = false");
-    return nullptr;
-  }
   TextOptions o;
+  o.constrain = constrain;
   o.max_new_tokens = max_new_tokens == 0 ? kDefaultMaxNewTokens : max_new_tokens;
   o.temperature = temperature;
   o.seed = seed;
@@ -869,6 +901,24 @@ char* needle_tokenizer_decode(NeedleTokenizer* t, const uint32_t* ids, size_t n)
     return nullptr;
   }
   return out_string(t->t->decode(ids, n));
+}
+
+bool needle_tokenizer_tool_mask(NeedleTokenizer* t, const char* tools_json, const unsigned char* out_bytes,
+                                size_t n, bool unique_keys, float* mask, size_t vocab) {
+  clear_err();
+  if (!t || !mask || (!out_bytes && n)) {
+    set_err("tokenizer, out_bytes or mask was null");
+    return false;
+  }
+  if (!utf8_ok(tools_json)) {
+    set_err("tools_json was null or not UTF-8");
+    return false;
+  }
+  nb::ConstrainedDecoder g(nb::parse_tools_json(tools_json), t->t->token_bytes(), unique_keys);
+  g.feed_bytes(std::string(reinterpret_cast<const char*>(out_bytes), n));
+  const std::vector<float> m = g.logit_mask(vocab);
+  std::copy(m.begin(), m.end(), mask);
+  return true;
 }
 
 bool needle_v3_geometry(NeedleV3Handle* h, int64_t* out) {

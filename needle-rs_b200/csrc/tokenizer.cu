@@ -283,4 +283,26 @@ std::string Tokenizer::decode(const uint32_t* ids, size_t n) const {
   return out;
 }
 
+std::vector<std::string> Tokenizer::token_bytes() const {
+  std::vector<std::string> out(pieces_.size());
+  for (size_t id = 0; id < pieces_.size(); ++id) {
+    const uint8_t ty = types_[id];
+    if (ty == BYTE) {
+      int b;
+      if (byte_of(pieces_[id], &b)) out[id] = std::string(1, (char)b);
+    } else if (ty != CONTROL && ty != UNKNOWN) {
+      const std::string& p = pieces_[id];
+      for (size_t i = 0; i < p.size();) {
+        if (p.compare(i, 3, kMetaSpace) == 0) {
+          out[id] += ' ';
+          i += 3;
+        } else {
+          out[id] += p[i++];
+        }
+      }
+    }
+  }
+  return out;
+}
+
 }  // namespace nb

@@ -28,6 +28,10 @@ class Tokenizer {
   // Exact surface -> id; false when absent.
   bool id_of(const std::string& surface, uint32_t* id) const;
   size_t size() const { return pieces_.size(); }
+  // Bytes each token contributes to decoded output, by id: a byte piece its
+  // byte, control and unknown pieces nothing, others their surface with the
+  // meta space as a space (sp_tokenizer.rs:370-388).
+  std::vector<std::string> token_bytes() const;
 
   uint32_t pad_id = 0, eos_id = 0, bos_id = 0, unk_id = 0;
   bool add_dummy_prefix = false, byte_fallback = false;
