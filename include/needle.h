@@ -71,8 +71,11 @@ char *needle_v3_run_stream(NeedleV3Handle *handle, const char *query, const char
 /* needle.h:438 / v3.rs:287-291. */
 bool needle_v3_has_confidence(NeedleV3Handle *handle);
 
-/* needle.h:452 / v3.rs:307-334. The probe head is not run by this build:
- * returns false with the last error set. */
+/* needle.h:452 / v3.rs:307-334. The confidence head over the chat prompt
+ * plus `completion` (v3_engine.rs:351-368): a prefill on the GPU engine that
+ * captures the per-layer cells, the head's two poolings and projection on the
+ * GPU, the sigmoid of its logit in *out. False with the last error set when
+ * the container exports no confidence head (or no tokenizer). */
 bool needle_v3_confidence_for(NeedleV3Handle *handle, const char *query, const char *tools_json,
                               const char *completion, float *out);
 

@@ -112,7 +112,7 @@ def lib() -> C.CDLL:
         "needle_tokenizer_decode": (vp, [vp, vp, sz]),
         "needle_tokenizer_tool_mask": (b, [vp, C.c_char_p, C.c_char_p, sz, b, vp, sz]),
         "needle_v3_has_confidence": (b, [vp]),
-        "needle_v3_confidence_for": (b, [vp, C.c_char_p, C.c_char_p, C.c_char_p, C.POINTER(C.c_float)]),
+        "needle_v3_confidence_for": (b, [vp, C.c_char_p, C.c_char_p, C.c_char_p, vp]),
         "needle_v3_kv_bytes": (sz, [vp, sz, b]),
         "needle_v3_max_seq_len": (sz, [vp]),
         "needle_v3_free": (None, [vp]),
@@ -257,6 +257,17 @@ class V3Engine:
         cb = STREAM_CB(lambda piece, _ud: on_piece(piece.decode("utf-8")))
         return self._text(lib().needle_v3_run_stream(self._h, query.encode(), tools_json.encode(), cb, None),
                           "needle_v3_run_stream")
+
+    def has_confidence(self) -> bool:
+        return bool(lib().needle_v3_has_confidence(self._h))
+
+    def confidence_for(self, query: str, tools_json: str, completion: str) -> float:
+        """Probability from the confidence head (V3Engine::confidence_for, v3_engine.rs:351-368)."""
+        out = np.zeros(1, np.float32)
+        if not lib().needle_v3_confidence_for(self._h, query.encode(), tools_json.encode(), completion.encode(),
+                                              out.ctypes.data):
+            _fail("needle_v3_confidence_for")
+        return float(out[0])
 
     def reasoning(self, text: str) -> str | None:
         return _take_str(lib().needle_v3_reasoning(self._h, text.encode()))

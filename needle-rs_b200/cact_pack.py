@@ -284,7 +284,8 @@ class _Writer:
 
 
 def build_container(geom: Geometry | None = None, seed: int = 0,
-                    codebook: np.ndarray | None = None, tokenizer: bytes | None = None) -> bytes:
+                    codebook: np.ndarray | None = None, tokenizer: bytes | None = None,
+                    confidence_head: bool = False) -> bytes:
     """A random-init Needle 3 container with `geom`'s geometry.
 
     Init profile (seeded, documented so parity runs are reproducible): CQ
@@ -357,6 +358,18 @@ def build_container(geom: Geometry | None = None, seed: int = 0,
         cqw(d, d, g.default_bits, 0.05)  # value_proj
         w.fp16(rng.normal(0, 0.5, (g.engram_conv_taps, d)))  # taps
     w.fp16(rng.normal(0, 0.02, d))  # final_norm
+    if confidence_head:
+        # heads.manifest [2] (confidence), then the head in canon order
+        # (v3.rs:491-560): probes [(L+1)*4, d] CQ, gain [L+1, 4], query [4, d]
+        # CQ, row_bias [4, L+1, 4], proj [1, 4*d] CQ, bias [1].
+        kp, qn = 4, 4
+        w.fp16(np.array([2.0]))
+        cqw((L + 1) * kp, d, g.mhc_bits, 0.05)
+        w.fp16(1.0 + rng.normal(0, 0.1, (L + 1, kp)))
+        cqw(qn, d, g.mhc_bits, 0.05)
+        w.fp16(rng.normal(0, 0.1, (qn, L + 1, kp)))
+        cqw(1, qn * d, g.mhc_bits, 0.05)
+        w.fp16(rng.normal(0, 0.1, 1))
     if tokenizer is not None:  # the RAW tokenizer record, last as in the shipped container
         w.recs.append((DT_RAW, (), bytes(tokenizer), 0, 0))
     return w.build(g.header_words(len(w.recs)), g.rope_theta, cb)

@@ -509,10 +509,29 @@ bool needle_v3_confidence_for(NeedleV3Handle* h, const char* query, const char* 
                               const char* completion, float* out) {
   clear_err();
   if (!h) set_err("handle was null");
-  else if (!query || !tools_json || !completion) set_err("an argument was null or not UTF-8");
+  else if (!utf8_ok(query) || !utf8_ok(tools_json) || !utf8_ok(completion))
+    set_err("an argument was null or not UTF-8");
   else if (!out) set_err("out was null");
   else if (!h->eng->cfg.has_heads) set_err("this container exports no confidence head");
-  else set_err("the confidence probe head is not run by this GPU build");
+  else if (!h->eng->tok) set_err(kNoTokenizer);
+  else {
+    // V3Engine::confidence_for (v3_engine.rs:351-368): the prompt plus the
+    // completion, [bos] + encode(), truncated to the context; the sigmoid of
+    // the head's first logit.
+    nb::Engine* E = h->eng.get();
+    std::vector<uint32_t> ids = {kBosId};
+    const std::vector<uint32_t> enc = E->tok->encode(build_prompt(query, tools_json) + completion);
+    ids.insert(ids.end(), enc.begin(), enc.end());
+    if (ids.size() > E->cfg.max_seq) ids.resize(E->cfg.max_seq);
+    float logit = 0.f;
+    std::string err;
+    if (!E->confidence(ids.data(), ids.size(), &logit, &err)) {
+      set_err(err);
+      return false;
+    }
+    *out = 1.0f / (1.0f + expf(-logit));
+    return true;
+  }
   return false;
 }
 

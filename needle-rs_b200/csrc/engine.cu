@@ -449,9 +449,47 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     *err = "directory has fewer tensors than the canon needs";
     return nullptr;
   }
+  // Probe heads (v3.rs:300-316, :486-560): the records between the final norm
+  // and the RAW tokenizer are a manifest of head codes, then six tensors per
+  // head (seven for the router) — probes, gain, query, row_bias, proj, bias.
+  // Only the confidence head (code 2) is kept.
+  size_t head_end = nt, conf_i = 0;
+  long conf_gain = -1, conf_rb = -1, conf_bias = -1;
+  for (size_t i = 0; i < nt; ++i)
+    if (L.recs[i].dtype == 4) {
+      head_end = i;
+      break;
+    }
   c.has_heads = false;
-  for (size_t i = cur; i < nt; ++i)
-    if (L.recs[i].dtype != 4) c.has_heads = true;
+  if (cur < head_end) {
+    const size_t mi = cur++;
+    const long mo = L.floats(mi);
+    if (mo < 0) {
+      *err = L.err;
+      return nullptr;
+    }
+    const size_t ncodes = (size_t)L.recs[mi].nbytes / (L.recs[mi].dtype == 1 ? 2 : 4);  // the arena pads
+    for (size_t k = 0; k < ncodes; ++k) {
+      const int code = (int)(uint8_t)L.arena[mo + k];
+      const size_t need = code == 3 ? 7 : 6;
+      if (cur + need > head_end) {
+        *err = "head tensors ran out";
+        return nullptr;
+      }
+      if (code == 2 && !c.has_heads) {
+        conf_i = cur;
+        conf_gain = L.floats(cur + 1);
+        conf_rb = L.floats(cur + 3);
+        conf_bias = L.floats(cur + 5);
+        if (conf_gain < 0 || conf_rb < 0 || conf_bias < 0) {
+          *err = L.err;
+          return nullptr;
+        }
+        c.has_heads = true;
+      }
+      cur += need;
+    }
+  }
   // Shape validation (v3.rs:336-383).
   const char* bad = nullptr;
   if (!shape2(emb, c.vocab, d)) bad = "embedding";
@@ -687,6 +725,62 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     for (size_t l = 0; l < c.layers; ++l) E->mp[l].phi_dense = E->d_phid + (size_t)src[l] * nr * Wd;
   }
   for (size_t s = 0; s < c.sites.size(); ++s) E->eng_taps.push_back(P + etaps[ssrc[s]]);
+  // The confidence head, dense, with the cells of this engine's blocks
+  // (confidence_head_at_depth, v3.rs:745-787: cell 0 and 1 + each kept block).
+  if (c.has_heads) {
+    CqMat pm, qm, jm;
+    if (!(L.cq(conf_i, E->d_blob, &pm) && L.cq(conf_i + 2, E->d_blob, &qm) && L.cq(conf_i + 4, E->d_blob, &jm))) {
+      *err = L.err;
+      return nullptr;
+    }
+    const size_t PL1 = (size_t)E->phi_pre.rows / c.lanes + 1, prow = (size_t)pm.rows;
+    const size_t ngain = (size_t)L.recs[conf_i + 1].nbytes / (L.recs[conf_i + 1].dtype == 1 ? 2 : 4);
+    if (prow % PL1 || ngain != prow || pm.in_feat != (int)d || qm.in_feat != (int)d ||
+        jm.in_feat != qm.rows * (int)d) {
+      *err = "probe head shapes disagree with num_layers + 1 cells";
+      return nullptr;
+    }
+    const size_t K = prow / PL1, Q = qm.rows, OD = jm.rows, mm = PL1 * K;
+    auto count = [&](size_t i) { return (size_t)L.recs[i].nbytes / (L.recs[i].dtype == 1 ? 2 : 4); };
+    if (count(conf_i + 3) != Q * mm || count(conf_i + 5) < OD) {
+      *err = "probe head row_bias or bias disagrees with its shapes";
+      return nullptr;
+    }
+    std::vector<size_t> cl = {0};
+    for (int sl : src) cl.push_back((size_t)sl + 1);
+    const size_t cells = cl.size(), m = cells * K;
+    std::vector<float> probes(m * d), gain(m), query(Q * d), rb(Q * m), proj(OD * Q * d), bias(OD);
+    for (size_t i = 0; i < cells; ++i)
+      for (size_t k = 0; k < K; ++k) {
+        cq_dense_row(raw, E->d_blob, pm, (int)(cl[i] * K + k), probes.data() + (i * K + k) * d);
+        gain[i * K + k] = L.arena[conf_gain + cl[i] * K + k];
+        for (size_t qi = 0; qi < Q; ++qi) rb[qi * m + i * K + k] = L.arena[conf_rb + qi * mm + cl[i] * K + k];
+      }
+    for (size_t qi = 0; qi < Q; ++qi) cq_dense_row(raw, E->d_blob, qm, (int)qi, query.data() + qi * d);
+    for (size_t o = 0; o < OD; ++o) {
+      cq_dense_row(raw, E->d_blob, jm, (int)o, proj.data() + o * Q * d);
+      bias[o] = L.arena[conf_bias + o];
+    }
+    std::vector<float> all;
+    for (const auto* v : {&probes, &gain, &query, &rb, &proj, &bias}) all.insert(all.end(), v->begin(), v->end());
+    e = cudaMalloc(&E->d_conf, all.size() * 4);
+    if (e == cudaSuccess) e = cudaMemcpy(E->d_conf, all.data(), all.size() * 4, cudaMemcpyHostToDevice);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("uploading the confidence head", e);
+      return nullptr;
+    }
+    ProbeHeadDev& h = E->conf;
+    h.probes = E->d_conf;
+    h.gain = h.probes + probes.size();
+    h.query = h.gain + gain.size();
+    h.row_bias = h.query + query.size();
+    h.proj = h.row_bias + rb.size();
+    h.bias = h.proj + proj.size();
+    h.cells = (int)cells;
+    h.probes_per_cell = (int)K;
+    h.queries = (int)Q;
+    h.out_dim = (int)OD;
+  }
   E->final_norm = P + fnorm;
   // HadamardMLP weight fragments for the tensor-core block tail.
   for (size_t l = 0; l < c.layers; ++l) E->lp[l].hfrag = nullptr;
@@ -764,6 +858,7 @@ Engine::~Engine() {
   if (d_rope) cudaFree(d_rope);
   if (d_hfrag) cudaFree(d_hfrag);
   if (d_phid) cudaFree(d_phid);
+  if (d_conf) cudaFree(d_conf);
   if (d_tables) cudaFree(d_tables);
   if (h_wait_flag) cudaFreeHost(h_wait_flag);
   if (stream) cudaStreamDestroy(stream);
@@ -971,6 +1066,7 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
     NB_MARK(PK_ENGRAM, S * cq_launches(eng_kv[0], M, &w.gs) + 2);
   }
   NB_TRY(launch_embed(G, emb, rb, w.lanes, st));
+  if (w.cells) NB_TRY(launch_lane_mean(w.lanes, M, G.lanes, d, true, w.cells, st));
   NB_MARK(PK_EMBED, 1);
   for (int l = 0; l < G.layers; ++l) {
     NB_TRY(launch_layer_pre(G, l, rb, w.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
@@ -991,6 +1087,7 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
     NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &w.gs));
     NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, w.projo, w.u, w.bx,
                              w.gates, w.lanes, st));
+    if (w.cells) NB_TRY(launch_lane_mean(w.lanes, M, G.lanes, d, false, w.cells + (size_t)(l + 1) * M * d, st));
     NB_MARK(PK_LAYER_POST, 1);
   }
   NB_TRY(launch_final(G, rb, w.lanes, final_norm, w.lm_in, st));
@@ -1030,10 +1127,14 @@ static bool ensure_logits(Engine* E, Workspace& w, size_t rows, std::string* err
 static constexpr size_t MAX_PREFILL_ROWS = 16384;
 
 bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_t* lens, size_t n,
-                     float* logits, uint32_t* picks, std::string* err) {
+                     float* logits, uint32_t* picks, std::string* err, float* d_cells) {
   std::lock_guard<std::mutex> lk(mu);
   cudaSetDevice(device);
   if (n == 0) return true;
+  if (d_cells && n != 1) {
+    *err = "cells are captured for one prompt at a time";
+    return false;
+  }
   for (size_t i = 0; i < n; ++i) {
     if (!ss[i] || ss[i]->eng != this) {
       *err = "session does not belong to this handle";
@@ -1078,7 +1179,9 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
     cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), rows * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
     if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tok.data(), rows * 4, cudaMemcpyHostToDevice, stream);
     RowBatch rb{ws.rows, ws.tokens, (int)rows, MODE_PREFILL};
+    ws.cells = d_cells;
     if (e == cudaSuccess) e = forward(ws, rb, stream, ss[i0]->int8, ns);
+    ws.cells = nullptr;
     if (e == cudaSuccess) e = launch_step_end(rb, stream);
     for (size_t i = 0; e == cudaSuccess && i < i1 - i0; ++i)
       e = cudaMemcpyAsync(ws.lm_last + i * dpad, ws.lm_in + (size_t)last[i] * dpad, dpad * 4,
@@ -1100,6 +1203,54 @@ bool Engine::prefill(Session* const* ss, const uint32_t* const* ids, const size_
     i0 = i1;
   }
   return true;
+}
+
+// model.rs:482-492 forward_head with the confidence head: a prefill of `ids`
+// on a scratch f32 session that also captures the cells, then the head.
+bool Engine::confidence(const uint32_t* ids, size_t n, float* logit, std::string* err) {
+  if (!cfg.has_heads) {
+    *err = "this container exports no confidence head";
+    return false;
+  }
+  if (n == 0 || n > cfg.max_seq) {
+    *err = "input length must be in 1..max_seq_len";
+    return false;
+  }
+  std::unique_ptr<Session> s(new_session(n, false, err));
+  if (!s) return false;
+  const size_t d = G.d, cells = conf.cells, m = cells * conf.probes_per_cell;
+  float* buf = nullptr;
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    cudaSetDevice(device);
+    cudaError_t e = cudaMalloc(&buf, (cells * n * d + m * d + conf.out_dim) * sizeof(float));
+    if (e != cudaSuccess) {
+      *err = cuda_msg("allocating the head cells", e);
+      return false;
+    }
+  }
+  Session* sp = s.get();
+  const uint32_t* idp[1] = {ids};
+  size_t lens[1] = {n};
+  bool ok = prefill(&sp, idp, lens, 1, nullptr, nullptr, err, buf);
+  if (ok) {
+    std::lock_guard<std::mutex> lk(mu);
+    cudaSetDevice(device);
+    float* r = buf + cells * n * d;
+    cudaError_t e = launch_probe_head(buf, (int)n, (int)d, conf, r, r + m * d, stream);
+    if (e == cudaSuccess) e = cudaMemcpyAsync(logit, r + m * d, sizeof(float), cudaMemcpyDeviceToHost, stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
+    if (e != cudaSuccess) {
+      *err = cuda_msg("confidence head", e);
+      ok = false;
+    }
+  }
+  {
+    std::lock_guard<std::mutex> lk(mu);
+    cudaSetDevice(device);
+    cudaFree(buf);
+  }
+  return ok;
 }
 
 bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float* logits,

@@ -74,6 +74,7 @@ struct Workspace {
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;
   int* last_rows = nullptr;
+  float* cells = nullptr;  // when set, the forward writes the probe-head cells here [layers + 1][rows][d]
   float* part = nullptr;  // attention split partials
   size_t part_cap = 0;    // floats
   void release();
@@ -132,8 +133,13 @@ class Engine {
   Session* new_session(size_t hint, bool int8, std::string* err);
   // Whole-prompt prefill of fresh sessions (model.rs:512-523). Writes the last
   // position's logits (host, [n][logit_rows]) and/or greedy picks (host, [n]).
+  // d_cells: capture the probe-head cells of a single prompt there (device,
+  // [layers + 1][len][d_model]).
   bool prefill(Session* const* ss, const uint32_t* const* ids, const size_t* lens, size_t n,
-               float* logits, uint32_t* picks, std::string* err);
+               float* logits, uint32_t* picks, std::string* err, float* d_cells = nullptr);
+  // The confidence head's logit over ids (model.rs:482-492); false with *err
+  // when the container has no confidence head.
+  bool confidence(const uint32_t* ids, size_t n, float* logit, std::string* err);
   // One decode step for each session (model.rs:150-375), host buffers.
   bool decode(Session* const* ss, const uint32_t* tokens, size_t n, float* logits,
               uint32_t* picks, std::string* err);
@@ -150,6 +156,8 @@ class Engine {
   float* d_rope = nullptr;
   uint32_t* d_hfrag = nullptr;  // HadamardMLP weight fragments, all layers
   float* d_phid = nullptr;
+  float* d_conf = nullptr;  // the confidence head's weights (conf points into it)
+  ProbeHeadDev conf{};
   // The container's tokenizer (its RAW record); null when the container has none.
   std::unique_ptr<Tokenizer> tok;      // mHC lane-matrix rows, dequantised and rotated, all container layers
   CqMat emb{}, phi_pre{}, phi_post{}, phi_res{};

@@ -31,6 +31,15 @@ struct LayerParams {
   float hinv[6];
 };
 
+// A probe head's dense weights on the device (heads.rs:41-62): probes
+// [cells * probes_per_cell][d], gain [cells * probes_per_cell], query
+// [queries][d], row_bias [queries][cells * probes_per_cell], proj
+// [out_dim][queries * d], bias [out_dim].
+struct ProbeHeadDev {
+  const float *probes, *gain, *query, *row_bias, *proj, *bias;
+  int cells, probes_per_cell, queries, out_dim;
+};
+
 // Longest causal QKV conv the GPU path runs (the shipped geometry has 3 taps).
 constexpr int MAX_QKV_TAPS = 4;
 
@@ -136,6 +145,13 @@ void hada_frags(const float* const* mats, int D, uint32_t* out, float* inv);
 cudaError_t launch_layer_post_tc(const Geo& G, const RowBatch& rb, const LayerParams& lp, const uint32_t* p1,
                                  const uint32_t* p2, const float* projo, const float* u, float* bx,
                                  const float* gates, float* lanes, cudaStream_t st);
+// Cells of the probe heads: out[M][d] = lane 0 of each row (copy0) or the
+// mean of its lanes; then one head over a captured cells array [cells][seq][d]
+// (r: scratch [cells * probes_per_cell][d]; out: out_dim logits).
+cudaError_t launch_lane_mean(const float* lanes, int M, int n, int d, bool copy0, float* out, cudaStream_t st);
+cudaError_t launch_probe_head(const float* cells, int seq, int d, const ProbeHeadDev& h, float* r, float* out,
+                              cudaStream_t st);
+
 cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
                          const float* final_norm, float* lm_in, cudaStream_t st);
 cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st);

@@ -225,6 +225,44 @@ std::string load_model(const uint8_t* raw, size_t len, V3Model* m) {
   m->perms.p2.resize(p2.size());
   for (size_t i = 0; i < p1.size(); ++i) m->perms.p1[i] = (uint32_t)p1[i];
   for (size_t i = 0; i < p2.size(); ++i) m->perms.p2[i] = (uint32_t)p2[i];
+  // Probe heads (v3.rs:300-316, :486-560): the records between the final norm
+  // and the RAW tokenizer are a manifest of head codes, then six tensors per
+  // head (seven for the router): probes, gain, query, row_bias, proj, bias.
+  size_t head_end = num_tensors;
+  for (size_t i = 0; i < num_tensors; ++i)
+    if (L.recs[i].dtype == DT_RAW) {
+      head_end = i;
+      break;
+    }
+  if (cur < head_end) {
+    std::vector<float> codes;
+    if (!L.floats(cur++, &codes)) return L.err;
+    for (float code : codes) {
+      const size_t need = (uint8_t)code == 3 ? 7 : 6;
+      if (cur + need > head_end) return "head tensors ran out";
+      const size_t pi = cur, gi = cur + 1, qi = cur + 2, ri = cur + 3, ji = cur + 4, bi = cur + 5;
+      cur += need;
+      if ((uint8_t)code != 2) continue;
+      ProbeHead& h = m->confidence;
+      auto dense = [&](size_t i, std::vector<float>* out) {
+        CqWeight w;
+        if (!L.cq(i, &w)) return false;
+        out->assign(w.out_feat * w.in_feat, 0.f);
+        for (size_t o = 0; o < w.out_feat; ++o) w.dequantize_row(o, out->data() + o * w.in_feat);
+        return true;
+      };
+      if (!(dense(pi, &h.probes) && L.floats(gi, &h.gain) && dense(qi, &h.query) && L.floats(ri, &h.row_bias) &&
+            dense(ji, &h.proj) && L.floats(bi, &h.bias)))
+        return L.err;
+      h.cells = c.num_layers + 1;
+      const size_t prow = L.recs[pi].shape[0];
+      if (prow % h.cells || h.gain.size() != prow) return "probe head shapes disagree with num_layers + 1 cells";
+      h.probes_per_cell = prow / h.cells;
+      h.queries = L.recs[qi].shape[0];
+      h.out_dim = L.recs[ji].shape[0];
+      m->has_confidence = true;
+    }
+  }
   // model.rs:110-136 V3Model::new
   if (m->embedding.out_feat != c.vocab_size || m->embedding.in_feat != c.d_model)
     return "embedding shape does not match geometry";

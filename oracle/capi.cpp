@@ -169,6 +169,34 @@ void* orc_model_load_depth(const uint8_t* data, size_t len, size_t depth, char* 
   }
   return m;
 }
+int orc_model_has_confidence(void* mp) { return ((V3Model*)mp)->has_confidence ? 1 : 0; }
+// The confidence head's first logit over the sequence (v3_engine.rs:351-368
+// before the sigmoid); 0 when the model has no head.
+int orc_confidence_logit(void* mp, const uint32_t* ids, size_t n, float* out) {
+  const V3Model* m = (const V3Model*)mp;
+  if (!m->has_confidence || n == 0) return 0;
+  std::vector<float> cells = m->forward_cells(ids, n);
+  *out = m->confidence.forward(cells.data(), n, m->cfg.d_model)[0];
+  return 1;
+}
+// ProbeHead::forward on explicit weights (heads.rs:65-118).
+void orc_probe_forward(const float* cells, size_t seq, size_t d, const float* probes, const float* gain,
+                       const float* query, const float* row_bias, const float* proj, const float* bias,
+                       size_t ncells, size_t k, size_t q, size_t out_dim, float* out) {
+  ProbeHead h;
+  h.probes.assign(probes, probes + ncells * k * d);
+  h.gain.assign(gain, gain + ncells * k);
+  h.query.assign(query, query + q * d);
+  h.row_bias.assign(row_bias, row_bias + q * ncells * k);
+  h.proj.assign(proj, proj + out_dim * q * d);
+  h.bias.assign(bias, bias + out_dim);
+  h.cells = ncells;
+  h.probes_per_cell = k;
+  h.queries = q;
+  h.out_dim = out_dim;
+  std::vector<float> r = h.forward(cells, seq, d);
+  for (size_t o = 0; o < out_dim; ++o) out[o] = r[o];
+}
 // ladder.rs:28: writes num_layers entries.
 void orc_ladder_order(size_t num_layers, int64_t* out) {
   std::vector<size_t> o = ladder_order(num_layers);

@@ -121,6 +121,27 @@ std::string slice_to_depth(V3Model* m, size_t depth) {
   if (!mh.phi_pre.select_rows(rows(n), &sliced.phi_pre) || !mh.phi_post.select_rows(rows(n), &sliced.phi_post) ||
       !mh.phi_res.select_rows(rows(n * n), &sliced.phi_res))
     return "mHC lane row out of range";
+  // confidence_head_at_depth (v3.rs:745-787): cells 0 and 1 + each kept block
+  // of probes and gain, and the same cells on the middle axis of row_bias.
+  if (m->has_confidence) {
+    ProbeHead& h = m->confidence;
+    const size_t k = h.probes_per_cell, q = h.queries, d = c.d_model, mm = h.cells * k;
+    std::vector<size_t> cl = {0};
+    for (size_t l : kept) cl.push_back(l + 1);
+    std::vector<float> probes, gain, row_bias;
+    for (size_t cc : cl) {
+      probes.insert(probes.end(), h.probes.begin() + cc * k * d, h.probes.begin() + (cc + 1) * k * d);
+      gain.insert(gain.end(), h.gain.begin() + cc * k, h.gain.begin() + (cc + 1) * k);
+    }
+    for (size_t qi = 0; qi < q; ++qi)
+      for (size_t cc : cl)
+        row_bias.insert(row_bias.end(), h.row_bias.begin() + qi * mm + cc * k,
+                        h.row_bias.begin() + qi * mm + (cc + 1) * k);
+    h.probes = std::move(probes);
+    h.gain = std::move(gain);
+    h.row_bias = std::move(row_bias);
+    h.cells = cl.size();
+  }
   c.num_layers = depth;
   c.global_layers = globals;
   c.engram.sites = sites;

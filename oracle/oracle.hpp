@@ -235,6 +235,14 @@ struct V3EngramSite {
   std::vector<float> taps;
 };
 
+// heads.rs:41-118: a probe head over the per-layer cells, dense weights.
+struct ProbeHead {
+  std::vector<float> probes, gain, query, row_bias, proj, bias;
+  size_t cells = 0, probes_per_cell = 0, queries = 0, out_dim = 0;
+  // `cells` shaped (seq, this->cells, d): out_dim logits (the two-pass form).
+  std::vector<float> forward(const float* cells, size_t seq, size_t d) const;
+};
+
 struct V3Model {
   V3Config cfg;
   CqWeight embedding;
@@ -248,7 +256,12 @@ struct V3Model {
   std::vector<float> decode_step(V3Cache& cache, uint32_t token) const;        // model.rs:150
   std::vector<float> prefill(const uint32_t* tokens, size_t n, V3Cache& cache) const;  // :512
   std::vector<float> forward_sequence(const uint32_t* tokens, size_t n) const;  // :478
-  std::vector<float> forward_impl(const uint32_t* tokens, size_t n, V3Cache* cache) const;  // :550
+  std::vector<float> forward_impl(const uint32_t* tokens, size_t n, V3Cache* cache,
+                                  std::vector<float>* cells = nullptr) const;  // :550
+  // (seq, num_layers + 1, d): the scaled embedding, then each layer's lane mean (model.rs:494-502).
+  std::vector<float> forward_cells(const uint32_t* tokens, size_t n) const;
+  bool has_confidence = false;
+  ProbeHead confidence;  // heads.rs HEAD_CONFIDENCE (code 2), when the container exports it
   size_t clamp_token(uint32_t t) const;
   void rope_at(size_t pos, float* c, float* s) const;
   void rope(size_t seq, std::vector<float>* c, std::vector<float>* s) const;

@@ -37,6 +37,9 @@ def lib():
             ("orc_ladder_order", None, [sz, vp]),
             ("orc_ladder_layers", C.c_int, [sz, sz, vp]),
             ("orc_model_layer_roles", C.c_int, [vp, vp, C.c_int]),
+            ("orc_model_has_confidence", C.c_int, [vp]),
+            ("orc_confidence_logit", C.c_int, [vp, vp, sz, vp]),
+            ("orc_probe_forward", None, [vp, sz, sz, vp, vp, vp, vp, vp, vp, sz, sz, sz, sz, vp]),
             ("orc_session_new", vp, [vp, sz, C.c_int]),
             ("orc_session_clone", vp, [vp]),
             ("orc_quant_into", C.c_float, [vp, vp, sz]),
@@ -184,6 +187,22 @@ def ngram_valid(p, table, orders, heads):
     return bool(lib().orc_ngram_valid(p, table, P(o), len(o), heads))
 
 
+def probe_forward(cells, probes, gain, query, row_bias, proj, bias):
+    """ProbeHead::forward (heads.rs:65-118) on explicit weights; cells (seq, ncells, d)."""
+    cells = np.ascontiguousarray(cells, np.float32)
+    seq, ncells, d = cells.shape
+    probes = np.ascontiguousarray(probes, np.float32)
+    k = probes.shape[0] // ncells
+    query = np.ascontiguousarray(query, np.float32)
+    proj = np.ascontiguousarray(proj, np.float32)
+    out_dim = proj.shape[0]
+    out = np.zeros(out_dim, np.float32)
+    arrs = [np.ascontiguousarray(a, np.float32) for a in (gain, row_bias, bias)]
+    lib().orc_probe_forward(P(cells), seq, d, P(probes), P(arrs[0]), P(query), P(arrs[1]), P(proj), P(arrs[2]),
+                            ncells, k, query.shape[0], out_dim, P(out))
+    return out
+
+
 def ladder_order(num_layers: int):
     """ladder.rs:28: the order blocks join the ladder."""
     out = np.zeros(max(num_layers, 1), np.int64)
@@ -226,6 +245,17 @@ class Model:
         out = np.zeros((len(ids), self.rows), np.float32)
         lib().orc_forward_sequence(C.c_void_p(self.h), P(ids), C.c_size_t(len(ids)), P(out))
         return out
+
+    def has_confidence(self) -> bool:
+        return bool(lib().orc_model_has_confidence(C.c_void_p(self.h)))
+
+    def confidence_logit(self, ids) -> float:
+        """The confidence head's logit over `ids` (v3_engine.rs:351-368 before the sigmoid)."""
+        ids = np.ascontiguousarray(ids, np.uint32)
+        out = np.zeros(1, np.float32)
+        if not lib().orc_confidence_logit(C.c_void_p(self.h), P(ids), C.c_size_t(len(ids)), P(out)):
+            raise ValueError("no confidence head or empty input")
+        return float(out[0])
 
     def layer_roles(self):
         """(global-attention layers, Engram sites) of this model's stack."""

@@ -763,7 +763,79 @@ std::vector<float> V3Model::prefill(const uint32_t* tokens, size_t n, V3Cache& c
 }
 
 // model.rs:550-980 (forward_impl_pooled without cells / probe pool).
-std::vector<float> V3Model::forward_impl(const uint32_t* tokens, size_t seq, V3Cache* cache) const {
+std::vector<float> V3Model::forward_cells(const uint32_t* tokens, size_t n) const {
+  std::vector<float> cells;
+  forward_impl(tokens, n, nullptr, &cells);
+  return cells;
+}
+
+// heads.rs:65-177: per (cell, probe) a softmax over positions of the scaled
+// probe dot, the weighted mean of the cells, rms_unit and the gain; per query a
+// softmax over all (cell, probe) pairs with the row bias, the weighted mean,
+// then the projection of the flattened (queries * d) vector plus the bias.
+std::vector<float> ProbeHead::forward(const float* cs, size_t seq, size_t d) const {
+  const size_t l1 = cells, k = probes_per_cell, q = queries, m = l1 * k;
+  const float scale = 1.0f / sqrtf((float)d);
+  std::vector<float> r(m * d, 0.f), sc(seq);
+  for (size_t l = 0; l < l1; ++l)
+    for (size_t kk = 0; kk < k; ++kk) {
+      const float* pr = probes.data() + (l * k + kk) * d;
+      float mx = -INFINITY;
+      for (size_t t = 0; t < seq; ++t) {
+        const float* cell = cs + (t * l1 + l) * d;
+        float acc = 0.f;
+        for (size_t i = 0; i < d; ++i) acc += cell[i] * pr[i];
+        sc[t] = acc * scale;
+        if (sc[t] > mx) mx = sc[t];
+      }
+      float sum = 0.f;
+      for (size_t t = 0; t < seq; ++t) {
+        sc[t] = expf(sc[t] - mx);
+        sum += sc[t];
+      }
+      const float inv = 1.0f / sum;
+      float* dst = r.data() + (l * k + kk) * d;
+      for (size_t t = 0; t < seq; ++t) {
+        const float w = sc[t] * inv;
+        const float* cell = cs + (t * l1 + l) * d;
+        for (size_t i = 0; i < d; ++i) dst[i] += w * cell[i];
+      }
+      rms_unit_to(dst, dst, d);
+      const float g = gain[l * k + kk];
+      for (size_t i = 0; i < d; ++i) dst[i] *= g;
+    }
+  std::vector<float> pooled(q * d, 0.f), u(m);
+  for (size_t qi = 0; qi < q; ++qi) {
+    const float* qv = query.data() + qi * d;
+    float mx = -INFINITY;
+    for (size_t idx = 0; idx < m; ++idx) {
+      float acc = 0.f;
+      for (size_t i = 0; i < d; ++i) acc += r[idx * d + i] * qv[i];
+      u[idx] = acc * scale + row_bias[qi * m + idx];
+      if (u[idx] > mx) mx = u[idx];
+    }
+    float sum = 0.f;
+    for (size_t idx = 0; idx < m; ++idx) {
+      u[idx] = expf(u[idx] - mx);
+      sum += u[idx];
+    }
+    const float inv = 1.0f / sum;
+    for (size_t idx = 0; idx < m; ++idx) {
+      const float w = u[idx] * inv;
+      for (size_t i = 0; i < d; ++i) pooled[qi * d + i] += w * r[idx * d + i];
+    }
+  }
+  std::vector<float> out(out_dim);
+  for (size_t o = 0; o < out_dim; ++o) {
+    float acc = 0.f;
+    for (size_t i = 0; i < q * d; ++i) acc += proj[o * q * d + i] * pooled[i];
+    out[o] = acc + (o < bias.size() ? bias[o] : 0.f);
+  }
+  return out;
+}
+
+std::vector<float> V3Model::forward_impl(const uint32_t* tokens, size_t seq, V3Cache* cache,
+                                         std::vector<float>* cells) const {
   const V3Config& c = cfg;
   size_t d = c.d_model, n = c.mhc_lanes, rows = c.logit_rows();
   bool quantised = cache && cache->precision == KvPrecision::Int8;
@@ -773,9 +845,12 @@ std::vector<float> V3Model::forward_impl(const uint32_t* tokens, size_t seq, V3C
   engram_kv_with_raw(tokens, seq, cache != nullptr, &ek, &ev, &ev_raw);
 
   std::vector<float> lanes(seq * n * d), emb(d);
+  const size_t l1 = c.num_layers + 1;
+  if (cells) cells->assign(seq * l1 * d, 0.f);
   for (size_t t = 0; t < seq; ++t) {
     embedding.dequantize_row(clamp_token(tokens[t]), emb.data());
     for (float& x : emb) x *= embed_scale;
+    if (cells) std::memcpy(cells->data() + t * l1 * d, emb.data(), d * 4);  // cell 0
     for (size_t l = 0; l < n; ++l) std::memcpy(lanes.data() + (t * n + l) * d, emb.data(), d * 4);
   }
   AttnDims dims{seq, c.num_heads, c.num_kv_heads, c.qk_head_dim, c.v_head_dim};
@@ -893,6 +968,13 @@ std::vector<float> V3Model::forward_impl(const uint32_t* tokens, size_t seq, V3C
       for (size_t i = 0; i < d; ++i) y[i] = bx[t * d + i] - u[t * d + i];
       scatter_up(ls, hpost.data(), hres.data(), y.data(), m, li, n, d);
     }
+    if (cells)  // cell li + 1: the lane stream after this layer, meaned over lanes (model.rs:910-926)
+      for (size_t t = 0; t < seq; ++t)
+        for (size_t i = 0; i < d; ++i) {
+          float a = 0.f;
+          for (size_t l = 0; l < n; ++l) a += lanes[(t * n + l) * d + i];
+          (*cells)[(t * l1 + li + 1) * d + i] = a / (float)n;
+        }
   }
 
   if (cache) {

@@ -115,5 +115,21 @@ def text_raw(sp_fixture):
     return raw
 
 
+@pytest.fixture(scope="session")
+def head_text_raw(sp_fixture):
+    """As text_raw, with a confidence probe head between the final norm and the
+    tokenizer (the weights before it are those of full_raw)."""
+    os.makedirs(CACHE, exist_ok=True)
+    path = os.path.join(CACHE, f"shipped_tok_head_0_{sha256(sp_fixture['blob'])[:12]}.cact")
+    if os.path.exists(path):
+        return open(path, "rb").read()
+    raw = cact_pack.build_container(cact_pack.shipped(), seed=0, tokenizer=sp_fixture["blob"], confidence_head=True)
+    tmp = path + f".{os.getpid()}"
+    with open(tmp, "wb") as f:
+        f.write(raw)
+    os.replace(tmp, path)
+    return raw
+
+
 def sha256(b: bytes) -> str:
     return hashlib.sha256(b).hexdigest()

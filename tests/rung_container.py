@@ -62,7 +62,36 @@ def write_rung(raw: bytes, kept) -> bytes:
             new_sites.append(kept.index(layer))
             for r in recs[at + 4 * s:at + 4 * s + 4]:
                 copy(r)
-    for r in recs[at + 4 * len(sites):]:  # final norm and anything after it
+    at += 4 * len(sites)
+    copy(recs[at])  # final norm
+    at += 1
+    # Probe heads (v3.rs:745-787): cells 0 and 1 + each kept block of probes
+    # (CQ rows) and gain, and the same cells on the middle axis of row_bias.
+    if at < len(recs) and recs[at]["dtype"] != cact_pack.DT_RAW:
+        man = recs[at]
+        copy(man)
+        codes = np.frombuffer(blob(man), "<f2" if man["dtype"] == cact_pack.DT_FP16 else "<f4").astype(int)
+        at += 1
+        cells = [0] + [k + 1 for k in kept]
+        for code in codes:
+            pr, ga, qu, rb, pj, bi = recs[at:at + 6]
+            k = pr["shape"][0] // (L + 1)
+            rows = [c * k + i for c in cells for i in range(k)]
+            w.recs.append((pr["dtype"], (len(rows), pr["shape"][1]), _cq_rows(raw, pr, rows), pr["group"], pr["bits"]))
+            isz = _ITEM[ga["dtype"]]
+            g = np.frombuffer(blob(ga), np.uint8).reshape(L + 1, k * isz)[cells]
+            w.recs.append((ga["dtype"], (len(cells), k), g.tobytes(), 0, 0))
+            copy(qu)
+            q = rb["shape"][0]
+            b = np.frombuffer(blob(rb), np.uint8).reshape(q, L + 1, k * _ITEM[rb["dtype"]])[:, cells]
+            w.recs.append((rb["dtype"], (q, len(cells), k), b.tobytes(), 0, 0))
+            copy(pj)
+            copy(bi)
+            at += 6
+            if code == 3:
+                copy(recs[at])
+                at += 1
+    for r in recs[at:]:  # the tokenizer
         copy(r)
     new_mask = 0
     for i, l in enumerate(kept):
