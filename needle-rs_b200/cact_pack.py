@@ -70,7 +70,17 @@ def random_codebook(rng: np.random.Generator, std: float = 0.02) -> np.ndarray:
     return f16_round(rng.normal(0.0, std, 28))
 
 
-def codebook_levels(codebook: np.ndarray, bits: int) -> np.ndarray:
+TERNARY = 5  # directory `bits` of a ternary tensor (cq.rs:55-61)
+TERNARY_CENTROID = np.float32(1.2240064)
+TERNARY_CRUMB = np.array([3, 0, 1], np.uint8)  # trit index 0, 1, 2 -> stored 2-bit crumb
+
+
+def codebook_levels(codebook: np.ndarray, bits: int, group: int = 128) -> np.ndarray:
+    """Levels of a width: slices cb2 | cb3 | cb4 of the header codebook, or the
+    analytic ternary levels {-s, 0, +s}, s = centroid / sqrt(group) in f32."""
+    if bits == TERNARY:
+        s = TERNARY_CENTROID / np.sqrt(np.float32(group))
+        return np.array([-s, 0.0, s], np.float32)
     start = {2: 0, 3: 4, 4: 12}[bits]
     return np.asarray(codebook[start:start + (1 << bits)], np.float32)
 
@@ -117,8 +127,9 @@ def unpack_indices(packed: np.ndarray, bits: int, in_pad: int) -> np.ndarray:
 
 
 def cq_blob(idx: np.ndarray, norms: np.ndarray, bits: int) -> bytes:
-    """Packed indices followed by FP16 norms (cq.rs:181-238 reads this)."""
-    packed = pack_indices(idx, bits)
+    """Packed indices followed by FP16 norms (cq.rs:181-238 reads this);
+    ternary stores each trit index as its 2-bit crumb."""
+    packed = pack_indices(TERNARY_CRUMB[idx], 2) if bits == TERNARY else pack_indices(idx, bits)
     return packed.tobytes() + np.asarray(norms, np.float32).astype("<f2").tobytes()
 
 
@@ -130,7 +141,7 @@ def cq_quantize(w: np.ndarray, bits: int, codebook: np.ndarray, group: int = 128
     out, in_feat = w.shape
     in_pad = -(-in_feat // group) * group
     ng = in_pad // group
-    levels = codebook_levels(codebook, bits).astype(np.float64)
+    levels = codebook_levels(codebook, bits, group).astype(np.float64)
     order = np.argsort(levels, kind="stable")
     srt = levels[order]
     mids = (srt[1:] + srt[:-1]) / 2.0
@@ -166,7 +177,7 @@ def dequantize(idx: np.ndarray, norms: np.ndarray, bits: int, codebook: np.ndarr
                in_feat: int, group: int = 128) -> np.ndarray:
     """Dense reconstruction (cq.rs:763-779): levels*norm, then the rotation."""
     out, in_pad = idx.shape
-    lv = codebook_levels(codebook, bits)[idx].reshape(out, in_pad // group, group)
+    lv = codebook_levels(codebook, bits, group)[idx].reshape(out, in_pad // group, group)
     g = lv.astype(np.float64) * norms[..., None]
     return (g @ walsh(group)).reshape(out, in_pad)[:, :in_feat].astype(np.float32)
 

@@ -145,6 +145,40 @@ bool Engine::ensure_part(Workspace& w, size_t rows, int nsplit, std::string* err
 
 // ------------------------------------------------------------------ loading
 namespace {
+// Widths of a CQ record: 2, 3 or 4 bits against the header codebook, or 5 for
+// ternary (four signed 2-bit crumbs per byte, cq.rs:55-61).
+constexpr int CQ_TERNARY = 5;
+
+// Level table of a record's width, 16 entries (unused ones zero): the header
+// codebook slice cb2 | cb3 | cb4, or the analytic ternary levels {-s, 0, +s}
+// with s = centroid / sqrt(group) (cq.rs:197-203).
+void cq_levels(int bits, int group, const float* codebook, float* lv) {
+  std::fill(lv, lv + 16, 0.f);
+  if (bits == CQ_TERNARY) {
+    const float s = 1.2240064f / sqrtf((float)group);
+    lv[0] = -s;
+    lv[2] = s;
+    return;
+  }
+  const float* src = bits == 2 ? codebook : bits == 3 ? codebook + 4 : codebook + 12;
+  for (int k = 0; k < (1 << bits); ++k) lv[k] = src[k];
+}
+
+// Level indices of the first n codes of a packed row: an LSB-first bitstream
+// of 2-, 3- or 4-bit codes, ternary crumbs 3, 0, 1 (2) meaning levels 0, 1, 2
+// (1) (cq.rs:395-420, :908-925).
+void cq_row_codes(const uint8_t* row, size_t n, int bits, uint8_t* idx) {
+  const bool ter = bits == CQ_TERNARY;
+  const int w = ter ? 2 : bits;
+  const uint32_t mask = (1u << w) - 1;
+  for (size_t k = 0; k < n; ++k) {
+    const size_t bit = k * w, byte = bit / 8, shift = bit % 8;
+    const uint32_t v = row[byte] | (shift + w > 8 ? (uint32_t)row[byte + 1] << 8 : 0u);
+    const uint32_t code = (v >> shift) & mask;
+    idx[k] = ter ? (uint8_t)(code == 3 ? 0 : code == 1 ? 2 : 1) : (uint8_t)code;
+  }
+}
+
 struct Loader {
   const uint8_t* raw;
   size_t len;
@@ -152,6 +186,7 @@ struct Loader {
   float codebook[28];
   std::vector<float> arena;  // f32 parameters, each tensor 16-byte aligned
   std::string err;
+  std::vector<void*>* owned = nullptr;  // device buffers of widened tensors, freed with the engine
 
   // FP16/FP32 record -> offset (floats) into the arena (cact.rs:494-524).
   long floats(size_t i, size_t expect = 0) {
@@ -190,10 +225,11 @@ struct Loader {
     const Record& r = recs[i];
     if (r.dtype != 3) return fail("expected a CQ tensor", i) >= 0;
     if (r.group != 128) return fail("GPU path supports CQ group 128 only", i) >= 0;
-    if (r.bits != 2 && r.bits != 4) return fail("GPU path supports 2- and 4-bit CQ tensors only", i) >= 0;
+    if (r.bits < 2 || r.bits > 5) return fail("CQ width must be 2, 3, 4 bits or ternary", i) >= 0;
     size_t out = r.shape[0], in = r.shape[1];
     if (!out || !in) return fail("empty CQ shape", i) >= 0;
-    size_t in_pad = (in + 127) / 128 * 128, groups = in_pad / 128, rb = in_pad * r.bits / 8;
+    const int w = r.bits == CQ_TERNARY ? 2 : (int)r.bits;
+    size_t in_pad = (in + 127) / 128 * 128, groups = in_pad / 128, rb = in_pad * w / 8;
     if (r.nbytes < out * rb + out * groups * 2) return fail("short CQ blob", i) >= 0;
     if (r.offset % 16) return fail("CQ blob not 16-byte aligned", i) >= 0;
     std::memset(W, 0, sizeof(*W));
@@ -208,8 +244,30 @@ struct Loader {
     W->groups = (int)groups;
     W->group = 128;
     W->bits = (int)r.bits;
-    const float* lv = r.bits == 2 ? codebook : codebook + 12;  // cb2 | cb3 | cb4
-    for (int k = 0; k < (1 << r.bits); ++k) W->levels[k] = lv[k];
+    cq_levels((int)r.bits, 128, codebook, W->levels);
+    if (r.bits == 3 || r.bits == CQ_TERNARY) {
+      // The kernels read byte-aligned 2- and 4-bit codes: 3-bit and ternary
+      // tensors are widened once to 4-bit codes indexing the same levels, so
+      // every product sees exactly the reference's dequantised values.
+      if (!owned) return fail("internal: no owner for a widened tensor", i) >= 0;
+      const size_t rb4 = in_pad / 2;
+      std::vector<uint8_t> idx(in_pad), packed(out * rb4);
+      for (size_t o = 0; o < out; ++o) {
+        cq_row_codes(raw + r.offset + o * rb, in_pad, (int)r.bits, idx.data());
+        for (size_t k = 0; k < in_pad; k += 2) packed[o * rb4 + k / 2] = (uint8_t)(idx[k] | (idx[k + 1] << 4));
+      }
+      void* d = nullptr;
+      cudaError_t e = cudaMalloc(&d, packed.size());
+      if (e == cudaSuccess) e = cudaMemcpy(d, packed.data(), packed.size(), cudaMemcpyHostToDevice);
+      if (e != cudaSuccess) {
+        if (d) cudaFree(d);
+        return fail("widening a CQ tensor failed on the device", i) >= 0;
+      }
+      owned->push_back(d);
+      W->seg[0].packed = static_cast<const uint8_t*>(d);
+      W->row_bytes = (int)rb4;
+      W->bits = 4;
+    }
     return true;
   }
 };
@@ -233,25 +291,26 @@ bool concat(CqMat* dst, const CqMat& add, std::string* err) {
 // repeatedly the midpoint of the widest gap between chosen blocks (the leftmost
 // gap on ties); the rung of depth k keeps the first k blocks of that order, in
 // stack order. Depths outside 2..layers are not rungs.
-// One row of a single-tensor CQ matrix as dense f32 weights, each 128-group
-// rotated: H (norm_g * levels[codes]) with H the normalised Walsh-Hadamard
-// matrix of the group (natural order, symmetric), so that
-// dense . x == norm_g * (levels . H x), the CQ dot of cq.rs:666-672. Computed
-// in double from the container's host bytes and rounded once.
-static void cq_dense_row(const uint8_t* raw, const uint8_t* d_blob, const CqMat& m, int row, float* out) {
-  const uint8_t* codes = raw + (m.seg[0].packed - d_blob) + (size_t)row * m.row_bytes;
-  const uint8_t* nb = raw + (reinterpret_cast<const uint8_t*>(m.seg[0].norms) - d_blob) + (size_t)row * m.groups * 2;
-  const int bits = m.bits, mask = (1 << bits) - 1;
+// One row of a CQ record as dense f32 weights, each 128-group rotated:
+// H (norm_g * levels[codes]) with H the normalised Walsh-Hadamard matrix of
+// the group (natural order, symmetric), so that dense . x == norm_g * (levels
+// . H x), the CQ dot of cq.rs:666-672. Computed in double from the
+// container's host bytes and rounded once.
+static void cq_dense_row(const uint8_t* raw, const Record& r, const float* codebook, size_t row, float* out) {
+  const int w = r.bits == CQ_TERNARY ? 2 : (int)r.bits;
+  const size_t in_pad = (r.shape[1] + 127) / 128 * 128, groups = in_pad / 128, rb = in_pad * w / 8;
+  const uint8_t* codes = raw + r.offset + row * rb;
+  const uint8_t* nb = raw + r.offset + r.shape[0] * rb + row * groups * 2;
+  float lv[16];
+  cq_levels((int)r.bits, 128, codebook, lv);
+  std::vector<uint8_t> idx(in_pad);
+  cq_row_codes(codes, in_pad, (int)r.bits, idx.data());
   double v[128];
-  for (int g = 0; g < m.groups; ++g) {
+  for (size_t g = 0; g < groups; ++g) {
     __half_raw hr;
     hr.x = (unsigned short)(nb[2 * g] | (nb[2 * g + 1] << 8));
     const double norm = (double)__half2float(__half(hr));
-    for (int j = 0; j < 128; ++j) {
-      const size_t bit = (size_t)(g * 128 + j) * bits;
-      const int c = (codes[bit / 8] >> (bit % 8)) & mask;
-      v[j] = (double)m.levels[c] * norm;
-    }
+    for (int j = 0; j < 128; ++j) v[j] = (double)lv[idx[g * 128 + j]] * norm;
     for (int h = 1; h < 128; h <<= 1)
       for (int i = 0; i < 128; i += 2 * h)
         for (int j = i; j < i + h; ++j) {
@@ -331,6 +390,7 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     L.recs.push_back(r);
   }
   std::unique_ptr<Engine> E(new Engine());
+  L.owned = &E->d_owned;
   // The tokenizer travels as the container's RAW record (cact.rs:1068-1075).
   // A malformed one fails the load; a container without one still serves the
   // token-level API.
@@ -712,9 +772,9 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     for (size_t l = 0; l < PL; ++l)
       for (size_t o = 0; o < nr; ++o) {
         float* dst = dense.data() + (l * nr + o) * Wd;
-        if (o < c.lanes) cq_dense_row(raw, E->d_blob, E->phi_pre, (int)(l * c.lanes + o), dst);
-        else if (o < 2 * c.lanes) cq_dense_row(raw, E->d_blob, E->phi_post, (int)(l * c.lanes + o - c.lanes), dst);
-        else cq_dense_row(raw, E->d_blob, E->phi_res, (int)(l * c.lanes * c.lanes + o - 2 * c.lanes), dst);
+        if (o < c.lanes) cq_dense_row(raw, L.recs[phi[0]], L.codebook, l * c.lanes + o, dst);
+        else if (o < 2 * c.lanes) cq_dense_row(raw, L.recs[phi[1]], L.codebook, l * c.lanes + o - c.lanes, dst);
+        else cq_dense_row(raw, L.recs[phi[2]], L.codebook, l * c.lanes * c.lanes + o - 2 * c.lanes, dst);
       }
     e = cudaMalloc(&E->d_phid, dense.size() * 4);
     if (e == cudaSuccess) e = cudaMemcpy(E->d_phid, dense.data(), dense.size() * 4, cudaMemcpyHostToDevice);
@@ -752,13 +812,13 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     std::vector<float> probes(m * d), gain(m), query(Q * d), rb(Q * m), proj(OD * Q * d), bias(OD);
     for (size_t i = 0; i < cells; ++i)
       for (size_t k = 0; k < K; ++k) {
-        cq_dense_row(raw, E->d_blob, pm, (int)(cl[i] * K + k), probes.data() + (i * K + k) * d);
+        cq_dense_row(raw, L.recs[conf_i], L.codebook, cl[i] * K + k, probes.data() + (i * K + k) * d);
         gain[i * K + k] = L.arena[conf_gain + cl[i] * K + k];
         for (size_t qi = 0; qi < Q; ++qi) rb[qi * m + i * K + k] = L.arena[conf_rb + qi * mm + cl[i] * K + k];
       }
-    for (size_t qi = 0; qi < Q; ++qi) cq_dense_row(raw, E->d_blob, qm, (int)qi, query.data() + qi * d);
+    for (size_t qi = 0; qi < Q; ++qi) cq_dense_row(raw, L.recs[conf_i + 2], L.codebook, qi, query.data() + qi * d);
     for (size_t o = 0; o < OD; ++o) {
-      cq_dense_row(raw, E->d_blob, jm, (int)o, proj.data() + o * Q * d);
+      cq_dense_row(raw, L.recs[conf_i + 4], L.codebook, o, proj.data() + o * Q * d);
       bias[o] = L.arena[conf_bias + o];
     }
     std::vector<float> all;
@@ -859,6 +919,7 @@ Engine::~Engine() {
   if (d_hfrag) cudaFree(d_hfrag);
   if (d_phid) cudaFree(d_phid);
   if (d_conf) cudaFree(d_conf);
+  for (void* p : d_owned) cudaFree(p);
   if (d_tables) cudaFree(d_tables);
   if (h_wait_flag) cudaFreeHost(h_wait_flag);
   if (stream) cudaStreamDestroy(stream);

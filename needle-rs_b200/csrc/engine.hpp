@@ -157,6 +157,7 @@ class Engine {
   uint32_t* d_hfrag = nullptr;  // HadamardMLP weight fragments, all layers
   float* d_phid = nullptr;
   float* d_conf = nullptr;  // the confidence head's weights (conf points into it)
+  std::vector<void*> d_owned;  // 3-bit and ternary tensors widened to 4-bit codes
   ProbeHeadDev conf{};
   // The container's tokenizer (its RAW record); null when the container has none.
   std::unique_ptr<Tokenizer> tok;      // mHC lane-matrix rows, dequantised and rotated, all container layers

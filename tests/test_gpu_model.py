@@ -158,6 +158,31 @@ def test_many_row_prefill_matches_oracle(full_gpu, full_oracle):
         assert rel_err(s.decode_step(int(t)), o.decode_step(int(t))) < tol(False)
 
 
+@pytest.mark.parametrize("bits", [3, 5])
+def test_three_bit_and_ternary_projections(cuda, bits):
+    """3-bit and ternary CQ projections (cq.rs:55-68, :197-203, :395-420),
+    widened at load to 4-bit codes indexing the same levels: the tiny geometry
+    with every q/k/v/gate/out and Engram projection at that width matches the
+    oracle, prefill and decode."""
+    from conftest import cact_pack
+    g = cact_pack.tiny()
+    g.default_bits = bits
+    raw = cact_pack.build_container(g, seed=2)
+    eng, o = nb.V3Engine.from_bytes(raw), orc.Model(raw)
+    try:
+        toks = np.random.default_rng(bits).integers(1, 512, 24).astype(np.uint32)
+        gs, os_ = eng.session(40, False), o.session(40, False)
+        lg, lo = gs.prefill(toks), os_.prefill(toks)
+        assert rel_err(lg, lo) < REL
+        for _ in range(8):
+            t = int(np.argmax(lo))
+            lg, lo = gs.decode_step(t), os_.decode_step(t)
+            assert rel_err(lg, lo) < REL
+    finally:
+        del gs
+        eng.close()
+
+
 def test_device_batch_graph_matches_eager(full_gpu, cuda):
     """The CUDA-graph replay of a batched decode step gives the same tokens and
     logits as the eager launch sequence (and both match single sessions)."""
