@@ -113,6 +113,16 @@ size_t needle_v3_session_pos(NeedleV3Session *session);
 size_t needle_v3_session_bytes(NeedleV3Session *session);
 size_t needle_v3_session_slots(NeedleV3Session *session, size_t layer);
 
+/* Host copy of one layer's KV ring, in the reference's layout (V3Cache::kv,
+ * cache.rs:382-393; ring slot of position p is p % slots): k [slots][kv_heads]
+ * [qk] and v [slots][kv_heads][v_head] as floats (f32 session) or int8 codes
+ * (int8 session), plus for int8 the f32 scales k_scale / v_scale
+ * [slots][kv_heads]; slots no position has reached yet read as zero codes
+ * with scale 1, the reference's initial state. Any of k, v may be NULL (with
+ * its scale for int8). Synchronous. */
+bool needle_v3_session_kv(NeedleV3Session *session, size_t layer, void *k, void *v, float *k_scale,
+                          float *v_scale);
+
 /* Prefill a fresh session with `n` token ids (V3Model::prefill, model.rs:512).
  * Writes the last position's logits (logit_rows floats) when `logits` is not
  * NULL. Host buffers. */
@@ -142,6 +152,15 @@ bool needle_v3_decode_batch(NeedleV3Handle *handle, NeedleV3Session *const *sess
 size_t needle_v3_generate_ids(NeedleV3Handle *handle, const uint32_t *prompt, size_t n,
                               size_t max_new_tokens, float temperature, uint64_t seed,
                               bool kv_int8, uint32_t eos_id, uint32_t *out_ids);
+
+/* One temperature draw from `n` logits (host) as generate_with takes it
+ * (sample, v3_engine.rs:422-443): softmax(logits / temperature) weights summed
+ * in f64, target = next_f64() * sum from the SplitMix64 generator whose state
+ * is *rng_state (v3_engine.rs:446-464; seed it with the generation seed), which
+ * advances by one draw. For callers that sample the logits of the batched
+ * calls themselves. UINT32_MAX with the last error set for NULL arguments,
+ * n == 0 or temperature <= 0. Host only. */
+uint32_t needle_v3_sample(const float *logits, size_t n, float temperature, uint64_t *rng_state);
 
 /* A fixed set of sessions decoded together with device-resident tokens; one
  * step is captured once as a CUDA graph and replayed. */
@@ -232,8 +251,9 @@ int nd_attend_step(const float *q, const void *k, const void *v, const float *ks
  * every GPU that loads the library until exit) instead of per-call scratch.
  * Requests needing more than 1048576 floats of partials even with a single
  * position split (B * heads * (vh + 2) floats) fail with cudaErrorInvalidValue
- * and a message in nd_last_error(). The first call on each device looks up the
- * array's device address; make that first call before any stream capture.
+ * and a message in nd_last_error(). The first call on each device (and the
+ * first after that device's context was reset) looks up the array's device
+ * address; make that call before any stream capture.
  * All calls on a device share the array and keep the last call's contents:
  * calls whose kernels overlap on the GPU race and must be serialised.
  * Arguments and result as nd_attend_step. */

@@ -123,11 +123,13 @@ def lib() -> C.CDLL:
         "needle_v3_session_pos": (sz, [vp]),
         "needle_v3_session_bytes": (sz, [vp]),
         "needle_v3_session_slots": (sz, [vp, sz]),
+        "needle_v3_session_kv": (b, [vp, sz, vp, vp, vp, vp]),
         "needle_v3_prefill": (b, [vp, vp, vp, sz, f32p]),
         "needle_v3_decode_step": (b, [vp, vp, C.c_uint32, f32p]),
         "needle_v3_prefill_batch": (b, [vp, vp, vp, vp, sz, f32p, vp]),
         "needle_v3_decode_batch": (b, [vp, vp, vp, sz, f32p, vp]),
         "needle_v3_generate_ids": (sz, [vp, vp, sz, sz, C.c_float, C.c_uint64, b, C.c_uint32, vp]),
+        "needle_v3_sample": (C.c_uint32, [vp, sz, C.c_float, vp]),
         "needle_v3_batch_new": (vp, [vp, vp, sz]),
         "needle_v3_batch_free": (None, [vp]),
         "needle_v3_batch_tokens": (vp, [vp]),
@@ -348,6 +350,21 @@ class Session:
     def slots(self, layer: int) -> int:
         return lib().needle_v3_session_slots(self._s, layer)
 
+    def kv(self, layer: int):
+        """Layer `layer`'s ring in the reference's layout (V3Cache::kv,
+        cache.rs:382-393), flattened: (k, v) f32 [slots * kv_heads * dim], or
+        for int8 (kq, k_scale, vq, v_scale) with scales [slots * kv_heads]."""
+        g = self.eng.geometry
+        n, kvh = self.slots(layer), g["kv_heads"]
+        dt = np.int8 if self.kv_int8 else np.float32
+        k = np.zeros(n * kvh * g["qk_head_dim"], dt)
+        v = np.zeros(n * kvh * g["v_head_dim"], dt)
+        ks = np.zeros(n * kvh, np.float32) if self.kv_int8 else None
+        vs = np.zeros(n * kvh, np.float32) if self.kv_int8 else None
+        if not lib().needle_v3_session_kv(self._s, layer, k.ctypes.data, v.ctypes.data, _ptr(ks), _ptr(vs)):
+            _fail("needle_v3_session_kv")
+        return (k, ks, v, vs) if self.kv_int8 else (k, v)
+
     def prefill(self, ids) -> np.ndarray:
         a = np.ascontiguousarray(ids, np.uint32)
         out = np.zeros(self.eng.logit_rows, np.float32)
@@ -417,6 +434,17 @@ class Batch:
         if not lib().needle_v3_batch_get_next(self._b, out.ctypes.data):
             _fail("needle_v3_batch_get_next")
         return out
+
+
+def sample(logits, temperature: float, state: int) -> tuple[int, int]:
+    """One temperature draw (sample + SplitMix64, v3_engine.rs:422-464):
+    returns (token id, the generator's next state)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    st = C.c_uint64(state)
+    pick = lib().needle_v3_sample(lg.ctypes.data, len(lg), temperature, C.byref(st))
+    if pick == 0xFFFFFFFF:
+        _fail("needle_v3_sample")
+    return int(pick), int(st.value)
 
 
 # ------------------------------------------------------------------ kernels

@@ -17,7 +17,9 @@
 // heads of a KV head share one CTA, so each key/value byte is read from HBM
 // once per row. Sums are reassociated relative to the reference's two-pass
 // loop; results agree to f32 rounding.
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 
 #include <algorithm>
 #include <mutex>
@@ -915,9 +917,13 @@ bool attn_fuses_finish(const Geo& G, int int8) {
   return int8 && (rep * G.vh) % 128 == 0 && rep <= 8;
 }
 
+// Attention CTAs a launch aims for: enough to cover the 148 SMs several times.
+constexpr int AT_SPLIT_TARGET = 148 * 6;
+
 int attn_nsplit(int rows, int kvh, int max_span) {
-  // Enough CTAs to cover the 148 SMs several times; never more splits than chunks.
-  const int target = 148 * 6;
+  // Split positions until the launch has AT_SPLIT_TARGET CTAs; never more
+  // splits than chunks.
+  const int target = AT_SPLIT_TARGET;
   int ns = (target + rows * kvh - 1) / (rows * kvh);
   ns = std::max(1, std::min(ns, (max_span + CH - 1) / CH));
   return std::min(ns, 64);
@@ -1115,20 +1121,18 @@ cudaError_t launch_attend_step(const float* q, const void* k, const void* v, con
 }
 
 // quant_into (crates/needle-core/src/v3/cache.rs:100-106) over `rows` vectors of
-// `dim` <= 64: one warp per vector. Bit-exact: IEEE division for the scale and
-// its reciprocal, roundf half away from zero, clamp [-128, 127].
+// `dim` <= 64: one warp per vector, through kv_quant_warp, the same quantiser
+// the forward's KV append runs.
 __global__ void kv_quant_kernel(const float* __restrict__ x, int rows, int dim, int8_t* __restrict__ q,
                                 float* __restrict__ scales) {
   const int w = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   if (w >= rows) return;
   const float* xr = x + (size_t)w * dim;
-  float a = lane < dim ? xr[lane] : 0.f, b = lane + 32 < dim ? xr[lane + 32] : 0.f;
-  float am = warp_max(fmaxf(fabsf(a), fabsf(b)));
-  float scale = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
-  float inv = __fdiv_rn(1.0f, scale);
-  if (lane < dim) q[(size_t)w * dim + lane] = (int8_t)fminf(fmaxf(roundf(__fmul_rn(a, inv)), -128.f), 127.f);
-  if (lane + 32 < dim)
-    q[(size_t)w * dim + lane + 32] = (int8_t)fminf(fmaxf(roundf(__fmul_rn(b, inv)), -128.f), 127.f);
+  const float a = lane < dim ? xr[lane] : 0.f, b = lane + 32 < dim ? xr[lane + 32] : 0.f;
+  float ca, cb;
+  const float scale = kv_quant_warp(a, b, &ca, &cb);
+  if (lane < dim) q[(size_t)w * dim + lane] = (int8_t)ca;
+  if (lane + 32 < dim) q[(size_t)w * dim + lane + 32] = (int8_t)cb;
   if (lane == 0) scales[w] = scale;
 }
 
@@ -1215,26 +1219,61 @@ cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, con
 constexpr size_t NB_NOALLOC_SCRATCH_FLOATS = (size_t)1 << 20;
 static __device__ __align__(256) float g_attn_noalloc_scratch[NB_NOALLOC_SCRATCH_FLOATS];
 
+// attn_nsplit splits positions only while B * kv_heads < AT_SPLIT_TARGET, so a
+// request with more than one split has B * kv_heads * splits < 2 *
+// AT_SPLIT_TARGET rows of partials; with at most AT_MAXREP query heads per KV
+// head and value heads of at most 64 floats those always fit the array. Only a
+// single-split request (B * kv_heads >= AT_SPLIT_TARGET) can be too large.
+static_assert((size_t)2 * AT_SPLIT_TARGET * AT_MAXREP * (64 + 2) <= NB_NOALLOC_SCRATCH_FLOATS,
+              "split requests of nd_attend_step_noalloc must fit the fixed scratch");
+
 namespace {
 std::mutex g_noalloc_mu;
-float* g_noalloc_ptr[256] = {};  // device address of the array, per device ordinal
+// Device address of the array per device ordinal, and the context it was
+// looked up in.
+struct NoallocSlot {
+  CUcontext ctx;
+  float* ptr;
+};
+NoallocSlot g_noalloc[256] = {};
+
+PFN_cuCtxGetCurrent_v4000 ctx_get_current() {
+  static PFN_cuCtxGetCurrent_v4000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuCtxGetCurrent_v4000>(p);
+  });
+  return fn;
+}
 
 // In host code the array's name stands for a host-side shadow, not a device
-// address; the device address is looked up once per device, with that device
-// current.
+// address. The device address is looked up with that device current, once per
+// device, and again when the device's context has changed since (a
+// cudaDeviceReset reloads the module, which may move the array).
 cudaError_t noalloc_scratch(float** out) {
   int dev = 0;
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess) return e;
   if (dev < 0 || dev >= 256) return cudaErrorInvalidDevice;
+  auto get_ctx = ctx_get_current();
+  if (!get_ctx) return cudaErrorNotSupported;
   std::lock_guard<std::mutex> lk(g_noalloc_mu);
-  if (!g_noalloc_ptr[dev]) {
+  CUcontext ctx = nullptr;
+  if (get_ctx(&ctx) != CUDA_SUCCESS) return cudaErrorInvalidDevice;
+  NoallocSlot& slot = g_noalloc[dev];
+  if (!slot.ptr || !ctx || slot.ctx != ctx) {
     void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);
+    e = cudaGetSymbolAddress(&p, g_attn_noalloc_scratch);  // also makes the primary context current
     if (e != cudaSuccess) return e;
-    g_noalloc_ptr[dev] = static_cast<float*>(p);
+    if (get_ctx(&ctx) != CUDA_SUCCESS || !ctx) return cudaErrorInvalidDevice;
+    slot.ctx = ctx;
+    slot.ptr = static_cast<float*>(p);
   }
-  *out = g_noalloc_ptr[dev];
+  *out = slot.ptr;
   return cudaSuccess;
 }
 }  // namespace
@@ -1247,15 +1286,14 @@ extern "C" int nd_attend_step_noalloc(const float* q, const void* k, const void*
                                       void* stream) {
   using namespace nb;
   if (!q || !k || !v || !lo || !hi || !out || (int8 && (!ks || !vs)) || kv_heads <= 0 || heads % kv_heads ||
-      slots <= 0 || vh <= 0) {
+      heads / kv_heads > AT_MAXREP || slots <= 0 || (vh != 32 && vh != 64)) {
     nd_record_error(cudaErrorInvalidValue, "nd_attend_step_noalloc: invalid argument");
     return (int)cudaErrorInvalidValue;
   }
   if (B <= 0) return 0;
-  // Fewer position splits need less scratch; the result does not depend on the
-  // split count beyond f32 rounding. Reject what one split cannot fit.
-  int ns = attn_nsplit(B, kv_heads, slots);
-  while (ns > 1 && attn_part_floats(B, heads, kv_heads, vh, ns) > NB_NOALLOC_SCRATCH_FLOATS) --ns;
+  // The split count of nd_attend_step; only a single-split request can exceed
+  // the array (see the static_assert above).
+  const int ns = attn_nsplit(B, kv_heads, slots);
   if (attn_part_floats(B, heads, kv_heads, vh, ns) > NB_NOALLOC_SCRATCH_FLOATS) {
     nd_record_error(cudaErrorInvalidValue,
                     "nd_attend_step_noalloc: B * heads * (v_head_dim + 2) floats exceed the fixed 4 MiB "

@@ -607,6 +607,41 @@ size_t needle_v3_session_slots(NeedleV3Session* s, size_t layer) {
   return (size_t)s->s->layers[layer].slots;
 }
 
+uint32_t needle_v3_sample(const float* logits, size_t n, float temperature, uint64_t* rng_state) {
+  clear_err();
+  if (!logits || !rng_state || n == 0) {
+    set_err("logits or rng_state was null, or n was 0");
+    return UINT32_MAX;
+  }
+  if (!(temperature > 0.f)) {
+    set_err("temperature must be positive");
+    return UINT32_MAX;
+  }
+  SplitMix64 rng{*rng_state};
+  const uint32_t pick = sample(logits, n, temperature, &rng);
+  *rng_state = rng.s;
+  return pick;
+}
+
+bool needle_v3_session_kv(NeedleV3Session* s, size_t layer, void* k, void* v, float* k_scale,
+                          float* v_scale) {
+  clear_err();
+  if (!s) {
+    set_err("session was null");
+    return false;
+  }
+  if (s->s->int8 && (!!k_scale != !!k || !!v_scale != !!v)) {
+    set_err("an int8 ring is read with its scales");
+    return false;
+  }
+  std::string err;
+  if (!s->eng->read_kv(s->s.get(), layer, k, v, k_scale, v_scale, &err)) {
+    set_err(err);
+    return false;
+  }
+  return true;
+}
+
 static bool check_sessions(NeedleV3Handle* h, NeedleV3Session* const* ss, size_t n,
                            std::vector<nb::Session*>* out) {
   if (!h) {
@@ -862,9 +897,8 @@ bool needle_v3_batch_get_next(NeedleV3Batch* b, uint32_t* next) {
   }
   cudaSetDevice(b->eng->device);
   cudaDeviceSynchronize();
-  int flag = 0;
-  if (nb::umma_take_error(&flag) == cudaSuccess && flag) {
-    set_err("a tensor-core projection of an earlier step gave up a bounded wait; its results are invalid");
+  if (b->eng->take_wait_flag() == cudaErrorTimeout) {
+    set_err("a kernel of an earlier step gave up a bounded wait; its results are invalid");
     return false;
   }
   return batch_copy(b, next, b->b->d_next, cudaMemcpyDeviceToHost);

@@ -105,6 +105,24 @@ __device__ __forceinline__ float block_max(float v, float* red) {
   return warp_max(t);
 }
 
+// quant_into (crates/needle-core/src/v3/cache.rs:100-106, quant_scale
+// :91-98) of one head vector held by a warp, two elements per lane (lanes past
+// the vector's end hold 0): scale = absmax / 127 (1 for an all-zero vector),
+// code = clamp(roundf(x * (1 / scale)), -128, 127). IEEE division for the
+// scale and its reciprocal and roundf's half-away-from-zero rounding make it
+// bit-exact with the reference on identical inputs. This is the only int8
+// quantiser on the GPU: the KV append and the query fake-quant of qkv_post and
+// the standalone nd_kv_quant all call it. Returns the scale; the codes come
+// back as floats holding integers in [-128, 127].
+__device__ __forceinline__ float kv_quant_warp(float a, float b, float* ca, float* cb) {
+  const float am = warp_max(fmaxf(fabsf(a), fabsf(b)));
+  const float scale = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
+  const float inv = __fdiv_rn(1.0f, scale);
+  *ca = fminf(fmaxf(roundf(__fmul_rn(a, inv)), -128.0f), 127.0f);
+  *cb = fminf(fmaxf(roundf(__fmul_rn(b, inv)), -128.0f), 127.0f);
+  return scale;
+}
+
 // Normalised Walsh-Hadamard transform of 128 floats held by one warp, 4 per
 // lane (element e = lane*4 + i). Same butterfly pairs and operand order as
 // crates/needle-core/src/hadamard.rs:24-55 (stride 1, 2, 4, ..., 64; a+b to the

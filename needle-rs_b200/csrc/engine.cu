@@ -120,6 +120,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
   w.gs.whi = w.whi;
   w.gs.wlo = w.wlo;
   w.gs.welems = wmax * kmax;
+  w.gs.werr = d_wait_flag;
   w.cap = cap;
   epoch++;
   return true;
@@ -576,7 +577,8 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
   // Device upload of the container.
   cudaError_t e = cudaGetDevice(&E->device);
   if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&E->stream, cudaStreamNonBlocking);
-  if (e == cudaSuccess) e = umma_error_ptr(&E->d_wait_flag);
+  if (e == cudaSuccess) e = cudaMalloc(&E->d_wait_flag, sizeof(int));
+  if (e == cudaSuccess) e = cudaMemset(E->d_wait_flag, 0, sizeof(int));
   if (e == cudaSuccess) e = cudaMallocHost(&E->h_wait_flag, sizeof(int));
   if (e == cudaSuccess) *E->h_wait_flag = 0;
   if (e == cudaSuccess) e = cudaMalloc(&E->d_blob, len);
@@ -922,6 +924,7 @@ Engine::~Engine() {
   for (void* p : d_owned) cudaFree(p);
   if (d_tables) cudaFree(d_tables);
   if (h_wait_flag) cudaFreeHost(h_wait_flag);
+  if (d_wait_flag) cudaFree(d_wait_flag);
   if (stream) cudaStreamDestroy(stream);
 }
 
@@ -934,6 +937,14 @@ cudaError_t Engine::wait_status(cudaStream_t st) {
   *h_wait_flag = 0;
   cudaError_t e = cudaMemsetAsync(d_wait_flag, 0, sizeof(int), st);
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e == cudaSuccess ? cudaErrorTimeout : e;
+}
+
+cudaError_t Engine::take_wait_flag() {
+  int v = 0;
+  cudaError_t e = cudaMemcpy(&v, d_wait_flag, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess || !v) return e;
+  e = cudaMemset(d_wait_flag, 0, sizeof(int));
   return e == cudaSuccess ? cudaErrorTimeout : e;
 }
 
@@ -1095,6 +1106,43 @@ bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
     }
     epoch++;
   }
+  return true;
+}
+
+bool Engine::read_kv(Session* s, size_t li, void* k, void* v, float* ks, float* vs, std::string* err) {
+  std::lock_guard<std::mutex> lk(mu);
+  cudaSetDevice(device);
+  if (li >= s->layers.size()) {
+    *err = "layer out of range";
+    return false;
+  }
+  const LayerKV& L = s->layers[li];
+  const size_t eb = kv_elem_bytes(s), S = (size_t)L.slots, H = (size_t)G.kvh;
+  std::vector<uint8_t> hk(H * S * G.qk * eb), hv(H * S * G.vh * eb);
+  std::vector<float> hks(s->int8 ? H * S : 0), hvs(s->int8 ? H * S : 0);
+  cudaError_t e = cudaStreamSynchronize(stream);
+  if (e == cudaSuccess) e = cudaMemcpy(hk.data(), L.k, hk.size(), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(hv.data(), L.v, hv.size(), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && s->int8) e = cudaMemcpy(hks.data(), L.ks, hks.size() * 4, cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess && s->int8) e = cudaMemcpy(hvs.data(), L.vs, hvs.size() * 4, cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) {
+    *err = cuda_msg("reading the KV ring", e);
+    return false;
+  }
+  // Head-major [kv_heads][slots][dim] on the device -> [slots][kv_heads][dim].
+  // Slots no position has reached yet (slot t >= pos while the ring is not
+  // full) hold zero codes and report the reference's initial scale of 1
+  // (cache.rs:214-215, :305-306); the device arena leaves them 0, which
+  // attention never reads.
+  const size_t kr = G.qk * eb, vr = G.vh * eb;
+  for (size_t h = 0; h < H; ++h)
+    for (size_t t = 0; t < S; ++t) {
+      const bool written = t < s->pos;
+      if (k) std::memcpy((uint8_t*)k + (t * H + h) * kr, hk.data() + (h * S + t) * kr, kr);
+      if (v) std::memcpy((uint8_t*)v + (t * H + h) * vr, hv.data() + (h * S + t) * vr, vr);
+      if (ks && s->int8) ks[t * H + h] = written ? hks[h * S + t] : 1.0f;
+      if (vs && s->int8) vs[t * H + h] = written ? hvs[h * S + t] : 1.0f;
+    }
   return true;
 }
 

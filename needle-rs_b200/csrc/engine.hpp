@@ -148,6 +148,11 @@ class Engine {
   bool decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, bool use_graph,
                            std::string* err);
   Batch* new_batch(Session* const* ss, size_t n, std::string* err);
+  // Host copy of layer `li`'s ring in the reference's layout (V3Cache::kv,
+  // cache.rs:382-393): k [slots][kv_heads][qk], v [slots][kv_heads][vh], f32
+  // or int8 codes by the session's precision, and for int8 the scales
+  // [slots][kv_heads]. Synchronous.
+  bool read_kv(Session* s, size_t li, void* k, void* v, float* ks, float* vs, std::string* err);
 
   // --- weights on the device
   uint8_t* d_blob = nullptr;
@@ -178,13 +183,18 @@ class Engine {
   uint64_t dec_graph_epoch = 0, dec_warm_epoch = 0;
   size_t dec_n = 0;
   int dec_ns = 0, dec_int8 = -1;
-  int* d_wait_flag = nullptr;  // tensor-core GEMM or int8 attention: a bounded wait expired (device flag)
+  // This engine's own device flag, raised by its tensor-core GEMMs and int8
+  // attention when a bounded wait expired; no other handle reads or clears it.
+  int* d_wait_flag = nullptr;
   int* h_wait_flag = nullptr;  // pinned host copy, refreshed before each synchronous return
 
   // Queues the copy of the device wait flag on `st`; after the stream is
   // synchronised, wait_status() turns a raised flag into an error and clears it.
   cudaError_t queue_wait_flag(cudaStream_t st);
   cudaError_t wait_status(cudaStream_t st);
+  // Synchronous read of the device flag: cudaErrorTimeout (and the flag
+  // cleared) when it was raised.
+  cudaError_t take_wait_flag();
 
   bool ensure_ws(Workspace& w, size_t rows, std::string* err);
   bool ensure_part(Workspace& w, size_t rows, int nsplit, std::string* err);

@@ -78,6 +78,9 @@ struct GemmScratch {
   __half* whi = nullptr;
   __half* wlo = nullptr;
   size_t welems = 0;
+  // Device flag the GEMM raises when one of its bounded waits gives up; null
+  // for the library-wide flag that umma_take_error reads.
+  int* werr = nullptr;
 };
 
 // force_path: 0 automatic (GEMV for M <= 8, else the tensor cores when `gs`
@@ -90,10 +93,11 @@ bool umma_supported(const CqMat& W);
 int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path = 0);
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                             int nrows, cudaStream_t st, const GemmScratch& gs);
-// Reads and clears the device flag raised when a bounded wait of the
-// tensor-core GEMM expired (*flag != 0).
+// Reads and clears the library-wide device flag raised when a bounded wait of
+// the tensor-core GEMM expired and the caller gave no flag of its own
+// (GemmScratch::werr null) (*flag != 0).
 cudaError_t umma_take_error(int* flag);
-// Device address of that flag on the current device.
+// Device address of that library-wide flag on the current device.
 cudaError_t umma_error_ptr(int** p);
 
 cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out,

@@ -788,18 +788,8 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
 // half-split RoPE (attention.rs:107-143), int8 query fake-quant (model.rs:289-293)
 // and quantize-on-append of K/V (cache.rs:346-377, quant_into :100-106).
 //
-// Quantisation is bit-exact with the reference on identical inputs: IEEE
-// absmax/127 and 1/scale, roundf (half away from zero), clamp [-128, 127].
-__device__ __forceinline__ float quant_scale_warp(float a0, float a1, float* inv) {
-  float am = warp_max(fmaxf(fabsf(a0), fabsf(a1)));
-  float scale = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
-  *inv = __fdiv_rn(1.0f, scale);
-  return scale;
-}
-__device__ __forceinline__ float q8(float x, float inv) {
-  float q = roundf(__fmul_rn(x, inv));
-  return fminf(fmaxf(q, -128.0f), 127.0f);
-}
+// Every quantisation goes through kv_quant_warp (common.cuh), the one int8
+// quantiser on the GPU, bit-exact with the reference on identical inputs.
 
 // One activation row, handled by the whole CTA (WARP = false: the conv phase
 // over every thread, the heads spread over the warps) or by one warp (WARP =
@@ -917,8 +907,8 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
         if (int8) {
           // The codes and scale also go to q8out / q8s for the integer score
           // path of the int8 attention; code * scale is the fake-quantised query.
-          float inv, scale = quant_scale_warp(x1, x2, &inv);
-          const float c1 = q8(x1, inv), c2 = q8(x2, inv);
+          float c1, c2;
+          const float scale = kv_quant_warp(x1, x2, &c1, &c2);
           if (q8out && lane < half) {
             q8out[(size_t)r * qd + h * G.qk + lane] = (int8_t)c1;
             q8out[(size_t)r * qd + h * G.qk + half + lane] = (int8_t)c2;
@@ -932,8 +922,9 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
           qpost[(size_t)r * qd + h * G.qk + half + lane] = x2;
         }
       } else if (int8) {
-        float inv, scale = quant_scale_warp(x1, x2, &inv);
-        int8_t a = (int8_t)q8(x1, inv), b = (int8_t)q8(x2, inv);
+        float c1, c2;
+        const float scale = kv_quant_warp(x1, x2, &c1, &c2);
+        const int8_t a = (int8_t)c1, b = (int8_t)c2;
         if (lane < half) {
           if (prefill) {
             int8_t* d8 = (int8_t*)pk + ((size_t)r * G.kvh + h) * G.qk;
@@ -969,8 +960,9 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
       const int vhalf = G.vh / 2;
       float x1 = lane < vhalf ? x[lane] : 0.f, x2 = lane < vhalf ? x[vhalf + lane] : 0.f;
       if (int8) {
-        float inv, scale = quant_scale_warp(x1, x2, &inv);
-        int8_t a = (int8_t)q8(x1, inv), b = (int8_t)q8(x2, inv);
+        float c1, c2;
+        const float scale = kv_quant_warp(x1, x2, &c1, &c2);
+        const int8_t a = (int8_t)c1, b = (int8_t)c2;
         if (lane < vhalf) {
           if (prefill) {
             int8_t* d8 = (int8_t*)pv + ((size_t)r * G.kvh + h) * G.vh;

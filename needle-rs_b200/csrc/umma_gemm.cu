@@ -53,7 +53,9 @@
 
 namespace nb {
 
-__device__ int g_umma_error;  // nonzero once a bounded wait in the tensor-core GEMM gave up
+// Raised when a bounded wait of the tensor-core GEMM gave up and no caller
+// flag was given (the standalone nd_cq_project); an engine passes its own.
+__device__ int g_umma_error;
 
 namespace {
 
@@ -108,11 +110,11 @@ __device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Wait for phase `parity` of `bar`. Gives up after WAIT_NS or as soon as
-// another role of the CTA gave up (`abort`), returning false. Between polls a
+// Wait for phase `parity` of `bar`. Gives up after WAIT_NS (raising *werr) or
+// as soon as another role of the CTA gave up (`abort`), returning false. Between polls a
 // waiter sleeps `backoff_ns` so waiting warps leave the issue slots to the
 // warps that decode weights on the same schedulers.
-__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort,
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile uint32_t* abort, int* werr,
                                           unsigned backoff_ns = 0) {
   if (mbar_try(bar, parity)) return true;
   const unsigned long long t0 = now_ns();
@@ -122,7 +124,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
     if (*abort) return false;
     if (now_ns() - t0 > WAIT_NS) {
       *abort = 1;
-      atomicExch(&g_umma_error, 1);
+      atomicExch(werr, 1);
       return false;
     }
   }
@@ -201,7 +203,7 @@ __global__ void __launch_bounds__(UTHREADS, 1)
 cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
                const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
-               int nrows) {
+               int nrows, int* werr) {
   constexpr int USTAGES = Pipe<EXACT>::STAGES;
   constexpr uint32_t STAGE_BYTES = Pipe<EXACT>::STAGE_BYTES;
   extern __shared__ unsigned char smraw[];
@@ -263,7 +265,7 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
     bool ok = true;
     for (int g = 0; g < ng; ++g) {
       const int b = g & 1;
-      if (!mbar_wait(&tfull[b], (uint32_t)(g >> 1) & 1u, abort, 128)) {
+      if (!mbar_wait(&tfull[b], (uint32_t)(g >> 1) & 1u, abort, werr, 128)) {
         ok = false;
         break;
       }
@@ -308,7 +310,7 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
       for (int kb = 0; kb < nk; ++kb) {
         const int s = kb % USTAGES;
         const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort)) break;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort, werr)) break;
         unsigned char* st = sm + s * STAGE_BYTES;
         mbar_arrive_tx(&full[s], (EXACT ? 3 : 4) * TILE);
         tma_load_2d(st, &mapAh, &full[s], kb * UK, m0);
@@ -329,13 +331,13 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
       bool ok = true;
       for (int g = 0; g < ng && ok; ++g) {
         const int b = g & 1;
-        if (!mbar_wait(&tempty[b], ((uint32_t)(g >> 1) & 1u) ^ 1u, abort)) break;
+        if (!mbar_wait(&tempty[b], ((uint32_t)(g >> 1) & 1u) ^ 1u, abort, werr)) break;
         tc_fence_after();
         const uint32_t dmain = tmem + b * 256, dcorr = dmain + 128;
         for (int j = 0; j < 2; ++j, ++kb) {
           const int s = kb % USTAGES;
           const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
-          if (!mbar_wait(&full[s], ph, abort)) {
+          if (!mbar_wait(&full[s], ph, abort, werr)) {
             ok = false;
             break;
           }
@@ -533,8 +535,14 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
   const size_t smem = exact ? umma_smem<true>() : umma_smem<false>();
   e = allow_smem((const void*)kern, smem);
   if (e != cudaSuccess) return e;
+  int* werr = gs.werr;
+  if (!werr) {
+    e = umma_error_ptr(&werr);
+    if (e != cudaSuccess) return e;
+  }
   dim3 grid((nrows + UN - 1) / UN, (M + UM - 1) / UM);
-  kern<<<grid, UTHREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy, row0, nrows);
+  kern<<<grid, UTHREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy, row0, nrows,
+                                     werr);
   return cudaGetLastError();
 }
 
