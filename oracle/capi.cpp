@@ -2,6 +2,7 @@
 // by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg only.
 #include <omp.h>
 
+#include <cmath>
 #include <cstring>
 #include <string>
 
@@ -287,6 +288,36 @@ size_t orc_decode_step(void* mp, void* sp, uint32_t tok, float* logits) {
   std::memcpy(logits, r.data(), r.size() * 4);
   return r.size();
 }
+// SplitMix64::next_u64 (crates/needle-infer/src/v3_engine.rs:446-459).
+uint64_t orc_splitmix64_next(uint64_t* state) {
+  *state += 0x9E3779B97F4A7C15ull;
+  uint64_t z = *state;
+  z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+  z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+  return z ^ (z >> 31);
+}
+// SplitMix64::next_f64 (v3_engine.rs:461-463): the top 53 bits over 2^53.
+double orc_splitmix64_next_f64(uint64_t* state) {
+  return (double)(orc_splitmix64_next(state) >> 11) / (double)(1ull << 53);
+}
+// sample (v3_engine.rs:422-443): softmax weights exp((v - max) / T) in f32,
+// summed in f64; the first index whose running subtraction from
+// next_f64 * sum reaches <= 0, else the last index.
+uint32_t orc_sample(const float* logits, size_t n, float temperature, uint64_t* state) {
+  const float inv = 1.0f / temperature;
+  float mx = -INFINITY;
+  for (size_t i = 0; i < n; ++i)
+    if (logits[i] > mx) mx = logits[i];
+  double sum = 0.0;
+  for (size_t i = 0; i < n; ++i) sum += (double)std::exp((logits[i] - mx) * inv);
+  double target = orc_splitmix64_next_f64(state) * sum;
+  for (size_t i = 0; i < n; ++i) {
+    target -= (double)std::exp((logits[i] - mx) * inv);
+    if (target <= 0.0) return (uint32_t)i;
+  }
+  return (uint32_t)(n - 1);
+}
+
 void orc_forward_sequence(void* mp, const uint32_t* ids, size_t n, float* logits) {
   std::vector<float> r = ((V3Model*)mp)->forward_sequence(ids, n);
   std::memcpy(logits, r.data(), r.size() * 4);

@@ -54,6 +54,9 @@ def lib():
             ("orc_model_kv_bytes", sz, [vp, sz, C.c_int]),
             ("orc_max_threads", C.c_int, []),
             ("orc_ngram_valid", C.c_int, [sz, sz, vp, sz, sz]),
+            ("orc_splitmix64_next", C.c_uint64, [vp]),
+            ("orc_splitmix64_next_f64", C.c_double, [vp]),
+            ("orc_sample", C.c_uint32, [vp, sz, C.c_float, vp]),
         ]:
             f = getattr(_lib, name)
             f.restype, f.argtypes = res, args
@@ -171,6 +174,25 @@ def attend(q, seq, heads, kv_heads, qk, vh, window, k=None, v=None, kq=None, ks=
     lib().orc_attend(P(q), p(k), p(v), p(kq), p(ks), p(vq), p(vs), C.c_size_t(seq), C.c_size_t(heads),
                      C.c_size_t(kv_heads), C.c_size_t(qk), C.c_size_t(vh), C.c_size_t(window), P(out))
     return out
+
+
+class SplitMix64:
+    """The reference's sampling RNG (v3_engine.rs:446-464), in the oracle."""
+
+    def __init__(self, seed: int):
+        self.state = C.c_uint64(seed)
+
+    def next_u64(self) -> int:
+        return int(lib().orc_splitmix64_next(C.byref(self.state)))
+
+    def next_f64(self) -> float:
+        return float(lib().orc_splitmix64_next_f64(C.byref(self.state)))
+
+
+def sample(logits, temperature: float, rng: SplitMix64) -> int:
+    """sample (v3_engine.rs:422-443): one draw from softmax(logits / T)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    return int(lib().orc_sample(P(lg), len(lg), C.c_float(temperature), C.byref(rng.state)))
 
 
 def engram_indices(tokens, orders, heads, slots, seed_heads=0):
