@@ -25,6 +25,7 @@ import hashlib
 import json
 import os
 import sys
+import tempfile
 
 import numpy as np
 
@@ -61,11 +62,12 @@ def main(ref_root):
     for name, geom, seed, T, keep_rows in (("tiny", cact_pack.tiny(), 1, 20, None),
                                            ("full", cact_pack.shipped(), 0, 16, [0, 7, 15])):
         raw = cact_pack.build_container(geom, seed=seed)
-        path = os.path.join("/tmp", f"golden_{name}.cact")
-        with open(path, "wb") as f:
-            f.write(raw)
-        toks = np.random.default_rng(seed).integers(1, geom.vocab_size, T).astype(np.int64)
-        logits = ref.Model(path).forward(toks).astype(np.float32)
+        with tempfile.TemporaryDirectory() as tmp:
+            path = os.path.join(tmp, f"golden_{name}.cact")
+            with open(path, "wb") as f:
+                f.write(raw)
+            toks = np.random.default_rng(seed).integers(1, geom.vocab_size, T).astype(np.int64)
+            logits = ref.Model(path).forward(toks).astype(np.float32)
         rows = list(range(T)) if keep_rows is None else keep_rows
         np.savez_compressed(os.path.join(HERE, f"numpy_ref_{name}.npz"), tokens=toks.astype(np.uint32),
                             rows=np.array(rows), logits=logits[rows], argmax=logits.argmax(-1),
@@ -74,4 +76,6 @@ def main(ref_root):
 
 
 if __name__ == "__main__":
-    main(sys.argv[1] if len(sys.argv) > 1 else "/root/reference")
+    if len(sys.argv) != 2:
+        sys.exit("usage: make_golden.py <path of the needle-rs checkout>")
+    main(sys.argv[1])
