@@ -32,7 +32,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 PKG_DIR = os.path.join(ROOT, "needle-rs_b200")
 PEAKS = os.path.join(ROOT, "MEASURED_PEAKS.json")
 METRIC = "decode tok/s (config 4: batched int8-KV sessions, 1024-token prompts)"
-HBM_FALLBACK, BF16_FALLBACK = 6650.0, 1590.0
+HBM_FALLBACK, BF16_FALLBACK, BF16_SUSTAINED_FALLBACK = 6650.0, 1590.0, 1400.0
 
 
 def pkg():
@@ -61,11 +61,13 @@ def container(seed: int = 0) -> bytes:
 
 
 def peaks():
+    """(HBM GB/s, bf16 TFLOP/s burst, bf16 TFLOP/s sustained, source)."""
     if os.path.exists(PEAKS):
         with open(PEAKS) as f:
             p = json.load(f)
-        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
-    return HBM_FALLBACK, BF16_FALLBACK, "fallback"
+        return (float(p["hbm_gbs"]), float(p["bf16_tflops"]),
+                float(p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured")
+    return HBM_FALLBACK, BF16_FALLBACK, BF16_SUSTAINED_FALLBACK, "fallback"
 
 
 def prompt(i: int, n: int) -> np.ndarray:
@@ -470,6 +472,56 @@ def attn_bytes_per_step(cfg, n_sessions, pos):
     return total
 
 
+def step_rooflines(cfg, prof, n_rows, pos, hbm, tflops_sustained):
+    """A roofline entry per kernel group of one decode step of n_rows sessions
+    at position pos (the shipped geometry): algorithmic work per step (HBM bytes
+    for the row kernels and attention, 2*M*N*K FLOPs for the projections), the
+    achieved rate from the group's measured milliseconds, and the fraction of
+    the measured peak (HBM copy rate; sustained bf16 rate for the projections,
+    which run inside a long step)."""
+    L, d, n = cfg["layers"], cfg["d_model"], cfg["lanes"]
+    H, KVH, QK, VH = cfg["heads"], cfg["kv_heads"], cfg["qk_head_dim"], cfg["v_head_dim"]
+    q_dim, k_dim, v_dim = H * QK, KVH * QK, KVH * VH
+    proj_dim = q_dim + k_dim + v_dim + H * VH  # q | k | v | output gate
+    taps = cfg["conv_taps"]
+    sites = 5  # Engram sites of the shipped geometry
+    lane_b = n * d * 4
+    per_row = {
+        # (kind, amount per row per step)
+        "engram": ("tensor", sites * 2 * (2 * d) * d),
+        "embed": ("hbm", d // 2 + (d // 128) * 2 + lane_b),
+        # lanes in; u, bx, xh, gates out; Engram key and value in at the sites
+        "layer_pre": ("hbm", L * (lane_b + 3 * d * 4 + 24 * 4) + sites * 2 * d * 4),
+        "qkvg_proj": ("tensor", L * 2 * proj_dim * d),
+        # raw q|k|v in, taps - 1 conv tail rows in and one out, q (f32 and int8 codes + scales) out,
+        # the int8 K/V append
+        "qkv_post": ("hbm", L * ((q_dim + k_dim + v_dim) * 4 * (1 + taps)
+                                 + q_dim * 5 + H * 4 + KVH * (QK + VH + 8))),
+        "attention": ("hbm", attn_bytes_per_step(cfg, 1, pos)),
+        "out_proj": ("tensor", L * 2 * d * d),
+        # attention output, u, bx and gates in; lanes in and out
+        "layer_post": ("hbm", L * (3 * d * 4 + 24 * 4 + 2 * lane_b)),
+        "final": ("hbm", lane_b + d * 4),
+        "lm_head": ("tensor", 2 * cfg["logit_rows"] * d),
+    }
+    out = {}
+    for kind, (bound, amount) in per_row.items():
+        ms = prof.get(kind, 0.0)
+        if ms <= 0:
+            continue
+        total = amount * n_rows
+        if bound == "hbm":
+            ach = total / (ms * 1e-3) / 1e9
+            out[kind] = {"ms": round(ms, 4), "bound": "hbm", "algorithmic_bytes": int(total),
+                         "achieved": round(ach, 1), "unit": "GB/s", "peak": hbm, "frac": round(ach / hbm, 4)}
+        else:
+            ach = total / (ms * 1e-3) / 1e12
+            out[kind] = {"ms": round(ms, 4), "bound": "tensor", "algorithmic_flop": int(total),
+                         "achieved": round(ach, 1), "unit": "TFLOP/s", "peak": tflops_sustained,
+                         "frac": round(ach / tflops_sustained, 4)}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -564,7 +616,7 @@ def main():
         _, toks = eng.decode_batch(sessions, toks, logits=False)
     e2e_s = max_over_ranks(time.perf_counter() - t0, dist, "cuda")
     e2e = args.sessions * args.steps / e2e_s
-    hbm, bf16, src = peaks()
+    hbm, bf16, bf16_sus, src = peaks()
     attn_ms = prof["attention"] / geo["layers"]
     abytes = attn_bytes_per_step(geo, per, pos_now) / geo["layers"]
     achieved = abytes / (attn_ms * 1e-3) / 1e9
@@ -602,6 +654,7 @@ def main():
                      "launch_ms": round(attn_ms, 4)},
         "profile_ms_per_step": {k: round(v, 4) for k, v in prof.items()},
         "profile_share": {k: round(v / total_prof, 4) for k, v in prof.items()} if total_prof else {},
+        "kernel_rooflines": step_rooflines(geo, prof, per, pos_now, hbm, bf16_sus),
         "e2e": {"value": round(e2e, 1), "unit": "tok/s", "h2d_bytes_per_step": 4 * per,
                 "d2h_bytes_per_step": 4 * per},
         "gpu_launches": launches * args.steps,

@@ -430,10 +430,12 @@ __device__ __forceinline__ float ex2_fast(float x) {
 }
 
 // Transpose of an 8x8 b16 matrix held in the accumulator-fragment layout
-// (lane 4r + c/2 holds row r, columns c and c + 1).
+// (lane 4r + c/2 holds row r, columns c and c + 1). A register-only
+// operation, so it is not volatile: the scheduler may interleave it with the
+// value-fragment loads and conversions of the same block.
 __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   uint32_t y;
-  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
+  asm("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(y) : "r"(x));
   return y;
 }
 
@@ -511,13 +513,28 @@ __device__ __forceinline__ bool mbar_try_parity(uint64_t* bar, uint32_t parity) 
   return ok != 0;
 }
 
+// try_wait that may suspend the thread until the phase completes, for at most
+// `hint_ns` (the hardware wakes it at completion), so a waiting warp issues no
+// polling instructions meanwhile.
+__device__ __forceinline__ bool mbar_try_parity_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // Wait for phase `parity` of `bar`, giving up after ATTN_WAIT_NS.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity) {
   if (mbar_try_parity(bar, parity)) return true;
   unsigned long long t0, t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
   while (true) {
-    if (mbar_try_parity(bar, parity)) return true;
+    if (mbar_try_parity_sleep(bar, parity, 20000u)) return true;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     if (t - t0 > ATTN_WAIT_NS) return false;
   }

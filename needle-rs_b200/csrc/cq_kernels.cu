@@ -13,6 +13,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cmath>
 
 #include "common.cuh"
 #include "kernels.hpp"
@@ -298,6 +299,413 @@ constexpr size_t G1_MAX_TABLE_BYTES = 100 * 1024;
 constexpr int G1_MIN_ROWS = 16384;
 
 // ----------------------------------------------------------------------------
+// Tensor-core GEMV: up to 8 activation rows on mma.sync m16n8k16 (f16 x f16
+// -> f32), for codebooks whose levels (times a power of two) are f16 values.
+//
+// A warp owns tiles of 16 weight rows. Per 128-element quantisation group
+// (cq.rs:666-672) it issues 8 MMAs of K = 16 into a fresh accumulator and adds
+// norm * accumulator to an f32 total, so the tensor cores never accumulate
+// across more than one group. The A operand is the levels of the packed
+// codes, decoded in registers straight from the `.cact` bytes:
+//   * 2-bit: half the bytes by byte_perm - a selector-byte table held in a
+//     register maps four 2-bit codes at once to the byte selectors of their
+//     f16 levels, and a second byte_perm picks two levels out of the 8-byte
+//     level table (about 1.3 integer instructions per code) - and half by a
+//     256-entry table of level quads (one 8-byte entry per packed byte, 16
+//     copies so that each half-warp reads its own banks). The integer pipe
+//     runs logical and permute instructions at half rate, and a table costs
+//     shared-memory bandwidth per decoded value; splitting the decode between
+//     them loads both pipes;
+//   * 4-bit: a 256-entry table of level pairs (one f16x2 per packed byte),
+//     replicated per lane so that every lane reads its own bank.
+// The K order inside a group is the one the decode produces (the sum over a
+// group does not depend on it); the activation is staged once per CTA in
+// shared memory in that order, as the B fragments of each group and K step.
+// The B operand's 8 columns carry each activation row split into an f16 high
+// part and remainder (row scaled by a power of two first), so one MMA yields
+// both halves: column 2m is x_hi * level, column 2m + 1 is x_lo * level, and
+// every product is exact in f32 (about 22 bits of the activation kept).
+// ----------------------------------------------------------------------------
+constexpr int TG_THREADS = 128;
+constexpr int TG_CTAS_PER_SM = 5;
+
+template <int BITS>
+struct TcTraits;
+template <>
+struct TcTraits<2> {
+  static constexpr int GB = 4;     // groups per work item
+  static constexpr int BYTES = 8;  // packed bytes of one group per lane and row
+};
+template <>
+struct TcTraits<4> {
+  static constexpr int GB = 2;
+  static constexpr int BYTES = 16;
+};
+
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+// Sixteen 2-bit codes c0..c15 of `w` (LSB first) -> eight f16x2 level pairs,
+// in the order (c0,c2) (c4,c6) (c8,c10) (c12,c14) (c1,c3) (c5,c7) (c9,c11)
+// (c13,c15). `la` holds the f16 levels 0 and 1, `lb` levels 2 and 3. The
+// selector bytes of level c are (2c, 2c+1) = 34c + 16, which byte_perm reads
+// out of 0x76543210 with the code itself as the selector nibble.
+__device__ __forceinline__ void decode2(uint32_t w, uint32_t la, uint32_t lb, uint32_t (&v)[8]) {
+  const uint32_t e = w & 0x33333333u, o = (w >> 2) & 0x33333333u;
+  const uint32_t win[4] = {e, e >> 16, o, o >> 16};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const uint32_t s = __byte_perm(0x76543210u, 0u, win[i]);
+    v[2 * i] = __byte_perm(la, lb, s);
+    v[2 * i + 1] = __byte_perm(la, lb, s >> 16);
+  }
+}
+
+// Offset inside the lane's 32 codes of a group (2-bit: the lane's 8 packed
+// bytes, two words of 16 codes) of element e (0..3 = a0.lo, a0.hi, a2.lo,
+// a2.hi) of K step j: decode2's order for a word decoded by byte_perm (steps
+// 0..3 always, steps 4..7 when `table` is false), the codes of byte j - 4 of
+// the second word in order when it is decoded through the table.
+__host__ __device__ __forceinline__ int tc_code_offset(int bits, int j, int e, bool table) {
+  if (bits == 4 || (table && j >= 4)) return 4 * j + e;
+  const int s = j & 3;
+  return 16 * (j >> 2) + (s >> 1) + 8 * (s & 1) + 2 * e;
+}
+
+// The codebook levels times 2^le as f16 bit patterns, two per word (level 2i
+// in the low half of h[i]).
+struct TcLevels {
+  uint32_t h[8];
+};
+
+// f16 high part (h = 0) or remainder (h = 1) of x.
+__device__ __forceinline__ uint32_t f16_part(float x, int h) {
+  const __half hi = __float2half_rn(x);
+  return h ? (uint32_t)__half_as_ushort(__float2half_rn(x - __half2float(hi))) : (uint32_t)__half_as_ushort(hi);
+}
+
+// SPLIT = false: warps own whole tiles (warp-strided over the matrix), GB
+// consecutive groups per work item. SPLIT = true (small matrices, where the
+// latency of one warp walking every group of a tile dominates): a CTA owns a
+// tile, warp w takes groups w, w + 4, ... (GB of them per item, the same item
+// count for every warp) and the four partial sums meet in shared memory in a
+// fixed order.
+template <int BITS, int NT, bool SPLIT>
+__global__ void __launch_bounds__(TG_THREADS) cq_gemv_tc_kernel(CqMat W, const float* __restrict__ xh, int ldx,
+                                                                int M, float* __restrict__ y, int ldy, int row0,
+                                                                int nrows, TcLevels L, float lsinv) {
+  using T = TcTraits<BITS>;
+  constexpr int GB = T::GB;
+  constexpr int NWARP = TG_THREADS / 32;
+  constexpr int GSTEP = SPLIT ? NWARP : 1;  // group stride between the slots of an item
+  constexpr int NW = T::BYTES / 4;  // packed words per lane, row and group
+  extern __shared__ __align__(16) unsigned char tsm[];
+  // [ng][8][NT][32] B fragments, then (4-bit) the level-pair table [256][32].
+  uint2* bs = reinterpret_cast<uint2*>(tsm);
+  __shared__ float xsc[8], xinv[8];                // row scales (CTA-wide form)
+  __shared__ float xsc_w[SPLIT ? 4 : 1][8], xinv_w[SPLIT ? 4 : 1][8];  // per warp (split form)
+  const uint32_t la = L.h[0], lb = L.h[1];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int c = lane & 3;
+  const int ng = W.groups;
+  uint32_t* ptab = reinterpret_cast<uint32_t*>(tsm + (size_t)ng * 8 * NT * 32 * sizeof(uint2));
+  const int ntiles = (nrows + 15) >> 4;
+  const int wstride = SPLIT ? gridDim.x : gridDim.x * NWARP;
+  const int nit = SPLIT ? (ng + GB * NWARP - 1) / (GB * NWARP) : (ng + GB - 1) / GB;  // items per tile
+  auto item_g0 = [&](int it) { return SPLIT ? warp + it * GB * NWARP : it * GB; };  // group of slot 0
+  __shared__ float red[SPLIT ? NWARP : 1][32][4];
+
+  // Rows g and g + 8 of tile t (null when outside the matrix).
+  struct Rows {
+    const uint8_t* p[2];
+    const __half* n[2];
+  };
+  auto rows_of = [&](int t, Rows& R) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = t * 16 + (lane >> 2) + 8 * h;
+      R.p[h] = nullptr;
+      R.n[h] = nullptr;
+      if (t < ntiles && r < nrows) {
+        int local;
+        const int s = find_seg(W, row0 + r, &local);
+        R.p[h] = W.seg[s].packed + (size_t)local * W.row_bytes;
+        R.n[h] = W.seg[s].norms + (size_t)local * W.groups;
+      }
+    }
+  };
+  // This lane's packed words of groups gb + q * GSTEP (q < GB) for both rows,
+  // and (lane c < GB) the norms of group gb + c * GSTEP.
+  auto load_item = [&](const Rows& R, int gb, uint32_t (&w)[GB][2][NW], float (&nv)[2]) {
+#pragma unroll
+    for (int q = 0; q < GB; ++q)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int G = gb + q * GSTEP;
+        const bool ok = R.p[h] && G < ng;
+        const uint8_t* src = ok ? R.p[h] + (size_t)G * (128 * BITS / 8) + c * T::BYTES : nullptr;
+        if constexpr (BITS == 2) {
+          const uint2 v = ok ? __ldg(reinterpret_cast<const uint2*>(src)) : make_uint2(0u, 0u);
+          w[q][h][0] = v.x;
+          w[q][h][1] = v.y;
+        } else {
+          const uint4 v = ok ? __ldg(reinterpret_cast<const uint4*>(src)) : make_uint4(0u, 0u, 0u, 0u);
+          w[q][h][0] = v.x;
+          w[q][h][1] = v.y;
+          w[q][h][2] = v.z;
+          w[q][h][3] = v.w;
+        }
+      }
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+      nv[h] = (R.p[h] && c < GB && gb + c * GSTEP < ng) ? __half2float(R.n[h][gb + c * GSTEP]) : 0.f;
+  };
+
+  // 1. the first work item's weights, before waiting for the activation
+  int tile = SPLIT ? blockIdx.x : blockIdx.x * NWARP + warp;
+  Rows cur;
+  rows_of(tile, cur);
+  uint32_t cw[GB][2][NW];
+  float cn[2];
+  load_item(cur, item_g0(0), cw, cn);
+  auto lev = [&](int i) { return (L.h[i >> 1] >> (16 * (i & 1))) & 0xFFFFu; };
+  if constexpr (BITS == 4) {
+    // Level pair of every packed byte (low nibble = the lower K index), one
+    // copy per lane: entry b of lane l at word b * 32 + l, in bank l.
+    for (int i = threadIdx.x; i < 256 * 32; i += TG_THREADS) {
+      const int b = i >> 5;
+      ptab[i] = lev(b & 15) | (lev(b >> 4) << 16);
+    }
+    if (SPLIT) __syncthreads();  // the split form has no CTA barrier before its tiles
+  } else if (!SPLIT) {
+    // Level quad of every packed byte (codes in K order as two f16x2), 16
+    // copies: entry b of copy c at uint2 b * 16 + c, banks 2c and 2c + 1; the
+    // two half-warps of an 8-byte access are served separately, lane l uses
+    // copy l % 16.
+    uint2* qtab = reinterpret_cast<uint2*>(ptab);
+    for (int i = threadIdx.x; i < 256 * 16; i += TG_THREADS) {
+      const int b = i >> 4;
+      qtab[i] = make_uint2(lev(b & 3) | (lev((b >> 2) & 3) << 16), lev((b >> 4) & 3) | (lev(b >> 6) << 16));
+    }
+  }
+  // 2. the activation rows: power-of-two row scales, then the B fragments
+  // (split form: each warp the rows' scales and its own groups' fragments,
+  // with no CTA barrier before its first tile)
+  pdl_wait();
+  float* xscw = SPLIT ? xsc_w[warp] : xsc;
+  float* xinvw = SPLIT ? xinv_w[warp] : xinv;
+  for (int m = SPLIT ? 0 : warp; m < M; m += SPLIT ? 1 : NWARP) {
+    float amax = 0.f;
+    for (int k = lane * 4; k < W.in_pad; k += 128) {
+      const float4 v = *reinterpret_cast<const float4*>(xh + (size_t)m * ldx + k);
+      amax = fmaxf(amax, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+    }
+    amax = warp_max(amax);
+    if (lane == 0) {
+      int e = 0;
+      if (amax > 0.f && isfinite(amax)) {
+        frexpf(amax, &e);
+        e = 14 - e;
+      }
+      xscw[m] = ldexpf(1.f, e);
+      xinvw[m] = ldexpf(1.f, -e);
+    }
+  }
+  if (SPLIT)
+    __syncwarp();
+  else
+    __syncthreads();
+  // Fragment slots (G, nt, lane): the lane's 32-element window of group G for
+  // activation row m, loaded as eight independent float4 reads, gives its B
+  // fragments of all 8 K steps. The split form fills the slots of its own
+  // groups (warp, warp + 4, ...) itself.
+  const int nslot = SPLIT ? ((ng - warp + NWARP - 1) / NWARP) * NT * 32 : ng * NT * 32;
+  for (int i = SPLIT ? lane : (int)threadIdx.x; i < nslot; i += SPLIT ? 32 : TG_THREADS) {
+    const int ln = i & 31, nt = (i >> 5) % NT;
+    const int G = SPLIT ? warp + ((i >> 5) / NT) * NWARP : (i >> 5) / NT;
+    const int n = ln >> 2, m = nt * 4 + (n >> 1), h = n & 1;
+    uint2* dst = bs + (size_t)G * 8 * NT * 32 + nt * 32 + ln;
+    if (m >= M) {  // unused column: zero, so every lane loads its fragments unconditionally
+#pragma unroll
+      for (int j = 0; j < 8; ++j) dst[j * NT * 32] = make_uint2(0u, 0u);
+      continue;
+    }
+    const float4* xr = reinterpret_cast<const float4*>(xh + (size_t)m * ldx + G * 128 + 32 * (ln & 3));
+    float xv[32];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const float4 v = xr[k];
+      xv[4 * k] = v.x;
+      xv[4 * k + 1] = v.y;
+      xv[4 * k + 2] = v.z;
+      xv[4 * k + 3] = v.w;
+    }
+    const float sc = xscw[m];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const uint32_t v0 = f16_part(xv[tc_code_offset(BITS, j, 0, !SPLIT)] * sc, h);
+      const uint32_t v1 = f16_part(xv[tc_code_offset(BITS, j, 1, !SPLIT)] * sc, h);
+      const uint32_t v2 = f16_part(xv[tc_code_offset(BITS, j, 2, !SPLIT)] * sc, h);
+      const uint32_t v3 = f16_part(xv[tc_code_offset(BITS, j, 3, !SPLIT)] * sc, h);
+      dst[j * NT * 32] = make_uint2(v0 | (v1 << 16), v2 | (v3 << 16));
+    }
+  }
+  if (SPLIT)
+    __syncwarp();
+  else
+    __syncthreads();
+  pdl_trigger();
+
+  // 3. tiles: warp-strided, GB groups per step, the next step's words in flight
+  const uint32_t* ptl = ptab + lane;
+  const uint2* qtl = reinterpret_cast<const uint2*>(ptab) + (lane & 15);
+  float tot[NT][2];
+#pragma unroll
+  for (int nt = 0; nt < NT; ++nt) tot[nt][0] = tot[nt][1] = 0.f;
+  int it = 0;
+  while (tile < ntiles) {
+    const int gb = item_g0(it);
+    int ntile = tile, nitn = it + 1;
+    Rows nxt = cur;
+    if (nitn >= nit) {
+      nitn = 0;
+      ntile = tile + wstride;
+      rows_of(ntile, nxt);
+    }
+    uint32_t nw[GB][2][NW];
+    float nn[2];
+    load_item(nxt, item_g0(nitn), nw, nn);
+    float acc[GB][NT][4];
+#pragma unroll
+    for (int q = 0; q < GB; ++q)
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) acc[q][nt][0] = acc[q][nt][1] = acc[q][nt][2] = acc[q][nt][3] = 0.f;
+#pragma unroll
+    for (int q = 0; q < GB; ++q) {
+      if (gb + q * GSTEP >= ng) break;
+      const uint2* bg = bs + (size_t)(gb + q * GSTEP) * 8 * NT * 32 + lane;
+      if constexpr (BITS == 2) {
+        {  // word 0: byte_perm decode, K steps 0..3
+          uint32_t va[8], vb[8];
+          decode2(cw[q][0][0], la, lb, va);
+          decode2(cw[q][1][0], la, lb, vb);
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint2 b = bg[(s * NT + nt) * 32];
+              mma16816(acc[q][nt], va[2 * s], vb[2 * s], va[2 * s + 1], vb[2 * s + 1], b.x, b.y);
+            }
+          }
+        }
+        if constexpr (SPLIT) {  // word 1 by byte_perm too (no table to build: latency first)
+          uint32_t va[8], vb[8];
+          decode2(cw[q][0][1], la, lb, va);
+          decode2(cw[q][1][1], la, lb, vb);
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint2 b = bg[((4 + s) * NT + nt) * 32];
+              mma16816(acc[q][nt], va[2 * s], vb[2 * s], va[2 * s + 1], vb[2 * s + 1], b.x, b.y);
+            }
+          }
+        } else {
+#pragma unroll
+          for (int s = 0; s < 4; ++s) {  // word 1: table decode, K steps 4..7
+            const uint2 ta = qtl[__byte_perm(cw[q][0][1], 0u, 0x4440u + s) * 16];
+            const uint2 tb = qtl[__byte_perm(cw[q][1][1], 0u, 0x4440u + s) * 16];
+            const int j = 4 + s;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint2 b = bg[(j * NT + nt) * 32];
+              mma16816(acc[q][nt], ta.x, tb.x, ta.y, tb.y, b.x, b.y);
+            }
+          }
+        }
+      } else {
+#pragma unroll
+        for (int wi = 0; wi < 4; ++wi) {
+          uint32_t va[4], vb[4];
+#pragma unroll
+          for (int bt = 0; bt < 4; ++bt) {
+            va[bt] = ptl[__byte_perm(cw[q][0][wi], 0u, 0x4440u + bt) * 32];
+            vb[bt] = ptl[__byte_perm(cw[q][1][wi], 0u, 0x4440u + bt) * 32];
+          }
+#pragma unroll
+          for (int s = 0; s < 2; ++s) {
+            const int j = 2 * wi + s;
+#pragma unroll
+            for (int nt = 0; nt < NT; ++nt) {
+              const uint2 b = bg[(j * NT + nt) * 32];
+              mma16816(acc[q][nt], va[2 * s], vb[2 * s], va[2 * s + 1], vb[2 * s + 1], b.x, b.y);
+            }
+          }
+        }
+      }
+    }
+#pragma unroll
+    for (int q = 0; q < GB; ++q) {
+      if (gb + q * GSTEP >= ng) break;
+      const float n0 = __shfl_sync(0xffffffffu, cn[0], (lane & ~3) | q);
+      const float n1 = __shfl_sync(0xffffffffu, cn[1], (lane & ~3) | q);
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        tot[nt][0] += n0 * (acc[q][nt][0] + acc[q][nt][1]);
+        tot[nt][1] += n1 * (acc[q][nt][2] + acc[q][nt][3]);
+      }
+    }
+    if (it + 1 == nit) {  // the tile is complete: rows g and g + 8, activation row c (+ 4)
+      if constexpr (SPLIT) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          red[warp][lane][2 * nt] = tot[nt][0];
+          red[warp][lane][2 * nt + 1] = tot[nt][1];
+        }
+        __syncthreads();
+        if (warp == 0) {
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            tot[nt][0] = ((red[0][lane][2 * nt] + red[1][lane][2 * nt]) + red[2][lane][2 * nt]) + red[3][lane][2 * nt];
+            tot[nt][1] = ((red[0][lane][2 * nt + 1] + red[1][lane][2 * nt + 1]) + red[2][lane][2 * nt + 1]) +
+                         red[3][lane][2 * nt + 1];
+          }
+        }
+      }
+      if (!SPLIT || warp == 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          const int m = nt * 4 + c;
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const int r = tile * 16 + (lane >> 2) + 8 * h;
+            if (m < M && r < nrows) y[(size_t)m * ldy + r] = (tot[nt][h] * lsinv) * xinvw[m];
+          }
+        }
+      }
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) tot[nt][0] = tot[nt][1] = 0.f;
+      if constexpr (SPLIT) __syncthreads();  // red is rewritten for the next tile
+    }
+    tile = ntile;
+    it = nitn;
+    cur = nxt;
+#pragma unroll
+    for (int q = 0; q < GB; ++q)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+#pragma unroll
+        for (int k = 0; k < NW; ++k) cw[q][h][k] = nw[q][h][k];
+    cn[0] = nn[0];
+    cn[1] = nn[1];
+  }
+}
+
+// ----------------------------------------------------------------------------
 // SIMT GEMM for many activation rows (prefill, batched decode).
 // Tile: 64 weight rows x 64 activation rows, K stepped one quantisation group
 // (128) at a time. The group's packed bytes are decoded once into shared memory
@@ -424,6 +832,50 @@ static cudaError_t gemv_lpr(const CqMat& W, const float* xh, int ldx, int M, flo
   return launch_gemv<BITS, 32, MT>(W, xh, ldx, M, y, ldy, row0, nrows, st);
 }
 
+// The codebook levels scaled by the power of two that puts max|level| in
+// [2^13, 2^14), as f16 bit patterns, and the inverse scale; false when a
+// scaled level is not an f16 value (such codebooks take the SIMT kernels).
+static bool tc_levels(const CqMat& W, TcLevels* L, float* lsinv) {
+  const int n = 1 << W.bits;
+  float lmax = 0.f;
+  for (int i = 0; i < n; ++i) lmax = std::max(lmax, std::fabs(W.levels[i]));
+  if (!std::isfinite(lmax)) return false;
+  int le = 0;
+  if (lmax > 0.f) {
+    int e;
+    std::frexp(lmax, &e);
+    le = 14 - e;
+  }
+  *L = TcLevels{};
+  for (int i = 0; i < n; ++i) {
+    const float v = std::ldexp(W.levels[i], le);
+    const __half h = __float2half_rn(v);
+    if (__half2float(h) != v) return false;
+    L->h[i >> 1] |= (uint32_t)__half_as_ushort(h) << (16 * (i & 1));
+  }
+  *lsinv = std::ldexp(1.f, -le);
+  return true;
+}
+
+// Tiles up to which the split-group form is used: a CTA per tile while that
+// keeps under about 16 warps per SM.
+constexpr int TG_SPLIT_MAX_TILES = 148 * 4;
+
+template <int BITS, int NT>
+static cudaError_t launch_gemv_tc(const CqMat& W, const TcLevels& L, float lsinv, const float* xh, int ldx, int M,
+                                  float* y, int ldy, int row0, int nrows, cudaStream_t st) {
+  // B fragments, then the 4-bit pair table (256 x 32 words) or the 2-bit quad
+  // table (256 x 16 uint2): 32 KB either way.
+  const size_t smem = (size_t)W.groups * 8 * NT * 32 * sizeof(uint2) + 256 * 32 * 4;
+  const int ntiles = (nrows + 15) / 16;
+  const bool split = ntiles <= TG_SPLIT_MAX_TILES;
+  const int grid = split ? ntiles : std::min((ntiles + TG_THREADS / 32 - 1) / (TG_THREADS / 32), 148 * TG_CTAS_PER_SM);
+  auto kern = split ? cq_gemv_tc_kernel<BITS, NT, true> : cq_gemv_tc_kernel<BITS, NT, false>;
+  cudaError_t e = allow_smem((const void*)kern, smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(kern, dim3(grid), dim3(TG_THREADS), smem, st, W, xh, ldx, M, y, ldy, row0, nrows, L, lsinv);
+}
+
 template <int BITS>
 static cudaError_t launch_gemm_simt(const CqMat& W, const float* xh, int ldx, int M, float* y,
                                     int ldy, int row0, int nrows, cudaStream_t st) {
@@ -435,8 +887,17 @@ static cudaError_t launch_gemm_simt(const CqMat& W, const float* xh, int ldx, in
 template <int BITS>
 static cudaError_t project_bits(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
                                 int row0, int nrows, cudaStream_t st) {
-  // Large one-row products stream through the table kernel; smaller ones are
-  // latency-bound and take the kernel above, whose set-up is shorter.
+  // Up to 8 rows on the tensor cores when the levels are f16 values (the
+  // packer writes f16 codebooks); otherwise the SIMT kernels: large one-row
+  // products stream through the table kernel, smaller ones take the
+  // latency-ordered GEMV.
+  if (M <= 8) {
+    TcLevels L;
+    float lsinv;
+    if (tc_levels(W, &L, &lsinv))
+      return M <= 4 ? launch_gemv_tc<BITS, 1>(W, L, lsinv, xh, ldx, M, y, ldy, row0, nrows, st)
+                    : launch_gemv_tc<BITS, 2>(W, L, lsinv, xh, ldx, M, y, ldy, row0, nrows, st);
+  }
   if (M == 1 && nrows >= G1_MIN_ROWS && (size_t)W.in_pad * BITS / 4 * 16 * sizeof(float) <= G1_MAX_TABLE_BYTES)
     return launch_gemv1<BITS>(W, xh, y, row0, nrows, st);
   if (M <= 1) return gemv_lpr<BITS, 1>(W, xh, ldx, M, y, ldy, row0, nrows, st);

@@ -59,25 +59,27 @@ __device__ int g_umma_error;
 
 namespace {
 
-constexpr int UM = 128;          // activation rows per CTA (MMA M)
-constexpr int UN = 128;          // weight rows per CTA (MMA N)
-constexpr int UK = 64;           // K per stage: 64 f16 = one 128-byte swizzle row
-// Pipeline stages and stage bytes: the three-MMA form carries four tiles per
-// stage (A hi, A lo, B hi, B lo) in three stages; the exact-level form three
-// tiles (no B remainder) in four stages of the same shared memory, one more
-// stage of loads in flight ahead of the MMAs.
-template <bool EXACT>
+constexpr int UM = 128;  // activation rows per tile (MMA M)
+constexpr int UK = 64;   // K per stage: 64 f16 = one 128-byte swizzle row
+// Pipeline of one tile width UN (weight rows per tile, the MMA N: 128 or 192).
+// A stage holds the activation tiles (high part and remainder, [128 rows][64 k]
+// f16 each) and the level tile(s) ([UN rows][64 k] f16; remainders too unless
+// the levels are exact), in as many stages as fit 192 KB.
+template <bool EXACT, int UN>
 struct Pipe {
-  static constexpr int STAGES = EXACT ? 4 : 3;
-  static constexpr uint32_t STAGE_BYTES = (EXACT ? 3u : 4u) * 128u * 128u;
+  static constexpr uint32_t A_TILE = UM * 128;
+  static constexpr uint32_t B_TILE = UN * 128;
+  static constexpr uint32_t STAGE_BYTES = 2 * A_TILE + (EXACT ? 1u : 2u) * B_TILE;
+  static constexpr int STAGES = (192 * 1024) / STAGE_BYTES;
+  static constexpr int EPI_WARPS = UN / 16;             // lane quarter x 64-column block
+  static constexpr int THREADS = (EPI_WARPS + 2) * 32;  // + TMA / TMEM warp + MMA warp
 };
-constexpr int UGMAX = 32;        // groups of 128 supported (in_pad <= 4096)
-constexpr int UTHREADS = 320;    // warps 0-7 epilogue, 8 TMA + TMEM, 9 MMA
-constexpr uint32_t TILE = 128 * 128;        // bytes of one [128 rows][128 B] tile
-constexpr uint32_t NSM_BYTES = UGMAX * UN * 4;  // norm * level scale, [group][weight row]
-template <bool EXACT>
-constexpr size_t umma_smem() {
-  return 1024 + (size_t)Pipe<EXACT>::STAGES * Pipe<EXACT>::STAGE_BYTES + NSM_BYTES + 256;
+constexpr int UGMAX = 32;  // groups of 128 supported (in_pad <= 4096)
+// Dynamic shared memory: alignment slack, the stages, the norm table of one
+// tile ([groups][UN] f32) and the barriers.
+template <bool EXACT, int UN>
+constexpr size_t umma_smem(int groups) {
+  return 1024 + (size_t)Pipe<EXACT, UN>::STAGES * Pipe<EXACT, UN>::STAGE_BYTES + (size_t)groups * UN * 4 + 256;
 }
 constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every wait: one second
 
@@ -155,15 +157,20 @@ __device__ __forceinline__ uint64_t sw128_desc(const void* tile) {
   return start | (uint64_t)(1024 >> 4) << 32 | (uint64_t)1 << 46 | (uint64_t)2 << 61;
 }
 
-// kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both K-major.
-constexpr uint32_t IDESC = (1u << 4) | ((uint32_t)(UN >> 3) << 17) | ((uint32_t)(UM >> 4) << 24);
+// kind::f16 instruction descriptor: f32 accumulate, f16 A and B, both K-major,
+// M = 128, N = UN.
+template <int UN>
+constexpr uint32_t idesc() {
+  return (1u << 4) | ((uint32_t)(UN >> 3) << 17) | ((uint32_t)(UM >> 4) << 24);
+}
 
+template <int UN>
 __device__ __forceinline__ void umma_f16(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc, uint32_t accum) {
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(IDESC), "r"(accum));
+      "l"(adesc), "l"(bdesc), "r"(idesc<UN>()), "r"(accum));
 }
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
   asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(su32(bar))
@@ -198,28 +205,38 @@ __device__ __forceinline__ int row_exp(float amax) {
 // EXACT: every level times the level scale is an f16 value, so the level
 // remainders are zero and only x_hi * l_hi and x_lo * l_hi are issued (two
 // MMAs per K step, no remainder tile).
-template <bool EXACT>
-__global__ void __launch_bounds__(UTHREADS, 1)
+//
+// Persistent: CTA b computes tiles b, b + gridDim.x, ... of 128 activation
+// rows x UN weight rows (tile t: activation rows (t / ntn) * 128, weight rows
+// (t % ntn) * UN, so CTAs running at the same time share activation tiles in
+// L2). Every MMA of a quantisation group accumulates into one TMEM accumulator
+// of UN columns; the groups of every tile alternate between two accumulators,
+// so the epilogue drains one (its last group of a tile included) while the
+// MMAs of the next group, of this tile or the next, fill the other.
+template <bool EXACT, int UN>
+__global__ void __launch_bounds__(Pipe<EXACT, UN>::THREADS, 1)
 cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
                const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
-               int nrows, int* werr) {
-  constexpr int USTAGES = Pipe<EXACT>::STAGES;
-  constexpr uint32_t STAGE_BYTES = Pipe<EXACT>::STAGE_BYTES;
+               int nrows, int ntn, int ntiles, int* werr) {
+  using P = Pipe<EXACT, UN>;
+  constexpr int USTAGES = P::STAGES;
+  constexpr uint32_t STAGE_BYTES = P::STAGE_BYTES;
+  constexpr int EW = P::EPI_WARPS;
+  constexpr uint32_t TMEM_COLS = 2 * UN <= 256 ? 256 : 512;  // two group accumulators (a power of two)
   extern __shared__ unsigned char smraw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
-  float* nsm = reinterpret_cast<float*>(sm + USTAGES * STAGE_BYTES);
-  uint64_t* full = reinterpret_cast<uint64_t*>(sm + USTAGES * STAGE_BYTES + NSM_BYTES);  // stage landed
+  const int nk = W.in_pad / UK, ng = W.in_pad / 128;
+  float* nsm = reinterpret_cast<float*>(sm + USTAGES * STAGE_BYTES);  // [ng][UN]
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + USTAGES * STAGE_BYTES + (size_t)ng * UN * 4);
   uint64_t* empty = full + USTAGES;   // stage consumed by the MMAs
-  uint64_t* tfull = empty + USTAGES;  // [2] a group's accumulator pair is complete
-  uint64_t* tempty = tfull + 2;       // [2] the pair has been drained
+  uint64_t* tfull = empty + USTAGES;  // [2] a group's accumulator is complete
+  uint64_t* tempty = tfull + 2;       // [2] the accumulator has been drained
   uint64_t* drainb = tempty + 2;      // every MMA of the CTA has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drainb + 1);
   volatile uint32_t* abort = tmem_slot + 1;
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  const int n0 = blockIdx.x * UN, m0 = blockIdx.y * UM;
-  const int nk = W.in_pad / UK, ng = W.in_pad / 128;
 
   if (tid == 0) {
     for (int s = 0; s < USTAGES; ++s) {
@@ -227,16 +244,16 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
       mbar_init(&empty[s], 1);  // one tcgen05.commit
     }
     for (int b = 0; b < 2; ++b) {
-      mbar_init(&tfull[b], 1);   // one tcgen05.commit
-      mbar_init(&tempty[b], 8);  // the eight epilogue warps
+      mbar_init(&tfull[b], 1);    // one tcgen05.commit
+      mbar_init(&tempty[b], EW);  // the epilogue warps
     }
     mbar_init(drainb, 1);
     *abort = 0;
     asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
   }
-  if (warp == 8) {
+  if (warp == EW) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(su32(tmem_slot)),
-                 "r"(512));
+                 "r"(TMEM_COLS));
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
   }
   tc_fence_before();
@@ -244,80 +261,89 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp < 8) {
+  if (warp < EW) {
     // ------------------------------------------------ epilogue: drain each group
-    // Group norms of the tile's weight rows (times the inverse level scale),
-    // one weight row per thread, built while the first stages load; the
-    // eight epilogue warps meet on named barrier 1 before the first drain.
-    for (int nl = tid; nl < UN; nl += 256) {
-      const __half* pn = nullptr;
-      if (n0 + nl < nrows) {
-        const uint8_t* prow;
-        cq_row_ptr(W, row0 + n0 + nl, &prow, &pn);
-      }
-      for (int g = 0; g < ng; ++g) nsm[g * UN + nl] = pn ? __half2float(pn[g]) * linv : 0.f;
-    }
-    asm volatile("bar.sync 1, 256;" ::: "memory");
-    const int q = warp & 3, h = warp >> 2;  // TMEM lane quarter, column half
-    float acc[64];
-#pragma unroll
-    for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+    // Warp w reads TMEM lanes 32 * (w % 4).. (its lane quarter) and columns
+    // 64 * (w / 4).. of each accumulator.
+    const int q = warp & 3, cq = warp >> 2;
     bool ok = true;
-    for (int g = 0; g < ng; ++g) {
-      const int b = g & 1;
-      if (!mbar_wait(&tfull[b], (uint32_t)(g >> 1) & 1u, abort, werr, 128)) {
-        ok = false;
-        break;
+    int gg = 0;  // groups drained so far, over every tile of this CTA
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      const int m0 = (t / ntn) * UM, n0 = (t % ntn) * UN;
+      // Group norms of the tile's weight rows times the inverse level scale,
+      // rebuilt once every epilogue warp is done with the previous tile's.
+      asm volatile("bar.sync 1, %0;" ::"r"(EW * 32) : "memory");
+      for (int nl = tid; nl < UN; nl += EW * 32) {
+        const __half* pn = nullptr;
+        if (n0 + nl < nrows) {
+          const uint8_t* prow;
+          cq_row_ptr(W, row0 + n0 + nl, &prow, &pn);
+        }
+        for (int g = 0; g < ng; ++g) nsm[g * UN + nl] = pn ? __half2float(pn[g]) * linv : 0.f;
       }
-      tc_fence_after();
-      const uint32_t tm = tmem + ((uint32_t)(q * 32) << 16) + b * 256 + h * 64;
-      const float* ng_ = nsm + g * UN + h * 64;
+      asm volatile("bar.sync 1, %0;" ::"r"(EW * 32) : "memory");
+      float acc[64];
 #pragma unroll
-      for (int cb = 0; cb < 4; ++cb) {
-        uint32_t r[16], c[16];
-        tmem_ld16(tm + cb * 16, r);
-        tmem_ld16(tm + 128 + cb * 16, c);
-        tmem_wait_ld();
+      for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+      for (int g = 0; g < ng; ++g, ++gg) {
+        const int b = gg & 1;
+        if (ok && !mbar_wait(&tfull[b], (uint32_t)(gg >> 1) & 1u, abort, werr, 128)) ok = false;
+        if (!ok) continue;
+        tc_fence_after();
+        const uint32_t tm = tmem + ((uint32_t)(q * 32) << 16) + b * UN + cq * 64;
+        const float* ngp = nsm + g * UN + cq * 64;
 #pragma unroll
-        for (int i = 0; i < 16; ++i)
-          acc[cb * 16 + i] += ng_[cb * 16 + i] * (__uint_as_float(r[i]) + __uint_as_float(c[i]));
+        for (int cb = 0; cb < 4; ++cb) {
+          uint32_t r[16];
+          tmem_ld16(tm + cb * 16, r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; ++i) acc[cb * 16 + i] += ngp[cb * 16 + i] * __uint_as_float(r[i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
+      const int m = m0 + q * 32 + lane;
+      if (ok && m < M) {
+        const float ai = ainv[m];
+        float* yr = y + (size_t)m * ldy + n0 + cq * 64;
+        const int lim = nrows - (n0 + cq * 64);
+        const bool vec = lim >= 64 && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
+        if (vec) {
+#pragma unroll
+          for (int i = 0; i < 64; i += 4)
+            *reinterpret_cast<float4*>(yr + i) =
+                make_float4(acc[i] * ai, acc[i + 1] * ai, acc[i + 2] * ai, acc[i + 3] * ai);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i < lim) yr[i] = acc[i] * ai;
+        }
+      }
     }
-    const int m = m0 + q * 32 + lane;
-    if (ok && m < M) {
-      const float ai = ainv[m];
-      float* yr = y + (size_t)m * ldy + n0 + h * 64;
-      const int lim = nrows - (n0 + h * 64);
-      const bool vec = lim >= 64 && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
-      if (vec) {
-#pragma unroll
-        for (int i = 0; i < 64; i += 4)
-          *reinterpret_cast<float4*>(yr + i) =
-              make_float4(acc[i] * ai, acc[i + 1] * ai, acc[i + 2] * ai, acc[i + 3] * ai);
-      } else {
-#pragma unroll
-        for (int i = 0; i < 64; ++i)
-          if (i < lim) yr[i] = acc[i] * ai;
-      }
-    }
-  } else if (warp == 8) {
+  } else if (warp == EW) {
     // ------------------------------------------------ operand producer (TMA)
     if (lane == 0) {
       int issued = 0;
-      for (int kb = 0; kb < nk; ++kb) {
-        const int s = kb % USTAGES;
-        const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort, werr)) break;
-        unsigned char* st = sm + s * STAGE_BYTES;
-        mbar_arrive_tx(&full[s], (EXACT ? 3 : 4) * TILE);
-        tma_load_2d(st, &mapAh, &full[s], kb * UK, m0);
-        tma_load_2d(st + TILE, &mapAl, &full[s], kb * UK, m0);
-        tma_load_2d(st + 2 * TILE, &mapBh, &full[s], kb * UK, n0);
-        if (!EXACT) tma_load_2d(st + 3 * TILE, &mapBl, &full[s], kb * UK, n0);
-        ++issued;
+      bool ok = true;
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+        const int m0 = (t / ntn) * UM, n0 = (t % ntn) * UN;
+        for (int kb = 0; kb < nk; ++kb) {
+          const int s = issued % USTAGES;
+          const uint32_t ph = (uint32_t)(issued / USTAGES) & 1u;
+          if (!mbar_wait(&empty[s], ph ^ 1u, abort, werr)) {
+            ok = false;
+            break;
+          }
+          unsigned char* st = sm + s * STAGE_BYTES;
+          mbar_arrive_tx(&full[s], STAGE_BYTES);
+          tma_load_2d(st, &mapAh, &full[s], kb * UK, m0);
+          tma_load_2d(st + P::A_TILE, &mapAl, &full[s], kb * UK, m0);
+          tma_load_2d(st + 2 * P::A_TILE, &mapBh, &full[s], kb * UK, n0);
+          if (!EXACT) tma_load_2d(st + 2 * P::A_TILE + P::B_TILE, &mapBl, &full[s], kb * UK, n0);
+          ++issued;
+        }
       }
       if (*abort) {  // let the copies already issued land before the CTA exits
         for (int kb = issued - USTAGES > 0 ? issued - USTAGES : 0; kb < issued; ++kb)
@@ -327,39 +353,39 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   } else {
     // ------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int kb = 0;
+      int kb = 0, gg = 0;
       bool ok = true;
-      for (int g = 0; g < ng && ok; ++g) {
-        const int b = g & 1;
-        if (!mbar_wait(&tempty[b], ((uint32_t)(g >> 1) & 1u) ^ 1u, abort, werr)) break;
-        tc_fence_after();
-        const uint32_t dmain = tmem + b * 256, dcorr = dmain + 128;
-        for (int j = 0; j < 2; ++j, ++kb) {
-          const int s = kb % USTAGES;
-          const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
-          if (!mbar_wait(&full[s], ph, abort, werr)) {
+      for (int t = blockIdx.x; ok && t < ntiles; t += gridDim.x) {
+        for (int g = 0; g < ng && ok; ++g, ++gg) {
+          const int b = gg & 1;
+          if (!mbar_wait(&tempty[b], ((uint32_t)(gg >> 1) & 1u) ^ 1u, abort, werr)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          unsigned char* st = sm + s * STAGE_BYTES;
-          const uint64_t dah = sw128_desc(st), dal = sw128_desc(st + TILE);
-          const uint64_t dbh = sw128_desc(st + 2 * TILE), dbl = sw128_desc(st + 3 * TILE);
-#pragma unroll
-          for (int kk = 0; kk < UK / 16; ++kk) {
-            const uint64_t o = (uint64_t)(kk * 2);  // 32 bytes along K, in 16-byte units
-            const uint32_t acc = (j | kk) != 0;     // a group starts from zero
-            umma_f16(dmain, dah + o, dbh + o, acc);
-            if (EXACT) {
-              umma_f16(dcorr, dal + o, dbh + o, acc);
-            } else {
-              umma_f16(dcorr, dah + o, dbl + o, acc);
-              umma_f16(dcorr, dal + o, dbh + o, 1);
+          const uint32_t d = tmem + b * UN;
+          for (int j = 0; j < 2; ++j, ++kb) {
+            const int s = kb % USTAGES;
+            const uint32_t ph = (uint32_t)(kb / USTAGES) & 1u;
+            if (!mbar_wait(&full[s], ph, abort, werr)) {
+              ok = false;
+              break;
             }
+            tc_fence_after();
+            unsigned char* st = sm + s * STAGE_BYTES;
+            const uint64_t dah = sw128_desc(st), dal = sw128_desc(st + P::A_TILE);
+            const uint64_t dbh = sw128_desc(st + 2 * P::A_TILE), dbl = sw128_desc(st + 2 * P::A_TILE + P::B_TILE);
+#pragma unroll
+            for (int kk = 0; kk < UK / 16; ++kk) {
+              const uint64_t o = (uint64_t)(kk * 2);  // 32 bytes along K, in 16-byte units
+              umma_f16<UN>(d, dah + o, dbh + o, (j | kk) != 0);  // a group starts from zero
+              umma_f16<UN>(d, dal + o, dbh + o, 1);
+              if (!EXACT) umma_f16<UN>(d, dah + o, dbl + o, 1);
+            }
+            umma_commit(&empty[s]);
           }
-          umma_commit(&empty[s]);
+          if (ok) umma_commit(&tfull[b]);
         }
-        if (ok) umma_commit(&tfull[b]);
       }
       // Every issued MMA completes before TMEM is freed.
       umma_commit(drainb);
@@ -368,9 +394,9 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 8) {
+  if (warp == EW) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512));
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(TMEM_COLS));
   }
 }
 
@@ -469,17 +495,36 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// Tensor map of an f16 [M][K] row-major array: box [128 rows][64 k], 128-byte swizzle.
-bool make_map(CUtensorMap* map, const __half* base, int M, int K) {
+// Tensor map of an f16 [M][K] row-major array: box [box_rows rows][64 k], 128-byte swizzle.
+bool make_map(CUtensorMap* map, const __half* base, int M, int K, int box_rows) {
   auto fn = encode_fn();
   if (!fn) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
   const cuuint64_t strides[1] = {(cuuint64_t)K * 2};
-  const cuuint32_t box[2] = {(cuuint32_t)UK, (cuuint32_t)UM};
+  const cuuint32_t box[2] = {(cuuint32_t)UK, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<__half*>(base), dims, strides, box, estr,
             CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <bool EXACT, int UN>
+cudaError_t launch_umma(const CqMat& W, const GemmScratch& gs, float linv, int M, float* y, int ldy, int row0,
+                        int nrows, int* werr, cudaStream_t st) {
+  const int K = W.in_pad;
+  CUtensorMap mah, mal, mbh, mbl;
+  if (!make_map(&mah, gs.hi, M, K, UM) || !make_map(&mal, gs.lo, M, K, UM) || !make_map(&mbh, gs.whi, nrows, K, UN) ||
+      !make_map(&mbl, gs.wlo, nrows, K, UN))
+    return cudaErrorNotSupported;
+  auto kern = cq_umma_kernel<EXACT, UN>;
+  const size_t smem = umma_smem<EXACT, UN>(K / 128);
+  cudaError_t e = allow_smem((const void*)kern, smem);
+  if (e != cudaSuccess) return e;
+  const int ntn = (nrows + UN - 1) / UN, ntiles = ntn * ((M + UM - 1) / UM);
+  const int grid = std::min(ntiles, 148);  // persistent: one CTA per SM
+  kern<<<grid, Pipe<EXACT, UN>::THREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, linv, M, y, ldy, row0, nrows,
+                                                      ntn, ntiles, werr);
+  return cudaGetLastError();
 }
 
 }  // namespace
@@ -527,23 +572,25 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
-  CUtensorMap mah, mal, mbh, mbl;
-  if (!make_map(&mah, gs.hi, M, K) || !make_map(&mal, gs.lo, M, K) || !make_map(&mbh, gs.whi, nrows, K) ||
-      !make_map(&mbl, gs.wlo, nrows, K))
-    return cudaErrorNotSupported;
-  auto kern = exact ? cq_umma_kernel<true> : cq_umma_kernel<false>;
-  const size_t smem = exact ? umma_smem<true>() : umma_smem<false>();
-  e = allow_smem((const void*)kern, smem);
-  if (e != cudaSuccess) return e;
   int* werr = gs.werr;
   if (!werr) {
     e = umma_error_ptr(&werr);
     if (e != cudaSuccess) return e;
   }
-  dim3 grid((nrows + UN - 1) / UN, (M + UM - 1) / UM);
-  kern<<<grid, UTHREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, std::ldexp(1.f, -le), M, y, ldy, row0, nrows,
-                                     werr);
-  return cudaGetLastError();
+  // Tile width by makespan: rounds of tiles over the 148 SMs times a tile's
+  // operand bytes (128 activation rows x 4 B + UN weight rows x 2 B per K;
+  // the operands stream from L2), 192 on a tie. (192 keeps the 14-warp CTA at
+  // 128 registers a thread; 256 would spill.)
+  const float linv = std::ldexp(1.f, -le);
+  const long mt = (M + UM - 1) / UM;
+  const long span128 = (((nrows + 127) / 128) * mt + 147) / 148 * (512 + 2 * 128);
+  const long span192 = (((nrows + 191) / 192) * mt + 147) / 148 * (512 + 2 * 192);
+  const bool wide = span192 <= span128;
+  if (exact)
+    return wide ? launch_umma<true, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
+                : launch_umma<true, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
+  return wide ? launch_umma<false, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
+              : launch_umma<false, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
 }
 
 cudaError_t umma_error_ptr(int** p) { return cudaGetSymbolAddress((void**)p, g_umma_error); }

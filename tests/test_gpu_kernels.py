@@ -75,19 +75,28 @@ def test_cq_index_unpacking_is_bit_exact(cuda, bits):
 
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("shape", [(3072, 768), (1568, 768), (768, 768), (8192, 768), (24, 3072), (1000, 300),
-                                   (20000, 768)])
-def test_cq_gemv_matches_oracle(cuda, bits, shape):
-    """(20000, 768): one activation row takes the partial-sum table kernel
-    (16384 rows and more); two to eight rows have more row blocks than the GEMV
-    grid, so CTAs loop over row blocks."""
+                                   (20000, 768), (40003, 768)])
+@pytest.mark.parametrize("levels_kind", ["f16", "f32"])
+def test_cq_gemv_matches_oracle(cuda, bits, shape, levels_kind):
+    """f16 codebook entries (the packer's codebooks) take the
+    tensor-core GEMV: ragged 16-row tiles, more tiles than the grid's warps at
+    (20000, 768) and (40003, 768) (warps loop over tiles), one and two 16-column
+    MMA tiles (M <= 4, M <= 8). Plain f32 entries are not f16 values and take
+    the SIMT kernels: the partial-sum table kernel for one row from 16384 rows,
+    the latency-ordered GEMV otherwise. Row 1 of every batch is zero."""
     torch = cuda
     out, inp = shape
-    cb = cact_pack.random_codebook(np.random.default_rng(9))  # BASELINE config 0 codebook
+    if levels_kind == "f16":
+        cb = cact_pack.random_codebook(np.random.default_rng(9))  # BASELINE config 0 codebook
+    else:
+        cb = (np.random.default_rng(9).normal(0.0, 0.02, 28) / np.sqrt(128)).astype(np.float32)
     d, pp, npp, w, _, _ = make_weight(torch, out, inp, bits, 2, cb)
     levels = cact_pack.codebook_levels(cb, bits)
     rng = np.random.default_rng(3)
-    for M in (1, 2, 3, 5, 8):
-        x = rng.normal(size=(M, inp)).astype(np.float32)
+    for M in (1, 2, 3, 4, 5, 8):
+        x = rng.normal(size=(M, inp)).astype(np.float32) * rng.choice([1e-3, 1.0, 40.0])
+        if M > 1:
+            x[1] = 0.0
         xh = np.stack([w.prepare(r) for r in x])
         y = torch.zeros(M, out, device="cuda")
         xd = dev(torch, xh)
@@ -146,6 +155,32 @@ def test_cq_tensor_core_gemm_matches_oracle(cuda, bits, shape, levels_kind):
         want = w.matmul_prepared(xh)
         got = y.cpu().numpy()
         assert close(got, want), (M, float(np.abs(got - want).max()))
+
+
+@pytest.mark.parametrize("shape,M", [((300, 768), 7680), ((1000, 768), 4000)])
+@pytest.mark.parametrize("levels_kind", ["f16", "f32"])
+def test_cq_tensor_core_persistent_tiles(cuda, shape, M, levels_kind):
+    """More tiles than SMs, so every persistent CTA computes several tiles and
+    the group accumulators alternate across tile boundaries: 128-row weight
+    tiles at (300, 768) x 7680 (180 tiles), 192-row tiles at (1000, 768) x 4000
+    (192 tiles), with f16 and plain f32 codebook entries."""
+    torch = cuda
+    out, inp = shape
+    if levels_kind == "f16":
+        cb = cact_pack.random_codebook(np.random.default_rng(9))
+    else:
+        cb = (np.random.default_rng(9).normal(0.0, 0.02, 28) / np.sqrt(128)).astype(np.float32)
+    d, pp, npp, w, _, _ = make_weight(torch, out, inp, 2, 8, cb)
+    levels = cact_pack.codebook_levels(cb, 2)
+    x = np.random.default_rng(12).normal(size=(M, inp)).astype(np.float32)
+    xh = np.stack([w.prepare(r) for r in x])
+    y = torch.zeros(M, out, device="cuda")
+    xd = dev(torch, xh)
+    nb.cq_project(pp, npp, out, inp, 2, levels, xd.data_ptr(), inp, M, y.data_ptr(), out, path=3)
+    torch.cuda.synchronize()
+    want = w.matmul_prepared(xh)
+    got = y.cpu().numpy()
+    assert close(got, want), float(np.abs(got - want).max())
 
 
 @pytest.mark.parametrize("bits", [2, 4])
