@@ -416,7 +416,11 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
         for _ in range(3):
             bt.step(None, stream=st)
             bt.feed_next(stream=st)
+        # NVTX range "config3_<kv>": a profiler can select these launches
+        # (ncu --nvtx --nvtx-include "config3_f32/").
+        torch.cuda.nvtx.range_push("config3_int8" if int8 else "config3_f32")
         us_tok = _event_us(torch, lambda: (bt.step(None, stream=st), bt.feed_next(stream=st)), 40)
+        torch.cuda.nvtx.range_pop()
         # oracle: prefill + 64 decode steps, all host cores
         so = m.session(320, int8)
         t0 = time.perf_counter()
@@ -622,6 +626,28 @@ def main():
     achieved = abytes / (attn_ms * 1e-3) / 1e9
     traffic = round(ATTN_TRAFFIC_PER_UNIT * attn_units_per_step(geo, per, pos_now) / geo["layers"])
     extra = {}
+    if world == 1 and per >= 1024:
+        # The per-GPU share of the 8-GPU run (sessions / 8), timed on this GPU:
+        # the first share of the prefilled sessions as a batch of its own.
+        share = per // 8
+        bs = eng.batch(sessions[:share])
+        bs.set_tokens(toks[:share])
+        for _ in range(args.warmup):
+            bs.step(None, stream=st)
+            bs.feed_next(stream=st)
+        torch.cuda.synchronize()
+        e0.record(stream)
+        for _ in range(args.steps):
+            bs.step(None, stream=st)
+            bs.feed_next(stream=st)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        sh_ms = e0.elapsed_time(e1) / args.steps
+        sprof, _ = bs.profile()
+        bs.close()
+        extra["share_8gpu"] = {"sessions": share, "ms_per_step": round(sh_ms, 3),
+                               "tok_per_s": round(share / (sh_ms * 1e-3), 1),
+                               "profile_ms_per_step": {k: round(v, 4) for k, v in sprof.items()}}
     if world == 1:  # the BASELINE config 0-3 lines and the CPU baseline are single-GPU items
         extra["gemv_config0"] = gemv_bandwidth(nb, torch, st)
         if not args.no_configs:

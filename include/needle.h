@@ -220,7 +220,8 @@ int needle_v3_device(NeedleV3Handle *handle);
  * codebook entries (host). xh is the rotated input (prepare_input, cq.rs:264),
  * [M][ldx] f32. path: 0 auto, 1 GEMV (M <= 8), 2 tiled SIMT GEMM, 3 tensor-core
  * GEMM (tcgen05; chosen by path 0 for M > 8; uses stream-ordered scratch of
- * 4*(M + nrows)*in_pad + 4*M bytes). Replaces
+ * 4*(M + nrows)*in_pad + 4*M bytes); for M <= 8, 4 the SIMT GEMV kernels and 5
+ * the tensor-core GEMV (mma.sync; codebooks whose levels are f16 values). Replaces
  * CqWeight::matvec_rows_prepared / matmul_rows_prepared (cq.rs:301, :446). */
 int nd_cq_project(const void *packed, const void *norms, int rows, int in_feat, int bits,
                   const float *levels, const float *xh, int ldx, int M, float *y, int ldy,

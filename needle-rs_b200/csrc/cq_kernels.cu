@@ -884,19 +884,27 @@ static cudaError_t launch_gemm_simt(const CqMat& W, const float* xh, int ldx, in
   return cudaGetLastError();
 }
 
+// gemv_kind (M <= 8 rows): 0 automatic, 1 the SIMT kernels, 2 the
+// tensor-core GEMV (f16-exact levels only).
 template <int BITS>
 static cudaError_t project_bits(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy,
-                                int row0, int nrows, cudaStream_t st) {
-  // Up to 8 rows on the tensor cores when the levels are f16 values (the
-  // packer writes f16 codebooks); otherwise the SIMT kernels: large one-row
-  // products stream through the table kernel, smaller ones take the
-  // latency-ordered GEMV.
-  if (M <= 8) {
+                                int row0, int nrows, cudaStream_t st, int gemv_kind = 0) {
+  // Up to 8 rows on the tensor cores for matrices past the split-group size
+  // when the levels are f16 values (the packer writes f16 codebooks): there
+  // the tensor-core GEMV streams faster than the SIMT kernels (1.77 against
+  // 1.26 TB/s for one row of a 300 MB 2-bit matrix on B200, 2.5x at two to
+  // eight rows), while on the model's own matrices (768 to 8192 rows) the
+  // latency-ordered SIMT GEMV finishes 0.6 to 6 us sooner. Otherwise the SIMT
+  // kernels: large one-row products stream through the table kernel, smaller
+  // ones take the latency-ordered GEMV.
+  const bool large = (nrows + 15) / 16 > TG_SPLIT_MAX_TILES;
+  if (M <= 8 && (gemv_kind == 2 || (gemv_kind == 0 && large))) {
     TcLevels L;
     float lsinv;
     if (tc_levels(W, &L, &lsinv))
       return M <= 4 ? launch_gemv_tc<BITS, 1>(W, L, lsinv, xh, ldx, M, y, ldy, row0, nrows, st)
                     : launch_gemv_tc<BITS, 2>(W, L, lsinv, xh, ldx, M, y, ldy, row0, nrows, st);
+    if (gemv_kind == 2) return cudaErrorInvalidValue;
   }
   if (M == 1 && nrows >= G1_MIN_ROWS && (size_t)W.in_pad * BITS / 4 * 16 * sizeof(float) <= G1_MAX_TABLE_BYTES)
     return launch_gemv1<BITS>(W, xh, y, row0, nrows, st);
@@ -960,8 +968,11 @@ cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y
                        int nrows, cudaStream_t st, int force_path, const GemmScratch* gs) {
   if (M <= 0 || nrows <= 0) return cudaSuccess;
   if (!cq_args_ok(W, xh, ldx) || row0 < 0 || row0 + nrows > W.rows) return cudaErrorInvalidValue;
-  if (force_path == 1 && M > 8) return cudaErrorInvalidValue;
-  if (force_path < 0 || force_path > 3) return cudaErrorInvalidValue;
+  if ((force_path == 1 || force_path >= 4) && M > 8) return cudaErrorInvalidValue;
+  if (force_path < 0 || force_path > 5) return cudaErrorInvalidValue;
+  if (force_path >= 4)  // one GEMV kernel by name: 4 the SIMT kernels, 5 the tensor-core GEMV
+    return W.bits == 2 ? project_bits<2>(W, xh, ldx, M, y, ldy, row0, nrows, st, force_path - 3)
+                       : project_bits<4>(W, xh, ldx, M, y, ldy, row0, nrows, st, force_path - 3);
   const bool scratch_ok = umma_scratch_ok(W, M, nrows, gs);
   if (force_path == 3) {
     if (!scratch_ok) return cudaErrorInvalidValue;

@@ -84,7 +84,9 @@ struct GemmScratch {
 };
 
 // force_path: 0 automatic (GEMV for M <= 8, else the tensor cores when `gs`
-// holds enough scratch, else the SIMT GEMM), 1 GEMV, 2 SIMT GEMM, 3 tensor cores.
+// holds enough scratch, else the SIMT GEMM), 1 GEMV, 2 SIMT GEMM, 3 tensor
+// cores; for M <= 8, 4 the SIMT GEMV kernels and 5 the tensor-core GEMV
+// (f16-exact levels only).
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                        int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr);
 bool umma_supported(const CqMat& W);

@@ -76,14 +76,16 @@ def test_cq_index_unpacking_is_bit_exact(cuda, bits):
 @pytest.mark.parametrize("bits", [2, 4])
 @pytest.mark.parametrize("shape", [(3072, 768), (1568, 768), (768, 768), (8192, 768), (24, 3072), (1000, 300),
                                    (20000, 768), (40003, 768)])
-@pytest.mark.parametrize("levels_kind", ["f16", "f32"])
-def test_cq_gemv_matches_oracle(cuda, bits, shape, levels_kind):
-    """f16 codebook entries (the packer's codebooks) take the
-    tensor-core GEMV: ragged 16-row tiles, more tiles than the grid's warps at
-    (20000, 768) and (40003, 768) (warps loop over tiles), one and two 16-column
-    MMA tiles (M <= 4, M <= 8). Plain f32 entries are not f16 values and take
-    the SIMT kernels: the partial-sum table kernel for one row from 16384 rows,
-    the latency-ordered GEMV otherwise. Row 1 of every batch is zero."""
+@pytest.mark.parametrize("levels_kind,path", [("f16", 1), ("f16", 5), ("f32", 1)])
+def test_cq_gemv_matches_oracle(cuda, bits, shape, levels_kind, path):
+    """Path 1 chooses: f16 codebook entries (the packer's
+    codebooks) take the tensor-core GEMV past 9472 rows ((20000, 768) and
+    (40003, 768): more tiles than the grid's warps, warps loop over tiles) and
+    the SIMT kernels below; plain f32 entries are not f16 values and always
+    take the SIMT kernels (the partial-sum table kernel for one row from 16384
+    rows, the latency-ordered GEMV otherwise). Path 5 forces the tensor-core
+    GEMV, so small matrices run its split-group form. One and two 16-column MMA
+    tiles (M <= 4, M <= 8). Row 1 of every batch is zero."""
     torch = cuda
     out, inp = shape
     if levels_kind == "f16":
@@ -101,7 +103,7 @@ def test_cq_gemv_matches_oracle(cuda, bits, shape, levels_kind):
         y = torch.zeros(M, out, device="cuda")
         xd = dev(torch, xh)
         nb.cq_project(pp, npp, out, inp, bits, levels, xd.data_ptr(), xh.shape[1], M, y.data_ptr(),
-                      out, path=1)
+                      out, path=path)
         torch.cuda.synchronize()
         want = w.matmul_prepared(xh)
         assert close(y.cpu().numpy(), want), (M, float(np.abs(y.cpu().numpy() - want).max()))
