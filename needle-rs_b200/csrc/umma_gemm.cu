@@ -61,7 +61,7 @@ namespace {
 
 constexpr int UM = 128;  // activation rows per tile (MMA M)
 constexpr int UK = 64;   // K per stage: 64 f16 = one 128-byte swizzle row
-// Pipeline of one tile width UN (weight rows per tile, the MMA N: 128 or 192).
+// Pipeline of one tile width UN (weight rows per tile, the MMA N: 64, 128 or 192).
 // A stage holds the activation tiles (high part and remainder, [128 rows][64 k]
 // f16 each) and the level tile(s) ([UN rows][64 k] f16; remainders too unless
 // the levels are exact), in as many stages as fit 192 KB.
@@ -223,7 +223,7 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   constexpr int USTAGES = P::STAGES;
   constexpr uint32_t STAGE_BYTES = P::STAGE_BYTES;
   constexpr int EW = P::EPI_WARPS;
-  constexpr uint32_t TMEM_COLS = 2 * UN <= 256 ? 256 : 512;  // two group accumulators (a power of two)
+  constexpr uint32_t TMEM_COLS = 2 * UN <= 128 ? 128 : 2 * UN <= 256 ? 256 : 512;  // two group accumulators
   extern __shared__ unsigned char smraw[];
   unsigned char* sm = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smraw) + 1023) & ~uintptr_t(1023));
   const int nk = W.in_pad / UK, ng = W.in_pad / 128;
@@ -579,18 +579,20 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
   }
   // Tile width by makespan: rounds of tiles over the 148 SMs times a tile's
   // operand bytes (128 activation rows x 4 B + UN weight rows x 2 B per K;
-  // the operands stream from L2), 192 on a tie. (192 keeps the 14-warp CTA at
-  // 128 registers a thread; 256 would spill.)
+  // the operands stream from L2), the wider tile on a tie. 64-row tiles put
+  // more SMs to work on small batches; 192 keeps the 14-warp CTA at 128
+  // registers a thread (256 would spill).
   const float linv = std::ldexp(1.f, -le);
   const long mt = (M + UM - 1) / UM;
-  const long span128 = (((nrows + 127) / 128) * mt + 147) / 148 * (512 + 2 * 128);
-  const long span192 = (((nrows + 191) / 192) * mt + 147) / 148 * (512 + 2 * 192);
-  const bool wide = span192 <= span128;
+  auto span = [&](long un) { return (((nrows + un - 1) / un) * mt + 147) / 148 * (512 + 2 * un); };
+  const int un = span(192) <= span(128) ? 192 : span(128) <= span(64) ? 128 : 64;
   if (exact)
-    return wide ? launch_umma<true, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
-                : launch_umma<true, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
-  return wide ? launch_umma<false, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
-              : launch_umma<false, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
+    return un == 192   ? launch_umma<true, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
+           : un == 128 ? launch_umma<true, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
+                       : launch_umma<true, 64>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
+  return un == 192   ? launch_umma<false, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
+         : un == 128 ? launch_umma<false, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
+                     : launch_umma<false, 64>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
 }
 
 cudaError_t umma_error_ptr(int** p) { return cudaGetSymbolAddress((void**)p, g_umma_error); }
