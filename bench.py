@@ -396,18 +396,24 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
     eng1 = nb.V3Engine.from_bytes(raw)
     p3 = prompt(0, 256)
     c3 = {}
-    m = orc.Model(raw)
+    gpu3 = {}
     for int8 in (False, True):
         eng1.generate_ids(p3, 64, kv_int8=int8)  # warm
         torch.cuda.synchronize()
-        t0 = time.perf_counter()
-        s = eng1.session(320, int8)
-        s.prefill(p3)
-        torch.cuda.synchronize()
-        pre_s = time.perf_counter() - t0
-        t0 = time.perf_counter()
-        ids = eng1.generate_ids(p3, 64, kv_int8=int8)
-        gen_s = time.perf_counter() - t0
+        # Host-API wall times: the best of three (host scheduling noise on
+        # the box moves single runs by several times).
+        pre_s = gen_s = float("inf")
+        for _ in range(3):
+            s = eng1.session(320, int8)
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            s.prefill(p3)
+            torch.cuda.synchronize()
+            pre_s = min(pre_s, time.perf_counter() - t0)
+            del s
+            t0 = time.perf_counter()
+            ids = eng1.generate_ids(p3, 64, kv_int8=int8)
+            gen_s = min(gen_s, time.perf_counter() - t0)
         # device-resident batch-1 decode: one session stepped as a CUDA-graph batch
         s2 = eng1.session(320, int8)
         _, pk = eng1.prefill_batch([s2], [p3], logits=False)
@@ -421,7 +427,12 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
         torch.cuda.nvtx.range_push("config3_int8" if int8 else "config3_f32")
         us_tok = _event_us(torch, lambda: (bt.step(None, stream=st), bt.feed_next(stream=st)), 40)
         torch.cuda.nvtx.range_pop()
-        # oracle: prefill + 64 decode steps, all host cores
+        gpu3[int8] = (pre_s, gen_s, us_tok, ids)
+        del bt, s2
+    # oracle, after every GPU measurement: prefill + 16 decode steps, all host cores
+    m = orc.Model(raw)
+    for int8 in (False, True):
+        pre_s, gen_s, us_tok, ids = gpu3[int8]
         so = m.session(320, int8)
         t0 = time.perf_counter()
         so.prefill(p3)
@@ -436,7 +447,7 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
             "decode_us_per_token_graph": round(us_tok, 1), "decode_tok_per_s_graph": round(1e6 / us_tok, 1),
             "cpu_prefill_ms": round(cpu_pre * 1e3, 1), "cpu_decode_tok_per_s": round(1 / cpu_dec, 1),
             "cpu_cores": ncpu, "cpu_sample": "oracle prefill of the 256-token prompt + 16 decode steps"}
-        del bt, s, s2, so
+        del so
     out["config3_batch1"] = {"metric": "batch-1 forward: 256-token prompt, greedy decode",
                              "roofline": "L2 / latency (17.6 MB of weights per token stay L2-resident)",
                              "by_kv": c3}

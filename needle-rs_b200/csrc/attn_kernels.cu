@@ -318,14 +318,71 @@ __device__ __forceinline__ AttnSrc layer_src(const Geo& G, int li, const RowBatc
   return src;
 }
 
-// Forward-pass attention: grid (rows, kv_heads, nsplit).
+// Finish of one (row, KV head) once every split's partial is in ps (natural-
+// log maxima): the softmax merge over the splits, the output gate
+// (model.rs:305-308) and the rotation of the rep * VH outputs, whole 128-wide
+// groups, into oh; the arithmetic of attn_finish_kernel with the splits of one
+// KV head. F: shared scratch of FINISH_SCRATCH floats. Contains
+// __syncthreads.
+constexpr int FINISH_SCRATCH = AT_MAXREP * 64 + 8 + AT_MAXREP * 64 + 64 * 2 * AT_MAXREP;
+template <int VH>
+__device__ void finish_kvhead(const Geo& G, int r, int kh, int rep, int nsplit, const float* ps,
+                              const float* __restrict__ proj, float* __restrict__ oh, float* F) {
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int pw = rep * (VH + 2);
+  float* Fw = F;              // [rep][64] split weights exp(m_z - M)
+  float* FL = Fw + rep * 64;  // [rep] sums
+  float* Fo = FL + 8;         // [rep * VH] gated outputs
+  float* Fm = Fo + rep * VH;  // [nsplit][2 * rep] the splits' maxima and sums
+  for (int i = tid; i < nsplit * 2 * rep; i += blockDim.x) Fm[i] = __ldcg(ps + (i / (2 * rep)) * pw + i % (2 * rep));
+  __syncthreads();
+  if (tid < rep) {
+    const int h = tid;
+    float M = -INFINITY;
+    for (int z = 0; z < nsplit; ++z) M = fmaxf(M, Fm[z * 2 * rep + h]);
+    float L = 0.f;
+    for (int z = 0; z < nsplit; ++z) {
+      const float mz = Fm[z * 2 * rep + h];
+      const float wz = mz == -INFINITY ? 0.f : expf(mz - M);
+      Fw[h * 64 + z] = wz;
+      L += wz * Fm[z * 2 * rep + rep + h];
+    }
+    FL[h] = L;
+  }
+  __syncthreads();
+  const float* gate = proj + (size_t)r * G.proj_dim + G.qkv_dim + (size_t)kh * rep * VH;
+  for (int i = tid; i < rep * VH; i += blockDim.x) {
+    const int h = i / VH;
+    float o = 0.f;
+#pragma unroll 4
+    for (int z = 0; z < nsplit; ++z) o += Fw[h * 64 + z] * __ldcg(ps + z * pw + 2 * rep + i);
+    Fo[i] = o / FL[h] * sigmoidf_(gate[i]);
+  }
+  __syncthreads();
+  const int opad = (G.o_dim + 127) / 128 * 128;
+  float* ohr = oh + (size_t)r * opad + (size_t)kh * rep * VH;
+  for (int gg = wid; gg < rep * VH / 128; gg += nw) {
+    const float4 v = reinterpret_cast<const float4*>(Fo + gg * 128)[lane];
+    float x[4] = {v.x, v.y, v.z, v.w};
+    fwht128_warp(x);
+    reinterpret_cast<float4*>(ohr + gg * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+  }
+}
+
+// Forward-pass attention: grid (rows, kv_heads, nsplit). With oh (and proj,
+// cnt: per-(row, KV head) counters, zero-initialised) the last CTA of each
+// (row, KV head) to arrive also finishes it (finish_kvhead) and resets its
+// counter; no CTA waits for another.
 template <bool INT8, int QK, int VH>
 __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, RowBatch rb, int window,
                                                                 int nsplit, const float* __restrict__ qpost,
                                                                 const void* pk, const void* pv,
                                                                 const float* pks, const float* pvs,
-                                                                float* __restrict__ part) {
+                                                                float* __restrict__ part,
+                                                                const float* __restrict__ proj,
+                                                                float* __restrict__ oh, int* __restrict__ cnt) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) unsigned char smraw[];
   auto& S = *reinterpret_cast<AttnSmem<INT8, QK, VH>*>(smraw);
   const int r = blockIdx.x, kh = blockIdx.y, z = blockIdx.z;
@@ -337,6 +394,22 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
   const int pw = rep * (VH + 2);
   attend_part<INT8, QK, VH>(S, qpost + (size_t)r * G.q_dim + (size_t)kh * rep * QK, rep, src, kh, a, b,
                             1.0f / sqrtf((float)QK), part + (((size_t)r * G.kvh + kh) * nsplit + z) * pw);
+  if (!oh) return;  // attn_finish combines and rotates
+  static_assert(sizeof(AttnSmem<INT8, QK, VH>) >= FINISH_SCRATCH * sizeof(float), "finish scratch");
+  __shared__ int last;
+  __syncthreads();  // this CTA's partial is written; its shared memory is free
+  if (nsplit > 1) {
+    if (threadIdx.x == 0) {
+      __threadfence();
+      last = atomicAdd(&cnt[(size_t)r * G.kvh + kh], 1) == nsplit - 1;
+    }
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    if (threadIdx.x == 0) cnt[(size_t)r * G.kvh + kh] = 0;  // ready for the next launch
+  }
+  finish_kvhead<VH>(G, r, kh, rep, nsplit, part + ((size_t)r * G.kvh + kh) * nsplit * pw, proj, oh,
+                    reinterpret_cast<float*>(smraw));
 }
 
 // ----------------------------------------------------------------------------
@@ -369,6 +442,7 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
 // the CTA writes the same (max, sum, P.V) partial as the f32 kernel.
 // ----------------------------------------------------------------------------
 constexpr int WB = 32;  // positions per warp block
+constexpr int NJ = WB / 16;  // 16-position MMA tiles per warp block
 
 template <int QK, int VH>
 struct MmaTile {
@@ -488,11 +562,12 @@ __device__ __forceinline__ void mma_issue(MmaWarpSmem<QK, VH>& W, int buf, const
     const long idx = ok ? block_index(src, idx0, i) : 0;
     cp_async16(W.v[buf] + i * VH + pc * 16, vb + idx * src.v_row + pc * 16, ok);
   }
-  {
-    const bool ok = n0 + lane <= hi;
-    const long idx = ok ? block_index(src, idx0, lane) : 0;
-    cp_async4(&W.ks[buf][lane], src.ks + idx * src.s_row + kh * src.s_head, ok);
-    cp_async4(&W.vs[buf][lane], src.vs + idx * src.s_row + kh * src.s_head, ok);
+#pragma unroll
+  for (int i = lane; i < WB; i += 32) {
+    const bool ok = n0 + i <= hi;
+    const long idx = ok ? block_index(src, idx0, i) : 0;
+    cp_async4(&W.ks[buf][i], src.ks + idx * src.s_row + kh * src.s_head, ok);
+    cp_async4(&W.vs[buf][i], src.vs + idx * src.s_row + kh * src.s_head, ok);
   }
 }
 
@@ -573,12 +648,15 @@ __device__ __forceinline__ void mma_issue_bulk(MmaWarpSmem<QK, VH>& W, int buf, 
       bulk_g2s(W.v[buf] + c1 * VH, vb, (uint32_t)(cnt - c1) * VH, &W.bar[buf]);
     }
   }
-  const bool ok = lane < cnt;
-  int idx = idx0 + lane;
-  idx = idx >= src.slots ? idx - src.slots : idx;
-  idx = ok ? idx : 0;
-  cp_async4(&W.ks[buf][lane], src.ks + (long)idx * src.s_row + kh * src.s_head, ok);
-  cp_async4(&W.vs[buf][lane], src.vs + (long)idx * src.s_row + kh * src.s_head, ok);
+#pragma unroll
+  for (int i = lane; i < WB; i += 32) {
+    const bool ok = i < cnt;
+    int idx = idx0 + i;
+    idx = idx >= src.slots ? idx - src.slots : idx;
+    idx = ok ? idx : 0;
+    cp_async4(&W.ks[buf][i], src.ks + (long)idx * src.s_row + kh * src.s_head, ok);
+    cp_async4(&W.vs[buf][i], src.vs + (long)idx * src.s_row + kh * src.s_head, ok);
+  }
 }
 
 template <int QK, int VH>
@@ -590,6 +668,7 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
                                                             float* __restrict__ oh, int* __restrict__ cnt,
                                                             int* __restrict__ werr) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   using T = MmaTile<QK, VH>;
   using WS = MmaWarpSmem<QK, VH>;
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -684,13 +763,13 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
     __syncwarp();
     // ---- integer key dots, positions as rows: m-tile j covers positions
     // j*16 .. j*16+15; d[j] = (pos g, heads 2t, 2t+1), (pos g+8, same heads)
-    int d[2][4];
+    int d[NJ][4];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0;
+    for (int j = 0; j < NJ; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0;
 #pragma unroll
     for (int s = 0; s < T::NK32; ++s)
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         const int8_t* k0 = W.k[buf] + (j * 16 + g) * T::KS + s * 32 + t * 4;
         const int8_t* k1 = k0 + 8 * T::KS;
         const uint32_t ka[4] = {*reinterpret_cast<const uint32_t*>(k0), *reinterpret_cast<const uint32_t*>(k1),
@@ -700,16 +779,16 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
       }
     if (T::K16) {
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int j = 0; j < NJ; ++j) {
         const int8_t* k0 = W.k[buf] + (j * 16 + g) * T::KS + T::NK32 * 32 + t * 4;
         mma_s8_k16(d[j], *reinterpret_cast<const uint32_t*>(k0),
                    *reinterpret_cast<const uint32_t*>(k0 + 8 * T::KS), qb16);
       }
     }
     // Score i of this lane: position j*16 + g + 8*hf (i = 4j + 2hf + e), head 2t + e.
-    float sc[8];
+    float sc[4 * NJ];
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+    for (int j = 0; j < NJ; ++j)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const int pi = j * 16 + hf * 8 + g;
@@ -720,11 +799,13 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
           sc[4 * j + 2 * hf + e] = ok ? (float)d[j][2 * hf + e] * qsc[e] * ksv : -INFINITY;
       }
     // ---- online softmax per head (column): the 8 lanes sharing t hold
-    // the block's 32 positions of heads 2t, 2t + 1
+    // the block's WB positions of heads 2t, 2t + 1
     float corr[2], mz[2];
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
-      float mx = fmaxf(fmaxf(sc[e], sc[2 + e]), fmaxf(sc[4 + e], sc[6 + e]));
+      float mx = sc[e];
+#pragma unroll
+      for (int q = 1; q < 2 * NJ; ++q) mx = fmaxf(mx, sc[2 * q + e]);
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
@@ -733,13 +814,18 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
       corr[e] = ex2_fast(m[e] - mz[e]);
       m[e] = mnew;
     }
-    float pw[8];
+    float pw[4 * NJ];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) pw[i] = ex2_fast(sc[i] - mz[i & 1]);
+    for (int i = 0; i < 4 * NJ; ++i) pw[i] = ex2_fast(sc[i] - mz[i & 1]);
 #pragma unroll
-    for (int e = 0; e < 2; ++e) l[e] = l[e] * corr[e] + ((pw[e] + pw[2 + e]) + (pw[4 + e] + pw[6 + e]));
+    for (int e = 0; e < 2; ++e) {
+      float sum = 0.f;
 #pragma unroll
-    for (int j = 0; j < 2; ++j)
+      for (int q = 0; q < NJ; ++q) sum += pw[4 * q + e] + pw[4 * q + 2 + e];
+      l[e] = l[e] * corr[e] + sum;
+    }
+#pragma unroll
+    for (int j = 0; j < NJ; ++j)
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         const float vsv = W.vs[buf][j * 16 + hf * 8 + g];
@@ -759,7 +845,7 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
     // the score fragment as [position][head]; movmatrix.trans turns each into
     // the [head][position] pairs of the B fragment.
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
+    for (int j = 0; j < NJ; ++j) {
       uint32_t bh[2], bl[2];
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
@@ -925,13 +1011,14 @@ static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb
   cudaError_t e = allow_smem((const void*)k, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(rb.M, G.kvh, nsplit);
-  k<<<grid, 128, smem, st>>>(G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, cnt, werr);
-  return cudaGetLastError();
+  return launch_pdl(k, grid, dim3(128), smem, st, G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj,
+                    oh, cnt, werr);
 }
 
 bool attn_fuses_finish(const Geo& G, int int8) {
+  (void)int8;  // both kernels finish in place
   const int rep = G.heads / G.kvh;
-  return int8 && (rep * G.vh) % 128 == 0 && rep <= 8;
+  return (rep * G.vh) % 128 == 0 && rep <= 8;
 }
 
 // Attention CTAs a launch aims for: enough to cover the 148 SMs several times.
@@ -953,14 +1040,15 @@ size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit) {
 template <bool INT8, int QK, int VH>
 static cudaError_t launch_layer_attn_t(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
                                        const float* qpost, const void* pk, const void* pv, const float* pks,
-                                       const float* pvs, float* part, cudaStream_t st) {
+                                       const float* pvs, float* part, const float* proj, float* oh, int* cnt,
+                                       cudaStream_t st) {
   const size_t smem = sizeof(AttnSmem<INT8, QK, VH>);
   auto k = layer_attn_kernel<INT8, QK, VH>;
   cudaError_t e = allow_smem((const void*)k, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(rb.M, G.kvh, nsplit);
-  k<<<grid, AT_THREADS, smem, st>>>(G, li, rb, window, nsplit, qpost, pk, pv, pks, pvs, part);
-  return cudaGetLastError();
+  return launch_pdl(k, grid, dim3(AT_THREADS), smem, st, G, li, rb, window, nsplit, qpost, pk, pv, pks, pvs, part,
+                    proj, oh, cnt);
 }
 
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
@@ -997,8 +1085,10 @@ cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const Lay
 #undef NB_ATI
     return cudaErrorInvalidValue;
   }
+  // With proj, oh and cnt the kernel also finishes (attn_fuses_finish).
+  if (!(proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64)) proj = nullptr, oh = nullptr, cnt = nullptr;
 #define NB_ATT(I8, Q, V) \
-  return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, st)
+  return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, proj, oh, cnt, st)
   const int key = G.qk * 2 + (int8 ? 1 : 0);
   if (G.vh == 64) {
     switch (key) {
@@ -1167,6 +1257,7 @@ cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float*
 __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ part,
                                    const float* __restrict__ proj, float* __restrict__ oh) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) float sm[];
   __shared__ float wsm[8][64];  // per-warp split weights (nsplit <= 64)
   const int r = blockIdx.x;
@@ -1212,8 +1303,7 @@ cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, con
   if (rb.M <= 0) return cudaSuccess;
   const int opad = (G.o_dim + 127) / 128 * 128;
   if (nsplit > 64) return cudaErrorInvalidValue;  // the kernel's split-weight buffer
-  attn_finish_kernel<<<rb.M, 256, opad * sizeof(float), st>>>(G, nsplit, part, proj, oh);
-  return cudaGetLastError();
+  return launch_pdl(attn_finish_kernel, dim3(rb.M), dim3(256), opad * sizeof(float), st, G, nsplit, part, proj, oh);
 }
 
 

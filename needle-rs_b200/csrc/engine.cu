@@ -58,7 +58,7 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
   void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, whi, wlo, cnt, oh, projo, gates, fetched, ekv, evc, lm_in,
-                pks, pvs, pk, pv, rows, tokens, next, last_rows};
+                pks, pvs, pk, pv, rows, tokens, next, last_rows, pre_part, pre_cnt};
   for (void* p : ps)
     if (p) cudaFree(p);
   if (logits) cudaFree(logits);
@@ -95,6 +95,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
       {(void**)&w.pks, cap * G.kvh * 4},           {(void**)&w.pvs, cap * G.kvh * 4},
       {(void**)&w.rows, cap * sizeof(RowInfo)},    {(void**)&w.tokens, cap * 4},
       {(void**)&w.next, cap * 4},                  {(void**)&w.last_rows, cap * 4},
+      {(void**)&w.pre_part, 8 * 32 * 32 * 4},     {(void**)&w.pre_cnt, 8 * 4},
   };
   for (auto& a : allocs) {
     cudaError_t e = cudaMalloc(a.p, std::max<size_t>(a.bytes, 256));
@@ -106,6 +107,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
   }
   {
     cudaError_t e = cudaMemset(w.cnt, 0, cap * G.kvh * 4);  // attention split counters start at zero
+    if (e == cudaSuccess) e = cudaMemset(w.pre_cnt, 0, 8 * 4);
     if (e != cudaSuccess) {
       w.release();
       *err = cuda_msg("workspace initialisation", e);
@@ -1179,7 +1181,7 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
   NB_MARK(PK_EMBED, 1);
   for (int l = 0; l < G.layers; ++l) {
     NB_TRY(launch_layer_pre(G, l, rb, w.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
-                            site_of[l], w.ekv, w.evc, w.u, w.bx, w.xh, w.gates, st));
+                            site_of[l], w.ekv, w.evc, w.u, w.bx, w.xh, w.gates, st, w.pre_part, w.pre_cnt));
     NB_MARK(PK_LAYER_PRE, 1);
     NB_TRY(cq_project(qkvg[l], w.xh, dpad, M, w.proj, G.proj_dim, 0, G.proj_dim, st, 0, &w.gs));
     NB_MARK(PK_QKVG, cq_launches(qkvg[l], M, &w.gs));

@@ -70,6 +70,8 @@ struct Workspace {
   float* ainv = nullptr;                  // and their inverse row scales
   __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
   int* cnt = nullptr;  // attention split-arrival counters [rows][kv heads], zero between launches
+  float* pre_part = nullptr;  // few-row mHC pre-projection partials [8][32][32]
+  int* pre_cnt = nullptr;     // and its per-row arrival counters [8], zero between launches
   GemmScratch gs;
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;

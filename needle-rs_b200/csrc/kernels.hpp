@@ -111,11 +111,13 @@ cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBat
                                  float* fetched, cudaStream_t st);
 cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const RowBatch& rb,
                                const float* ekv, float* evc, cudaStream_t st);
+// split_part / split_cnt (nullable): scratch of the few-row form, 8 rows x 32
+// groups x 32 floats and 8 zero-initialised counters (reset by the kernel).
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                              const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
                              const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                              const float* evc, float* u, float* bx, float* xh, float* gates,
-                             cudaStream_t st);
+                             cudaStream_t st, float* split_part = nullptr, int* split_cnt = nullptr);
 // In int8 mode q8out / q8s (when non-null) receive the query's int8 codes
 // [M][heads][qk] and per-head scales [M][heads].
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
@@ -128,8 +130,8 @@ int attn_nsplit(int rows, int kvh, int max_span);
 size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit);
 // int8 = 1 runs the tensor-core kernel on the query codes q8 / q8s;
 // int8 = 0 the f32 kernel on qpost.
-// int8 = 1 with proj / oh / cnt (per-row, per-KV-head counters, zero-initialised)
-// and attn_fuses_finish(): the kernel also merges the splits, gates and
+// With proj / oh / cnt (per-row, per-KV-head counters, zero-initialised) and
+// attn_fuses_finish(), either kernel also merges the splits, gates and
 // rotates into oh, so attn_finish is not launched.
 // werr: device flag set to 2 when a bounded wait of the int8 kernel's copies
 // expired (required for int8 = 1).

@@ -39,6 +39,8 @@ __device__ __forceinline__ void load_levels(const CqMat& W, float* lev) {
 // model.rs:196-203: dequantize_row (levels*norm, inverse rotation) then
 // * sqrt(d_model), broadcast into every mHC lane.
 __global__ void embed_kernel(Geo G, CqMat emb, RowBatch rb, float* __restrict__ lanes) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float lev[16];
   load_levels(emb, lev);
   const int r = blockIdx.x;
@@ -66,8 +68,7 @@ __global__ void embed_kernel(Geo G, CqMat emb, RowBatch rb, float* __restrict__ 
 cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, float* lanes,
                          cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
-  embed_kernel<<<rb.M, 256, 0, st>>>(G, emb, rb, lanes);
-  return cudaGetLastError();
+  return launch_pdl(embed_kernel, dim3(rb.M), dim3(256), 0, st, G, emb, rb, lanes);
 }
 
 // ---------------------------------------------------------------- Engram
@@ -78,6 +79,7 @@ cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, flo
 __global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, RowBatch rb,
                                      float* __restrict__ fetched) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   const int r = blockIdx.x, site = blockIdx.y;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const RowInfo ri = rb.rows[r];
@@ -118,8 +120,7 @@ cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBat
                                  float* fetched, cudaStream_t st) {
   if (rb.M <= 0 || G.n_sites == 0) return cudaSuccess;
   dim3 grid(rb.M, G.n_sites);
-  engram_gather_kernel<<<grid, 256, 0, st>>>(G, tables, rb, fetched);
-  return cudaGetLastError();
+  return launch_pdl(engram_gather_kernel, grid, dim3(256), 0, st, G, tables, rb, fetched);
 }
 
 // value_conv (engram.rs:89-106) / engram_conv_step (cache.rs:444-479): dilated
@@ -135,6 +136,8 @@ struct EngTaps {
 // row descriptor and the session's tail pointer are read once per row).
 __global__ void engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float* __restrict__ ekv,
                                    float* __restrict__ evc) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos, reach = G.e_reach, d = G.d, d4 = d / 4;
@@ -178,8 +181,7 @@ cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const Row
   EngTaps t;
   for (int i = 0; i < G.n_sites; ++i) t.t[i] = taps[i];
   if (G.d % 4) return cudaErrorInvalidValue;
-  engram_conv_kernel<<<rb.M, 256, 0, st>>>(G, t, rb, ekv, evc);
-  return cudaGetLastError();
+  return launch_pdl(engram_conv_kernel, dim3(rb.M), dim3(256), 0, st, G, t, rb, ekv, evc);
 }
 
 // ---------------------------------------------------------------- mHC pre
@@ -227,6 +229,75 @@ __device__ __forceinline__ float sinkhorn_lane_fast(float m, int n) {
   return __expf(m);
 }
 
+
+// Hardware reciprocal (MUFU, about 1 ulp): the Sinkhorn scalings sit in a
+// 160-step dependency chain where an IEEE-rounded reciprocal sequence costs
+// several times its latency.
+__device__ __forceinline__ float rcp_approx(float x) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// The same Sinkhorn iterations in the linear domain (n <= 4): with K =
+// exp(m - max m), the log-domain iterate after t row/column steps is
+// log(r_i K_ij c_j) for the scalings r_i = 1 / sum_j K_ij c_j and c_j = 1 /
+// sum_i K_ij r_i, so each step is four dot products and four reciprocals
+// instead of a logsumexp per row or column. Every lane holds the whole matrix.
+// When a row or column maximum lies more than 60 below the overall maximum the
+// scalings could leave the f32 range; the warp then takes the log-domain form.
+// Lane l < n * n returns element l of the result.
+__device__ __forceinline__ float sinkhorn_lane_lin(float m, int n) {
+  const int lane = threadIdx.x & 31;
+  float v[4][4];
+  float M = -INFINITY;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float x = __shfl_sync(0xffffffffu, m, (i * n + j) & 31);
+      v[i][j] = (i < n && j < n) ? x : -INFINITY;
+      M = fmaxf(M, v[i][j]);
+    }
+  bool ok = isfinite(M);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float rm = -INFINITY, cm = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      rm = fmaxf(rm, v[i][j]);
+      cm = fmaxf(cm, v[j][i]);
+    }
+    if (i < n) ok = ok && rm >= M - 60.0f && cm >= M - 60.0f;
+  }
+  if (!ok) return sinkhorn_lane_fast(m, n);  // the same decision in every lane
+  float K[4][4], r[4], c[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    c[i] = i < n ? 1.0f : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) K[i][j] = (i < n && j < n) ? __expf(v[i][j] - M) : 0.0f;
+  }
+  for (int it = 0; it < 20; ++it) {
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float sr = K[i][0] * c[0] + K[i][1] * c[1] + K[i][2] * c[2] + K[i][3] * c[3];
+      r[i] = i < n ? rcp_approx(sr) : 0.0f;
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const float sc = K[0][j] * r[0] + K[1][j] * r[1] + K[2][j] * r[2] + K[3][j] * r[3];
+      c[j] = j < n ? rcp_approx(sc) : 0.0f;
+    }
+  }
+  float out = 0.0f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (i < n && j < n && lane == i * n + j) out = r[i] * K[i][j] * c[j];
+  return out;
+}
 
 // Dot of one CQ row (4- or 2-bit) with a prepared activation in shared memory,
 // one warp; lane l covers elements g*128 + l*4 .. +3 of every group, so the
@@ -304,6 +375,109 @@ __device__ __forceinline__ void phi_row(int o, int li, int n, const CqMat& a, co
   }
 }
 
+// The mHC pre-projection of row r after the 2n + n^2 projected values of
+// rms_unit(lanes) are in phi[] (shared): the gates and Sinkhorn (mhc.rs:109-130;
+// warp 0), mix_down (mhc.rs:79-102), the Engram gate (engram.rs:112-132) and
+// the pre-attention norm + rotation of the q|k|v|gate input (model.rs:230-262)
+// on the other warps. L: the row's lanes [lanes][d]; ek, ev: the row's Engram
+// key and value at this layer's site (null without one); norm_in: the layer's
+// input norm scale (each shared or global). gsm (24), red (32), bx (d) and hb
+// (d rounded up to 128): shared scratch. Every thread of the CTA calls it last.
+__device__ __forceinline__ void layer_pre_tail(const Geo& G, int li, int r, const MhcParams& mp,
+                                               const float* phi, const float* L, float* gsm, float* red,
+                                               float* bx, float* hb, const float* norm_in, const float* ek,
+                                               const float* ev, float* __restrict__ u_out,
+                                               float* __restrict__ bx_out, float* __restrict__ xh_out,
+                                               float* __restrict__ gates) {
+  const int n = G.lanes, d = G.d;
+  const int dpad = (d + 127) / 128 * 128;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  // Warp 0 forms the gates; the mix-down gate releases warps 1.. (named
+  // barrier 1) while warp 0 runs Sinkhorn, which nothing below depends on.
+  const int nwo = nw - 1, wo = wid - 1, to = tid - 32, NT = blockDim.x - 32;
+  if (wid == 0) {
+    const int act = li % n;
+    float hpost = 0.f;
+    if (lane < n) {
+      const float pre_off = lane == act ? 4.0f : -4.0f;   // mhc.rs:56
+      const float post_off = lane == act ? 0.0f : -4.0f;  // mhc.rs:65
+      gsm[lane] = sigmoidf_(mp.a_pre * phi[lane] + mp.b_pre[lane] + pre_off);
+      hpost = 2.0f * sigmoidf_(mp.a_post * phi[n + lane] + mp.b_post[lane] + post_off);
+    }
+    __syncwarp();
+    asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
+    const float m = lane < n * n ? mp.a_res * phi[2 * n + lane] + mp.b_res[lane] : 0.f;
+    const float hres = sinkhorn_lane_lin(m, n);
+    float* gout = gates + (size_t)r * 24;
+    if (lane < n) gout[lane] = hpost;
+    if (lane < n * n) gout[n + lane] = hres;
+    return;
+  }
+  asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
+  // Warps 1..: reductions over NT threads on named barrier 2.
+  auto gsum = [&](float v) {
+    v = warp_sum(v);
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+    if (lane == 0) red[wo] = v;
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+    return warp_sum(lane < nwo ? red[lane] : 0.f);
+  };
+  // Three sums at once (red holds 3 x 8 partials; nwo <= 8).
+  auto gsum3 = [&](float& a, float& b, float& c) {
+    a = warp_sum(a);
+    b = warp_sum(b);
+    c = warp_sum(c);
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+    if (lane == 0) red[wo] = a, red[8 + wo] = b, red[16 + wo] = c;
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+    a = warp_sum(lane < nwo ? red[lane] : 0.f);
+    b = warp_sum(lane < nwo ? red[8 + lane] : 0.f);
+    c = warp_sum(lane < nwo ? red[16 + lane] : 0.f);
+  };
+  // u = sum_i hpre_i * lane_i (mix_down), bx = u (+ Engram).
+#pragma unroll 4
+  for (int c = to; c < d; c += NT) {
+    float acc = 0.f;
+    for (int l = 0; l < n; ++l) acc += gsm[l] * L[l * d + c];
+    bx[c] = acc;
+    u_out[(size_t)r * d + c] = acc;
+  }
+  asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+  if (ek) {
+    float sx = 0.f, sk = 0.f, sd = 0.f;
+#pragma unroll 4
+    for (int c = to; c < d; c += NT) {
+      float x = bx[c], k = ek[c];
+      sx += x * x;
+      sk += k * k;
+      sd += x * k;
+    }
+    gsum3(sx, sk, sd);
+    const float ux = 1.0f / sqrtf(sx / (float)d + 1e-6f);
+    const float uk = 1.0f / sqrtf(sk / (float)d + 1e-6f);
+    const float alpha = sigmoidf_(sd * ux * uk / sqrtf((float)d));
+#pragma unroll 4
+    for (int c = to; c < d; c += NT) bx[c] += alpha * ev[c];
+    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+  }
+  float s2 = 0.f;
+  for (int c = to; c < d; c += NT) s2 += bx[c] * bx[c];
+  s2 = gsum(s2);
+  const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
+#pragma unroll 4
+  for (int c = to; c < dpad; c += NT) {
+    hb[c] = c < d ? (1.0f + norm_in[c]) * bx[c] * inv2 : 0.f;
+    if (c < d) bx_out[(size_t)r * d + c] = bx[c];
+  }
+  asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
+  for (int g = wo; g < dpad / 128; g += nwo) {
+    float4 v = reinterpret_cast<float4*>(hb + g * 128)[lane];
+    float x[4] = {v.x, v.y, v.z, v.w};
+    fwht128_warp(x);
+    reinterpret_cast<float4*>(xh_out + (size_t)r * dpad + g * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+  }
+}
+
 // mhc.rs:79-102 (mix_down) with the gate and Sinkhorn of mhc.rs:109-130, the
 // Engram gate (engram.rs:112-132) and the pre-attention norm + rotation of the
 // q|k|v|gate input (model.rs:230-262). phi_post / phi_res read the same
@@ -317,6 +491,7 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
                                  float* __restrict__ xh_out, float* __restrict__ gates, int rbmax,
                                  int gmax) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x;
   const int n = G.lanes, d = G.d, W = n * d;
@@ -415,83 +590,124 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
     }
   }
   __syncthreads();
-  // Warp 0 forms the gates; the mix-down gate releases warps 1.. (named
-  // barrier 1) while warp 0 runs Sinkhorn, which nothing below depends on.
-  const int nwo = nw - 1, wo = wid - 1, to = tid - 32, NT = blockDim.x - 32;
+  const float* ek = site >= 0 ? ekv + (size_t)r * G.n_sites * 2 * d + (size_t)site * 2 * d : nullptr;
+  const float* ev = site >= 0 ? evc + ((size_t)r * G.n_sites + site) * d : nullptr;
+  layer_pre_tail(G, li, r, mp, phi, L, gsm, red, bx, hb, norm_in, ek, ev, u_out, bx_out, xh_out, gates);
+}
+
+// The same computation for a few rows (batch-1 and small-batch decode), split
+// over the 128-wide groups of the lanes so that one row occupies many SMs.
+// CTA (g, r) rotates group g of row r's lanes, adds its sum of squares and its
+// part of each of the 2n + n^2 dots (row k's group-g codes against the rotated
+// group, times the group norm; cq.rs:666-672 sums norm * group_dot) into
+// part[r][g][...]; the last CTA of the row to arrive (per-row counter, reset by
+// that CTA) sums the groups in order, applies rms_unit (kernels.rs:32; a common
+// factor of every dot, applied to the finished sums) and runs the tail. No CTA
+// waits for another.
+constexpr int PRE_SPLIT_MAX_ROWS = 8;
+constexpr int PRE_SPLIT_MAX_GROUPS = 32;
+__global__ void __launch_bounds__(256) layer_pre_split_kernel(
+    Geo G, int li, RowBatch rb, const float* __restrict__ lanes, CqMat phi_pre, CqMat phi_post, CqMat phi_res,
+    MhcParams mp, const float* __restrict__ norm_in, int site, const float* __restrict__ ekv,
+    const float* __restrict__ evc, float* __restrict__ u_out, float* __restrict__ bx_out, float* __restrict__ xh_out,
+    float* __restrict__ gates, float* __restrict__ part, int* __restrict__ cnt) {
+  pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  extern __shared__ __align__(16) float sm[];
+  __shared__ __align__(16) float X[128];
+  __shared__ float lev[48], phi[32], red[32], gsm[24];
+  __shared__ int last;
+  load_phi_levels(phi_pre, phi_post, phi_res, lev);  // kernel parameters only: before the wait
+  pdl_wait();  // everything below reads or writes what earlier kernels touch
+  const int g = blockIdx.x, r = blockIdx.y;
+  const int n = G.lanes, d = G.d, W = n * d, ng = W / 128, nrow = 2 * n + n * n;
+  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
+  const int dpad = (d + 127) / 128 * 128;
+  float* bx = sm;              // [d]
+  float* hb = sm + d;          // [dpad]
+  float* Ls = hb + dpad;       // [W] the row's lanes (last CTA)
+  float* eks = Ls + W;         // [d] Engram key (last CTA, with a site)
+  float* evs = eks + d;        // [d] Engram value
+  float* nis = evs + d;        // [d] norm_in
+  float* pr = part + ((size_t)r * PRE_SPLIT_MAX_GROUPS + g) * 32;  // [0, nrow): dots; [31]: sum of squares
   if (wid == 0) {
-    const int act = li % n;
-    float hpost = 0.f;
-    if (lane < n) {
-      const float pre_off = lane == act ? 4.0f : -4.0f;   // mhc.rs:56
-      const float post_off = lane == act ? 0.0f : -4.0f;  // mhc.rs:65
-      gsm[lane] = sigmoidf_(mp.a_pre * phi[lane] + mp.b_pre[lane] + pre_off);
-      hpost = 2.0f * sigmoidf_(mp.a_post * phi[n + lane] + mp.b_post[lane] + post_off);
-    }
-    __syncwarp();
-    asm volatile("bar.arrive 1, %0;" ::"r"(blockDim.x) : "memory");
-    const float m = lane < n * n ? mp.a_res * phi[2 * n + lane] + mp.b_res[lane] : 0.f;
-    const float hres = sinkhorn_lane_fast(m, n);
-    float* gout = gates + (size_t)r * 24;
-    if (lane < n) gout[lane] = hpost;
-    if (lane < n * n) gout[n + lane] = hres;
-    return;
-  }
-  asm volatile("bar.sync 1, %0;" ::"r"(blockDim.x) : "memory");
-  // Warps 1..: reductions over NT threads on named barrier 2.
-  auto gsum = [&](float v) {
-    v = warp_sum(v);
-    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
-    if (lane == 0) red[wo] = v;
-    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
-    return warp_sum(lane < nwo ? red[lane] : 0.f);
-  };
-  // u = sum_i hpre_i * lane_i (mix_down), bx = u (+ Engram).
-#pragma unroll 4
-  for (int c = to; c < d; c += NT) {
-    float acc = 0.f;
-    for (int l = 0; l < n; ++l) acc += gsm[l] * L[l * d + c];
-    bx[c] = acc;
-    u_out[(size_t)r * d + c] = acc;
-  }
-  asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
-  if (site >= 0) {
-    const size_t kv_ld = (size_t)G.n_sites * 2 * d;
-    const float* ek = ekv + (size_t)r * kv_ld + (size_t)site * 2 * d;
-    const float* ev = evc + ((size_t)r * G.n_sites + site) * d;
-    float sx = 0.f, sk = 0.f, sd = 0.f;
-#pragma unroll 4
-    for (int c = to; c < d; c += NT) {
-      float x = bx[c], k = ek[c];
-      sx += x * x;
-      sk += k * k;
-      sd += x * k;
-    }
-    sx = gsum(sx);
-    sk = gsum(sk);
-    sd = gsum(sd);
-    const float ux = 1.0f / sqrtf(sx / (float)d + 1e-6f);
-    const float uk = 1.0f / sqrtf(sk / (float)d + 1e-6f);
-    const float alpha = sigmoidf_(sd * ux * uk / sqrtf((float)d));
-#pragma unroll 4
-    for (int c = to; c < d; c += NT) bx[c] += alpha * ev[c];
-    asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
-  }
-  float s2 = 0.f;
-  for (int c = to; c < d; c += NT) s2 += bx[c] * bx[c];
-  s2 = gsum(s2);
-  const float inv2 = 1.0f / sqrtf(s2 / (float)d + EPS);  // zc_rms_norm_vec, norm.rs:23
-#pragma unroll 4
-  for (int c = to; c < dpad; c += NT) {
-    hb[c] = c < d ? (1.0f + norm_in[c]) * bx[c] * inv2 : 0.f;
-    if (c < d) bx_out[(size_t)r * d + c] = bx[c];
-  }
-  asm volatile("bar.sync 2, %0;" ::"r"(NT) : "memory");
-  for (int g = wo; g < dpad / 128; g += nwo) {
-    float4 v = reinterpret_cast<float4*>(hb + g * 128)[lane];
+    const float4 v = __ldg(reinterpret_cast<const float4*>(lanes + (size_t)r * W + g * 128) + lane);
     float x[4] = {v.x, v.y, v.z, v.w};
+    const float ss = warp_sum(x[0] * x[0] + x[1] * x[1] + x[2] * x[2] + x[3] * x[3]);
     fwht128_warp(x);
-    reinterpret_cast<float4*>(xh_out + (size_t)r * dpad + g * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    reinterpret_cast<float4*>(X)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    if (lane == 0) pr[31] = ss;
   }
+  __syncthreads();
+  const float4 x = reinterpret_cast<const float4*>(X)[lane];
+  // Rows wid, wid + 8, wid + 16 (nrow <= 24): every row's codes and norm are
+  // loaded before any is used, one L2 round trip for the three.
+  uint32_t cw[3] = {0u, 0u, 0u};
+  float nw3[3] = {0.f, 0.f, 0.f};
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    const int k = wid + q * nw;
+    if (k < nrow) {
+      const uint8_t* row;
+      const __half* nrm;
+      int rbo, go;
+      phi_row(k, mp.phi_layer, n, phi_pre, phi_post, phi_res, &row, &nrm, &rbo, &go);
+      const int b = k < n ? phi_pre.bits : (k < 2 * n ? phi_post.bits : phi_res.bits);
+      cw[q] = cq_quad_codes(row, b, g, lane);
+      nw3[q] = __half2float(nrm[g]);
+    }
+  }
+#pragma unroll
+  for (int q = 0; q < 3; ++q) {
+    const int k = wid + q * nw;
+    if (k < nrow) {
+      const int b = k < n ? phi_pre.bits : (k < 2 * n ? phi_post.bits : phi_res.bits), mask = (1 << b) - 1;
+      const float* lv = lev + (k < n ? 0 : (k < 2 * n ? 16 : 32));
+      const uint32_t c = cw[q];
+      float p = lv[c & mask] * x.x;
+      p += lv[(c >> b) & mask] * x.y;
+      p += lv[(c >> (2 * b)) & mask] * x.z;
+      p += lv[(c >> (3 * b)) & mask] * x.w;
+      p = warp_sum(p);
+      if (lane == 0) pr[k] = nw3[q] * p;
+    }
+  }
+  __threadfence();
+  __syncthreads();
+  if (tid == 0) last = atomicAdd(&cnt[r], 1) == ng - 1;
+  __syncthreads();
+  if (!last) return;
+  __threadfence();
+  if (tid == 0) cnt[r] = 0;  // ready for the next launch
+  // The tail's inputs, copied while the partials are summed.
+  const float* ek = site >= 0 ? ekv + (size_t)r * G.n_sites * 2 * d + (size_t)site * 2 * d : nullptr;
+  const float* ev = site >= 0 ? evc + ((size_t)r * G.n_sites + site) * d : nullptr;
+  for (int i = 4 * tid; i < W; i += 4 * blockDim.x) cp_async16(Ls + i, lanes + (size_t)r * W + i, true);
+  for (int i = 4 * tid; i < d; i += 4 * blockDim.x) {
+    cp_async16(nis + i, norm_in + i, true);
+    if (ek) {
+      cp_async16(eks + i, ek + i, true);
+      cp_async16(evs + i, ev + i, true);
+    }
+  }
+  cp_commit();
+  if (tid < 32) {
+    // All partials in flight at once (one L2 round trip), then summed in
+    // group order.
+    float pv[PRE_SPLIT_MAX_GROUPS];
+    const bool used = tid < nrow || tid == 31;
+#pragma unroll
+    for (int gg = 0; gg < PRE_SPLIT_MAX_GROUPS; ++gg)
+      pv[gg] = (used && gg < ng) ? __ldcg(part + ((size_t)r * PRE_SPLIT_MAX_GROUPS + gg) * 32 + tid) : 0.f;
+    float v = 0.f;
+#pragma unroll
+    for (int gg = 0; gg < PRE_SPLIT_MAX_GROUPS; ++gg) v += pv[gg];
+    const float inv = 1.0f / sqrtf(__shfl_sync(0xffffffffu, v, 31) / (float)W + EPS);  // rms_unit_to, kernels.rs:32
+    if (tid < nrow) phi[tid] = v * inv;
+  }
+  cp_wait<0>();
+  __syncthreads();
+  layer_pre_tail(G, li, r, mp, phi, Ls, gsm, red, bx, hb, nis, ek ? eks : nullptr, ek ? evs : nullptr, u_out,
+                 bx_out, xh_out, gates);
 }
 
 // The same computation for many rows: PT_M rows per CTA so each mHC weight
@@ -521,6 +737,7 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
                        const float* __restrict__ evc, float* __restrict__ u_out, float* __restrict__ bx_out,
                        float* __restrict__ xh_out, float* __restrict__ gates) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   __shared__ __align__(16) float Xr[PT_S][PT_M][128];
   __shared__ float phi_s[PT_M][24];
   __shared__ float ss_s[PT_M];
@@ -747,18 +964,29 @@ static cudaError_t launch_pre_tiled(const Geo& G, int li, const RowBatch& rb, co
                                     const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                                     const float* evc, float* u, float* bx, float* xh, float* gates,
                                     cudaStream_t st) {
-  layer_pre_tiled_kernel<PT_M><<<(rb.M + PT_M - 1) / PT_M, 256, 0, st>>>(G, li, rb, lanes, mp, norm_in, site, ekv,
-                                                                       evc, u, bx, xh, gates);
-  return cudaGetLastError();
+  return launch_pdl(layer_pre_tiled_kernel<PT_M>, dim3((rb.M + PT_M - 1) / PT_M), dim3(256), 0, st, G, li, rb, lanes,
+                    mp, norm_in, site, ekv, evc, u, bx, xh, gates);
 }
 
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                              const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
                              const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                              const float* evc, float* u, float* bx, float* xh, float* gates,
-                             cudaStream_t st) {
+                             cudaStream_t st, float* split_part, int* split_cnt) {
   if (rb.M <= 0) return cudaSuccess;
   const int nrow = 2 * G.lanes + G.lanes * G.lanes;
+  // Up to PRE_SPLIT_MAX_ROWS rows: every row over (lanes x d_model) / 128 CTAs.
+  const int ngr = G.lanes * G.d / 128;
+  if (split_part && split_cnt && rb.M <= PRE_SPLIT_MAX_ROWS && G.d % 128 == 0 && ngr <= PRE_SPLIT_MAX_GROUPS &&
+      nrow <= 24 && phi_pre.groups == ngr && phi_post.groups == ngr && phi_res.groups == ngr &&
+      (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0 && (reinterpret_cast<uintptr_t>(lanes) & 15) == 0 &&
+      (reinterpret_cast<uintptr_t>(ekv) & 15) == 0 && (reinterpret_cast<uintptr_t>(evc) & 15) == 0) {
+    const size_t smem = (size_t)(G.d + G.d + ngr * 128 + 3 * G.d) * sizeof(float);
+    cudaError_t e = allow_smem((const void*)layer_pre_split_kernel, smem);
+    if (e != cudaSuccess) return e;
+    return launch_pdl(layer_pre_split_kernel, dim3(ngr, rb.M), dim3(256), smem, st, G, li, rb, lanes, phi_pre,
+                      phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates, split_part, split_cnt);
+  }
   const int rbmax = std::max(phi_pre.row_bytes, std::max(phi_post.row_bytes, phi_res.row_bytes));
   const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
   const bool tiled_ok = G.d % 128 == 0 && G.d / 128 <= PT_DQ && nrow <= 24 && G.lanes <= 4 &&
@@ -778,9 +1006,8 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
                       (size_t)nrow * rbmax + 16;
   cudaError_t e = allow_smem((const void*)layer_pre_kernel, smem);
   if (e != cudaSuccess) return e;
-  layer_pre_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lanes, phi_pre, phi_post, phi_res, mp, norm_in,
-                                            site, ekv, evc, u, bx, xh, gates, rbmax, gmax);
-  return cudaGetLastError();
+  return launch_pdl(layer_pre_kernel, dim3(rb.M), dim3(256), smem, st, G, li, rb, lanes, phi_pre, phi_post, phi_res,
+                    mp, norm_in, site, ekv, evc, u, bx, xh, gates, rbmax, gmax);
 }
 
 // ---------------------------------------------------------------- Q/K/V post-processing
@@ -794,6 +1021,201 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
 // One activation row, handled by the whole CTA (WARP = false: the conv phase
 // over every thread, the heads spread over the warps) or by one warp (WARP =
 // true: many rows per CTA, for large batches). `sm` holds qkv_dim floats.
+// Causal depthwise conv of channel c of row r (attention.rs:82-100,
+// cache.rs:401-438): taps over the raw projections of the previous positions
+// (the prompt's own rows in prefill, the session's tail ring in decode), and
+// the raw value stored into the ring for the positions after it. The
+// vectorised loop of qkv_post_row performs the same operations per channel.
+__device__ __forceinline__ float qkv_conv_chan(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
+                                               const RowInfo& ri, const float* __restrict__ proj, int r, int c) {
+  const int qd = G.q_dim, kd = G.k_dim, vd = G.v_dim, qkv = G.qkv_dim;
+  const int taps = G.taps, tl = taps > 0 ? taps - 1 : 0, p = ri.pos;
+  const float* tp;
+  int dim, cc;
+  if (c < qd) {
+    tp = lp.q_taps; dim = qd; cc = c;
+  } else if (c < qd + kd) {
+    tp = lp.k_taps; dim = kd; cc = c - qd;
+  } else {
+    tp = lp.v_taps; dim = vd; cc = c - qd - kd;
+  }
+  const float x = proj[(size_t)r * G.proj_dim + c];
+  if (taps <= 0) return x;
+  float* tail = tl ? ri.s->qkv_tail + (size_t)li * tl * qkv : nullptr;
+  float acc = tp[cc] * x;
+#pragma unroll
+  for (int j = 1; j < MAX_QKV_TAPS; ++j) {
+    if (j >= taps || j > p) continue;
+    const float prev = rb.mode == MODE_PREFILL ? proj[(size_t)(r - j) * G.proj_dim + c]
+                                               : tail[(size_t)((p - j) % tl) * qkv + c];
+    acc += tp[j * dim + cc] * prev;
+  }
+  if (tl && (rb.mode == MODE_DECODE || p >= ri.len - tl)) tail[(size_t)(p % tl) * qkv + c] = x;
+  return acc;
+}
+
+// Task t of row r held by one warp: q head t (t < heads) or k head t - heads
+// (norm + RoPE, attention.rs:107-143; int8 query fake-quant, model.rs:289-293)
+// or v head t - heads - kvh, then the stores (quantize-on-append in int8
+// mode, cache.rs:346-377). x1, x2: the lane's two conv outputs, channels
+// qkv_task_chan gives (0 on lanes past the head's half).
+// What every task of one row needs, read once per row: the layer's KV ring,
+// the RoPE row of the position and where the new K/V go.
+struct QkvRowCtx {
+  LayerKV kv;
+  const float* cs;  // cos
+  const float* sn;  // sin
+  int slot;
+  bool int8, prefill, to_ring;
+};
+__device__ __forceinline__ QkvRowCtx qkv_row_ctx(const Geo& G, int li, const RowBatch& rb, const RowInfo& ri,
+                                                 const float* __restrict__ rope_cs) {
+  QkvRowCtx c;
+  const int p = ri.pos, half = G.qk / 2;
+  c.cs = rope_cs + (size_t)p * half;
+  c.sn = rope_cs + (size_t)G.max_seq * half + (size_t)p * half;
+  c.int8 = ri.s->int8 != 0;
+  c.prefill = rb.mode == MODE_PREFILL;
+  c.kv = ri.s->layers[li];
+  c.slot = p % c.kv.slots;
+  c.to_ring = !c.prefill || p >= ri.len - c.kv.slots;
+  return c;
+}
+
+__device__ __forceinline__ void qkv_task(const Geo& G, const LayerParams& lp, float* __restrict__ qpost, void* pk,
+                                         void* pv, float* pks, float* pvs, int8_t* __restrict__ q8out,
+                                         float* __restrict__ q8s, int r, const QkvRowCtx& ctx, int t, float x1,
+                                         float x2) {
+  const int lane = threadIdx.x & 31;
+  const int qd = G.q_dim;
+  const int half = G.qk / 2;
+  const float* cs = ctx.cs;
+  const float* sn = ctx.sn;
+  const bool int8 = ctx.int8;
+  const bool prefill = ctx.prefill;
+  const LayerKV& kv = ctx.kv;
+  const int slot = ctx.slot;
+  const bool to_ring = ctx.to_ring;
+  if (t < G.heads + G.kvh) {
+    // q head t, or k head t-heads: norm + rope.
+    const bool isq = t < G.heads;
+    const int h = isq ? t : t - G.heads;
+    const float* sc = isq ? lp.q_norm : lp.k_norm;
+    float sq = warp_sum(x1 * x1 + x2 * x2);
+    float rms = sqrtf(sq / (float)G.qk + 1e-6f);
+    if (lane < half) {
+      x1 = (1.0f + sc[lane]) * x1 / rms;
+      x2 = (1.0f + sc[half + lane]) * x2 / rms;
+      float c = cs[lane], s = sn[lane];
+      float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
+      x1 = y1;
+      x2 = y2;
+    }
+    if (isq) {
+      if (int8) {
+        // The codes and scale also go to q8out / q8s for the integer score
+        // path of the int8 attention; code * scale is the fake-quantised query.
+        float c1, c2;
+        const float scale = kv_quant_warp(x1, x2, &c1, &c2);
+        if (q8out && lane < half) {
+          q8out[(size_t)r * qd + h * G.qk + lane] = (int8_t)c1;
+          q8out[(size_t)r * qd + h * G.qk + half + lane] = (int8_t)c2;
+        }
+        if (q8out && lane == 0) q8s[(size_t)r * G.heads + h] = scale;
+        x1 = c1 * scale;
+        x2 = c2 * scale;
+      }
+      if (lane < half) {
+        qpost[(size_t)r * qd + h * G.qk + lane] = x1;
+        qpost[(size_t)r * qd + h * G.qk + half + lane] = x2;
+      }
+    } else if (int8) {
+      float c1, c2;
+      const float scale = kv_quant_warp(x1, x2, &c1, &c2);
+      const int8_t a = (int8_t)c1, b = (int8_t)c2;
+      if (lane < half) {
+        if (prefill) {
+          int8_t* d8 = (int8_t*)pk + ((size_t)r * G.kvh + h) * G.qk;
+          d8[lane] = a;
+          d8[half + lane] = b;
+        }
+        if (to_ring) {
+          int8_t* d8 = (int8_t*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
+          d8[lane] = a;
+          d8[half + lane] = b;
+        }
+      }
+      if (lane == 0) {
+        if (prefill) pks[(size_t)r * G.kvh + h] = scale;
+        if (to_ring) kv.ks[(size_t)h * kv.slots + slot] = scale;
+      }
+    } else if (lane < half) {
+      if (prefill) {
+        float* df = (float*)pk + ((size_t)r * G.kvh + h) * G.qk;
+        df[lane] = x1;
+        df[half + lane] = x2;
+      }
+      if (to_ring) {
+        float* df = (float*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
+        df[lane] = x1;
+        df[half + lane] = x2;
+      }
+    }
+  } else {
+    // v head: conv output only, then store (quantised in int8 mode).
+    const int h = t - G.heads - G.kvh;
+    const int vhalf = G.vh / 2;
+    if (int8) {
+      float c1, c2;
+      const float scale = kv_quant_warp(x1, x2, &c1, &c2);
+      const int8_t a = (int8_t)c1, b = (int8_t)c2;
+      if (lane < vhalf) {
+        if (prefill) {
+          int8_t* d8 = (int8_t*)pv + ((size_t)r * G.kvh + h) * G.vh;
+          d8[lane] = a;
+          d8[vhalf + lane] = b;
+        }
+        if (to_ring) {
+          int8_t* d8 = (int8_t*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
+          d8[lane] = a;
+          d8[vhalf + lane] = b;
+        }
+      }
+      if (lane == 0) {
+        if (prefill) pvs[(size_t)r * G.kvh + h] = scale;
+        if (to_ring) kv.vs[(size_t)h * kv.slots + slot] = scale;
+      }
+    } else if (lane < vhalf) {
+      if (prefill) {
+        float* df = (float*)pv + ((size_t)r * G.kvh + h) * G.vh;
+        df[lane] = x1;
+        df[vhalf + lane] = x2;
+      }
+      if (to_ring) {
+        float* df = (float*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
+        df[lane] = x1;
+        df[vhalf + lane] = x2;
+      }
+    }
+  }
+}
+
+// The two channels (of the q|k|v conv output) lane `lane` holds in task t, or
+// false on lanes past the head's half.
+__device__ __forceinline__ bool qkv_task_chan(const Geo& G, int t, int lane, int* c1, int* c2) {
+  int base, hf;
+  if (t < G.heads + G.kvh) {
+    base = t < G.heads ? t * G.qk : G.q_dim + (t - G.heads) * G.qk;
+    hf = G.qk / 2;
+  } else {
+    base = G.q_dim + G.k_dim + (t - G.heads - G.kvh) * G.vh;
+    hf = G.vh / 2;
+  }
+  *c1 = base + lane;
+  *c2 = base + hf + lane;
+  return lane < hf;
+}
+
 template <bool WARP>
 __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                                              const float* __restrict__ rope_cs, const float* __restrict__ proj,
@@ -844,160 +1266,29 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
       }
       *reinterpret_cast<float4*>(sm + c) = acc;
     }
-  } else
+  } else {
 #pragma unroll 4
-  for (int c = tix; c < qkv; c += nthr) {
-    const float* tp;
-    int dim, cc;
-    if (c < qd) {
-      tp = lp.q_taps; dim = qd; cc = c;
-    } else if (c < qd + kd) {
-      tp = lp.k_taps; dim = kd; cc = c - qd;
-    } else {
-      tp = lp.v_taps; dim = vd; cc = c - qd - kd;
-    }
-    float x = raw[c];
-    float acc = x;
-    if (taps > 0) {
-      acc = tp[cc] * x;
-#pragma unroll
-      for (int j = 1; j < MAX_QKV_TAPS; ++j) {
-        if (j >= taps || j > p) continue;
-        float prev = rb.mode == MODE_PREFILL ? proj[(size_t)(r - j) * G.proj_dim + c]
-                                             : tail[(size_t)((p - j) % tl) * qkv + c];
-        acc += tp[j * dim + cc] * prev;
-      }
-      if (tl && (rb.mode == MODE_DECODE || p >= ri.len - tl)) tail[(size_t)(p % tl) * qkv + c] = x;
-    }
-    sm[c] = acc;
+    for (int c = tix; c < qkv; c += nthr) sm[c] = qkv_conv_chan(G, li, rb, lp, ri, proj, r, c);
   }
   if (WARP)
     __syncwarp();
   else
     __syncthreads();
   const int lane = threadIdx.x & 31, wid = WARP ? 0 : (int)(threadIdx.x >> 5), nw = WARP ? 1 : (int)(blockDim.x >> 5);
-  const int half = G.qk / 2;
-  const float* cs = rope_cs + (size_t)p * half;                     // cos
-  const float* sn = rope_cs + (size_t)G.max_seq * half + (size_t)p * half;  // sin
-  const bool int8 = ri.s->int8 != 0;
-  const bool prefill = rb.mode == MODE_PREFILL;
-  const LayerKV kv = ri.s->layers[li];
-  const int slot = p % kv.slots;
-  const bool to_ring = !prefill || p >= ri.len - kv.slots;
   const int ntask = G.heads + 2 * G.kvh;
+  const QkvRowCtx ctx = qkv_row_ctx(G, li, rb, ri, rope_cs);
   for (int t = wid; t < ntask; t += nw) {
-    if (t < G.heads + G.kvh) {
-      // q head t, or k head t-heads: norm + rope.
-      const bool isq = t < G.heads;
-      const int h = isq ? t : t - G.heads;
-      float* x = sm + (isq ? h * G.qk : qd + h * G.qk);
-      const float* sc = isq ? lp.q_norm : lp.k_norm;
-      float x1 = lane < half ? x[lane] : 0.f, x2 = lane < half ? x[half + lane] : 0.f;
-      float sq = warp_sum(x1 * x1 + x2 * x2);
-      float rms = sqrtf(sq / (float)G.qk + 1e-6f);
-      if (lane < half) {
-        x1 = (1.0f + sc[lane]) * x1 / rms;
-        x2 = (1.0f + sc[half + lane]) * x2 / rms;
-        float c = cs[lane], s = sn[lane];
-        float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
-        x1 = y1;
-        x2 = y2;
-      }
-      if (isq) {
-        if (int8) {
-          // The codes and scale also go to q8out / q8s for the integer score
-          // path of the int8 attention; code * scale is the fake-quantised query.
-          float c1, c2;
-          const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-          if (q8out && lane < half) {
-            q8out[(size_t)r * qd + h * G.qk + lane] = (int8_t)c1;
-            q8out[(size_t)r * qd + h * G.qk + half + lane] = (int8_t)c2;
-          }
-          if (q8out && lane == 0) q8s[(size_t)r * G.heads + h] = scale;
-          x1 = c1 * scale;
-          x2 = c2 * scale;
-        }
-        if (lane < half) {
-          qpost[(size_t)r * qd + h * G.qk + lane] = x1;
-          qpost[(size_t)r * qd + h * G.qk + half + lane] = x2;
-        }
-      } else if (int8) {
-        float c1, c2;
-        const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-        const int8_t a = (int8_t)c1, b = (int8_t)c2;
-        if (lane < half) {
-          if (prefill) {
-            int8_t* d8 = (int8_t*)pk + ((size_t)r * G.kvh + h) * G.qk;
-            d8[lane] = a;
-            d8[half + lane] = b;
-          }
-          if (to_ring) {
-            int8_t* d8 = (int8_t*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
-            d8[lane] = a;
-            d8[half + lane] = b;
-          }
-        }
-        if (lane == 0) {
-          if (prefill) pks[(size_t)r * G.kvh + h] = scale;
-          if (to_ring) kv.ks[(size_t)h * kv.slots + slot] = scale;
-        }
-      } else if (lane < half) {
-        if (prefill) {
-          float* df = (float*)pk + ((size_t)r * G.kvh + h) * G.qk;
-          df[lane] = x1;
-          df[half + lane] = x2;
-        }
-        if (to_ring) {
-          float* df = (float*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
-          df[lane] = x1;
-          df[half + lane] = x2;
-        }
-      }
-    } else {
-      // v head: conv output only, then store (quantised in int8 mode).
-      const int h = t - G.heads - G.kvh;
-      const float* x = sm + qd + kd + h * G.vh;
-      const int vhalf = G.vh / 2;
-      float x1 = lane < vhalf ? x[lane] : 0.f, x2 = lane < vhalf ? x[vhalf + lane] : 0.f;
-      if (int8) {
-        float c1, c2;
-        const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-        const int8_t a = (int8_t)c1, b = (int8_t)c2;
-        if (lane < vhalf) {
-          if (prefill) {
-            int8_t* d8 = (int8_t*)pv + ((size_t)r * G.kvh + h) * G.vh;
-            d8[lane] = a;
-            d8[vhalf + lane] = b;
-          }
-          if (to_ring) {
-            int8_t* d8 = (int8_t*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
-            d8[lane] = a;
-            d8[vhalf + lane] = b;
-          }
-        }
-        if (lane == 0) {
-          if (prefill) pvs[(size_t)r * G.kvh + h] = scale;
-          if (to_ring) kv.vs[(size_t)h * kv.slots + slot] = scale;
-        }
-      } else if (lane < vhalf) {
-        if (prefill) {
-          float* df = (float*)pv + ((size_t)r * G.kvh + h) * G.vh;
-          df[lane] = x1;
-          df[vhalf + lane] = x2;
-        }
-        if (to_ring) {
-          float* df = (float*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
-          df[lane] = x1;
-          df[vhalf + lane] = x2;
-        }
-      }
-    }
+    int c1, c2;
+    const bool on = qkv_task_chan(G, t, lane, &c1, &c2);
+    qkv_task(G, lp, qpost, pk, pv, pks, pvs, q8out, q8s, r, ctx, t, on ? sm[c1] : 0.f, on ? sm[c2] : 0.f);
   }
 }
 
 __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
                                 const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv,
                                 float* pks, float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) float sm[];
   qkv_post_row<false>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, blockIdx.x, sm);
 }
@@ -1010,11 +1301,36 @@ __global__ void __launch_bounds__(QP_ROWS * 32)
 qkv_post_rows_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
                      const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv, float* pks,
                      float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) float sm[];
   const int w = threadIdx.x >> 5, r = blockIdx.x * QP_ROWS + w;
   if (r >= rb.M) return;
   const int stride = (G.qkv_dim + 3) / 4 * 4;
   qkv_post_row<true>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, r, sm + (size_t)w * stride);
+}
+
+// Small batches: one warp per task (q, k or v head) of a row, QH_TASKS tasks
+// per CTA, each warp running the conv of its own channels, so that a row's
+// heads spread over many SMs instead of queueing on one CTA's eight warps.
+constexpr int QH_TASKS = 4;
+constexpr int QH_MAX_ROWS = 128;
+__global__ void __launch_bounds__(QH_TASKS * 32)
+qkv_post_head_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
+                     const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv, float* pks,
+                     float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x, t = blockIdx.y * QH_TASKS + (int)(threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (t >= G.heads + 2 * G.kvh) return;  // the whole warp
+  const RowInfo ri = rb.rows[r];
+  int c1, c2;
+  float x1 = 0.f, x2 = 0.f;
+  if (qkv_task_chan(G, t, lane, &c1, &c2)) {
+    x1 = qkv_conv_chan(G, li, rb, lp, ri, proj, r, c1);
+    x2 = qkv_conv_chan(G, li, rb, lp, ri, proj, r, c2);
+  }
+  qkv_task(G, lp, qpost, pk, pv, pks, pvs, q8out, q8s, r, qkv_row_ctx(G, li, rb, ri, rope_cs), t, x1, x2);
 }
 
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
@@ -1026,13 +1342,17 @@ cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const Laye
     const size_t smem = (size_t)QP_ROWS * ((G.qkv_dim + 3) / 4 * 4) * sizeof(float);
     cudaError_t e = allow_smem((const void*)qkv_post_rows_kernel, smem);
     if (e != cudaSuccess) return e;
-    qkv_post_rows_kernel<<<(rb.M + QP_ROWS - 1) / QP_ROWS, QP_ROWS * 32, smem, st>>>(
-        G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
-    return cudaGetLastError();
+    return launch_pdl(qkv_post_rows_kernel, dim3((rb.M + QP_ROWS - 1) / QP_ROWS), dim3(QP_ROWS * 32), smem, st, G,
+                      li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
+  }
+  if (rb.M <= QH_MAX_ROWS) {
+    const int ntask = G.heads + 2 * G.kvh;
+    return launch_pdl(qkv_post_head_kernel, dim3(rb.M, (ntask + QH_TASKS - 1) / QH_TASKS), dim3(QH_TASKS * 32), 0,
+                      st, G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
   }
   const size_t smem = (size_t)G.qkv_dim * sizeof(float);
-  qkv_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s);
-  return cudaGetLastError();
+  return launch_pdl(qkv_post_kernel, dim3(rb.M), dim3(256), smem, st, G, li, rb, lp, rope_cs, proj, qpost, pk, pv,
+                    pks, pvs, q8out, q8s);
 }
 
 // ---------------------------------------------------------------- block tail
@@ -1115,6 +1435,8 @@ __global__ void layer_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp,
                                   const float* __restrict__ projo, const float* __restrict__ u,
                                   const float* __restrict__ bx_in, const float* __restrict__ gates,
                                   float* __restrict__ lanes) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) float sm[];
   const int r = blockIdx.x;
   const int d = G.d, n = G.hada_n, nl = G.lanes;
@@ -1218,8 +1540,8 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
       (size_t)(2 * G.d + 4 * G.hada_n + 4 * G.bb + G.ba * G.ba + G.bb * G.bb + 32 + 8 + 24) * sizeof(float);
   cudaError_t e = allow_smem((const void*)layer_post_kernel, smem);
   if (e != cudaSuccess) return e;
-  layer_post_kernel<<<rb.M, 256, smem, st>>>(G, li, rb, lp, p1, p2, projo, u, bx, gates, lanes);
-  return cudaGetLastError();
+  return launch_pdl(layer_post_kernel, dim3(rb.M), dim3(256), smem, st, G, li, rb, lp, p1, p2, projo, u, bx, gates,
+                    lanes);
 }
 
 // ---------------------------------------------------------------- head
@@ -1227,6 +1549,7 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
 __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float* __restrict__ fnorm,
                              float* __restrict__ lm_in) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
+  pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) float sm[];
   float* red = sm;
   float* x = sm + 32;
@@ -1254,13 +1577,15 @@ cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
                          const float* final_norm, float* lm_in, cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   const int dpad = (G.d + 127) / 128 * 128;
-  final_kernel<<<rb.M, 256, (32 + dpad) * sizeof(float), st>>>(G, lanes, final_norm, lm_in);
-  return cudaGetLastError();
+  return launch_pdl(final_kernel, dim3(rb.M), dim3(256), (32 + dpad) * sizeof(float), st, G, lanes, final_norm,
+                    lm_in);
 }
 
 // Greedy pick: the first maximum, as argmax (v3_engine.rs:410-420) keeps the
 // lowest index on ties and never picks a NaN.
 __global__ void argmax_kernel(const float* __restrict__ logits, int n, int ld, uint32_t* out) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int r = blockIdx.x;
@@ -1305,8 +1630,7 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n, int ld, u
 
 cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
-  argmax_kernel<<<M, 256, 0, st>>>(logits, n, ld, out);
-  return cudaGetLastError();
+  return launch_pdl(argmax_kernel, dim3(M), dim3(256), 0, st, logits, n, ld, out);
 }
 
 // ---------------------------------------------------------------- step bookkeeping
