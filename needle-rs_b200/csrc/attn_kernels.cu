@@ -628,11 +628,11 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
 // copied by lane 0 and completing on W.bar[buf]; the scales go by cp.async
 // (zero-filled past hi). Rows past hi keep stale bytes: their scores are
 // masked and their value scales are zero, so they contribute nothing.
+// idx0 = n0 mod slots (the caller steps it from block to block).
 template <int QK, int VH>
 __device__ __forceinline__ void mma_issue_bulk(MmaWarpSmem<QK, VH>& W, int buf, const AttnSrc& src, int kh,
-                                               int n0, int hi, int lane) {
+                                               int n0, int idx0, int hi, int lane) {
   const int cnt = min(WB, hi - n0 + 1);
-  const int idx0 = n0 % src.slots;
   if (lane == 0) {
     const int c1 = min(cnt, src.slots - idx0);
     const int8_t* kb = (const int8_t*)src.k + kh * src.k_head;
@@ -732,14 +732,19 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
   }
   // Block c of this warp (position a + (wid + 4c) * WB) goes to buffer c % NBUF;
   // one cp.async commit group per block (empty past the last) keeps the
-  // group count uniform.
+  // group count uniform. Blocks are issued in order, so the ring index of the
+  // next one steps by 4 * WB instead of a modulo per block.
+  int ring_idx = bulk ? (a + wid * WB) % src.slots : 0;
   auto issue = [&](int c) {
     if (c < mine) {
       const int n0 = a + (wid + 4 * c) * WB;
-      if (bulk)
-        mma_issue_bulk<QK, VH>(W, c % NBUF, src, kh, n0, b, lane);
-      else
+      if (bulk) {
+        mma_issue_bulk<QK, VH>(W, c % NBUF, src, kh, n0, ring_idx, b, lane);
+        ring_idx += 4 * WB;
+        while (ring_idx >= src.slots) ring_idx -= src.slots;
+      } else {
         mma_issue<QK, VH>(W, c % NBUF, src, kh, n0, b, lane);
+      }
     }
     cp_commit();
   };
@@ -787,20 +792,34 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
     }
     // Score i of this lane: position j*16 + g + 8*hf (i = 4j + 2hf + e), head 2t + e.
     float sc[4 * NJ];
+    if (n0 + WB - 1 <= b) {  // a full block (warp-uniform): no position masked
 #pragma unroll
-    for (int j = 0; j < NJ; ++j)
+      for (int j = 0; j < NJ; ++j)
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        const int pi = j * 16 + hf * 8 + g;
-        const float ksv = W.ks[buf][pi];
-        const bool ok = n0 + pi <= b;
+        for (int hf = 0; hf < 2; ++hf) {
+          const float ksv = W.ks[buf][j * 16 + hf * 8 + g];
 #pragma unroll
-        for (int e = 0; e < 2; ++e)
-          sc[4 * j + 2 * hf + e] = ok ? (float)d[j][2 * hf + e] * qsc[e] * ksv : -INFINITY;
-      }
+          for (int e = 0; e < 2; ++e) sc[4 * j + 2 * hf + e] = (float)d[j][2 * hf + e] * qsc[e] * ksv;
+        }
+    } else {
+#pragma unroll
+      for (int j = 0; j < NJ; ++j)
+#pragma unroll
+        for (int hf = 0; hf < 2; ++hf) {
+          const int pi = j * 16 + hf * 8 + g;
+          const float ksv = W.ks[buf][pi];
+          const bool ok = n0 + pi <= b;
+#pragma unroll
+          for (int e = 0; e < 2; ++e)
+            sc[4 * j + 2 * hf + e] = ok ? (float)d[j][2 * hf + e] * qsc[e] * ksv : -INFINITY;
+        }
+    }
     // ---- online softmax per head (column): the 8 lanes sharing t hold
     // the block's WB positions of heads 2t, 2t + 1
-    float corr[2], mz[2];
+    // When no running max of the warp moved, every correction factor is
+    // exp2(0) = 1 and the rescale of l and O is skipped (warp-uniform).
+    float mold[2], mz[2];
+    bool moved = false;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       float mx = sc[e];
@@ -810,19 +829,26 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
       const float mnew = fmaxf(m[e], mx);
+      moved |= mnew != m[e];
       mz[e] = mnew == -INFINITY ? 0.f : mnew;  // every position so far masked: weights are 0
-      corr[e] = ex2_fast(m[e] - mz[e]);
+      mold[e] = m[e];
       m[e] = mnew;
     }
+    const bool rescale = __any_sync(0xffffffffu, moved);
     float pw[4 * NJ];
 #pragma unroll
     for (int i = 0; i < 4 * NJ; ++i) pw[i] = ex2_fast(sc[i] - mz[i & 1]);
+    float corr[2] = {1.f, 1.f};
+    if (rescale) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) corr[e] = ex2_fast(mold[e] - mz[e]);
+    }
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       float sum = 0.f;
 #pragma unroll
       for (int q = 0; q < NJ; ++q) sum += pw[4 * q + e] + pw[4 * q + 2 + e];
-      l[e] = l[e] * corr[e] + sum;
+      l[e] = rescale ? l[e] * corr[e] + sum : l[e] + sum;
     }
 #pragma unroll
     for (int j = 0; j < NJ; ++j)
@@ -832,12 +858,14 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
         pw[4 * j + 2 * hf] *= vsv;
         pw[4 * j + 2 * hf + 1] *= vsv;
       }
+    if (rescale) {
 #pragma unroll
-    for (int i = 0; i < MT; ++i) {
-      o[i][0] *= corr[0];
-      o[i][1] *= corr[1];
-      o[i][2] *= corr[0];
-      o[i][3] *= corr[1];
+      for (int i = 0; i < MT; ++i) {
+        o[i][0] *= corr[0];
+        o[i][1] *= corr[1];
+        o[i][2] *= corr[0];
+        o[i][3] *= corr[1];
+      }
     }
     __syncwarp();  // f16 values visible to every lane
     // ---- O^T += V^T P^T: k-step j covers positions j*16 .. j*16+15. The
