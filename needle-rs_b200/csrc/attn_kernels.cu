@@ -487,6 +487,22 @@ __device__ __forceinline__ void mma_f16_k16(float (&d)[4], const uint32_t (&a)[4
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
+// Four (two) 8x8 b16 matrices from shared memory, lane l supplying the row
+// address of row l & 7 of matrix l >> 3; as s8 data, the A fragment of an
+// m16n8k32 (m16n8k16) integer MMA when the matrices are (rows 0-7, bytes
+// 0-15), (rows 8-15, bytes 0-15), (rows 0-7, bytes 16-31), (rows 8-15, bytes
+// 16-31) of the tile.
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* smem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(s));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t (&r)[2], const void* smem) {
+  unsigned s = (unsigned)__cvta_generic_to_shared(smem);
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n" : "=r"(r[0]), "=r"(r[1]) : "r"(s));
+}
+
 __device__ __forceinline__ void ldsm_x4_trans(uint32_t (&r)[4], const void* smem) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);
   asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
@@ -513,11 +529,11 @@ __device__ __forceinline__ uint32_t movmatrix_t(uint32_t x) {
   return y;
 }
 
-// Bytes (a0, a1, b0, b1) of two adjacent positions' dimension pair ->
-// f16 pairs (a0, b0) and (a1, b1) (exact), for V^T fragments read by
-// ldmatrix.trans straight from the int8 values.
-__device__ __forceinline__ void i8pairs_to_h2(uint32_t w, uint32_t* even, uint32_t* odd) {
-  const uint32_t u = w ^ 0x80808080u;
+// Offset-binary value bytes (code ^ 0x80, as the KV append stores them) (a0,
+// a1, b0, b1) of two adjacent positions' dimension pair -> f16 code pairs
+// (a0, b0) and (a1, b1) (exact: the byte is the low mantissa of 1024 + byte,
+// less 1152), for V^T fragments read by ldmatrix.trans straight from the ring.
+__device__ __forceinline__ void i8pairs_to_h2(uint32_t u, uint32_t* even, uint32_t* odd) {
   const __half2 bias = __halves2half2(__ushort_as_half(0x6480), __ushort_as_half(0x6480));  // 1152
   uint32_t a = __byte_perm(u, 0x64646464u, 0x4240), b = __byte_perm(u, 0x64646464u, 0x4341);
   __half2 ha = __hsub2(*reinterpret_cast<__half2*>(&a), bias);
@@ -654,8 +670,8 @@ __device__ __forceinline__ void mma_issue_bulk(MmaWarpSmem<QK, VH>& W, int buf, 
     int idx = idx0 + i;
     idx = idx >= src.slots ? idx - src.slots : idx;
     idx = ok ? idx : 0;
-    cp_async4(&W.ks[buf][i], src.ks + (long)idx * src.s_row + kh * src.s_head, ok);
-    cp_async4(&W.vs[buf][i], src.vs + (long)idx * src.s_row + kh * src.s_head, ok);
+    cp_async4(&W.ks[buf][i], src.ks + kh * src.s_head + idx, ok);  // a ring's scales: [kv head][slot]
+    cp_async4(&W.vs[buf][i], src.vs + kh * src.s_head + idx, ok);
   }
 }
 
@@ -771,23 +787,25 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
     int d[NJ][4];
 #pragma unroll
     for (int j = 0; j < NJ; ++j) d[j][0] = d[j][1] = d[j][2] = d[j][3] = 0;
+    // A fragments by ldmatrix: lane l addresses row (l >> 3 & 1) * 8 + (l & 7)
+    // of the 16-position tile at byte offset (l >> 4) * 16 of the 32-byte step
+    // (rows KS bytes apart: 16-byte aligned and bank-conflict free).
+    const int8_t* krow = W.k[buf] + (((lane >> 3) & 1) * 8 + (lane & 7)) * T::KS + (lane >> 4) * 16;
 #pragma unroll
     for (int s = 0; s < T::NK32; ++s)
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
-        const int8_t* k0 = W.k[buf] + (j * 16 + g) * T::KS + s * 32 + t * 4;
-        const int8_t* k1 = k0 + 8 * T::KS;
-        const uint32_t ka[4] = {*reinterpret_cast<const uint32_t*>(k0), *reinterpret_cast<const uint32_t*>(k1),
-                                *reinterpret_cast<const uint32_t*>(k0 + 16),
-                                *reinterpret_cast<const uint32_t*>(k1 + 16)};
+        uint32_t ka[4];
+        ldsm_x4(ka, krow + j * 16 * T::KS + s * 32);
         mma_s8_k32(d[j], ka, qb[s][0], qb[s][1]);
       }
     if (T::K16) {
+      const int8_t* krow16 = W.k[buf] + (((lane >> 3) & 1) * 8 + (lane & 7)) * T::KS + T::NK32 * 32;
 #pragma unroll
       for (int j = 0; j < NJ; ++j) {
-        const int8_t* k0 = W.k[buf] + (j * 16 + g) * T::KS + T::NK32 * 32 + t * 4;
-        mma_s8_k16(d[j], *reinterpret_cast<const uint32_t*>(k0),
-                   *reinterpret_cast<const uint32_t*>(k0 + 8 * T::KS), qb16);
+        uint32_t ka[2];
+        ldsm_x2(ka, krow16 + j * 16 * T::KS);
+        mma_s8_k16(d[j], ka[0], ka[1], qb16);
       }
     }
     // Score i of this lane: position j*16 + g + 8*hf (i = 4j + 2hf + e), head 2t + e.
@@ -1117,28 +1135,20 @@ cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const Lay
   if (!(proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64)) proj = nullptr, oh = nullptr, cnt = nullptr;
 #define NB_ATT(I8, Q, V) \
   return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, proj, oh, cnt, st)
-  const int key = G.qk * 2 + (int8 ? 1 : 0);
+  const int key = G.qk * 2;  // f32 KV (int8 KV returned above)
   if (G.vh == 64) {
     switch (key) {
       case 32: NB_ATT(false, 16, 64);
-      case 33: NB_ATT(true, 16, 64);
       case 64: NB_ATT(false, 32, 64);
-      case 65: NB_ATT(true, 32, 64);
       case 96: NB_ATT(false, 48, 64);
-      case 97: NB_ATT(true, 48, 64);
       case 128: NB_ATT(false, 64, 64);
-      case 129: NB_ATT(true, 64, 64);
     }
   } else if (G.vh == 32) {
     switch (key) {
       case 32: NB_ATT(false, 16, 32);
-      case 33: NB_ATT(true, 16, 32);
       case 64: NB_ATT(false, 32, 32);
-      case 65: NB_ATT(true, 32, 32);
       case 96: NB_ATT(false, 48, 32);
-      case 97: NB_ATT(true, 48, 32);
       case 128: NB_ATT(false, 64, 32);
-      case 129: NB_ATT(true, 64, 32);
     }
   }
 #undef NB_ATT

@@ -1137,11 +1137,20 @@ bool Engine::read_kv(Session* s, size_t li, void* k, void* v, float* ks, float* 
   // (cache.rs:214-215, :305-306); the device arena leaves them 0, which
   // attention never reads.
   const size_t kr = G.qk * eb, vr = G.vh * eb;
+  // int8 value codes sit offset-binary in the ring (code ^ 0x80): flip back.
+  if (s->int8)
+    for (uint8_t& c : hv) c ^= 0x80;
   for (size_t h = 0; h < H; ++h)
     for (size_t t = 0; t < S; ++t) {
       const bool written = t < s->pos;
       if (k) std::memcpy((uint8_t*)k + (t * H + h) * kr, hk.data() + (h * S + t) * kr, kr);
-      if (v) std::memcpy((uint8_t*)v + (t * H + h) * vr, hv.data() + (h * S + t) * vr, vr);
+      if (v) {
+        uint8_t* dv = (uint8_t*)v + (t * H + h) * vr;
+        if (s->int8 && !written)
+          std::memset(dv, 0, vr);  // never written: the reference's zero codes
+        else
+          std::memcpy(dv, hv.data() + (h * S + t) * vr, vr);
+      }
       if (ks && s->int8) ks[t * H + h] = written ? hks[h * S + t] : 1.0f;
       if (vs && s->int8) vs[t * H + h] = written ? hvs[h * S + t] : 1.0f;
     }

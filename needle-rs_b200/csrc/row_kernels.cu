@@ -1162,13 +1162,16 @@ __device__ __forceinline__ void qkv_task(const Geo& G, const LayerParams& lp, fl
       }
     }
   } else {
-    // v head: conv output only, then store (quantised in int8 mode).
+    // v head: conv output only, then store (quantised in int8 mode). Value
+    // codes are stored offset-binary (code ^ 0x80, the byte of code + 128):
+    // the attention widens them to f16 without a sign flip per byte, and the
+    // KV read-back flips them back.
     const int h = t - G.heads - G.kvh;
     const int vhalf = G.vh / 2;
     if (int8) {
       float c1, c2;
       const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-      const int8_t a = (int8_t)c1, b = (int8_t)c2;
+      const int8_t a = (int8_t)((int)c1 ^ 0x80), b = (int8_t)((int)c2 ^ 0x80);
       if (lane < vhalf) {
         if (prefill) {
           int8_t* d8 = (int8_t*)pv + ((size_t)r * G.kvh + h) * G.vh;
