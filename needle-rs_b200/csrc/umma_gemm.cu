@@ -75,11 +75,18 @@ struct Pipe {
   static constexpr int THREADS = (EPI_WARPS + 2) * 32;  // + TMA / TMEM warp + MMA warp
 };
 constexpr int UGMAX = 32;  // groups of 128 supported (in_pad <= 4096)
+// Output staging of one epilogue warp: 32 rows x 16 columns, rows 20 floats
+// apart (float4 writes of a row per lane and float4 reads of 8 rows x 64
+// bytes per warp instruction are both bank-conflict free or nearly).
+constexpr int OST = 20;
+constexpr uint32_t OUT_STAGE = 32 * OST * 4;
 // Dynamic shared memory: alignment slack, the stages, the norm table of one
-// tile ([groups][UN] f32) and the barriers.
+// tile ([groups][UN] f32), the barriers and (when it fits: every shipped
+// shape) the epilogue warps' output staging.
 template <bool EXACT, int UN>
-constexpr size_t umma_smem(int groups) {
-  return 1024 + (size_t)Pipe<EXACT, UN>::STAGES * Pipe<EXACT, UN>::STAGE_BYTES + (size_t)groups * UN * 4 + 256;
+constexpr size_t umma_smem(int groups, bool out_stage) {
+  return 1024 + (size_t)Pipe<EXACT, UN>::STAGES * Pipe<EXACT, UN>::STAGE_BYTES + (size_t)groups * UN * 4 + 256 +
+         (out_stage ? (size_t)Pipe<EXACT, UN>::EPI_WARPS * OUT_STAGE : 0);
 }
 constexpr unsigned long long WAIT_NS = 1000000000ull;  // bound of every wait: one second
 
@@ -218,7 +225,7 @@ __global__ void __launch_bounds__(Pipe<EXACT, UN>::THREADS, 1)
 cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
                const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
-               int nrows, int ntn, int ntiles, int* werr) {
+               int nrows, int ntn, int ntiles, int* werr, int out_stage) {
   using P = Pipe<EXACT, UN>;
   constexpr int USTAGES = P::STAGES;
   constexpr uint32_t STAGE_BYTES = P::STAGE_BYTES;
@@ -235,6 +242,7 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   uint64_t* drainb = tempty + 2;      // every MMA of the CTA has completed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(drainb + 1);
   volatile uint32_t* abort = tmem_slot + 1;
+  float* ostage = reinterpret_cast<float*>(sm + USTAGES * STAGE_BYTES + (size_t)ng * UN * 4 + 256);  // [EW][32][OST]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
@@ -292,34 +300,57 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
         tc_fence_after();
         const uint32_t tm = tmem + ((uint32_t)(q * 32) << 16) + b * UN + cq * 64;
         const float* ngp = nsm + g * UN + cq * 64;
+        // Two TMEM loads per wait where the registers allow (the 14-warp
+        // UN = 192 CTA is held to 128 registers a thread).
+        constexpr int LPW = UN >= 192 ? 1 : 2;
 #pragma unroll
-        for (int cb = 0; cb < 4; ++cb) {
-          uint32_t r[16];
-          tmem_ld16(tm + cb * 16, r);
+        for (int cb = 0; cb < 4; cb += LPW) {
+          uint32_t r[LPW][16];
+#pragma unroll
+          for (int h = 0; h < LPW; ++h) tmem_ld16(tm + (cb + h) * 16, r[h]);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 16; ++i) acc[cb * 16 + i] += ngp[cb * 16 + i] * __uint_as_float(r[i]);
+          for (int h = 0; h < LPW; ++h)
+#pragma unroll
+            for (int i = 0; i < 16; ++i) acc[(cb + h) * 16 + i] += ngp[(cb + h) * 16 + i] * __uint_as_float(r[h][i]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
       const int m = m0 + q * 32 + lane;
-      if (ok && m < M) {
+      const int lim = nrows - (n0 + cq * 64);
+      // Warp-uniform: the warp's 32 rows x 64 columns lie inside y and every
+      // row start is 16-byte aligned. The rows then leave through shared
+      // memory, 16 columns at a time, so that one store instruction writes 8
+      // rows x 64 contiguous bytes instead of 32 rows x 16 bytes.
+      const bool vec = out_stage && ok && m0 + q * 32 + 32 <= M && lim >= 64 && (ldy & 3) == 0 &&
+                       (reinterpret_cast<uintptr_t>(y + n0 + cq * 64) & 15) == 0;
+      if (vec) {
+        const float ai = ainv[m];
+        float* ob = ostage + (size_t)warp * 32 * OST;
+#pragma unroll
+        for (int cb = 0; cb < 4; ++cb) {
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(ob + lane * OST + i) =
+                make_float4(acc[cb * 16 + i] * ai, acc[cb * 16 + i + 1] * ai, acc[cb * 16 + i + 2] * ai,
+                            acc[cb * 16 + i + 3] * ai);
+          __syncwarp();
+#pragma unroll
+          for (int it = 0; it < 4; ++it) {
+            const int rr = it * 8 + (lane >> 2), c4 = (lane & 3) * 4;
+            *reinterpret_cast<float4*>(y + (size_t)(m0 + q * 32 + rr) * ldy + n0 + cq * 64 + cb * 16 + c4) =
+                *reinterpret_cast<const float4*>(ob + rr * OST + c4);
+          }
+          __syncwarp();
+        }
+      } else if (ok && m < M) {
         const float ai = ainv[m];
         float* yr = y + (size_t)m * ldy + n0 + cq * 64;
-        const int lim = nrows - (n0 + cq * 64);
-        const bool vec = lim >= 64 && ((reinterpret_cast<uintptr_t>(yr) & 15) == 0);
-        if (vec) {
 #pragma unroll
-          for (int i = 0; i < 64; i += 4)
-            *reinterpret_cast<float4*>(yr + i) =
-                make_float4(acc[i] * ai, acc[i + 1] * ai, acc[i + 2] * ai, acc[i + 3] * ai);
-        } else {
-#pragma unroll
-          for (int i = 0; i < 64; ++i)
-            if (i < lim) yr[i] = acc[i] * ai;
-        }
+        for (int i = 0; i < 64; ++i)
+          if (i < lim) yr[i] = acc[i] * ai;
       }
     }
   } else if (warp == EW) {
@@ -517,13 +548,14 @@ cudaError_t launch_umma(const CqMat& W, const GemmScratch& gs, float linv, int M
       !make_map(&mbl, gs.wlo, nrows, K, UN))
     return cudaErrorNotSupported;
   auto kern = cq_umma_kernel<EXACT, UN>;
-  const size_t smem = umma_smem<EXACT, UN>(K / 128);
+  const bool out_stage = umma_smem<EXACT, UN>(K / 128, true) <= 227 * 1024;
+  const size_t smem = umma_smem<EXACT, UN>(K / 128, out_stage);
   cudaError_t e = allow_smem((const void*)kern, smem);
   if (e != cudaSuccess) return e;
   const int ntn = (nrows + UN - 1) / UN, ntiles = ntn * ((M + UM - 1) / UM);
   const int grid = std::min(ntiles, 148);  // persistent: one CTA per SM
   kern<<<grid, Pipe<EXACT, UN>::THREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, linv, M, y, ldy, row0, nrows,
-                                                      ntn, ntiles, werr);
+                                                      ntn, ntiles, werr, out_stage ? 1 : 0);
   return cudaGetLastError();
 }
 
