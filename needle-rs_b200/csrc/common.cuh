@@ -40,6 +40,12 @@ struct CqMat {
   int group;      // 128 on every shipped tensor
   int bits;       // 2 or 4 (byte-aligned widths)
   float levels[16];
+  // Every row's levels expanded once to f16 for the tensor-core projection
+  // ([rows][in_pad], times the power of two umma_level_scale gives), or null:
+  // the projection then expands the rows it needs on every call. lvl_lo holds
+  // the remainders and is null when the scaled levels are exact in f16.
+  const __half* lvl_hi;
+  const __half* lvl_lo;
 };
 
 // Per-layer KV ring of one session. Device layout is head-major so one KV

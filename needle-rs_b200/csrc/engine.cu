@@ -718,6 +718,21 @@ Engine* Engine::load(const uint8_t* raw, size_t len, std::string* err, size_t de
     if (err->empty()) *err = L.err;
     return nullptr;
   }
+  // The projections that run on the tensor cores (batches past 8 rows) read
+  // f16 level tiles: expanded once here instead of on every call.
+  {
+    cudaError_t ec = umma_cache_levels(&E->emb, &E->d_owned, 0);
+    for (size_t l = 0; ec == cudaSuccess && l < c.layers; ++l) {
+      ec = umma_cache_levels(&E->qkvg[l], &E->d_owned, 0);
+      if (ec == cudaSuccess) ec = umma_cache_levels(&E->outp[l], &E->d_owned, 0);
+    }
+    for (size_t s = 0; ec == cudaSuccess && s < c.sites.size(); ++s) ec = umma_cache_levels(&E->eng_kv[s], &E->d_owned, 0);
+    if (ec == cudaSuccess) ec = cudaStreamSynchronize(0);
+    if (ec != cudaSuccess) {
+      *err = cuda_msg("expanding the projection levels", ec);
+      return nullptr;
+    }
+  }
   if (!c.sites.empty()) {
     e = cudaMalloc(&E->d_tables, c.sites.size() * sizeof(CqMat));
     if (e == cudaSuccess)

@@ -3,6 +3,8 @@
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
+#include <vector>
+
 #include "common.cuh"
 
 namespace nb {
@@ -90,6 +92,11 @@ struct GemmScratch {
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                        int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr);
 bool umma_supported(const CqMat& W);
+// Expands every row's levels to the f16 tiles the tensor-core projection reads
+// (W->lvl_hi / lvl_lo), once, for a matrix the engine keeps; the buffers are
+// appended to `owned` for the caller to free. A matrix the tensor cores cannot
+// take is left as it is.
+cudaError_t umma_cache_levels(CqMat* W, std::vector<void*>* owned, cudaStream_t st);
 // Kernel launches cq_project makes for these arguments (3 on the tensor-core
 // path: the activation split, the level expansion and the GEMM).
 int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path = 0);

@@ -46,6 +46,7 @@
 #include <algorithm>
 #include <cmath>
 #include <mutex>
+#include <vector>
 
 #include "common.cuh"
 #include "kernels.hpp"
@@ -539,13 +540,14 @@ bool make_map(CUtensorMap* map, const __half* base, int M, int K, int box_rows) 
             CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// whi / wlo: the level tiles of rows [row0, row0 + nrows) ([nrows][in_pad] f16).
 template <bool EXACT, int UN>
-cudaError_t launch_umma(const CqMat& W, const GemmScratch& gs, float linv, int M, float* y, int ldy, int row0,
-                        int nrows, int* werr, cudaStream_t st) {
+cudaError_t launch_umma(const CqMat& W, const GemmScratch& gs, const __half* whi, const __half* wlo, float linv,
+                        int M, float* y, int ldy, int row0, int nrows, int* werr, cudaStream_t st) {
   const int K = W.in_pad;
   CUtensorMap mah, mal, mbh, mbl;
-  if (!make_map(&mah, gs.hi, M, K, UM) || !make_map(&mal, gs.lo, M, K, UM) || !make_map(&mbh, gs.whi, nrows, K, UN) ||
-      !make_map(&mbl, gs.wlo, nrows, K, UN))
+  if (!make_map(&mah, gs.hi, M, K, UM) || !make_map(&mal, gs.lo, M, K, UM) || !make_map(&mbh, whi, nrows, K, UN) ||
+      !make_map(&mbl, wlo, nrows, K, UN))
     return cudaErrorNotSupported;
   auto kern = cq_umma_kernel<EXACT, UN>;
   const bool out_stage = umma_smem<EXACT, UN>(K / 128, true) <= 227 * 1024;
@@ -565,6 +567,63 @@ bool umma_supported(const CqMat& W) {
   return W.group == 128 && (W.bits == 2 || W.bits == 4) && W.in_pad % 128 == 0 && W.in_pad <= UGMAX * 128;
 }
 
+// Level scale of the f16 level tiles: a power of two 2^le putting max|level|
+// in [2^13, 2^14); exact when every scaled level survives the round trip
+// through f16 (then the tiles need no remainders).
+static void umma_level_scale(const CqMat& W, int* le_out, bool* exact_out) {
+  float lmax = 0.f;
+  for (int i = 0; i < (1 << W.bits); ++i) lmax = std::max(lmax, std::fabs(W.levels[i]));
+  int le = 0;
+  if (lmax > 0.f && std::isfinite(lmax)) {
+    int e;
+    std::frexp(lmax, &e);
+    le = 14 - e;
+  }
+  bool exact = true;
+  for (int i = 0; i < (1 << W.bits); ++i) {
+    const float v = std::ldexp(W.levels[i], le);
+    if (__half2float(__float2half_rn(v)) != v) exact = false;
+  }
+  *le_out = le;
+  *exact_out = exact;
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256) expand_all_kernel(CqMat W, int le, __half* __restrict__ whi,
+                                                         __half* __restrict__ wlo) {
+  expand_levels<BITS>(W, 0, W.rows, le, whi, wlo, blockIdx.x, gridDim.x);
+}
+
+cudaError_t umma_cache_levels(CqMat* W, std::vector<void*>* owned, cudaStream_t st) {
+  if (!umma_supported(*W) || W->lvl_hi) return cudaSuccess;
+  int le;
+  bool exact;
+  umma_level_scale(*W, &le, &exact);
+  const size_t n = (size_t)W->rows * W->in_pad;
+  __half *hi = nullptr, *lo = nullptr;
+  cudaError_t e = cudaMalloc(&hi, n * sizeof(__half));
+  if (e == cudaSuccess && !exact) e = cudaMalloc(&lo, n * sizeof(__half));
+  if (e == cudaSuccess) {
+    const long total = (long)W->rows * (W->in_pad / 8);
+    const int blocks = (int)std::min<long>((total + 255) / 256, 148L * 8);
+    if (W->bits == 2)
+      expand_all_kernel<2><<<blocks, 256, 0, st>>>(*W, le, hi, lo);
+    else
+      expand_all_kernel<4><<<blocks, 256, 0, st>>>(*W, le, hi, lo);
+    e = cudaGetLastError();
+  }
+  if (e != cudaSuccess) {
+    if (hi) cudaFree(hi);
+    if (lo) cudaFree(lo);
+    return e;
+  }
+  owned->push_back(hi);
+  if (lo) owned->push_back(lo);
+  W->lvl_hi = hi;
+  W->lvl_lo = lo;
+  return cudaSuccess;
+}
+
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
                             int nrows, cudaStream_t st, const GemmScratch& gs) {
   const int K = W.in_pad;
@@ -574,33 +633,25 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
   const uintptr_t al = reinterpret_cast<uintptr_t>(gs.hi) | reinterpret_cast<uintptr_t>(gs.lo) |
                        reinterpret_cast<uintptr_t>(gs.whi) | reinterpret_cast<uintptr_t>(gs.wlo);
   if (al & 15) return cudaErrorInvalidValue;
-  // Level scale: a power of two putting max|level| in [2^13, 2^14).
-  float lmax = 0.f;
-  for (int i = 0; i < (1 << W.bits); ++i) lmax = std::max(lmax, std::fabs(W.levels[i]));
-  int le = 0;
-  if (lmax > 0.f && std::isfinite(lmax)) {
-    int e;
-    std::frexp(lmax, &e);
-    le = 14 - e;
-  }
-  // Exact levels: every scaled level survives the round trip through f16.
-  bool exact = true;
-  for (int i = 0; i < (1 << W.bits); ++i) {
-    const float v = std::ldexp(W.levels[i], le);
-    if (__half2float(__float2half_rn(v)) != v) exact = false;
-  }
+  int le;
+  bool exact;
+  umma_level_scale(W, &le, &exact);
+  // Level tiles expanded at load (the engine's matrices) or now, into scratch.
+  const bool cached = W.lvl_hi && (exact || W.lvl_lo);
+  const __half* whi = cached ? W.lvl_hi + (size_t)row0 * K : gs.whi;
+  const __half* wlo = cached ? (W.lvl_lo ? W.lvl_lo + (size_t)row0 * K : whi) : gs.wlo;
   cudaError_t e;
   {
     const int split_blocks = (M + 7) / 8;
     const long total = (long)nrows * (K / 8);
-    const int eblocks = (int)std::min<long>((total + 255) / 256, 148L * 8);
-    __half* wlo = exact ? nullptr : gs.wlo;
+    const int eblocks = cached ? 0 : (int)std::min<long>((total + 255) / 256, 148L * 8);
+    __half* xwlo = exact ? nullptr : gs.wlo;  // remainders, when the levels need them
     if (W.bits == 2)
       umma_prep_kernel<2><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv, split_blocks,
-                                                                  W, row0, nrows, le, gs.whi, wlo);
+                                                                  W, row0, nrows, le, gs.whi, xwlo);
     else
       umma_prep_kernel<4><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv, split_blocks,
-                                                                  W, row0, nrows, le, gs.whi, wlo);
+                                                                  W, row0, nrows, le, gs.whi, xwlo);
     e = cudaGetLastError();
     if (e != cudaSuccess) return e;
   }
@@ -619,12 +670,12 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
   auto span = [&](long un) { return (((nrows + un - 1) / un) * mt + 147) / 148 * (512 + 2 * un); };
   const int un = span(192) <= span(128) ? 192 : span(128) <= span(64) ? 128 : 64;
   if (exact)
-    return un == 192   ? launch_umma<true, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
-           : un == 128 ? launch_umma<true, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
-                       : launch_umma<true, 64>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
-  return un == 192   ? launch_umma<false, 192>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
-         : un == 128 ? launch_umma<false, 128>(W, gs, linv, M, y, ldy, row0, nrows, werr, st)
-                     : launch_umma<false, 64>(W, gs, linv, M, y, ldy, row0, nrows, werr, st);
+    return un == 192   ? launch_umma<true, 192>(W, gs, whi, wlo, linv, M, y, ldy, row0, nrows, werr, st)
+           : un == 128 ? launch_umma<true, 128>(W, gs, whi, wlo, linv, M, y, ldy, row0, nrows, werr, st)
+                       : launch_umma<true, 64>(W, gs, whi, wlo, linv, M, y, ldy, row0, nrows, werr, st);
+  return un == 192   ? launch_umma<false, 192>(W, gs, whi, wlo, linv, M, y, ldy, row0, nrows, werr, st)
+         : un == 128 ? launch_umma<false, 128>(W, gs, whi, wlo, linv, M, y, ldy, row0, nrows, werr, st)
+                     : launch_umma<false, 64>(W, gs, whi, wlo, linv, M, y, ldy, row0, nrows, werr, st);
 }
 
 cudaError_t umma_error_ptr(int** p) { return cudaGetSymbolAddress((void**)p, g_umma_error); }
