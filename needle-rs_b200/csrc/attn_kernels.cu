@@ -327,7 +327,7 @@ __device__ __forceinline__ AttnSrc layer_src(const Geo& G, int li, const RowBatc
 constexpr int FINISH_SCRATCH = AT_MAXREP * 64 + 8 + AT_MAXREP * 64 + 64 * 2 * AT_MAXREP;
 template <int VH>
 __device__ void finish_kvhead(const Geo& G, int r, int kh, int rep, int nsplit, const float* ps,
-                              const float* __restrict__ proj, float* __restrict__ oh, float* F) {
+                              const float* __restrict__ proj, float* __restrict__ oh, float* F, const SplitOut& so) {
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
   const int pw = rep * (VH + 2);
   float* Fw = F;              // [rep][64] split weights exp(m_z - M)
@@ -365,7 +365,13 @@ __device__ void finish_kvhead(const Geo& G, int r, int kh, int rep, int nsplit, 
     const float4 v = reinterpret_cast<const float4*>(Fo + gg * 128)[lane];
     float x[4] = {v.x, v.y, v.z, v.w};
     fwht128_warp(x);
-    reinterpret_cast<float4*>(ohr + gg * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    if (so.hi) {  // out_proj's tensor-core operands
+      const int g = kh * rep * VH / 128 + gg;
+      split_group_store(x, so.hi + (size_t)r * opad + g * 128, so.lo + (size_t)r * opad + g * 128,
+                        so.inv + (size_t)r * (opad / 128) + g);
+    } else {
+      reinterpret_cast<float4*>(ohr + gg * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    }
   }
 }
 
@@ -380,7 +386,8 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
                                                                 const float* pks, const float* pvs,
                                                                 float* __restrict__ part,
                                                                 const float* __restrict__ proj,
-                                                                float* __restrict__ oh, int* __restrict__ cnt) {
+                                                                float* __restrict__ oh, int* __restrict__ cnt,
+                                                                SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) unsigned char smraw[];
@@ -409,7 +416,7 @@ __global__ void __launch_bounds__(AT_THREADS) layer_attn_kernel(Geo G, int li, R
     if (threadIdx.x == 0) cnt[(size_t)r * G.kvh + kh] = 0;  // ready for the next launch
   }
   finish_kvhead<VH>(G, r, kh, rep, nsplit, part + ((size_t)r * G.kvh + kh) * nsplit * pw, proj, oh,
-                    reinterpret_cast<float*>(smraw));
+                    reinterpret_cast<float*>(smraw), so);
 }
 
 // ----------------------------------------------------------------------------
@@ -682,7 +689,7 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
                                                             const void* pv, const float* pks, const float* pvs,
                                                             float* __restrict__ part, const float* __restrict__ proj,
                                                             float* __restrict__ oh, int* __restrict__ cnt,
-                                                            int* __restrict__ werr) {
+                                                            int* __restrict__ werr, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
   using T = MmaTile<QK, VH>;
@@ -1040,7 +1047,13 @@ __global__ void __launch_bounds__(128, 5) layer_attn_i8_kernel(Geo G, int li, Ro
     const float4 v = reinterpret_cast<const float4*>(Fo + gg * 128)[lane];
     float x[4] = {v.x, v.y, v.z, v.w};
     fwht128_warp(x);
-    reinterpret_cast<float4*>(ohr + gg * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    if (so.hi) {  // out_proj's tensor-core operands
+      const int g = kh * rep * VH / 128 + gg;
+      split_group_store(x, so.hi + (size_t)r * opad + g * 128, so.lo + (size_t)r * opad + g * 128,
+                        so.inv + (size_t)r * (opad / 128) + g);
+    } else {
+      reinterpret_cast<float4*>(ohr + gg * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    }
   }
 }
 
@@ -1048,7 +1061,7 @@ template <int QK, int VH>
 static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
                                         const int8_t* q8, const float* q8s, const void* pk, const void* pv,
                                         const float* pks, const float* pvs, float* part, const float* proj,
-                                        float* oh, int* cnt, int* werr, cudaStream_t st) {
+                                        float* oh, int* cnt, int* werr, SplitOut so, cudaStream_t st) {
   using WS = MmaWarpSmem<QK, VH>;
   const int rep = G.heads / G.kvh;
   const size_t fin = (size_t)(64 + 4 * 8 * VH + rep * (VH + 2) + rep * 64 + 8 + rep * VH) * sizeof(float);
@@ -1058,7 +1071,7 @@ static cudaError_t launch_layer_attn_i8(const Geo& G, int li, const RowBatch& rb
   if (e != cudaSuccess) return e;
   dim3 grid(rb.M, G.kvh, nsplit);
   return launch_pdl(k, grid, dim3(128), smem, st, G, li, rb, window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj,
-                    oh, cnt, werr);
+                    oh, cnt, werr, so);
 }
 
 bool attn_fuses_finish(const Geo& G, int int8) {
@@ -1087,20 +1100,21 @@ template <bool INT8, int QK, int VH>
 static cudaError_t launch_layer_attn_t(const Geo& G, int li, const RowBatch& rb, int window, int nsplit,
                                        const float* qpost, const void* pk, const void* pv, const float* pks,
                                        const float* pvs, float* part, const float* proj, float* oh, int* cnt,
-                                       cudaStream_t st) {
+                                       SplitOut so, cudaStream_t st) {
   const size_t smem = sizeof(AttnSmem<INT8, QK, VH>);
   auto k = layer_attn_kernel<INT8, QK, VH>;
   cudaError_t e = allow_smem((const void*)k, smem);
   if (e != cudaSuccess) return e;
   dim3 grid(rb.M, G.kvh, nsplit);
   return launch_pdl(k, grid, dim3(AT_THREADS), smem, st, G, li, rb, window, nsplit, qpost, pk, pv, pks, pvs, part,
-                    proj, oh, cnt);
+                    proj, oh, cnt, so);
 }
 
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
                              const void* pv, const float* pks, const float* pvs, float* part,
-                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt, int* werr) {
+                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt, int* werr,
+                             SplitOut so) {
   if (rb.M <= 0) return cudaSuccess;
   const int rep = G.heads / G.kvh;
   if (rep > AT_MAXREP || nsplit < 1) return cudaErrorInvalidValue;
@@ -1109,10 +1123,10 @@ cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const Lay
     // With proj, oh and cnt the kernel also finishes (attn_fuses_finish);
     // without them it leaves the partials to attn_finish.
     const bool fuse = proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64;
-    if (!fuse) proj = nullptr, oh = nullptr, cnt = nullptr;
+    if (!fuse) proj = nullptr, oh = nullptr, cnt = nullptr, so = SplitOut{};
 #define NB_ATI(Q, V)                                                                                         \
   return launch_layer_attn_i8<Q, V>(G, li, rb, lp.window, nsplit, q8, q8s, pk, pv, pks, pvs, part, proj, oh, \
-                                    cnt, werr, st)
+                                    cnt, werr, so, st)
     if (G.vh == 64) {
       switch (G.qk) {
         case 16: NB_ATI(16, 64);
@@ -1132,9 +1146,11 @@ cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const Lay
     return cudaErrorInvalidValue;
   }
   // With proj, oh and cnt the kernel also finishes (attn_fuses_finish).
-  if (!(proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64)) proj = nullptr, oh = nullptr, cnt = nullptr;
-#define NB_ATT(I8, Q, V) \
-  return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, proj, oh, cnt, st)
+  if (!(proj && oh && cnt && attn_fuses_finish(G, int8) && nsplit <= 64))
+    proj = nullptr, oh = nullptr, cnt = nullptr, so = SplitOut{};
+#define NB_ATT(I8, Q, V)                                                                                          \
+  return launch_layer_attn_t<I8, Q, V>(G, li, rb, lp.window, nsplit, qpost, pk, pv, pks, pvs, part, proj, oh, cnt, \
+                                       so, st)
   const int key = G.qk * 2;  // f32 KV (int8 KV returned above)
   if (G.vh == 64) {
     switch (key) {
@@ -1293,7 +1309,7 @@ cudaError_t launch_kv_quant(const float* x, int rows, int dim, int8_t* q, float*
 // Combine of the forward's attention partials, fused with the output gate
 // (model.rs:305-308) and the rotation of out_proj's prepare_input.
 __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ part,
-                                   const float* __restrict__ proj, float* __restrict__ oh) {
+                                   const float* __restrict__ proj, float* __restrict__ oh, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) float sm[];
@@ -1331,17 +1347,28 @@ __global__ void attn_finish_kernel(Geo G, int nsplit, const float* __restrict__ 
   }
   for (int i = od + threadIdx.x; i < opad; i += blockDim.x) sm[i] = 0.f;
   __syncthreads();
+  if (so.hi) {  // rotation and out_proj's tensor-core operands, one warp per group
+    for (int g = wid; g < opad / 128; g += nw) {
+      const float4 v = reinterpret_cast<const float4*>(sm + g * 128)[lane];
+      float x[4] = {v.x, v.y, v.z, v.w};
+      fwht128_warp(x);
+      split_group_store(x, so.hi + (size_t)r * opad + g * 128, so.lo + (size_t)r * opad + g * 128,
+                        so.inv + (size_t)r * (opad / 128) + g);
+    }
+    return;
+  }
   fwht_groups_warp(sm, opad / 128);
   __syncthreads();
   for (int i = threadIdx.x; i < opad; i += blockDim.x) oh[(size_t)r * opad + i] = sm[i];
 }
 
 cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
-                               const float* proj, float* oh, cudaStream_t st) {
+                               const float* proj, float* oh, cudaStream_t st, SplitOut so) {
   if (rb.M <= 0) return cudaSuccess;
   const int opad = (G.o_dim + 127) / 128 * 128;
   if (nsplit > 64) return cudaErrorInvalidValue;  // the kernel's split-weight buffer
-  return launch_pdl(attn_finish_kernel, dim3(rb.M), dim3(256), opad * sizeof(float), st, G, nsplit, part, proj, oh);
+  return launch_pdl(attn_finish_kernel, dim3(rb.M), dim3(256), opad * sizeof(float), st, G, nsplit, part, proj, oh,
+                    so);
 }
 
 

@@ -1031,7 +1031,9 @@ int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, 
   gs.elems = (size_t)M * W.in_pad;
   gs.welems = (size_t)nrows * W.in_pad;
   void* mem = nullptr;
-  cudaError_t e = scratch_alloc(&mem, (gs.elems + gs.welems) * 2 * sizeof(__half) + (size_t)M * sizeof(float), st);
+  // hi / lo [M][in_pad], the level tiles, and one inverse scale per 128-wide group.
+  cudaError_t e = scratch_alloc(
+      &mem, (gs.elems + gs.welems) * 2 * sizeof(__half) + (size_t)M * (W.in_pad / 128) * sizeof(float), st);
   if (e != cudaSuccess) return nd_status(e);
   gs.hi = (__half*)mem;
   gs.lo = gs.hi + gs.elems;

@@ -168,6 +168,54 @@ __device__ __forceinline__ void fwht_groups_warp(float* buf, int n128) {
   }
 }
 
+// x as an f16 high part (low half) and the f16 of the remainder (high half).
+__device__ __forceinline__ uint32_t split_h16(float x) {
+  const __half h = __float2half_rn(x);
+  const __half l = __float2half_rn(x - __half2float(h));
+  return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
+}
+
+// Destination of a projection input written straight in the tensor-core
+// projection's operand form: hi / lo [rows][K] f16 and inv [rows][K / 128]
+// (the inverse scale of each 128-wide group). Null hi: the producer writes
+// its f32 rows instead.
+struct SplitOut {
+  __half* hi;
+  __half* lo;
+  float* inv;
+};
+
+// One 128-wide group of an activation row held by a warp (element lane*4 + i
+// in x[i]) in that form: scaled by the power of two 2^e that brings the
+// group's max|x| into [2^13, 2^14) (e = 0 for an all-zero, denormal-only or
+// non-finite max; e held at 126 for groups below 2^-112), each value split
+// into an f16 high part and
+// the f16 of its remainder (22 bits together), and the inverse scale. hi / lo
+// point at the group's first element, inv at its scale.
+__device__ __forceinline__ void split_group_store(const float (&x)[4], __half* hi, __half* lo, float* inv) {
+  const int lane = threadIdx.x & 31;
+  // The warp's max|x| in one instruction: non-negative floats order as their
+  // bit patterns. (fmaxf skips a NaN; the NaN itself still reaches the
+  // operands and the product.)
+  const uint32_t mb = __float_as_uint(fmaxf(fmaxf(fabsf(x[0]), fabsf(x[1])), fmaxf(fabsf(x[2]), fabsf(x[3]))));
+  uint32_t wb;
+  asm("redux.sync.max.u32 %0, %1, 0xffffffff;" : "=r"(wb) : "r"(mb));
+  // e from the exponent field f of a normal max (max in [2^(f-127),
+  // 2^(f-126))), and 2^e, 2^-e built from their bits.
+  const int f = (int)(wb >> 23);
+  const int e = (f == 0 || f >= 255) ? 0 : min(140 - f, 126);
+  const float sc = __uint_as_float((uint32_t)(127 + e) << 23);
+  const __half2 h01 = __floats2half2_rn(x[0] * sc, x[1] * sc), h23 = __floats2half2_rn(x[2] * sc, x[3] * sc);
+  const float2 f01 = __half22float2(h01), f23 = __half22float2(h23);
+  const __half2 l01 = __floats2half2_rn(x[0] * sc - f01.x, x[1] * sc - f01.y);
+  const __half2 l23 = __floats2half2_rn(x[2] * sc - f23.x, x[3] * sc - f23.y);
+  *reinterpret_cast<uint2*>(hi + lane * 4) =
+      make_uint2(*reinterpret_cast<const uint32_t*>(&h01), *reinterpret_cast<const uint32_t*>(&h23));
+  *reinterpret_cast<uint2*>(lo + lane * 4) =
+      make_uint2(*reinterpret_cast<const uint32_t*>(&l01), *reinterpret_cast<const uint32_t*>(&l23));
+  if (lane == 0) *inv = __uint_as_float((uint32_t)(127 - e) << 23);
+}
+
 // cp.async copies global -> shared (src-size 0 when !valid: zero-fill, nothing read).
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);

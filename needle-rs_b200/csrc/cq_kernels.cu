@@ -957,15 +957,19 @@ static bool umma_scratch_ok(const CqMat& W, int M, int nrows, const GemmScratch*
          gs->rows >= (size_t)M && gs->welems >= (size_t)nrows * W.in_pad;
 }
 
-int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path) {
+bool cq_umma_takes(const CqMat& W, int M, const GemmScratch* gs) {
+  return M > 8 && umma_scratch_ok(W, M, W.rows, gs) && umma_supported(W);
+}
+
+int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path, bool presplit) {
   if (M <= 0) return 0;
-  if (force_path == 3 || (force_path == 0 && M > 8 && umma_scratch_ok(W, M, W.rows, gs) && umma_supported(W)))
-    return 2;  // operand preparation + tensor-core GEMM
+  if (force_path == 3 || (force_path == 0 && cq_umma_takes(W, M, gs)))
+    return presplit && W.lvl_hi ? 1 : 2;  // (operand preparation +) tensor-core GEMM
   return 1;
 }
 
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                       int nrows, cudaStream_t st, int force_path, const GemmScratch* gs) {
+                       int nrows, cudaStream_t st, int force_path, const GemmScratch* gs, bool presplit) {
   if (M <= 0 || nrows <= 0) return cudaSuccess;
   if (!cq_args_ok(W, xh, ldx) || row0 < 0 || row0 + nrows > W.rows) return cudaErrorInvalidValue;
   if ((force_path == 1 || force_path >= 4) && M > 8) return cudaErrorInvalidValue;
@@ -976,10 +980,11 @@ cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y
   const bool scratch_ok = umma_scratch_ok(W, M, nrows, gs);
   if (force_path == 3) {
     if (!scratch_ok) return cudaErrorInvalidValue;
-    return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs);
+    return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs, presplit);
   }
   if (force_path == 0 && M > 8 && scratch_ok && umma_supported(W))
-    return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs);
+    return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs, presplit);
+  if (presplit) return cudaErrorInvalidValue;  // the input exists only in the split form
   if (force_path == 2)
     return W.bits == 2 ? launch_gemm_simt<2>(W, xh, ldx, M, y, ldy, row0, nrows, st)
                        : launch_gemm_simt<4>(W, xh, ldx, M, y, ldy, row0, nrows, st);

@@ -85,7 +85,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
       {(void**)&w.proj, cap * G.proj_dim * 4},     {(void**)&w.qpost, cap * G.q_dim * 4},
       {(void**)&w.q8s, cap * G.heads * 4},         {(void**)&w.q8, cap * G.q_dim},
       {(void**)&w.ahi, cap * kmax * 2},            {(void**)&w.alo, cap * kmax * 2},
-      {(void**)&w.ainv, cap * 4},                  {(void**)&w.cnt, cap * G.kvh * 4},
+      {(void**)&w.ainv, cap * 32 * 4},                  {(void**)&w.cnt, cap * G.kvh * 4},
       {(void**)&w.whi, wmax * kmax * 2},           {(void**)&w.wlo, wmax * kmax * 2},
       {(void**)&w.oh, cap * opad * 4},
       {(void**)&w.projo, cap * d * 4},             {(void**)&w.gates, cap * 24 * 4},
@@ -1189,7 +1189,8 @@ cudaError_t Prof::mark(int kind, cudaStream_t st, int nlaunch) {
 #define NB_MARK(kind, n) \
   if (prof) NB_TRY(prof->mark(kind, st, n))
 
-cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof) {
+cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, bool int8, int nsplit, Prof* prof,
+                            bool split_head) {
   const int M = rb.M, d = G.d, S = G.n_sites;
   const int dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   if (S > 0) {
@@ -1203,29 +1204,36 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
   NB_TRY(launch_embed(G, emb, rb, w.lanes, st));
   if (w.cells) NB_TRY(launch_lane_mean(w.lanes, M, G.lanes, d, true, w.cells, st));
   NB_MARK(PK_EMBED, 1);
+  // Inputs of tensor-core projections are written by their producers in the
+  // split form, straight into the projection scratch.
+  const SplitOut to_gs{w.gs.hi, w.gs.lo, w.gs.inv};
   for (int l = 0; l < G.layers; ++l) {
+    const SplitOut sq = cq_umma_takes(qkvg[l], M, &w.gs) ? to_gs : SplitOut{};
     NB_TRY(launch_layer_pre(G, l, rb, w.lanes, phi_pre, phi_post, phi_res, mp[l], lp[l].norm_in,
-                            site_of[l], w.ekv, w.evc, w.u, w.bx, w.xh, w.gates, st, w.pre_part, w.pre_cnt));
+                            site_of[l], w.ekv, w.evc, w.u, w.bx, w.xh, w.gates, st, w.pre_part, w.pre_cnt, sq));
     NB_MARK(PK_LAYER_PRE, 1);
-    NB_TRY(cq_project(qkvg[l], w.xh, dpad, M, w.proj, G.proj_dim, 0, G.proj_dim, st, 0, &w.gs));
-    NB_MARK(PK_QKVG, cq_launches(qkvg[l], M, &w.gs));
+    NB_TRY(cq_project(qkvg[l], w.xh, dpad, M, w.proj, G.proj_dim, 0, G.proj_dim, st, 0, &w.gs, sq.hi != nullptr));
+    NB_MARK(PK_QKVG, cq_launches(qkvg[l], M, &w.gs, 0, sq.hi != nullptr));
     NB_TRY(launch_qkv_post(G, l, rb, lp[l], d_rope, w.proj, w.qpost, w.pk, w.pv, w.pks, w.pvs,
                            int8 ? w.q8 : nullptr, int8 ? w.q8s : nullptr, st));
     NB_MARK(PK_QKV_POST, 1);
     const bool fused = attn_fuses_finish(G, int8 ? 1 : 0) && nsplit <= 64;
+    const SplitOut so = cq_umma_takes(outp[l], M, &w.gs) ? to_gs : SplitOut{};
     NB_TRY(launch_attention(G, l, rb, lp[l], nsplit, w.qpost, w.q8, w.q8s, w.pk, w.pv, w.pks, w.pvs,
-                            w.part, st, int8 ? 1 : 0, w.proj, w.oh, w.cnt, d_wait_flag));
+                            w.part, st, int8 ? 1 : 0, w.proj, w.oh, w.cnt, d_wait_flag, so));
     NB_MARK(PK_ATTN, 1);
-    if (!fused) NB_TRY(launch_attn_finish(G, rb, nsplit, w.part, w.proj, w.oh, st));
+    if (!fused) NB_TRY(launch_attn_finish(G, rb, nsplit, w.part, w.proj, w.oh, st, so));
     NB_MARK(PK_ATTN_FINISH, fused ? 0 : 1);
-    NB_TRY(cq_project(outp[l], w.oh, opad, M, w.projo, d, 0, d, st, 0, &w.gs));
-    NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &w.gs));
+    NB_TRY(cq_project(outp[l], w.oh, opad, M, w.projo, d, 0, d, st, 0, &w.gs, so.hi != nullptr));
+    NB_MARK(PK_OUT_PROJ, cq_launches(outp[l], M, &w.gs, 0, so.hi != nullptr));
     NB_TRY(launch_layer_post(G, l, rb, lp[l], d_perm, d_perm + G.hada_n, w.projo, w.u, w.bx,
                              w.gates, w.lanes, st));
     if (w.cells) NB_TRY(launch_lane_mean(w.lanes, M, G.lanes, d, false, w.cells + (size_t)(l + 1) * M * d, st));
     NB_MARK(PK_LAYER_POST, 1);
   }
-  NB_TRY(launch_final(G, rb, w.lanes, final_norm, w.lm_in, st));
+  const SplitOut sh = split_head && cq_umma_takes(emb, M, &w.gs) ? to_gs : SplitOut{};
+  NB_TRY(launch_final(G, rb, w.lanes, final_norm, w.lm_in, st, sh));
+  w.head_presplit = sh.hi != nullptr;
   NB_MARK(PK_FINAL, 1);
   return cudaSuccess;
 }
@@ -1233,8 +1241,11 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
 // Tied head over logit_rows (model.rs:358-374, :942-978) and the greedy pick.
 cudaError_t Engine::head(Workspace& w, const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                          cudaStream_t st, Prof* prof) {
-  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &w.gs));
-  NB_MARK(PK_HEAD, cq_launches(emb, M, &w.gs));
+  // The last forward's final kernel may have written this input split (lm_in
+  // itself then holds nothing).
+  const bool presplit = lm_in == w.lm_in && w.head_presplit;
+  NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &w.gs, presplit));
+  NB_MARK(PK_HEAD, cq_launches(emb, M, &w.gs, 0, presplit));
   if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
   NB_MARK(PK_BOOK, picks ? 1 : 0);
   return cudaSuccess;
@@ -1428,7 +1439,7 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   RowBatch rb{ws.rows, ws.tokens, (int)n, MODE_DECODE};
   const int int8 = ss[0]->int8 ? 1 : 0;
   auto body = [&](cudaStream_t s) -> cudaError_t {
-    NB_TRY(forward(ws, rb, s, int8, ns));
+    NB_TRY(forward(ws, rb, s, int8, ns, nullptr, true));
     NB_TRY(launch_step_end(rb, s));
     return head(ws, ws.lm_in, dpad, (int)n, ws.logits, ws.next, s);
   };
@@ -1562,7 +1573,7 @@ bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, boo
   RowBatch rb{ws.rows, b->d_tok, (int)n, MODE_DECODE};
   auto body = [&](cudaStream_t s) -> cudaError_t {
     NB_TRY(launch_step_begin(rb, b->d_sess, s));
-    NB_TRY(forward(ws, rb, s, b->int8, ns));
+    NB_TRY(forward(ws, rb, s, b->int8, ns, nullptr, true));
     NB_TRY(launch_step_end(rb, s));
     NB_TRY(head(ws, ws.lm_in, dpad, (int)n, lg, b->d_next, s));
     return cudaSuccess;
@@ -1630,7 +1641,7 @@ bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string*
     NB_TRY(p->mark(PK_BOOK, st, 0));
     NB_TRY(launch_step_begin(rb, b->d_sess, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
-    NB_TRY(forward(ws, rb, st, b->int8, ns, p));
+    NB_TRY(forward(ws, rb, st, b->int8, ns, p, true));
     NB_TRY(launch_step_end(rb, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
     NB_TRY(head(ws, ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p));

@@ -67,7 +67,9 @@ struct Workspace {
   void *pk = nullptr, *pv = nullptr;
   int8_t* q8 = nullptr;  // int8 mode: query codes [rows][heads][qk], scales in q8s [rows][heads]
   __half *ahi = nullptr, *alo = nullptr;  // tensor-core projections: split activations
-  float* ainv = nullptr;                  // and their inverse row scales
+  float* ainv = nullptr;                  // and their inverse group scales [rows][32]
+  // The last forward wrote the LM head's input in the split form (not lm_in).
+  bool head_presplit = false;
   __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
   int* cnt = nullptr;  // attention split-arrival counters [rows][kv heads], zero between launches
   float* pre_part = nullptr;  // few-row mHC pre-projection partials [8][32][32]
@@ -201,8 +203,10 @@ class Engine {
   bool ensure_ws(Workspace& w, size_t rows, std::string* err);
   bool ensure_part(Workspace& w, size_t rows, int nsplit, std::string* err);
   bool ensure_slots(Session* s, size_t pos, std::string* err);
+  // split_head: every row goes to the LM head next (decode), so the final
+  // kernel may write the head's tensor-core operands instead of lm_in.
   cudaError_t forward(Workspace& w, const RowBatch& rb, cudaStream_t st, bool int8, int nsplit,
-                      Prof* prof = nullptr);
+                      Prof* prof = nullptr, bool split_head = false);
   cudaError_t head(Workspace& w, const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
                    cudaStream_t st, Prof* prof = nullptr);
 };

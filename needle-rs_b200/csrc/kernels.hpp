@@ -67,8 +67,9 @@ struct RowBatch {
 };
 
 // Scratch of the tensor-core path (16-byte aligned): the activations split
-// into f16 high parts and remainders, `elems` (>= M * in_pad) halves each, and
-// `rows` (>= M) inverse row scales.
+// into f16 high parts and remainders ([M][in_pad]), `elems` (>= M * in_pad)
+// halves each, and the inverse scale of every 128-wide group ([M][in_pad /
+// 128]), room for `rows` (>= M) rows of them.
 struct GemmScratch {
   __half* hi = nullptr;
   __half* lo = nullptr;
@@ -89,19 +90,27 @@ struct GemmScratch {
 // holds enough scratch, else the SIMT GEMM), 1 GEMV, 2 SIMT GEMM, 3 tensor
 // cores; for M <= 8, 4 the SIMT GEMV kernels and 5 the tensor-core GEMV
 // (f16-exact levels only).
+// presplit: the tensor-core path's operands are already in gs->hi / lo / inv
+// (the kernel that produced the rows wrote them, see SplitOut): no split and,
+// with levels cached at load, no preparation launch; only for a call that
+// cq_umma_takes.
 cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                       int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr);
+                       int nrows, cudaStream_t st, int force_path = 0, const GemmScratch* gs = nullptr,
+                       bool presplit = false);
 bool umma_supported(const CqMat& W);
+// True when cq_project with force_path 0 runs these M rows of W on the tensor
+// cores with the scratch gs.
+bool cq_umma_takes(const CqMat& W, int M, const GemmScratch* gs);
 // Expands every row's levels to the f16 tiles the tensor-core projection reads
 // (W->lvl_hi / lvl_lo), once, for a matrix the engine keeps; the buffers are
 // appended to `owned` for the caller to free. A matrix the tensor cores cannot
 // take is left as it is.
 cudaError_t umma_cache_levels(CqMat* W, std::vector<void*>* owned, cudaStream_t st);
-// Kernel launches cq_project makes for these arguments (3 on the tensor-core
-// path: the activation split, the level expansion and the GEMM).
-int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path = 0);
+// Kernel launches cq_project makes for these arguments (on the tensor-core
+// path the GEMM plus, unless presplit with cached levels, the preparation).
+int cq_launches(const CqMat& W, int M, const GemmScratch* gs, int force_path = 0, bool presplit = false);
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                            int nrows, cudaStream_t st, const GemmScratch& gs);
+                            int nrows, cudaStream_t st, const GemmScratch& gs, bool presplit = false);
 // Reads and clears the library-wide device flag raised when a bounded wait of
 // the tensor-core GEMM expired and the caller gave no flag of its own
 // (GemmScratch::werr null) (*flag != 0).
@@ -120,11 +129,14 @@ cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const Row
                                const float* ekv, float* evc, cudaStream_t st);
 // split_part / split_cnt (nullable): scratch of the few-row form, 8 rows x 32
 // groups x 32 floats and 8 zero-initialised counters (reset by the kernel).
+// so.hi non-null: the rotated attention input goes to so (the q|k|v|gate
+// projection's tensor-core operands, [M][dpad]) instead of xh.
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                              const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
                              const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                              const float* evc, float* u, float* bx, float* xh, float* gates,
-                             cudaStream_t st, float* split_part = nullptr, int* split_cnt = nullptr);
+                             cudaStream_t st, float* split_part = nullptr, int* split_cnt = nullptr,
+                             SplitOut so = SplitOut{});
 // In int8 mode q8out / q8s (when non-null) receive the query's int8 codes
 // [M][heads][qk] and per-head scales [M][heads].
 cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
@@ -141,14 +153,16 @@ size_t attn_part_floats(int rows, int heads, int kvh, int vh, int nsplit);
 // attn_fuses_finish(), either kernel also merges the splits, gates and
 // rotates into oh, so attn_finish is not launched.
 // werr: device flag set to 2 when a bounded wait of the int8 kernel's copies
-// expired (required for int8 = 1).
+// expired (required for int8 = 1). so.hi non-null: the rotated output goes to
+// so (out_proj's tensor-core operands, [M][opad]) instead of oh.
 cudaError_t launch_attention(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp, int nsplit,
                              const float* qpost, const int8_t* q8, const float* q8s, const void* pk,
                              const void* pv, const float* pks, const float* pvs, float* part,
-                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt, int* werr);
+                             cudaStream_t st, int int8, const float* proj, float* oh, int* cnt, int* werr,
+                             SplitOut so = SplitOut{});
 bool attn_fuses_finish(const Geo& G, int int8);
 cudaError_t launch_attn_finish(const Geo& G, const RowBatch& rb, int nsplit, const float* part,
-                               const float* proj, float* oh, cudaStream_t st);
+                               const float* proj, float* oh, cudaStream_t st, SplitOut so = SplitOut{});
 cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                               const uint32_t* p1, const uint32_t* p2, const float* projo,
                               const float* u, float* bx, const float* gates, float* lanes,
@@ -167,8 +181,10 @@ cudaError_t launch_lane_mean(const float* lanes, int M, int n, int d, bool copy0
 cudaError_t launch_probe_head(const float* cells, int seq, int d, const ProbeHeadDev& h, float* r, float* out,
                               cudaStream_t st);
 
+// so.hi non-null: the rotated head input goes to so (the LM head's
+// tensor-core operands, [M][dpad]) instead of lm_in.
 cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
-                         const float* final_norm, float* lm_in, cudaStream_t st);
+                         const float* final_norm, float* lm_in, cudaStream_t st, SplitOut so = SplitOut{});
 cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st);
 cudaError_t launch_step_begin(const RowBatch& rb, SessDesc* const* sess, cudaStream_t st);
 cudaError_t launch_step_end(const RowBatch& rb, cudaStream_t st);

@@ -388,7 +388,7 @@ __device__ __forceinline__ void layer_pre_tail(const Geo& G, int li, int r, cons
                                                float* bx, float* hb, const float* norm_in, const float* ek,
                                                const float* ev, float* __restrict__ u_out,
                                                float* __restrict__ bx_out, float* __restrict__ xh_out,
-                                               float* __restrict__ gates) {
+                                               float* __restrict__ gates, SplitOut so) {
   const int n = G.lanes, d = G.d;
   const int dpad = (d + 127) / 128 * 128;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5, nw = blockDim.x >> 5;
@@ -474,7 +474,11 @@ __device__ __forceinline__ void layer_pre_tail(const Geo& G, int li, int r, cons
     float4 v = reinterpret_cast<float4*>(hb + g * 128)[lane];
     float x[4] = {v.x, v.y, v.z, v.w};
     fwht128_warp(x);
-    reinterpret_cast<float4*>(xh_out + (size_t)r * dpad + g * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
+    if (so.hi)  // the q|k|v|gate projection's tensor-core operands
+      split_group_store(x, so.hi + (size_t)r * dpad + g * 128, so.lo + (size_t)r * dpad + g * 128,
+                        so.inv + (size_t)r * (dpad / 128) + g);
+    else
+      reinterpret_cast<float4*>(xh_out + (size_t)r * dpad + g * 128)[lane] = make_float4(x[0], x[1], x[2], x[3]);
   }
 }
 
@@ -489,7 +493,7 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
                                  const float* __restrict__ ekv, const float* __restrict__ evc,
                                  float* __restrict__ u_out, float* __restrict__ bx_out,
                                  float* __restrict__ xh_out, float* __restrict__ gates, int rbmax,
-                                 int gmax) {
+                                 int gmax, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) float sm[];
@@ -592,7 +596,7 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
   __syncthreads();
   const float* ek = site >= 0 ? ekv + (size_t)r * G.n_sites * 2 * d + (size_t)site * 2 * d : nullptr;
   const float* ev = site >= 0 ? evc + ((size_t)r * G.n_sites + site) * d : nullptr;
-  layer_pre_tail(G, li, r, mp, phi, L, gsm, red, bx, hb, norm_in, ek, ev, u_out, bx_out, xh_out, gates);
+  layer_pre_tail(G, li, r, mp, phi, L, gsm, red, bx, hb, norm_in, ek, ev, u_out, bx_out, xh_out, gates, so);
 }
 
 // The same computation for a few rows (batch-1 and small-batch decode), split
@@ -707,7 +711,7 @@ __global__ void __launch_bounds__(256) layer_pre_split_kernel(
   cp_wait<0>();
   __syncthreads();
   layer_pre_tail(G, li, r, mp, phi, Ls, gsm, red, bx, hb, nis, ek ? eks : nullptr, ek ? evs : nullptr, u_out,
-                 bx_out, xh_out, gates);
+                 bx_out, xh_out, gates, SplitOut{});
 }
 
 // The same computation for many rows: PT_M rows per CTA so each mHC weight
@@ -735,7 +739,7 @@ __global__ void __launch_bounds__(256, 2)
 layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lanes, MhcParams mp,
                        const float* __restrict__ norm_in, int site, const float* __restrict__ ekv,
                        const float* __restrict__ evc, float* __restrict__ u_out, float* __restrict__ bx_out,
-                       float* __restrict__ xh_out, float* __restrict__ gates) {
+                       float* __restrict__ xh_out, float* __restrict__ gates, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
   __shared__ __align__(16) float Xr[PT_S][PT_M][128];
@@ -952,7 +956,10 @@ layer_pre_tiled_kernel(Geo G, int li, RowBatch rb, const float* __restrict__ lan
     float h[4] = {(1.0f + ni.x) * bxv[m][0] * inv2, (1.0f + ni.y) * bxv[m][1] * inv2,
                   (1.0f + ni.z) * bxv[m][2] * inv2, (1.0f + ni.w) * bxv[m][3] * inv2};
     fwht128_warp(h);
-    *reinterpret_cast<float4*>(xh_out + r * d + c0) = make_float4(h[0], h[1], h[2], h[3]);
+    if (so.hi)  // the q|k|v|gate projection's tensor-core operands (d is a multiple of 128 here)
+      split_group_store(h, so.hi + r * d + wid * 128, so.lo + r * d + wid * 128, so.inv + r * (d / 128) + wid);
+    else
+      *reinterpret_cast<float4*>(xh_out + r * d + c0) = make_float4(h[0], h[1], h[2], h[3]);
   }
 }
 
@@ -963,21 +970,22 @@ template <int PT_M>
 static cudaError_t launch_pre_tiled(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                                     const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                                     const float* evc, float* u, float* bx, float* xh, float* gates,
-                                    cudaStream_t st) {
+                                    cudaStream_t st, SplitOut so) {
   return launch_pdl(layer_pre_tiled_kernel<PT_M>, dim3((rb.M + PT_M - 1) / PT_M), dim3(256), 0, st, G, li, rb, lanes,
-                    mp, norm_in, site, ekv, evc, u, bx, xh, gates);
+                    mp, norm_in, site, ekv, evc, u, bx, xh, gates, so);
 }
 
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,
                              const CqMat& phi_pre, const CqMat& phi_post, const CqMat& phi_res,
                              const MhcParams& mp, const float* norm_in, int site, const float* ekv,
                              const float* evc, float* u, float* bx, float* xh, float* gates,
-                             cudaStream_t st, float* split_part, int* split_cnt) {
+                             cudaStream_t st, float* split_part, int* split_cnt, SplitOut so) {
   if (rb.M <= 0) return cudaSuccess;
   const int nrow = 2 * G.lanes + G.lanes * G.lanes;
-  // Up to PRE_SPLIT_MAX_ROWS rows: every row over (lanes x d_model) / 128 CTAs.
+  // Up to PRE_SPLIT_MAX_ROWS rows (f32 output for the GEMV): every row over
+  // (lanes x d_model) / 128 CTAs.
   const int ngr = G.lanes * G.d / 128;
-  if (split_part && split_cnt && rb.M <= PRE_SPLIT_MAX_ROWS && G.d % 128 == 0 && ngr <= PRE_SPLIT_MAX_GROUPS &&
+  if (!so.hi && split_part && split_cnt && rb.M <= PRE_SPLIT_MAX_ROWS && G.d % 128 == 0 && ngr <= PRE_SPLIT_MAX_GROUPS &&
       nrow <= 24 && phi_pre.groups == ngr && phi_post.groups == ngr && phi_res.groups == ngr &&
       (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0 && (reinterpret_cast<uintptr_t>(lanes) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(ekv) & 15) == 0 && (reinterpret_cast<uintptr_t>(evc) & 15) == 0) {
@@ -997,17 +1005,17 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
   auto busiest = [&](int pt) { return ((rb.M + pt - 1) / pt + 2 * 148 - 1) / (2 * 148) * pt; };
   if (tiled_ok && rb.M >= 2048)
     return busiest(14) < busiest(16)
-               ? launch_pre_tiled<14>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st)
-               : launch_pre_tiled<16>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
+               ? launch_pre_tiled<14>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so)
+               : launch_pre_tiled<16>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so);
   if (tiled_ok && rb.M >= PRE_TILED_MIN_ROWS)
-    return launch_pre_tiled<4>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st);
+    return launch_pre_tiled<4>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so);
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
   const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48 + nrow * gmax) * sizeof(float) +
                       (size_t)nrow * rbmax + 16;
   cudaError_t e = allow_smem((const void*)layer_pre_kernel, smem);
   if (e != cudaSuccess) return e;
   return launch_pdl(layer_pre_kernel, dim3(rb.M), dim3(256), smem, st, G, li, rb, lanes, phi_pre, phi_post, phi_res,
-                    mp, norm_in, site, ekv, evc, u, bx, xh, gates, rbmax, gmax);
+                    mp, norm_in, site, ekv, evc, u, bx, xh, gates, rbmax, gmax, so);
 }
 
 // ---------------------------------------------------------------- Q/K/V post-processing
@@ -1550,7 +1558,7 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
 // ---------------------------------------------------------------- head
 // model.rs:358-374: lane mean, final ZCRMS norm, rotation for the tied head.
 __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float* __restrict__ fnorm,
-                             float* __restrict__ lm_in) {
+                             float* __restrict__ lm_in, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
   extern __shared__ __align__(16) float sm[];
@@ -1571,17 +1579,28 @@ __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float
   const float inv = 1.0f / sqrtf(ss / (float)d + EPS);
   for (int c = threadIdx.x; c < dpad; c += blockDim.x) x[c] = c < d ? (1.0f + fnorm[c]) * x[c] * inv : 0.f;
   __syncthreads();
+  if (so.hi) {  // rotation and the LM head's tensor-core operands, one warp per group
+    const int lane = threadIdx.x & 31;
+    for (int g = threadIdx.x >> 5; g < dpad / 128; g += blockDim.x >> 5) {
+      const float4 v = reinterpret_cast<const float4*>(x + g * 128)[lane];
+      float h[4] = {v.x, v.y, v.z, v.w};
+      fwht128_warp(h);
+      split_group_store(h, so.hi + (size_t)r * dpad + g * 128, so.lo + (size_t)r * dpad + g * 128,
+                        so.inv + (size_t)r * (dpad / 128) + g);
+    }
+    return;
+  }
   fwht_groups_warp(x, dpad / 128);
   __syncthreads();
   for (int c = threadIdx.x; c < dpad; c += blockDim.x) lm_in[(size_t)r * dpad + c] = x[c];
 }
 
 cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
-                         const float* final_norm, float* lm_in, cudaStream_t st) {
+                         const float* final_norm, float* lm_in, cudaStream_t st, SplitOut so) {
   if (rb.M <= 0) return cudaSuccess;
   const int dpad = (G.d + 127) / 128 * 128;
   return launch_pdl(final_kernel, dim3(rb.M), dim3(256), (32 + dpad) * sizeof(float), st, G, lanes, final_norm,
-                    lm_in);
+                    lm_in, so);
 }
 
 // Greedy pick: the first maximum, as argmax (v3_engine.rs:410-420) keeps the

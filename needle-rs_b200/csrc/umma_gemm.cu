@@ -5,36 +5,38 @@
 // for many activation rows. The tensor cores multiply f16 operands into f32
 // accumulators held in tensor memory (TMEM). To keep f32 accuracy both
 // operands are split into an f16 high part and an f16 remainder,
-// x = x_hi + x_lo and level = l_hi + l_lo, and per 128-element group
-//     main = sum x_hi * l_hi        corr = sum (x_hi * l_lo + x_lo * l_hi)
-// accumulate in two TMEM accumulators (f16 products are exact; the dropped
-// x_lo * l_lo term and the remainders' rounding leave ~2^-22 per product).
-// The tensor cores' f32 accumulation truncates toward zero, so the
-// accumulators only ever span one group: after each group the epilogue warps
-// read them and add norm * (main + corr) into f32 registers with
-// round-to-nearest, the same norm-times-group-dot structure as the reference.
-// Activation rows and the level table are scaled by powers of two that keep
-// every f16 remainder in the normal range; the epilogue undoes them exactly.
+// x = x_hi + x_lo and level = l_hi + l_lo, and per 128-element group the
+// products x_hi*l_hi, x_lo*l_hi (and x_hi*l_lo) accumulate in one TMEM
+// accumulator (f16 products are exact; the dropped x_lo*l_lo term and the
+// remainders' rounding leave ~2^-22 per product). The tensor cores' f32
+// accumulation truncates toward zero, so an accumulator only ever spans one
+// group: after each group the epilogue warps read it and add norm * group dot
+// into f32 registers with round-to-nearest, the reference's own
+// norm-times-group-dot structure. Every 128-wide group of an activation row
+// and the level table are scaled by powers of two that keep each f16
+// remainder in the normal range; the epilogue undoes them exactly (the
+// activation scale per row and group, the level scale folded into the norms).
 // When every scaled level is itself an f16 value (codebooks stored as f16
 // numbers, as the packer writes them), the level remainders are zero: that
 // form skips their tile and their MMA, two MMAs per K step instead of three.
 //
-// Per call, one preparation launch (umma_prep_kernel) splits the activation
-// rows and reads the packed `.cact` codes of the requested weight rows in
-// place, writing their level high parts (and remainders) as f16
-// [rows][in_pad] tiles (L2-resident for the GEMM that follows), once, instead
-// of once per 128-row activation tile; the group norms stay in the container
-// and are applied by the epilogue.
+// Operands: the engine's matrices have their level tiles expanded once at
+// load (umma_cache_levels); other callers get them from the packed codes per
+// call. The split activations come from the kernel that produced the rows
+// (the engine's row and attention kernels write this form directly) or from
+// a preparation launch (umma_prep_kernel), which also expands uncached levels.
 //
-// One CTA computes 128 activation rows x 128 weight rows with 10 warps:
-//   * warp 8 loads [128 rows x 64 k] tiles of the split activations and of the
-//     expanded levels with TMA and 128-byte swizzle into a ring of four
-//     (three with level remainders) stages, and owns the TMEM allocation;
-//   * warp 9 (one thread) issues tcgen05.mma kind::f16 M=128 N=128 K=16, two
-//     (three) per K step, into the group's accumulator pair; groups alternate
-//     between two pairs so one is drained while the other fills;
-//   * warps 0-7 drain the accumulators (warp w reads TMEM lanes 32*(w%4)..,
-//     columns of half w/4) and store y.
+// Persistent: one CTA per SM walks tiles of 128 activation rows x UN (64, 128
+// or 192) weight rows with UN / 16 + 2 warps:
+//   * one warp loads [128 rows x 64 k] tiles of the split activations and of
+//     the levels with TMA and 128-byte swizzle into a ring of stages, and owns
+//     the TMEM allocation;
+//   * one thread issues tcgen05.mma kind::f16 M=128 N=UN K=16, two (three)
+//     per K step; the groups of every tile alternate between two accumulators
+//     so one is drained while the other fills;
+//   * UN / 16 epilogue warps drain the accumulators (warp w reads TMEM lanes
+//     32*(w%4).. and 64 columns from 64*(w/4)) and store y through a per-warp
+//     shared-memory transpose.
 // Every wait on an mbarrier is bounded in time; on expiry the CTA raises a
 // device error flag, stops, waits (bounded) for its issued copies and MMAs,
 // frees its TMEM and returns, and the host reports the flag.
@@ -194,21 +196,6 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, uint32_t (&r)[16]) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// f32 -> (f16 high part, f16 remainder), packed as lo16 = hi, hi16 = remainder.
-__device__ __forceinline__ uint32_t split_h(float x) {
-  const __half h = __float2half_rn(x);
-  const __half l = __float2half_rn(x - __half2float(h));
-  return (uint32_t)__half_as_ushort(h) | ((uint32_t)__half_as_ushort(l) << 16);
-}
-
-// Power of two that brings max|v| into [2^13, 2^14) (1 for an all-zero row).
-__device__ __forceinline__ int row_exp(float amax) {
-  if (!(amax > 0.f) || !isfinite(amax)) return 0;
-  int e;
-  frexpf(amax, &e);  // amax in [2^(e-1), 2^e)
-  return 14 - e;
-}
-
 
 // EXACT: every level times the level scale is an f16 value, so the level
 // remainders are zero and only x_hi * l_hi and x_lo * l_hi are issued (two
@@ -294,8 +281,11 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
       float acc[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) acc[i] = 0.f;
+      const int m = m0 + q * 32 + lane;
+      const float* arow = ainv + (size_t)(m < M ? m : 0) * ng;  // this row's group scales
       for (int g = 0; g < ng; ++g, ++gg) {
         const int b = gg & 1;
+        const float ag = arow[g];  // in flight while the group completes
         if (ok && !mbar_wait(&tfull[b], (uint32_t)(gg >> 1) & 1u, abort, werr, 128)) ok = false;
         if (!ok) continue;
         tc_fence_after();
@@ -313,13 +303,13 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
 #pragma unroll
           for (int h = 0; h < LPW; ++h)
 #pragma unroll
-            for (int i = 0; i < 16; ++i) acc[(cb + h) * 16 + i] += ngp[(cb + h) * 16 + i] * __uint_as_float(r[h][i]);
+            for (int i = 0; i < 16; ++i)
+              acc[(cb + h) * 16 + i] += (ngp[(cb + h) * 16 + i] * ag) * __uint_as_float(r[h][i]);
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&tempty[b]);
       }
-      const int m = m0 + q * 32 + lane;
       const int lim = nrows - (n0 + cq * 64);
       // Warp-uniform: the warp's 32 rows x 64 columns lie inside y and every
       // row start is 16-byte aligned. The rows then leave through shared
@@ -328,15 +318,13 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
       const bool vec = out_stage && ok && m0 + q * 32 + 32 <= M && lim >= 64 && (ldy & 3) == 0 &&
                        (reinterpret_cast<uintptr_t>(y + n0 + cq * 64) & 15) == 0;
       if (vec) {
-        const float ai = ainv[m];
         float* ob = ostage + (size_t)warp * 32 * OST;
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
 #pragma unroll
           for (int i = 0; i < 16; i += 4)
             *reinterpret_cast<float4*>(ob + lane * OST + i) =
-                make_float4(acc[cb * 16 + i] * ai, acc[cb * 16 + i + 1] * ai, acc[cb * 16 + i + 2] * ai,
-                            acc[cb * 16 + i + 3] * ai);
+                make_float4(acc[cb * 16 + i], acc[cb * 16 + i + 1], acc[cb * 16 + i + 2], acc[cb * 16 + i + 3]);
           __syncwarp();
 #pragma unroll
           for (int it = 0; it < 4; ++it) {
@@ -347,11 +335,10 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
           __syncwarp();
         }
       } else if (ok && m < M) {
-        const float ai = ainv[m];
         float* yr = y + (size_t)m * ldy + n0 + cq * 64;
 #pragma unroll
         for (int i = 0; i < 64; ++i)
-          if (i < lim) yr[i] = acc[i] * ai;
+          if (i < lim) yr[i] = acc[i];
       }
     }
   } else if (warp == EW) {
@@ -440,7 +427,7 @@ template <int BITS>
 __device__ __forceinline__ void expand_levels(const CqMat& W, int row0, int nrows, int le, __half* __restrict__ whi,
                                               __half* __restrict__ wlo, int blk, int nblk) {
   __shared__ uint32_t tab[16];  // level * 2^le as (hi | lo << 16)
-  if (threadIdx.x < 16) tab[threadIdx.x] = split_h(ldexpf(W.levels[threadIdx.x < (1 << BITS) ? threadIdx.x : 0], le));
+  if (threadIdx.x < 16) tab[threadIdx.x] = split_h16(ldexpf(W.levels[threadIdx.x < (1 << BITS) ? threadIdx.x : 0], le));
   __syncthreads();
   const int per_row = W.in_pad / 8;
   const long total = (long)nrows * per_row;
@@ -467,34 +454,19 @@ __device__ __forceinline__ void expand_levels(const CqMat& W, int row0, int nrow
 // f32 activations [M][ldx] -> row-scaled f16 high parts and remainders
 // [M][K] and the inverse row scales [M]. One warp per row (block `blk`: rows
 // blk * 8 ..).
+// Activation rows [M][K] f32 -> hi / lo [M][K] f16 and inv [M][K / 128], each
+// 128-wide group scaled on its own (split_group_store); one warp per row.
 __device__ __forceinline__ void split_rows(const float* __restrict__ x, int ldx, int M, int K, __half* __restrict__ hi,
                                            __half* __restrict__ lo, float* __restrict__ inv, int blk) {
   const int lane = threadIdx.x & 31;
   const int m = blk * (blockDim.x >> 5) + (threadIdx.x >> 5);
-  if (m >= M) return;
+  if (m >= M) return;  // the whole warp
   const float* xr = x + (size_t)m * ldx;
-  float amax = 0.f;
-  for (int c = lane * 4; c < K; c += 128) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + c);
-    amax = fmaxf(amax, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(a.z), fabsf(a.w))));
-  }
-  amax = warp_max(amax);
-  const int e = row_exp(amax);
-  const float sc = ldexpf(1.f, e);
-  if (lane == 0) inv[m] = ldexpf(1.f, -e);
-  for (int c = lane * 8; c < K; c += 256) {
-    const float4 a = *reinterpret_cast<const float4*>(xr + c);
-    const float4 b = *reinterpret_cast<const float4*>(xr + c + 4);
-    const float v[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
-    uint32_t h[4], l[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t p = split_h(v[2 * j] * sc), q = split_h(v[2 * j + 1] * sc);
-      h[j] = __byte_perm(p, q, 0x5410);
-      l[j] = __byte_perm(p, q, 0x7632);
-    }
-    *reinterpret_cast<uint4*>(hi + (size_t)m * K + c) = make_uint4(h[0], h[1], h[2], h[3]);
-    *reinterpret_cast<uint4*>(lo + (size_t)m * K + c) = make_uint4(l[0], l[1], l[2], l[3]);
+  const int ng = K / 128;
+  for (int g = 0; g < ng; ++g) {
+    const float4 a = *reinterpret_cast<const float4*>(xr + g * 128 + lane * 4);
+    const float v[4] = {a.x, a.y, a.z, a.w};
+    split_group_store(v, hi + (size_t)m * K + g * 128, lo + (size_t)m * K + g * 128, inv + (size_t)m * ng + g);
   }
 }
 
@@ -625,7 +597,7 @@ cudaError_t umma_cache_levels(CqMat* W, std::vector<void*>* owned, cudaStream_t 
 }
 
 cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                            int nrows, cudaStream_t st, const GemmScratch& gs) {
+                            int nrows, cudaStream_t st, const GemmScratch& gs, bool presplit) {
   const int K = W.in_pad;
   if (!umma_supported(W) || !gs.hi || !gs.lo || !gs.inv || !gs.whi || !gs.wlo || gs.elems < (size_t)M * K ||
       gs.rows < (size_t)M || gs.welems < (size_t)nrows * K)
@@ -642,18 +614,21 @@ cudaError_t cq_project_umma(const CqMat& W, const float* xh, int ldx, int M, flo
   const __half* wlo = cached ? (W.lvl_lo ? W.lvl_lo + (size_t)row0 * K : whi) : gs.wlo;
   cudaError_t e;
   {
-    const int split_blocks = (M + 7) / 8;
+    // presplit: the producer of xh already wrote gs.hi / lo / inv.
+    const int split_blocks = presplit ? 0 : (M + 7) / 8;
     const long total = (long)nrows * (K / 8);
     const int eblocks = cached ? 0 : (int)std::min<long>((total + 255) / 256, 148L * 8);
     __half* xwlo = exact ? nullptr : gs.wlo;  // remainders, when the levels need them
-    if (W.bits == 2)
-      umma_prep_kernel<2><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv, split_blocks,
-                                                                  W, row0, nrows, le, gs.whi, xwlo);
-    else
-      umma_prep_kernel<4><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv, split_blocks,
-                                                                  W, row0, nrows, le, gs.whi, xwlo);
-    e = cudaGetLastError();
-    if (e != cudaSuccess) return e;
+    if (split_blocks + eblocks > 0) {  // else nothing to prepare: the projection is one launch
+      if (W.bits == 2)
+        umma_prep_kernel<2><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv,
+                                                                    split_blocks, W, row0, nrows, le, gs.whi, xwlo);
+      else
+        umma_prep_kernel<4><<<split_blocks + eblocks, 256, 0, st>>>(xh, ldx, M, K, gs.hi, gs.lo, gs.inv,
+                                                                    split_blocks, W, row0, nrows, le, gs.whi, xwlo);
+      e = cudaGetLastError();
+      if (e != cudaSuccess) return e;
+    }
   }
   int* werr = gs.werr;
   if (!werr) {
