@@ -214,6 +214,7 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
                const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
                int nrows, int ntn, int ntiles, int* werr, int out_stage) {
+  pdl_trigger();  // the consumer of y may launch now; it waits for this grid before reading y
   using P = Pipe<EXACT, UN>;
   constexpr int USTAGES = P::STAGES;
   constexpr uint32_t STAGE_BYTES = P::STAGE_BYTES;
@@ -256,6 +257,9 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  // Launched with programmatic dependent launch: the set-up above overlaps the
+  // producer of the activations; everything below reads what it wrote.
+  pdl_wait();
 
   if (warp < EW) {
     // ------------------------------------------------ epilogue: drain each group
@@ -528,9 +532,8 @@ cudaError_t launch_umma(const CqMat& W, const GemmScratch& gs, const __half* whi
   if (e != cudaSuccess) return e;
   const int ntn = (nrows + UN - 1) / UN, ntiles = ntn * ((M + UM - 1) / UM);
   const int grid = std::min(ntiles, 148);  // persistent: one CTA per SM
-  kern<<<grid, Pipe<EXACT, UN>::THREADS, smem, st>>>(W, mah, mal, mbh, mbl, gs.inv, linv, M, y, ldy, row0, nrows,
-                                                      ntn, ntiles, werr, out_stage ? 1 : 0);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(Pipe<EXACT, UN>::THREADS), smem, st, W, mah, mal, mbh, mbl, gs.inv, linv,
+                    M, y, ldy, row0, nrows, ntn, ntiles, werr, out_stage ? 1 : 0);
 }
 
 }  // namespace
