@@ -76,6 +76,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
   const size_t S = std::max(1, G.n_sites);
   const size_t kmax = std::max(dpad, opad);  // widest input of a projection
   const size_t wmax = std::max<size_t>(std::max<size_t>(G.logit_rows, G.proj_dim), 2 * d);  // most weight rows
+  const size_t pre_rows = std::min<size_t>(cap, PRE_SPLIT_MAX_ROWS);  // rows of the split mHC pre-projection
   struct A {
     void** p;
     size_t bytes;
@@ -95,7 +96,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
       {(void**)&w.pks, cap * G.kvh * 4},           {(void**)&w.pvs, cap * G.kvh * 4},
       {(void**)&w.rows, cap * sizeof(RowInfo)},    {(void**)&w.tokens, cap * 4},
       {(void**)&w.next, cap * 4},                  {(void**)&w.last_rows, cap * 4},
-      {(void**)&w.pre_part, 8 * 32 * 32 * 4},     {(void**)&w.pre_cnt, 8 * 4},
+      {(void**)&w.pre_part, pre_rows * 32 * 32 * 4}, {(void**)&w.pre_cnt, pre_rows * 4},
   };
   for (auto& a : allocs) {
     cudaError_t e = cudaMalloc(a.p, std::max<size_t>(a.bytes, 256));
@@ -107,7 +108,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
   }
   {
     cudaError_t e = cudaMemset(w.cnt, 0, cap * G.kvh * 4);  // attention split counters start at zero
-    if (e == cudaSuccess) e = cudaMemset(w.pre_cnt, 0, 8 * 4);
+    if (e == cudaSuccess) e = cudaMemset(w.pre_cnt, 0, pre_rows * 4);
     if (e != cudaSuccess) {
       w.release();
       *err = cuda_msg("workspace initialisation", e);

@@ -72,8 +72,8 @@ struct Workspace {
   bool head_presplit = false;
   __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
   int* cnt = nullptr;  // attention split-arrival counters [rows][kv heads], zero between launches
-  float* pre_part = nullptr;  // few-row mHC pre-projection partials [8][32][32]
-  int* pre_cnt = nullptr;     // and its per-row arrival counters [8], zero between launches
+  float* pre_part = nullptr;  // split mHC pre-projection partials [rows][32][32]
+  int* pre_cnt = nullptr;     // and its per-row arrival counters, zero between launches
   GemmScratch gs;
   RowInfo* rows = nullptr;
   uint32_t *tokens = nullptr, *next = nullptr;

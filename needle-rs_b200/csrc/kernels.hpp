@@ -127,8 +127,13 @@ cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBat
                                  float* fetched, cudaStream_t st);
 cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const RowBatch& rb,
                                const float* ekv, float* evc, cudaStream_t st);
-// split_part / split_cnt (nullable): scratch of the few-row form, 8 rows x 32
-// groups x 32 floats and 8 zero-initialised counters (reset by the kernel).
+// Rows up to which launch_layer_pre spreads each row over one CTA per 128-wide
+// lane group (the last CTA of a row runs its tail). Measured at 512 rows this
+// form took 1.93 ms per decode step against 0.78 for 4-row tiles.
+constexpr int PRE_SPLIT_MAX_ROWS = 8;
+// split_part / split_cnt (nullable): scratch of that form, PRE_SPLIT_MAX_ROWS
+// rows x 32 groups x 32 floats and PRE_SPLIT_MAX_ROWS zero-initialised counters
+// (reset by the kernel).
 // so.hi non-null: the rotated attention input goes to so (the q|k|v|gate
 // projection's tensor-core operands, [M][dpad]) instead of xh.
 cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const float* lanes,

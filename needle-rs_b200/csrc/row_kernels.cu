@@ -608,13 +608,12 @@ __global__ void layer_pre_kernel(Geo G, int li, RowBatch rb, const float* __rest
 // that CTA) sums the groups in order, applies rms_unit (kernels.rs:32; a common
 // factor of every dot, applied to the finished sums) and runs the tail. No CTA
 // waits for another.
-constexpr int PRE_SPLIT_MAX_ROWS = 8;
 constexpr int PRE_SPLIT_MAX_GROUPS = 32;
 __global__ void __launch_bounds__(256) layer_pre_split_kernel(
     Geo G, int li, RowBatch rb, const float* __restrict__ lanes, CqMat phi_pre, CqMat phi_post, CqMat phi_res,
     MhcParams mp, const float* __restrict__ norm_in, int site, const float* __restrict__ ekv,
     const float* __restrict__ evc, float* __restrict__ u_out, float* __restrict__ bx_out, float* __restrict__ xh_out,
-    float* __restrict__ gates, float* __restrict__ part, int* __restrict__ cnt) {
+    float* __restrict__ gates, float* __restrict__ part, int* __restrict__ cnt, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   extern __shared__ __align__(16) float sm[];
   __shared__ __align__(16) float X[128];
@@ -711,7 +710,7 @@ __global__ void __launch_bounds__(256) layer_pre_split_kernel(
   cp_wait<0>();
   __syncthreads();
   layer_pre_tail(G, li, r, mp, phi, Ls, gsm, red, bx, hb, nis, ek ? eks : nullptr, ek ? evs : nullptr, u_out,
-                 bx_out, xh_out, gates, SplitOut{});
+                 bx_out, xh_out, gates, so);
 }
 
 // The same computation for many rows: PT_M rows per CTA so each mHC weight
@@ -982,10 +981,9 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
                              cudaStream_t st, float* split_part, int* split_cnt, SplitOut so) {
   if (rb.M <= 0) return cudaSuccess;
   const int nrow = 2 * G.lanes + G.lanes * G.lanes;
-  // Up to PRE_SPLIT_MAX_ROWS rows (f32 output for the GEMV): every row over
-  // (lanes x d_model) / 128 CTAs.
+  // Up to PRE_SPLIT_MAX_ROWS rows: every row over (lanes x d_model) / 128 CTAs.
   const int ngr = G.lanes * G.d / 128;
-  if (!so.hi && split_part && split_cnt && rb.M <= PRE_SPLIT_MAX_ROWS && G.d % 128 == 0 && ngr <= PRE_SPLIT_MAX_GROUPS &&
+  if (split_part && split_cnt && rb.M <= PRE_SPLIT_MAX_ROWS && G.d % 128 == 0 && ngr <= PRE_SPLIT_MAX_GROUPS &&
       nrow <= 24 && phi_pre.groups == ngr && phi_post.groups == ngr && phi_res.groups == ngr &&
       (reinterpret_cast<uintptr_t>(norm_in) & 15) == 0 && (reinterpret_cast<uintptr_t>(lanes) & 15) == 0 &&
       (reinterpret_cast<uintptr_t>(ekv) & 15) == 0 && (reinterpret_cast<uintptr_t>(evc) & 15) == 0) {
@@ -993,7 +991,7 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
     cudaError_t e = allow_smem((const void*)layer_pre_split_kernel, smem);
     if (e != cudaSuccess) return e;
     return launch_pdl(layer_pre_split_kernel, dim3(ngr, rb.M), dim3(256), smem, st, G, li, rb, lanes, phi_pre,
-                      phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates, split_part, split_cnt);
+                      phi_post, phi_res, mp, norm_in, site, ekv, evc, u, bx, xh, gates, split_part, split_cnt, so);
   }
   const int rbmax = std::max(phi_pre.row_bytes, std::max(phi_post.row_bytes, phi_res.row_bytes));
   const int gmax = std::max(phi_pre.groups, std::max(phi_post.groups, phi_res.groups));
