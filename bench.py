@@ -338,6 +338,7 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
     lv = cact_pack.codebook_levels(cb, 2)
     x = rng.normal(size=(512, 768)).astype(np.float32)
     c1 = {}
+    kept = []  # the three matrices, for the grouped launch below
     for n_out in (768, 2304, 3072):
         idx, norms = cact_pack.random_cq(np.random.default_rng(n_out), n_out, 768, 2)
         blob = cact_pack.cq_blob(idx, norms, 2)
@@ -355,6 +356,17 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
         c1[str(n_out)] = {"us": round(us, 2), "tflops": round(flop / us / 1e6, 2),
                           "frac_of_bf16_peak": round(flop / us / 1e6 / bf16, 4),
                           "cpu_us": round(cpu_s * 1e6, 1), "cpu_cores": ncpu}
+        kept.append((d, n_out))
+    # The three as one launch (the input's rotation is the same for every matrix).
+    n_all = sum(n for _, n in kept)
+    ya = torch.zeros(512, n_all, device="cuda")
+    grp = [(dd.data_ptr(), dd.data_ptr() + n * 192, n) for dd, n in kept]
+    us = _graph_us(torch, lambda s: nb.cq_project_grouped(grp, 768, 2, lv, xd.data_ptr(), 768, 512, ya.data_ptr(),
+                                                          n_all, stream=s), 50)
+    flop = 2 * 512 * 768 * n_all
+    c1["grouped"] = {"us": round(us, 2), "tflops": round(flop / us / 1e6, 2),
+                     "frac_of_bf16_peak": round(flop / us / 1e6 / bf16, 4),
+                     "note": "the three matrices in one call (nd_cq_project_grouped)"}
     out["config1_gemm"] = {"metric": "X[512,768] x W[N,768] 2-bit CQ projection (tensor cores, f16 hi/lo split), "
                                      "device time per call from a CUDA graph of 50 calls",
                            "roofline": "tensor (bf16 dense peak, measured)", "by_n": c1}

@@ -220,12 +220,23 @@ int needle_v3_device(NeedleV3Handle *handle);
  * codebook entries (host). xh is the rotated input (prepare_input, cq.rs:264),
  * [M][ldx] f32. path: 0 auto, 1 GEMV (M <= 8), 2 tiled SIMT GEMM, 3 tensor-core
  * GEMM (tcgen05; chosen by path 0 for M > 8; uses stream-ordered scratch of
- * 4*(M + nrows)*in_pad + 4*M bytes); for M <= 8, 4 the SIMT GEMV kernels and 5
+ * 4*(M + nrows)*in_pad + 4*M*in_pad/128 bytes); for M <= 8, 4 the SIMT GEMV kernels and 5
  * the tensor-core GEMV (mma.sync; codebooks whose levels are f16 values). Replaces
  * CqWeight::matvec_rows_prepared / matmul_rows_prepared (cq.rs:301, :446). */
 int nd_cq_project(const void *packed, const void *norms, int rows, int in_feat, int bits,
                   const float *levels, const float *xh, int ldx, int M, float *y, int ldy,
                   int row0, int nrows, int path, void *stream);
+
+/* Several CQ projections of the same input as one: matrix i (packed[i],
+ * norms[i], rows[i] rows, laid out as for nd_cq_project; every matrix with the
+ * same in_feat, bits and levels; 1 <= count <= 4) fills columns [r_i, r_i +
+ * rows[i]) of y [M][ldy], r_i the rows of the matrices before it: one tensor-
+ * core launch for all of them (path 0 or 3 with M > 8), as the engine runs a
+ * block's q, k, v and gate projections (v3/model.rs:260-262, :309). Other
+ * paths and the scratch are those of nd_cq_project over all the rows. */
+int nd_cq_project_grouped(int count, const void *const *packed, const void *const *norms, const int *rows,
+                          int in_feat, int bits, const float *levels, const float *xh, int ldx, int M,
+                          float *y, int ldy, int path, void *stream);
 
 /* prepare_input (cq.rs:264-274): zero-pad x [M][in_feat] to in_pad and apply
  * the normalised Walsh-Hadamard transform to every group of 128. */

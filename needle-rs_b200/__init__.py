@@ -143,6 +143,8 @@ def lib() -> C.CDLL:
         "needle_v3_device": (C.c_int, [vp]),
         "nd_cq_project": (C.c_int, [vp, vp, C.c_int, C.c_int, C.c_int, vp, vp, C.c_int, C.c_int, vp,
                                     C.c_int, C.c_int, C.c_int, C.c_int, vp]),
+        "nd_cq_project_grouped": (C.c_int, [C.c_int, vp, vp, vp, C.c_int, C.c_int, vp, vp, C.c_int, C.c_int, vp,
+                                            C.c_int, C.c_int, vp]),
         "nd_cq_prepare": (C.c_int, [vp, C.c_int, C.c_int, vp, C.c_int, vp]),
         "nd_kv_quant": (C.c_int, [vp, C.c_int, C.c_int, vp, vp, vp]),
         "nd_attend_step": (C.c_int, [vp, vp, vp, vp, vp, C.c_int, C.c_int, vp, vp, C.c_int, C.c_int,
@@ -460,6 +462,21 @@ def cq_project(packed_ptr, norms_ptr, rows, in_feat, bits, levels, xh_ptr, ldx, 
     _check(lib().nd_cq_project(packed_ptr, norms_ptr, rows, in_feat, bits, lv.ctypes.data, xh_ptr, ldx,
                                M, y_ptr, ldy, row0, rows - row0 if nrows is None else nrows, path, stream),
            "nd_cq_project")
+
+
+def cq_project_grouped(mats, in_feat, bits, levels, xh_ptr, ldx, M, y_ptr, ldy, path=0, stream=None):
+    """mats: [(packed_ptr, norms_ptr, rows)], up to four matrices sharing
+    in_feat, bits and levels; y [M][ldy] receives their rows side by side."""
+    n = len(mats)
+    packed = (C.c_void_p * n)(*[m[0] for m in mats])
+    norms = (C.c_void_p * n)(*[m[1] for m in mats])
+    rows = (C.c_int * n)(*[m[2] for m in mats])
+    lv = np.zeros(16, np.float32)
+    lv[: 1 << bits] = np.asarray(levels, np.float32)[: 1 << bits]
+    _check(lib().nd_cq_project_grouped(n, C.cast(packed, C.c_void_p), C.cast(norms, C.c_void_p),
+                                       C.cast(rows, C.c_void_p), in_feat, bits, lv.ctypes.data, xh_ptr, ldx, M,
+                                       y_ptr, ldy, path, stream),
+           "nd_cq_project_grouped")
 
 
 def cq_prepare(x_ptr, M, in_feat, xh_ptr, ld_out, stream=None):

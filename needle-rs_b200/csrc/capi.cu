@@ -1016,13 +1016,11 @@ bool needle_v3_debug_buffer(NeedleV3Handle* h, int which, float* out, size_t cou
 }
 
 // ------------------------------------------------------------------ Part 3
-int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, int bits,
-                  const float* levels, const float* xh, int ldx, int M, float* y, int ldy, int row0,
-                  int nrows, int path, void* stream) {
-  if (!packed || !norms || !levels || !xh || !y || rows <= 0 || in_feat <= 0 || (bits != 2 && bits != 4))
-    return nd_status(cudaErrorInvalidValue);
-  nb::CqMat W = make_cq(packed, norms, rows, in_feat, bits, levels);
-  cudaStream_t st = (cudaStream_t)stream;
+// One projection of a built matrix: the tensor-core path gets stream-ordered
+// scratch, the others run directly.
+static int project_mat(const nb::CqMat& W, const float* xh, int ldx, int M, float* y, int ldy, int row0, int nrows,
+                       int path, cudaStream_t st) {
+  const int rows = W.rows;
   const bool tensor_cores = path == 3 || (path == 0 && M > 8 && nb::umma_supported(W));
   if (!tensor_cores || M <= 0) return nd_status(nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, st, path));
   // The split activations live in stream-ordered scratch, released on `stream`.
@@ -1044,6 +1042,36 @@ int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, 
   e = nb::cq_project(W, xh, ldx, M, y, ldy, row0, nrows, st, path, &gs);
   cudaError_t f = cudaFreeAsync(mem, st);
   return nd_status(e != cudaSuccess ? e : f);
+}
+
+int nd_cq_project(const void* packed, const void* norms, int rows, int in_feat, int bits,
+                  const float* levels, const float* xh, int ldx, int M, float* y, int ldy, int row0,
+                  int nrows, int path, void* stream) {
+  if (!packed || !norms || !levels || !xh || !y || rows <= 0 || in_feat <= 0 || (bits != 2 && bits != 4))
+    return nd_status(cudaErrorInvalidValue);
+  const nb::CqMat W = make_cq(packed, norms, rows, in_feat, bits, levels);
+  return project_mat(W, xh, ldx, M, y, ldy, row0, nrows, path, (cudaStream_t)stream);
+}
+
+int nd_cq_project_grouped(int count, const void* const* packed, const void* const* norms, const int* rows,
+                          int in_feat, int bits, const float* levels, const float* xh, int ldx, int M, float* y,
+                          int ldy, int path, void* stream) {
+  if (count < 1 || count > nb::MAX_SEG || !packed || !norms || !rows || !levels || !xh || !y || in_feat <= 0 ||
+      (bits != 2 && bits != 4))
+    return nd_status(cudaErrorInvalidValue);
+  for (int i = 0; i < count; ++i)
+    if (!packed[i] || !norms[i] || rows[i] <= 0) return nd_status(cudaErrorInvalidValue);
+  // One matrix whose row segments are the given matrices (the form the engine
+  // gives a block's q|k|v|gate).
+  nb::CqMat W = make_cq(packed[0], norms[0], rows[0], in_feat, bits, levels);
+  for (int i = 1; i < count; ++i) {
+    W.seg[i].packed = (const uint8_t*)packed[i];
+    W.seg[i].norms = (const __half*)norms[i];
+    W.seg[i].rows = rows[i];
+    W.rows += rows[i];
+  }
+  W.nseg = count;
+  return project_mat(W, xh, ldx, M, y, ldy, 0, W.rows, path, (cudaStream_t)stream);
 }
 
 int nd_cq_prepare(const float* x, int M, int in_feat, float* xh, int ld_out, void* stream) {

@@ -321,3 +321,35 @@ def test_attend_step_ring_wrap_and_ragged_ranges(cuda):
     for b, (l, h) in enumerate(ranges):
         want = orc.attend_step(q[b].ravel(), S, l, h, H, KVH, QK, VH, k=k[b].ravel(), v=v[b].ravel())
         assert close(got[b], want, 1e-4)
+
+
+@pytest.mark.parametrize("M", [512, 40])
+def test_cq_grouped_projection_is_the_separate_ones(cuda, M):
+    """nd_cq_project_grouped over config 1's three matrices (768, 2304 and 3072
+    rows of 768, sharing the codebook) fills y with each matrix's projection
+    side by side, matching both the oracle and three nd_cq_project calls."""
+    torch = cuda
+    cb = cact_pack.random_codebook(np.random.default_rng(21))
+    levels = cact_pack.codebook_levels(cb, 2)
+    shapes = [(768, 768), (2304, 768), (3072, 768)]
+    mats = [make_weight(torch, out, inp, 2, 30 + i, cb) for i, (out, inp) in enumerate(shapes)]
+    inp = 768
+    x = np.random.default_rng(22).normal(size=(M, inp)).astype(np.float32)
+    xh = np.stack([mats[0][3].prepare(r) for r in x])
+    xd = dev(torch, xh)
+    total = sum(o for o, _ in shapes)
+    yg = torch.zeros(M, total, device="cuda")
+    nb.cq_project_grouped([(m[1], m[2], o) for m, (o, _) in zip(mats, shapes)], inp, 2, levels, xd.data_ptr(), inp,
+                          M, yg.data_ptr(), total)
+    ys = []
+    for m, (o, _) in zip(mats, shapes):
+        y = torch.zeros(M, o, device="cuda")
+        nb.cq_project(m[1], m[2], o, inp, 2, levels, xd.data_ptr(), inp, M, y.data_ptr(), o)
+        ys.append(y)
+    torch.cuda.synchronize()
+    got = yg.cpu().numpy()
+    sep = np.concatenate([y.cpu().numpy() for y in ys], axis=1)
+    want = np.concatenate([m[3].matmul_prepared(xh) for m in mats], axis=1)
+    assert close(got, want), float(np.abs(got - want).max())
+    # The same products in the same order: one launch or three agree exactly.
+    assert np.array_equal(got, sep)
