@@ -295,9 +295,15 @@ class V3Engine:
             _fail("needle_v3_prefill_batch")
         return out, picks
 
+    def group(self, sessions) -> "SessionGroup":
+        """The sessions as a group for repeated batched calls (decode_batch)."""
+        return SessionGroup(sessions)
+
     def decode_batch(self, sessions, tokens, logits: bool = True):
+        """One decode step of every session (a list or a SessionGroup) with host
+        tokens in; returns (logits [n, rows] or None, picks [n])."""
         n = len(sessions)
-        arr = (C.c_void_p * n)(*[s._s for s in sessions])
+        arr = sessions._arr if isinstance(sessions, SessionGroup) else (C.c_void_p * n)(*[s._s for s in sessions])
         tok = np.ascontiguousarray(tokens, np.uint32)
         out = np.zeros((n, self.logit_rows), np.float32) if logits else None
         picks = np.zeros(n, np.uint32)
@@ -323,6 +329,20 @@ class V3Engine:
         if not b:
             _fail("needle_v3_batch_new")
         return Batch(self, b, list(sessions))
+
+
+class SessionGroup:
+    """A fixed list of one engine's sessions whose handle array is built once,
+    for repeated batched calls (building it from a list of thousands of
+    sessions costs about as much as a decode step's host work). Holds the
+    sessions; they must stay open while the group is used."""
+
+    def __init__(self, sessions):
+        self.sessions = list(sessions)
+        self._arr = (C.c_void_p * len(self.sessions))(*[s._s for s in self.sessions])
+
+    def __len__(self):
+        return len(self.sessions)
 
 
 class Session:

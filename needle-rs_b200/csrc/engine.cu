@@ -1420,13 +1420,15 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
     }
     if (!ensure_slots(ss[i], ss[i]->pos, err)) return false;
   }
-  {
-    std::vector<Session*> sorted(ss, ss + n);
-    std::sort(sorted.begin(), sorted.end());
-    if (std::adjacent_find(sorted.begin(), sorted.end()) != sorted.end()) {
+  // A session twice in one batch: every session carries the stamp of the last
+  // call that saw it (one pass instead of a sort of the list).
+  ++batch_stamp;
+  for (size_t i = 0; i < n; ++i) {
+    if (ss[i]->seen == batch_stamp) {
       *err = "a session appears twice in one decode batch";
       return false;
     }
+    ss[i]->seen = batch_stamp;
   }
   size_t maxpos = 0;
   for (size_t i = 0; i < n; ++i) maxpos = std::max(maxpos, ss[i]->pos);

@@ -53,6 +53,7 @@ class Session {
   void* d_state = nullptr;        // tails + token ring (inside the arena)
   void* d_arena = nullptr;        // one allocation holding the initial rings, state and descriptors
   std::vector<char> owned;        // layer ring grown into its own allocation
+  uint64_t seen = 0;              // the engine's batch-check stamp of the last call it was in
   size_t state_bytes = 0;
   size_t bytes() const;           // device bytes held, as V3Cache::bytes counts them
 };
@@ -133,6 +134,7 @@ class Engine {
   int device = 0;
   cudaStream_t stream = nullptr;
   std::mutex mu;
+  uint64_t batch_stamp = 0;  // per call of a session-list API, under mu: O(n) duplicate checks
 
   Session* new_session(size_t hint, bool int8, std::string* err);
   // Whole-prompt prefill of fresh sessions (model.rs:512-523). Writes the last

@@ -115,8 +115,10 @@ def test_batched_sessions_match_single_sessions(full_gpu):
             assert rel_err(a, b) < tol_pair(int8)
         assert np.array_equal(picks, np.array([int(np.argmax(r)) for r in ref]))
         toks = picks
-        for _ in range(6):
-            lg, picks = full_gpu.decode_batch(batch, toks)
+        grp = full_gpu.group(batch)
+        for step in range(6):
+            # a plain list and a SessionGroup (handle array built once) alternate
+            lg, picks = full_gpu.decode_batch(grp if step % 2 else batch, toks)
             ref = [s.decode_step(int(t)) for s, t in zip(singles, toks)]
             for a, b in zip(lg, ref):
                 assert rel_err(a, b) < tol_pair(int8)
@@ -219,3 +221,11 @@ def test_engine_errors_are_reported(full_gpu):
         full_gpu.prefill_batch([a, b], [[1, 2], [3, 4]])
     with pytest.raises(nb.NeedleError):
         full_gpu.session(8).prefill(np.ones(8193, np.uint32))
+    # One session twice in a batched decode is refused; the same sessions in a
+    # valid batch right after still decode.
+    c = full_gpu.session(8)
+    c.prefill(np.arange(1, 5, dtype=np.uint32))
+    with pytest.raises(nb.NeedleError, match="twice"):
+        full_gpu.decode_batch([s, c, s], np.array([1, 2, 3], np.uint32), logits=False)
+    _, picks = full_gpu.decode_batch(full_gpu.group([s, c]), np.array([1, 2], np.uint32), logits=False)
+    assert len(picks) == 2
