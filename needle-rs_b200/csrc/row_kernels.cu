@@ -1006,7 +1006,8 @@ cudaError_t launch_layer_pre(const Geo& G, int li, const RowBatch& rb, const flo
                ? launch_pre_tiled<14>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so)
                : launch_pre_tiled<16>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so);
   if (tiled_ok && rb.M >= PRE_TILED_MIN_ROWS)
-    return launch_pre_tiled<4>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so);
+    return rb.M < 1024 ? launch_pre_tiled<2>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so)
+                       : launch_pre_tiled<4>(G, li, rb, lanes, mp, norm_in, site, ekv, evc, u, bx, xh, gates, st, so);
   const int W = G.lanes * G.d, dpad = (G.d + 127) / 128 * 128;
   const size_t smem = (size_t)(W + phi_pre.in_pad + G.d + dpad + 32 + 32 + 24 + 48 + nrow * gmax) * sizeof(float) +
                       (size_t)nrow * rbmax + 16;
