@@ -119,14 +119,27 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // bit-exact with the reference on identical inputs. This is the only int8
 // quantiser on the GPU: the KV append and the query fake-quant of qkv_post and
 // the standalone nd_kv_quant all call it. Returns the scale; the codes come
-// back as floats holding integers in [-128, 127].
-__device__ __forceinline__ float kv_quant_warp(float a, float b, float* ca, float* cb) {
-  const float am = warp_max(fmaxf(fabsf(a), fabsf(b)));
+// back as floats holding integers in [-128, 127]. Split in two steps
+// (kv_quant_absmax_warp, kv_quant_codes) so that a warp holding several
+// vectors can run their reductions back to back.
+//
+// The absolute maximum is one redux.sync over the IEEE bits: non-negative
+// floats order as their bit patterns. A NaN lane counts as 0, as fmaxf
+// ignores a NaN; an all-NaN vector gives 0 and scale 1 either way.
+__device__ __forceinline__ float kv_quant_absmax_warp(float a, float b) {
+  uint32_t u = __float_as_uint(fmaxf(fabsf(a), fabsf(b)));
+  u = u > 0x7f800000u ? 0u : u;
+  return __uint_as_float(__reduce_max_sync(0xffffffffu, u));
+}
+__device__ __forceinline__ float kv_quant_codes(float am, float a, float b, float* ca, float* cb) {
   const float scale = am > 0.0f ? __fdiv_rn(am, 127.0f) : 1.0f;
   const float inv = __fdiv_rn(1.0f, scale);
   *ca = fminf(fmaxf(roundf(__fmul_rn(a, inv)), -128.0f), 127.0f);
   *cb = fminf(fmaxf(roundf(__fmul_rn(b, inv)), -128.0f), 127.0f);
   return scale;
+}
+__device__ __forceinline__ float kv_quant_warp(float a, float b, float* ca, float* cb) {
+  return kv_quant_codes(kv_quant_absmax_warp(a, b), a, b, ca, cb);
 }
 
 // Normalised Walsh-Hadamard transform of 128 floats held by one warp, 4 per

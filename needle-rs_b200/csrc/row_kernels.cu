@@ -76,23 +76,28 @@ cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, flo
 // (gather). The fetched row feeds key/value projections whose prepare_input
 // rotates it again; the rotation is an involution, so the projection input is
 // the decoded codes levels[idx]*norm directly and both rotations are skipped.
-__global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, RowBatch rb,
-                                     float* __restrict__ fetched) {
+// One CTA per row, one warp per table (an order's hash head): the slot
+// depends on the tokens and the table only, not on the site, so it is hashed
+// once and the row of that slot is fetched from every site's table, EG_SITES
+// sites' loads in flight together.
+constexpr int EG_SITES = 8;
+__global__ void __launch_bounds__(256) engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, RowBatch rb,
+                                                            float* __restrict__ fetched) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
-  pdl_wait();     // everything below reads or writes what earlier kernels touch
-  const int r = blockIdx.x, site = blockIdx.y;
+  __shared__ float lev[16][16];
+  for (int i = threadIdx.x; i < G.n_sites * 16; i += blockDim.x) lev[i >> 4][i & 15] = tables[i >> 4].levels[i & 15];
+  pdl_wait();  // everything below reads or writes what earlier kernels touch
+  const int r = blockIdx.x;
   const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos;
-  const CqMat& T = tables[site];
-  __shared__ float lev[16];
-  load_levels(T, lev);
-  float* out = fetched + ((size_t)r * G.n_sites + site) * G.d;
+  __syncthreads();
   for (int t = wid; t < G.e_tables; t += nw) {
     const int oi = t / G.e_heads, h = t % G.e_heads;
     const int order = G.orders[oi];
-    float v[4] = {0.f, 0.f, 0.f, 0.f};
-    if (p + 1 >= order) {  // ngram_valid
+    const bool valid = p + 1 >= order;  // ngram_valid
+    uint32_t slot = 0;
+    if (valid) {
       uint32_t acc = 0x9E3779B9u * (uint32_t)(oi * G.e_stride + h + 1);
       for (int j = 0; j < order; ++j) {
         uint32_t tok;
@@ -107,20 +112,43 @@ __global__ void engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, Ro
         acc = (acc ^ tok) * 0x01000193u;
       }
       acc ^= acc >> 15;
-      const uint32_t slot = acc % (uint32_t)G.e_slots;
-      const size_t trow = (size_t)t * G.e_slots + slot;
-      const uint8_t* row = T.seg[0].packed + trow * T.row_bytes;
-      decode_group_lane(T, lev, row, __half2float(T.seg[0].norms[trow * T.groups]), 0, v);
+      slot = acc % (uint32_t)G.e_slots;
     }
-    reinterpret_cast<float4*>(out + t * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+    const size_t trow = (size_t)t * G.e_slots + slot;
+    for (int s0 = 0; s0 < G.n_sites; s0 += EG_SITES) {
+      uint32_t code[EG_SITES];
+      float nrm[EG_SITES];
+#pragma unroll
+      for (int k = 0; k < EG_SITES; ++k) {
+        code[k] = 0;
+        nrm[k] = 0.f;
+        const int site = s0 + k;
+        if (!valid || site >= G.n_sites) continue;
+        const CqMat& T = tables[site];
+        code[k] = cq_quad_codes(T.seg[0].packed + trow * T.row_bytes, T.bits, 0, lane);
+        nrm[k] = __half2float(T.seg[0].norms[trow * T.groups]);
+      }
+#pragma unroll
+      for (int k = 0; k < EG_SITES; ++k) {
+        const int site = s0 + k;
+        if (site >= G.n_sites) break;
+        const int bits = tables[site].bits, mask = (1 << bits) - 1;
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) v[i] = valid ? lev[site][(code[k] >> (i * bits)) & mask] * nrm[k] : 0.f;
+        float* out = fetched + ((size_t)r * G.n_sites + site) * G.d;
+        reinterpret_cast<float4*>(out + t * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+      }
+    }
   }
 }
 
 cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBatch& rb,
                                  float* fetched, cudaStream_t st) {
   if (rb.M <= 0 || G.n_sites == 0) return cudaSuccess;
-  dim3 grid(rb.M, G.n_sites);
-  return launch_pdl(engram_gather_kernel, grid, dim3(256), 0, st, G, tables, rb, fetched);
+  if (G.n_sites > 16) return cudaErrorInvalidValue;
+  const int warps = std::min(8, std::max(1, G.e_tables));
+  return launch_pdl(engram_gather_kernel, dim3(rb.M), dim3(warps * 32), 0, st, G, tables, rb, fetched);
 }
 
 // value_conv (engram.rs:89-106) / engram_conv_step (cache.rs:444-479): dilated
@@ -134,7 +162,7 @@ struct EngTaps {
 
 // One CTA per row covering every site, four channels per thread-step (the
 // row descriptor and the session's tail pointer are read once per row).
-__global__ void engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float* __restrict__ ekv,
+__global__ void __launch_bounds__(256, 5) engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float* __restrict__ ekv,
                                    float* __restrict__ evc) {
   pdl_wait();
   pdl_trigger();
@@ -147,7 +175,12 @@ __global__ void engram_conv_kernel(Geo G, EngTaps taps, RowBatch rb, const float
   const float* row_kv = ekv + (size_t)r * kv_ld;
   for (int i = threadIdx.x; i < G.n_sites * d4; i += blockDim.x) {
     const int site = i / d4, c = (i % d4) * 4;
-    const float* tp = taps.t[site];
+    // Selected by compares, not indexed: a dynamic index into the parameter
+    // array would copy it to local memory in every thread.
+    const float* tp = taps.t[0];
+#pragma unroll
+    for (int k = 1; k < 16; ++k)
+      if (k == site) tp = taps.t[k];
     const float4 raw = *reinterpret_cast<const float4*>(row_kv + (size_t)site * 2 * d + d + c);
     float* tail = tails + (size_t)site * reach * d;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -1061,11 +1094,6 @@ __device__ __forceinline__ float qkv_conv_chan(const Geo& G, int li, const RowBa
   return acc;
 }
 
-// Task t of row r held by one warp: q head t (t < heads) or k head t - heads
-// (norm + RoPE, attention.rs:107-143; int8 query fake-quant, model.rs:289-293)
-// or v head t - heads - kvh, then the stores (quantize-on-append in int8
-// mode, cache.rs:346-377). x1, x2: the lane's two conv outputs, channels
-// qkv_task_chan gives (0 on lanes past the head's half).
 // What every task of one row needs, read once per row: the layer's KV ring,
 // the RoPE row of the position and where the new K/V go.
 struct QkvRowCtx {
@@ -1089,125 +1117,105 @@ __device__ __forceinline__ QkvRowCtx qkv_row_ctx(const Geo& G, int li, const Row
   return c;
 }
 
+// Stores of task t of row r. x1, x2: the lane's two values after norm and
+// RoPE (q, k) or the conv (v); in int8 mode c1, c2 are their codes and
+// `scale` the head's scale (kv_quant_codes), and a q head stores the
+// fake-quantised code * scale plus, for the integer score path of the int8
+// attention, the codes and scale in q8out / q8s. Value codes are stored
+// offset-binary (code ^ 0x80, the byte of code + 128): the attention widens
+// them to f16 without a sign flip per byte, and the KV read-back flips them.
+__device__ __forceinline__ void qkv_task_store(const Geo& G, float* __restrict__ qpost, void* pk, void* pv,
+                                               float* pks, float* pvs, int8_t* __restrict__ q8out,
+                                               float* __restrict__ q8s, int r, const QkvRowCtx& ctx, int t,
+                                               float x1, float x2, float c1, float c2, float scale) {
+  const int lane = threadIdx.x & 31;
+  const int qd = G.q_dim;
+  const bool int8 = ctx.int8, prefill = ctx.prefill, to_ring = ctx.to_ring;
+  const LayerKV& kv = ctx.kv;
+  const int slot = ctx.slot;
+  if (t < G.heads) {
+    const int h = t, half = G.qk / 2;
+    if (int8) {
+      if (q8out && lane < half) {
+        q8out[(size_t)r * qd + h * G.qk + lane] = (int8_t)c1;
+        q8out[(size_t)r * qd + h * G.qk + half + lane] = (int8_t)c2;
+      }
+      if (q8out && lane == 0) q8s[(size_t)r * G.heads + h] = scale;
+      x1 = c1 * scale;
+      x2 = c2 * scale;
+    }
+    if (lane < half) {
+      qpost[(size_t)r * qd + h * G.qk + lane] = x1;
+      qpost[(size_t)r * qd + h * G.qk + half + lane] = x2;
+    }
+    return;
+  }
+  const bool isk = t < G.heads + G.kvh;
+  const int h = isk ? t - G.heads : t - G.heads - G.kvh;
+  const int dim = isk ? G.qk : G.vh, hf = dim / 2;
+  void* const scratch = isk ? pk : pv;
+  void* const ring = isk ? kv.k : kv.v;
+  if (int8) {
+    const int x = isk ? 0 : 0x80;
+    const int8_t a = (int8_t)((int)c1 ^ x), b = (int8_t)((int)c2 ^ x);
+    if (lane < hf) {
+      if (prefill) {
+        int8_t* d8 = (int8_t*)scratch + ((size_t)r * G.kvh + h) * dim;
+        d8[lane] = a;
+        d8[hf + lane] = b;
+      }
+      if (to_ring) {
+        int8_t* d8 = (int8_t*)ring + ((size_t)h * kv.slots + slot) * dim;
+        d8[lane] = a;
+        d8[hf + lane] = b;
+      }
+    }
+    if (lane == 0) {
+      if (prefill) (isk ? pks : pvs)[(size_t)r * G.kvh + h] = scale;
+      if (to_ring) (isk ? kv.ks : kv.vs)[(size_t)h * kv.slots + slot] = scale;
+    }
+  } else if (lane < hf) {
+    if (prefill) {
+      float* df = (float*)scratch + ((size_t)r * G.kvh + h) * dim;
+      df[lane] = x1;
+      df[hf + lane] = x2;
+    }
+    if (to_ring) {
+      float* df = (float*)ring + ((size_t)h * kv.slots + slot) * dim;
+      df[lane] = x1;
+      df[hf + lane] = x2;
+    }
+  }
+}
+
+// Task t of row r held by one warp: q head t (t < heads) or k head t - heads
+// (norm + RoPE, attention.rs:107-143; int8 query fake-quant, model.rs:289-293)
+// or v head t - heads - kvh, then the stores (quantize-on-append in int8
+// mode, cache.rs:346-377). x1, x2: the lane's two conv outputs, channels
+// qkv_task_chan gives (0 on lanes past the head's half).
 __device__ __forceinline__ void qkv_task(const Geo& G, const LayerParams& lp, float* __restrict__ qpost, void* pk,
                                          void* pv, float* pks, float* pvs, int8_t* __restrict__ q8out,
                                          float* __restrict__ q8s, int r, const QkvRowCtx& ctx, int t, float x1,
                                          float x2) {
   const int lane = threadIdx.x & 31;
-  const int qd = G.q_dim;
-  const int half = G.qk / 2;
-  const float* cs = ctx.cs;
-  const float* sn = ctx.sn;
-  const bool int8 = ctx.int8;
-  const bool prefill = ctx.prefill;
-  const LayerKV& kv = ctx.kv;
-  const int slot = ctx.slot;
-  const bool to_ring = ctx.to_ring;
   if (t < G.heads + G.kvh) {
-    // q head t, or k head t-heads: norm + rope.
     const bool isq = t < G.heads;
-    const int h = isq ? t : t - G.heads;
+    const int half = G.qk / 2;
     const float* sc = isq ? lp.q_norm : lp.k_norm;
     float sq = warp_sum(x1 * x1 + x2 * x2);
     float rms = sqrtf(sq / (float)G.qk + 1e-6f);
     if (lane < half) {
       x1 = (1.0f + sc[lane]) * x1 / rms;
       x2 = (1.0f + sc[half + lane]) * x2 / rms;
-      float c = cs[lane], s = sn[lane];
+      float c = ctx.cs[lane], s = ctx.sn[lane];
       float y1 = x1 * c - x2 * s, y2 = x2 * c + x1 * s;
       x1 = y1;
       x2 = y2;
     }
-    if (isq) {
-      if (int8) {
-        // The codes and scale also go to q8out / q8s for the integer score
-        // path of the int8 attention; code * scale is the fake-quantised query.
-        float c1, c2;
-        const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-        if (q8out && lane < half) {
-          q8out[(size_t)r * qd + h * G.qk + lane] = (int8_t)c1;
-          q8out[(size_t)r * qd + h * G.qk + half + lane] = (int8_t)c2;
-        }
-        if (q8out && lane == 0) q8s[(size_t)r * G.heads + h] = scale;
-        x1 = c1 * scale;
-        x2 = c2 * scale;
-      }
-      if (lane < half) {
-        qpost[(size_t)r * qd + h * G.qk + lane] = x1;
-        qpost[(size_t)r * qd + h * G.qk + half + lane] = x2;
-      }
-    } else if (int8) {
-      float c1, c2;
-      const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-      const int8_t a = (int8_t)c1, b = (int8_t)c2;
-      if (lane < half) {
-        if (prefill) {
-          int8_t* d8 = (int8_t*)pk + ((size_t)r * G.kvh + h) * G.qk;
-          d8[lane] = a;
-          d8[half + lane] = b;
-        }
-        if (to_ring) {
-          int8_t* d8 = (int8_t*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
-          d8[lane] = a;
-          d8[half + lane] = b;
-        }
-      }
-      if (lane == 0) {
-        if (prefill) pks[(size_t)r * G.kvh + h] = scale;
-        if (to_ring) kv.ks[(size_t)h * kv.slots + slot] = scale;
-      }
-    } else if (lane < half) {
-      if (prefill) {
-        float* df = (float*)pk + ((size_t)r * G.kvh + h) * G.qk;
-        df[lane] = x1;
-        df[half + lane] = x2;
-      }
-      if (to_ring) {
-        float* df = (float*)kv.k + ((size_t)h * kv.slots + slot) * G.qk;
-        df[lane] = x1;
-        df[half + lane] = x2;
-      }
-    }
-  } else {
-    // v head: conv output only, then store (quantised in int8 mode). Value
-    // codes are stored offset-binary (code ^ 0x80, the byte of code + 128):
-    // the attention widens them to f16 without a sign flip per byte, and the
-    // KV read-back flips them back.
-    const int h = t - G.heads - G.kvh;
-    const int vhalf = G.vh / 2;
-    if (int8) {
-      float c1, c2;
-      const float scale = kv_quant_warp(x1, x2, &c1, &c2);
-      const int8_t a = (int8_t)((int)c1 ^ 0x80), b = (int8_t)((int)c2 ^ 0x80);
-      if (lane < vhalf) {
-        if (prefill) {
-          int8_t* d8 = (int8_t*)pv + ((size_t)r * G.kvh + h) * G.vh;
-          d8[lane] = a;
-          d8[vhalf + lane] = b;
-        }
-        if (to_ring) {
-          int8_t* d8 = (int8_t*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
-          d8[lane] = a;
-          d8[vhalf + lane] = b;
-        }
-      }
-      if (lane == 0) {
-        if (prefill) pvs[(size_t)r * G.kvh + h] = scale;
-        if (to_ring) kv.vs[(size_t)h * kv.slots + slot] = scale;
-      }
-    } else if (lane < vhalf) {
-      if (prefill) {
-        float* df = (float*)pv + ((size_t)r * G.kvh + h) * G.vh;
-        df[lane] = x1;
-        df[vhalf + lane] = x2;
-      }
-      if (to_ring) {
-        float* df = (float*)kv.v + ((size_t)h * kv.slots + slot) * G.vh;
-        df[lane] = x1;
-        df[vhalf + lane] = x2;
-      }
-    }
   }
+  float c1 = 0.f, c2 = 0.f, scale = 1.f;
+  if (ctx.int8) scale = kv_quant_warp(x1, x2, &c1, &c2);
+  qkv_task_store(G, qpost, pk, pv, pks, pvs, q8out, q8s, r, ctx, t, x1, x2, c1, c2, scale);
 }
 
 // The two channels (of the q|k|v conv output) lane `lane` holds in task t, or
@@ -1226,13 +1234,13 @@ __device__ __forceinline__ bool qkv_task_chan(const Geo& G, int t, int lane, int
   return lane < hf;
 }
 
-template <bool WARP>
+// One row over the CTA: the conv into `sm` ([qkv_dim] floats), then the heads
+// over the warps.
 __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatch& rb, const LayerParams& lp,
                                              const float* __restrict__ rope_cs, const float* __restrict__ proj,
                                              float* __restrict__ qpost, void* pk, void* pv, float* pks, float* pvs,
                                              int8_t* __restrict__ q8out, float* __restrict__ q8s, int r, float* sm) {
-  const int tix = WARP ? (int)(threadIdx.x & 31) : (int)threadIdx.x;
-  const int nthr = WARP ? 32 : (int)blockDim.x;
+  const int tix = threadIdx.x, nthr = blockDim.x;
   const RowInfo ri = rb.rows[r];
   const int p = ri.pos;
   const int qd = G.q_dim, kd = G.k_dim, vd = G.v_dim, qkv = G.qkv_dim;
@@ -1280,11 +1288,8 @@ __device__ __forceinline__ void qkv_post_row(const Geo& G, int li, const RowBatc
 #pragma unroll 4
     for (int c = tix; c < qkv; c += nthr) sm[c] = qkv_conv_chan(G, li, rb, lp, ri, proj, r, c);
   }
-  if (WARP)
-    __syncwarp();
-  else
-    __syncthreads();
-  const int lane = threadIdx.x & 31, wid = WARP ? 0 : (int)(threadIdx.x >> 5), nw = WARP ? 1 : (int)(blockDim.x >> 5);
+  __syncthreads();
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
   const int ntask = G.heads + 2 * G.kvh;
   const QkvRowCtx ctx = qkv_row_ctx(G, li, rb, ri, rope_cs);
   for (int t = wid; t < ntask; t += nw) {
@@ -1300,24 +1305,121 @@ __global__ void qkv_post_kernel(Geo G, int li, RowBatch rb, LayerParams lp, cons
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) float sm[];
-  qkv_post_row<false>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, blockIdx.x, sm);
+  qkv_post_row(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, blockIdx.x, sm);
 }
 
 // Large batches: one warp per row, QP_ROWS rows per CTA, each warp with its
-// own qkv_dim-float slice of shared memory.
-// Seven rows: 4096 rows make 586 CTAs, four resident on each of the 148 SMs.
+// own qkv_dim-float slice of shared memory for the conv output. The RoPE row
+// and the norm scales are read once per row, and the heads run QP_CHUNK at a
+// time with their reductions interleaved (each head's sums in the order
+// qkv_task uses, so the results are the same). Needs q_dim, k_dim and v_dim
+// multiples of 4. Seven rows: 4096 rows make 586 CTAs, four resident on each
+// of the 148 SMs.
 constexpr int QP_ROWS = 7;
-__global__ void __launch_bounds__(QP_ROWS * 32)
+constexpr int QP_CHUNK = 4;
+__global__ void __launch_bounds__(QP_ROWS * 32, 4)
 qkv_post_rows_kernel(Geo G, int li, RowBatch rb, LayerParams lp, const float* __restrict__ rope_cs,
                      const float* __restrict__ proj, float* __restrict__ qpost, void* pk, void* pv, float* pks,
                      float* pvs, int8_t* __restrict__ q8out, float* __restrict__ q8s) {
   pdl_wait();
   pdl_trigger();
   extern __shared__ __align__(16) float sm[];
-  const int w = threadIdx.x >> 5, r = blockIdx.x * QP_ROWS + w;
+  const int w = threadIdx.x >> 5, lane = threadIdx.x & 31, r = blockIdx.x * QP_ROWS + w;
   if (r >= rb.M) return;
-  const int stride = (G.qkv_dim + 3) / 4 * 4;
-  qkv_post_row<true>(G, li, rb, lp, rope_cs, proj, qpost, pk, pv, pks, pvs, q8out, q8s, r, sm + (size_t)w * stride);
+  const int qd = G.q_dim, kd = G.k_dim, qkv = G.qkv_dim;
+  float* const xs = sm + (size_t)w * ((qkv + 3) / 4 * 4);
+  const RowInfo ri = rb.rows[r];
+  const int p = ri.pos;
+  const int taps = G.taps, tl = taps > 0 ? taps - 1 : 0;
+  const float* raw = proj + (size_t)r * G.proj_dim;
+  float* tail = tl ? ri.s->qkv_tail + (size_t)li * tl * qkv : nullptr;
+  // Conv (the arithmetic of qkv_post_row).
+  for (int c = 4 * lane; c < qkv; c += 128) {
+    const float* tp;
+    int dim, cc;
+    if (c < qd) {
+      tp = lp.q_taps; dim = qd; cc = c;
+    } else if (c < qd + kd) {
+      tp = lp.k_taps; dim = kd; cc = c - qd;
+    } else {
+      tp = lp.v_taps; dim = G.v_dim; cc = c - qd - kd;
+    }
+    const float4 x = *reinterpret_cast<const float4*>(raw + c);
+    float4 acc = x;
+    if (taps > 0) {
+      const float4 t0 = *reinterpret_cast<const float4*>(tp + cc);
+      acc = make_float4(t0.x * x.x, t0.y * x.y, t0.z * x.z, t0.w * x.w);
+#pragma unroll
+      for (int j = 1; j < MAX_QKV_TAPS; ++j) {
+        if (j >= taps || j > p) continue;
+        const float4 pv4 = *reinterpret_cast<const float4*>(
+            rb.mode == MODE_PREFILL ? proj + (size_t)(r - j) * G.proj_dim + c : tail + (size_t)((p - j) % tl) * qkv + c);
+        const float4 tj = *reinterpret_cast<const float4*>(tp + j * dim + cc);
+        acc.x += tj.x * pv4.x;
+        acc.y += tj.y * pv4.y;
+        acc.z += tj.z * pv4.z;
+        acc.w += tj.w * pv4.w;
+      }
+      if (tl && (rb.mode == MODE_DECODE || p >= ri.len - tl))
+        *reinterpret_cast<float4*>(tail + (size_t)(p % tl) * qkv + c) = x;
+    }
+    *reinterpret_cast<float4*>(xs + c) = acc;
+  }
+  __syncwarp();
+  const QkvRowCtx ctx = qkv_row_ctx(G, li, rb, ri, rope_cs);
+  const int half = G.qk / 2;
+  float qn1 = 0.f, qn2 = 0.f, kn1 = 0.f, kn2 = 0.f, rc = 0.f, rs = 0.f;
+  if (lane < half) {
+    qn1 = lp.q_norm[lane];
+    qn2 = lp.q_norm[half + lane];
+    kn1 = lp.k_norm[lane];
+    kn2 = lp.k_norm[half + lane];
+    rc = ctx.cs[lane];
+    rs = ctx.sn[lane];
+  }
+  const int ntask = G.heads + 2 * G.kvh, nqk = G.heads + G.kvh;
+  for (int t0 = 0; t0 < ntask; t0 += QP_CHUNK) {
+    float x1[QP_CHUNK], x2[QP_CHUNK], sq[QP_CHUNK];
+#pragma unroll
+    for (int k = 0; k < QP_CHUNK; ++k) {
+      int c1, c2;
+      const bool on = t0 + k < ntask && qkv_task_chan(G, t0 + k, lane, &c1, &c2);
+      x1[k] = on ? xs[c1] : 0.f;
+      x2[k] = on ? xs[c2] : 0.f;
+      sq[k] = x1[k] * x1[k] + x2[k] * x2[k];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1)
+#pragma unroll
+      for (int k = 0; k < QP_CHUNK; ++k) sq[k] += __shfl_xor_sync(0xffffffffu, sq[k], o);
+#pragma unroll
+    for (int k = 0; k < QP_CHUNK; ++k) {
+      const int t = t0 + k;
+      if (t < nqk && lane < half) {  // q or k head: norm + RoPE
+        const bool isq = t < G.heads;
+        const float rms = sqrtf(sq[k] / (float)G.qk + 1e-6f);
+        const float a = (1.0f + (isq ? qn1 : kn1)) * x1[k] / rms;
+        const float b = (1.0f + (isq ? qn2 : kn2)) * x2[k] / rms;
+        x1[k] = a * rc - b * rs;
+        x2[k] = b * rc + a * rs;
+      }
+    }
+    float c1[QP_CHUNK], c2[QP_CHUNK], scale[QP_CHUNK];
+    if (ctx.int8) {
+      float am[QP_CHUNK];
+#pragma unroll
+      for (int k = 0; k < QP_CHUNK; ++k) am[k] = kv_quant_absmax_warp(x1[k], x2[k]);
+#pragma unroll
+      for (int k = 0; k < QP_CHUNK; ++k) scale[k] = kv_quant_codes(am[k], x1[k], x2[k], &c1[k], &c2[k]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < QP_CHUNK; ++k) c1[k] = c2[k] = 0.f, scale[k] = 1.f;
+    }
+#pragma unroll
+    for (int k = 0; k < QP_CHUNK; ++k)
+      if (t0 + k < ntask)
+        qkv_task_store(G, qpost, pk, pv, pks, pvs, q8out, q8s, r, ctx, t0 + k, x1[k], x2[k], c1[k], c2[k], scale[k]);
+  }
 }
 
 // Small batches: one warp per task (q, k or v head) of a row, QH_TASKS tasks
@@ -1348,7 +1450,8 @@ cudaError_t launch_qkv_post(const Geo& G, int li, const RowBatch& rb, const Laye
                             void* pv, float* pks, float* pvs, int8_t* q8out, float* q8s, cudaStream_t st) {
   if (rb.M <= 0) return cudaSuccess;
   if (G.qk > 64 || G.vh > 64 || (G.qk & 1) || (G.vh & 1)) return cudaErrorInvalidValue;
-  if (rb.M >= 2048) {  // enough rows that the per-row head loop of one warp overlaps across warps
+  const bool rows_ok = (G.q_dim | G.k_dim | G.v_dim) % 4 == 0 && G.taps <= MAX_QKV_TAPS;
+  if (rb.M >= 2048 && rows_ok) {  // enough rows to fill the SMs with one warp per row
     const size_t smem = (size_t)QP_ROWS * ((G.qkv_dim + 3) / 4 * 4) * sizeof(float);
     cudaError_t e = allow_smem((const void*)qkv_post_rows_kernel, smem);
     if (e != cudaSuccess) return e;
