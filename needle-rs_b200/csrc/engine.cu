@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <cstdint>
 #include <cmath>
 #include <cstring>
 
@@ -57,13 +58,15 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
-  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, whi, wlo, cnt, oh, projo, gates, fetched, ekv, evc, lm_in,
-                pks, pvs, pk, pv, rows, tokens, next, last_rows, pre_part, pre_cnt};
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, ehi, elo, einv, whi, wlo, cnt, oh, projo, gates,
+                fetched, ekv, evc, lm_in, pks, pvs, pk, pv, rows, tokens, next, last_rows, pre_part, pre_cnt};
   for (void* p : ps)
     if (p) cudaFree(p);
   if (logits) cudaFree(logits);
   if (part) cudaFree(part);
   if (lm_last) cudaFree(lm_last);
+  for (void* h : {(void*)h_rows, (void*)h_tok, (void*)h_pick})
+    if (h) cudaFreeHost(h);
   *this = Workspace();
 }
 
@@ -87,6 +90,8 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
       {(void**)&w.q8s, cap * G.heads * 4},         {(void**)&w.q8, cap * G.q_dim},
       {(void**)&w.ahi, cap * kmax * 2},            {(void**)&w.alo, cap * kmax * 2},
       {(void**)&w.ainv, cap * 32 * 4},                  {(void**)&w.cnt, cap * G.kvh * 4},
+      {(void**)&w.ehi, cap * S * dpad * 2},        {(void**)&w.elo, cap * S * dpad * 2},
+      {(void**)&w.einv, cap * S * (dpad / 128) * 4},
       {(void**)&w.whi, wmax * kmax * 2},           {(void**)&w.wlo, wmax * kmax * 2},
       {(void**)&w.oh, cap * opad * 4},
       {(void**)&w.projo, cap * d * 4},             {(void**)&w.gates, cap * 24 * 4},
@@ -103,6 +108,16 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
     if (e != cudaSuccess) {
       w.release();
       *err = cuda_msg("workspace allocation", e);
+      return false;
+    }
+  }
+  {
+    cudaError_t e = cudaMallocHost((void**)&w.h_rows, cap * sizeof(RowInfo));
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&w.h_tok, cap * 4);
+    if (e == cudaSuccess) e = cudaMallocHost((void**)&w.h_pick, cap * 4);
+    if (e != cudaSuccess) {
+      w.release();
+      *err = cuda_msg("pinned staging allocation", e);
       return false;
     }
   }
@@ -1082,6 +1097,7 @@ Session* Engine::new_session(size_t hint, bool int8, std::string* err) {
 // window wraps instead. Old contents are kept: while a ring is below its cap
 // the slot of position p is p itself.
 bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
+  if (pos < s->grow_at) return true;
   bool changed = false;
   const size_t eb = kv_elem_bytes(s);
   for (size_t l = 0; l < cfg.layers; ++l) {
@@ -1124,6 +1140,10 @@ bool Engine::ensure_slots(Session* s, size_t pos, std::string* err) {
     }
     epoch++;
   }
+  size_t next = SIZE_MAX;
+  for (size_t l = 0; l < cfg.layers; ++l)
+    if (s->layers[l].slots < s->layers[l].cap) next = std::min(next, (size_t)s->layers[l].slots);
+  s->grow_at = next;
   return true;
 }
 
@@ -1195,12 +1215,23 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
   const int M = rb.M, d = G.d, S = G.n_sites;
   const int dpad = (d + 127) / 128 * 128, opad = (G.o_dim + 127) / 128 * 128;
   if (S > 0) {
-    NB_TRY(launch_engram_gather(G, d_tables, rb, w.fetched, st));
-    for (int s = 0; s < S; ++s)
-      NB_TRY(cq_project(eng_kv[s], w.fetched + (size_t)s * d, S * d, M, w.ekv + (size_t)s * 2 * d,
-                        S * 2 * d, 0, 2 * d, st, 0, &w.gs));
+    // On the tensor cores the gather writes every site's projection operands
+    // in the split form, so each projection is a single launch.
+    bool pre = d == dpad;
+    for (int s = 0; s < S; ++s) pre = pre && cq_umma_takes(eng_kv[s], M, &w.gs);
+    NB_TRY(launch_engram_gather(G, d_tables, rb, w.fetched, st, pre ? SplitOut{w.ehi, w.elo, w.einv} : SplitOut{}));
+    for (int s = 0; s < S; ++s) {
+      GemmScratch gs = w.gs;
+      if (pre) {
+        gs.hi = w.ehi + (size_t)s * M * d;
+        gs.lo = w.elo + (size_t)s * M * d;
+        gs.inv = w.einv + (size_t)s * M * (d / 128);
+      }
+      NB_TRY(cq_project(eng_kv[s], w.fetched + (size_t)s * d, S * d, M, w.ekv + (size_t)s * 2 * d, S * 2 * d, 0,
+                        2 * d, st, 0, &gs, pre));
+    }
     NB_TRY(launch_engram_conv(G, eng_taps.data(), rb, w.ekv, w.evc, st));
-    NB_MARK(PK_ENGRAM, S * cq_launches(eng_kv[0], M, &w.gs) + 2);
+    NB_MARK(PK_ENGRAM, S * cq_launches(eng_kv[0], M, &w.gs, 0, pre) + 2);
   }
   NB_TRY(launch_embed(G, emb, rb, w.lanes, st));
   if (w.cells) NB_TRY(launch_lane_mean(w.lanes, M, G.lanes, d, true, w.cells, st));
@@ -1434,11 +1465,13 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   for (size_t i = 0; i < n; ++i) maxpos = std::max(maxpos, ss[i]->pos);
   const int ns = attn_nsplit((int)n, G.kvh, (int)maxpos + 1);
   if (!ensure_ws(ws, n, err) || !ensure_logits(this, ws, n, err) || !ensure_part(ws, n, ns, err)) return false;
-  std::vector<RowInfo> ri(n);
-  for (size_t i = 0; i < n; ++i) ri[i] = RowInfo{ss[i]->d_desc, (int)ss[i]->pos, -1, -1, 0};
+  // The stream is idle here (every call ends synchronised), so the pinned
+  // staging buffers are free to refill.
+  for (size_t i = 0; i < n; ++i) ws.h_rows[i] = RowInfo{ss[i]->d_desc, (int)ss[i]->pos, -1, -1, 0};
+  std::memcpy(ws.h_tok, tokens, n * 4);
   const int dpad = (G.d + 127) / 128 * 128;
-  cudaError_t e = cudaMemcpyAsync(ws.rows, ri.data(), n * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
-  if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, tokens, n * 4, cudaMemcpyHostToDevice, stream);
+  cudaError_t e = cudaMemcpyAsync(ws.rows, ws.h_rows, n * sizeof(RowInfo), cudaMemcpyHostToDevice, stream);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(ws.tokens, ws.h_tok, n * 4, cudaMemcpyHostToDevice, stream);
   RowBatch rb{ws.rows, ws.tokens, (int)n, MODE_DECODE};
   const int int8 = ss[0]->int8 ? 1 : 0;
   auto body = [&](cudaStream_t s) -> cudaError_t {
@@ -1487,7 +1520,7 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   }
   if (e == cudaSuccess && logits)
     e = cudaMemcpyAsync(logits, ws.logits, n * G.logit_rows * 4, cudaMemcpyDeviceToHost, stream);
-  if (e == cudaSuccess && picks) e = cudaMemcpyAsync(picks, ws.next, n * 4, cudaMemcpyDeviceToHost, stream);
+  if (e == cudaSuccess && picks) e = cudaMemcpyAsync(ws.h_pick, ws.next, n * 4, cudaMemcpyDeviceToHost, stream);
   if (e == cudaSuccess) e = queue_wait_flag(stream);
   if (e == cudaSuccess) e = cudaStreamSynchronize(stream);
   if (e == cudaSuccess) e = wait_status(stream);
@@ -1495,6 +1528,7 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
     *err = cuda_msg("decode step", e);
     return false;
   }
+  if (picks) std::memcpy(picks, ws.h_pick, n * 4);
   for (size_t i = 0; i < n; ++i) ss[i]->pos += 1;
   return true;
 }

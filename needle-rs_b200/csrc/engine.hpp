@@ -54,6 +54,10 @@ class Session {
   void* d_arena = nullptr;        // one allocation holding the initial rings, state and descriptors
   std::vector<char> owned;        // layer ring grown into its own allocation
   uint64_t seen = 0;              // the engine's batch-check stamp of the last call it was in
+  // The smallest position at which some layer's ring must grow (its slot count
+  // while below its cap); 0 until ensure_slots first computes it, so a step
+  // below it skips the per-layer check.
+  size_t grow_at = 0;
   size_t state_bytes = 0;
   size_t bytes() const;           // device bytes held, as V3Cache::bytes counts them
 };
@@ -69,6 +73,10 @@ struct Workspace {
   int8_t* q8 = nullptr;  // int8 mode: query codes [rows][heads][qk], scales in q8s [rows][heads]
   __half *ahi = nullptr, *alo = nullptr;  // tensor-core projections: split activations
   float* ainv = nullptr;                  // and their inverse group scales [rows][32]
+  // The Engram key|value projections' operands, written by the gather in the
+  // split form: [sites][rows][d_model] halves, scales [sites][rows][d_model / 128].
+  __half *ehi = nullptr, *elo = nullptr;
+  float* einv = nullptr;
   // The last forward wrote the LM head's input in the split form (not lm_in).
   bool head_presplit = false;
   __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
@@ -82,6 +90,11 @@ struct Workspace {
   float* cells = nullptr;  // when set, the forward writes the probe-head cells here [layers + 1][rows][d]
   float* part = nullptr;  // attention split partials
   size_t part_cap = 0;    // floats
+  // Pinned host staging of a host-API decode step ([cap] each): the rows and
+  // tokens go to the device and the picks come back by DMA, without the
+  // driver's pageable-memory staging.
+  RowInfo* h_rows = nullptr;
+  uint32_t *h_tok = nullptr, *h_pick = nullptr;
   void release();
 };
 

@@ -123,8 +123,12 @@ cudaError_t launch_cq_prepare(const float* x, int M, int in_feat, float* xh, int
 
 cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, float* lanes,
                          cudaStream_t st);
+// so: when set, the fetched rows go out only in the tensor-core operand form of
+// the Engram key|value projections, site s at so.hi / lo + s * M * d_model and
+// so.inv + s * M * (d_model / 128) (each a [M][d_model] split matrix), instead
+// of f32 into `fetched`.
 cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBatch& rb,
-                                 float* fetched, cudaStream_t st);
+                                 float* fetched, cudaStream_t st, SplitOut so = SplitOut{});
 cudaError_t launch_engram_conv(const Geo& G, const float* const* taps, const RowBatch& rb,
                                const float* ekv, float* evc, cudaStream_t st);
 // Rows up to which launch_layer_pre spreads each row over one CTA per 128-wide

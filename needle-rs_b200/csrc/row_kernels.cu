@@ -82,7 +82,7 @@ cudaError_t launch_embed(const Geo& G, const CqMat& emb, const RowBatch& rb, flo
 // sites' loads in flight together.
 constexpr int EG_SITES = 8;
 __global__ void __launch_bounds__(256) engram_gather_kernel(Geo G, const CqMat* __restrict__ tables, RowBatch rb,
-                                                            float* __restrict__ fetched) {
+                                                            float* __restrict__ fetched, SplitOut so) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   __shared__ float lev[16][16];
   for (int i = threadIdx.x; i < G.n_sites * 16; i += blockDim.x) lev[i >> 4][i & 15] = tables[i >> 4].levels[i & 15];
@@ -136,19 +136,24 @@ __global__ void __launch_bounds__(256) engram_gather_kernel(Geo G, const CqMat* 
         float v[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) v[i] = valid ? lev[site][(code[k] >> (i * bits)) & mask] * nrm[k] : 0.f;
-        float* out = fetched + ((size_t)r * G.n_sites + site) * G.d;
-        reinterpret_cast<float4*>(out + t * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+        if (so.hi) {  // table t is the 128-wide group t of the site's projection input
+          const size_t e0 = ((size_t)site * rb.M + r) * G.d + t * 128;
+          split_group_store(v, so.hi + e0, so.lo + e0, so.inv + ((size_t)site * rb.M + r) * (G.d / 128) + t);
+        } else {
+          float* out = fetched + ((size_t)r * G.n_sites + site) * G.d;
+          reinterpret_cast<float4*>(out + t * 128)[lane] = make_float4(v[0], v[1], v[2], v[3]);
+        }
       }
     }
   }
 }
 
 cudaError_t launch_engram_gather(const Geo& G, const CqMat* tables, const RowBatch& rb,
-                                 float* fetched, cudaStream_t st) {
+                                 float* fetched, cudaStream_t st, SplitOut so) {
   if (rb.M <= 0 || G.n_sites == 0) return cudaSuccess;
   if (G.n_sites > 16) return cudaErrorInvalidValue;
   const int warps = std::min(8, std::max(1, G.e_tables));
-  return launch_pdl(engram_gather_kernel, dim3(rb.M), dim3(warps * 32), 0, st, G, tables, rb, fetched);
+  return launch_pdl(engram_gather_kernel, dim3(rb.M), dim3(warps * 32), 0, st, G, tables, rb, fetched, so);
 }
 
 // value_conv (engram.rs:89-106) / engram_conv_step (cache.rs:444-479): dilated
