@@ -469,9 +469,8 @@ def kernel_configs(nb, torch, raw, hbm, bf16):
 
 # DRAM bytes per (position, KV head) of one int8 decode-attention launch,
 # measured by ncu (dram__bytes_read.sum + dram__bytes_write.sum = 261.65 MB of
-# one launch over 1024 sessions x 1024 positions x 2 KV heads, the capture
-# recorded in profiles/decode_attention_int8.md). Scaled by the units of the
-# bench's own launch to report roofline.traffic.
+# one captured launch over 1024 sessions x 1024 positions x 2 KV heads).
+# Scaled by the units of the bench's own launch to report roofline.traffic.
 ATTN_TRAFFIC_PER_UNIT = 124.8
 
 
