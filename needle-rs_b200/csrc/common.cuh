@@ -229,6 +229,21 @@ __device__ __forceinline__ void split_group_store(const float (&x)[4], __half* h
   if (lane == 0) *inv = __uint_as_float((uint32_t)(127 - e) << 23);
 }
 
+// Greedy-pick key of output column `col` holding v (not a NaN): larger for a
+// larger value and, among equal values, for a lower column, so the maximum key
+// of a row is its first maximum, as argmax keeps it (v3_engine.rs:410-420);
+// -0 counts as +0, as the comparison does. Never 0, which stands for a row
+// whose outputs are all NaN (pick 0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, uint32_t col) {
+  uint32_t b = __float_as_uint(v);
+  if (b == 0x80000000u) b = 0u;
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+  return ((unsigned long long)b << 32) | (0xffffffffu - col);
+}
+__host__ __device__ __forceinline__ uint32_t argmax_pick(unsigned long long key) {
+  return key ? 0xffffffffu - (uint32_t)key : 0u;
+}
+
 // cp.async copies global -> shared (src-size 0 when !valid: zero-fill, nothing read).
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem, bool valid) {
   unsigned s = (unsigned)__cvta_generic_to_shared(smem);

@@ -974,6 +974,7 @@ cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y
   if (!cq_args_ok(W, xh, ldx) || row0 < 0 || row0 + nrows > W.rows) return cudaErrorInvalidValue;
   if ((force_path == 1 || force_path >= 4) && M > 8) return cudaErrorInvalidValue;
   if (force_path < 0 || force_path > 5) return cudaErrorInvalidValue;
+  if (force_path >= 4 && gs && gs->amax) return cudaErrorInvalidValue;
   if (force_path >= 4)  // one GEMV kernel by name: 4 the SIMT kernels, 5 the tensor-core GEMV
     return W.bits == 2 ? project_bits<2>(W, xh, ldx, M, y, ldy, row0, nrows, st, force_path - 3)
                        : project_bits<4>(W, xh, ldx, M, y, ldy, row0, nrows, st, force_path - 3);
@@ -984,7 +985,9 @@ cudaError_t cq_project(const CqMat& W, const float* xh, int ldx, int M, float* y
   }
   if (force_path == 0 && M > 8 && scratch_ok && umma_supported(W))
     return cq_project_umma(W, xh, ldx, M, y, ldy, row0, nrows, st, *gs, presplit);
-  if (presplit) return cudaErrorInvalidValue;  // the input exists only in the split form
+  // The input exists only in the split form, or the caller wants the greedy
+  // pick, which only the tensor-core path computes.
+  if (presplit || (gs && gs->amax)) return cudaErrorInvalidValue;
   if (force_path == 2)
     return W.bits == 2 ? launch_gemm_simt<2>(W, xh, ldx, M, y, ldy, row0, nrows, st)
                        : launch_gemm_simt<4>(W, xh, ldx, M, y, ldy, row0, nrows, st);

@@ -58,7 +58,7 @@ size_t HostConfig::kv_bytes_at(size_t seq_len, bool int8) const {
 
 // ------------------------------------------------------------------ workspace
 void Workspace::release() {
-  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, ehi, elo, einv, whi, wlo, cnt, oh, projo, gates,
+  void* ps[] = {lanes, u, bx, xh, proj, qpost, q8s, q8, ahi, alo, ainv, ehi, elo, einv, whi, wlo, cnt, keys, oh, projo, gates,
                 fetched, ekv, evc, lm_in, pks, pvs, pk, pv, rows, tokens, next, last_rows, pre_part, pre_cnt};
   for (void* p : ps)
     if (p) cudaFree(p);
@@ -91,7 +91,7 @@ bool Engine::ensure_ws(Workspace& w, size_t rows, std::string* err) {
       {(void**)&w.ahi, cap * kmax * 2},            {(void**)&w.alo, cap * kmax * 2},
       {(void**)&w.ainv, cap * 32 * 4},                  {(void**)&w.cnt, cap * G.kvh * 4},
       {(void**)&w.ehi, cap * S * dpad * 2},        {(void**)&w.elo, cap * S * dpad * 2},
-      {(void**)&w.einv, cap * S * (dpad / 128) * 4},
+      {(void**)&w.einv, cap * S * (dpad / 128) * 4}, {(void**)&w.keys, cap * 8},
       {(void**)&w.whi, wmax * kmax * 2},           {(void**)&w.wlo, wmax * kmax * 2},
       {(void**)&w.oh, cap * opad * 4},
       {(void**)&w.projo, cap * d * 4},             {(void**)&w.gates, cap * 24 * 4},
@@ -1264,7 +1264,7 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
     NB_MARK(PK_LAYER_POST, 1);
   }
   const SplitOut sh = split_head && cq_umma_takes(emb, M, &w.gs) ? to_gs : SplitOut{};
-  NB_TRY(launch_final(G, rb, w.lanes, final_norm, w.lm_in, st, sh));
+  NB_TRY(launch_final(G, rb, w.lanes, final_norm, w.lm_in, st, sh, sh.hi ? w.keys : nullptr));
   w.head_presplit = sh.hi != nullptr;
   NB_MARK(PK_FINAL, 1);
   return cudaSuccess;
@@ -1272,10 +1272,21 @@ cudaError_t Engine::forward(Workspace& w, const RowBatch& rb, cudaStream_t st, b
 
 // Tied head over logit_rows (model.rs:358-374, :942-978) and the greedy pick.
 cudaError_t Engine::head(Workspace& w, const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
-                         cudaStream_t st, Prof* prof) {
+                         cudaStream_t st, Prof* prof, bool need_logits) {
   // The last forward's final kernel may have written this input split (lm_in
   // itself then holds nothing).
   const bool presplit = lm_in == w.lm_in && w.head_presplit;
+  if (picks && !need_logits && presplit) {
+    // The split input means the tensor-core path, and the final kernel zeroed
+    // the rows' keys: the projection keeps each row's first maximum only.
+    GemmScratch gs = w.gs;
+    gs.amax = w.keys;
+    NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &gs, true));
+    NB_MARK(PK_HEAD, cq_launches(emb, M, &w.gs, 0, true));
+    NB_TRY(launch_argmax_keys(w.keys, M, picks, st));
+    NB_MARK(PK_BOOK, 1);
+    return cudaSuccess;
+  }
   NB_TRY(cq_project(emb, lm_in, ldx, M, logits, G.logit_rows, 0, G.logit_rows, st, 0, &w.gs, presplit));
   NB_MARK(PK_HEAD, cq_launches(emb, M, &w.gs, 0, presplit));
   if (picks) NB_TRY(launch_argmax(logits, M, G.logit_rows, G.logit_rows, picks, st));
@@ -1477,12 +1488,12 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
   auto body = [&](cudaStream_t s) -> cudaError_t {
     NB_TRY(forward(ws, rb, s, int8, ns, nullptr, true));
     NB_TRY(launch_step_end(rb, s));
-    return head(ws, ws.lm_in, dpad, (int)n, ws.logits, ws.next, s);
+    return head(ws, ws.lm_in, dpad, (int)n, ws.logits, ws.next, s, nullptr, logits != nullptr);
   };
   // Replay the captured step while its shapes and buffers are unchanged; a
   // new shape or epoch first runs one eager step (one-time set-up such as
   // shared-memory opt-ins happens outside any capture), then captures.
-  const bool same = dec_n == n && dec_ns == ns && dec_int8 == int8;
+  const bool same = dec_n == n && dec_ns == ns && dec_int8 == int8 && dec_logits == (logits ? 1 : 0);
   if (e == cudaSuccess) {
     if (dec_graph && same && dec_graph_epoch == epoch) {
       e = cudaGraphLaunch(dec_graph, stream);
@@ -1515,6 +1526,7 @@ bool Engine::decode(Session* const* ss, const uint32_t* tokens, size_t n, float*
       dec_n = n;
       dec_ns = ns;
       dec_int8 = int8;
+      dec_logits = logits ? 1 : 0;
       dec_warm_epoch = epoch;
     }
   }
@@ -1612,7 +1624,7 @@ bool Engine::decode_batch_device(Batch* b, float* d_logits, cudaStream_t st, boo
     NB_TRY(launch_step_begin(rb, b->d_sess, s));
     NB_TRY(forward(ws, rb, s, b->int8, ns, nullptr, true));
     NB_TRY(launch_step_end(rb, s));
-    NB_TRY(head(ws, ws.lm_in, dpad, (int)n, lg, b->d_next, s));
+    NB_TRY(head(ws, ws.lm_in, dpad, (int)n, lg, b->d_next, s, nullptr, d_logits != nullptr));
     return cudaSuccess;
   };
   cudaError_t e = cudaSuccess;
@@ -1681,7 +1693,7 @@ bool Engine::profile_batch_step(Batch* b, float* ms, int* launches, std::string*
     NB_TRY(forward(ws, rb, st, b->int8, ns, p, true));
     NB_TRY(launch_step_end(rb, st));
     NB_TRY(p->mark(PK_BOOK, st, 1));
-    NB_TRY(head(ws, ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p));
+    NB_TRY(head(ws, ws.lm_in, dpad, (int)n, ws.logits, b->d_next, st, p, false));
     return cudaStreamSynchronize(st);
   };
   cudaError_t e = run();

@@ -81,6 +81,7 @@ struct Workspace {
   bool head_presplit = false;
   __half *whi = nullptr, *wlo = nullptr;  // expanded levels of the projection being computed
   int* cnt = nullptr;  // attention split-arrival counters [rows][kv heads], zero between launches
+  unsigned long long* keys = nullptr;  // the LM head's greedy-pick keys [rows] (GemmScratch::amax)
   float* pre_part = nullptr;  // split mHC pre-projection partials [rows][32][32]
   int* pre_cnt = nullptr;     // and its per-row arrival counters, zero between launches
   GemmScratch gs;
@@ -201,7 +202,7 @@ class Engine {
   cudaGraphExec_t dec_graph = nullptr;
   uint64_t dec_graph_epoch = 0, dec_warm_epoch = 0;
   size_t dec_n = 0;
-  int dec_ns = 0, dec_int8 = -1;
+  int dec_ns = 0, dec_int8 = -1, dec_logits = -1;
   // This engine's own device flag, raised by its tensor-core GEMMs and int8
   // attention when a bounded wait expired; no other handle reads or clears it.
   int* d_wait_flag = nullptr;
@@ -222,8 +223,11 @@ class Engine {
   // kernel may write the head's tensor-core operands instead of lm_in.
   cudaError_t forward(Workspace& w, const RowBatch& rb, cudaStream_t st, bool int8, int nsplit,
                       Prof* prof = nullptr, bool split_head = false);
+  // need_logits false: only the picks are wanted, and a head on the
+  // tensor-core operands the final kernel wrote folds the greedy pick into the
+  // projection instead of storing [M][logit_rows] logits.
   cudaError_t head(Workspace& w, const float* lm_in, int ldx, int M, float* logits, uint32_t* picks,
-                   cudaStream_t st, Prof* prof = nullptr);
+                   cudaStream_t st, Prof* prof = nullptr, bool need_logits = true);
 };
 
 }  // namespace nb

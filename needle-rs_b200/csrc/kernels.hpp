@@ -84,6 +84,11 @@ struct GemmScratch {
   // Device flag the GEMM raises when one of its bounded waits gives up; null
   // for the library-wide flag that umma_take_error reads.
   int* werr = nullptr;
+  // Greedy pick instead of outputs (tensor-core path only): when set, the
+  // projection stores nothing and folds each row's outputs into amax[row] by
+  // atomicMax of argmax_key (the row's keys zeroed beforehand); the first
+  // maximum's column is then argmax_pick(amax[row]).
+  unsigned long long* amax = nullptr;
 };
 
 // force_path: 0 automatic (GEMV for M <= 8, else the tensor cores when `gs`
@@ -192,9 +197,15 @@ cudaError_t launch_probe_head(const float* cells, int seq, int d, const ProbeHea
 
 // so.hi non-null: the rotated head input goes to so (the LM head's
 // tensor-core operands, [M][dpad]) instead of lm_in.
+// keys: when set (with so), each row's greedy-pick key is zeroed for the LM
+// head's GemmScratch::amax.
 cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
-                         const float* final_norm, float* lm_in, cudaStream_t st, SplitOut so = SplitOut{});
+                         const float* final_norm, float* lm_in, cudaStream_t st, SplitOut so = SplitOut{},
+                         unsigned long long* keys = nullptr);
 cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st);
+// out[r] = argmax_pick(keys[r]) for the rows of a projection run with
+// GemmScratch::amax.
+cudaError_t launch_argmax_keys(const unsigned long long* keys, int M, uint32_t* out, cudaStream_t st);
 cudaError_t launch_step_begin(const RowBatch& rb, SessDesc* const* sess, cudaStream_t st);
 cudaError_t launch_step_end(const RowBatch& rb, cudaStream_t st);
 

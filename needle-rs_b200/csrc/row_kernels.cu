@@ -1665,9 +1665,10 @@ cudaError_t launch_layer_post(const Geo& G, int li, const RowBatch& rb, const La
 // ---------------------------------------------------------------- head
 // model.rs:358-374: lane mean, final ZCRMS norm, rotation for the tied head.
 __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float* __restrict__ fnorm,
-                             float* __restrict__ lm_in, SplitOut so) {
+                             float* __restrict__ lm_in, SplitOut so, unsigned long long* __restrict__ keys) {
   pdl_trigger();  // a PDL-launched projection after this kernel may start its weight prefetch
   pdl_wait();     // everything below reads or writes what earlier kernels touch
+  if (keys && threadIdx.x == 0) keys[blockIdx.x] = 0ull;  // the head's greedy pick starts empty
   extern __shared__ __align__(16) float sm[];
   float* red = sm;
   float* x = sm + 32;
@@ -1703,11 +1704,12 @@ __global__ void final_kernel(Geo G, const float* __restrict__ lanes, const float
 }
 
 cudaError_t launch_final(const Geo& G, const RowBatch& rb, const float* lanes,
-                         const float* final_norm, float* lm_in, cudaStream_t st, SplitOut so) {
+                         const float* final_norm, float* lm_in, cudaStream_t st, SplitOut so,
+                         unsigned long long* keys) {
   if (rb.M <= 0) return cudaSuccess;
   const int dpad = (G.d + 127) / 128 * 128;
   return launch_pdl(final_kernel, dim3(rb.M), dim3(256), (32 + dpad) * sizeof(float), st, G, lanes, final_norm,
-                    lm_in, so);
+                    lm_in, so, keys);
 }
 
 // Greedy pick: the first maximum, as argmax (v3_engine.rs:410-420) keeps the
@@ -1760,6 +1762,18 @@ __global__ void argmax_kernel(const float* __restrict__ logits, int n, int ld, u
 cudaError_t launch_argmax(const float* logits, int M, int n, int ld, uint32_t* out, cudaStream_t st) {
   if (M <= 0) return cudaSuccess;
   return launch_pdl(argmax_kernel, dim3(M), dim3(256), 0, st, logits, n, ld, out);
+}
+
+__global__ void argmax_keys_kernel(const unsigned long long* __restrict__ keys, int M, uint32_t* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x * blockDim.x + threadIdx.x;
+  if (r < M) out[r] = argmax_pick(keys[r]);
+}
+
+cudaError_t launch_argmax_keys(const unsigned long long* keys, int M, uint32_t* out, cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  return launch_pdl(argmax_keys_kernel, dim3((M + 255) / 256), dim3(256), 0, st, keys, M, out);
 }
 
 // ---------------------------------------------------------------- step bookkeeping

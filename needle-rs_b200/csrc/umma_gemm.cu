@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(Pipe<EXACT, UN>::THREADS, 1)
 cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_constant__ CUtensorMap mapAl,
                const __grid_constant__ CUtensorMap mapBh, const __grid_constant__ CUtensorMap mapBl,
                const float* __restrict__ ainv, float linv, int M, float* __restrict__ y, int ldy, int row0,
-               int nrows, int ntn, int ntiles, int* werr, int out_stage) {
+               int nrows, int ntn, int ntiles, int* werr, int out_stage, unsigned long long* __restrict__ amax) {
   pdl_trigger();  // the consumer of y may launch now; it waits for this grid before reading y
   using P = Pipe<EXACT, UN>;
   constexpr int USTAGES = P::STAGES;
@@ -321,7 +321,15 @@ cq_umma_kernel(CqMat W, const __grid_constant__ CUtensorMap mapAh, const __grid_
       // rows x 64 contiguous bytes instead of 32 rows x 16 bytes.
       const bool vec = out_stage && ok && m0 + q * 32 + 32 <= M && lim >= 64 && (ldy & 3) == 0 &&
                        (reinterpret_cast<uintptr_t>(y + n0 + cq * 64) & 15) == 0;
-      if (vec) {
+      if (amax) {  // greedy pick: the row's best key over this warp's columns
+        if (ok && m < M) {
+          unsigned long long best = 0ull;
+#pragma unroll
+          for (int i = 0; i < 64; ++i)
+            if (i < lim && acc[i] == acc[i]) best = max(best, argmax_key(acc[i], (uint32_t)(n0 + cq * 64 + i)));
+          if (best) atomicMax(amax + m, best);
+        }
+      } else if (vec) {
         float* ob = ostage + (size_t)warp * 32 * OST;
 #pragma unroll
         for (int cb = 0; cb < 4; ++cb) {
@@ -533,7 +541,7 @@ cudaError_t launch_umma(const CqMat& W, const GemmScratch& gs, const __half* whi
   const int ntn = (nrows + UN - 1) / UN, ntiles = ntn * ((M + UM - 1) / UM);
   const int grid = std::min(ntiles, 148);  // persistent: one CTA per SM
   return launch_pdl(kern, dim3(grid), dim3(Pipe<EXACT, UN>::THREADS), smem, st, W, mah, mal, mbh, mbl, gs.inv, linv,
-                    M, y, ldy, row0, nrows, ntn, ntiles, werr, out_stage ? 1 : 0);
+                    M, y, ldy, row0, nrows, ntn, ntiles, werr, out_stage ? 1 : 0, gs.amax);
 }
 
 }  // namespace

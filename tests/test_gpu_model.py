@@ -211,6 +211,50 @@ def test_device_batch_graph_matches_eager(full_gpu, cuda):
         assert np.array_equal(la, lb)
 
 
+def test_greedy_pick_without_logits_is_the_first_maximum(full_gpu, cuda):
+    """Steps that want no logits fold the greedy pick into the LM head's
+    tensor-core epilogue (per-row atomicMax of a value/column key) instead of
+    storing the logits and running argmax: twin session sets fed the same
+    tokens must pick identically with and without logits, and every pick is the
+    first maximum of the logits row (v3_engine.rs:410-420), through the
+    device batch (graph and eager) and through decode_batch."""
+    torch = cuda
+    rng = np.random.default_rng(9)
+    n = 24  # above the 8-row GEMV limit: the head runs on the tensor cores
+    prompts = [rng.integers(1, 8192, 20 + i).astype(np.uint32) for i in range(n)]
+    twins = []
+    for _ in range(2):
+        ss = [full_gpu.session(64, True) for _ in prompts]
+        _, picks = full_gpu.prefill_batch(ss, prompts, logits=False)
+        twins.append((ss, picks))
+    (sa, pa), (sb, pb) = twins
+    assert np.array_equal(pa, pb)
+    ba, bb = full_gpu.batch(sa), full_gpu.batch(sb)
+    ba.set_tokens(pa)
+    bb.set_tokens(pb)
+    logits = torch.zeros(n, full_gpu.logit_rows, device="cuda")
+    for step in range(4):
+        use_graph = step % 2 == 1
+        ba.step(logits.data_ptr(), use_graph=use_graph)
+        bb.step(None, use_graph=use_graph)
+        torch.cuda.synchronize()
+        ka, kb = ba.get_next(), bb.get_next()
+        assert np.array_equal(ka, kb), step
+        assert np.array_equal(ka, np.argmax(logits.cpu().numpy(), axis=1).astype(np.uint32)), step
+        ba.feed_next()
+        bb.feed_next()
+    ta, tb = ba.get_next(), bb.get_next()
+    ba.close()
+    bb.close()
+    for _ in range(2):
+        la, ta = full_gpu.decode_batch(sa, ta)
+        _, tb = full_gpu.decode_batch(sb, tb, logits=False)
+        assert np.array_equal(ta, tb)
+        assert np.array_equal(ta, np.argmax(la, axis=1).astype(np.uint32))
+    for s in sa + sb:
+        s.close()
+
+
 def test_engine_errors_are_reported(full_gpu):
     s = full_gpu.session(8)
     s.prefill(np.arange(1, 5, dtype=np.uint32))
